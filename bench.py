@@ -1,0 +1,322 @@
+"""Headline benchmark: MoE training tokens/sec on N GPUs of one node.
+
+    python bench.py --gpus 1 --steps 10 --warmup 3
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
+        bench.py --gpus N --steps K --warmup W
+    python bench.py --impl reference ...      # the unmodified reference build, same metric and config
+
+Config 2: vocab 32000, d_model 1024, 16 layers, 16 heads, 64 SwiGLU experts (hidden 2816), top_k 2, capacity 1.25,
+aux 0.01, 32 sequences of 2048 (+1 label token) per GPU, Zipf(1.1) token ids from a seeded generator, random init
+N(0, 0.02), bf16 compute, AdamW with fp32 master weights. Experts are sharded expert-parallel over the N GPUs.
+
+``value`` is device-timed (CUDA events, barrier + synchronize on both sides, max over ranks) over exactly K full
+training steps (forward, backward, gradient clip, optimizer step) with inputs already on the device; ``e2e``
+repeats K steps through the public training API with the per-step pinned host->device input copy and the
+device->host loss read inside the timed region. Every step touches far more than the 126 MB L2, so no flush is
+needed between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+import traceback
+
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "MoE train tokens/sec"
+BASELINE_VALUE = None  # BASELINE.md publishes no number for this config (published: {})
+
+CONFIG2 = dict(vocab_size=32000, hidden_size=1024, layers=16, attention_heads=16, num_experts=64, ffn_size=2816,
+               top_k=2, capacity_factor=1.25, router_aux_loss_coef=0.01)
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("native", "reference"), default="native")
+    p.add_argument("--seqs-per-gpu", type=int, default=32)
+    p.add_argument("--seq-len", type=int, default=2048)
+    p.add_argument("--layers", type=int, default=CONFIG2["layers"], help="debug override (the metric needs 16)")
+    p.add_argument("--recompute", choices=("auto", "on", "off"), default="auto")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--kernel-breakdown", action="store_true",
+                   help="after timing, profile one extra step and print per-kernel CUDA time shares to stderr")
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+def dist_setup(gpus: int):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != gpus:
+        raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    torch.cuda.set_device(local)
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def emit(rank: int, record: dict) -> None:
+    if rank == 0:
+        print(json.dumps(record), flush=True)
+
+
+def count_launches(step_fn) -> int:
+    """Kernels of this framework's extension launched by one step (profiled once, outside the timed region)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    ours = [n for n in names if "qw::" in n or n.startswith("void qw::")]
+    return len(ours)
+
+
+def kernel_breakdown(step_fn) -> None:
+    """Per-kernel CUDA time of one step (shares only; numbers taken under a profiler are never reported)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    totals: dict = {}
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            name = e.name[:110]
+            t, n = totals.get(name, (0.0, 0))
+            totals[name] = (t + e.device_time_total, n + 1)
+    grand = sum(t for t, _ in totals.values()) or 1.0
+    print(f"kernel breakdown: {grand / 1e3:.1f} ms of device time in one step", file=sys.stderr)
+    for name, (t, n) in sorted(totals.items(), key=lambda kv: -kv[1][0])[:40]:
+        print(f"  {100 * t / grand:5.1f}%  {t / 1e3:8.2f} ms  x{n:<5d} {name}", file=sys.stderr)
+
+
+# ================================================================================================ native arm
+def run_native(args, rank, world, local):
+    import torch
+
+    sys.path.insert(0, ROOT)
+    from quantaweave_b200 import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM
+    from quantaweave_b200.data.pipeline import SyntheticTokenStream
+    from quantaweave_b200.optim.adamw import FusedAdamW
+    from quantaweave_b200.training.native import prepare_model
+    from quantaweave_b200.utils.timing import ClockSampler, DeviceTimer
+
+    cfg = QuantaWeaveConfig(**{**CONFIG2, "layers": args.layers}, max_sequence_length=args.seq_len + 1,
+                            norm_type="rmsnorm", position_embedding="rope", attention_bias=False, init_std=0.02)
+    ep = None
+    if world > 1:
+        from quantaweave_b200.parallel.expert_parallel import init_expert_parallel
+
+        ep = init_expert_parallel("cuda", 1)
+    torch.manual_seed(args.seed + rank)
+    with torch.device("cuda"):
+        model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ep)
+    local_experts = cfg.num_experts // world
+    recompute = args.recompute == "on" or (args.recompute == "auto" and local_experts > 16)
+    prepare_model(model, "bf16", recompute_experts=recompute)
+    if ep is not None:
+        from quantaweave_b200.parallel.expert_parallel import broadcast_shared_parameters
+
+        broadcast_shared_parameters(model, ep)
+    model.train()
+    opt = FusedAdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    stream = SyntheticTokenStream(cfg.vocab_size, args.seq_len, args.seqs_per_gpu, seed=args.seed,
+                                  distribution="zipf", zipf_s=1.1, rank=rank, world_size=world)
+
+    def train_step(batch):
+        out = model(batch, labels=batch, return_logits=False)
+        out["loss"].backward()
+        if ep is not None:
+            from quantaweave_b200.parallel.expert_parallel import clip_grad_norm_parallel, sync_gradients
+
+            sync_gradients(model, ep, None)
+            clip_grad_norm_parallel(model, ep, 1.0, False, opt)
+        else:
+            opt.clip_grad_norm_(1.0)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        return out["loss"]
+
+    host_batches = [stream.batch(i)[0].pin_memory() for i in range(args.warmup + 2 * args.steps + 1)]
+    dev_batches = [b.to("cuda", non_blocking=True) for b in host_batches[: args.warmup + args.steps]]
+    for i in range(args.warmup):
+        train_step(dev_batches[i])
+    torch.cuda.synchronize()
+    # ---- device-timed K steps (inputs resident) ----
+    with ClockSampler(local) as clocks:
+        with DeviceTimer() as t:
+            for i in range(args.steps):
+                loss = train_step(dev_batches[args.warmup + i])
+    ms_per_step = t.ms / args.steps
+    tokens_per_step = args.seqs_per_gpu * args.seq_len * world
+    value = tokens_per_step / (ms_per_step / 1000.0)
+    final_loss = float(loss.item())
+    with torch.no_grad():
+        probe = model(dev_batches[-1], labels=dev_batches[-1], return_logits=False)
+        routes = args.seqs_per_gpu * (args.seq_len + 1) * cfg.top_k * args.layers
+        overflow_fraction = float(probe["overflow_routes"]) / routes
+    del dev_batches
+    # ---- end-to-end: pinned H2D of each step's inputs and D2H of its loss inside the timed region ----
+    e2e = None
+    if not args.no_e2e:
+        h2d = host_batches[0].numel() * host_batches[0].element_size()
+        with DeviceTimer() as te:
+            for i in range(args.steps):
+                batch = host_batches[args.warmup + args.steps + i].to("cuda", non_blocking=True)
+                loss_value = float(train_step(batch).item())
+        e2e = {"value": tokens_per_step / (te.ms / args.steps / 1000.0), "unit": "tokens/s",
+               "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4 * world, "ms_per_step": te.ms / args.steps,
+               "final_loss": loss_value}
+    launches = count_launches(lambda: train_step(host_batches[-1].to("cuda"))) * args.steps
+    if args.kernel_breakdown and rank == 0:
+        kernel_breakdown(lambda: train_step(host_batches[-1].to("cuda")))
+    peak_gb = torch.cuda.max_memory_allocated() / 1e9
+    emit(rank, {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None, "dtype": "bf16",
+        "data": "synthetic: seeded Zipf(1.1) token ids, random-init N(0,0.02) weights",
+        "config": {"model": "moe-1b-e64 (BASELINE config 2: vocab 32000, d1024, 16 layers, 16 heads, 64 experts "
+                            "h2816, top2, cf1.25, RMSNorm+RoPE)" if args.layers == 16 else
+                            f"DEBUG {args.layers}-layer variant of config 2",
+                   "global_batch": args.seqs_per_gpu * world, "seq_len": args.seq_len,
+                   "parallelism": f"ep{world}" if world > 1 else "single-gpu (all 64 experts local)",
+                   "l2": "no flush: every step streams >100 GB through HBM, far above the 126 MB L2",
+                   "recompute_expert_activations": recompute, "optimizer": "fused AdamW, fp32 master, clip 1.0"},
+        "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches, "impl": "native",
+        "final_loss": final_loss, "peak_mem_gb": round(peak_gb, 1), "overflow_fraction": round(overflow_fraction, 4),
+    })
+
+
+# ================================================================================================ reference arm
+def run_reference(args, rank, world, local):
+    import torch
+
+    ref_src = os.path.join(ROOT, "baseline", "_ref", "src")
+    if not os.path.isdir(ref_src):
+        emit(rank, {"impl": "reference", "unavailable": "baseline/_ref/src is missing (reference not installed)"})
+        return
+    sys.path.insert(0, ref_src)
+    from quantweave_moe_model import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM  # the reference's own modules
+
+    sys.path.insert(0, ROOT)
+    from quantaweave_b200.data.pipeline import SyntheticTokenStream
+    from quantaweave_b200.utils.timing import ClockSampler, DeviceTimer
+
+    cfg = QuantaWeaveConfig(vocab_size=CONFIG2["vocab_size"], hidden_size=CONFIG2["hidden_size"], layers=args.layers,
+                            ffn_size=CONFIG2["ffn_size"], num_experts=CONFIG2["num_experts"], top_k=CONFIG2["top_k"],
+                            attention_heads=CONFIG2["attention_heads"], max_sequence_length=args.seq_len + 1,
+                            router_aux_loss_coef=CONFIG2["router_aux_loss_coef"],
+                            capacity_factor=CONFIG2["capacity_factor"])
+    device = torch.device("cuda", local)
+    ep = None
+    if world > 1:
+        from expert_parallel import init_expert_parallel, broadcast_shared_parameters
+
+        ep = init_expert_parallel("cuda", 1)
+    torch.manual_seed(args.seed + rank)
+    try:
+        model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ep).to(device)
+        if ep is not None:
+            broadcast_shared_parameters(model, ep)
+        kernel = "loop"
+        if ep is None:
+            from moe_kernels import kernels_available
+
+            if kernels_available(device):
+                kernel = model.set_moe_kernel("triton")
+        optimizer = torch.optim.AdamW(model.parameters(), lr=3e-4)
+        stream = SyntheticTokenStream(cfg.vocab_size, args.seq_len, args.seqs_per_gpu, seed=args.seed,
+                                      distribution="zipf", zipf_s=1.1, rank=rank, world_size=world)
+        model.train()
+
+        def train_step(batch):
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = model(batch, labels=batch)
+            loss = out["loss"]
+            loss.backward()
+            if ep is not None:
+                from expert_parallel import clip_grad_norm_parallel, sync_gradients
+
+                sync_gradients(model, ep, None)
+                clip_grad_norm_parallel(model, ep, 1.0, False)
+            else:
+                torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+            optimizer.step()
+            optimizer.zero_grad(set_to_none=True)
+            return loss
+
+        host = [stream.batch(i)[0].pin_memory() for i in range(args.warmup + 2 * args.steps)]
+        dev = [b.to(device) for b in host[: args.warmup + args.steps]]
+        for i in range(args.warmup):
+            train_step(dev[i])
+        with ClockSampler(local) as clocks:
+            with DeviceTimer() as t:
+                for i in range(args.steps):
+                    loss = train_step(dev[args.warmup + i])
+        del dev
+        tokens = args.seqs_per_gpu * args.seq_len * world
+        ms = t.ms / args.steps
+        e2e = None
+        if not args.no_e2e:
+            with DeviceTimer() as te:
+                for i in range(args.steps):
+                    float(train_step(host[args.warmup + args.steps + i].to(device, non_blocking=True)).item())
+            e2e = {"value": tokens / (te.ms / args.steps / 1000.0), "unit": "tokens/s",
+                   "h2d_bytes_per_step": host[0].numel() * host[0].element_size() * world,
+                   "d2h_bytes_per_step": 4 * world}
+        emit(rank, {"metric": METRIC, "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
+                    "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                    "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "impl": "reference",
+                    "data": "synthetic: seeded Zipf(1.1) token ids, random init (reference's own init)",
+                    "config": {"model": "reference architecture at config-2 shape (LayerNorm, learned positions, MHA)",
+                               "global_batch": args.seqs_per_gpu * world, "seq_len": args.seq_len,
+                               "parallelism": f"ep{world}" if world > 1 else "single-gpu",
+                               "moe_kernel": kernel},
+                    "clocks": clocks.summary(), "e2e": e2e, "final_loss": float(loss.item())})
+    except torch.OutOfMemoryError as exc:
+        emit(rank, {"impl": "reference", "unavailable": f"out of memory on B200 at config 2: {str(exc)[:160]}"})
+
+
+def main():
+    args = parse()
+    try:
+        rank, world, local = dist_setup(args.gpus)
+    except SystemExit:
+        raise
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world, local)
+        else:
+            run_native(args, rank, world, local)
+    finally:
+        import torch.distributed as dist
+
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    try:
+        main()
+    except Exception:  # noqa: BLE001
+        traceback.print_exc()
+        sys.exit(1)

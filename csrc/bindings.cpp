@@ -1,0 +1,402 @@
+// PyTorch bindings: tensor validation and stream selection around the raw-pointer launchers (launchers.h).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "launchers.h"
+
+namespace {
+
+using torch::Tensor;
+using OptT = c10::optional<Tensor>;
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_DTYPE(t, dt) TORCH_CHECK((t).scalar_type() == (dt), #t " has the wrong dtype")
+#define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+#define CHECK_ROWS(t) TORCH_CHECK((t).dim() == 2 && (t).stride(1) == 1, #t " must be 2-D with unit inner stride")
+
+const qw::bf16* bptr(const Tensor& t) { return reinterpret_cast<const qw::bf16*>(t.data_ptr()); }
+qw::bf16* bptr_mut(const Tensor& t) { return reinterpret_cast<qw::bf16*>(t.data_ptr()); }
+template <typename T>
+const T* optptr(const OptT& t) { return t && t->defined() ? t->data_ptr<T>() : nullptr; }
+const qw::bf16* optb(const OptT& t) { return t && t->defined() ? bptr(*t) : nullptr; }
+qw::bf16* optb_mut(const OptT& t) { return t && t->defined() ? bptr_mut(*t) : nullptr; }
+
+// ------------------------------------------------------------------------------------------------ GEMM
+void linear_fwd(Tensor x, Tensor w, OptT bias, OptT residual, Tensor out) {
+  CHECK_CUDA(x); CHECK_ROWS(x); CHECK_DTYPE(x, torch::kBFloat16);
+  CHECK_ROWS(w); CHECK_DTYPE(w, torch::kBFloat16); CHECK_ROWS(out);
+  TORCH_CHECK(w.size(1) == x.size(1) && out.size(0) == x.size(0) && out.size(1) == w.size(0), "linear_fwd shapes");
+  if (bias) { CHECK_DTYPE(*bias, torch::kFloat32); TORCH_CHECK(bias->numel() == w.size(0)); }
+  if (residual) { CHECK_ROWS(*residual); CHECK_DTYPE(*residual, torch::kBFloat16); }
+  const bool fp32 = out.scalar_type() == torch::kFloat32;
+  TORCH_CHECK(fp32 || out.scalar_type() == torch::kBFloat16);
+  c10::cuda::CUDAGuard g(x.device());
+  qw::linear_fwd(bptr(x), x.stride(0), bptr(w), w.stride(0), x.size(0), w.size(0), x.size(1), optptr<float>(bias),
+                 optb(residual), residual ? residual->stride(0) : 0, out.data_ptr(), out.stride(0), fp32, stream());
+}
+
+void linear_dgrad(Tensor dy, Tensor w, Tensor dx, bool accumulate) {
+  CHECK_CUDA(dy); CHECK_ROWS(dy); CHECK_DTYPE(dy, torch::kBFloat16);
+  CHECK_ROWS(w); CHECK_DTYPE(w, torch::kBFloat16); CHECK_ROWS(dx);
+  TORCH_CHECK(w.size(0) == dy.size(1) && dx.size(0) == dy.size(0) && dx.size(1) == w.size(1), "linear_dgrad shapes");
+  const bool fp32 = dx.scalar_type() == torch::kFloat32;
+  c10::cuda::CUDAGuard g(dy.device());
+  qw::linear_dgrad(bptr(dy), dy.stride(0), bptr(w), w.stride(0), dy.size(0), dy.size(1), w.size(1), dx.data_ptr(),
+                   dx.stride(0), fp32, accumulate, stream());
+}
+
+void linear_wgrad(Tensor dy, Tensor x, Tensor dw, bool accumulate) {
+  CHECK_CUDA(dy); CHECK_ROWS(dy); CHECK_DTYPE(dy, torch::kBFloat16);
+  CHECK_ROWS(x); CHECK_DTYPE(x, torch::kBFloat16); CHECK_ROWS(dw);
+  TORCH_CHECK(x.size(0) == dy.size(0) && dw.size(0) == dy.size(1) && dw.size(1) == x.size(1), "linear_wgrad shapes");
+  const bool fp32 = dw.scalar_type() == torch::kFloat32;
+  c10::cuda::CUDAGuard g(dy.device());
+  qw::linear_wgrad(bptr(dy), dy.stride(0), bptr(x), x.stride(0), dy.size(0), dy.size(1), x.size(1), dw.data_ptr(),
+                   dw.stride(0), fp32, accumulate, stream());
+}
+
+void check_groups(const Tensor& counts, const Tensor& offsets, int64_t E) {
+  CHECK_DTYPE(counts, torch::kInt32); CHECK_DTYPE(offsets, torch::kInt32);
+  TORCH_CHECK(counts.numel() >= E && offsets.numel() >= E, "group tables too short");
+}
+
+void moe_gate_up_fwd(Tensor x, Tensor w, Tensor counts, Tensor offsets, Tensor h, OptT gu) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_CONTIG(w); CHECK_CONTIG(h); CHECK_DTYPE(w, torch::kBFloat16);
+  const int64_t E = w.size(0), F = w.size(1) / 2, H = w.size(2), R = x.size(0);
+  TORCH_CHECK(x.size(1) == H && h.size(0) == R && h.size(1) == F, "moe_gate_up_fwd shapes");
+  if (gu) { CHECK_CONTIG(*gu); TORCH_CHECK(gu->size(0) == R && gu->size(1) == 2 * F); }
+  const int64_t G = counts.numel();
+  check_groups(counts, offsets, G);
+  TORCH_CHECK(G % E == 0, "groups must be a multiple of the expert count");
+  c10::cuda::CUDAGuard g(x.device());
+  qw::moe_gate_up_fwd(bptr(x), bptr(w), counts.data_ptr<int>(), offsets.data_ptr<int>(), R, G, E, H, F, bptr_mut(h),
+                      optb_mut(gu), stream());
+}
+
+void moe_down_fwd(Tensor h, Tensor w, Tensor counts, Tensor offsets, Tensor y) {
+  CHECK_CUDA(h); CHECK_CONTIG(h); CHECK_CONTIG(w); CHECK_CONTIG(y);
+  const int64_t E = w.size(0), H = w.size(1), F = w.size(2), R = h.size(0);
+  TORCH_CHECK(h.size(1) == F && y.size(0) == R && y.size(1) == H, "moe_down_fwd shapes");
+  const int64_t G = counts.numel();
+  check_groups(counts, offsets, G);
+  TORCH_CHECK(G % E == 0, "groups must be a multiple of the expert count");
+  c10::cuda::CUDAGuard g(h.device());
+  qw::moe_down_fwd(bptr(h), bptr(w), counts.data_ptr<int>(), offsets.data_ptr<int>(), R, G, E, H, F, bptr_mut(y),
+                   stream());
+}
+
+void moe_down_bwd(Tensor dy, Tensor w, Tensor counts, Tensor offsets, Tensor gu, Tensor route_w, Tensor dgu,
+                  OptT h_weighted, Tensor dw_partial) {
+  CHECK_CUDA(dy); CHECK_CONTIG(dy); CHECK_CONTIG(w); CHECK_CONTIG(gu); CHECK_CONTIG(dgu); CHECK_CONTIG(dw_partial);
+  const int64_t E = w.size(0), H = w.size(1), F = w.size(2), R = dy.size(0);
+  TORCH_CHECK(dy.size(1) == H && gu.size(0) == R && gu.size(1) == 2 * F && dgu.sizes() == gu.sizes(),
+              "moe_down_bwd shapes");
+  CHECK_DTYPE(route_w, torch::kFloat32);
+  CHECK_DTYPE(dw_partial, torch::kFloat32);
+  TORCH_CHECK(dw_partial.size(0) == R && dw_partial.size(1) == qw::moe_dw_tiles(F));
+  if (h_weighted) TORCH_CHECK(h_weighted->size(0) == R && h_weighted->size(1) == F);
+  const int64_t G = counts.numel();
+  check_groups(counts, offsets, G);
+  TORCH_CHECK(G % E == 0, "groups must be a multiple of the expert count");
+  c10::cuda::CUDAGuard g(dy.device());
+  qw::moe_down_bwd(bptr(dy), bptr(w), counts.data_ptr<int>(), offsets.data_ptr<int>(), R, G, E, H, F, bptr(gu),
+                   route_w.data_ptr<float>(), bptr_mut(dgu), optb_mut(h_weighted), dw_partial.data_ptr<float>(),
+                   static_cast<int>(dw_partial.size(1)), stream());
+}
+
+void moe_gate_up_dgrad(Tensor dgu, Tensor w, Tensor counts, Tensor offsets, Tensor dx) {
+  CHECK_CUDA(dgu); CHECK_CONTIG(dgu); CHECK_CONTIG(w); CHECK_CONTIG(dx);
+  const int64_t E = w.size(0), F = w.size(1) / 2, H = w.size(2), R = dgu.size(0);
+  TORCH_CHECK(dgu.size(1) == 2 * F && dx.size(0) == R && dx.size(1) == H, "moe_gate_up_dgrad shapes");
+  const int64_t G = counts.numel();
+  check_groups(counts, offsets, G);
+  TORCH_CHECK(G % E == 0, "groups must be a multiple of the expert count");
+  c10::cuda::CUDAGuard g(dgu.device());
+  qw::moe_gate_up_dgrad(bptr(dgu), bptr(w), counts.data_ptr<int>(), offsets.data_ptr<int>(), R, G, E, H, F,
+                        bptr_mut(dx), stream());
+}
+
+void moe_wgrad(Tensor a, Tensor b, Tensor counts, Tensor offsets, Tensor out, bool accumulate, int64_t segments,
+               double alpha) {
+  CHECK_CUDA(a); CHECK_CONTIG(a); CHECK_CONTIG(b); CHECK_CONTIG(out);
+  const int64_t E = out.size(0), M = out.size(1), N = out.size(2), R = a.size(0);
+  TORCH_CHECK(a.size(1) == M && b.size(1) == N && b.size(0) == R, "moe_wgrad shapes");
+  TORCH_CHECK(segments >= 1 && counts.numel() == E * segments, "moe_wgrad: counts must hold segments * experts");
+  check_groups(counts, offsets, E * segments);
+  const bool fp32 = out.scalar_type() == torch::kFloat32;
+  c10::cuda::CUDAGuard g(a.device());
+  qw::moe_wgrad(bptr(a), bptr(b), counts.data_ptr<int>(), offsets.data_ptr<int>(), R, E, static_cast<int>(segments), M,
+                N, out.data_ptr(), fp32, accumulate, static_cast<float>(alpha), stream());
+}
+
+// ------------------------------------------------------------------------------------------------ norm / rope
+void norm_fwd(Tensor x, OptT delta, OptT x_out, Tensor w, OptT b, Tensor y, OptT mean, Tensor rstd, double eps,
+              bool rms) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_CONTIG(y);
+  CHECK_DTYPE(w, torch::kFloat32); CHECK_DTYPE(rstd, torch::kFloat32);
+  const int H = static_cast<int>(x.size(-1));
+  const int64_t rows = x.numel() / H;
+  c10::cuda::CUDAGuard g(x.device());
+  qw::norm_fwd(bptr(x), optb(delta), optb_mut(x_out), w.data_ptr<float>(), optptr<float>(b), bptr_mut(y),
+               mean ? mean->data_ptr<float>() : nullptr, rstd.data_ptr<float>(), rows, H, static_cast<float>(eps), rms,
+               stream());
+}
+
+int64_t norm_bwd_blocks(int64_t rows) { return qw::norm_bwd_blocks(rows); }
+
+void norm_bwd(Tensor dy, Tensor x, Tensor w, OptT mean, Tensor rstd, OptT dres, Tensor dx, Tensor dw_part,
+              OptT db_part, Tensor dw, OptT db, bool rms, bool accumulate) {
+  CHECK_CUDA(dy); CHECK_CONTIG(dy); CHECK_CONTIG(x); CHECK_CONTIG(dx);
+  const int H = static_cast<int>(x.size(-1));
+  const int64_t rows = x.numel() / H;
+  c10::cuda::CUDAGuard g(x.device());
+  qw::norm_bwd(bptr(dy), bptr(x), w.data_ptr<float>(), mean ? mean->data_ptr<float>() : nullptr, rstd.data_ptr<float>(),
+               optb(dres), bptr_mut(dx), dw_part.data_ptr<float>(), db_part ? db_part->data_ptr<float>() : nullptr,
+               dw.data_ptr<float>(), db ? db->data_ptr<float>() : nullptr, rows, H, rms, accumulate, stream());
+}
+
+void rope_apply(Tensor qkv, int64_t heads_rot, int64_t head_dim, int64_t seq, OptT positions, Tensor cos_t,
+                Tensor sin_t, bool inverse) {
+  CHECK_CUDA(qkv); CHECK_ROWS(qkv);
+  CHECK_DTYPE(cos_t, torch::kFloat32); CHECK_DTYPE(sin_t, torch::kFloat32);
+  c10::cuda::CUDAGuard g(qkv.device());
+  qw::rope_apply(bptr_mut(qkv), qkv.size(0), static_cast<int>(heads_rot), static_cast<int>(head_dim), qkv.stride(0),
+                 static_cast<int>(seq), optptr<int>(positions), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+                 inverse, stream());
+}
+
+// ------------------------------------------------------------------------------------------------ routing
+void router_logits(Tensor x, Tensor w, Tensor logits) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DTYPE(w, torch::kFloat32); CHECK_CONTIG(w); CHECK_CONTIG(logits);
+  c10::cuda::CUDAGuard g(x.device());
+  qw::router_logits(bptr(x), w.data_ptr<float>(), x.size(0), static_cast<int>(x.size(1)), static_cast<int>(w.size(0)),
+                    logits.data_ptr<float>(), stream());
+}
+
+void router_topk(Tensor logits, OptT bias, int64_t k, double temperature, Tensor probs, Tensor top_idx, Tensor top_w,
+                 Tensor counts) {
+  CHECK_CUDA(logits); CHECK_CONTIG(logits);
+  c10::cuda::CUDAGuard g(logits.device());
+  qw::router_topk(logits.data_ptr<float>(), optptr<float>(bias), logits.size(0), static_cast<int>(logits.size(1)),
+                  static_cast<int>(k), static_cast<float>(temperature), probs.data_ptr<float>(), top_idx.data_ptr<int>(),
+                  top_w.data_ptr<float>(), counts.data_ptr<int>(), stream());
+}
+
+int64_t moe_plan_chunks(int64_t routes) { return qw::moe_plan_chunks(routes); }
+
+void moe_plan(Tensor top_idx, Tensor top_w, Tensor counts, int64_t cap, int64_t slot_rows, Tensor kept, Tensor offsets,
+              Tensor uoffsets, Tensor meta, Tensor chunk_hist, Tensor sorted_routes, Tensor route_row) {
+  CHECK_CUDA(top_idx);
+  const int E = static_cast<int>(counts.numel());
+  c10::cuda::CUDAGuard g(top_idx.device());
+  qw::moe_plan(top_idx.data_ptr<int>(), top_w.data_ptr<float>(), counts.data_ptr<int>(), top_idx.numel(), E,
+               static_cast<int>(std::min<int64_t>(cap, INT32_MAX)), static_cast<int>(slot_rows), kept.data_ptr<int>(),
+               offsets.data_ptr<int>(),
+               uoffsets.data_ptr<int>(), meta.data_ptr<int>(), chunk_hist.data_ptr<int>(), sorted_routes.data_ptr<int>(),
+               route_row.data_ptr<int>(), stream());
+}
+
+void moe_permute(Tensor x, int64_t k, Tensor route_row, Tensor top_w, Tensor kept, Tensor offsets, Tensor x_perm,
+                 Tensor row_token, Tensor row_w) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_CONTIG(x_perm);
+  c10::cuda::CUDAGuard g(x.device());
+  qw::moe_permute(bptr(x), route_row.numel(), static_cast<int>(k), static_cast<int>(x.size(1)),
+                  route_row.data_ptr<int>(), top_w.data_ptr<float>(), kept.data_ptr<int>(), offsets.data_ptr<int>(),
+                  static_cast<int>(kept.numel()), bptr_mut(x_perm), row_token.data_ptr<int>(), row_w.data_ptr<float>(),
+                  stream());
+}
+
+void moe_pad_zero(Tensor kept, Tensor offsets, Tensor buf) {
+  CHECK_CUDA(buf); CHECK_CONTIG(buf);
+  c10::cuda::CUDAGuard g(buf.device());
+  qw::moe_pad_zero(kept.data_ptr<int>(), offsets.data_ptr<int>(), static_cast<int>(kept.numel()),
+                   static_cast<int>(buf.size(1)), bptr_mut(buf), stream());
+}
+
+void moe_gather_rows(Tensor src, Tensor row_token, Tensor meta, Tensor dst) {
+  CHECK_CUDA(src); CHECK_CONTIG(src); CHECK_CONTIG(dst);
+  c10::cuda::CUDAGuard g(src.device());
+  qw::moe_gather_rows(bptr(src), row_token.data_ptr<int>(), meta.data_ptr<int>(), dst.size(0),
+                      static_cast<int>(dst.size(1)), bptr_mut(dst), stream());
+}
+
+void moe_combine(Tensor y, Tensor route_row, Tensor top_w, OptT resid, int64_t k, Tensor out) {
+  CHECK_CUDA(y); CHECK_CONTIG(y); CHECK_CONTIG(out);
+  c10::cuda::CUDAGuard g(y.device());
+  qw::moe_combine(bptr(y), route_row.data_ptr<int>(), top_w.data_ptr<float>(), optb(resid), out.size(0),
+                  static_cast<int>(k), static_cast<int>(out.size(1)), bptr_mut(out), stream());
+}
+
+void moe_combine_grad(Tensor dx_perm, Tensor route_row, OptT extra, int64_t k, Tensor dx) {
+  CHECK_CUDA(dx_perm); CHECK_CONTIG(dx_perm); CHECK_CONTIG(dx);
+  c10::cuda::CUDAGuard g(dx.device());
+  qw::moe_combine_grad(bptr(dx_perm), route_row.data_ptr<int>(), optptr<float>(extra), dx.size(0), static_cast<int>(k),
+                       static_cast<int>(dx.size(1)), bptr_mut(dx), stream());
+}
+
+void moe_route_dw(Tensor partial, Tensor route_row, Tensor d_w) {
+  CHECK_CUDA(partial);
+  c10::cuda::CUDAGuard g(partial.device());
+  qw::moe_route_dw(partial.data_ptr<float>(), static_cast<int>(partial.size(1)), route_row.data_ptr<int>(),
+                   route_row.numel(), d_w.data_ptr<float>(), stream());
+}
+
+void router_backward(Tensor probs, Tensor top_idx, Tensor top_w, Tensor d_w, OptT d_probs, double temperature,
+                     Tensor d_logits) {
+  CHECK_CUDA(probs);
+  c10::cuda::CUDAGuard g(probs.device());
+  qw::router_backward(probs.data_ptr<float>(), top_idx.data_ptr<int>(), top_w.data_ptr<float>(), d_w.data_ptr<float>(),
+                      optptr<float>(d_probs), probs.size(0), static_cast<int>(probs.size(1)),
+                      static_cast<int>(top_idx.size(1)), static_cast<float>(temperature), d_logits.data_ptr<float>(),
+                      stream());
+}
+
+void router_dx(Tensor d_logits, Tensor w, Tensor dx) {
+  CHECK_CUDA(d_logits);
+  c10::cuda::CUDAGuard g(d_logits.device());
+  qw::router_dx(d_logits.data_ptr<float>(), w.data_ptr<float>(), d_logits.size(0), static_cast<int>(d_logits.size(1)),
+                static_cast<int>(w.size(1)), dx.data_ptr<float>(), stream());
+}
+
+int64_t router_dw_split(int64_t T) { return qw::router_dw_split(T); }
+
+void router_dw(Tensor d_logits, Tensor x, Tensor dw, bool accumulate, Tensor workspace) {
+  CHECK_CUDA(d_logits);
+  c10::cuda::CUDAGuard g(d_logits.device());
+  qw::router_dw(d_logits.data_ptr<float>(), bptr(x), d_logits.size(0), static_cast<int>(d_logits.size(1)),
+                static_cast<int>(x.size(1)), dw.data_ptr<float>(), accumulate, workspace.data_ptr<float>(), stream());
+}
+
+// ------------------------------------------------------------------------------------------------ optimizer / CE
+int64_t adam_chunk_size() { return qw::adam_chunk_size(); }
+
+static_assert(sizeof(qw::AdamTensor) == 64, "AdamTensor layout is mirrored in Python (8 x 8 bytes)");
+
+void adam_grad_norm(Tensor table, Tensor chunk_tensor, Tensor chunk_start, Tensor partial, OptT extra_sumsq,
+                    double max_norm, Tensor norm_out) {
+  CHECK_CUDA(table);
+  c10::cuda::CUDAGuard g(table.device());
+  qw::adam_grad_norm(reinterpret_cast<const qw::AdamTensor*>(table.data_ptr()), chunk_tensor.data_ptr<int>(),
+                     chunk_start.data_ptr<int64_t>(), static_cast<int>(chunk_tensor.numel()),
+                     partial.data_ptr<double>(), optptr<double>(extra_sumsq), static_cast<float>(max_norm),
+                     norm_out.data_ptr<float>(), stream());
+}
+
+void adam_sumsq(Tensor table, Tensor chunk_tensor, Tensor chunk_start, Tensor partial) {
+  CHECK_CUDA(table);
+  c10::cuda::CUDAGuard g(table.device());
+  qw::adam_sumsq(reinterpret_cast<const qw::AdamTensor*>(table.data_ptr()), chunk_tensor.data_ptr<int>(),
+                 chunk_start.data_ptr<int64_t>(), static_cast<int>(chunk_tensor.numel()), partial.data_ptr<double>(),
+                 stream());
+}
+
+void adam_step(Tensor table, Tensor chunk_tensor, Tensor chunk_start, double lr, double beta1, double beta2, double eps,
+               double weight_decay, int64_t step, OptT clip) {
+  CHECK_CUDA(table);
+  qw::AdamHyper h;
+  h.lr = static_cast<float>(lr);
+  h.beta1 = static_cast<float>(beta1);
+  h.beta2 = static_cast<float>(beta2);
+  h.eps = static_cast<float>(eps);
+  h.weight_decay = static_cast<float>(weight_decay);
+  h.bias_correction1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
+  h.bias_correction2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
+  c10::cuda::CUDAGuard g(table.device());
+  qw::adam_step(reinterpret_cast<const qw::AdamTensor*>(table.data_ptr()), chunk_tensor.data_ptr<int>(),
+                chunk_start.data_ptr<int64_t>(), static_cast<int>(chunk_tensor.numel()), h, optptr<float>(clip),
+                stream());
+}
+
+void cross_entropy_chunk(Tensor logits, Tensor labels, double grad_scale, Tensor loss_out, int64_t ignore_index) {
+  CHECK_CUDA(logits); CHECK_ROWS(logits); CHECK_DTYPE(labels, torch::kInt64);
+  c10::cuda::CUDAGuard g(logits.device());
+  qw::cross_entropy_chunk(bptr_mut(logits), logits.size(0), logits.stride(0), static_cast<int>(logits.size(1)),
+                          labels.data_ptr<int64_t>(), static_cast<float>(grad_scale), loss_out.data_ptr<float>(),
+                          static_cast<int>(ignore_index), stream());
+}
+
+void scale_bf16(Tensor x, Tensor scale) {
+  CHECK_CUDA(x); CHECK_CONTIG(x);
+  c10::cuda::CUDAGuard g(x.device());
+  qw::scale_bf16(bptr_mut(x), x.numel(), scale.data_ptr<float>(), stream());
+}
+
+// ------------------------------------------------------------------------------------------------ attention
+void flash_attn_fwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, int64_t B, int64_t S, int64_t Hq, int64_t Hkv,
+                    int64_t D, double scale) {
+  CHECK_CUDA(q); CHECK_ROWS(q); CHECK_ROWS(k); CHECK_ROWS(v); CHECK_ROWS(o);
+  TORCH_CHECK(q.stride(0) % 8 == 0 && k.stride(0) % 8 == 0 && v.stride(0) % 8 == 0 && o.stride(0) % 8 == 0,
+              "attention rows must be 16-byte aligned");
+  c10::cuda::CUDAGuard g(q.device());
+  qw::flash_attn_fwd(bptr(q), q.stride(0), bptr(k), k.stride(0), bptr(v), v.stride(0), bptr_mut(o), o.stride(0),
+                     lse.data_ptr<float>(), static_cast<int>(B), static_cast<int>(S), static_cast<int>(Hq),
+                     static_cast<int>(Hkv), static_cast<int>(D), static_cast<float>(scale), stream());
+}
+
+void flash_attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor dout, Tensor lse, Tensor delta, Tensor dq,
+                    Tensor dk, Tensor dv, int64_t B, int64_t S, int64_t Hq, int64_t Hkv, int64_t D, double scale) {
+  CHECK_CUDA(q); CHECK_ROWS(q); CHECK_ROWS(dout); CHECK_ROWS(dq); CHECK_ROWS(dk); CHECK_ROWS(dv);
+  c10::cuda::CUDAGuard g(q.device());
+  qw::flash_attn_bwd(bptr(q), q.stride(0), bptr(k), k.stride(0), bptr(v), v.stride(0), bptr(o), o.stride(0),
+                     bptr(dout), dout.stride(0), lse.data_ptr<float>(), delta.data_ptr<float>(), bptr_mut(dq),
+                     dq.stride(0), bptr_mut(dk), dk.stride(0), bptr_mut(dv), dv.stride(0), static_cast<int>(B),
+                     static_cast<int>(S), static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(D),
+                     static_cast<float>(scale), stream());
+}
+
+// ------------------------------------------------------------------------------------------------ status
+int64_t read_status(bool clear) {
+  int s = qw::gemm_status(clear);
+  int t;
+  if ((t = qw::norm_status(clear)) && !s) s = t;
+  if ((t = qw::routing_status(clear)) && !s) s = t;
+  if ((t = qw::optim_status(clear)) && !s) s = t;
+  if ((t = qw::attention_status(clear)) && !s) s = t;
+  return s;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "QuantaWeave-B200 sm_100a kernels";
+  m.def("linear_fwd", &linear_fwd);
+  m.def("linear_dgrad", &linear_dgrad);
+  m.def("linear_wgrad", &linear_wgrad);
+  m.def("moe_gate_up_fwd", &moe_gate_up_fwd);
+  m.def("moe_down_fwd", &moe_down_fwd);
+  m.def("moe_down_bwd", &moe_down_bwd);
+  m.def("moe_gate_up_dgrad", &moe_gate_up_dgrad);
+  m.def("moe_wgrad", &moe_wgrad, py::arg("a"), py::arg("b"), py::arg("counts"), py::arg("offsets"), py::arg("out"),
+        py::arg("accumulate"), py::arg("segments") = 1, py::arg("alpha") = 1.0);
+  m.def("moe_dw_tiles", [](int64_t F) { return static_cast<int64_t>(qw::moe_dw_tiles(F)); });
+  m.def("norm_fwd", &norm_fwd);
+  m.def("norm_bwd_blocks", &norm_bwd_blocks);
+  m.def("norm_bwd", &norm_bwd);
+  m.def("rope_apply", &rope_apply);
+  m.def("router_logits", &router_logits);
+  m.def("router_topk", &router_topk);
+  m.def("moe_plan_chunks", &moe_plan_chunks);
+  m.def("moe_plan", &moe_plan);
+  m.def("moe_permute", &moe_permute);
+  m.def("moe_pad_zero", &moe_pad_zero);
+  m.def("moe_gather_rows", &moe_gather_rows);
+  m.def("moe_combine", &moe_combine);
+  m.def("moe_combine_grad", &moe_combine_grad);
+  m.def("moe_route_dw", &moe_route_dw);
+  m.def("router_backward", &router_backward);
+  m.def("router_dx", &router_dx);
+  m.def("router_dw_split", &router_dw_split);
+  m.def("router_dw", &router_dw);
+  m.def("adam_chunk_size", &adam_chunk_size);
+  m.def("adam_grad_norm", &adam_grad_norm);
+  m.def("adam_sumsq", &adam_sumsq);
+  m.def("adam_step", &adam_step);
+  m.def("cross_entropy_chunk", &cross_entropy_chunk);
+  m.def("scale_bf16", &scale_bf16);
+  m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("read_status", &read_status, py::arg("clear") = true);
+}

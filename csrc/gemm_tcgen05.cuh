@@ -1,0 +1,529 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a (bf16 in, fp32 accumulate in TMEM).
+//
+//   C[m, n] = sum_k A[m, k] * B[n, k]        (A: M x K, B: N x K, either operand K-major or MN-major in memory)
+//
+// Roles (192 threads = 6 warps, one CTA per SM):
+//   warp 0     TMA producer: one elected thread streams A/B k-blocks (64 wide, 128-byte swizzle) into a ring of
+//              shared-memory stages, signalling `full[s]` with the transaction byte count.
+//   warp 1     MMA issuer: allocates 2 x BN TMEM columns (double-buffered accumulators), one thread issues
+//              tcgen05.mma (M=128, N=BN, K=16) and frees each stage with tcgen05.commit -> `empty[s]`; after the
+//              last k-block of a tile it commits `accum_full[b]`.
+//   warps 2-5  epilogue: tcgen05.ld the 128 x BN accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows),
+//              apply the fused epilogue and store to global memory, then release the buffer (`accum_empty[b]`).
+//
+// Tile schedules (device-side, no host synchronisation):
+//   kGroupM  grouped over rows: group g owns rows [row_off[g], row_off[g]+rows[g]) of A and C, and its own B
+//            (B row base g*b_group_rows). Forward expert GEMMs and their input gradients.
+//   kGroupK  grouped over the reduction: group g reduces over rows [row_off[g], ...+rows[g]) of both operands and
+//            writes its own C block (C + g*c_group_stride). Weight gradients (dW = dY^T X per expert).
+// Grouped row segments are padded to 128 rows with zero rows, so a tile never mixes two groups.
+//
+// Every mbarrier wait is bounded (see common.cuh); on a timeout all roles stop, in-flight TMA loads are drained
+// with a bounded wait, TMEM is freed and the kernel returns with qw_status set.
+#pragma once
+
+#include "common.cuh"
+
+namespace qw {
+namespace gemm {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kThreads = 192;
+
+enum Mode : int { kGroupM = 0, kGroupK = 1 };
+
+enum Epi : int {
+  kEpiStore = 0,      // C = alpha*acc (+bias[n]) (+residual[m,n]) (+C if accumulate); bf16 or fp32 out
+  kEpiSwiGLU = 1,     // acc = [gate(BN/2) | up(BN/2)] -> H = silu(g)*u ; optional raw GU store
+  kEpiSwiGLUBwd = 2,  // acc = dH (unweighted) ; reads GU, route weight w ; writes dGU, w*H, per-row <acc,H> partials
+};
+
+struct Params {
+  int M, N, K;                 // dense sizes (kGroupM: M unused; kGroupK: K unused)
+  int num_groups;
+  const int* group_rows;       // rows per group (kGroupM: M_g ; kGroupK: K_g)
+  const int* group_off;        // padded first row of each group
+  int b_group_rows;            // kGroupM: B row/K offset between groups
+  int expert_mod;              // >0: group g uses B block (g % expert_mod) (groups = (source, local expert) pairs)
+  int k_segments;              // kGroupK: each group reduces over this many row segments; segment s of group g uses
+                               // group_rows/group_off entry s*num_groups + g (1 = a single contiguous segment)
+  int dual_b_offset;           // >0: second half of each N tile comes from B rows + dual_b_offset (gate | up)
+  int n_tiles;                 // ceil(N / BN) (kEpiSwiGLU: ceil(F / (BN/2)))
+  int m_tiles;                 // kGroupK: ceil(M / 128)
+  int max_tiles;               // upper bound used when group sizes are device-side
+  // epilogue
+  void* out;
+  long ldo;
+  long out_group_stride;       // kGroupK: elements between group outputs
+  int out_fp32;
+  int accumulate;
+  float alpha;
+  const float* bias;
+  const __nv_bfloat16* residual;
+  long ldr;
+  int zero_pad_rows;           // write zeros into padded rows of a group's last tile
+  // SwiGLU
+  int ffn;                     // F
+  __nv_bfloat16* gu_out;       // kEpiSwiGLU: optional raw [gate|up] store, ld = 2F
+  const __nv_bfloat16* gu_in;  // kEpiSwiGLUBwd: saved/recomputed [gate|up], ld = 2F
+  const float* route_w;        // kEpiSwiGLUBwd: per-row route weight
+  __nv_bfloat16* h_out;        // kEpiSwiGLUBwd: optional H = silu(g)*u, ld = F
+  float* dw_partial;           // kEpiSwiGLUBwd: [rows, n_tiles] partial <dH_raw, H>
+};
+
+template <int BN>
+struct Smem {
+  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kDataBytes = kStages * kStageBytes;
+  static constexpr int kTotal = kDataBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct TileInfo {
+  int group;
+  int m_tile;
+  int n_tile;
+  int rows;      // valid rows of this tile (kGroupM) or K extent (kGroupK)
+  int row0;      // first A row (kGroupM) / first K row (kGroupK)
+  int num_kb;
+};
+
+template <int BN, int MODE>
+__device__ __forceinline__ bool tile_info(const Params& p, const int* s_prefix, int ngroups, int tile, TileInfo& t) {
+  if (MODE == kGroupM) {
+    if (tile >= s_prefix[ngroups]) return false;
+    int lo = 0, hi = ngroups - 1;
+    while (lo < hi) {  // last g with prefix[g] <= tile
+      int mid = (lo + hi + 1) >> 1;
+      if (s_prefix[mid] <= tile) lo = mid; else hi = mid - 1;
+    }
+    const int g = lo;
+    const int local = tile - s_prefix[g];
+    t.group = g;
+    t.m_tile = local / p.n_tiles;
+    t.n_tile = local % p.n_tiles;
+    const int grows = p.group_rows ? p.group_rows[g] : p.M;
+    const int goff = p.group_off ? p.group_off[g] : 0;
+    t.row0 = goff + t.m_tile * kBM;
+    t.rows = min(kBM, grows - t.m_tile * kBM);
+    t.num_kb = (p.K + kBK - 1) / kBK;
+  } else {
+    const int per_group = p.m_tiles * p.n_tiles;
+    if (tile >= per_group * ngroups) return false;
+    const int g = tile / per_group;
+    const int local = tile % per_group;
+    t.group = g;
+    t.m_tile = local / p.n_tiles;
+    t.n_tile = local % p.n_tiles;
+    if (p.k_segments > 1) {
+      int kb = 0;
+      for (int sgi = 0; sgi < p.k_segments; ++sgi) kb += (p.group_rows[sgi * ngroups + g] + kBK - 1) / kBK;
+      t.row0 = 0;
+      t.rows = 0;
+      t.num_kb = kb;
+    } else {
+      const int krows = p.group_rows ? p.group_rows[g] : p.K;
+      t.row0 = p.group_off ? p.group_off[g] : 0;
+      t.rows = krows;
+      t.num_kb = (krows + kBK - 1) / kBK;
+    }
+  }
+  return true;
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// epilogue: one thread = one accumulator row, 32 columns at a time
+// ---------------------------------------------------------------------------------------------------------
+template <int BN, int MODE, int EPI>
+__device__ __forceinline__ void epilogue_tile(const Params& p, const TileInfo& t, uint32_t tmem_acc, int row_in_tile,
+                                              int warp_lane_base) {
+  const bool empty_k = (t.num_kb == 0);
+  if (EPI == kEpiStore) {
+    long out_row;
+    bool row_ok, row_write;
+    if (MODE == kGroupM) {
+      out_row = t.row0 + row_in_tile;
+      row_ok = row_in_tile < t.rows;
+      row_write = row_ok || p.zero_pad_rows;
+    } else {
+      out_row = static_cast<long>(t.m_tile) * kBM + row_in_tile;
+      row_ok = out_row < p.M;
+      row_write = row_ok;
+    }
+    const int n0 = t.n_tile * BN;
+    char* base = static_cast<char*>(p.out);
+    if (MODE == kGroupK) base += static_cast<long>(t.group) * p.out_group_stride * (p.out_fp32 ? 4 : 2);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      if (!empty_k) {
+        tmem_ld32(tmem_acc + (static_cast<uint32_t>(warp_lane_base) << 16) + c, v);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      if (!row_write || n0 + c >= p.N) continue;
+      const bool full = (n0 + c + 32 <= p.N);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        float x = row_ok ? v[i] * p.alpha : 0.f;
+        if (row_ok && p.bias && (full || n0 + c + i < p.N)) x += p.bias[n0 + c + i];
+        v[i] = x;
+      }
+      if (row_ok && p.residual) {
+        const __nv_bfloat16* r = p.residual + out_row * p.ldr + n0 + c;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (full || n0 + c + i < p.N) v[i] += __bfloat162float(r[i]);
+      }
+      if (p.out_fp32) {
+        float* o = reinterpret_cast<float*>(base) + out_row * p.ldo + n0 + c;
+        if (full && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 w = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            if (p.accumulate) {
+              float4 old = *reinterpret_cast<float4*>(o + i);
+              w.x += old.x; w.y += old.y; w.z += old.z; w.w += old.w;
+            }
+            *reinterpret_cast<float4*>(o + i) = w;
+          }
+        } else {
+          for (int i = 0; i < 32; ++i)
+            if (n0 + c + i < p.N) o[i] = p.accumulate ? o[i] + v[i] : v[i];
+        }
+      } else {
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(base) + out_row * p.ldo + n0 + c;
+        if (full && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            if (p.accumulate) {
+              uint4 old = *reinterpret_cast<uint4*>(o + i);
+              const __nv_bfloat16* ob = reinterpret_cast<const __nv_bfloat16*>(&old);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[i + j] += __bfloat162float(ob[j]);
+            }
+            uint4 w;
+            w.x = pack_bf16(v[i], v[i + 1]);
+            w.y = pack_bf16(v[i + 2], v[i + 3]);
+            w.z = pack_bf16(v[i + 4], v[i + 5]);
+            w.w = pack_bf16(v[i + 6], v[i + 7]);
+            *reinterpret_cast<uint4*>(o + i) = w;
+          }
+        } else {
+          for (int i = 0; i < 32; ++i)
+            if (n0 + c + i < p.N) {
+              float x = v[i];
+              if (p.accumulate) x += __bfloat162float(o[i]);
+              o[i] = __float2bfloat16(x);
+            }
+        }
+      }
+    }
+  } else if (EPI == kEpiSwiGLU) {
+    // acc columns [0, BN/2) = gate, [BN/2, BN) = up for FFN columns f0 + [0, BN/2)
+    constexpr int HALF = BN / 2;
+    const long out_row = t.row0 + row_in_tile;
+    const bool row_ok = row_in_tile < t.rows;
+    const bool row_write = row_ok || p.zero_pad_rows;
+    const int f0 = t.n_tile * HALF;
+#pragma unroll 1
+    for (int c = 0; c < HALF; c += 32) {
+      float g[32], u[32];
+      tmem_ld32(tmem_acc + (static_cast<uint32_t>(warp_lane_base) << 16) + c, g);
+      tmem_ld32(tmem_acc + (static_cast<uint32_t>(warp_lane_base) << 16) + HALF + c, u);
+      if (!row_write || f0 + c >= p.ffn) continue;
+      const bool full = (f0 + c + 32 <= p.ffn);
+      __nv_bfloat16* h = static_cast<__nv_bfloat16*>(p.out) + out_row * p.ldo + f0 + c;
+      __nv_bfloat16* gu = p.gu_out ? p.gu_out + out_row * (2L * p.ffn) + f0 + c : nullptr;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w, wg, wu;
+          float hv[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) hv[j] = row_ok ? silu(g[i + j]) * u[i + j] : 0.f;
+          w.x = pack_bf16(hv[0], hv[1]); w.y = pack_bf16(hv[2], hv[3]);
+          w.z = pack_bf16(hv[4], hv[5]); w.w = pack_bf16(hv[6], hv[7]);
+          *reinterpret_cast<uint4*>(h + i) = w;
+          if (gu) {
+            const float zg = row_ok ? 1.f : 0.f;
+            wg.x = pack_bf16(zg * g[i], zg * g[i + 1]); wg.y = pack_bf16(zg * g[i + 2], zg * g[i + 3]);
+            wg.z = pack_bf16(zg * g[i + 4], zg * g[i + 5]); wg.w = pack_bf16(zg * g[i + 6], zg * g[i + 7]);
+            wu.x = pack_bf16(zg * u[i], zg * u[i + 1]); wu.y = pack_bf16(zg * u[i + 2], zg * u[i + 3]);
+            wu.z = pack_bf16(zg * u[i + 4], zg * u[i + 5]); wu.w = pack_bf16(zg * u[i + 6], zg * u[i + 7]);
+            *reinterpret_cast<uint4*>(gu + i) = wg;
+            *reinterpret_cast<uint4*>(gu + p.ffn + i) = wu;
+          }
+        }
+      } else {
+        for (int i = 0; i < 32; ++i) {
+          if (f0 + c + i >= p.ffn) break;
+          h[i] = __float2bfloat16(row_ok ? silu(g[i]) * u[i] : 0.f);
+          if (gu) {
+            gu[i] = __float2bfloat16(row_ok ? g[i] : 0.f);
+            gu[p.ffn + i] = __float2bfloat16(row_ok ? u[i] : 0.f);
+          }
+        }
+      }
+    }
+  } else {  // kEpiSwiGLUBwd
+    const long row = t.row0 + row_in_tile;
+    const bool row_ok = row_in_tile < t.rows;
+    const bool row_write = row_ok || p.zero_pad_rows;
+    const int f0 = t.n_tile * BN;
+    const float w = row_ok ? p.route_w[row] : 0.f;
+    float dot = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float a[32];
+      tmem_ld32(tmem_acc + (static_cast<uint32_t>(warp_lane_base) << 16) + c, a);
+      if (!row_write || f0 + c >= p.ffn) continue;
+      const int lim = min(32, p.ffn - (f0 + c));
+      const __nv_bfloat16* gp = p.gu_in + row * (2L * p.ffn) + f0 + c;
+      __nv_bfloat16* dg = static_cast<__nv_bfloat16*>(p.out) + row * (2L * p.ffn) + f0 + c;
+      __nv_bfloat16* hp = p.h_out ? p.h_out + row * static_cast<long>(p.ffn) + f0 + c : nullptr;
+      for (int i0 = 0; i0 < lim; i0 += 8) {
+        float gv[8], uv[8];
+        if (i0 + 8 <= lim) {
+          uint4 graw = *reinterpret_cast<const uint4*>(gp + i0);
+          uint4 uraw = *reinterpret_cast<const uint4*>(gp + p.ffn + i0);
+          const __nv_bfloat16* gb = reinterpret_cast<const __nv_bfloat16*>(&graw);
+          const __nv_bfloat16* ub = reinterpret_cast<const __nv_bfloat16*>(&uraw);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) { gv[j] = __bfloat162float(gb[j]); uv[j] = __bfloat162float(ub[j]); }
+        } else {
+          for (int j = 0; j < 8; ++j) {
+            gv[j] = (i0 + j < lim) ? __bfloat162float(gp[i0 + j]) : 0.f;
+            uv[j] = (i0 + j < lim) ? __bfloat162float(gp[p.ffn + i0 + j]) : 0.f;
+          }
+        }
+        float dgv[8], duv[8], hv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float sg = 1.f / (1.f + __expf(-gv[j]));
+          const float sl = gv[j] * sg;
+          hv[j] = sl * uv[j];
+          const float dh = row_ok ? w * a[i0 + j] : 0.f;
+          dot += row_ok ? a[i0 + j] * hv[j] : 0.f;
+          duv[j] = dh * sl;
+          dgv[j] = dh * uv[j] * (sg + sl * (1.f - sg));
+          hv[j] = row_ok ? w * hv[j] : 0.f;  // router-weighted H feeds the down-projection weight gradient
+        }
+        if (i0 + 8 <= lim) {
+          uint4 o1, o2;
+          o1.x = pack_bf16(dgv[0], dgv[1]); o1.y = pack_bf16(dgv[2], dgv[3]);
+          o1.z = pack_bf16(dgv[4], dgv[5]); o1.w = pack_bf16(dgv[6], dgv[7]);
+          o2.x = pack_bf16(duv[0], duv[1]); o2.y = pack_bf16(duv[2], duv[3]);
+          o2.z = pack_bf16(duv[4], duv[5]); o2.w = pack_bf16(duv[6], duv[7]);
+          *reinterpret_cast<uint4*>(dg + i0) = o1;
+          *reinterpret_cast<uint4*>(dg + p.ffn + i0) = o2;
+          if (hp) {
+            uint4 o3;
+            o3.x = pack_bf16(hv[0], hv[1]); o3.y = pack_bf16(hv[2], hv[3]);
+            o3.z = pack_bf16(hv[4], hv[5]); o3.w = pack_bf16(hv[6], hv[7]);
+            *reinterpret_cast<uint4*>(hp + i0) = o3;
+          }
+        } else {
+          for (int j = 0; j < 8 && i0 + j < lim; ++j) {
+            dg[i0 + j] = __float2bfloat16(dgv[j]);
+            dg[p.ffn + i0 + j] = __float2bfloat16(duv[j]);
+            if (hp) hp[i0 + j] = __float2bfloat16(hv[j]);
+          }
+        }
+      }
+    }
+    if (p.dw_partial && row_write) p.dw_partial[row * p.n_tiles + t.n_tile] = dot;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------------------------------------
+template <int BN, int MODE, int EPI, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p) {
+  using S = Smem<BN>;
+  constexpr int kStages = S::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kDataBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* teardown = acc_empty + 2;
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(teardown + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
+  __shared__ int s_prefix[1025];
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int ngroups = p.num_groups;
+
+  // group prefix (tiles before each group) for kGroupM
+  if (MODE == kGroupM && threadIdx.x == 0) {
+    int acc = 0;
+    for (int g = 0; g < ngroups; ++g) {
+      s_prefix[g] = acc;
+      const int rows = p.group_rows ? p.group_rows[g] : p.M;
+      acc += ((rows + kBM - 1) / kBM) * p.n_tiles;
+    }
+    s_prefix[ngroups] = min(acc, p.max_tiles);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(teardown, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) tmem_alloc(tmem_base_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued_phase[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) issued_phase[s] = -1;
+      TileInfo t;
+      for (int tile = blockIdx.x; !*abort_flag && tile_info<BN, MODE>(p, s_prefix, ngroups, tile, t);
+           tile += gridDim.x) {
+        for (int kb = 0; kb < t.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, kTimeoutEmpty)) { *abort_flag = 1; break; }
+          uint8_t* sa = smem + stage * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          mbar_arrive_expect_tx(&full[stage], S::kStageBytes);
+          issued_phase[stage] = static_cast<int>(phase);
+          if (MODE == kGroupM) {
+            const int k0 = kb * kBK;
+            if (!A_MN) {
+              tma_load_2d(sa, &map_a, &full[stage], k0, t.row0);
+            } else {
+              tma_load_2d(sa, &map_a, &full[stage], t.row0, k0);
+              tma_load_2d(sa + S::kABytes / 2, &map_a, &full[stage], t.row0 + 64, k0);
+            }
+            const int bgroup = p.expert_mod > 0 ? t.group % p.expert_mod : t.group;
+            if (!B_MN) {
+              const int brow = bgroup * p.b_group_rows;
+              if (p.dual_b_offset > 0) {
+                const int half = BN / 2;
+                tma_load_2d(sb, &map_b, &full[stage], k0, brow + t.n_tile * half);
+                tma_load_2d(sb + S::kBBytes / 2, &map_b, &full[stage], k0, brow + p.dual_b_offset + t.n_tile * half);
+              } else {
+                tma_load_2d(sb, &map_b, &full[stage], k0, brow + t.n_tile * BN);
+              }
+            } else {
+              const int krow = bgroup * p.b_group_rows + k0;
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_2d(sb + j * (kBK * 64 * 2), &map_b, &full[stage], t.n_tile * BN + 64 * j, krow);
+            }
+          } else {  // kGroupK: both operands MN-major, K = rows
+            int krow = t.row0 + kb * kBK;
+            if (p.k_segments > 1) {  // walk the segments to find the one holding k-block kb
+              int rem = kb;
+              for (int sgi = 0; sgi < p.k_segments; ++sgi) {
+                const int idx = sgi * ngroups + t.group;
+                const int nkb = (p.group_rows[idx] + kBK - 1) / kBK;
+                if (rem < nkb) { krow = p.group_off[idx] + rem * kBK; break; }
+                rem -= nkb;
+              }
+            }
+            tma_load_2d(sa, &map_a, &full[stage], t.m_tile * kBM, krow);
+            tma_load_2d(sa + S::kABytes / 2, &map_a, &full[stage], t.m_tile * kBM + 64, krow);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * (kBK * 64 * 2), &map_b, &full[stage], t.n_tile * BN + 64 * j, krow);
+          }
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      // drain: every stage this thread filled must have landed before the CTA may exit
+      for (int s = 0; s < kStages; ++s)
+        if (issued_phase[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(issued_phase[s]), kTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      TileInfo t;
+      for (int tile = blockIdx.x; !*abort_flag && tile_info<BN, MODE>(p, s_prefix, ngroups, tile, t);
+           tile += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, kTimeoutAccumFree)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < t.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, kTimeoutFull)) { *abort_flag = 1; ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
+          const uint32_t sb = sa + S::kABytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            uint64_t da, db;
+            if (!A_MN) da = smem_desc_sw128(sa + k * 32, 16, 1024);
+            else       da = smem_desc_sw128(sa + k * 2048, 8192, 1024);
+            if (!B_MN) db = smem_desc_sw128(sb + k * 32, 16, 1024);
+            else       db = smem_desc_sw128(sb + k * 2048, 8192, 1024);
+            umma_bf16(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        umma_commit(&acc_full[acc]);
+        if (!ok) break;
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      // all issued MMAs must finish before TMEM is released
+      umma_commit(teardown);
+      mbar_wait(teardown, 0, kTimeoutAccum);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int lane_base = 32 * (warp % 4);
+    const int row_in_tile = lane_base + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    TileInfo t;
+    for (int tile = blockIdx.x; tile_info<BN, MODE>(p, s_prefix, ngroups, tile, t); tile += gridDim.x) {
+      if (*abort_flag) break;
+      if (!mbar_wait(&acc_full[acc], acc_phase, kTimeoutAccum)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      epilogue_tile<BN, MODE, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, 2 * BN);
+}
+
+}  // namespace gemm
+}  // namespace qw

@@ -1,0 +1,120 @@
+// Raw-pointer launch API of the CUDA kernels (no torch types); bindings.cpp validates tensors and calls these.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <stdexcept>
+#include <string>
+
+namespace qw {
+
+using bf16 = __nv_bfloat16;
+
+inline void check_cuda(cudaError_t err, const char* what) {
+  if (err != cudaSuccess) throw std::runtime_error(std::string("CUDA error in ") + what + ": " + cudaGetErrorString(err));
+}
+
+// ---- gemm.cu (tcgen05) ----
+void linear_fwd(const bf16* x, int64_t ldx, const bf16* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                const float* bias, const bf16* residual, int64_t ldr, void* out, int64_t ldo, bool out_fp32,
+                cudaStream_t stream);
+void linear_dgrad(const bf16* dy, int64_t lddy, const bf16* w, int64_t ldw, int64_t M, int64_t N, int64_t K, void* dx,
+                  int64_t lddx, bool out_fp32, bool accumulate, cudaStream_t stream);
+void linear_wgrad(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int64_t T, int64_t N, int64_t K, void* dw,
+                  int64_t lddw, bool out_fp32, bool accumulate, cudaStream_t stream);
+// Grouped MoE GEMMs. `G` groups of rows (counts/offsets), group g uses expert weight block g % E (E = weight
+// stack size; G = sources * E for expert-parallel receive buffers).
+void moe_gate_up_fwd(const bf16* x, const bf16* w_gate_up, const int* counts, const int* offsets, int64_t R, int64_t G,
+                     int64_t E, int64_t H, int64_t F, bf16* h, bf16* gu, cudaStream_t stream);
+void moe_down_fwd(const bf16* h, const bf16* w_down, const int* counts, const int* offsets, int64_t R, int64_t G,
+                  int64_t E, int64_t H, int64_t F, bf16* y, cudaStream_t stream);
+void moe_down_bwd(const bf16* dy, const bf16* w_down, const int* counts, const int* offsets, int64_t R, int64_t G,
+                  int64_t E, int64_t H, int64_t F, const bf16* gu, const float* route_w, bf16* dgu, bf16* h_weighted,
+                  float* dw_partial, int dw_tiles, cudaStream_t stream);
+int moe_dw_tiles(int64_t F);
+void moe_gate_up_dgrad(const bf16* dgu, const bf16* w_gate_up, const int* counts, const int* offsets, int64_t R,
+                       int64_t G, int64_t E, int64_t H, int64_t F, bf16* dx, cudaStream_t stream);
+// out[e] (+)= sum over the `segments` row groups s*E + e of a^T b   (segments = sources in expert parallelism)
+void moe_wgrad(const bf16* a, const bf16* b, const int* counts, const int* offsets, int64_t R, int64_t E, int segments,
+               int64_t M, int64_t N, void* out, bool out_fp32, bool accumulate, float alpha, cudaStream_t stream);
+int gemm_status(bool clear);
+
+// ---- norm_rope.cu ----
+void norm_fwd(const bf16* x, const bf16* delta, bf16* x_out, const float* w, const float* b, bf16* y, float* mean,
+              float* rstd, int64_t rows, int H, float eps, bool rms, cudaStream_t stream);
+int norm_bwd_blocks(int64_t rows);
+void norm_bwd(const bf16* dy, const bf16* x, const float* w, const float* mean, const float* rstd, const bf16* dres,
+              bf16* dx, float* dw_part, float* db_part, float* dw, float* db, int64_t rows, int H, bool rms,
+              bool accumulate, cudaStream_t stream);
+void rope_apply(bf16* qkv, int64_t rows, int heads_rot, int D, int64_t ld, int seq, const int* positions,
+                const float* cos_t, const float* sin_t, bool inverse, cudaStream_t stream);
+int norm_status(bool clear);
+
+// ---- moe_routing.cu ----
+void router_logits(const bf16* x, const float* w, int64_t T, int H, int E, float* logits, cudaStream_t stream);
+void router_topk(const float* logits, const float* bias, int64_t T, int E, int k, float temperature, float* probs,
+                 int* top_idx, float* top_w, int* counts, cudaStream_t stream);
+int moe_plan_chunks(int64_t routes);
+void moe_plan(const int* top_idx, const float* top_w, const int* counts, int64_t routes, int E, int cap, int slot_rows,
+              int* kept, int* offsets, int* uoffsets, int* meta, int* chunk_hist, int* sorted_routes, int* route_row,
+              cudaStream_t stream);
+void moe_permute(const bf16* x, int64_t routes, int k, int H, const int* route_row, const float* top_w, const int* kept,
+                 const int* offsets, int E, bf16* x_perm, int* row_token, float* row_w, cudaStream_t stream);
+void moe_pad_zero(const int* kept, const int* offsets, int E, int H, bf16* buf, cudaStream_t stream);
+void moe_gather_rows(const bf16* src, const int* row_token, const int* meta, int64_t max_rows, int H, bf16* dst,
+                     cudaStream_t stream);
+void moe_combine(const bf16* y, const int* route_row, const float* top_w, const bf16* resid, int64_t T, int k, int H,
+                 bf16* out, cudaStream_t stream);
+void moe_combine_grad(const bf16* dx_perm, const int* route_row, const float* extra, int64_t T, int k, int H, bf16* dx,
+                      cudaStream_t stream);
+void moe_route_dw(const float* partial, int tiles, const int* route_row, int64_t routes, float* d_w,
+                  cudaStream_t stream);
+void router_backward(const float* probs, const int* top_idx, const float* top_w, const float* d_w,
+                     const float* d_probs_ext, int64_t T, int E, int k, float temperature, float* d_logits,
+                     cudaStream_t stream);
+void router_dx(const float* d_logits, const float* w, int64_t T, int E, int H, float* dx, cudaStream_t stream);
+int router_dw_split(int64_t T);
+void router_dw(const float* d_logits, const bf16* x, int64_t T, int E, int H, float* dw, bool accumulate,
+               float* workspace, cudaStream_t stream);
+int routing_status(bool clear);
+
+// ---- optim_ce.cu ----
+struct AdamTensor {
+  void* param;         // bf16 (with master) or fp32 (updated in place)
+  const void* grad;    // fp32 (grad_dtype 0) or bf16 (grad_dtype 1)
+  float* master;       // fp32 master copy, or nullptr when the parameter itself is fp32
+  float* exp_avg;
+  float* exp_avg_sq;
+  int64_t numel;
+  int grad_dtype;
+  float decay_scale;   // 1 = apply weight decay, 0 = exempt
+  float grad_scale;    // multiplies the stored gradient (e.g. 1/ep for expert gradients summed over ranks)
+  int reserved;        // keeps the record at 64 bytes (mirrored by the Python table builder)
+};
+struct AdamHyper {
+  float lr, beta1, beta2, eps, weight_decay, bias_correction1, bias_correction2_sqrt;
+};
+int adam_chunk_size();
+void adam_grad_norm(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
+                    double* partial, const double* extra_sumsq, float max_norm, float* norm_out, cudaStream_t stream);
+void adam_sumsq(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
+                double* partial, cudaStream_t stream);
+void adam_step(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
+               const AdamHyper& hyper, const float* clip, cudaStream_t stream);
+void cross_entropy_chunk(bf16* logits, int64_t rows, int64_t ld, int V, const int64_t* labels, float grad_scale,
+                         float* loss_out, int ignore_index, cudaStream_t stream);
+void scale_bf16(bf16* x, int64_t n, const float* scale, cudaStream_t stream);
+int optim_status(bool clear);
+
+// ---- attention.cu ----
+void flash_attn_fwd(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv, bf16* o,
+                    int64_t ldo, float* lse, int B, int S, int Hq, int Hkv, int D, float scale, cudaStream_t stream);
+void flash_attn_bwd(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv, const bf16* o,
+                    int64_t ldo, const bf16* dout, int64_t lddo, const float* lse, float* delta, bf16* dq,
+                    int64_t lddq, bf16* dk, int64_t lddk, bf16* dv, int64_t lddv, int B, int S, int Hq, int Hkv, int D,
+                    float scale, cudaStream_t stream);
+int attention_status(bool clear);
+
+}  // namespace qw

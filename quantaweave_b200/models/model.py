@@ -46,7 +46,13 @@ class QuantaWeaveBlock(nn.Module):
         del tp_rank
 
     def forward(self, hidden: Tensor, token_domains: Optional[Tensor] = None, num_domains: int = 0):
-        hidden = hidden + self.attention(self.attention_norm(hidden))
+        if hidden.is_cuda and type(self.attention) is Attention:
+            from ..ops.attention import self_attention
+
+            # residual add fused into the output-projection GEMM epilogue
+            hidden = self_attention(self.attention, self.attention_norm(hidden), residual=hidden)
+        else:
+            hidden = hidden + self.attention(self.attention_norm(hidden))
         moe_out, balance, dropped, overflow, domain = self.moe(self.moe_norm(hidden), token_domains, num_domains)
         return hidden + moe_out, balance, dropped, overflow, domain
 
@@ -163,7 +169,9 @@ class QuantaWeaveMoEForCausalLM(nn.Module):
         if normed.is_cuda:
             from ..ops import cross_entropy as ce_ops
 
-            return ce_ops.linear_cross_entropy(normed[:, :-1], self.lm_head.weight, labels[:, 1:])
+            # every position is scored against the next token; the last one has none (ignore index)
+            shifted = torch.cat([labels[:, 1:], labels.new_full((labels.size(0), 1), ce_ops.IGNORE_INDEX)], dim=1)
+            return ce_ops.linear_cross_entropy(normed, self.lm_head.weight, shifted)
         logits = self.lm_head(normed)
         return F.cross_entropy(logits[:, :-1].reshape(-1, logits.size(-1)), labels[:, 1:].reshape(-1))
 

@@ -127,6 +127,7 @@ class TopKMoE(nn.Module):
         self.expert_bias: Optional[Tensor] = None     # straggler-aware routing, selection only
         self.capacity_scale: float = 1.0
         self.simulated_cost_per_row: float = 0.0
+        self.recompute_activations = False           # native path: recompute gate/up in backward instead of saving
         self.expert_seconds = [0.0] * self.num_local_experts
         self.last_top_indices: Optional[Tensor] = None
         self.last_stats: dict[str, Tensor] = {}
@@ -183,6 +184,7 @@ class TopKMoE(nn.Module):
         if hidden.is_cuda and self._native_ok():
             from ..ops import moe as moe_ops
 
+            self._last_counts = None
             output, probs, top_indices, overflow, kept_counts, dropped = moe_ops.moe_forward(self, flat, self.capacity(num_tokens))
             self.last_top_indices = top_indices.detach()
             if self.collect_stats:
@@ -200,15 +202,20 @@ class TopKMoE(nn.Module):
                     self._record_stats(probs, top_indices, kept_counts, dropped)
         zero = torch.zeros((), device=hidden.device, dtype=torch.long)
         dropped_routes = overflow if self.overflow_policy == "drop" else zero
-        balance_loss = self.balance_loss(probs, top_indices)
+        counts = getattr(self, "_last_counts", None) if hidden.is_cuda else None
+        balance_loss = self.balance_loss(probs, top_indices, counts)
         domain_loss = probs.new_zeros(())
         if token_domains is not None and num_domains > 1:
             domain_loss = self._domain_loss(probs, token_domains, num_domains)
         return output.reshape(batch, sequence, width), balance_loss, dropped_routes, overflow, domain_loss
 
-    def balance_loss(self, probs: Tensor, top_indices: Tensor) -> Tensor:
+    def balance_loss(self, probs: Tensor, top_indices: Tensor, counts: Optional[Tensor] = None) -> Tensor:
+        """``E * sum(mean(probs) * share of routes per expert)``; ``counts`` (the router kernel's per-expert route
+        counts) avoids a bincount, which synchronises with the host on CUDA."""
         importance = probs.mean(dim=0)
-        assignments = torch.bincount(top_indices.reshape(-1), minlength=self.num_experts).float() / top_indices.numel()
+        if counts is None:
+            counts = torch.bincount(top_indices.reshape(-1), minlength=self.num_experts)
+        assignments = counts.float() / top_indices.numel()
         return self.num_experts * (importance * assignments).sum()
 
     def _native_ok(self) -> bool:

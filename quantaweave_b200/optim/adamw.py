@@ -1,0 +1,189 @@
+"""Fused multi-tensor AdamW for CUDA parameters.
+
+* bf16 parameters get an fp32 master copy; fp32 parameters are updated in place.
+* One kernel computes the global gradient norm (fixed-order fp64 reduction, deterministic); the clip coefficient
+  stays on the device and is folded into the single fused update kernel that walks every parameter.
+* The update matches ``torch.optim.AdamW`` (decoupled weight decay, bias-corrected moments).
+
+State is kept as the usual ``self.state[p]`` dict (``step``, ``exp_avg``, ``exp_avg_sq`` and ``master`` for bf16
+parameters), always in fp32; ``state_dict``/``load_state_dict`` preserve those dtypes.
+"""
+
+from __future__ import annotations
+
+from typing import Iterable, Optional
+
+import torch
+from torch import Tensor
+
+from ..ops import ext
+
+
+class FusedAdamW(torch.optim.Optimizer):
+    def __init__(self, params: Iterable, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 1e-2, moment_bits: int = 32) -> None:
+        if moment_bits != 32:
+            raise NotImplementedError("8-bit moments are not implemented by the fused optimizer yet")
+        super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
+        self._chunk = None
+        self._clip: Optional[Tensor] = None
+        # per-parameter factor applied to the stored gradient inside the fused kernels (norm and update), e.g.
+        # 1/ep for expert gradients that the expert-parallel backward sums over every rank's tokens
+        self.grad_scale: dict = {}
+        self._norm_buf: Optional[Tensor] = None
+
+    # ---- state -----------------------------------------------------------------------------------
+    def _init_state(self, p: Tensor) -> dict:
+        state = self.state[p]
+        if "exp_avg" not in state:
+            state["step"] = 0
+            state["exp_avg"] = torch.zeros(p.shape, device=p.device, dtype=torch.float32)
+            state["exp_avg_sq"] = torch.zeros(p.shape, device=p.device, dtype=torch.float32)
+            if p.dtype != torch.float32:
+                state["master"] = p.detach().float().contiguous()
+        return state
+
+    def _params(self):
+        for group in self.param_groups:
+            for p in group["params"]:
+                yield group, p
+
+    def _build_tables(self, params: list[Tensor], device) -> tuple[Tensor, Tensor, Tensor]:
+        """AdamTensor records (8 x int64 each) and the chunk -> (tensor, start) map."""
+        C = ext()
+        chunk = C.adam_chunk_size()
+        rows, chunk_tensor, chunk_start = [], [], []
+        for index, p in enumerate(params):
+            st = self.state[p]
+            g = p.grad
+            grad_dtype = 0 if g.dtype == torch.float32 else 1
+            import struct
+
+            tail = struct.unpack("<q", struct.pack("<if", grad_dtype, float(st["decay_scale"])))[0]
+            scale = struct.unpack("<q", struct.pack("<fi", float(self.grad_scale.get(p, 1.0)), 0))[0]
+            rows.append([p.data_ptr(), g.data_ptr(), st["master"].data_ptr() if "master" in st else 0,
+                         st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr(), p.numel(), tail, scale])
+            for start in range(0, p.numel(), chunk):
+                chunk_tensor.append(index)
+                chunk_start.append(start)
+        table = torch.tensor(rows, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+        ct = torch.tensor(chunk_tensor, dtype=torch.int32).pin_memory().to(device, non_blocking=True)
+        cs = torch.tensor(chunk_start, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+        return table, ct, cs
+
+    def _live(self):
+        out = []
+        for group, p in self._params():
+            if p.grad is None:
+                continue
+            if not p.grad.is_contiguous():
+                p.grad = p.grad.contiguous()
+            st = self._init_state(p)
+            st["decay_scale"] = 1.0
+            out.append((group, p))
+        return out
+
+    # ---- clipping --------------------------------------------------------------------------------
+    @torch.no_grad()
+    def clip_grad_norm_(self, max_norm: float, extra_sumsq: Optional[Tensor] = None) -> Tensor:
+        """Global L2 norm of all gradients (plus ``extra_sumsq`` from other ranks' shards); the clip coefficient is
+        applied inside the next ``step()``. Returns the norm as a 0-d device tensor."""
+        C = ext()
+        live = self._live()
+        if not live:
+            return torch.zeros(())
+        params = [p for _, p in live]
+        device = params[0].device
+        table, ct, cs = self._build_tables(params, device)
+        partial = torch.empty(max(1, ct.numel()), device=device, dtype=torch.float64)
+        norm = torch.empty(2, device=device, dtype=torch.float32)
+        C.adam_grad_norm(table, ct, cs, partial, extra_sumsq, float(max_norm), norm)
+        self._clip = norm
+        return norm[0]
+
+    @torch.no_grad()
+    def grad_sumsq(self, subset: Optional[Iterable[Tensor]] = None) -> Tensor:
+        """Sum of squared (scaled) gradients as an fp64 device scalar, over all parameters or ``subset``; used for
+        norms that combine several ranks."""
+        C = ext()
+        live = self._live()
+        params = [p for _, p in live]
+        if subset is not None:
+            wanted = {id(p) for p in subset}
+            params = [p for p in params if id(p) in wanted]
+        if not params:
+            return torch.zeros((), dtype=torch.float64)
+        table, ct, cs = self._build_tables(params, params[0].device)
+        partial = torch.empty(max(1, ct.numel()), device=params[0].device, dtype=torch.float64)
+        C.adam_sumsq(table, ct, cs, partial)
+        return partial.sum()
+
+    def set_clip_coefficient(self, coef: Tensor, norm: Optional[Tensor] = None) -> None:
+        """Use an externally computed clip coefficient (device scalar) in the next step."""
+        n = norm.float().reshape(()) if norm is not None else torch.zeros((), device=coef.device)
+        self._clip = torch.stack([n, coef.float().reshape(())])
+
+    # ---- step ------------------------------------------------------------------------------------
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = closure() if closure is not None else None
+        C = ext()
+        live = self._live()
+        by_group: dict[int, list[Tensor]] = {}
+        for group, p in live:
+            by_group.setdefault(id(group), []).append(p)
+        for group in self.param_groups:
+            params = by_group.get(id(group), [])
+            if not params:
+                continue
+            steps = {self.state[p]["step"] for p in params}
+            for p in params:
+                self.state[p]["step"] += 1
+            if len(steps) != 1:  # parameters that joined late: step them one group at a time per step count
+                for p in params:
+                    self._step_tensors([p], group, self.state[p]["step"])
+            else:
+                self._step_tensors(params, group, steps.pop() + 1)
+        self._clip = None
+        return loss
+
+    def _step_tensors(self, params: list[Tensor], group: dict, step: int) -> None:
+        C = ext()
+        table, ct, cs = self._build_tables(params, params[0].device)
+        beta1, beta2 = group["betas"]
+        C.adam_step(table, ct, cs, float(group["lr"]), float(beta1), float(beta2), float(group["eps"]),
+                    float(group["weight_decay"]), int(step), self._clip)
+
+    # ---- checkpoints -----------------------------------------------------------------------------
+    def state_dict(self) -> dict:
+        index = {}
+        groups = []
+        for group in self.param_groups:
+            ids = []
+            for p in group["params"]:
+                index.setdefault(id(p), len(index))
+                ids.append(index[id(p)])
+            groups.append({k: v for k, v in group.items() if k != "params"} | {"params": ids})
+        state = {}
+        for group in self.param_groups:
+            for p in group["params"]:
+                if p in self.state and "exp_avg" in self.state[p]:
+                    st = self.state[p]
+                    state[index[id(p)]] = {k: v for k, v in st.items() if k != "decay_scale"}
+        return {"state": state, "param_groups": groups}
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        params = [p for group in self.param_groups for p in group["params"]]
+        for group, saved in zip(self.param_groups, state_dict["param_groups"]):
+            for key, value in saved.items():
+                if key != "params":
+                    group[key] = value
+        for idx, st in state_dict["state"].items():
+            p = params[int(idx)]
+            new = {"step": int(st["step"])}
+            for key in ("exp_avg", "exp_avg_sq", "master"):
+                if key in st:
+                    new[key] = st[key].to(device=p.device, dtype=torch.float32).contiguous()
+            if p.dtype != torch.float32 and "master" not in new:
+                new["master"] = p.detach().float().contiguous()
+            self.state[p] = new

@@ -1,0 +1,567 @@
+"""Expert parallelism (optionally with tensor parallelism) on one node.
+
+API and semantics follow the reference ``src/expert_parallel.py``: ranks form a grid
+``global_rank = ep_rank * T + tp_rank`` (:69-101); experts are sharded over the expert-parallel group; capacity is
+enforced per *source* rank on its local batch (:14); replicated gradients are averaged over the expert group and
+expert gradients are scaled by ``1/ep`` (:203-224); clipping uses the true global norm (:227-260); the straggler
+controller biases routers away from slow ranks (:280-384).
+
+B200 native path (``_SlotDispatch``): each source rank plans capacity on the device into FIXED slots
+(expert ``e`` at rows ``e * slot``, ``slot = roundup(capacity, 128)``), so the dispatch and the combine are even
+exchanges whose sizes never need a host synchronisation. The receiving rank sees a ``[source, local expert, slot]``
+buffer and runs the grouped tcgen05 SwiGLU GEMMs over ``source x local-expert`` groups (group ``g`` uses expert
+``g % local``); weight gradients reduce each expert over the per-source segments inside one GEMM. The exchange
+itself is pluggable: NCCL ``all_to_all_single`` (the baseline) or the fused peer-memory transport in
+``parallel.p2p`` (in-kernel NVLink stores into the peer's receive slots).
+
+The CPU (gloo) path keeps the reference's algorithm with uneven differentiable all-to-alls; it is the oracle the
+multi-process tests compare against single-device training.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import time
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from ..config import QuantaWeaveConfig
+from ..models.moe import TopKMoE
+
+
+@dataclass
+class ExpertParallelContext:
+    rank: int
+    world_size: int
+    device: torch.device
+    group: Optional[object] = None
+    owns_process_group: bool = False
+    tp_rank: int = 0
+    tp_size: int = 1
+    tp_group: Optional[object] = None
+    global_rank: int = -1
+    global_size: int = -1
+    transport: str = "nccl"          # native dispatch: "nccl" (all_to_all) or "p2p" (fused peer stores)
+
+    def __post_init__(self) -> None:
+        if self.global_size < 0:
+            self.global_size = self.world_size * self.tp_size
+        if self.global_rank < 0:
+            self.global_rank = self.rank * self.tp_size + self.tp_rank
+
+    def layout(self) -> dict:
+        return {"kind": "ep", "ep_rank": self.rank, "ep_size": self.world_size, "tp_rank": self.tp_rank,
+                "tp_size": self.tp_size}
+
+    @property
+    def group_root(self) -> int:
+        return dist.get_global_rank(self.group, 0) if self.group is not None else 0
+
+
+def init_expert_parallel(device_arg: str = "auto", tensor_parallel: int = 1,
+                         transport: Optional[str] = None) -> ExpertParallelContext:
+    """Join (or create) the process group from torchrun's environment and build the EP x TP grid."""
+    from .groups import ensure_process_group
+
+    owns, device = ensure_process_group(device_arg)
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if tensor_parallel < 1 or world % tensor_parallel:
+        raise ValueError(f"world size {world} is not divisible by --tensor-parallel {tensor_parallel}")
+    ep_size = world // tensor_parallel
+    ep_rank, tp_rank = divmod(rank, tensor_parallel)
+    ep_group = tp_group = None
+    if tensor_parallel > 1:
+        for column in range(tensor_parallel):
+            g = dist.new_group([row * tensor_parallel + column for row in range(ep_size)])
+            ep_group = g if column == tp_rank else ep_group
+        for row in range(ep_size):
+            g = dist.new_group([row * tensor_parallel + column for column in range(tensor_parallel)])
+            tp_group = g if row == ep_rank else tp_group
+    transport = transport or os.environ.get("QW_EP_TRANSPORT", "nccl")
+    return ExpertParallelContext(ep_rank, ep_size, device, ep_group, owns, tp_rank, tensor_parallel, tp_group, rank,
+                                 world, transport)
+
+
+# ------------------------------------------------------------------------------------------ reference-style exchange
+class _AllToAll(torch.autograd.Function):
+    """Uneven all_to_all_single whose backward is the reverse exchange (CPU / gloo oracle path)."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, in_splits: list, out_splits: list, group):
+        ctx.in_splits, ctx.out_splits, ctx.group = in_splits, out_splits, group
+        x = x.contiguous()
+        out = x.new_empty((sum(out_splits),) + tuple(x.shape[1:]))
+        dist.all_to_all_single(out, x, out_splits, in_splits, group=group)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad: Tensor):
+        grad = grad.contiguous()
+        out = grad.new_empty((sum(ctx.in_splits),) + tuple(grad.shape[1:]))
+        dist.all_to_all_single(out, grad, ctx.in_splits, ctx.out_splits, group=ctx.group)
+        return out, None, None, None
+
+
+def _even_exchange(x: Tensor, group) -> Tensor:
+    out = torch.empty_like(x)
+    dist.all_to_all_single(out, x.contiguous(), group=group)
+    return out
+
+
+# ------------------------------------------------------------------------------------------ native slot dispatch
+class _SlotDispatch(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x: Tensor, router_weight: Tensor, w_gate_up: Tensor, w_down: Tensor, moe: "ExpertParallelMoE",
+                capacity: int):
+        from ..ops import ext
+        from ..ops.moe import route
+
+        C = ext()
+        ep = moe.context
+        world, local = ep.world_size, moe.num_local_experts
+        T, H = x.shape
+        E = moe.num_experts
+        F2 = w_gate_up.size(1)
+        F = F2 // 2
+        k = moe.top_k
+        dev = x.device
+        slot = (capacity + 127) // 128 * 128
+        x = x.to(torch.bfloat16).contiguous()
+        plan = route(x, router_weight, k, capacity, float(moe.router_temperature), moe.expert_bias, slot_rows=slot)
+        rows = E * slot
+        send = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+        row_token = torch.full((rows,), -1, device=dev, dtype=torch.int32)
+        row_w = torch.zeros(rows, device=dev, dtype=torch.float32)
+        C.moe_permute(x, k, plan.route_row, plan.top_w, plan.kept, plan.offsets, send, row_token, row_w)
+        transport = moe.transport()
+        recv_counts = transport.exchange_counts(plan.kept)            # [world * local] (source-major)
+        x_recv = transport.exchange(send)                             # [world * local * slot, H]
+        w_recv = transport.exchange(row_w)
+        offsets = moe.recv_offsets(slot, dev)
+        h = torch.empty(rows, F, device=dev, dtype=torch.bfloat16)
+        gu = None if moe.recompute_activations else torch.empty(rows, F2, device=dev, dtype=torch.bfloat16)
+        C.moe_gate_up_fwd(x_recv, w_gate_up, recv_counts, offsets, h, gu)
+        y = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+        C.moe_down_fwd(h, w_down, recv_counts, offsets, y)
+        del h
+        y_back = transport.exchange(y)
+        out = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+        C.moe_combine(y_back, plan.route_row, plan.top_w, None, k, out)
+        saved = [x, router_weight, w_gate_up, w_down, plan.probs, plan.top_idx, plan.top_w, plan.meta, plan.route_row,
+                 row_token, recv_counts, offsets, x_recv, w_recv]
+        if gu is not None:
+            saved.append(gu)
+        ctx.save_for_backward(*saved)
+        ctx.moe, ctx.slot = moe, slot
+        ctx.mark_non_differentiable(plan.top_idx, plan.counts, plan.kept, plan.meta, plan.route_row)
+        return out, plan.probs, plan.top_idx, plan.counts, plan.kept, plan.meta, plan.route_row
+
+    @staticmethod
+    def backward(ctx, d_out, d_probs, *_):
+        from ..ops import ext
+
+        C = ext()
+        moe, slot = ctx.moe, ctx.slot
+        saved = ctx.saved_tensors
+        (x, router_weight, w_gate_up, w_down, probs, top_idx, top_w, meta, route_row, row_token, recv_counts, offsets,
+         x_recv, w_recv) = saved[:14]
+        gu = saved[14] if len(saved) > 14 else None
+        ep = moe.context
+        world, local = ep.world_size, moe.num_local_experts
+        T, H = x.shape
+        F2 = w_gate_up.size(1)
+        F = F2 // 2
+        k = moe.top_k
+        dev = x.device
+        rows = x_recv.size(0)
+        transport = moe.transport()
+        if d_out is None:
+            d_out = torch.zeros(T, H, device=dev, dtype=torch.bfloat16)
+        d_out = d_out.to(torch.bfloat16).contiguous()
+        dy_send = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+        C.moe_gather_rows(d_out, row_token, meta, dy_send)
+        dy_recv = transport.exchange(dy_send)
+        del dy_send
+        if gu is None:
+            gu = torch.empty(rows, F2, device=dev, dtype=torch.bfloat16)
+            scratch = torch.empty(rows, F, device=dev, dtype=torch.bfloat16)
+            C.moe_gate_up_fwd(x_recv, w_gate_up, recv_counts, offsets, scratch, gu)
+            del scratch
+        tiles = C.moe_dw_tiles(F)
+        dgu = torch.empty(rows, F2, device=dev, dtype=torch.bfloat16)
+        hw = torch.empty(rows, F, device=dev, dtype=torch.bfloat16)
+        partial = torch.zeros(rows, tiles, device=dev, dtype=torch.float32)
+        C.moe_down_bwd(dy_recv, w_down, recv_counts, offsets, gu, w_recv, dgu, hw, partial)
+        del gu
+        d_w_down = torch.empty_like(w_down)
+        C.moe_wgrad(dy_recv, hw, recv_counts, offsets, d_w_down, False, world, 1.0)
+        del hw, dy_recv
+        d_w_gate_up = torch.empty_like(w_gate_up)
+        C.moe_wgrad(dgu, x_recv, recv_counts, offsets, d_w_gate_up, False, world, 1.0)
+        dx_recv = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+        C.moe_gate_up_dgrad(dgu, w_gate_up, recv_counts, offsets, dx_recv)
+        del dgu
+        dx_send = transport.exchange(dx_recv)
+        partial_back = transport.exchange(partial)
+        d_w = torch.empty(T * k, device=dev, dtype=torch.float32)
+        C.moe_route_dw(partial_back, route_row, d_w)
+        d_logits = torch.empty_like(probs)
+        dp = d_probs.float().contiguous() if d_probs is not None else None
+        C.router_backward(probs, top_idx, top_w, d_w, dp, float(moe.router_temperature), d_logits)
+        rw = router_weight.float().contiguous()
+        dx_router = torch.empty(T, H, device=dev, dtype=torch.float32)
+        C.router_dx(d_logits, rw, dx_router)
+        split = C.router_dw_split(T)
+        workspace = torch.empty(split * moe.num_experts * H if split > 1 else 1, device=dev, dtype=torch.float32)
+        d_router = torch.empty(moe.num_experts, H, device=dev, dtype=torch.float32)
+        C.router_dw(d_logits, x, d_router, False, workspace)
+        dx = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
+        C.moe_combine_grad(dx_send, route_row, dx_router, k, dx)
+        del local
+        return dx, d_router.to(router_weight.dtype), d_w_gate_up, d_w_down, None, None
+
+
+class NcclTransport:
+    """Even exchanges over NCCL ``all_to_all_single`` (the baseline the fused P2P transport replaces)."""
+
+    def __init__(self, group) -> None:
+        self.group = group
+
+    def exchange_counts(self, kept: Tensor) -> Tensor:
+        return _even_exchange(kept, self.group)
+
+    def exchange(self, t: Tensor) -> Tensor:
+        return _even_exchange(t, self.group)
+
+
+class ExpertParallelMoE(TopKMoE):
+    def __init__(self, config: QuantaWeaveConfig, context: ExpertParallelContext) -> None:
+        if config.num_experts % context.world_size:
+            raise ValueError(f"num_experts {config.num_experts} must be divisible by the expert-parallel size "
+                             f"{context.world_size}")
+        super().__init__(config, num_local_experts=config.num_experts // context.world_size, tensor_parallel=context)
+        self.context = context
+        self.measure_load = False
+        self.load_rows = 0
+        self.load_seconds = 0.0
+        self._offsets_cache: dict = {}
+        self._transport = None
+
+    def transport(self):
+        if self._transport is None:
+            if self.context.transport == "p2p":
+                from .p2p import P2PTransport
+
+                self._transport = P2PTransport.for_group(self.context.group, self.context.device)
+            else:
+                self._transport = NcclTransport(self.context.group)
+        return self._transport
+
+    def recv_offsets(self, slot: int, device) -> Tensor:
+        key = (slot, str(device))
+        if key not in self._offsets_cache:
+            groups = self.context.world_size * self.num_local_experts
+            self._offsets_cache[key] = torch.arange(groups, device=device, dtype=torch.int32) * slot
+        return self._offsets_cache[key]
+
+    def forward(self, hidden: Tensor, token_domains: Optional[Tensor] = None, num_domains: int = 0):
+        if not (hidden.is_cuda and self.kernel != "loop" and self.tp_size == 1 and not self.static_dispatch
+                and not self.profile_experts and not self.simulated_cost_per_row and not self.measure_load):
+            return super().forward(hidden, token_domains, num_domains)
+        from ..ops import native_required
+
+        native_required()
+        batch, seq, width = hidden.shape
+        flat = hidden.reshape(-1, width)
+        cap = self.capacity(flat.size(0))
+        out, probs, top_idx, counts, kept, meta, route_row = _SlotDispatch.apply(
+            flat, self.router.weight, self.w_gate_up, self.w_down, self, cap)
+        self.last_top_indices = top_idx.detach().long()
+        if self.collect_stats:
+            from ..ops.moe import _Dropped
+
+            self._record_stats(probs, top_idx.long(), kept, _Dropped(route_row, top_idx, self.top_k))
+        overflow = meta[1].long()
+        zero = torch.zeros((), device=hidden.device, dtype=torch.long)
+        dropped = overflow if self.overflow_policy == "drop" else zero
+        balance = self.balance_loss(probs, top_idx, counts)
+        domain = probs.new_zeros(())
+        if token_domains is not None and num_domains > 1:
+            domain = self._domain_loss(probs, token_domains, num_domains)
+        return out.reshape(batch, seq, width).to(hidden.dtype), balance, dropped, overflow, domain
+
+    # ---- reference algorithm (CPU / gloo, and the profiling/straggler paths) ----
+    def _execute(self, flat_hidden: Tensor, tokens: Tensor, weights: Tensor, kept_counts: Tensor) -> Tensor:
+        ctx, group = self.context, self.context.group
+        world, local = ctx.world_size, self.num_local_experts
+        counts = kept_counts.tolist()
+        send_splits = [sum(counts[r * local:(r + 1) * local]) for r in range(world)]
+        recv_counts = torch.empty_like(kept_counts)
+        dist.all_to_all_single(recv_counts, kept_counts.contiguous(), group=group)
+        per_source = recv_counts.reshape(world, local).tolist()
+        recv_splits = [sum(row) for row in per_source]
+        received = self._tp_in(_AllToAll.apply(flat_hidden[tokens], send_splits, recv_splits, group))
+        offset, positions = 0, [[] for _ in range(local)]
+        for source in range(world):
+            for e in range(local):
+                n = per_source[source][e]
+                positions[e].append(torch.arange(offset, offset + n, device=received.device))
+                offset += n
+        started = self._start_clock(received) if self.measure_load else None
+        processed = received.new_zeros(received.shape)
+        for e in range(local):
+            rows = torch.cat(positions[e])
+            if rows.numel():
+                processed = processed.index_copy(0, rows, self.expert_forward(e, received[rows]).to(received.dtype))
+        if started is not None:
+            self.load_rows += received.size(0)
+            self.load_seconds += self._stop_clock(received, started) + received.size(0) * self.simulated_cost_per_row
+        returned = _AllToAll.apply(self._tp_out(processed), recv_splits, send_splits, group)
+        output = torch.zeros_like(flat_hidden)
+        output.index_add_(0, tokens, (returned * weights[:, None]).to(output.dtype))
+        return output
+
+    def _run_expert(self, index: int, inputs: Tensor) -> Tensor:
+        return self.expert_forward(index, inputs)
+
+    @staticmethod
+    def _start_clock(reference: Tensor) -> float:
+        if reference.is_cuda:
+            torch.cuda.synchronize()
+        return time.perf_counter()
+
+    @staticmethod
+    def _stop_clock(reference: Tensor, started: float) -> float:
+        if reference.is_cuda:
+            torch.cuda.synchronize()
+        return time.perf_counter() - started
+
+
+# ------------------------------------------------------------------------------------------ parameter classes
+def is_expert_parameter(name: str) -> bool:
+    return name.endswith(("moe.w_gate_up", "moe.w_down")) or ".moe.experts." in name
+
+
+def broadcast_shared_parameters(model, ctx: ExpertParallelContext) -> None:
+    """Make replicated tensors identical: tensor-parallel slices across the expert group, everything else across
+    the world. Experts stay rank-local."""
+    from .tensor_parallel import is_tp_sharded_shared
+
+    for name, param in model.named_parameters():
+        if is_expert_parameter(name):
+            continue
+        if is_tp_sharded_shared(name) and ctx.tp_size > 1:
+            if ctx.world_size > 1:
+                dist.broadcast(param.data, src=ctx.group_root, group=ctx.group)
+        else:
+            dist.broadcast(param.data, src=0)
+    for _, buf in model.named_buffers():
+        dist.broadcast(buf.data, src=0)
+
+
+def _shared_and_expert(model):
+    shared, experts = [], []
+    for name, p in model.named_parameters():
+        (experts if is_expert_parameter(name) else shared).append(p)
+    return shared, experts
+
+
+def sync_gradients(model, ctx: ExpertParallelContext, sharded_optimizer=None, optimizer=None) -> None:
+    """Average replicated gradients over the expert group (one flat all-reduce per dtype); scale expert gradients
+    by ``1/ep`` (folded into the fused optimizer when it is given, else applied in place)."""
+    shared, experts = _shared_and_expert(model)
+    if ctx.world_size > 1:
+        if sharded_optimizer is not None:
+            sharded_optimizer.reduce_gradients()
+        else:
+            for p in shared:
+                if p.grad is None:
+                    p.grad = torch.zeros_like(p)
+            by_dtype: dict = {}
+            for p in shared:
+                by_dtype.setdefault(p.grad.dtype, []).append(p)
+            for dtype, params in by_dtype.items():
+                flat = torch.cat([p.grad.reshape(-1) for p in params])
+                if flat.is_cuda:
+                    dist.all_reduce(flat, op=dist.ReduceOp.AVG, group=ctx.group)
+                else:
+                    dist.all_reduce(flat, group=ctx.group)
+                    flat /= ctx.world_size
+                offset = 0
+                for p in params:
+                    p.grad.copy_(flat[offset:offset + p.numel()].view_as(p))
+                    offset += p.numel()
+    scale = 1.0 / ctx.world_size
+    fused = optimizer is not None and hasattr(optimizer, "grad_scale")
+    for p in experts:
+        if p.grad is None:
+            continue
+        if fused:
+            optimizer.grad_scale[p] = scale
+        elif ctx.world_size > 1:
+            p.grad.mul_(scale)
+
+
+def clip_grad_norm_parallel(model, ctx: ExpertParallelContext, max_norm: float, sharded: bool = False,
+                            optimizer=None):
+    """Clip by the true global norm, identically on every rank: replicated tensors once, tensor-parallel slices
+    summed over the tensor group, experts summed over the world. With the fused optimizer the norm is computed by
+    its kernels and the clip is folded into its step (no host synchronisation)."""
+    from .tensor_parallel import is_tp_sharded_shared
+
+    fused = optimizer is not None and hasattr(optimizer, "grad_sumsq")
+    replicated, tp_slices, experts = [], [], []
+    for name, p in model.named_parameters():
+        if p.grad is None:
+            continue
+        if is_expert_parameter(name):
+            experts.append(p)
+        elif is_tp_sharded_shared(name) and ctx.tp_size > 1:
+            tp_slices.append(p)
+        else:
+            replicated.append(p)
+    device = ctx.device
+
+    def sumsq(params):
+        if not params:
+            return torch.zeros((), dtype=torch.float64, device=device)
+        if fused:
+            return optimizer.grad_sumsq(params).to(device)
+        return sum(p.grad.detach().double().pow(2).sum() for p in params)
+
+    rep, tps, exp = sumsq(replicated), sumsq(tp_slices), sumsq(experts)
+    if sharded and ctx.world_size > 1:
+        rep, tps = rep.clone(), tps.clone()
+        dist.all_reduce(rep, group=ctx.group)
+        dist.all_reduce(tps, group=ctx.group)
+    if ctx.tp_size > 1:
+        tps = tps.clone()
+        dist.all_reduce(tps, group=ctx.tp_group)
+    exp = exp.clone()
+    if dist.is_initialized() and ctx.global_size > 1:
+        dist.all_reduce(exp)
+    total = (rep + tps + exp).sqrt()
+    coef = torch.clamp(max_norm / (total + 1e-6), max=1.0)
+    if fused:
+        optimizer.set_clip_coefficient(coef, total)
+        return total
+    for p in model.parameters():
+        if p.grad is not None:
+            p.grad.mul_(coef.to(p.grad.dtype))
+    return float(total)
+
+
+def all_reduce_mean(values: list, ctx: ExpertParallelContext) -> list:
+    t = torch.tensor(values, dtype=torch.float64, device=ctx.device)
+    dist.all_reduce(t, group=ctx.group)
+    return (t / ctx.world_size).tolist()
+
+
+def barrier(ctx=None) -> None:
+    from .groups import barrier as _barrier
+
+    _barrier()
+
+
+def finish(ctx) -> None:
+    from .groups import finish as _finish
+
+    _finish(ctx)
+
+
+# ------------------------------------------------------------------------------------------ straggler control
+class DeviceLoadTracker:
+    """Per-rank expert time/rows controller (reference ``DeviceLoadTracker``, ``src/expert_parallel.py:280-384``).
+
+    Every ``interval`` steps the accumulated per-layer expert seconds and rows are gathered; the routing bias is an
+    integral controller ``bias_r -= rate * strength * log(t_r / mean)``, clamped to ``max_bias`` and re-centred, added to
+    the router logits for selection only. ``adapt_capacity`` additionally sets each rank's ``capacity_scale`` to
+    ``clamp(mean / t_r)``. Measuring per-expert time synchronises the device, so tracked layers take the reference
+    (per-expert) path.
+    """
+
+    def __init__(self, model, ctx: ExpertParallelContext, strength: float = 0.5, max_bias: float = 2.0,
+                 rate: float = 0.5, interval: int = 10, adapt_capacity: bool = False,
+                 capacity_scale_min: float = 0.5, capacity_scale_max: float = 2.0) -> None:
+        self.model, self.ctx = model, ctx
+        self.strength, self.max_bias, self.rate, self.interval = strength, max_bias, rate, interval
+        self.adapt_capacity = adapt_capacity
+        self.capacity_scale_min, self.capacity_scale_max = capacity_scale_min, capacity_scale_max
+        self.layers = len(model.moes())
+        self.rank_bias = torch.zeros(self.layers, ctx.world_size, dtype=torch.float64)
+        self.history: list = []
+        for moe in model.moes():
+            moe.measure_load = True
+
+    def _gather(self):
+        local = torch.tensor([[moe.load_seconds, float(moe.load_rows)] for moe in self.model.moes()],
+                             dtype=torch.float64, device=self.ctx.device)
+        for moe in self.model.moes():
+            moe.load_seconds, moe.load_rows = 0.0, 0
+        if self.ctx.tp_size > 1:
+            dist.all_reduce(local, group=self.ctx.tp_group)
+            local /= self.ctx.tp_size
+        gathered = [torch.zeros_like(local) for _ in range(self.ctx.world_size)]
+        dist.all_gather(gathered, local, group=self.ctx.group)
+        stacked = torch.stack(gathered, dim=1).cpu()
+        return stacked[..., 0], stacked[..., 1]
+
+    def update(self, step: int) -> Optional[dict]:
+        if step % self.interval:
+            return None
+        seconds, rows = self._gather()
+        per_rank_seconds, per_rank_rows = seconds.sum(dim=0), rows.sum(dim=0)
+        metrics = {"step": step, "device_rows": per_rank_rows.tolist(), "device_seconds": per_rank_seconds.tolist(),
+                   "rows_imbalance": float(per_rank_rows.max() / per_rank_rows.mean().clamp(min=1e-9)),
+                   "time_imbalance": float(per_rank_seconds.max() / per_rank_seconds.mean().clamp(min=1e-9))}
+        if self.strength > 0 and float(seconds.sum()) > 0:
+            relative = seconds / seconds.mean(dim=1, keepdim=True).clamp(min=1e-12)
+            correction = -self.strength * torch.log(relative.clamp(min=0.05))
+            bias = (self.rank_bias + self.rate * correction).clamp(-self.max_bias, self.max_bias)
+            self.rank_bias = bias - bias.mean(dim=1, keepdim=True)
+            self._apply()
+        metrics["rank_bias"] = self.rank_bias.mean(dim=0).tolist()
+        if self.adapt_capacity and float(seconds.sum()) > 0:
+            mean_time = seconds.mean(dim=1, keepdim=True).clamp(min=1e-12)
+            scale = (mean_time / seconds.clamp(min=1e-12)).clamp(self.capacity_scale_min, self.capacity_scale_max)
+            for layer, moe in enumerate(self.model.moes()):
+                moe.capacity_scale = float(scale[layer, self.ctx.rank])
+            metrics["capacity_scale"] = scale.mean(dim=0).tolist()
+        self.history.append(metrics)
+        return metrics
+
+    def _apply(self) -> None:
+        per_rank = self.model.moes()[0].num_local_experts
+        for layer, moe in enumerate(self.model.moes()):
+            moe.expert_bias = self.rank_bias[layer].repeat_interleave(per_rank).to(torch.float32).to(self.ctx.device)
+
+    def gather_expert_utilization(self) -> Tensor:
+        local = torch.stack([moe.last_stats["expert_load"].to(torch.float64) for moe in self.model.moes()])
+        local = local.to(self.ctx.device)
+        if self.ctx.tp_size > 1:
+            dist.all_reduce(local, group=self.ctx.tp_group)
+            local /= self.ctx.tp_size
+        gathered = [torch.zeros_like(local) for _ in range(self.ctx.world_size)]
+        dist.all_gather(gathered, local, group=self.ctx.group)
+        return torch.stack(gathered).cpu()
+
+    def state_dict(self) -> dict:
+        return {"rank_bias": self.rank_bias.tolist()}
+
+    def load_state_dict(self, state: dict) -> None:
+        self.rank_bias = torch.tensor(state["rank_bias"], dtype=torch.float64)
+        if bool(self.rank_bias.abs().sum() > 0):
+            self._apply()
+
+
+def simulated_slow_rank(spec: str) -> tuple[int, float]:
+    rank, cost = spec.split(":")
+    return int(rank), float(cost)
+
+
+del math

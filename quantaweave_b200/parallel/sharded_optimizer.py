@@ -1,0 +1,161 @@
+"""ZeRO-style sharded AdamW over a data-parallel group (reference ``src/sharded_optimizer.py``).
+
+The reference assigns whole replicated parameters to owner ranks (reduce to owner, owner steps, broadcast). This
+implementation shards *flat*: every replicated gradient is packed into one buffer per dtype, padded to a multiple
+of the group size, and
+
+1. ``reduce_gradients``: ``reduce_scatter`` (average) -> each rank holds its contiguous gradient shard only;
+2. ``step``: AdamW on the shard against an fp32 master shard (moments exist only for the shard: ZeRO-1/2 memory);
+3. the updated shard is ``all_gather``-ed back into the replicated parameters.
+
+Expert (rank-local) parameters use a local AdamW (the fused kernel on CUDA). ``state_dict`` records the shard
+layout and refuses to load into a different world size or parameter set, like the reference.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from .expert_parallel import is_expert_parameter
+
+
+class ShardedAdamW:
+    def __init__(self, model, ctx, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 1e-2, group=None) -> None:
+        self.model, self.ctx = model, ctx
+        self.group = group if group is not None else getattr(ctx, "group", None) or getattr(ctx, "dp_group", None)
+        self.world = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(self.group) if dist.is_initialized() else 0
+        named = list(model.named_parameters())
+        self.shared = [p for n, p in named if not is_expert_parameter(n)]
+        self.local = [p for n, p in named if is_expert_parameter(n)]
+        self.defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        self._groups: dict = {}
+        for p in self.shared:
+            self._groups.setdefault(p.dtype, []).append(p)
+        self.shards: dict = {}
+        for dtype, params in self._groups.items():
+            total = sum(p.numel() for p in params)
+            per = (total + self.world - 1) // self.world
+            start = self.rank * per
+            flat = torch.cat([p.detach().reshape(-1).float() for p in params])
+            flat = torch.nn.functional.pad(flat, (0, per * self.world - total))
+            self.shards[dtype] = {"numel": total, "per": per, "master": flat[start:start + per].clone(),
+                                  "exp_avg": torch.zeros(per, device=flat.device),
+                                  "exp_avg_sq": torch.zeros(per, device=flat.device), "grad": None}
+        self.step_count = 0
+        self.local_opt = None
+        if self.local:
+            if any(p.is_cuda for p in self.local):
+                from ..optim.adamw import FusedAdamW
+
+                self.local_opt = FusedAdamW(self.local, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+            else:
+                self.local_opt = torch.optim.AdamW(self.local, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
+        self.param_groups = [dict(self.defaults, params=self.shared)] + (self.local_opt.param_groups if self.local_opt else [])
+        self._clip = None
+
+    # ---- gradients ------------------------------------------------------------------------------
+    def reduce_gradients(self) -> None:
+        for dtype, params in self._groups.items():
+            for p in params:
+                if p.grad is None:
+                    p.grad = torch.zeros_like(p)
+            sh = self.shards[dtype]
+            flat = torch.cat([p.grad.reshape(-1).float() for p in params])
+            flat = torch.nn.functional.pad(flat, (0, sh["per"] * self.world - sh["numel"]))
+            out = torch.empty(sh["per"], device=flat.device, dtype=flat.dtype)
+            if self.world > 1:
+                dist.reduce_scatter_tensor(out, flat, group=self.group)
+                out /= self.world
+            else:
+                out.copy_(flat)
+            sh["grad"] = out
+            for p in params:
+                p.grad = None
+
+    def shard_sumsq(self) -> Tensor:
+        total = None
+        for sh in self.shards.values():
+            if sh["grad"] is not None:
+                s = sh["grad"].double().pow(2).sum()
+                total = s if total is None else total + s
+        if total is None:
+            device = next(iter(self.shards.values()))["master"].device if self.shards else "cpu"
+            total = torch.zeros((), dtype=torch.float64, device=device)
+        return total
+
+    def set_clip_coefficient(self, coef: Tensor, norm=None) -> None:
+        self._clip = coef
+        if self.local_opt is not None and hasattr(self.local_opt, "set_clip_coefficient"):
+            self.local_opt.set_clip_coefficient(coef, norm)
+
+    # ---- update ---------------------------------------------------------------------------------
+    @torch.no_grad()
+    def step(self) -> None:
+        group = self.param_groups[0]
+        lr = group["lr"]
+        beta1, beta2 = group["betas"]
+        eps, wd = group["eps"], group["weight_decay"]
+        self.step_count += 1
+        t = self.step_count
+        for dtype, params in self._groups.items():
+            sh = self.shards[dtype]
+            g = sh["grad"]
+            if g is None:
+                continue
+            if self._clip is not None:
+                g = g * self._clip.to(g.device, g.dtype)
+            p = sh["master"]
+            p.mul_(1 - lr * wd)
+            sh["exp_avg"].lerp_(g, 1 - beta1)
+            sh["exp_avg_sq"].mul_(beta2).addcmul_(g, g, value=1 - beta2)
+            denom = (sh["exp_avg_sq"].sqrt() / (1 - beta2 ** t) ** 0.5).add_(eps)
+            p.addcdiv_(sh["exp_avg"], denom, value=-lr / (1 - beta1 ** t))
+            full = torch.empty(sh["per"] * self.world, device=p.device, dtype=p.dtype)
+            if self.world > 1:
+                dist.all_gather_into_tensor(full, p, group=self.group)
+            else:
+                full.copy_(p)
+            offset = 0
+            for q in params:
+                q.data.copy_(full[offset:offset + q.numel()].view_as(q).to(q.dtype))
+                offset += q.numel()
+            sh["grad"] = None
+        if self.local_opt is not None:
+            if len(self.param_groups) > 1:
+                for g_ in self.local_opt.param_groups:
+                    g_["lr"] = lr
+            self.local_opt.step()
+        self._clip = None
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        for p in self.model.parameters():
+            if set_to_none:
+                p.grad = None
+            elif p.grad is not None:
+                p.grad.zero_()
+
+    def state_numel(self) -> int:
+        return sum(2 * sh["per"] for sh in self.shards.values())
+
+    def state_dict(self) -> dict:
+        return {"shards": {str(k): {n: v for n, v in sh.items() if n != "grad"} for k, sh in self.shards.items()},
+                "step": self.step_count, "world": self.world, "rank": self.rank,
+                "local": self.local_opt.state_dict() if self.local_opt is not None else None}
+
+    def load_state_dict(self, state: dict) -> None:
+        if state["world"] != self.world or state["rank"] != self.rank:
+            raise ValueError("sharded optimizer state was saved with a different world size or rank")
+        for key, saved in state["shards"].items():
+            match = [d for d in self.shards if str(d) == key]
+            if not match or saved["numel"] != self.shards[match[0]]["numel"]:
+                raise ValueError("sharded optimizer state was saved for a different parameter set")
+            sh = self.shards[match[0]]
+            for name in ("master", "exp_avg", "exp_avg_sq"):
+                sh[name].copy_(saved[name])
+        self.step_count = int(state["step"])
+        if self.local_opt is not None and state.get("local") is not None:
+            self.local_opt.load_state_dict(state["local"])

@@ -1,0 +1,131 @@
+"""tcgen05 GEMM numerics against a plain PyTorch fp32 reference (dense linear layers and grouped MoE GEMMs)."""
+
+import pytest
+import torch
+
+from conftest import cuda_ready
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ready(), reason="needs a B200")]
+
+
+def _ext():
+    from quantaweave_b200.ops import native_required
+
+    return native_required()
+
+
+def _close(out, ref, tol=2e-2):
+    out, ref = out.float(), ref.float()
+    if out.numel() == 0:
+        assert ref.numel() == 0
+        return
+    err = (out - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max abs err {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 384, 192), (1024, 1000, 1024), (77, 3072, 512)])
+def test_linear_fwd(M, N, K):
+    C = _ext()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    bias = torch.randn(N, device="cuda", generator=g)
+    res = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.linear_fwd(x, w, bias, res, out)
+    ref = x.float() @ w.float().t() + bias + res.float()
+    _close(out, ref)
+    out32 = torch.empty(M, N, device="cuda", dtype=torch.float32)
+    C.linear_fwd(x, w, None, None, out32)
+    _close(out32, x.float() @ w.float().t(), 1e-3)
+    assert C.read_status(True) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (130, 1024, 320)])
+def test_linear_dgrad_wgrad(M, N, K):
+    C = _ext()
+    g = torch.Generator(device="cuda").manual_seed(1)
+    dy = torch.randn(M, N, device="cuda", generator=g).bfloat16()
+    w = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    dx = torch.empty(M, K, device="cuda", dtype=torch.float32)
+    C.linear_dgrad(dy, w, dx, False)
+    _close(dx, dy.float() @ w.float(), 1e-3)
+    dw = torch.zeros(N, K, device="cuda", dtype=torch.float32)
+    C.linear_wgrad(dy, x, dw, False)
+    _close(dw, dy.float().t() @ x.float(), 1e-3)
+    C.linear_wgrad(dy, x, dw, True)  # accumulate
+    _close(dw, 2 * dy.float().t() @ x.float(), 1e-3)
+    assert C.read_status(True) == 0
+
+
+def _grouped_layout(counts, H, device):
+    counts_t = torch.tensor(counts, dtype=torch.int32, device=device)
+    padded = [(c + 127) // 128 * 128 for c in counts]
+    offs = [0]
+    for p in padded[:-1]:
+        offs.append(offs[-1] + p)
+    return counts_t, torch.tensor(offs, dtype=torch.int32, device=device), sum(padded), offs
+
+
+@pytest.mark.parametrize("counts", [[0, 5, 37, 1, 0, 64, 33, 2], [300, 0, 129, 256]])
+def test_moe_grouped_forward_backward(counts):
+    C = _ext()
+    torch.manual_seed(0)
+    E, H, F = len(counts), 256, 256
+    dev = "cuda"
+    counts_t, offs_t, R, offs = _grouped_layout(counts, H, dev)
+    x = torch.zeros(R, H, device=dev, dtype=torch.bfloat16)
+    for e, c in enumerate(counts):
+        x[offs[e]:offs[e] + c] = torch.randn(c, H, device=dev).bfloat16()
+    wgu = (torch.randn(E, 2 * F, H, device=dev) * 0.05).bfloat16()
+    wd = (torch.randn(E, H, F, device=dev) * 0.05).bfloat16()
+    h = torch.full((R, F), 7.0, device=dev, dtype=torch.bfloat16)
+    gu = torch.empty(R, 2 * F, device=dev, dtype=torch.bfloat16)
+    C.moe_gate_up_fwd(x, wgu, counts_t, offs_t, h, gu)
+    y = torch.empty(R, H, device=dev, dtype=torch.bfloat16)
+    C.moe_down_fwd(h, wd, counts_t, offs_t, y)
+    dy = torch.zeros(R, H, device=dev, dtype=torch.bfloat16)
+    route_w = torch.zeros(R, device=dev)
+    for e, c in enumerate(counts):
+        dy[offs[e]:offs[e] + c] = torch.randn(c, H, device=dev).bfloat16()
+        route_w[offs[e]:offs[e] + c] = torch.rand(c, device=dev)
+    tiles = C.moe_dw_tiles(F)
+    dgu = torch.empty_like(gu)
+    hw = torch.empty_like(h)
+    part = torch.empty(R, tiles, device=dev)
+    C.moe_down_bwd(dy, wd, counts_t, offs_t, gu, route_w, dgu, hw, part)
+    dx = torch.empty(R, H, device=dev, dtype=torch.bfloat16)
+    C.moe_gate_up_dgrad(dgu, wgu, counts_t, offs_t, dx)
+    dwd = torch.empty(E, H, F, device=dev)
+    C.moe_wgrad(dy, hw, counts_t, offs_t, dwd, False)
+    dwgu = torch.empty(E, 2 * F, H, device=dev)
+    C.moe_wgrad(dgu, x, counts_t, offs_t, dwgu, False)
+    assert C.read_status(True) == 0
+    for e, c in enumerate(counts):
+        sl = slice(offs[e], offs[e] + c)
+        pad = slice(offs[e] + c, offs[e] + (c + 127) // 128 * 128)
+        xe = x[sl].float()
+        g_ = xe @ wgu[e, :F].float().t()
+        u_ = xe @ wgu[e, F:].float().t()
+        he = torch.nn.functional.silu(g_) * u_
+        _close(h[sl], he)
+        _close(gu[sl, :F], g_)
+        assert torch.all(h[pad] == 0)
+        ye = h[sl].float() @ wd[e].float().t()
+        _close(y[sl], ye)
+        a = dy[sl].float() @ wd[e].float()
+        w = route_w[sl][:, None]
+        gf, uf = gu[sl, :F].float(), gu[sl, F:].float()
+        sg = torch.sigmoid(gf)
+        _close(dgu[sl, :F], w * a * uf * (sg + gf * sg * (1 - sg)), 3e-2)
+        _close(dgu[sl, F:], w * a * gf * sg, 3e-2)
+        _close(part[sl].sum(1), (a * (gf * sg * uf)).sum(1), 3e-2)
+        _close(hw[sl], w * gf * sg * uf, 3e-2)
+        _close(dx[sl], dgu[sl].float() @ wgu[e].float(), 3e-2)
+        if c:
+            _close(dwd[e], dy[sl].float().t() @ hw[sl].float(), 3e-2)
+            _close(dwgu[e], dgu[sl].float().t() @ xe, 3e-2)
+        else:
+            assert torch.all(dwd[e] == 0) and torch.all(dwgu[e] == 0)
