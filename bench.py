@@ -45,6 +45,8 @@ def parse():
     p.add_argument("--seq-len", type=int, default=2048)
     p.add_argument("--layers", type=int, default=CONFIG2["layers"], help="debug override (the metric needs 16)")
     p.add_argument("--recompute", choices=("auto", "on", "off"), default="auto")
+    p.add_argument("--transport", choices=("p2p", "nccl"), default=os.environ.get("QW_EP_TRANSPORT", "nccl"),
+                   help="expert-parallel dispatch/combine: in-kernel NVLink stores (p2p) or NCCL all_to_all")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--kernel-breakdown", action="store_true",
                    help="after timing, profile one extra step and print per-kernel CUDA time shares to stderr")
@@ -119,13 +121,15 @@ def run_native(args, rank, world, local):
     from quantaweave_b200.training.native import prepare_model
     from quantaweave_b200.utils.timing import ClockSampler, DeviceTimer
 
+    # the reference's layout (LayerNorm, learned positions, biased MHA projections) so both arms run the same
+    # architecture with the same N(0, 0.02) initialisation and therefore the same routing statistics
     cfg = QuantaWeaveConfig(**{**CONFIG2, "layers": args.layers}, max_sequence_length=args.seq_len + 1,
-                            norm_type="rmsnorm", position_embedding="rope", attention_bias=False, init_std=0.02)
+                            norm_type="layernorm", position_embedding="learned", attention_bias=True, init_std=0.02)
     ep = None
     if world > 1:
         from quantaweave_b200.parallel.expert_parallel import init_expert_parallel
 
-        ep = init_expert_parallel("cuda", 1)
+        ep = init_expert_parallel("cuda", 1, transport=args.transport)
     torch.manual_seed(args.seed + rank)
     with torch.device("cuda"):
         model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ep)
@@ -195,10 +199,12 @@ def run_native(args, rank, world, local):
         "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None, "dtype": "bf16",
         "data": "synthetic: seeded Zipf(1.1) token ids, random-init N(0,0.02) weights",
         "config": {"model": "moe-1b-e64 (BASELINE config 2: vocab 32000, d1024, 16 layers, 16 heads, 64 experts "
-                            "h2816, top2, cf1.25, RMSNorm+RoPE)" if args.layers == 16 else
+                            "h2816, top2, cf1.25; reference layout: LayerNorm, learned positions, biased MHA)"
+                            if args.layers == 16 else
                             f"DEBUG {args.layers}-layer variant of config 2",
                    "global_batch": args.seqs_per_gpu * world, "seq_len": args.seq_len,
                    "parallelism": f"ep{world}" if world > 1 else "single-gpu (all 64 experts local)",
+                   "ep_transport": args.transport if world > 1 else None,
                    "l2": "no flush: every step streams >100 GB through HBM, far above the 126 MB L2",
                    "recompute_expert_activations": recompute, "optimizer": "fused AdamW, fp32 master, clip 1.0"},
         "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches, "impl": "native",
@@ -235,6 +241,10 @@ def run_reference(args, rank, world, local):
     torch.manual_seed(args.seed + rank)
     try:
         model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ep).to(device)
+        with torch.no_grad():  # the config's N(0, 0.02) initialisation, applied through the public module tree
+            for name, param in model.named_parameters():
+                if param.dim() >= 2:
+                    param.normal_(0.0, 0.02)
         if ep is not None:
             broadcast_shared_parameters(model, ep)
         kernel = "loop"
@@ -272,7 +282,11 @@ def run_reference(args, rank, world, local):
             with DeviceTimer() as t:
                 for i in range(args.steps):
                     loss = train_step(dev[args.warmup + i])
-        del dev
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            probe = model(dev[-1], labels=dev[-1])
+        overflow_fraction = float(probe["overflow_routes"]) / (args.seqs_per_gpu * (args.seq_len + 1) * cfg.top_k
+                                                               * args.layers)
+        del dev, probe
         tokens = args.seqs_per_gpu * args.seq_len * world
         ms = t.ms / args.steps
         e2e = None
@@ -286,12 +300,14 @@ def run_reference(args, rank, world, local):
         emit(rank, {"metric": METRIC, "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
                     "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                     "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "impl": "reference",
-                    "data": "synthetic: seeded Zipf(1.1) token ids, random init (reference's own init)",
+                    "data": "synthetic: seeded Zipf(1.1) token ids, random-init N(0,0.02) weights",
                     "config": {"model": "reference architecture at config-2 shape (LayerNorm, learned positions, MHA)",
                                "global_batch": args.seqs_per_gpu * world, "seq_len": args.seq_len,
                                "parallelism": f"ep{world}" if world > 1 else "single-gpu",
                                "moe_kernel": kernel},
-                    "clocks": clocks.summary(), "e2e": e2e, "final_loss": float(loss.item())})
+                    "clocks": clocks.summary(), "e2e": e2e, "final_loss": float(loss.item()),
+                    "overflow_fraction": round(overflow_fraction, 4),
+                    "peak_mem_gb": round(torch.cuda.max_memory_allocated() / 1e9, 1)})
     except torch.OutOfMemoryError as exc:
         emit(rank, {"impl": "reference", "unavailable": f"out of memory on B200 at config 2: {str(exc)[:160]}"})
 

@@ -347,6 +347,25 @@ void flash_attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor dout, Tensor 
                      static_cast<float>(scale), stream());
 }
 
+// ------------------------------------------------------------------------------------------------ p2p
+// peer_bufs / peer_flags: int64 device tensors of raw peer addresses (from the symmetric-memory rendezvous)
+void p2p_push(Tensor src, int64_t block_bytes, Tensor peer_bufs, Tensor peer_flags, int64_t me, int64_t epoch,
+              Tensor done) {
+  CHECK_CUDA(src); CHECK_CONTIG(src);
+  TORCH_CHECK(src.numel() * src.element_size() == block_bytes * peer_bufs.numel(), "p2p_push: src size");
+  c10::cuda::CUDAGuard g(src.device());
+  qw::p2p_push(src.data_ptr(), block_bytes, reinterpret_cast<void* const*>(peer_bufs.data_ptr<int64_t>()),
+               reinterpret_cast<int* const*>(peer_flags.data_ptr<int64_t>()), static_cast<int>(peer_bufs.numel()),
+               static_cast<int>(me), static_cast<int>(epoch), reinterpret_cast<unsigned int*>(done.data_ptr<int>()),
+               stream());
+}
+
+void p2p_wait(Tensor flags, int64_t world, int64_t epoch, double timeout_s) {
+  CHECK_CUDA(flags);
+  c10::cuda::CUDAGuard g(flags.device());
+  qw::p2p_wait(flags.data_ptr<int>(), static_cast<int>(world), static_cast<int>(epoch), timeout_s, stream());
+}
+
 // ------------------------------------------------------------------------------------------------ status
 int64_t read_status(bool clear) {
   int s = qw::gemm_status(clear);
@@ -355,6 +374,7 @@ int64_t read_status(bool clear) {
   if ((t = qw::routing_status(clear)) && !s) s = t;
   if ((t = qw::optim_status(clear)) && !s) s = t;
   if ((t = qw::attention_status(clear)) && !s) s = t;
+  if ((t = qw::p2p_status(clear)) && !s) s = t;
   return s;
 }
 
@@ -398,5 +418,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("scale_bf16", &scale_bf16);
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("p2p_push", &p2p_push);
+  m.def("p2p_wait", &p2p_wait);
   m.def("read_status", &read_status, py::arg("clear") = true);
 }

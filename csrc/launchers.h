@@ -117,4 +117,10 @@ void flash_attn_bwd(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, cons
                     float scale, cudaStream_t stream);
 int attention_status(bool clear);
 
+// ---- p2p.cu ----
+void p2p_push(const void* src, int64_t block_bytes, void* const* peer_bufs, int* const* peer_flags, int world, int me,
+              int epoch, unsigned int* done, cudaStream_t stream);
+void p2p_wait(const int* flags, int world, int epoch, double timeout_s, cudaStream_t stream);
+int p2p_status(bool clear);
+
 }  // namespace qw

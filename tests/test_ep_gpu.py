@@ -1,0 +1,105 @@
+"""Expert parallelism on 2+ B200s (NCCL): the native slot-dispatch MoE against the single-GPU native model."""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import cuda_ready
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not cuda_ready() or torch.cuda.device_count() < 2, reason="needs 2 B200s")]
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, transport, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), QW_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
+    try:
+        queue.put((rank, "ok", _case(rank, world, transport)))
+    except Exception:  # noqa: BLE001
+        queue.put((rank, "error", traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _case(rank, world, transport):
+    from quantaweave_b200 import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM
+    from quantaweave_b200.ops import ext
+    from quantaweave_b200.parallel.expert_parallel import (clip_grad_norm_parallel, init_expert_parallel,
+                                                           sync_gradients)
+    from quantaweave_b200.training.native import prepare_model
+
+    torch.cuda.set_device(rank)
+    cfg = QuantaWeaveConfig(vocab_size=512, hidden_size=256, layers=2, ffn_size=256, num_experts=8, top_k=2,
+                            attention_heads=4, max_sequence_length=129, capacity_factor=1.25, norm_type="rmsnorm",
+                            position_embedding="rope", attention_bias=False, init_std=0.02)
+    torch.manual_seed(0)
+    full = QuantaWeaveMoEForCausalLM(cfg).cuda()
+    prepare_model(full, "bf16")
+    ep = init_expert_parallel("cuda", 1, transport=transport)
+    model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ep).cuda()
+    prepare_model(model, "bf16")
+    per = cfg.num_experts // world
+    state = {}
+    for key, value in full.state_dict().items():
+        if ".experts." in key:
+            e = int(key.split(".experts.")[1].split(".")[0])
+            if rank * per <= e < (rank + 1) * per:
+                state[key.replace(f".experts.{e}.", f".experts.{e - rank * per}.")] = value
+        else:
+            state[key] = value
+    model.load_state_dict(state)
+    g = torch.Generator().manual_seed(1)
+    batches = [torch.randint(0, cfg.vocab_size, (2, 129), generator=g).cuda() for _ in range(world)]
+    out = model(batches[rank], labels=batches[rank], return_logits=False)
+    out["loss"].backward()
+    sync_gradients(model, ep)
+    norm = float(clip_grad_norm_parallel(model, ep, 1e9))
+    ref_losses = []
+    for b in batches:
+        o = full(b, labels=b, return_logits=False)
+        (o["loss"] / world).backward()
+        ref_losses.append(float(o["loss"]))
+    ref = {n: p.grad.float() for n, p in full.named_parameters()}
+    ref_norm = float(torch.sqrt(sum(v.double().pow(2).sum() for v in ref.values())))
+    got = {n: p.grad.float() for n, p in model.named_parameters()}
+    assert abs(float(out["loss"]) - ref_losses[rank]) < 2e-2, (float(out["loss"]), ref_losses[rank])
+    assert abs(norm - ref_norm) < 5e-2 * ref_norm, (norm, ref_norm)
+    for name, grad in got.items():
+        r = ref[name]
+        if name.endswith(("w_gate_up", "w_down")):
+            r = r[rank * per:(rank + 1) * per]
+        rel = float((grad - r).norm() / (r.norm() + 1e-12))
+        assert rel < (0.1 if grad.dim() >= 2 else 0.3), (name, rel)
+    assert ext().read_status(True) == 0
+    return float(out["loss"])
+
+
+@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+def test_expert_parallel_native_matches_single_gpu(transport):
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, transport, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for _ in range(world):
+        rank, status, payload = queue.get(timeout=600)
+        if status != "ok":
+            for p in procs:
+                p.join(timeout=30)
+            raise AssertionError(f"rank {rank} failed:\n{payload}")
+    for p in procs:
+        p.join(timeout=60)
