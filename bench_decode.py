@@ -1,0 +1,142 @@
+"""Second headline metric: int4 weight-only MoE decode tokens/sec on one B200.
+
+    python bench_decode.py --batch 1 --bits 4
+    python bench_decode.py --batch 32 --bits 4
+    python bench_decode.py --impl reference --batch 1
+
+Config 5: the config-2 architecture (vocab 32000, d1024, 16 layers, 16 heads, 64 SwiGLU experts h2816, top-2) with
+random-init N(0, 0.02) weights, experts quantised to int4 (group 128, fp16 scales, symmetric) or int8 per-channel;
+a 512-token seeded uniform prompt, 256 generated tokens, greedy decoding. Decode time is measured with CUDA events
+around the generation loop only (the prefill is timed separately); per-token latency is the p50 over steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+CONFIG = dict(vocab_size=32000, hidden_size=1024, layers=16, attention_heads=16, num_experts=64, ffn_size=2816,
+              top_k=2, capacity_factor=1.25, router_aux_loss_coef=0.01)
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--bits", type=int, choices=(4, 8, 16), default=4)
+    p.add_argument("--prompt", type=int, default=512)
+    p.add_argument("--new", type=int, default=256)
+    p.add_argument("--impl", choices=("native", "reference"), default="native")
+    p.add_argument("--seed", type=int, default=0)
+    return p.parse_args()
+
+
+def main():
+    import torch
+
+    args = parse()
+    torch.manual_seed(args.seed)
+    gen = torch.Generator().manual_seed(args.seed)
+    prompts = torch.randint(0, CONFIG["vocab_size"], (args.batch, args.prompt), generator=gen)
+    group = 128 if args.bits == 4 else None
+    if args.impl == "reference":
+        return run_reference(args, prompts, group)
+    sys.path.insert(0, ROOT)
+    from quantaweave_b200 import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM
+    from quantaweave_b200.inference.fast_decode import FastDecoder
+    from quantaweave_b200.inference.quantization import quantize_model
+
+    cfg = QuantaWeaveConfig(**CONFIG, max_sequence_length=args.prompt + max(args.new, 8) + 1, norm_type="layernorm",
+                            position_embedding="learned", attention_bias=True, init_std=0.02)
+    with torch.device("cuda"):
+        model = QuantaWeaveMoEForCausalLM(cfg).eval()
+    if args.bits != 16:
+        quantize_model(model, args.bits, group)
+    dec = FastDecoder(model, torch.device("cuda"), max_batch=args.batch)
+    prompts = prompts.cuda()
+    # warm-up generation (graph already captured at construction)
+    dec.generate(prompts, 8)
+    torch.cuda.synchronize()
+    start, mid = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    dec._prefill(prompts[:, :-1])
+    mid.record()
+    token = prompts[:, -1]
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.new + 1)]
+    events[0].record()
+    for i in range(args.new):
+        pos = torch.full((args.batch,), args.prompt - 1 + i, dtype=torch.int32, device="cuda")
+        token = dec.run_step(token, pos).argmax(-1)
+        events[i + 1].record()
+    torch.cuda.synchronize()
+    step_ms = [events[i].elapsed_time(events[i + 1]) for i in range(args.new)]
+    decode_ms = events[0].elapsed_time(events[-1])
+    print(json.dumps({
+        "metric": "int4 decode tokens/sec" if args.bits == 4 else f"int{args.bits} decode tokens/sec",
+        "value": args.batch * args.new / (decode_ms / 1000.0), "unit": "tokens/s", "n_gpus": 1,
+        "batch": args.batch, "prompt": args.prompt, "new_tokens": args.new,
+        "p50_token_latency_ms": statistics.median(step_ms), "prefill_ms": start.elapsed_time(mid),
+        "higher_is_better": True, "impl": "native", "graph": dec.uses_graph, "weights": f"int{args.bits}"
+        + (f" g{group} fp16 scales" if args.bits == 4 else " per-channel" if args.bits == 8 else " bf16"),
+        "data": "synthetic seeded uniform prompt, random-init N(0,0.02) weights",
+    }))
+
+
+def run_reference(args, prompts, group):
+    import torch
+
+    src = os.path.join(ROOT, "baseline", "_ref", "src")
+    if not os.path.isdir(src):
+        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref/src is missing"}))
+        return
+    sys.path.insert(0, src)
+    from fast_decode import FastDecoder
+    from quantization import quantize_model
+    from quantweave_moe_model import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM
+
+    if args.batch != 1:
+        print(json.dumps({"impl": "reference", "unavailable": "the reference FastDecoder decodes batch 1 only "
+                          "(src/fast_decode.py); no batched decode path exists"}))
+        return
+    cfg = QuantaWeaveConfig(vocab_size=CONFIG["vocab_size"], hidden_size=CONFIG["hidden_size"], layers=CONFIG["layers"],
+                            ffn_size=CONFIG["ffn_size"], num_experts=CONFIG["num_experts"], top_k=CONFIG["top_k"],
+                            attention_heads=CONFIG["attention_heads"], max_sequence_length=args.prompt + max(args.new, 8) + 1)
+    model = QuantaWeaveMoEForCausalLM(cfg)
+    with torch.no_grad():
+        for _, param in model.named_parameters():
+            if param.dim() >= 2:
+                param.normal_(0.0, 0.02)
+    model = model.cuda().eval()
+    if args.bits != 16:
+        quantize_model(model, args.bits, group)
+    dec = FastDecoder(model, torch.device("cuda"))
+    ids = prompts[0].tolist()
+    list(dec.stream(ids, 8, temperature=0.0))
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dec.feed(ids)
+    torch.cuda.synchronize()
+    start.record()
+    token = int(dec.logits.argmax())
+    steps = []
+    for _ in range(args.new):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        token = int(dec.append(token).argmax())
+        e.record()
+        steps.append((s, e))
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    print(json.dumps({
+        "metric": f"int{args.bits} decode tokens/sec", "value": args.new / (ms / 1000.0), "unit": "tokens/s",
+        "n_gpus": 1, "batch": 1, "prompt": args.prompt, "new_tokens": args.new,
+        "p50_token_latency_ms": statistics.median(s.elapsed_time(e) for s, e in steps), "impl": "reference",
+        "description": dec.description}))
+
+
+if __name__ == "__main__":
+    main()

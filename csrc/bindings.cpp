@@ -366,6 +366,74 @@ void p2p_wait(Tensor flags, int64_t world, int64_t epoch, double timeout_s) {
   qw::p2p_wait(flags.data_ptr<int>(), static_cast<int>(world), static_cast<int>(epoch), timeout_s, stream());
 }
 
+// ------------------------------------------------------------------------------------------------ decode
+// w: [G, rows, ...] packed weights (uint8 / int8 / bf16 viewed as bytes), scales: fp16 or None (bf16 weights)
+void grouped_gemv(Tensor x, Tensor w, OptT scales, int64_t N, int64_t K, int64_t group, int64_t fmt, bool swiglu,
+                  OptT tok, OptT off, OptT cnt, int64_t groups, int64_t dense_rows, Tensor out, bool out_by_route,
+                  OptT bias, OptT resid, OptT active) {
+  CHECK_CUDA(x); CHECK_ROWS(x); CHECK_CONTIG(w); CHECK_ROWS(out);
+  TORCH_CHECK(x.scalar_type() == torch::kBFloat16 && out.scalar_type() == torch::kBFloat16);
+  if (scales) TORCH_CHECK(scales->scalar_type() == torch::kFloat16 && scales->is_contiguous());
+  const int64_t w_group_bytes = w.numel() * w.element_size() / groups;
+  const int64_t s_group = scales ? scales->numel() / groups : 0;
+  c10::cuda::CUDAGuard g(x.device());
+  qw::grouped_gemv(bptr(x), x.stride(0), w.data_ptr(), scales ? scales->data_ptr() : nullptr, w_group_bytes, s_group,
+                   static_cast<int>(N), static_cast<int>(K), static_cast<int>(group), static_cast<int>(fmt), swiglu,
+                   optptr<int>(tok), optptr<int>(off), optptr<int>(cnt), static_cast<int>(groups),
+                   static_cast<int>(dense_rows), bptr_mut(out), out.stride(0), out_by_route, optptr<float>(bias),
+                   optb(resid), resid ? resid->stride(0) : 0, optptr<int>(active),
+                   active ? static_cast<int>(active->numel()) : 0, stream());
+}
+
+void decode_route(Tensor x, Tensor wr, OptT ebias, int64_t k, double temperature, Tensor logits, Tensor cnt, Tensor off,
+                  Tensor order, Tensor route_slot, Tensor top_w, Tensor active, Tensor ticket) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DTYPE(wr, torch::kFloat32);
+  c10::cuda::CUDAGuard g(x.device());
+  qw::decode_route(bptr(x), wr.data_ptr<float>(), optptr<float>(ebias), static_cast<int>(x.size(0)),
+                   static_cast<int>(x.size(1)), static_cast<int>(wr.size(0)), static_cast<int>(k),
+                   static_cast<float>(temperature), logits.data_ptr<float>(), cnt.data_ptr<int>(), off.data_ptr<int>(),
+                   order.data_ptr<int>(), route_slot.data_ptr<int>(), top_w.data_ptr<float>(), active.data_ptr<int>(),
+                   ticket.data_ptr<int>(), stream());
+}
+
+int64_t decode_attn_chunks(int64_t Lmax) { return qw::decode_attn_chunks(static_cast<int>(Lmax)); }
+
+void decode_attention(Tensor q, Tensor kc, Tensor vc, Tensor lens, double scale, Tensor part_o, Tensor part_ml,
+                      Tensor tickets, Tensor out) {
+  CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(kc); CHECK_CONTIG(vc); CHECK_CONTIG(out);
+  const int B = static_cast<int>(kc.size(0)), Hkv = static_cast<int>(kc.size(1)), Lmax = static_cast<int>(kc.size(2));
+  const int D = static_cast<int>(kc.size(3)), Hq = static_cast<int>(q.size(1));
+  c10::cuda::CUDAGuard g(q.device());
+  qw::decode_attention(bptr(q), bptr(kc), bptr(vc), lens.data_ptr<int>(), B, Hq, Hkv, D, Lmax,
+                       static_cast<float>(scale), part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+                       tickets.data_ptr<int>(), bptr_mut(out), stream());
+}
+
+// tokens given: the input row is tok_emb[tokens[t]] (+ pos_emb[positions[t]]); else x[t]. y given: add the MoE output
+// sum_j top_w[t, j] * y[slot[t, j]]. Writes the residual to x_out (optional) and the normalised row to n_out.
+void decode_combine_norm(OptT x, OptT tokens, OptT tok_emb, OptT pos_emb, OptT positions, OptT y, OptT slot,
+                         OptT top_w, int64_t k, Tensor w, OptT bias, double eps, bool rms, OptT x_out, Tensor n_out) {
+  CHECK_CUDA(n_out); CHECK_CONTIG(n_out); CHECK_DTYPE(w, torch::kFloat32);
+  if (x) { CHECK_CONTIG((*x)); }
+  if (tokens) TORCH_CHECK(tokens->scalar_type() == torch::kInt64 && tok_emb && positions);
+  c10::cuda::CUDAGuard g(n_out.device());
+  qw::decode_combine_norm(optb(x), tokens ? tokens->data_ptr<int64_t>() : nullptr, optb(tok_emb), optb(pos_emb),
+                          optptr<int>(positions), optb(y), optptr<int>(slot), optptr<float>(top_w),
+                          static_cast<int>(k), static_cast<int>(n_out.size(0)), static_cast<int>(n_out.size(1)),
+                          w.data_ptr<float>(), optptr<float>(bias), static_cast<float>(eps), rms, optb_mut(x_out),
+                          bptr_mut(n_out), stream());
+}
+
+void rope_append(Tensor qkv, Tensor pos, int64_t Hq, int64_t Hkv, Tensor cos_t, Tensor sin_t, bool rope, Tensor q_out,
+                 Tensor kc, Tensor vc) {
+  CHECK_CUDA(qkv); CHECK_CONTIG(qkv);
+  const int B = static_cast<int>(qkv.size(0)), D = static_cast<int>(kc.size(3)), Lmax = static_cast<int>(kc.size(2));
+  c10::cuda::CUDAGuard g(qkv.device());
+  qw::rope_append(bptr(qkv), pos.data_ptr<int>(), B, static_cast<int>(Hq), static_cast<int>(Hkv), D, Lmax,
+                  cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), rope, bptr_mut(q_out), bptr_mut(kc), bptr_mut(vc),
+                  stream());
+}
+
 // ------------------------------------------------------------------------------------------------ status
 int64_t read_status(bool clear) {
   int s = qw::gemm_status(clear);
@@ -375,6 +443,7 @@ int64_t read_status(bool clear) {
   if ((t = qw::optim_status(clear)) && !s) s = t;
   if ((t = qw::attention_status(clear)) && !s) s = t;
   if ((t = qw::p2p_status(clear)) && !s) s = t;
+  if ((t = qw::decode_status(clear)) && !s) s = t;
   return s;
 }
 
@@ -418,6 +487,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("scale_bf16", &scale_bf16);
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("grouped_gemv", &grouped_gemv);
+  m.def("decode_attn_chunks", &decode_attn_chunks);
+  m.def("decode_route", &decode_route);
+  m.def("decode_attention", &decode_attention);
+  m.def("rope_append", &rope_append);
+  m.def("decode_combine_norm", &decode_combine_norm);
   m.def("p2p_push", &p2p_push);
   m.def("p2p_wait", &p2p_wait);
   m.def("read_status", &read_status, py::arg("clear") = true);

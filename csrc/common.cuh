@@ -254,6 +254,12 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Programmatic dependent launch: wait for the preceding grid's completion (and memory flush) / let the next grid's
+// blocks be scheduled. Both are no-ops when the launch carried no programmatic dependency.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

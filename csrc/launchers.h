@@ -123,4 +123,25 @@ void p2p_push(const void* src, int64_t block_bytes, void* const* peer_bufs, int*
 void p2p_wait(const int* flags, int world, int epoch, double timeout_s, cudaStream_t stream);
 int p2p_status(bool clear);
 
+// ---- decode.cu ----
+void grouped_gemv(const bf16* x, int64_t ldx, const void* w, const void* scales, int64_t w_group_bytes,
+                  int64_t s_group_elems, int N, int K, int group, int fmt, bool swiglu, const int* tok, const int* off,
+                  const int* cnt, int groups, int dense_rows, bf16* out, int64_t ldo, bool out_by_route,
+                  const float* bias, const bf16* resid, int64_t ldr, const int* active, int active_slots,
+                  cudaStream_t stream);
+int decode_attn_chunks(int Lmax);
+void decode_route(const bf16* x, const float* wr, const float* ebias, int T, int H, int E, int k, float temperature,
+                  float* logits, int* cnt, int* off, int* order, int* route_slot, float* top_w, int* active,
+                  int* ticket, cudaStream_t stream);
+void decode_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* lens, int B, int Hq, int Hkv, int D,
+                      int Lmax, float scale, float* part_o, float* part_ml, int* tickets, bf16* out,
+                      cudaStream_t stream);
+void rope_append(const bf16* qkv, const int* pos, int B, int Hq, int Hkv, int D, int Lmax, const float* cos_t,
+                 const float* sin_t, bool rope, bf16* q_out, bf16* kc, bf16* vc, cudaStream_t stream);
+void decode_combine_norm(const bf16* x, const int64_t* tokens, const bf16* tok_emb, const bf16* pos_emb,
+                         const int* positions, const bf16* y, const int* slot, const float* top_w, int k, int T, int H,
+                         const float* w, const float* bias, float eps, bool rms, bf16* x_out, bf16* n_out,
+                         cudaStream_t stream);
+int decode_status(bool clear);
+
 }  // namespace qw

@@ -28,7 +28,7 @@ from torch import Tensor, nn
 
 from ..config import QuantaWeaveConfig
 
-_EXPERT_KEY = re.compile(r"^experts\.(\d+)\.(gate|up|down)\.weight$")
+_EXPERT_KEY = re.compile(r"^experts\.(\d+)\.(gate|up|down)\.(weight|qweight|scales)$")
 
 
 class SparseSwiGLU(nn.Module):
@@ -250,8 +250,25 @@ class TopKMoE(nn.Module):
             (dropped // self.top_k, route_experts[dropped]),
         )
 
+    def expert_weights(self, index: int) -> tuple[Tensor, Tensor]:
+        """(gate|up [2F, H], down [H, F]) of one expert; quantised experts are dequantised on the fly."""
+        if getattr(self, "quant", None) is not None:
+            from ..inference.quantization import dequantized_expert
+
+            return dequantized_expert(self, index)
+        return self.w_gate_up[index], self.w_down[index]
+
     def expert_forward(self, index: int, x: Tensor) -> Tensor:
         f = self.ffn_local
+        if getattr(self, "quant", None) is not None or getattr(self, "lora", None) is not None:
+            wgu, wd = self.expert_weights(index)
+            wgu, wd = wgu.to(x.dtype), wd.to(x.dtype)
+            hidden = F.silu(F.linear(x, wgu[:f])) * F.linear(x, wgu[f:])
+            out = F.linear(hidden, wd)
+            lora = getattr(self, "lora", None)
+            if lora is not None:
+                out = out + lora.delta(index, x, hidden)
+            return out
         w = self.w_gate_up[index]
         hidden = F.silu(F.linear(x, w[:f])) * F.linear(x, w[f:])
         return F.linear(hidden, self.w_down[index])
@@ -344,6 +361,18 @@ class TopKMoE(nn.Module):
 # ---- checkpoint-format translation -------------------------------------------------------------
 def _expert_state_dict_hook(module: TopKMoE, state_dict: dict, prefix: str, local_metadata) -> None:
     """Replace the stacked tensors by the reference's per-expert keys (views, so nothing is copied)."""
+    if prefix + "q_gate_up" in state_dict:
+        q_gu, s_gu = state_dict.pop(prefix + "q_gate_up"), state_dict.pop(prefix + "s_gate_up")
+        q_d, s_d = state_dict.pop(prefix + "q_down"), state_dict.pop(prefix + "s_down")
+        f = module.ffn_local
+        for e in range(module.num_local_experts):
+            state_dict[f"{prefix}experts.{e}.gate.qweight"] = q_gu[e, :f]
+            state_dict[f"{prefix}experts.{e}.gate.scales"] = s_gu[e, :f].float()
+            state_dict[f"{prefix}experts.{e}.up.qweight"] = q_gu[e, f:]
+            state_dict[f"{prefix}experts.{e}.up.scales"] = s_gu[e, f:].float()
+            state_dict[f"{prefix}experts.{e}.down.qweight"] = q_d[e]
+            state_dict[f"{prefix}experts.{e}.down.scales"] = s_d[e].float()
+        return
     gate_up = state_dict.pop(prefix + "w_gate_up", None)
     down = state_dict.pop(prefix + "w_down", None)
     if gate_up is None or down is None:
@@ -359,15 +388,29 @@ def _expert_load_pre_hook(module: TopKMoE, state_dict: dict, prefix: str, local_
                           unexpected_keys, error_msgs) -> None:
     """Stack ``experts.{e}.{gate,up,down}.weight`` back into ``w_gate_up``/``w_down``."""
     found: dict[tuple[int, str], Tensor] = {}
+    quant: dict[tuple[int, str, str], Tensor] = {}
     for key in list(state_dict.keys()):
         if not key.startswith(prefix):
             continue
         match = _EXPERT_KEY.match(key[len(prefix):])
-        if match:
+        if match and match.group(3) == "weight":
             found[(int(match.group(1)), match.group(2))] = state_dict.pop(key)
+        elif match:
+            quant[(int(match.group(1)), match.group(2), match.group(3))] = state_dict.pop(key)
+    n = module.num_local_experts
+    if quant:
+        try:
+            state_dict[prefix + "q_gate_up"] = torch.stack(
+                [torch.cat([quant[(e, "gate", "qweight")], quant[(e, "up", "qweight")]]) for e in range(n)])
+            state_dict[prefix + "s_gate_up"] = torch.stack(
+                [torch.cat([quant[(e, "gate", "scales")], quant[(e, "up", "scales")]]) for e in range(n)]).half()
+            state_dict[prefix + "q_down"] = torch.stack([quant[(e, "down", "qweight")] for e in range(n)])
+            state_dict[prefix + "s_down"] = torch.stack([quant[(e, "down", "scales")] for e in range(n)]).half()
+        except KeyError as missing:
+            error_msgs.append(f"missing quantized expert tensor {missing} under {prefix}experts")
+        return
     if not found:
         return
-    n = module.num_local_experts
     try:
         gates = [found[(e, "gate")] for e in range(n)]
         ups = [found[(e, "up")] for e in range(n)]

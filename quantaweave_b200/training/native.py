@@ -27,6 +27,8 @@ def prepare_model(model, precision: str = "bf16", recompute_experts: bool | None
             if param.dtype != want:
                 param.data = param.data.to(want)
     for moe in model.moes():
+        if getattr(moe, "quant", None) is not None:
+            continue  # quantised experts are inference-only: the decoder's dequant-GEMV kernels serve them
         moe.kernel = "native"
         if recompute_experts is not None:
             moe.recompute_activations = bool(recompute_experts)
