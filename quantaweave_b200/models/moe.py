@@ -221,6 +221,8 @@ class TopKMoE(nn.Module):
     def _native_ok(self) -> bool:
         if self.kernel == "loop" or self.static_dispatch or self.profile_experts:
             return False
+        if getattr(self, "lora", None) is not None or getattr(self, "quant", None) is not None:
+            return False  # adapters / quantised bases run the per-expert path (the decoder serves quantised models)
         from ..ops import native_required
 
         native_required()
@@ -260,14 +262,18 @@ class TopKMoE(nn.Module):
 
     def expert_forward(self, index: int, x: Tensor) -> Tensor:
         f = self.ffn_local
-        if getattr(self, "quant", None) is not None or getattr(self, "lora", None) is not None:
+        lora = getattr(self, "lora", None)
+        if getattr(self, "quant", None) is not None or lora is not None:
             wgu, wd = self.expert_weights(index)
             wgu, wd = wgu.to(x.dtype), wd.to(x.dtype)
-            hidden = F.silu(F.linear(x, wgu[:f])) * F.linear(x, wgu[f:])
+            gate, up = F.linear(x, wgu[:f]), F.linear(x, wgu[f:])
+            if lora is not None:  # low-rank updates of the three projections (gate/up before the activation)
+                gate = gate + lora.project(index, "gate", x)
+                up = up + lora.project(index, "up", x)
+            hidden = F.silu(gate) * up
             out = F.linear(hidden, wd)
-            lora = getattr(self, "lora", None)
             if lora is not None:
-                out = out + lora.delta(index, x, hidden)
+                out = out + lora.project(index, "down", hidden)
             return out
         w = self.w_gate_up[index]
         hidden = F.silu(F.linear(x, w[:f])) * F.linear(x, w[f:])
