@@ -3,8 +3,8 @@
 
 Behaviour kept from the reference: no expert capacity at inference; a context of ``max_sequence_length - 1`` tokens
 (learned positions) with the oldest half dropped and re-read when it fills; ``feed``/``append``/``stream``/``warm``;
-sampling inside the step (greedy argmax or Gumbel-max with top-k/top-p filtering on seeded noise drawn outside the
-step); one host synchronisation per ``BATCH`` tokens when streaming.
+greedy argmax or Gumbel-max sampling with top-k/top-p filtering. ``stream`` reads each token id back to the host
+(callers check stop strings per token); ``generate`` keeps greedy tokens on the device.
 
 B200 design:
 
@@ -13,7 +13,8 @@ B200 design:
   grouped GEMV kernel, which streams each selected expert's rows once for all tokens routed to it;
 * split-K decode attention over a bf16 ``[B, Hkv, Lmax, D]`` cache (GQA heads packed per block), RoPE and the cache
   append fused in one kernel, routing by the fp32 router kernels with the capacity plan disabled;
-* the whole one-token step (all layers, the LM head and the sampler) is captured as one CUDA graph;
+* the whole one-token step (all layers and the LM head) is captured as one CUDA graph; every decode kernel is
+  launched with programmatic dependent launch so the next kernel's weight prefetch overlaps the previous one;
 * prefill runs the training kernels (tcgen05 GEMMs, flash attention, grouped SwiGLU) over the prompt.
 
 On CPU the same step runs as plain fp32 PyTorch (the oracle the GPU path is tested against).

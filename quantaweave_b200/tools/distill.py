@@ -117,14 +117,15 @@ def run_distillation(args) -> dict:
         from ..training.native import prepare_model
 
         prepare_model(model, "bf16")
-    optimizer = build_optimizer("adamw", list(model.parameters()), args.lr, device=device)
-    start_step = 0
-    if args.resume and checkpoint_exists(args.checkpoint_dir):
-        start_step = load_checkpoint(args.checkpoint_dir, model, optimizer, device)
-        print(f"resumed distillation from step {start_step}")
-    else:
+    resume = args.resume and checkpoint_exists(args.checkpoint_dir)
+    if not resume:  # weights first: the fused optimizer snapshots fp32 master copies when it is built
         model.load_state_dict(load_file(args.student / "model.pt", map_location="cpu")["model"])
         print(f"initialised from student weights at {args.student / 'model.pt'}")
+    optimizer = build_optimizer("adamw", list(model.parameters()), args.lr, device=device)
+    start_step = 0
+    if resume:
+        start_step = load_checkpoint(args.checkpoint_dir, model, optimizer, device)
+        print(f"resumed distillation from step {start_step}")
     mode = "cross-tokenizer" if cross is not None else "logit" if teacher is not None else "sequence"
     print(f"distillation mode: {mode}")
     model.train()

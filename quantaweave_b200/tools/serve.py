@@ -1,0 +1,423 @@
+"""Serve a checkpoint over HTTP (FastAPI).
+
+    python -m quantaweave_b200.tools.serve --latest --host 127.0.0.1 --port 8000
+    curl -s localhost:8000/generate -d '{"prompt": "Once upon a time", "temperature": 0}'
+    curl -s localhost:8000/chat -d '{"messages": [{"role": "user", "content": "hi"}]}'
+    curl -N localhost:8000/generate/stream -d '{"prompt": "Once upon a time", "tokens": 200}'   # SSE
+
+Parity with the reference ``src/serve_quantweave.py`` (routes ``/health``, ``/metrics``, ``/generate``, ``/chat``,
+``/generate/stream`` :377-413; ``RateLimiter`` :114, ``Moderation`` :138, Prometheus ``Metrics`` :158, ``Server``
+:217-345 with the queue / timeout / API-key semantics; JSON logs :84-106). Requests reuse the chat tool's
+``ChatSession`` so a request behaves like the equivalent ``tools.chat -m`` call. The decoder's KV cache is per-request
+state, so requests are serialised behind an asyncio lock and generation runs in a worker thread.
+
+Hardening, all opt-in: ``--api-key`` (Bearer or X-API-Key on every route but /health), ``--rate-limit`` per caller per
+``--rate-limit-window``, ``--max-queue`` (429 once that many wait), ``--request-timeout`` (503 when a request waits
+that long to START; a generation in progress is never cancelled), ``--moderation-blocklist`` (422 on a regex match;
+a keyword guardrail, not a safety system).
+"""
+
+import argparse
+import asyncio
+import json
+import logging
+import re
+import time
+import uuid
+from collections import defaultdict, deque
+from pathlib import Path
+from typing import Optional
+
+import torch
+from pydantic import BaseModel, Field
+
+from .chat import DEFAULT_CHECKPOINT, ChatSession, Settings, load_for_chat, resolve_model
+
+logger = logging.getLogger("quantaweave_b200.serve")
+
+
+class GenerateRequest(BaseModel):
+    prompt: str
+    tokens: int = Field(200, ge=1, le=8192)
+    temperature: float = Field(0.8, ge=0)
+    top_k: int = Field(0, ge=0)
+    top_p: float = Field(1.0, gt=0, le=1)
+    seed: Optional[int] = None
+    stop: list[str] = Field(default_factory=list)
+
+
+class ChatMessage(BaseModel):
+    role: str
+    content: str
+
+
+class ChatRequest(BaseModel):
+    messages: list[ChatMessage]
+    system: str = ""
+    tokens: int = Field(200, ge=1, le=8192)
+    temperature: float = Field(0.8, ge=0)
+    top_k: int = Field(0, ge=0)
+    top_p: float = Field(1.0, gt=0, le=1)
+    seed: Optional[int] = None
+
+
+class JSONLogFormatter(logging.Formatter):
+    """One JSON object per line: time, level, message and every ``extra=`` field."""
+
+    _STANDARD = set(vars(logging.LogRecord("", 0, "", 0, "", (), None))) | {"message", "asctime"}
+
+    def format(self, record: logging.LogRecord) -> str:
+        payload = {"time": self.formatTime(record, "%Y-%m-%dT%H:%M:%S"), "level": record.levelname,
+                   "message": record.getMessage()}
+        payload.update({k: v for k, v in vars(record).items() if k not in self._STANDARD})
+        return json.dumps(payload, default=str)
+
+
+def configure_logging(log_format: str) -> None:
+    handler = logging.StreamHandler()
+    handler.setFormatter(JSONLogFormatter() if log_format == "json"
+                         else logging.Formatter("%(asctime)s %(levelname)s %(message)s"))
+    logger.handlers = [handler]
+    logger.setLevel(logging.INFO)
+    logger.propagate = False
+
+
+class RateLimiter:
+    """At most ``limit`` calls per ``window`` seconds per key (sliding window, in memory); ``None`` disables it."""
+
+    def __init__(self, limit: Optional[int], window: float = 60.0) -> None:
+        self.limit, self.window = limit, window
+        self.hits: dict[str, deque] = defaultdict(deque)
+
+    def allow(self, key: str) -> bool:
+        if self.limit is None:
+            return True
+        now = time.monotonic()
+        recent = self.hits[key]
+        while recent and now - recent[0] > self.window:
+            recent.popleft()
+        if len(recent) >= self.limit:
+            return False
+        recent.append(now)
+        return True
+
+
+class Moderation:
+    """Case-insensitive regex blocklist (one pattern per line; blank and ``#`` lines ignored)."""
+
+    def __init__(self, patterns_file: Optional[Path]) -> None:
+        self.patterns: list[re.Pattern] = []
+        if patterns_file is not None:
+            for line in Path(patterns_file).read_text().splitlines():
+                line = line.strip()
+                if line and not line.startswith("#"):
+                    self.patterns.append(re.compile(line, re.IGNORECASE))
+
+    def blocked(self, text: str) -> Optional[str]:
+        return next((p.pattern for p in self.patterns if p.search(text)), None)
+
+
+class Metrics:
+    """Prometheus text exposition: requests by route/status, errors, request seconds, tokens, in-flight gauge."""
+
+    def __init__(self) -> None:
+        self.requests_total: dict[tuple[str, int], int] = defaultdict(int)
+        self.errors_total: dict[str, int] = defaultdict(int)
+        self.seconds_sum: dict[str, float] = defaultdict(float)
+        self.seconds_count: dict[str, int] = defaultdict(int)
+        self.tokens_generated_total = 0
+        self.requests_in_flight = 0
+
+    def observe(self, route: str, status: int, seconds: float, tokens: int = 0) -> None:
+        self.requests_total[(route, status)] += 1
+        if status >= 400:
+            self.errors_total[route] += 1
+        self.seconds_sum[route] += seconds
+        self.seconds_count[route] += 1
+        self.tokens_generated_total += tokens
+
+    def render(self) -> str:
+        out = ["# HELP quantweave_requests_total Total requests by route and status.",
+               "# TYPE quantweave_requests_total counter"]
+        out += [f'quantweave_requests_total{{route="{r}",status="{s}"}} {n}'
+                for (r, s), n in sorted(self.requests_total.items())]
+        out += ["# HELP quantweave_errors_total Total error responses (status >= 400) by route.",
+                "# TYPE quantweave_errors_total counter"]
+        out += [f'quantweave_errors_total{{route="{r}"}} {n}' for r, n in sorted(self.errors_total.items())]
+        out += ["# HELP quantweave_request_seconds_sum Total request handling seconds by route.",
+                "# TYPE quantweave_request_seconds_sum counter"]
+        for r in sorted(self.seconds_sum):
+            out.append(f'quantweave_request_seconds_sum{{route="{r}"}} {self.seconds_sum[r]:.6f}')
+            out.append(f'quantweave_request_seconds_count{{route="{r}"}} {self.seconds_count[r]}')
+        out += ["# HELP quantweave_tokens_generated_total Total tokens generated across all requests.",
+                "# TYPE quantweave_tokens_generated_total counter",
+                f"quantweave_tokens_generated_total {self.tokens_generated_total}",
+                "# HELP quantweave_requests_in_flight Requests currently being handled.",
+                "# TYPE quantweave_requests_in_flight gauge",
+                f"quantweave_requests_in_flight {self.requests_in_flight}"]
+        return "\n".join(out) + "\n"
+
+
+def reply_payload(reply) -> dict:
+    return {"text": reply.response, "tokens": reply.tokens, "seconds": reply.seconds,
+            "tokens_per_second": reply.tokens_per_second, "stop_reason": reply.stop_reason,
+            "unknown_characters": reply.unknown_characters, "truncated_context": reply.truncated_context}
+
+
+class Server:
+    """The loaded model, with access to its stateful decoder serialised across requests."""
+
+    def __init__(self, checkpoint, adapter, device: torch.device, precision: str, use_cache: bool = True, *,
+                 api_key: Optional[str] = None, rate_limit: Optional[int] = None, rate_limit_window: float = 60.0,
+                 request_timeout: Optional[float] = None, max_queue: Optional[int] = None,
+                 moderation_patterns: Optional[Path] = None, sessions: Optional[tuple] = None) -> None:
+        from ..utils.hardware import choose_precision, detect
+
+        self.checkpoint, self.adapter, self.device = checkpoint, adapter, device
+        self.precision = choose_precision(detect(device.type), precision)
+        if sessions is None:
+            model, tokenizer = load_for_chat(checkpoint, adapter, 0, device)
+            complete = ChatSession(model, tokenizer, device, self.precision, Settings(mode="complete"), use_cache)
+            chat = ChatSession(model, tokenizer, device, self.precision, Settings(mode="chat"), use_cache=False)
+            chat.decoder, chat.cache_note = complete.decoder, complete.cache_note  # one decoder (and graph) per model
+            sessions = (complete, chat)
+        self.complete_session, self.chat_session = sessions
+        self.lock = asyncio.Lock()
+        self.started_at = time.time()
+        self.requests_served = 0
+        self.api_key = api_key
+        self.rate_limiter = RateLimiter(rate_limit, rate_limit_window)
+        self.request_timeout, self.max_queue = request_timeout, max_queue
+        self.waiting = 0
+        self.moderation = Moderation(moderation_patterns)
+        self.metrics = Metrics()
+
+    def info(self) -> dict:
+        s = self.complete_session
+        return {"checkpoint": str(self.checkpoint), "adapter": str(self.adapter) if self.adapter else None,
+                "device": str(self.device), "precision": self.precision, "decoding": s.cache_note,
+                "tokenizer": s.tokenizer.kind, "vocab_size": s.tokenizer.vocab_size,
+                "context_length": s.model.config.max_sequence_length - 1,
+                "uptime_seconds": time.time() - self.started_at, "requests_served": self.requests_served,
+                "auth_required": self.api_key is not None, "rate_limit": self.rate_limiter.limit,
+                "request_timeout": self.request_timeout, "max_queue": self.max_queue}
+
+    async def _acquire(self) -> None:
+        """Take the generation lock. A request that finds it free always proceeds (even ``max_queue=0``); one that
+        must wait is refused past ``max_queue`` waiters and gives up after ``request_timeout`` seconds."""
+        from fastapi import HTTPException
+
+        if not self.lock.locked():
+            await self.lock.acquire()
+            return
+        if self.max_queue is not None and self.waiting >= self.max_queue:
+            raise HTTPException(429, f"too many requests already queued (max {self.max_queue})")
+        self.waiting += 1
+        try:
+            if self.request_timeout is None:
+                await self.lock.acquire()
+            else:
+                try:
+                    await asyncio.wait_for(self.lock.acquire(), timeout=self.request_timeout)
+                except asyncio.TimeoutError:
+                    raise HTTPException(503, f"timed out after {self.request_timeout}s waiting to start "
+                                             "(the server may still be busy with an earlier request)") from None
+        finally:
+            self.waiting -= 1
+
+    def _check(self, text: str, what: str) -> None:
+        from fastapi import HTTPException
+
+        pattern = self.moderation.blocked(text)
+        if pattern is not None:
+            raise HTTPException(422, f"{what} blocked by moderation pattern: {pattern}")
+
+    def _complete_settings(self, r: GenerateRequest) -> Settings:
+        return Settings(mode="complete", tokens=r.tokens, temperature=r.temperature, top_k=r.top_k, top_p=r.top_p,
+                        seed=r.seed, stop=r.stop)
+
+    async def generate(self, request: GenerateRequest) -> dict:
+        self._check(request.prompt, "prompt")
+        await self._acquire()
+        try:
+            self.complete_session.settings = self._complete_settings(request)
+            reply = await asyncio.to_thread(self.complete_session.send, request.prompt)
+            self.requests_served += 1
+        finally:
+            self.lock.release()
+        self.metrics.tokens_generated_total += reply.tokens
+        return reply_payload(reply)
+
+    async def chat(self, request: ChatRequest) -> dict:
+        from fastapi import HTTPException
+
+        if not request.messages or request.messages[-1].role != "user":
+            raise HTTPException(422, "messages must end with a 'user' turn")
+        self._check(request.messages[-1].content, "message")
+        await self._acquire()
+        try:
+            session = self.chat_session
+            session.reset()
+            session.settings = Settings(mode="chat", tokens=request.tokens, temperature=request.temperature,
+                                        top_k=request.top_k, top_p=request.top_p, seed=request.seed,
+                                        system=request.system)
+            for turn in request.messages[:-1]:
+                if turn.role == "user":
+                    session.history.append((turn.content, ""))
+                elif turn.role == "assistant" and session.history:
+                    session.history[-1] = (session.history[-1][0], turn.content)
+            reply = await asyncio.to_thread(session.send, request.messages[-1].content)
+            self.requests_served += 1
+        finally:
+            self.lock.release()
+        self.metrics.tokens_generated_total += reply.tokens
+        return reply_payload(reply)
+
+    async def stream_generate(self, request: GenerateRequest):
+        """Server-sent events: ``data: {"text": ...}`` per piece, then ``event: done`` with the full reply."""
+        self._check(request.prompt, "prompt")
+        await self._acquire()
+        try:
+            self.complete_session.settings = self._complete_settings(request)
+            queue: asyncio.Queue = asyncio.Queue()
+            loop = asyncio.get_running_loop()
+            done = object()
+
+            def on_text(piece: str) -> None:
+                loop.call_soon_threadsafe(queue.put_nowait, piece)
+
+            async def run():
+                reply = await asyncio.to_thread(self.complete_session.send, request.prompt, on_text)
+                loop.call_soon_threadsafe(queue.put_nowait, done)
+                return reply
+
+            task = asyncio.ensure_future(run())
+            try:
+                while (item := await queue.get()) is not done:
+                    yield f"data: {json.dumps({'text': item})}\n\n"
+                reply = await task
+                self.requests_served += 1
+                self.metrics.tokens_generated_total += reply.tokens
+                yield f"event: done\ndata: {json.dumps(reply_payload(reply))}\n\n"
+            finally:
+                if not task.done():
+                    task.cancel()
+        finally:
+            self.lock.release()
+
+
+def build_app(server: Server):
+    from fastapi import Depends, FastAPI, HTTPException, Request
+    from fastapi.responses import PlainTextResponse, StreamingResponse
+
+    app = FastAPI(title="QuantaWeave-B200 inference server")
+
+    def require_auth(request: Request) -> None:
+        if server.api_key is None:
+            return
+        header = request.headers.get("authorization", "")
+        key = header[7:] if header.lower().startswith("bearer ") else request.headers.get("x-api-key", "")
+        if key != server.api_key:
+            raise HTTPException(401, "invalid or missing API key (Authorization: Bearer <key> or X-API-Key: <key>)")
+
+    def require_rate_limit(request: Request) -> None:
+        caller = request.headers.get("x-api-key") or (request.client.host if request.client else "unknown")
+        if not server.rate_limiter.allow(caller):
+            raise HTTPException(429, "rate limit exceeded")
+
+    async def timed(route: str, handler):
+        request_id = uuid.uuid4().hex[:12]
+        server.metrics.requests_in_flight += 1
+        started = time.perf_counter()
+        status = 200
+        try:
+            return await handler()
+        except HTTPException as error:
+            status = error.status_code
+            raise
+        except ValueError as error:
+            status = 422
+            raise HTTPException(422, str(error)) from error
+        except Exception:
+            status = 500
+            raise
+        finally:
+            seconds = time.perf_counter() - started
+            server.metrics.requests_in_flight -= 1
+            server.metrics.observe(route, status, seconds)
+            logger.log(logging.INFO if status < 400 else logging.WARNING, f"{route} {status} {seconds:.3f}s",
+                       extra={"request_id": request_id, "route": route, "status": status,
+                              "seconds": round(seconds, 4)})
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok", **server.info()}
+
+    @app.get("/metrics")
+    async def metrics(_auth: None = Depends(require_auth)):
+        return PlainTextResponse(server.metrics.render(), media_type="text/plain; version=0.0.4")
+
+    @app.post("/generate")
+    async def generate(request: GenerateRequest, _auth: None = Depends(require_auth),
+                       _rate: None = Depends(require_rate_limit)):
+        return await timed("/generate", lambda: server.generate(request))
+
+    @app.post("/chat")
+    async def chat(request: ChatRequest, _auth: None = Depends(require_auth),
+                   _rate: None = Depends(require_rate_limit)):
+        return await timed("/chat", lambda: server.chat(request))
+
+    @app.post("/generate/stream")
+    async def generate_stream(request: GenerateRequest, _auth: None = Depends(require_auth),
+                              _rate: None = Depends(require_rate_limit)):
+        return StreamingResponse(server.stream_generate(request), media_type="text/event-stream")
+
+    app.state.server = server
+    return app
+
+
+def build_parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--checkpoint", type=Path, help=f"a checkpoint directory (default {DEFAULT_CHECKPOINT})")
+    p.add_argument("--run", help="an archived run: its epoch id under artifacts/runs, or the folder path")
+    p.add_argument("--latest", action="store_true", help="the newest archived run that contains a model")
+    p.add_argument("--adapter", type=Path, help="a QLoRA adapter directory")
+    p.add_argument("--runs-dir", type=Path, default=Path("artifacts/runs"))
+    p.add_argument("--no-cache", action="store_true", help="plain forward pass per token instead of the KV cache")
+    p.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")
+    p.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
+    p.add_argument("--host", default="127.0.0.1")
+    p.add_argument("--port", type=int, default=8000)
+    h = p.add_argument_group("hardening")
+    h.add_argument("--api-key", help="require this key (Authorization: Bearer or X-API-Key) on every route but /health")
+    h.add_argument("--rate-limit", type=int, help="429 past this many requests per --rate-limit-window per caller")
+    h.add_argument("--rate-limit-window", type=float, default=60.0)
+    h.add_argument("--request-timeout", type=float, help="503 when a request waits this long merely to start")
+    h.add_argument("--max-queue", type=int, help="429 once this many requests are already waiting to start")
+    h.add_argument("--moderation-blocklist", type=Path, help="regex patterns (one per line); a match is a 422")
+    h.add_argument("--log-format", choices=("text", "json"), default="text")
+    return p
+
+
+def main(argv=None) -> None:
+    from ..training.trainer import select_device
+
+    args = build_parser().parse_args(argv)
+    configure_logging(args.log_format)
+    checkpoint, adapter = resolve_model(args.checkpoint, args.adapter, args.run, args.latest, args.runs_dir)
+    device = select_device(args.device)
+    server = Server(checkpoint, adapter, device, args.precision, use_cache=not args.no_cache, api_key=args.api_key,
+                    rate_limit=args.rate_limit, rate_limit_window=args.rate_limit_window,
+                    request_timeout=args.request_timeout, max_queue=args.max_queue,
+                    moderation_patterns=args.moderation_blocklist)
+    print(f"model: {checkpoint}" + (f" + adapter {adapter}" if adapter else "")
+          + f"  device: {device}  decoding: {server.complete_session.cache_note}")
+    if server.api_key is None:
+        print("WARNING: no --api-key set; this server accepts unauthenticated requests from anyone who can reach it.")
+    import uvicorn
+
+    uvicorn.run(build_app(server), host=args.host, port=args.port, log_level="info")
+
+
+if __name__ == "__main__":
+    main()
