@@ -40,6 +40,7 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--trace", help="write a chrome trace of one extra (untimed) step to this path (diagnostics)")
     p.add_argument("--impl", choices=("native", "reference"), default="native")
     p.add_argument("--seqs-per-gpu", type=int, default=32)
     p.add_argument("--seq-len", type=int, default=2048)
@@ -108,6 +109,17 @@ def kernel_breakdown(step_fn) -> None:
     print(f"kernel breakdown: {grand / 1e3:.1f} ms of device time in one step", file=sys.stderr)
     for name, (t, n) in sorted(totals.items(), key=lambda kv: -kv[1][0])[:40]:
         print(f"  {100 * t / grand:5.1f}%  {t / 1e3:8.2f} ms  x{n:<5d} {name}", file=sys.stderr)
+
+
+def save_trace(step_fn, path: str) -> None:
+    """Chrome trace (host + device timeline) of one step, for finding idle gaps; diagnostics only."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        step_fn()
+        torch.cuda.synchronize()
+    prof.export_chrome_trace(path)
 
 
 # ================================================================================================ native arm
@@ -192,6 +204,8 @@ def run_native(args, rank, world, local):
     launches = count_launches(lambda: train_step(host_batches[-1].to("cuda"))) * args.steps
     if args.kernel_breakdown and rank == 0:
         kernel_breakdown(lambda: train_step(host_batches[-1].to("cuda")))
+    if args.trace and rank == 0:
+        save_trace(lambda: train_step(host_batches[-1].to("cuda")), args.trace)
     peak_gb = torch.cuda.max_memory_allocated() / 1e9
     emit(rank, {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,

@@ -147,6 +147,16 @@ void norm_fwd(Tensor x, OptT delta, OptT x_out, Tensor w, OptT b, Tensor y, OptT
 
 int64_t norm_bwd_blocks(int64_t rows) { return qw::norm_bwd_blocks(rows); }
 
+int64_t bias_grad_slabs(int64_t rows) { return qw::bias_grad_slabs(rows); }
+
+// out[c] (+)= sum_r g[r, c] in fp32 (deterministic two-stage reduction); part: [bias_grad_slabs(rows), N] fp32
+void bias_grad(Tensor g, Tensor part, Tensor out, bool accumulate) {
+  CHECK_CUDA(g); CHECK_ROWS(g); CHECK_DTYPE(out, torch::kFloat32); CHECK_DTYPE(part, torch::kFloat32);
+  c10::cuda::CUDAGuard guard(g.device());
+  qw::bias_grad(bptr(g), g.stride(0), g.size(0), static_cast<int>(g.size(1)), part.data_ptr<float>(),
+                out.data_ptr<float>(), accumulate, stream());
+}
+
 void norm_bwd(Tensor dy, Tensor x, Tensor w, OptT mean, Tensor rstd, OptT dres, Tensor dx, Tensor dw_part,
               OptT db_part, Tensor dw, OptT db, bool rms, bool accumulate) {
   CHECK_CUDA(dy); CHECK_CONTIG(dy); CHECK_CONTIG(x); CHECK_CONTIG(dx);
@@ -492,6 +502,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_route", &decode_route);
   m.def("decode_attention", &decode_attention);
   m.def("rope_append", &rope_append);
+  m.def("bias_grad_slabs", &bias_grad_slabs);
+  m.def("bias_grad", &bias_grad);
   m.def("decode_combine_norm", &decode_combine_norm);
   m.def("p2p_push", &p2p_push);
   m.def("p2p_wait", &p2p_wait);

@@ -45,6 +45,9 @@ int gemm_status(bool clear);
 void norm_fwd(const bf16* x, const bf16* delta, bf16* x_out, const float* w, const float* b, bf16* y, float* mean,
               float* rstd, int64_t rows, int H, float eps, bool rms, cudaStream_t stream);
 int norm_bwd_blocks(int64_t rows);
+int bias_grad_slabs(int64_t rows);
+void bias_grad(const bf16* g, int64_t ldg, int64_t rows, int N, float* part, float* out, bool accumulate,
+               cudaStream_t stream);
 void norm_bwd(const bf16* dy, const bf16* x, const float* w, const float* mean, const float* rstd, const bf16* dres,
               bf16* dx, float* dw_part, float* db_part, float* dw, float* db, int64_t rows, int H, bool rms,
               bool accumulate, cudaStream_t stream);

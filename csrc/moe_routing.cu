@@ -24,43 +24,63 @@ namespace {
 // ------------------------------------------------------------------------------------------------ SIMT GEMM
 // C[M,N] (+)= alpha * sum_k A[m,k] * B[k,n], generic strides, fp32 accumulate; split-K along gridDim.z writes
 // partial slabs C + z*M*N (reduced by a fixed-order kernel).
-template <typename TA, typename TB>
+// C[M,N] (+)= alpha * A[M,K] . B[K,N], fp32 FMA (the router runs in fp32). 64x64 tile, BK = 32, 256 threads with 4x4
+// outputs each. Global loads are coalesced along whichever dimension of A / B is contiguous (A_KC: A's K is
+// contiguous, else its M; B_KC: B's K is contiguous, else its N); the next K-slab is fetched into registers while the
+// current one is multiplied. grid.z splits K into chunks written to separate slabs (reduced in a fixed order).
+template <typename TA, typename TB, bool A_KC, bool B_KC>
 __global__ void __launch_bounds__(256) simt_gemm_kernel(const TA* __restrict__ A, int64_t sam, int64_t sak,
                                                         const TB* __restrict__ B, int64_t sbk, int64_t sbn,
                                                         float* __restrict__ C, int64_t ldc, int M, int N, int K,
                                                         int k_chunk, float alpha, int accumulate) {
-  __shared__ float As[16][68];
-  __shared__ float Bs[16][68];
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  constexpr int BM = 64, BN = 64, BK = 32;
+  __shared__ __align__(16) float As[BK][BM + 4];
+  __shared__ __align__(16) float Bs[BK][BN + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
   const int kbeg = blockIdx.z * k_chunk;
   const int kend = min(K, kbeg + k_chunk);
-  float acc[4][4] = {};
-  for (int k0 = kbeg; k0 < kend; k0 += 16) {
-    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
-      const int kk = i / 64, mm = i % 64;
-      const int gm = m0 + mm, gk = k0 + kk;
-      float a = 0.f, b = 0.f;
-      if (gm < M && gk < kend) a = to_float(A[gm * sam + gk * sak]);
-      const int gn = n0 + mm;
-      if (gn < N && gk < kend) b = to_float(B[gk * sbk + gn * sbn]);
-      As[kk][mm] = a;
-      Bs[kk][mm] = b;
+  float ra[8], rb[8];  // 64*32 / 256 = 8 elements of each tile per thread
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + 256 * i;
+      const int mm = A_KC ? idx / BK : idx % BM;
+      const int ka = A_KC ? idx % BK : idx / BM;
+      const int gm = m0 + mm, gk = k0 + ka;
+      ra[i] = (gm < M && gk < kend) ? to_float(A[gm * sam + gk * sak]) : 0.f;
+      const int nn = B_KC ? idx / BK : idx % BN;
+      const int kb = B_KC ? idx % BK : idx / BN;
+      const int gn = n0 + nn, gkb = k0 + kb;
+      rb[i] = (gn < N && gkb < kend) ? to_float(B[gkb * sbk + gn * sbn]) : 0.f;
     }
+  };
+  auto stash = [&]() {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + 256 * i;
+      As[A_KC ? idx % BK : idx / BM][A_KC ? idx / BK : idx % BM] = ra[i];
+      Bs[B_KC ? idx % BK : idx / BN][B_KC ? idx / BK : idx % BN] = rb[i];
+    }
+  };
+  float acc[4][4] = {};
+  if (kbeg < kend) fetch(kbeg);
+  for (int k0 = kbeg; k0 < kend; k0 += BK) {
     __syncthreads();
+    stash();
+    __syncthreads();
+    if (k0 + BK < kend) fetch(k0 + BK);  // next slab in flight during the math
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
-      float a[4], b[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx * 4 + j];
+    for (int kk = 0; kk < BK; ++kk) {
+      const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] += a[i] * b[j];
+        for (int j = 0; j < 4; ++j) acc[i][j] += av[i] * bv[j];
     }
-    __syncthreads();
   }
   float* Cz = C + static_cast<int64_t>(blockIdx.z) * M * ldc;
 #pragma unroll
@@ -72,7 +92,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const TA* __restrict__ A
       const int gn = n0 + tx * 4 + j;
       if (gn >= N) continue;
       const float v = alpha * acc[i][j];
-      Cz[gm * ldc + gn] = accumulate ? Cz[gm * ldc + gn] + v : v;
+      Cz[static_cast<int64_t>(gm) * ldc + gn] = accumulate ? Cz[static_cast<int64_t>(gm) * ldc + gn] + v : v;
     }
   }
 }
@@ -516,20 +536,30 @@ __global__ void router_bwd_kernel(const float* __restrict__ probs, const int* __
   }
 }
 
+template <typename TA, typename TB, bool AK, bool BK>
+void launch_simt(dim3 grid, const TA* A, int64_t sam, int64_t sak, const TB* B, int64_t sbk, int64_t sbn, float* C,
+                 int64_t ldc, int M, int N, int K, int k_chunk, float alpha, int accumulate, cudaStream_t stream) {
+  simt_gemm_kernel<TA, TB, AK, BK><<<grid, 256, 0, stream>>>(A, sam, sak, B, sbk, sbn, C, ldc, M, N, K, k_chunk, alpha,
+                                                             accumulate);
+}
+
 template <typename TA, typename TB>
 void simt_gemm(const TA* A, int64_t sam, int64_t sak, const TB* B, int64_t sbk, int64_t sbn, float* C, int64_t ldc,
                int M, int N, int K, float alpha, bool accumulate, float* workspace, int split_k, cudaStream_t stream) {
   if (M == 0 || N == 0) return;
-  split_k = std::max(1, std::min(split_k, (K + 15) / 16));
-  const int k_chunk = ((K + split_k - 1) / split_k + 15) / 16 * 16;
+  split_k = std::max(1, std::min(split_k, (K + 31) / 32));
+  const int k_chunk = ((K + split_k - 1) / split_k + 31) / 32 * 32;
   split_k = std::max(1, (K + k_chunk - 1) / k_chunk);
   dim3 grid((N + 63) / 64, (M + 63) / 64, split_k);
-  if (split_k == 1) {
-    simt_gemm_kernel<TA, TB><<<grid, 256, 0, stream>>>(A, sam, sak, B, sbk, sbn, C, ldc, M, N, K, k_chunk, alpha,
-                                                       accumulate);
-  } else {
-    simt_gemm_kernel<TA, TB><<<grid, 256, 0, stream>>>(A, sam, sak, B, sbk, sbn, workspace, N, M, N, K, k_chunk, alpha,
-                                                       0);
+  const bool ak = sak == 1, bk = sbk == 1;  // which dimension of each operand is contiguous
+  float* out = split_k == 1 ? C : workspace;
+  const int64_t ld = split_k == 1 ? ldc : N;
+  const int acc = split_k == 1 && accumulate ? 1 : 0;
+  if (ak && bk) launch_simt<TA, TB, true, true>(grid, A, sam, sak, B, sbk, sbn, out, ld, M, N, K, k_chunk, alpha, acc, stream);
+  else if (ak) launch_simt<TA, TB, true, false>(grid, A, sam, sak, B, sbk, sbn, out, ld, M, N, K, k_chunk, alpha, acc, stream);
+  else if (bk) launch_simt<TA, TB, false, true>(grid, A, sam, sak, B, sbk, sbn, out, ld, M, N, K, k_chunk, alpha, acc, stream);
+  else launch_simt<TA, TB, false, false>(grid, A, sam, sak, B, sbk, sbn, out, ld, M, N, K, k_chunk, alpha, acc, stream);
+  if (split_k > 1) {
     const int64_t n = static_cast<int64_t>(M) * N;
     slab_sum_kernel<<<static_cast<int>((n + 255) / 256), 256, 0, stream>>>(workspace, split_k, n, C, accumulate);
   }

@@ -53,7 +53,10 @@ class _LinearFn(torch.autograd.Function):
                              if ctx.weight_dtype in (torch.bfloat16, torch.float32) else torch.float32)
             C.linear_wgrad(g2, x2, dw, False)
         if ctx.has_bias and ctx.needs_input_grad[2]:
-            db = g2.float().sum(0).to(ctx.bias_dtype)
+            db = torch.empty(g2.size(1), device=grad.device, dtype=torch.float32)
+            part = torch.empty(C.bias_grad_slabs(g2.size(0)), g2.size(1), device=grad.device, dtype=torch.float32)
+            C.bias_grad(g2, part, db, False)
+            db = db.to(ctx.bias_dtype)
         if ctx.has_res and ctx.needs_input_grad[3]:
             dres = grad
         return dx, dw, db, dres

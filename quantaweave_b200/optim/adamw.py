@@ -49,26 +49,41 @@ class FusedAdamW(torch.optim.Optimizer):
                 yield group, p
 
     def _build_tables(self, params: list[Tensor], device) -> tuple[Tensor, Tensor, Tensor]:
-        """AdamTensor records (8 x int64 each) and the chunk -> (tensor, start) map."""
+        """AdamTensor records (8 x int64 each) and the chunk -> (tensor, start) map.
+
+        The chunk map depends only on the tensor sizes and is cached; the records are rebuilt only when a pointer or
+        a per-tensor factor changed (gradients are usually reallocated every step), so the host cost per step is one
+        small table, not one Python entry per chunk."""
+        import struct
+
         C = ext()
-        chunk = C.adam_chunk_size()
-        rows, chunk_tensor, chunk_start = [], [], []
-        for index, p in enumerate(params):
+        rows = []
+        for p in params:
             st = self.state[p]
             g = p.grad
-            grad_dtype = 0 if g.dtype == torch.float32 else 1
-            import struct
-
-            tail = struct.unpack("<q", struct.pack("<if", grad_dtype, float(st["decay_scale"])))[0]
+            tail = struct.unpack("<q", struct.pack("<if", 0 if g.dtype == torch.float32 else 1,
+                                                   float(st["decay_scale"])))[0]
             scale = struct.unpack("<q", struct.pack("<fi", float(self.grad_scale.get(p, 1.0)), 0))[0]
-            rows.append([p.data_ptr(), g.data_ptr(), st["master"].data_ptr() if "master" in st else 0,
-                         st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr(), p.numel(), tail, scale])
-            for start in range(0, p.numel(), chunk):
-                chunk_tensor.append(index)
-                chunk_start.append(start)
+            rows.append((p.data_ptr(), g.data_ptr(), st["master"].data_ptr() if "master" in st else 0,
+                         st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr(), p.numel(), tail, scale))
+        key = (str(device), tuple(rows))
+        cached = getattr(self, "_table_cache", None)
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        sizes = tuple(r[5] for r in rows)
+        chunk_cache = getattr(self, "_chunk_cache", {})
+        if (str(device), sizes) not in chunk_cache:
+            chunk = C.adam_chunk_size()
+            numels = torch.tensor(sizes, dtype=torch.int64)
+            counts = (numels + chunk - 1) // chunk
+            owner = torch.repeat_interleave(torch.arange(len(sizes), dtype=torch.int32), counts)
+            first = torch.repeat_interleave(torch.cumsum(counts, 0) - counts, counts)
+            starts = (torch.arange(owner.numel(), dtype=torch.int64) - first) * chunk
+            chunk_cache = {(str(device), sizes): (owner.to(device), starts.to(device))}
+            self._chunk_cache = chunk_cache
+        ct, cs = chunk_cache[(str(device), sizes)]
         table = torch.tensor(rows, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
-        ct = torch.tensor(chunk_tensor, dtype=torch.int32).pin_memory().to(device, non_blocking=True)
-        cs = torch.tensor(chunk_start, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
+        self._table_cache = (key, (table, ct, cs))
         return table, ct, cs
 
     def _live(self):
