@@ -49,6 +49,8 @@ def parse():
     p.add_argument("--transport", choices=("p2p", "nccl"), default=os.environ.get("QW_EP_TRANSPORT", "nccl"),
                    help="expert-parallel dispatch/combine: in-kernel NVLink stores (p2p) or NCCL all_to_all")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-launch-count", action="store_true",
+                   help="skip the profiler-based launch count (for runs under an external profiler)")
     p.add_argument("--kernel-breakdown", action="store_true",
                    help="after timing, profile one extra step and print per-kernel CUDA time shares to stderr")
     p.add_argument("--seed", type=int, default=0)
@@ -201,7 +203,8 @@ def run_native(args, rank, world, local):
         e2e = {"value": tokens_per_step / (te.ms / args.steps / 1000.0), "unit": "tokens/s",
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4 * world, "ms_per_step": te.ms / args.steps,
                "final_loss": loss_value}
-    launches = count_launches(lambda: train_step(host_batches[-1].to("cuda"))) * args.steps
+    launches = None if args.no_launch_count else count_launches(
+        lambda: train_step(host_batches[-1].to("cuda"))) * args.steps
     if args.kernel_breakdown and rank == 0:
         kernel_breakdown(lambda: train_step(host_batches[-1].to("cuda")))
     if args.trace and rank == 0:
