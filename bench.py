@@ -46,7 +46,7 @@ def parse():
     p.add_argument("--seq-len", type=int, default=2048)
     p.add_argument("--layers", type=int, default=CONFIG2["layers"], help="debug override (the metric needs 16)")
     p.add_argument("--recompute", choices=("auto", "on", "off"), default="auto")
-    p.add_argument("--transport", choices=("p2p", "nccl"), default=os.environ.get("QW_EP_TRANSPORT", "nccl"),
+    p.add_argument("--transport", choices=("fused", "p2p", "nccl"), default=os.environ.get("QW_EP_TRANSPORT", "nccl"),
                    help="expert-parallel dispatch/combine: in-kernel NVLink stores (p2p) or NCCL all_to_all")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-launch-count", action="store_true",

@@ -282,6 +282,7 @@ void router_dw(Tensor d_logits, Tensor x, Tensor dw, bool accumulate, Tensor wor
 
 // ------------------------------------------------------------------------------------------------ optimizer / CE
 int64_t adam_chunk_size() { return qw::adam_chunk_size(); }
+int64_t adam8_block_size() { return qw::adam8_block_size(); }
 
 static_assert(sizeof(qw::AdamTensor) == 64, "AdamTensor layout is mirrored in Python (8 x 8 bytes)");
 
@@ -304,7 +305,7 @@ void adam_sumsq(Tensor table, Tensor chunk_tensor, Tensor chunk_start, Tensor pa
 }
 
 void adam_step(Tensor table, Tensor chunk_tensor, Tensor chunk_start, double lr, double beta1, double beta2, double eps,
-               double weight_decay, int64_t step, OptT clip) {
+               double weight_decay, int64_t step, OptT clip, bool eight_bit) {
   CHECK_CUDA(table);
   qw::AdamHyper h;
   h.lr = static_cast<float>(lr);
@@ -317,7 +318,7 @@ void adam_step(Tensor table, Tensor chunk_tensor, Tensor chunk_start, double lr,
   c10::cuda::CUDAGuard g(table.device());
   qw::adam_step(reinterpret_cast<const qw::AdamTensor*>(table.data_ptr()), chunk_tensor.data_ptr<int>(),
                 chunk_start.data_ptr<int64_t>(), static_cast<int>(chunk_tensor.numel()), h, optptr<float>(clip),
-                stream());
+                eight_bit, stream());
 }
 
 void cross_entropy_chunk(Tensor logits, Tensor labels, double grad_scale, Tensor loss_out, int64_t ignore_index) {
@@ -374,6 +375,43 @@ void p2p_wait(Tensor flags, int64_t world, int64_t epoch, double timeout_s) {
   CHECK_CUDA(flags);
   c10::cuda::CUDAGuard g(flags.device());
   qw::p2p_wait(flags.data_ptr<int>(), static_cast<int>(world), static_cast<int>(epoch), timeout_s, stream());
+}
+
+// ------------------------------------------------------------------------------------------------ fused EP exchange
+// peer / peer_flags: int64 device tensors of every rank's buffer / flag base addresses (symmetric memory)
+void ep_dispatch(Tensor x, Tensor route_row, OptT top_w, OptT kept, int64_t k, int64_t E, int64_t local, int64_t slot,
+                 int64_t me, Tensor peer, int64_t w_off, int64_t c_off, Tensor peer_flags, int64_t epoch, Tensor done) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DTYPE(x, torch::kBFloat16);
+  c10::cuda::CUDAGuard g(x.device());
+  qw::ep_dispatch(bptr(x), x.size(0), static_cast<int>(k), static_cast<int>(x.size(1)), route_row.data_ptr<int>(),
+                  optptr<float>(top_w), optptr<int>(kept), static_cast<int>(E), static_cast<int>(local),
+                  static_cast<int>(slot), static_cast<int>(me), static_cast<int>(peer.numel()),
+                  reinterpret_cast<uint8_t* const*>(peer.data_ptr<int64_t>()), w_off, c_off,
+                  reinterpret_cast<int* const*>(peer_flags.data_ptr<int64_t>()), static_cast<int>(epoch),
+                  reinterpret_cast<unsigned int*>(done.data_ptr<int>()), stream());
+}
+
+void ep_pad(Tensor counts, int64_t slot, Tensor rows, OptT w) {
+  CHECK_CUDA(rows); CHECK_ROWS(rows);
+  c10::cuda::CUDAGuard g(rows.device());
+  qw::ep_pad(counts.data_ptr<int>(), static_cast<int>(counts.numel()), static_cast<int>(slot),
+             static_cast<int>(rows.size(1)), bptr_mut(rows), w ? w->data_ptr<float>() : nullptr, stream());
+}
+
+void ep_signal(Tensor peer_flags, int64_t me, int64_t epoch) {
+  c10::cuda::CUDAGuard g(peer_flags.device());
+  qw::ep_signal(reinterpret_cast<int* const*>(peer_flags.data_ptr<int64_t>()), static_cast<int>(peer_flags.numel()),
+                static_cast<int>(me), static_cast<int>(epoch), stream());
+}
+
+void ep_gather(Tensor peer_rows, Tensor route_row, OptT top_w, OptT extra, OptT resid, int64_t k, int64_t local,
+               int64_t slot, int64_t me, Tensor out) {
+  CHECK_CUDA(out); CHECK_CONTIG(out);
+  c10::cuda::CUDAGuard g(out.device());
+  qw::ep_gather(reinterpret_cast<const qw::bf16* const*>(peer_rows.data_ptr<int64_t>()), route_row.data_ptr<int>(),
+                optptr<float>(top_w), optptr<float>(extra), optb(resid), out.size(0), static_cast<int>(k),
+                static_cast<int>(out.size(1)), static_cast<int>(local), static_cast<int>(slot), static_cast<int>(me),
+                bptr_mut(out), stream());
 }
 
 // ------------------------------------------------------------------------------------------------ decode
@@ -490,6 +528,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_dw_split", &router_dw_split);
   m.def("router_dw", &router_dw);
   m.def("adam_chunk_size", &adam_chunk_size);
+  m.def("adam8_block_size", &adam8_block_size);
   m.def("adam_grad_norm", &adam_grad_norm);
   m.def("adam_sumsq", &adam_sumsq);
   m.def("adam_step", &adam_step);
@@ -502,6 +541,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_route", &decode_route);
   m.def("decode_attention", &decode_attention);
   m.def("rope_append", &rope_append);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_pad", &ep_pad);
+  m.def("ep_signal", &ep_signal);
+  m.def("ep_gather", &ep_gather);
   m.def("bias_grad_slabs", &bias_grad_slabs);
   m.def("bias_grad", &bias_grad);
   m.def("decode_combine_norm", &decode_combine_norm);

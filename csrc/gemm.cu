@@ -36,6 +36,11 @@ static void require(bool ok, const char* what) {
 
 // 2-D bf16 map over a row-major [outer, inner] region with row stride `ld` elements; box = [box_outer, box_inner].
 static CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner, int box_outer) {
+  // the driver call needs a current context; threads that have not touched the runtime yet (the autograd engine's
+  // device threads) get the primary context of the current device here
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaSetDevice(dev);
   require((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
   require((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes (ld % 8 == 0)");
   require(box_inner * 2 == 128, "swizzle-128 boxes are 64 bf16 wide");
@@ -47,7 +52,12 @@ static CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64
   CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, elem,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  require(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed");
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("qw gemm: cuTensorMapEncodeTiled failed (code " + std::to_string(static_cast<int>(r)) +
+                             ", inner " + std::to_string(inner) + ", outer " + std::to_string(outer) + ", ld " +
+                             std::to_string(ld) + ", box " + std::to_string(box_inner) + "x" +
+                             std::to_string(box_outer) + ", base " +
+                             std::to_string(reinterpret_cast<uintptr_t>(ptr) % 1024) + " mod 1024)");
   return map;
 }
 

@@ -105,7 +105,8 @@ void adam_grad_norm(const AdamTensor* tensors, const int* chunk_tensor, const in
 void adam_sumsq(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
                 double* partial, cudaStream_t stream);
 void adam_step(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
-               const AdamHyper& hyper, const float* clip, cudaStream_t stream);
+               const AdamHyper& hyper, const float* clip, bool eight_bit, cudaStream_t stream);
+int adam8_block_size();
 void cross_entropy_chunk(bf16* logits, int64_t rows, int64_t ld, int V, const int64_t* labels, float grad_scale,
                          float* loss_out, int ignore_index, cudaStream_t stream);
 void scale_bf16(bf16* x, int64_t n, const float* scale, cudaStream_t stream);
@@ -125,6 +126,16 @@ void p2p_push(const void* src, int64_t block_bytes, void* const* peer_bufs, int*
               int epoch, unsigned int* done, cudaStream_t stream);
 void p2p_wait(const int* flags, int world, int epoch, double timeout_s, cudaStream_t stream);
 int p2p_status(bool clear);
+
+// ---- ep_fused.cu (expert-parallel dispatch / return over peer memory) ----
+void ep_dispatch(const bf16* x, int64_t T, int k, int H, const int* route_row, const float* top_w, const int* kept,
+                 int E, int local, int slot, int me, int world, uint8_t* const* peer, int64_t w_off, int64_t c_off,
+                 int* const* peer_flags, int epoch, unsigned int* done, cudaStream_t stream);
+void ep_pad(const int* counts, int groups, int slot, int H, bf16* rows, float* w, cudaStream_t stream);
+void ep_signal(int* const* peer_flags, int world, int me, int epoch, cudaStream_t stream);
+void ep_gather(const bf16* const* peer_rows, const int* route_row, const float* top_w, const float* extra,
+               const bf16* resid, int64_t T, int k, int H, int local, int slot, int me, bf16* out,
+               cudaStream_t stream);
 
 // ---- decode.cu ----
 void grouped_gemv(const bf16* x, int64_t ldx, const void* w, const void* scales, int64_t w_group_bytes,

@@ -141,6 +141,84 @@ __global__ void adamw_kernel(const AdamTensor* __restrict__ tensors, const int* 
   }
 }
 
+// 8-bit moments: the state of a tensor is one byte buffer [m: int8 x P][sqrt v: uint8 x P][scales: fp32 x 2 per
+// 2048-element block], P = numel rounded up to 16; exp_avg points at its start and exp_avg_sq at the second part.
+// m is stored linearly against its block absmax (127 levels each side), sqrt(v) linearly against its block max (255
+// levels): block-wise quantisation of the optimiser state. The update itself runs in fp32 on the dequantised values;
+// the new block scales come from a block reduction before re-quantising.
+constexpr int kQBlock = 2048;
+
+__global__ void __launch_bounds__(256) adamw8_kernel(const AdamTensor* __restrict__ tensors,
+                                                     const int* __restrict__ chunk_tensor,
+                                                     const int64_t* __restrict__ chunk_start, AdamHyper h,
+                                                     const float* __restrict__ clip) {
+  __shared__ float red_m[8], red_v[8];
+  const AdamTensor& t = tensors[chunk_tensor[blockIdx.x]];
+  const int64_t begin = chunk_start[blockIdx.x];
+  const int64_t end = min(t.numel, begin + kAdamChunk);
+  const int64_t padded = (t.numel + 15) / 16 * 16;
+  int8_t* mq = static_cast<int8_t*>(static_cast<void*>(t.exp_avg));
+  uint8_t* vq = static_cast<uint8_t*>(static_cast<void*>(t.exp_avg_sq));
+  float* scales = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(t.exp_avg) + 2 * padded);
+  const float coef = (clip ? clip[1] : 1.f) * t.grad_scale;
+  const float decay = 1.f - h.lr * h.weight_decay * t.decay_scale;
+  const float step_size = h.lr / h.bias_correction1;
+  float* master = t.master ? t.master : static_cast<float*>(t.param);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  for (int64_t b0 = begin; b0 < end; b0 += kQBlock) {
+    const int64_t qb = b0 / kQBlock;
+    const float sm_old = scales[2 * qb], sv_old = scales[2 * qb + 1];
+    float m[8], v[8];
+    float amax_m = 0.f, amax_v = 0.f;
+    const int64_t i0 = b0 + threadIdx.x * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t i = i0 + j;
+      m[j] = v[j] = 0.f;
+      if (i >= end) continue;
+      const float g = load_val(t.grad, i, t.grad_dtype) * coef;
+      const float root = static_cast<float>(vq[i]) * sv_old;
+      float mm = h.beta1 * (static_cast<float>(mq[i]) * sm_old) + (1.f - h.beta1) * g;
+      float vv = h.beta2 * (root * root) + (1.f - h.beta2) * g * g;
+      float p = master[i] * decay;
+      p -= step_size * mm / (sqrtf(vv) / h.bias_correction2_sqrt + h.eps);
+      master[i] = p;
+      if (t.master) static_cast<bf16*>(t.param)[i] = __float2bfloat16(p);
+      m[j] = mm;
+      v[j] = sqrtf(vv);
+      amax_m = fmaxf(amax_m, fabsf(mm));
+      amax_v = fmaxf(amax_v, v[j]);
+    }
+    amax_m = warp_max(amax_m);
+    amax_v = warp_max(amax_v);
+    if (lane == 0) {
+      red_m[warp] = amax_m;
+      red_v[warp] = amax_v;
+    }
+    __syncthreads();
+    amax_m = 0.f;
+    amax_v = 0.f;
+    for (int w = 0; w < blockDim.x / 32; ++w) {
+      amax_m = fmaxf(amax_m, red_m[w]);
+      amax_v = fmaxf(amax_v, red_v[w]);
+    }
+    const float inv_m = amax_m > 0.f ? 127.f / amax_m : 0.f;
+    const float inv_v = amax_v > 0.f ? 255.f / amax_v : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int64_t i = i0 + j;
+      if (i >= end) continue;
+      mq[i] = static_cast<int8_t>(fminf(127.f, fmaxf(-127.f, rintf(m[j] * inv_m))));
+      vq[i] = static_cast<uint8_t>(fminf(255.f, rintf(v[j] * inv_v)));
+    }
+    if (threadIdx.x == 0) {
+      scales[2 * qb] = amax_m / 127.f;
+      scales[2 * qb + 1] = amax_v / 255.f;
+    }
+    __syncthreads();
+  }
+}
+
 // in-place per-row cross-entropy gradient on a logits chunk; loss_out[row] = lse - logit[label] (0 if ignored)
 __global__ void __launch_bounds__(256) ce_kernel(bf16* __restrict__ logits, int64_t ld, int V,
                                                  const int64_t* __restrict__ labels, float grad_scale,
@@ -211,6 +289,7 @@ __global__ void scale_bf16_kernel(bf16* __restrict__ x, int64_t n, const float* 
 }  // namespace
 
 int adam_chunk_size() { return kAdamChunk; }
+int adam8_block_size() { return kQBlock; }
 
 void adam_grad_norm(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
                     double* partial, const double* extra_sumsq, float max_norm, float* norm_out, cudaStream_t stream) {
@@ -226,9 +305,12 @@ void adam_sumsq(const AdamTensor* tensors, const int* chunk_tensor, const int64_
 }
 
 void adam_step(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
-               const AdamHyper& hyper, const float* clip, cudaStream_t stream) {
+               const AdamHyper& hyper, const float* clip, bool eight_bit, cudaStream_t stream) {
   if (chunks == 0) return;
-  adamw_kernel<<<chunks, 256, 0, stream>>>(tensors, chunk_tensor, chunk_start, hyper, clip);
+  if (eight_bit)
+    adamw8_kernel<<<chunks, 256, 0, stream>>>(tensors, chunk_tensor, chunk_start, hyper, clip);
+  else
+    adamw_kernel<<<chunks, 256, 0, stream>>>(tensors, chunk_tensor, chunk_start, hyper, clip);
   check_cuda(cudaGetLastError(), "adam_step");
 }
 

@@ -22,9 +22,10 @@ from ..ops import ext
 class FusedAdamW(torch.optim.Optimizer):
     def __init__(self, params: Iterable, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 1e-2, moment_bits: int = 32) -> None:
-        if moment_bits != 32:
-            raise NotImplementedError("8-bit moments are not implemented by the fused optimizer yet")
+        if moment_bits not in (8, 32):
+            raise ValueError("moment_bits must be 8 or 32")
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
+        self.moment_bits = moment_bits
         self._chunk = None
         self._clip: Optional[Tensor] = None
         # per-parameter factor applied to the stored gradient inside the fused kernels (norm and update), e.g.
@@ -37,11 +38,27 @@ class FusedAdamW(torch.optim.Optimizer):
         state = self.state[p]
         if "exp_avg" not in state:
             state["step"] = 0
-            state["exp_avg"] = torch.zeros(p.shape, device=p.device, dtype=torch.float32)
-            state["exp_avg_sq"] = torch.zeros(p.shape, device=p.device, dtype=torch.float32)
+            if self.moment_bits == 8:
+                self._alloc8(p, state, None)
+            else:
+                state["exp_avg"] = torch.zeros(p.shape, device=p.device, dtype=torch.float32)
+                state["exp_avg_sq"] = torch.zeros(p.shape, device=p.device, dtype=torch.float32)
             if p.dtype != torch.float32:
                 state["master"] = p.detach().float().contiguous()
         return state
+
+    @staticmethod
+    def _alloc8(p: Tensor, state: dict, saved: Optional[Tensor]) -> None:
+        """One byte buffer per tensor: [m int8 x P][sqrt(v) uint8 x P][fp32 scales x 2 per 2048 block], P = numel
+        rounded up to 16; ``exp_avg`` / ``exp_avg_sq`` are views of its two parts (the kernel derives the rest)."""
+        n = p.numel()
+        padded = (n + 15) // 16 * 16
+        blocks = (n + 2047) // 2048
+        buf = torch.zeros(2 * padded + 8 * blocks, device=p.device, dtype=torch.uint8) if saved is None else \
+            saved.to(p.device, torch.uint8).contiguous()
+        state["state8"] = buf
+        state["exp_avg"] = buf[:padded]
+        state["exp_avg_sq"] = buf[padded:2 * padded]
 
     def _params(self):
         for group in self.param_groups:
@@ -167,7 +184,7 @@ class FusedAdamW(torch.optim.Optimizer):
         table, ct, cs = self._build_tables(params, params[0].device)
         beta1, beta2 = group["betas"]
         C.adam_step(table, ct, cs, float(group["lr"]), float(beta1), float(beta2), float(group["eps"]),
-                    float(group["weight_decay"]), int(step), self._clip)
+                    float(group["weight_decay"]), int(step), self._clip, self.moment_bits == 8)
 
     # ---- checkpoints -----------------------------------------------------------------------------
     def state_dict(self) -> dict:
@@ -184,7 +201,8 @@ class FusedAdamW(torch.optim.Optimizer):
             for p in group["params"]:
                 if p in self.state and "exp_avg" in self.state[p]:
                     st = self.state[p]
-                    state[index[id(p)]] = {k: v for k, v in st.items() if k != "decay_scale"}
+                    skip = {"decay_scale"} | ({"exp_avg", "exp_avg_sq"} if "state8" in st else set())
+                    state[index[id(p)]] = {k: v for k, v in st.items() if k not in skip}
         return {"state": state, "param_groups": groups}
 
     def load_state_dict(self, state_dict: dict) -> None:
@@ -196,8 +214,14 @@ class FusedAdamW(torch.optim.Optimizer):
         for idx, st in state_dict["state"].items():
             p = params[int(idx)]
             new = {"step": int(st["step"])}
+            if "state8" in st:
+                if self.moment_bits != 8:
+                    raise ValueError("checkpoint holds 8-bit optimizer moments; build the optimizer with moment_bits=8")
+                self._alloc8(p, new, st["state8"])
+            elif self.moment_bits == 8 and "exp_avg" in st:
+                raise ValueError("checkpoint holds fp32 optimizer moments; build the optimizer with moment_bits=32")
             for key in ("exp_avg", "exp_avg_sq", "master"):
-                if key in st:
+                if key in st and key not in new:
                     new[key] = st[key].to(device=p.device, dtype=torch.float32).contiguous()
             if p.dtype != torch.float32 and "master" not in new:
                 new["master"] = p.detach().float().contiguous()

@@ -11,8 +11,10 @@ B200 native path (``_SlotDispatch``): each source rank plans capacity on the dev
 exchanges whose sizes never need a host synchronisation. The receiving rank sees a ``[source, local expert, slot]``
 buffer and runs the grouped tcgen05 SwiGLU GEMMs over ``source x local-expert`` groups (group ``g`` uses expert
 ``g % local``); weight gradients reduce each expert over the per-source segments inside one GEMM. The exchange
-itself is pluggable: NCCL ``all_to_all_single`` (the baseline) or the fused peer-memory transport in
-``parallel.p2p`` (in-kernel NVLink stores into the peer's receive slots).
+itself is pluggable: NCCL ``all_to_all_single`` (the baseline), the peer-store exchange of ``parallel.p2p``
+(``p2p``), or the fused transport (``fused``): the permute kernel stores routed rows, weights and counts straight
+into the owners' receive buffers, the expert GEMMs write their outputs into a symmetric return buffer, and the
+combine kernel pulls each token's expert rows over NVLink and reduces them (``csrc/ep_fused.cu``).
 
 The CPU (gloo) path keeps the reference's algorithm with uneven differentiable all-to-alls; it is the oracle the
 multi-process tests compare against single-device training.
@@ -46,7 +48,7 @@ class ExpertParallelContext:
     tp_group: Optional[object] = None
     global_rank: int = -1
     global_size: int = -1
-    transport: str = "nccl"          # native dispatch: "nccl" (all_to_all) or "p2p" (fused peer stores)
+    transport: str = "nccl"  # native dispatch: "nccl" (all_to_all), "p2p" (peer-store exchange) or "fused"
 
     def __post_init__(self) -> None:
         if self.global_size < 0:
@@ -134,24 +136,37 @@ class _SlotDispatch(torch.autograd.Function):
         x = x.to(torch.bfloat16).contiguous()
         plan = route(x, router_weight, k, capacity, float(moe.router_temperature), moe.expert_bias, slot_rows=slot)
         rows = E * slot
-        send = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
-        row_token = torch.full((rows,), -1, device=dev, dtype=torch.int32)
-        row_w = torch.zeros(rows, device=dev, dtype=torch.float32)
-        C.moe_permute(x, k, plan.route_row, plan.top_w, plan.kept, plan.offsets, send, row_token, row_w)
         transport = moe.transport()
-        recv_counts = transport.exchange_counts(plan.kept)            # [world * local] (source-major)
-        x_recv = transport.exchange(send)                             # [world * local * slot, H]
-        w_recv = transport.exchange(row_w)
+        fused = getattr(transport, "dispatch", None) is not None
+        if fused:  # permute + exchange in one kernel, straight into the owners' receive buffers
+            rx, rw, rc = transport.dispatch(x, plan.route_row, plan.top_w, plan.kept, k, E, local, slot)
+            x_recv, w_recv, recv_counts = rx.clone(), rw.clone(), rc.clone()  # saved for backward
+            row_token = torch.empty(0, device=dev, dtype=torch.int32)
+        else:
+            send = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+            row_token = torch.full((rows,), -1, device=dev, dtype=torch.int32)
+            row_w = torch.zeros(rows, device=dev, dtype=torch.float32)
+            C.moe_permute(x, k, plan.route_row, plan.top_w, plan.kept, plan.offsets, send, row_token, row_w)
+            recv_counts = transport.exchange_counts(plan.kept)            # [world * local] (source-major)
+            x_recv = transport.exchange(send)                             # [world * local * slot, H]
+            w_recv = transport.exchange(row_w)
         offsets = moe.recv_offsets(slot, dev)
         h = torch.empty(rows, F, device=dev, dtype=torch.bfloat16)
         gu = None if moe.recompute_activations else torch.empty(rows, F2, device=dev, dtype=torch.bfloat16)
         C.moe_gate_up_fwd(x_recv, w_gate_up, recv_counts, offsets, h, gu)
-        y = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
-        C.moe_down_fwd(h, w_down, recv_counts, offsets, y)
-        del h
-        y_back = transport.exchange(y)
         out = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
-        C.moe_combine(y_back, plan.route_row, plan.top_w, None, k, out)
+        if fused:  # expert outputs land in this rank's return buffer; each source pulls and combines its rows
+            y = transport.return_buffer(rows, H)
+            C.moe_down_fwd(h, w_down, recv_counts, offsets, y)
+            del h
+            transport.publish()
+            transport.gather(plan.route_row, plan.top_w, None, k, local, slot, out)
+        else:
+            y = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+            C.moe_down_fwd(h, w_down, recv_counts, offsets, y)
+            del h
+            y_back = transport.exchange(y)
+            C.moe_combine(y_back, plan.route_row, plan.top_w, None, k, out)
         saved = [x, router_weight, w_gate_up, w_down, plan.probs, plan.top_idx, plan.top_w, plan.meta, plan.route_row,
                  row_token, recv_counts, offsets, x_recv, w_recv]
         if gu is not None:
@@ -183,10 +198,15 @@ class _SlotDispatch(torch.autograd.Function):
         if d_out is None:
             d_out = torch.zeros(T, H, device=dev, dtype=torch.bfloat16)
         d_out = d_out.to(torch.bfloat16).contiguous()
-        dy_send = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
-        C.moe_gather_rows(d_out, row_token, meta, dy_send)
-        dy_recv = transport.exchange(dy_send)
-        del dy_send
+        fused = getattr(transport, "dispatch", None) is not None
+        if fused:
+            dy_recv, _, _ = transport.dispatch(d_out, route_row, None, None, k, moe.num_experts, local, slot,
+                                               pad_counts=recv_counts)
+        else:
+            dy_send = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+            C.moe_gather_rows(d_out, row_token, meta, dy_send)
+            dy_recv = transport.exchange(dy_send)
+            del dy_send
         if gu is None:
             gu = torch.empty(rows, F2, device=dev, dtype=torch.bfloat16)
             scratch = torch.empty(rows, F, device=dev, dtype=torch.bfloat16)
@@ -203,10 +223,15 @@ class _SlotDispatch(torch.autograd.Function):
         del hw, dy_recv
         d_w_gate_up = torch.empty_like(w_gate_up)
         C.moe_wgrad(dgu, x_recv, recv_counts, offsets, d_w_gate_up, False, world, 1.0)
-        dx_recv = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+        dx_recv = transport.return_buffer(rows, H) if fused else torch.empty(rows, H, device=dev,
+                                                                                dtype=torch.bfloat16)
         C.moe_gate_up_dgrad(dgu, w_gate_up, recv_counts, offsets, dx_recv)
         del dgu
-        dx_send = transport.exchange(dx_recv)
+        if fused:
+            transport.publish()
+            dx_send = None
+        else:
+            dx_send = transport.exchange(dx_recv)
         partial_back = transport.exchange(partial)
         d_w = torch.empty(T * k, device=dev, dtype=torch.float32)
         C.moe_route_dw(partial_back, route_row, d_w)
@@ -221,7 +246,10 @@ class _SlotDispatch(torch.autograd.Function):
         d_router = torch.empty(moe.num_experts, H, device=dev, dtype=torch.float32)
         C.router_dw(d_logits, x, d_router, False, workspace)
         dx = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
-        C.moe_combine_grad(dx_send, route_row, dx_router, k, dx)
+        if fused:  # pull the input-gradient rows of this rank's routes from the expert ranks
+            transport.gather(route_row, None, dx_router, k, local, slot, dx)
+        else:
+            C.moe_combine_grad(dx_send, route_row, dx_router, k, dx)
         del local
         return dx, d_router.to(router_weight.dtype), d_w_gate_up, d_w_down, None, None
 
@@ -258,6 +286,10 @@ class ExpertParallelMoE(TopKMoE):
                 from .p2p import P2PTransport
 
                 self._transport = P2PTransport.for_group(self.context.group, self.context.device)
+            elif self.context.transport == "fused":
+                from .p2p import FusedTransport
+
+                self._transport = FusedTransport.for_group(self.context.group, self.context.device)
             else:
                 self._transport = NcclTransport(self.context.group)
         return self._transport

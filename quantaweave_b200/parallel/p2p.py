@@ -98,3 +98,123 @@ class P2PTransport:
         padded[:, : kept.numel() // self.world] = kept.view(self.world, -1)
         out = self.exchange(padded)
         return out[:, : kept.numel() // self.world].reshape(-1).contiguous()
+
+
+class _Channel:
+    """Two-parity symmetric buffers with per-source flags and an epoch (one direction of the fused EP exchange)."""
+
+    def __init__(self, transport: "P2PTransport") -> None:
+        self.t = transport
+        symm, dev, world = transport.symm, transport.device, transport.world
+        self.flags = symm.empty(2 * world, dtype=torch.int32, device=dev)
+        self.flags.zero_()
+        handle = symm.rendezvous(self.flags, transport._group_name())
+        ptrs = [int(p) for p in handle.buffer_ptrs]
+        self.peer_flags = [torch.tensor([p + parity * world * 4 for p in ptrs], dtype=torch.int64, device=dev)
+                           for parity in range(2)]
+        self._flag_handle = handle
+        self.done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.epoch = 0
+        self.capacity = 0
+        self.bufs: list = []
+
+    def grow(self, nbytes: int) -> None:
+        """Collective: every rank asks for the same size."""
+        nbytes = (nbytes + (1 << 20) - 1) // (1 << 20) * (1 << 20)
+        if nbytes <= self.capacity:
+            return
+        t = self.t
+        torch.cuda.synchronize(t.device)
+        bufs = []
+        for _ in range(2):
+            buf = t.symm.empty(nbytes, dtype=torch.uint8, device=t.device)
+            handle = t.symm.rendezvous(buf, t._group_name())
+            peers = torch.tensor([int(p) for p in handle.buffer_ptrs], dtype=torch.int64, device=t.device)
+            bufs.append((buf, handle, peers))
+        self.bufs = bufs
+        self.capacity = nbytes
+
+    def next(self) -> int:
+        self.epoch += 1
+        return self.epoch % 2
+
+    def wait(self, parity: int) -> None:
+        from ..ops import ext
+
+        w = self.t.world
+        ext().p2p_wait(self.flags[parity * w:(parity + 1) * w], w, self.epoch, self.t.timeout_s)
+
+
+class FusedTransport(P2PTransport):
+    """Expert-parallel exchange fused into the routing kernels (``csrc/ep_fused.cu``).
+
+    ``dispatch`` stores each routed row (and its weight and the per-expert counts) straight into the owning rank's
+    receive buffer; ``return_buffer`` / ``publish`` / ``gather`` let the expert rank's GEMM write its output into its
+    own symmetric buffer and each source rank pull and reduce its rows with NVLink loads. Plain ``exchange`` (used for
+    small tensors) is the P2P push of ``P2PTransport``."""
+
+    def __init__(self, group, device: torch.device, capacity_bytes: int = 1 << 20) -> None:
+        super().__init__(group, device, capacity_bytes)
+        self.send = _Channel(self)
+        self.back = _Channel(self)
+        dist.barrier(group=self.group, device_ids=[device.index] if device.type == "cuda" else None)
+
+    @classmethod
+    def for_group(cls, group, device) -> "FusedTransport":
+        key = ("fused", id(group), str(device))
+        if key not in _TRANSPORTS:
+            _TRANSPORTS[key] = cls(group, device)
+        return _TRANSPORTS[key]
+
+    @staticmethod
+    def _layout(rows: int, H: int, groups: int) -> tuple[int, int, int]:
+        w_off = (rows * H * 2 + 255) // 256 * 256
+        c_off = (w_off + rows * 4 + 255) // 256 * 256
+        return w_off, c_off, c_off + groups * 4
+
+    def dispatch(self, x: Tensor, route_row: Tensor, top_w, kept, k: int, E: int, local: int, slot: int,
+                 pad_counts: Tensor | None = None):
+        """Rows (and, when given, weights and counts) of this rank's routes into the owners' receive buffers.
+        Returns views of this rank's receive buffer: rows [world*local*slot, H] bf16, weights [rows] fp32, counts
+        [world*local] int32 (valid until the next dispatch of the other parity)."""
+        from ..ops import ext
+
+        C = ext()
+        H = x.size(1)
+        groups = self.world * local
+        rows = groups * slot
+        w_off, c_off, total = self._layout(rows, H, groups)
+        ch = self.send
+        ch.grow(total)
+        parity = ch.next()
+        buf, _, peers = ch.bufs[parity]
+        C.ep_dispatch(x.contiguous(), route_row, top_w, kept, k, E, local, slot, self.me, peers, w_off, c_off,
+                      ch.peer_flags[parity], ch.epoch, ch.done)
+        ch.wait(parity)
+        rows_t = buf[: rows * H * 2].view(torch.bfloat16).view(rows, H)
+        w_t = buf[w_off:w_off + rows * 4].view(torch.float32)
+        counts = buf[c_off:c_off + groups * 4].view(torch.int32)
+        counts_for_pad = counts if kept is not None else pad_counts
+        C.ep_pad(counts_for_pad, slot, rows_t, w_t if top_w is not None else None)
+        return rows_t, w_t, counts
+
+    def return_buffer(self, rows: int, H: int) -> Tensor:
+        ch = self.back
+        ch.grow(rows * H * 2)
+        self._back_parity = ch.next()
+        buf = ch.bufs[self._back_parity][0]
+        return buf[: rows * H * 2].view(torch.bfloat16).view(rows, H)
+
+    def publish(self) -> None:
+        from ..ops import ext
+
+        ch = self.back
+        ext().ep_signal(ch.peer_flags[self._back_parity], self.me, ch.epoch)
+
+    def gather(self, route_row: Tensor, top_w, extra, k: int, local: int, slot: int, out: Tensor) -> Tensor:
+        from ..ops import ext
+
+        ch = self.back
+        ch.wait(self._back_parity)
+        ext().ep_gather(ch.bufs[self._back_parity][2], route_row, top_w, extra, None, k, local, slot, self.me, out)
+        return out

@@ -86,7 +86,7 @@ def _case(rank, world, transport):
     return float(out["loss"])
 
 
-@pytest.mark.parametrize("transport", ["nccl", "p2p"])
+@pytest.mark.parametrize("transport", ["nccl", "p2p", "fused"])
 def test_expert_parallel_native_matches_single_gpu(transport):
     world = 2
     ctx = mp.get_context("spawn")

@@ -244,3 +244,27 @@ def test_gpu_training_is_deterministic(tmp_path):
     assert losses[0] == losses[1]
     assert losses[0][-1] < losses[0][0]
     _status_ok()
+
+
+def test_adamw_8bit_tracks_fp32_adamw():
+    """8-bit block-quantised moments stay close to the fp32 optimizer over a few steps, and round-trip a state dict."""
+    from quantaweave_b200.optim.adamw import FusedAdamW
+
+    torch.manual_seed(3)
+    ref = torch.nn.Parameter(torch.randn(5000, device="cuda"))
+    p8 = torch.nn.Parameter(ref.detach().clone())
+    opt_ref = torch.optim.AdamW([ref], lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1)
+    opt8 = FusedAdamW([p8], lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, moment_bits=8)
+    for step in range(20):
+        g = torch.randn(5000, device="cuda") * (1 + step % 3)
+        ref.grad, p8.grad = g.clone(), g.clone()
+        opt_ref.step()
+        opt8.step()
+    rel = float((p8 - ref).norm() / (ref.norm()))
+    assert rel < 1e-2, rel
+    state = opt8.state_dict()
+    assert "state8" in state["state"][0] and "exp_avg" not in state["state"][0]
+    opt_b = FusedAdamW([torch.nn.Parameter(p8.detach().clone())], lr=1e-2, moment_bits=8)
+    opt_b.load_state_dict(state)
+    assert torch.equal(opt_b.state[opt_b.param_groups[0]["params"][0]]["state8"], opt8.state[p8]["state8"])
+    _status_ok()
