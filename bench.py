@@ -46,8 +46,9 @@ def parse():
     p.add_argument("--seq-len", type=int, default=2048)
     p.add_argument("--layers", type=int, default=CONFIG2["layers"], help="debug override (the metric needs 16)")
     p.add_argument("--recompute", choices=("auto", "on", "off"), default="auto")
-    p.add_argument("--transport", choices=("fused", "p2p", "nccl"), default=os.environ.get("QW_EP_TRANSPORT", "nccl"),
-                   help="expert-parallel dispatch/combine: in-kernel NVLink stores (p2p) or NCCL all_to_all")
+    p.add_argument("--transport", choices=("auto", "fused", "p2p", "nccl"), default=os.environ.get("QW_EP_TRANSPORT", "auto"),
+                   help="expert-parallel exchange: fused (permute/combine kernels with NVLink peer stores and "
+                        "loads), p2p (peer-store exchange), nccl (all_to_all), auto (fused at 2 ranks, else nccl)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-launch-count", action="store_true",
                    help="skip the profiler-based launch count (for runs under an external profiler)")
@@ -71,7 +72,10 @@ def dist_setup(gpus: int):
         from datetime import timedelta
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+        # short enough that a rank left waiting on a collective fails within minutes instead of holding the GPUs
+        timeout_s = float(os.environ.get("QW_PG_TIMEOUT_S", "180"))
+        os.environ["QW_PG_TIMEOUT_S"] = str(timeout_s)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=timeout_s), device_id=torch.device("cuda", local))
     return rank, world, local
 
 
@@ -93,7 +97,7 @@ def count_launches(step_fn) -> int:
     return len(ours)
 
 
-def kernel_breakdown(step_fn) -> None:
+def kernel_breakdown(step_fn, report: bool = True) -> None:
     """Per-kernel CUDA time of one step (shares only; numbers taken under a profiler are never reported)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
@@ -101,6 +105,8 @@ def kernel_breakdown(step_fn) -> None:
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         step_fn()
         torch.cuda.synchronize()
+    if not report:
+        return
     totals: dict = {}
     for e in prof.events():
         if e.device_type == torch.autograd.DeviceType.CUDA:
@@ -113,15 +119,17 @@ def kernel_breakdown(step_fn) -> None:
         print(f"  {100 * t / grand:5.1f}%  {t / 1e3:8.2f} ms  x{n:<5d} {name}", file=sys.stderr)
 
 
-def save_trace(step_fn, path: str) -> None:
-    """Chrome trace (host + device timeline) of one step, for finding idle gaps; diagnostics only."""
+def save_trace(step_fn, path) -> None:
+    """Chrome trace (host + device timeline) of one step, for finding idle gaps; diagnostics only. ``path`` None:
+    run the step under the profiler without writing (ranks other than 0)."""
     import torch
     from torch.profiler import ProfilerActivity, profile
 
     with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
         step_fn()
         torch.cuda.synchronize()
-    prof.export_chrome_trace(path)
+    if path:
+        prof.export_chrome_trace(path)
 
 
 # ================================================================================================ native arm
@@ -205,10 +213,11 @@ def run_native(args, rank, world, local):
                "final_loss": loss_value}
     launches = None if args.no_launch_count else count_launches(
         lambda: train_step(host_batches[-1].to("cuda"))) * args.steps
-    if args.kernel_breakdown and rank == 0:
-        kernel_breakdown(lambda: train_step(host_batches[-1].to("cuda")))
-    if args.trace and rank == 0:
-        save_trace(lambda: train_step(host_batches[-1].to("cuda")), args.trace)
+    # every rank runs the profiled steps (they contain collectives); only rank 0 reports
+    if args.kernel_breakdown:
+        kernel_breakdown(lambda: train_step(host_batches[-1].to("cuda")), report=rank == 0)
+    if args.trace:
+        save_trace(lambda: train_step(host_batches[-1].to("cuda")), args.trace if rank == 0 else None)
     peak_gb = torch.cuda.max_memory_allocated() / 1e9
     emit(rank, {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -221,7 +230,7 @@ def run_native(args, rank, world, local):
                             f"DEBUG {args.layers}-layer variant of config 2",
                    "global_batch": args.seqs_per_gpu * world, "seq_len": args.seq_len,
                    "parallelism": f"ep{world}" if world > 1 else "single-gpu (all 64 experts local)",
-                   "ep_transport": args.transport if world > 1 else None,
+                   "ep_transport": ep.transport if ep is not None else None,
                    "l2": "no flush: every step streams >100 GB through HBM, far above the 126 MB L2",
                    "recompute_expert_activations": recompute, "optimizer": "fused AdamW, fp32 master, clip 1.0"},
         "clocks": clocks.summary(), "e2e": e2e, "gpu_launches": launches, "impl": "native",
