@@ -414,6 +414,37 @@ void ep_gather(Tensor peer_rows, Tensor route_row, OptT top_w, OptT extra, OptT 
                 bptr_mut(out), stream());
 }
 
+// ------------------------------------------------------------------------------------------------ fused ZeRO
+int64_t zero_rs_blocks(int64_t per) { return qw::zero_rs_blocks(per); }
+
+// peers: int64 tensor of every rank's flat staging (gradients) or parameter buffer; dtype 0 fp32, 1 bf16
+void zero_reduce_scatter(Tensor peers, int64_t dtype, int64_t start, Tensor shard, Tensor partial) {
+  CHECK_CUDA(shard); CHECK_DTYPE(shard, torch::kFloat32); CHECK_DTYPE(partial, torch::kFloat64);
+  c10::cuda::CUDAGuard g(shard.device());
+  qw::zero_reduce_scatter(reinterpret_cast<const void* const*>(peers.data_ptr<int64_t>()),
+                          static_cast<int>(peers.numel()), static_cast<int>(dtype), start, shard.numel(),
+                          shard.data_ptr<float>(), partial.data_ptr<double>(), stream());
+}
+
+void zero_adamw_gather(Tensor master, Tensor m, Tensor v, Tensor grad, OptT clip, double lr, double beta1, double beta2,
+                       double eps, double weight_decay, int64_t step, Tensor peers, int64_t dtype, int64_t start,
+                       int64_t valid) {
+  CHECK_CUDA(master);
+  qw::AdamHyper h;
+  h.lr = static_cast<float>(lr);
+  h.beta1 = static_cast<float>(beta1);
+  h.beta2 = static_cast<float>(beta2);
+  h.eps = static_cast<float>(eps);
+  h.weight_decay = static_cast<float>(weight_decay);
+  h.bias_correction1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
+  h.bias_correction2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
+  c10::cuda::CUDAGuard g(master.device());
+  qw::zero_adamw_gather(master.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), grad.data_ptr<float>(),
+                        optptr<float>(clip), h, reinterpret_cast<void* const*>(peers.data_ptr<int64_t>()),
+                        static_cast<int>(peers.numel()), static_cast<int>(dtype), start, master.numel(), valid,
+                        stream());
+}
+
 // ------------------------------------------------------------------------------------------------ decode
 // w: [G, rows, ...] packed weights (uint8 / int8 / bf16 viewed as bytes), scales: fp16 or None (bf16 weights)
 void grouped_gemv(Tensor x, Tensor w, OptT scales, int64_t N, int64_t K, int64_t group, int64_t fmt, bool swiglu,
@@ -542,6 +573,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &decode_attention);
   m.def("rope_append", &rope_append);
   m.def("ep_dispatch", &ep_dispatch);
+  m.def("zero_rs_blocks", &zero_rs_blocks);
+  m.def("zero_reduce_scatter", &zero_reduce_scatter);
+  m.def("zero_adamw_gather", &zero_adamw_gather);
   m.def("ep_pad", &ep_pad);
   m.def("ep_signal", &ep_signal);
   m.def("ep_gather", &ep_gather);

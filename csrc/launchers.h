@@ -137,6 +137,14 @@ void ep_gather(const bf16* const* peer_rows, const int* route_row, const float* 
                const bf16* resid, int64_t T, int k, int H, int local, int slot, int me, bf16* out,
                cudaStream_t stream);
 
+// ---- zero_fused.cu (ZeRO reduce-scatter and AdamW + all-gather over peer memory) ----
+int zero_rs_blocks(int64_t per);
+void zero_reduce_scatter(const void* const* peers, int world, int dtype, int64_t start, int64_t per, float* shard,
+                         double* partial, cudaStream_t stream);
+void zero_adamw_gather(float* master, float* m, float* v, const float* grad, const float* clip, const AdamHyper& h,
+                       void* const* peers, int world, int dtype, int64_t start, int64_t per, int64_t valid,
+                       cudaStream_t stream);
+
 // ---- decode.cu ----
 void grouped_gemv(const bf16* x, int64_t ldx, const void* w, const void* scales, int64_t w_group_bytes,
                   int64_t s_group_elems, int N, int K, int group, int fmt, bool swiglu, const int* tok, const int* off,

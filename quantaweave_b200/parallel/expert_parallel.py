@@ -469,6 +469,9 @@ def clip_grad_norm_parallel(model, ctx: ExpertParallelContext, max_norm: float, 
         return sum(p.grad.detach().double().pow(2).sum() for p in params)
 
     rep, tps, exp = sumsq(replicated), sumsq(tp_slices), sumsq(experts)
+    zero = optimizer if (sharded and hasattr(optimizer, "shard_sumsq")) else None
+    if zero is not None:  # replicated gradients now live as averaged shards inside the ZeRO optimizer
+        rep = rep + zero.shard_sumsq().to(device)
     if sharded and ctx.world_size > 1:
         rep, tps = rep.clone(), tps.clone()
         dist.all_reduce(rep, group=ctx.group)
@@ -484,6 +487,12 @@ def clip_grad_norm_parallel(model, ctx: ExpertParallelContext, max_norm: float, 
     if fused:
         optimizer.set_clip_coefficient(coef, total)
         return total
+    if zero is not None:  # shards are scaled inside the ZeRO step; expert gradients here unless its local
+        zero.set_clip_coefficient(coef, total)  # optimizer applies the coefficient itself
+        if not hasattr(zero.local_opt, "set_clip_coefficient"):
+            for p in experts:
+                p.grad.mul_(coef.to(p.grad.dtype))
+        return float(total)
     for p in model.parameters():
         if p.grad is not None:
             p.grad.mul_(coef.to(p.grad.dtype))

@@ -10,9 +10,17 @@ of the group size, and
 
 Expert (rank-local) parameters use a local AdamW (the fused kernel on CUDA). ``state_dict`` records the shard
 layout and refuses to load into a different world size or parameter set, like the reference.
+
+On CUDA with more than one rank the collectives are fused into the optimizer kernels (``csrc/zero_fused.cu``;
+``QW_ZERO_FUSED=0`` selects the NCCL path): the replicated parameters are re-homed into symmetric memory, each rank
+packs its gradients into a symmetric staging buffer, the reduce-scatter kernel sums its shard straight from the
+peers' buffers (fixed rank order, cast and 1/world scale fused, sums of squares for the clip norm), and the AdamW
+kernel stores each updated value into every rank's parameter buffer, which is the all-gather.
 """
 
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -56,9 +64,79 @@ class ShardedAdamW:
                 self.local_opt = torch.optim.AdamW(self.local, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
         self.param_groups = [dict(self.defaults, params=self.shared)] + (self.local_opt.param_groups if self.local_opt else [])
         self._clip = None
+        self.fused = (self.world > 1 and bool(self.shared) and all(p.is_cuda for p in self.shared)
+                      and os.environ.get("QW_ZERO_FUSED", "1") != "0")
+        if self.fused:
+            self._setup_fused()
+
+    # ---- fused path (CUDA) --------------------------------------------------------------------------
+    def _setup_fused(self) -> None:
+        """Re-home the replicated parameters into symmetric memory and create the gradient staging buffers."""
+        from .p2p import P2PTransport, _Channel
+
+        device = self.shared[0].device
+        transport = P2PTransport.for_group(self.group, device)
+        symm = transport.symm
+        name = transport._group_name()
+        self._ready, self._done = _Channel(transport), _Channel(transport)
+        self._transport = transport
+        for dtype, params in self._groups.items():
+            sh = self.shards[dtype]
+            n = sh["per"] * self.world
+            pbuf = symm.empty(n, dtype=dtype, device=device)
+            gbuf = symm.empty(n, dtype=dtype, device=device)
+            hp, hg = symm.rendezvous(pbuf, name), symm.rendezvous(gbuf, name)
+            pbuf.zero_()
+            gbuf.zero_()
+            offset = 0
+            with torch.no_grad():
+                for p in params:
+                    view = pbuf[offset:offset + p.numel()].view_as(p)
+                    view.copy_(p.detach())
+                    p.data = view
+                    offset += p.numel()
+            sh.update(pbuf=pbuf, gbuf=gbuf, handles=(hp, hg),
+                      ppeers=torch.tensor([int(x) for x in hp.buffer_ptrs], dtype=torch.int64, device=device),
+                      gpeers=torch.tensor([int(x) for x in hg.buffer_ptrs], dtype=torch.int64, device=device),
+                      code=0 if dtype == torch.float32 else 1)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group, device_ids=[device.index])
+
+    def _barrier(self, channel) -> None:
+        from ..ops import ext
+
+        parity = channel.next()
+        ext().ep_signal(channel.peer_flags[parity], self.rank, channel.epoch)
+        channel.wait(parity)
+
+    def _reduce_fused(self) -> None:
+        from ..ops import ext
+
+        C = ext()
+        for dtype, params in self._groups.items():
+            gbuf = self.shards[dtype]["gbuf"]
+            offset = 0
+            for p in params:
+                n = p.numel()
+                if p.grad is None:
+                    gbuf[offset:offset + n].zero_()
+                else:
+                    gbuf[offset:offset + n].copy_(p.grad.reshape(-1))
+                    p.grad = None
+                offset += n
+        self._barrier(self._ready)  # every rank's gradients are staged
+        for dtype in self._groups:
+            sh = self.shards[dtype]
+            grad = torch.empty(sh["per"], device=sh["gbuf"].device, dtype=torch.float32)
+            partial = torch.empty(C.zero_rs_blocks(sh["per"]), device=grad.device, dtype=torch.float64)
+            C.zero_reduce_scatter(sh["gpeers"], sh["code"], self.rank * sh["per"], grad, partial)
+            sh["grad"], sh["sumsq"] = grad, partial.sum()
 
     # ---- gradients ------------------------------------------------------------------------------
     def reduce_gradients(self) -> None:
+        if self.fused:
+            self._reduce_fused()
+            return
         for dtype, params in self._groups.items():
             for p in params:
                 if p.grad is None:
@@ -80,7 +158,7 @@ class ShardedAdamW:
         total = None
         for sh in self.shards.values():
             if sh["grad"] is not None:
-                s = sh["grad"].double().pow(2).sum()
+                s = sh["sumsq"] if (self.fused and "sumsq" in sh) else sh["grad"].double().pow(2).sum()
                 total = s if total is None else total + s
         if total is None:
             device = next(iter(self.shards.values()))["master"].device if self.shards else "cpu"
@@ -101,6 +179,9 @@ class ShardedAdamW:
         eps, wd = group["eps"], group["weight_decay"]
         self.step_count += 1
         t = self.step_count
+        if self.fused:
+            self._step_fused(lr, beta1, beta2, eps, wd, t)
+            return
         for dtype, params in self._groups.items():
             sh = self.shards[dtype]
             g = sh["grad"]
@@ -131,6 +212,27 @@ class ShardedAdamW:
             self.local_opt.step()
         self._clip = None
 
+    def _step_fused(self, lr, beta1, beta2, eps, wd, t) -> None:
+        from ..ops import ext
+
+        C = ext()
+        clip = None if self._clip is None else self._clip.reshape(-1)[:1].float().contiguous()
+        for dtype in self._groups:
+            sh = self.shards[dtype]
+            if sh["grad"] is None:
+                continue
+            C.zero_adamw_gather(sh["master"], sh["exp_avg"], sh["exp_avg_sq"], sh["grad"], clip, lr, beta1, beta2,
+                                eps, wd, t, sh["ppeers"], sh["code"], self.rank * sh["per"], sh["numel"])
+            sh["grad"] = None
+            sh.pop("sumsq", None)
+        self._barrier(self._done)  # every shard's update has landed in every rank's parameters
+        if self.local_opt is not None:
+            if len(self.param_groups) > 1:
+                for g_ in self.local_opt.param_groups:
+                    g_["lr"] = lr
+            self.local_opt.step()
+        self._clip = None
+
     def zero_grad(self, set_to_none: bool = True) -> None:
         for p in self.model.parameters():
             if set_to_none:
@@ -142,7 +244,8 @@ class ShardedAdamW:
         return sum(2 * sh["per"] for sh in self.shards.values())
 
     def state_dict(self) -> dict:
-        return {"shards": {str(k): {n: v for n, v in sh.items() if n != "grad"} for k, sh in self.shards.items()},
+        keep = ("numel", "per", "master", "exp_avg", "exp_avg_sq")
+        return {"shards": {str(k): {n: v for n, v in sh.items() if n in keep} for k, sh in self.shards.items()},
                 "step": self.step_count, "world": self.world, "rank": self.rank,
                 "local": self.local_opt.state_dict() if self.local_opt is not None else None}
 
