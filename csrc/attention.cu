@@ -10,6 +10,8 @@
 // Backward (no atomics, bit-reproducible): kernel 1 owns a key tile and loops over query tiles and the q-heads of
 // its kv group to accumulate dK, dV; kernel 2 owns a query tile and loops over key tiles to accumulate dQ.
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 
 #include "common.cuh"
 #include "launchers.h"
@@ -522,6 +524,18 @@ void flash_attn_bwd(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, cons
   if (B == 0 || S == 0) return;
   const int64_t rows = static_cast<int64_t>(B) * S * Hq;
   attn_delta_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, stream>>>(o, ldo, dout, lddo, delta, B, S, Hq, D);
+  // head_dim 64 / 128 run on the tcgen05 kernels (attention_tc.cu); QW_ATTN_BWD=mma keeps the mma.sync kernels
+  // below for comparison
+  static const bool use_mma = [] {
+    const char* e = std::getenv("QW_ATTN_BWD");
+    return e && std::string(e) == "mma";
+  }();
+  if ((D == 64 || D == 128) && !use_mma) {
+    check_cuda(cudaGetLastError(), "attn_delta");
+    flash_attn_bwd_tc(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq, lddq, dk, lddk, dv, lddv, B, S, Hq, Hkv, D,
+                      scale, stream);
+    return;
+  }
   dim3 grid_kv((S + 63) / 64, B * Hkv);
   dim3 grid_q((S + 63) / 64, B * Hq);
   if (D == 32) {

@@ -1,0 +1,497 @@
+// Causal flash-attention backward on the Blackwell tensor cores: tcgen05.mma with TMEM accumulators, operands
+// staged by TMA into 128-byte-swizzled shared memory, head_dim 64 or 128, grouped-query attention.
+//
+// One kernel template serves both passes (deterministic, no atomics):
+//
+//   dK/dV pass  CTA = 128 keys of one (batch, kv-head). It loops over the group's q-heads and over the 64-query
+//               tiles at or after its first key. Row operands X1 = K, X2 = V; column operands Y1 = Q, Y2 = dO.
+//                 S^T = K Q^T, dP^T = V dO^T                      (TMEM, 128 x 64, double-buffered)
+//                 P^T = exp2(S^T * scale*log2e - lse2[q]),  dS^T = P^T * (dP^T - delta[q])   (softmax warps)
+//                 dV += P^T dO,  dK += dS^T Q                    (TMEM, 128 x D each; P^T/dS^T from shared memory)
+//   dQ pass     CTA = 128 queries of one (batch, q-head); loops over the 64-key tiles up to the diagonal.
+//               X1 = Q, X2 = dO; Y1 = K, Y2 = V.  S = Q K^T, dP = dO V^T, dS = P * (dP - delta[q]), dQ += dS K.
+//
+// Roles (320 threads, one CTA per SM — the shared-memory request guarantees it, so the 512 TMEM columns never
+// contend):
+//   warp 0      TMA: the two row tiles once, then the column tiles through a ring of stages; in the dK/dV pass its
+//               lanes also stage the 64 lse/delta values of each query tile next to the tile.
+//   warp 1      MMA issuer (one thread): S/dP of tile j, then the accumulation of tile j-1 once the softmax warps
+//               have written its P/dS operands, so the tensor core works on tile j while tile j-1 is in softmax.
+//   warps 2-9   softmax: warp w reads TMEM lanes 32*(w%4).. (its row quarter); warps 2-5 take columns 0-31 and
+//               warps 6-9 columns 32-63 of each tile. They write bf16 P/dS rows into the swizzled K-major layout the
+//               next MMA reads, and at the end read dK/dV (or dQ) out of TMEM and store them.
+//
+// TMEM columns: [0,128) S (2 x 64), [128,256) dP (2 x 64), [256,256+D) dV or dQ, [256+D,256+2D) dK.
+// Every mbarrier wait is bounded (common.cuh): on a timeout all roles stop, in-flight TMA loads and MMAs are
+// waited for (bounded), TMEM is freed and the status word records the cause.
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "launchers.h"
+
+namespace qw {
+
+CUtensorMap make_bf16_map_3d(const void* ptr, int64_t inner, int64_t rows, int64_t batches, int64_t ld,
+                             int64_t batch_stride, int box_rows);
+
+namespace attn_tc {
+
+constexpr int kRows = 128;                 // tile rows (keys in dK/dV, queries in dQ)
+constexpr int kCols = 64;                  // columns per inner step
+constexpr int kSoftWarps = 8;
+constexpr int kThreads = 64 + 32 * kSoftWarps;
+constexpr int kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+enum Mode : int { kDKDV = 0, kDQ = 1 };
+
+template <int D, int MODE>
+struct Layout {
+  static constexpr int kBoxes = D / 64;                      // 64-wide (128-byte) boxes per row
+  static constexpr int kXBytes = kBoxes * kRows * 128;       // one row operand
+  static constexpr int kYBytes = kBoxes * kCols * 128;       // one column operand
+  static constexpr int kStages = (D == 64) ? 3 : 2;
+  static constexpr int kOBytes = kRows * kCols * 2;          // one bf16 [128 x 64] operand (P^T or dS)
+  static constexpr int kONum = (MODE == kDKDV) ? 2 : 1;
+  static constexpr int kX1 = 0;
+  static constexpr int kX2 = kXBytes;
+  static constexpr int kY = 2 * kXBytes;                     // stages of [Y1 | Y2]
+  static constexpr int kO = kY + kStages * 2 * kYBytes;      // 2 buffers of kONum operands
+  static constexpr int kVec = kO + 2 * kONum * kOBytes;      // stages of [lse2 | delta] (64 floats each)
+  static constexpr int kBar = kVec + kStages * 2 * kCols * 4;
+  static constexpr int kUsed = kBar + 256;
+  static constexpr int kTotal = (kUsed + 1024 > 120 * 1024) ? kUsed + 1024 : 120 * 1024;
+};
+
+struct Params {
+  const float* lse;    // [B, Hq, S], natural log
+  const float* delta;  // [B, Hq, S]
+  bf16* out1;          // dV (dK/dV pass) or dQ
+  int64_t ld1;
+  bf16* out2;          // dK
+  int64_t ld2;
+  int S, Hq, Hkv;
+  float scale;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void store_row32(bf16* dst, const float* v, float mul) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint4 w;
+    w.x = pack_bf16(v[i] * mul, v[i + 1] * mul);
+    w.y = pack_bf16(v[i + 2] * mul, v[i + 3] * mul);
+    w.z = pack_bf16(v[i + 4] * mul, v[i + 5] * mul);
+    w.w = pack_bf16(v[i + 6] * mul, v[i + 7] * mul);
+    *reinterpret_cast<uint4*>(dst + i) = w;
+  }
+}
+
+template <int D, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
+                       Params p) {
+  using L = Layout<D, MODE>;
+  constexpr int kStages = L::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* empty = full + kStages;
+  uint64_t* s_full = empty + kStages;  // [2] S/dP of a tile are in TMEM
+  uint64_t* s_empty = s_full + 2;      // [2] softmax has read them
+  uint64_t* p_full = s_empty + 2;      // [2] P/dS operands written
+  uint64_t* p_empty = p_full + 2;      // [2] accumulation MMAs done with them
+  uint64_t* x_full = p_empty + 2;
+  uint64_t* acc_full = x_full + 1;
+  uint64_t* teardown = acc_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(teardown + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int group = p.Hq / p.Hkv;
+  int b, hk, hq, row0, n, per_head;
+  if (MODE == kDKDV) {
+    b = blockIdx.x / p.Hkv;
+    hk = blockIdx.x % p.Hkv;
+    hq = hk * group;
+    row0 = blockIdx.y * kRows;  // tile 0 (first keys) sees the most queries: scheduled first
+    per_head = (p.S - row0 + kCols - 1) / kCols;
+    n = per_head * group;
+  } else {
+    b = blockIdx.x / p.Hq;
+    hq = blockIdx.x % p.Hq;
+    hk = hq / group;
+    row0 = (gridDim.y - 1 - blockIdx.y) * kRows;  // the last query tile sees the most keys: scheduled first
+    n = (min(p.S, row0 + kRows) + kCols - 1) / kCols;
+    per_head = n;
+  }
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], kSoftWarps);
+      mbar_init(&p_full[i], kSoftWarps);
+      mbar_init(&p_empty[i], 1);
+    }
+    mbar_init(x_full, 1);
+    mbar_init(acc_full, 1);
+    mbar_init(teardown, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_v);
+    tma_prefetch_desc(&map_do);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    const CUtensorMap* mx1 = MODE == kDKDV ? &map_k : &map_q;
+    const CUtensorMap* mx2 = MODE == kDKDV ? &map_v : &map_do;
+    const CUtensorMap* my1 = MODE == kDKDV ? &map_q : &map_k;
+    const CUtensorMap* my2 = MODE == kDKDV ? &map_do : &map_v;
+    const int xh = MODE == kDKDV ? hk : hq;
+    int issued[kStages];
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) issued[s] = -1;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(x_full, 2 * L::kXBytes);
+#pragma unroll
+      for (int c = 0; c < L::kBoxes; ++c) {
+        tma_load_3d(smem + L::kX1 + c * kRows * 128, mx1, x_full, xh * D + c * 64, row0, b);
+        tma_load_3d(smem + L::kX2 + c * kRows * 128, mx2, x_full, xh * D + c * 64, row0, b);
+      }
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int j = 0; j < n; ++j) {
+      int go = 1;
+      if (lane == 0) go = (mbar_wait(&empty[stage], phase ^ 1, kTimeoutEmpty) && !*abort_flag) ? 1 : 0;
+      go = __shfl_sync(0xffffffffu, go, 0);  // one decision for the whole warp
+      if (!go) {
+        if (lane == 0) *abort_flag = 1;
+        break;
+      }
+      const int yh = MODE == kDKDV ? hq + j / per_head : hk;
+      const int cs = MODE == kDKDV ? row0 + (j % per_head) * kCols : j * kCols;
+      if (MODE == kDKDV) {
+        float* vec = reinterpret_cast<float*>(smem + L::kVec + stage * 2 * kCols * 4);
+        const int64_t base = (static_cast<int64_t>(b) * p.Hq + yh) * p.S;
+        for (int i = lane; i < kCols; i += 32) {
+          const int qi = cs + i;
+          vec[i] = qi < p.S ? p.lse[base + qi] * kLog2e : 0.f;
+          vec[kCols + i] = qi < p.S ? p.delta[base + qi] : 0.f;
+        }
+        __syncwarp();
+      }
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[stage], 2 * L::kYBytes);
+        issued[stage] = static_cast<int>(phase);
+        uint8_t* y1 = smem + L::kY + stage * 2 * L::kYBytes;
+        uint8_t* y2 = y1 + L::kYBytes;
+#pragma unroll
+        for (int c = 0; c < L::kBoxes; ++c) {
+          tma_load_3d(y1 + c * kCols * 128, my1, &full[stage], yh * D + c * 64, cs, b);
+          tma_load_3d(y2 + c * kCols * 128, my2, &full[stage], yh * D + c * 64, cs, b);
+        }
+      }
+      if (++stage == kStages) { stage = 0; phase ^= 1; }
+    }
+    if (lane == 0) {  // drain: every load this warp issued has landed before the CTA may exit
+      mbar_wait(x_full, 0, kTimeoutFull);
+      for (int s = 0; s < kStages; ++s)
+        if (issued[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(issued[s]), kTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16(kRows, kCols, false, false);
+      constexpr uint32_t id_acc = idesc_bf16(kRows, D, false, true);
+      const uint32_t sx1 = smem_u32(smem + L::kX1), sx2 = smem_u32(smem + L::kX2);
+      bool ok = mbar_wait(x_full, 0, kTimeoutFull);
+      if (!ok) *abort_flag = 1;
+      tc_fence_after();
+      int stage = 0, prev_stage = 0;
+      uint32_t phase = 0;
+      for (int j = 0; ok && j <= n; ++j) {
+        if (*abort_flag) break;
+        if (j < n) {
+          const int buf = j & 1;
+          const uint32_t use = (j >> 1) & 1;
+          if (!mbar_wait(&full[stage], phase, kTimeoutFull) ||
+              !mbar_wait(&s_empty[buf], use ^ 1, kTimeoutAccumFree)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sy1 = smem_u32(smem + L::kY + stage * 2 * L::kYBytes), sy2 = sy1 + L::kYBytes;
+          const uint32_t ts = tmem + buf * kCols, tdp = tmem + 128 + buf * kCols;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            const uint32_t ox = (k / 4) * (kRows * 128) + (k % 4) * 32;
+            const uint32_t oy = (k / 4) * (kCols * 128) + (k % 4) * 32;
+            umma_bf16(ts, smem_desc_sw128(sx1 + ox, 16, 1024), smem_desc_sw128(sy1 + oy, 16, 1024), id_s,
+                      k > 0 ? 1u : 0u);
+            umma_bf16(tdp, smem_desc_sw128(sx2 + ox, 16, 1024), smem_desc_sw128(sy2 + oy, 16, 1024), id_s,
+                      k > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[buf]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1;
+          const int buf = jj & 1;
+          if (!mbar_wait(&p_full[buf], (jj >> 1) & 1, kTimeoutAccum)) {
+            *abort_flag = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sy1 = smem_u32(smem + L::kY + prev_stage * 2 * L::kYBytes), sy2 = sy1 + L::kYBytes;
+          const uint32_t so = smem_u32(smem + L::kO + buf * L::kONum * L::kOBytes);
+#pragma unroll
+          for (int k = 0; k < kCols / 16; ++k) {
+            const uint32_t acc = (jj > 0 || k > 0) ? 1u : 0u;
+            // B operands are the column tiles read MN-major: 64-wide MN blocks one box apart, K rows of 128 B
+            const uint64_t b1 = smem_desc_sw128(sy1 + k * 2048, kCols * 128, 1024);
+            const uint64_t b2 = smem_desc_sw128(sy2 + k * 2048, kCols * 128, 1024);
+            if (MODE == kDKDV) {
+              umma_bf16(tmem + 256, smem_desc_sw128(so + k * 32, 16, 1024), b2, id_acc, acc);                // dV
+              umma_bf16(tmem + 256 + D, smem_desc_sw128(so + L::kOBytes + k * 32, 16, 1024), b1, id_acc, acc);  // dK
+            } else {
+              umma_bf16(tmem + 256, smem_desc_sw128(so + k * 32, 16, 1024), b1, id_acc, acc);  // dQ
+            }
+          }
+          umma_commit(&empty[prev_stage]);
+          umma_commit(&p_empty[buf]);
+        }
+        if (j < n) {
+          prev_stage = stage;
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      umma_commit(acc_full);  // fires once every MMA issued above has completed
+      umma_commit(teardown);
+      mbar_wait(teardown, 0, kTimeoutAccum);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax + epilogue (warps 2..9)
+    const int sw = warp - 2;
+    const int quarter = warp % 4;
+    const int half = sw / 4;
+    const int row = quarter * 32 + lane;
+    const int grow = row0 + row;  // key (dK/dV) or query (dQ) index of this thread's row
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const float sl2 = p.scale * kLog2e;
+    float row_lse2 = 0.f, row_delta = 0.f;
+    if (MODE == kDQ && grow < p.S) {
+      const int64_t idx = (static_cast<int64_t>(b) * p.Hq + hq) * p.S + grow;
+      row_lse2 = p.lse[idx] * kLog2e;
+      row_delta = p.delta[idx];
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      // every exit decision is warp-uniform: the TMEM loads and __syncwarp below need the full warp
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+      const int buf = j & 1;
+      const uint32_t use = (j >> 1) & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[buf], use, kTimeoutAccum))) { *abort_flag = 1; ok = false; break; }
+      tc_fence_after();
+      float s[32], dp[32];
+      tmem_ld32(tmem + lane_off + buf * kCols + half * 32, s);
+      tmem_ld32(tmem + lane_off + 128 + buf * kCols + half * 32, dp);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_empty[buf]);
+
+      const int cs = MODE == kDKDV ? row0 + (j % per_head) * kCols : j * kCols;
+      const int col0 = cs + half * 32;
+      bool need_mask = (col0 + 32 > p.S) || (row0 + kRows > p.S);
+      if (MODE == kDKDV) need_mask = need_mask || (col0 < row0 + kRows);
+      else need_mask = need_mask || (col0 + 31 > row0);
+      uint32_t pk[16], dk[16];
+      if (MODE == kDKDV) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, kTimeoutFull))) { *abort_flag = 1; ok = false; break; }
+        const float4* l4 = reinterpret_cast<const float4*>(smem + L::kVec + stage * 2 * kCols * 4) + half * 8;
+        const float4* d4 = l4 + kCols / 4;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 l = l4[i], d = d4[i];
+          const float lv[4] = {l.x, l.y, l.z, l.w}, dv[4] = {d.x, d.y, d.z, d.w};
+          float pv[4], ds[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = 4 * i + e;
+            float x = ex2(fmaf(s[c], sl2, -lv[e]));
+            if (need_mask) {
+              const int qi = col0 + c;
+              if (qi < grow || qi >= p.S || grow >= p.S) x = 0.f;
+            }
+            pv[e] = x;
+            ds[e] = x * (dp[c] - dv[e]);
+          }
+          pk[2 * i] = pack_bf16(pv[0], pv[1]);
+          pk[2 * i + 1] = pack_bf16(pv[2], pv[3]);
+          dk[2 * i] = pack_bf16(ds[0], ds[1]);
+          dk[2 * i + 1] = pack_bf16(ds[2], ds[3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float ds2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = 2 * i + e;
+            float x = ex2(fmaf(s[c], sl2, -row_lse2));
+            if (need_mask) {
+              const int ki = col0 + c;
+              if (ki > grow || ki >= p.S || grow >= p.S) x = 0.f;
+            }
+            ds2[e] = x * (dp[c] - row_delta);
+          }
+          dk[i] = pack_bf16(ds2[0], ds2[1]);
+        }
+      }
+      if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[buf], use ^ 1, kTimeoutAccumFree))) {
+        *abort_flag = 1;
+        ok = false;
+        break;
+      }
+      uint8_t* obuf = smem + L::kO + buf * L::kONum * L::kOBytes + row * 128;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int chunk = (half * 4 + q) ^ (row & 7);
+        if (MODE == kDKDV) {
+          *reinterpret_cast<uint4*>(obuf + chunk * 16) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(obuf + L::kOBytes + chunk * 16) =
+              make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
+        } else {
+          *reinterpret_cast<uint4*>(obuf + chunk * 16) = make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
+        }
+      }
+      fence_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[buf]);
+      if (++stage == kStages) { stage = 0; phase ^= 1; }
+    }
+    // epilogue: accumulators -> bf16 rows (dK and dQ carry the softmax scale)
+    if (__all_sync(0xffffffffu, ok && !*abort_flag)) {
+      if (__all_sync(0xffffffffu, mbar_wait(acc_full, 0, kTimeoutAccum))) {
+        tc_fence_after();
+        const int h1 = MODE == kDKDV ? hk : hq;
+        const int64_t tok = static_cast<int64_t>(b) * p.S + grow;
+#pragma unroll
+        for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
+          float v[32];
+          tmem_ld32(tmem + lane_off + 256 + c, v);
+          if (grow < p.S) store_row32(p.out1 + tok * p.ld1 + h1 * D + c, v, MODE == kDKDV ? 1.f : p.scale);
+          if (MODE == kDKDV) {
+            tmem_ld32(tmem + lane_off + 256 + D + c, v);
+            if (grow < p.S) store_row32(p.out2 + tok * p.ld2 + hk * D + c, v, p.scale);
+          }
+        }
+      } else {
+        *abort_flag = 1;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+template <int D, int MODE>
+void launch(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+            const Params& p, dim3 grid, cudaStream_t stream) {
+  auto kernel = attn_bwd_tc_kernel<D, MODE>;
+  static bool configured = false;
+  if (!configured) {
+    check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<D, MODE>::kTotal),
+               "attention tc smem");
+    configured = true;
+  }
+  kernel<<<grid, kThreads, Layout<D, MODE>::kTotal, stream>>>(mq, mk, mv, mdo, p);
+  check_cuda(cudaGetLastError(), "attention tc launch");
+}
+
+template <int D>
+void run(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv, const bf16* dout,
+         int64_t lddo, const float* lse, const float* delta, bf16* dq, int64_t lddq, bf16* dk, int64_t lddk, bf16* dv,
+         int64_t lddv, int B, int S, int Hq, int Hkv, float scale, cudaStream_t stream) {
+  const int tiles = (S + kRows - 1) / kRows;
+  Params p{};
+  p.lse = lse;
+  p.delta = delta;
+  p.S = S;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale = scale;
+  // dK/dV: K, V are 128-row tiles; Q, dO 64-row tiles
+  {
+    auto mq = make_bf16_map_3d(q, static_cast<int64_t>(Hq) * D, S, B, ldq, S * ldq, kCols);
+    auto mdo = make_bf16_map_3d(dout, static_cast<int64_t>(Hq) * D, S, B, lddo, S * lddo, kCols);
+    auto mk = make_bf16_map_3d(k, static_cast<int64_t>(Hkv) * D, S, B, ldk, S * ldk, kRows);
+    auto mv = make_bf16_map_3d(v, static_cast<int64_t>(Hkv) * D, S, B, ldv, S * ldv, kRows);
+    p.out1 = dv;
+    p.ld1 = lddv;
+    p.out2 = dk;
+    p.ld2 = lddk;
+    launch<D, kDKDV>(mq, mk, mv, mdo, p, dim3(B * Hkv, tiles), stream);
+  }
+  // dQ: Q, dO are 128-row tiles; K, V 64-row tiles
+  {
+    auto mq = make_bf16_map_3d(q, static_cast<int64_t>(Hq) * D, S, B, ldq, S * ldq, kRows);
+    auto mdo = make_bf16_map_3d(dout, static_cast<int64_t>(Hq) * D, S, B, lddo, S * lddo, kRows);
+    auto mk = make_bf16_map_3d(k, static_cast<int64_t>(Hkv) * D, S, B, ldk, S * ldk, kCols);
+    auto mv = make_bf16_map_3d(v, static_cast<int64_t>(Hkv) * D, S, B, ldv, S * ldv, kCols);
+    p.out1 = dq;
+    p.ld1 = lddq;
+    p.out2 = nullptr;
+    p.ld2 = 0;
+    launch<D, kDQ>(mq, mk, mv, mdo, p, dim3(B * Hq, tiles), stream);
+  }
+}
+
+}  // namespace attn_tc
+
+void flash_attn_bwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv,
+                       const bf16* dout, int64_t lddo, const float* lse, const float* delta, bf16* dq, int64_t lddq,
+                       bf16* dk, int64_t lddk, bf16* dv, int64_t lddv, int B, int S, int Hq, int Hkv, int D,
+                       float scale, cudaStream_t stream) {
+  if (B == 0 || S == 0) return;
+  if (D == 64)
+    attn_tc::run<64>(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq, lddq, dk, lddk, dv, lddv, B, S, Hq, Hkv, scale,
+                     stream);
+  else if (D == 128)
+    attn_tc::run<128>(q, ldq, k, ldk, v, ldv, dout, lddo, lse, delta, dq, lddq, dk, lddk, dv, lddv, B, S, Hq, Hkv,
+                      scale, stream);
+  else
+    throw std::runtime_error("flash_attn_bwd_tc: head_dim must be 64 or 128");
+}
+
+int attention_tc_status(bool clear) { return read_status_word(clear); }
+
+}  // namespace qw

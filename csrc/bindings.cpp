@@ -521,6 +521,7 @@ int64_t read_status(bool clear) {
   if ((t = qw::routing_status(clear)) && !s) s = t;
   if ((t = qw::optim_status(clear)) && !s) s = t;
   if ((t = qw::attention_status(clear)) && !s) s = t;
+  if ((t = qw::attention_tc_status(clear)) && !s) s = t;
   if ((t = qw::p2p_status(clear)) && !s) s = t;
   if ((t = qw::decode_status(clear)) && !s) s = t;
   return s;

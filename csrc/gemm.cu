@@ -61,6 +61,36 @@ static CUtensorMap make_map(const void* ptr, int64_t inner, int64_t outer, int64
   return map;
 }
 
+}  // namespace gemm
+
+// 3-D bf16 map over [batches][rows][inner] with row stride `ld` and batch stride `batch_stride` elements; the box is
+// 64 elements (128 B, swizzle-128) x box_rows x 1. Coordinates past `rows` read as zeros, so a tile never reaches
+// into the next batch.
+CUtensorMap make_bf16_map_3d(const void* ptr, int64_t inner, int64_t rows, int64_t batches, int64_t ld,
+                             int64_t batch_stride, int box_rows) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaSetDevice(dev);
+  gemm::require((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base must be 16-byte aligned");
+  gemm::require((ld * 2) % 16 == 0 && (batch_stride * 2) % 16 == 0, "TMA strides must be multiples of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(batches)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * 2), static_cast<cuuint64_t>(batch_stride * 2)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = gemm::encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+                                 elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("qw: cuTensorMapEncodeTiled (3-D) failed (code " + std::to_string(static_cast<int>(r)) +
+                             ", inner " + std::to_string(inner) + ", rows " + std::to_string(rows) + ", ld " +
+                             std::to_string(ld) + ")");
+  return map;
+}
+
+namespace gemm {
+
 static int num_sms() {
   static int n = 0;
   if (!n) {

@@ -120,6 +120,12 @@ void flash_attn_bwd(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, cons
                     int64_t lddq, bf16* dk, int64_t lddk, bf16* dv, int64_t lddv, int B, int S, int Hq, int Hkv, int D,
                     float scale, cudaStream_t stream);
 int attention_status(bool clear);
+// tcgen05 backward (dK/dV and dQ kernels) for head_dim 64 / 128; `delta` must already hold rowsum(dO * O)
+void flash_attn_bwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv,
+                       const bf16* dout, int64_t lddo, const float* lse, const float* delta, bf16* dq, int64_t lddq,
+                       bf16* dk, int64_t lddk, bf16* dv, int64_t lddv, int B, int S, int Hq, int Hkv, int D,
+                       float scale, cudaStream_t stream);
+int attention_tc_status(bool clear);
 
 // ---- p2p.cu ----
 void p2p_push(const void* src, int64_t block_bytes, void* const* peer_bufs, int* const* peer_flags, int world, int me,

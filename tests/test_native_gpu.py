@@ -57,7 +57,8 @@ def test_norm(kind, H):
     _status_ok()
 
 
-@pytest.mark.parametrize("B,S,hq,hkv,d", [(2, 200, 4, 4, 64), (1, 333, 8, 2, 128), (2, 128, 2, 1, 64)])
+@pytest.mark.parametrize("B,S,hq,hkv,d", [(2, 200, 4, 4, 64), (1, 333, 8, 2, 128), (2, 128, 2, 1, 64),
+                                         (1, 1024, 4, 2, 64), (1, 640, 2, 2, 128)])
 def test_attention(B, S, hq, hkv, d):
     from quantaweave_b200.models.layers import apply_rope_reference, rope_tables
     from quantaweave_b200.ops.attention import attention_core
