@@ -11,15 +11,19 @@
 //   dQ pass     CTA = 128 queries of one (batch, q-head); loops over the 64-key tiles up to the diagonal.
 //               X1 = Q, X2 = dO; Y1 = K, Y2 = V.  S = Q K^T, dP = dO V^T, dS = P * (dP - delta[q]), dQ += dS K.
 //
-// Roles (320 threads, one CTA per SM — the shared-memory request guarantees it, so the 512 TMEM columns never
+// Roles (576 threads, one CTA per SM — the shared-memory request guarantees it, so the 512 TMEM columns never
 // contend):
-//   warp 0      TMA: the two row tiles once, then the column tiles through a ring of stages; in the dK/dV pass its
-//               lanes also stage the 64 lse/delta values of each query tile next to the tile.
-//   warp 1      MMA issuer (one thread): S/dP of tile j, then the accumulation of tile j-1 once the softmax warps
-//               have written its P/dS operands, so the tensor core works on tile j while tile j-1 is in softmax.
-//   warps 2-9   softmax: warp w reads TMEM lanes 32*(w%4).. (its row quarter); warps 2-5 take columns 0-31 and
-//               warps 6-9 columns 32-63 of each tile. They write bf16 P/dS rows into the swizzled K-major layout the
-//               next MMA reads, and at the end read dK/dV (or dQ) out of TMEM and store them.
+//   warp 0       TMA: the two row tiles once, then the column tiles through a ring of 3 stages; in the dK/dV pass
+//                its lanes also stage the 64 lse/delta values of each query tile next to the tile.
+//   warp 1       MMA issuer (one thread), polling: S/dP of the next tile as soon as its stage has landed and the
+//                softmax group owning its TMEM buffer has loaded that buffer's previous tile, and the accumulation of
+//                the oldest tile whose P/dS operands are written — whichever is ready first, so neither the tensor
+//                core nor a softmax group waits behind an unrelated condition.
+//   warps 2-17   softmax, two groups of 8 warps working on alternate tiles (group g: tiles j % 2 == g, TMEM S/dP
+//                buffer g, operand buffer g), so one group's latency chain overlaps the other's. In a group, warp w
+//                reads TMEM lanes 32*(w%4).. (its row quarter), and the first four warps take columns 0-31, the last
+//                four 32-63. They write bf16 P/dS rows into the swizzled K-major layout the next MMA reads, and at
+//                the end read dK/dV (or dQ) out of TMEM and store them.
 //
 // TMEM columns: [0,128) S (2 x 64), [128,256) dP (2 x 64), [256,256+D) dV or dQ, [256+D,256+2D) dK.
 // Every mbarrier wait is bounded (common.cuh): on a timeout all roles stop, in-flight TMA loads and MMAs are
@@ -40,7 +44,7 @@ namespace attn_tc {
 
 constexpr int kRows = 128;                 // tile rows (keys in dK/dV, queries in dQ)
 constexpr int kCols = 64;                  // columns per inner step
-constexpr int kSoftWarps = 8;
+constexpr int kSoftWarps = 16;  // two groups of 8
 constexpr int kThreads = 64 + 32 * kSoftWarps;
 constexpr int kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -52,7 +56,8 @@ struct Layout {
   static constexpr int kBoxes = D / 64;                      // 64-wide (128-byte) boxes per row
   static constexpr int kXBytes = kBoxes * kRows * 128;       // one row operand
   static constexpr int kYBytes = kBoxes * kCols * 128;       // one column operand
-  static constexpr int kStages = (D == 64) ? 3 : 2;
+  // tiles j, j+1, j+2 (S issued ahead) resident, plus one stage of TMA lead where shared memory allows
+  static constexpr int kStages = (D == 64) ? 6 : 3;
   static constexpr int kOBytes = kRows * kCols * 2;          // one bf16 [128 x 64] operand (P^T or dS)
   static constexpr int kONum = (MODE == kDKDV) ? 2 : 1;
   static constexpr int kX1 = 0;
@@ -82,11 +87,68 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Bounded wait that parks the thread: try_wait with a suspend-time hint sleeps until the phase completes (or the
+// hint elapses), so waiting warps take no issue slots from the softmax warps sharing their SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_sleep_wait(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
+  const uint64_t start = globaltimer();
+  while (!mbar_try_wait_hint(bar, parity, 1000000u)) {
+    if (globaltimer() - start > QW_WAIT_TIMEOUT_NS) {
+      set_status(code);
+      return false;
+    }
+  }
+  return true;
+}
+
+// Non-blocking probe of an mbarrier phase (the MMA issuer polls two kinds of barriers and must not park on either).
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void store_row32(bf16* dst, const float* v, float mul) {
+// Two 32-column TMEM loads (32 lanes x 32 bit each) issued back to back with one wait, in one asm block so no use of
+// the results can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld32_pair(uint32_t taddr_a, uint32_t taddr_b, float* fa, float* fb) {
+  uint32_t a[32], b[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15]), "=r"(a[16]), "=r"(a[17]), "=r"(a[18]), "=r"(a[19]), "=r"(a[20]), "=r"(a[21]), "=r"(a[22]), "=r"(a[23]), "=r"(a[24]), "=r"(a[25]), "=r"(a[26]), "=r"(a[27]), "=r"(a[28]), "=r"(a[29]), "=r"(a[30]), "=r"(a[31]), "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]), "=r"(b[10]), "=r"(b[11]), "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15]), "=r"(b[16]), "=r"(b[17]), "=r"(b[18]), "=r"(b[19]), "=r"(b[20]), "=r"(b[21]), "=r"(b[22]), "=r"(b[23]), "=r"(b[24]), "=r"(b[25]), "=r"(b[26]), "=r"(b[27]), "=r"(b[28]), "=r"(b[29]), "=r"(b[30]), "=r"(b[31])
+      : "r"(taddr_a), "r"(taddr_b)
+      : "memory");
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
+  for (int i = 0; i < 32; ++i) {
+    fa[i] = __uint_as_float(a[i]);
+    fb[i] = __uint_as_float(b[i]);
+  }
+}
+
+__device__ __forceinline__ void store_row16(bf16* dst, const float* v, float mul) {
+#pragma unroll
+  for (int i = 0; i < 16; i += 8) {
     uint4 w;
     w.x = pack_bf16(v[i] * mul, v[i + 1] * mul);
     w.y = pack_bf16(v[i + 2] * mul, v[i + 3] * mul);
@@ -97,6 +159,8 @@ __device__ __forceinline__ void store_row32(bf16* dst, const float* v, float mul
 }
 
 template <int D, int MODE>
+// 18 warps: the register file is split over the 4 SM sub-partitions, one of which holds 5 warps, so a thread gets
+// at most 16384 / 160 -> 96 registers; __launch_bounds__ lets ptxas apply that limit.
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_do,
@@ -138,13 +202,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], MODE == kDKDV ? 2 : 1);  // dK/dV: the TMA arrival plus the lse/delta staging arrival
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kSoftWarps);
-      mbar_init(&p_full[i], kSoftWarps);
+      mbar_init(&s_empty[i], kSoftWarps / 2);
+      mbar_init(&p_full[i], kSoftWarps / 2);
       mbar_init(&p_empty[i], 1);
     }
     mbar_init(x_full, 1);
@@ -183,11 +247,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(smem + L::kX2 + c * kRows * 128, mx2, x_full, xh * D + c * 64, row0, b);
       }
     }
+    // lse2 / delta of the 64 queries of a dK/dV tile: lane l holds columns l and l+32
+    float next_l[kCols / 32], next_d[kCols / 32];
+    auto load_vec = [&](int t) {
+      const int th = hq + t / per_head;
+      const int tcs = row0 + (t % per_head) * kCols;
+      const int64_t base = (static_cast<int64_t>(b) * p.Hq + th) * p.S;
+#pragma unroll
+      for (int k = 0; k < kCols / 32; ++k) {
+        const int qi = tcs + lane + 32 * k;
+        next_l[k] = qi < p.S ? p.lse[base + qi] * kLog2e : 0.f;
+        next_d[k] = qi < p.S ? p.delta[base + qi] : 0.f;
+      }
+    };
+    if (MODE == kDKDV && n > 0) load_vec(0);
     int stage = 0;
     uint32_t phase = 0;
     for (int j = 0; j < n; ++j) {
       int go = 1;
-      if (lane == 0) go = (mbar_wait(&empty[stage], phase ^ 1, kTimeoutEmpty) && !*abort_flag) ? 1 : 0;
+      if (lane == 0) go = (mbar_sleep_wait(&empty[stage], phase ^ 1, kTimeoutEmpty) && !*abort_flag) ? 1 : 0;
       go = __shfl_sync(0xffffffffu, go, 0);  // one decision for the whole warp
       if (!go) {
         if (lane == 0) *abort_flag = 1;
@@ -195,17 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int yh = MODE == kDKDV ? hq + j / per_head : hk;
       const int cs = MODE == kDKDV ? row0 + (j % per_head) * kCols : j * kCols;
-      if (MODE == kDKDV) {
-        float* vec = reinterpret_cast<float*>(smem + L::kVec + stage * 2 * kCols * 4);
-        const int64_t base = (static_cast<int64_t>(b) * p.Hq + yh) * p.S;
-        for (int i = lane; i < kCols; i += 32) {
-          const int qi = cs + i;
-          vec[i] = qi < p.S ? p.lse[base + qi] * kLog2e : 0.f;
-          vec[kCols + i] = qi < p.S ? p.delta[base + qi] : 0.f;
-        }
-        __syncwarp();
-      }
-      if (lane == 0) {
+      if (lane == 0) {  // the tile loads first, so their latency overlaps the lse/delta staging below
         mbar_arrive_expect_tx(&full[stage], 2 * L::kYBytes);
         issued[stage] = static_cast<int>(phase);
         uint8_t* y1 = smem + L::kY + stage * 2 * L::kYBytes;
@@ -216,12 +284,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(y2 + c * kCols * 128, my2, &full[stage], yh * D + c * 64, cs, b);
         }
       }
+      if (MODE == kDKDV) {
+        // the values of tile j were loaded into registers one iteration earlier; load tile j+1's now, so the
+        // global-load latency overlaps this warp's wait for the next free stage instead of serialising the ring
+        float* vec = reinterpret_cast<float*>(smem + L::kVec + stage * 2 * kCols * 4);
+#pragma unroll
+        for (int k = 0; k < kCols / 32; ++k) {
+          vec[lane + 32 * k] = next_l[k];
+          vec[kCols + lane + 32 * k] = next_d[k];
+        }
+        if (j + 1 < n) load_vec(j + 1);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[stage]);  // second arrival: the staged values are written
+      }
       if (++stage == kStages) { stage = 0; phase ^= 1; }
     }
     if (lane == 0) {  // drain: every load this warp issued has landed before the CTA may exit
-      mbar_wait(x_full, 0, kTimeoutFull);
+      mbar_sleep_wait(x_full, 0, kTimeoutFull);
       for (int s = 0; s < kStages; ++s)
-        if (issued[s] >= 0) mbar_wait(&full[s], static_cast<uint32_t>(issued[s]), kTimeoutFull);
+        if (issued[s] >= 0) mbar_sleep_wait(&full[s], static_cast<uint32_t>(issued[s]), kTimeoutFull);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -229,75 +310,95 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t id_s = idesc_bf16(kRows, kCols, false, false);
       constexpr uint32_t id_acc = idesc_bf16(kRows, D, false, true);
       const uint32_t sx1 = smem_u32(smem + L::kX1), sx2 = smem_u32(smem + L::kX2);
-      bool ok = mbar_wait(x_full, 0, kTimeoutFull);
-      if (!ok) *abort_flag = 1;
+      // S/dP of tile t into TMEM buffer t&1 (its stage has landed; from t = 2 on, the softmax group owning the buffer
+      // has loaded tile t-2)
+      auto s_ready = [&](int t) {
+        return mbar_test(&full[t % kStages], (t / kStages) & 1) &&
+               (t < 2 || mbar_test(&s_empty[t & 1], ((t >> 1) - 1) & 1));
+      };
+      auto issue_s = [&](int t) {
+        const int st = t % kStages;
+        const int buf = t & 1;
+        tc_fence_after();
+        const uint32_t sy1 = smem_u32(smem + L::kY + st * 2 * L::kYBytes), sy2 = sy1 + L::kYBytes;
+        const uint32_t ts = tmem + buf * kCols, tdp = tmem + 128 + buf * kCols;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t ox = (k / 4) * (kRows * 128) + (k % 4) * 32;
+          const uint32_t oy = (k / 4) * (kCols * 128) + (k % 4) * 32;
+          umma_bf16(ts, smem_desc_sw128(sx1 + ox, 16, 1024), smem_desc_sw128(sy1 + oy, 16, 1024), id_s,
+                    k > 0 ? 1u : 0u);
+          umma_bf16(tdp, smem_desc_sw128(sx2 + ox, 16, 1024), smem_desc_sw128(sy2 + oy, 16, 1024), id_s,
+                    k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[buf]);
+      };
+      // accumulation of tile j once the softmax group has written its P/dS operands
+      auto issue_acc = [&](int j) {
+        const int buf = j & 1;
+        const int st = j % kStages;
+        tc_fence_after();
+        const uint32_t sy1 = smem_u32(smem + L::kY + st * 2 * L::kYBytes), sy2 = sy1 + L::kYBytes;
+        const uint32_t so = smem_u32(smem + L::kO + buf * L::kONum * L::kOBytes);
+#pragma unroll
+        for (int k = 0; k < kCols / 16; ++k) {
+          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          // B operands are the column tiles read MN-major: 64-wide MN blocks one box apart, K rows of 128 B
+          const uint64_t b1 = smem_desc_sw128(sy1 + k * 2048, kCols * 128, 1024);
+          const uint64_t b2 = smem_desc_sw128(sy2 + k * 2048, kCols * 128, 1024);
+          if (MODE == kDKDV) {
+            umma_bf16(tmem + 256, smem_desc_sw128(so + k * 32, 16, 1024), b2, id_acc, acc);                  // dV
+            umma_bf16(tmem + 256 + D, smem_desc_sw128(so + L::kOBytes + k * 32, 16, 1024), b1, id_acc, acc);  // dK
+          } else {
+            umma_bf16(tmem + 256, smem_desc_sw128(so + k * 32, 16, 1024), b1, id_acc, acc);  // dQ
+          }
+        }
+        umma_commit(&empty[st]);
+        umma_commit(&p_empty[buf]);
+      };
+      bool ok = mbar_sleep_wait(x_full, 0, kTimeoutFull);
       tc_fence_after();
-      int stage = 0, prev_stage = 0;
-      uint32_t phase = 0;
-      for (int j = 0; ok && j <= n; ++j) {
-        if (*abort_flag) break;
-        if (j < n) {
-          const int buf = j & 1;
-          const uint32_t use = (j >> 1) & 1;
-          if (!mbar_wait(&full[stage], phase, kTimeoutFull) ||
-              !mbar_wait(&s_empty[buf], use ^ 1, kTimeoutAccumFree)) {
-            *abort_flag = 1;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sy1 = smem_u32(smem + L::kY + stage * 2 * L::kYBytes), sy2 = sy1 + L::kYBytes;
-          const uint32_t ts = tmem + buf * kCols, tdp = tmem + 128 + buf * kCols;
-#pragma unroll
-          for (int k = 0; k < D / 16; ++k) {
-            const uint32_t ox = (k / 4) * (kRows * 128) + (k % 4) * 32;
-            const uint32_t oy = (k / 4) * (kCols * 128) + (k % 4) * 32;
-            umma_bf16(ts, smem_desc_sw128(sx1 + ox, 16, 1024), smem_desc_sw128(sy1 + oy, 16, 1024), id_s,
-                      k > 0 ? 1u : 0u);
-            umma_bf16(tdp, smem_desc_sw128(sx2 + ox, 16, 1024), smem_desc_sw128(sy2 + oy, 16, 1024), id_s,
-                      k > 0 ? 1u : 0u);
-          }
-          umma_commit(&s_full[buf]);
+      // issue whichever of (next accumulation, next S/dP) is ready, so neither waits behind the other
+      int ns = 0, na = 0;
+      int idle = 0;
+      uint64_t idle_start = 0;
+      while (ok && na < n) {
+        bool progress = false;
+        if (na < ns && mbar_test(&p_full[na & 1], (na >> 1) & 1)) {
+          issue_acc(na++);
+          progress = true;
         }
-        if (j >= 1) {
-          const int jj = j - 1;
-          const int buf = jj & 1;
-          if (!mbar_wait(&p_full[buf], (jj >> 1) & 1, kTimeoutAccum)) {
-            *abort_flag = 1;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sy1 = smem_u32(smem + L::kY + prev_stage * 2 * L::kYBytes), sy2 = sy1 + L::kYBytes;
-          const uint32_t so = smem_u32(smem + L::kO + buf * L::kONum * L::kOBytes);
-#pragma unroll
-          for (int k = 0; k < kCols / 16; ++k) {
-            const uint32_t acc = (jj > 0 || k > 0) ? 1u : 0u;
-            // B operands are the column tiles read MN-major: 64-wide MN blocks one box apart, K rows of 128 B
-            const uint64_t b1 = smem_desc_sw128(sy1 + k * 2048, kCols * 128, 1024);
-            const uint64_t b2 = smem_desc_sw128(sy2 + k * 2048, kCols * 128, 1024);
-            if (MODE == kDKDV) {
-              umma_bf16(tmem + 256, smem_desc_sw128(so + k * 32, 16, 1024), b2, id_acc, acc);                // dV
-              umma_bf16(tmem + 256 + D, smem_desc_sw128(so + L::kOBytes + k * 32, 16, 1024), b1, id_acc, acc);  // dK
-            } else {
-              umma_bf16(tmem + 256, smem_desc_sw128(so + k * 32, 16, 1024), b1, id_acc, acc);  // dQ
-            }
-          }
-          umma_commit(&empty[prev_stage]);
-          umma_commit(&p_empty[buf]);
+        if (ns < n && s_ready(ns)) {
+          issue_s(ns++);
+          progress = true;
         }
-        if (j < n) {
-          prev_stage = stage;
-          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        if (progress) {
+          idle = 0;
+          continue;
+        }
+        // nothing ready: park until the oldest tile's operands arrive (or briefly, when no accumulation is pending)
+        if (na < ns) mbar_try_wait_hint(&p_full[na & 1], (na >> 1) & 1, 2000u);
+        else __nanosleep(64);
+        if ((++idle & 63) == 0) {  // bounded: give up after the wait budget without progress
+          if (*abort_flag) { ok = false; break; }
+          const uint64_t now = globaltimer();
+          if (idle == 64) idle_start = now;
+          else if (now - idle_start > QW_WAIT_TIMEOUT_NS) { set_status(kTimeoutAccum); ok = false; break; }
         }
       }
+      if (!ok) *abort_flag = 1;
       umma_commit(acc_full);  // fires once every MMA issued above has completed
       umma_commit(teardown);
-      mbar_wait(teardown, 0, kTimeoutAccum);
+      mbar_sleep_wait(teardown, 0, kTimeoutAccum);
     }
   } else {
-    // ------------------------------------------------------------------ softmax + epilogue (warps 2..9)
+    // ------------------------------------------------------------------ softmax + epilogue (warps 2..17)
+    // group g (warps 2+8g .. 9+8g) takes the tiles j with j % 2 == g and owns TMEM S/dP buffer g and operand buffer g,
+    // so the two groups work on consecutive tiles at the same time
     const int sw = warp - 2;
+    const int grp = sw / 8;
     const int quarter = warp % 4;
-    const int half = sw / 4;
+    const int half = (sw % 8) / 4;
     const int row = quarter * 32 + lane;
     const int grow = row0 + row;  // key (dK/dV) or query (dQ) index of this thread's row
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
@@ -308,19 +409,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       row_lse2 = p.lse[idx] * kLog2e;
       row_delta = p.delta[idx];
     }
-    int stage = 0;
-    uint32_t phase = 0;
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
+    for (int j = grp; j < n; j += 2) {
       // every exit decision is warp-uniform: the TMEM loads and __syncwarp below need the full warp
       if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
-      const int buf = j & 1;
+      const int buf = grp;
       const uint32_t use = (j >> 1) & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[buf], use, kTimeoutAccum))) { *abort_flag = 1; ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_sleep_wait(&s_full[buf], use, kTimeoutAccum))) { *abort_flag = 1; ok = false; break; }
       tc_fence_after();
       float s[32], dp[32];
-      tmem_ld32(tmem + lane_off + buf * kCols + half * 32, s);
-      tmem_ld32(tmem + lane_off + 128 + buf * kCols + half * 32, dp);
+      tmem_ld32_pair(tmem + lane_off + buf * kCols + half * 32, tmem + lane_off + 128 + buf * kCols + half * 32, s, dp);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_empty[buf]);
@@ -330,86 +428,93 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool need_mask = (col0 + 32 > p.S) || (row0 + kRows > p.S);
       if (MODE == kDKDV) need_mask = need_mask || (col0 < row0 + kRows);
       else need_mask = need_mask || (col0 + 31 > row0);
-      uint32_t pk[16], dk[16];
+      const float* vec = nullptr;
       if (MODE == kDKDV) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, kTimeoutFull))) { *abort_flag = 1; ok = false; break; }
-        const float4* l4 = reinterpret_cast<const float4*>(smem + L::kVec + stage * 2 * kCols * 4) + half * 8;
-        const float4* d4 = l4 + kCols / 4;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 l = l4[i], d = d4[i];
-          const float lv[4] = {l.x, l.y, l.z, l.w}, dv[4] = {d.x, d.y, d.z, d.w};
-          float pv[4], ds[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = 4 * i + e;
-            float x = ex2(fmaf(s[c], sl2, -lv[e]));
-            if (need_mask) {
-              const int qi = col0 + c;
-              if (qi < grow || qi >= p.S || grow >= p.S) x = 0.f;
-            }
-            pv[e] = x;
-            ds[e] = x * (dp[c] - dv[e]);
-          }
-          pk[2 * i] = pack_bf16(pv[0], pv[1]);
-          pk[2 * i + 1] = pack_bf16(pv[2], pv[3]);
-          dk[2 * i] = pack_bf16(ds[0], ds[1]);
-          dk[2 * i + 1] = pack_bf16(ds[2], ds[3]);
+        const int st = j % kStages;
+        if (!__all_sync(0xffffffffu, mbar_sleep_wait(&full[st], (j / kStages) & 1, kTimeoutFull))) {
+          *abort_flag = 1;
+          ok = false;
+          break;
         }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float ds2[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int c = 2 * i + e;
-            float x = ex2(fmaf(s[c], sl2, -row_lse2));
-            if (need_mask) {
-              const int ki = col0 + c;
-              if (ki > grow || ki >= p.S || grow >= p.S) x = 0.f;
-            }
-            ds2[e] = x * (dp[c] - row_delta);
-          }
-          dk[i] = pack_bf16(ds2[0], ds2[1]);
-        }
+        vec = reinterpret_cast<const float*>(smem + L::kVec + st * 2 * kCols * 4) + half * 32;
       }
-      if (!__all_sync(0xffffffffu, mbar_wait(&p_empty[buf], use ^ 1, kTimeoutAccumFree))) {
+      if (!__all_sync(0xffffffffu, mbar_sleep_wait(&p_empty[buf], use ^ 1, kTimeoutAccumFree))) {
         *abort_flag = 1;
         ok = false;
         break;
       }
       uint8_t* obuf = smem + L::kO + buf * L::kONum * L::kOBytes + row * 128;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 4; ++q) {  // 8 columns -> one 16-byte chunk of P and of dS
+        uint32_t pw[4], dw[4];
+        float lv[8], dv[8];  // lse2 / delta of the chunk's 8 columns (broadcast 16-byte shared loads)
+        if (MODE == kDKDV) {
+          const float4* v4 = reinterpret_cast<const float4*>(vec) + 2 * q;
+          const float4 l0 = v4[0], l1 = v4[1], d0 = v4[kCols / 4], d1 = v4[kCols / 4 + 1];
+          lv[0] = l0.x; lv[1] = l0.y; lv[2] = l0.z; lv[3] = l0.w; lv[4] = l1.x; lv[5] = l1.y; lv[6] = l1.z; lv[7] = l1.w;
+          dv[0] = d0.x; dv[1] = d0.y; dv[2] = d0.z; dv[3] = d0.w; dv[4] = d1.x; dv[5] = d1.y; dv[6] = d1.z; dv[7] = d1.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) { lv[e] = row_lse2; dv[e] = row_delta; }
+        }
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {  // column pairs
+          float pv[2], ds[2];
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int e = 2 * e2 + h2;
+            const int c = 8 * q + e;
+            float x = ex2(fmaf(s[c], sl2, -lv[e]));
+            if (need_mask) {
+              const int other = col0 + c;  // query (dK/dV) or key (dQ) index of this column
+              const bool bad = MODE == kDKDV ? (other < grow || other >= p.S || grow >= p.S)
+                                             : (other > grow || other >= p.S || grow >= p.S);
+              if (bad) x = 0.f;
+            }
+            pv[h2] = x;
+            ds[h2] = x * (dp[c] - dv[e]);
+          }
+          pw[e2] = pack_bf16(pv[0], pv[1]);
+          dw[e2] = pack_bf16(ds[0], ds[1]);
+        }
         const int chunk = (half * 4 + q) ^ (row & 7);
         if (MODE == kDKDV) {
-          *reinterpret_cast<uint4*>(obuf + chunk * 16) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-          *reinterpret_cast<uint4*>(obuf + L::kOBytes + chunk * 16) =
-              make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(obuf + chunk * 16) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+          *reinterpret_cast<uint4*>(obuf + L::kOBytes + chunk * 16) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
         } else {
-          *reinterpret_cast<uint4*>(obuf + chunk * 16) = make_uint4(dk[4 * q], dk[4 * q + 1], dk[4 * q + 2], dk[4 * q + 3]);
+          *reinterpret_cast<uint4*>(obuf + chunk * 16) = make_uint4(dw[0], dw[1], dw[2], dw[3]);
         }
       }
       fence_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[buf]);
-      if (++stage == kStages) { stage = 0; phase ^= 1; }
     }
-    // epilogue: accumulators -> bf16 rows (dK and dQ carry the softmax scale)
+    // epilogue: accumulators -> bf16 rows (dK and dQ carry the softmax scale). dK/dV: group 0 stores dV, group 1
+    // dK, each half of the columns; dQ: each (group, half) a quarter of the columns.
     if (__all_sync(0xffffffffu, ok && !*abort_flag)) {
-      if (__all_sync(0xffffffffu, mbar_wait(acc_full, 0, kTimeoutAccum))) {
+      if (__all_sync(0xffffffffu, mbar_sleep_wait(acc_full, 0, kTimeoutAccum))) {
         tc_fence_after();
-        const int h1 = MODE == kDKDV ? hk : hq;
         const int64_t tok = static_cast<int64_t>(b) * p.S + grow;
-#pragma unroll
-        for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
-          float v[32];
-          tmem_ld32(tmem + lane_off + 256 + c, v);
-          if (grow < p.S) store_row32(p.out1 + tok * p.ld1 + h1 * D + c, v, MODE == kDKDV ? 1.f : p.scale);
-          if (MODE == kDKDV) {
-            tmem_ld32(tmem + lane_off + 256 + D + c, v);
-            if (grow < p.S) store_row32(p.out2 + tok * p.ld2 + hk * D + c, v, p.scale);
-          }
+        int c0, c1, tcol;
+        bf16* out;
+        float mul;
+        if (MODE == kDKDV) {
+          c0 = half * (D / 2);
+          c1 = c0 + D / 2;
+          tcol = 256 + grp * D;
+          out = grp == 0 ? p.out1 + tok * p.ld1 + hk * D : p.out2 + tok * p.ld2 + hk * D;
+          mul = grp == 0 ? 1.f : p.scale;
+        } else {
+          c0 = (2 * grp + half) * (D / 4);
+          c1 = c0 + D / 4;
+          tcol = 256;
+          out = p.out1 + tok * p.ld1 + hq * D;
+          mul = p.scale;
+        }
+        for (int c = c0; c < c1; c += 16) {
+          float v[16];
+          tmem_ld16(tmem + lane_off + tcol + c, v);
+          if (grow < p.S) store_row16(out + c, v, mul);
         }
       } else {
         *abort_flag = 1;

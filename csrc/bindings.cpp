@@ -182,8 +182,16 @@ void rope_apply(Tensor qkv, int64_t heads_rot, int64_t head_dim, int64_t seq, Op
 void router_logits(Tensor x, Tensor w, Tensor logits) {
   CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DTYPE(w, torch::kFloat32); CHECK_CONTIG(w); CHECK_CONTIG(logits);
   c10::cuda::CUDAGuard g(x.device());
-  qw::router_logits(bptr(x), w.data_ptr<float>(), x.size(0), static_cast<int>(x.size(1)), static_cast<int>(w.size(0)),
-                    logits.data_ptr<float>(), stream());
+  const int64_t T = x.size(0);
+  const int H = static_cast<int>(x.size(1)), E = static_cast<int>(w.size(0));
+  if (qw::router_tc_ok(T, H, E)) {  // tensor cores over the bf16 split of Wr (fp32-exact products)
+    auto w3 = torch::empty({3 * E, H}, x.options().dtype(torch::kBFloat16));
+    auto out3 = torch::empty({T, 3 * E}, x.options().dtype(torch::kFloat32));
+    qw::router_logits_tc(bptr(x), w.data_ptr<float>(), T, H, E, logits.data_ptr<float>(), bptr_mut(w3),
+                         out3.data_ptr<float>(), stream());
+    return;
+  }
+  qw::router_logits(bptr(x), w.data_ptr<float>(), T, H, E, logits.data_ptr<float>(), stream());
 }
 
 void router_topk(Tensor logits, OptT bias, int64_t k, double temperature, Tensor probs, Tensor top_idx, Tensor top_w,
@@ -265,19 +273,37 @@ void router_backward(Tensor probs, Tensor top_idx, Tensor top_w, Tensor d_w, Opt
 }
 
 void router_dx(Tensor d_logits, Tensor w, Tensor dx) {
-  CHECK_CUDA(d_logits);
+  CHECK_CUDA(d_logits); CHECK_CONTIG(d_logits); CHECK_CONTIG(w); CHECK_CONTIG(dx);
   c10::cuda::CUDAGuard g(d_logits.device());
-  qw::router_dx(d_logits.data_ptr<float>(), w.data_ptr<float>(), d_logits.size(0), static_cast<int>(d_logits.size(1)),
-                static_cast<int>(w.size(1)), dx.data_ptr<float>(), stream());
+  const int64_t T = d_logits.size(0);
+  const int E = static_cast<int>(d_logits.size(1)), H = static_cast<int>(w.size(1));
+  if (qw::router_tc_ok(T, H, E)) {
+    auto dls = torch::empty({T, 3 * E}, d_logits.options().dtype(torch::kBFloat16));
+    auto w3 = torch::empty({3 * E, H}, d_logits.options().dtype(torch::kBFloat16));
+    qw::router_dx_tc(d_logits.data_ptr<float>(), w.data_ptr<float>(), T, E, H, dx.data_ptr<float>(), bptr_mut(dls),
+                     bptr_mut(w3), stream());
+    return;
+  }
+  qw::router_dx(d_logits.data_ptr<float>(), w.data_ptr<float>(), T, E, H, dx.data_ptr<float>(), stream());
 }
 
 int64_t router_dw_split(int64_t T) { return qw::router_dw_split(T); }
 
 void router_dw(Tensor d_logits, Tensor x, Tensor dw, bool accumulate, Tensor workspace) {
-  CHECK_CUDA(d_logits);
+  CHECK_CUDA(d_logits); CHECK_CONTIG(d_logits); CHECK_CONTIG(x); CHECK_DTYPE(x, torch::kBFloat16);
   c10::cuda::CUDAGuard g(d_logits.device());
-  qw::router_dw(d_logits.data_ptr<float>(), bptr(x), d_logits.size(0), static_cast<int>(d_logits.size(1)),
-                static_cast<int>(x.size(1)), dw.data_ptr<float>(), accumulate, workspace.data_ptr<float>(), stream());
+  const int64_t T = d_logits.size(0);
+  const int E = static_cast<int>(d_logits.size(1)), H = static_cast<int>(x.size(1));
+  if (qw::router_tc_ok(T, H, E)) {
+    const int64_t chunks = (T + qw::router_dw_chunk(T, H) - 1) / qw::router_dw_chunk(T, H);
+    auto dls = torch::empty({T, 3 * E}, d_logits.options().dtype(torch::kBFloat16));
+    auto partial = torch::empty({chunks * 2 * E * H}, d_logits.options().dtype(torch::kFloat32));
+    qw::router_dw_tc(d_logits.data_ptr<float>(), bptr(x), T, E, H, dw.data_ptr<float>(), accumulate, bptr_mut(dls),
+                     partial.data_ptr<float>(), stream());
+    return;
+  }
+  qw::router_dw(d_logits.data_ptr<float>(), bptr(x), T, E, H, dw.data_ptr<float>(), accumulate,
+                workspace.data_ptr<float>(), stream());
 }
 
 // ------------------------------------------------------------------------------------------------ optimizer / CE

@@ -178,6 +178,27 @@ void linear_wgrad(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int6
   launch<BN, kGroupK, kEpiStore, true, true>(ma, mb, p, static_cast<int64_t>(p.m_tiles) * p.n_tiles, stream);
 }
 
+// partial[c][N,K] = dy[rows of chunk c, N]^T @ x[rows of chunk c, K] for chunks of `chunk` rows (a multiple of 64):
+// split-K for weight gradients whose output is too small to fill the GPU (the caller reduces the partials)
+void linear_wgrad_chunks(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int64_t T, int64_t N, int64_t K,
+                         int64_t chunk, float* partial, cudaStream_t stream) {
+  if (N == 0 || K == 0 || T == 0) return;
+  require(chunk % kBK == 0, "split-K chunk must be a multiple of 64 rows");
+  constexpr int BN = 256;
+  Params p = base_params();
+  p.M = N; p.N = K; p.K = T;
+  p.num_groups = static_cast<int>((T + chunk - 1) / chunk);
+  p.k_chunk = static_cast<int>(chunk);
+  p.m_tiles = static_cast<int>((N + kBM - 1) / kBM);
+  p.n_tiles = static_cast<int>((K + BN - 1) / BN);
+  p.out = partial; p.ldo = K; p.out_fp32 = 1;
+  p.out_group_stride = N * K;
+  auto ma = make_map(dy, N, T, lddy, 64, 64);
+  auto mb = make_map(x, K, T, ldx, 64, 64);
+  launch<BN, kGroupK, kEpiStore, true, true>(ma, mb, p,
+                                             static_cast<int64_t>(p.m_tiles) * p.n_tiles * p.num_groups, stream);
+}
+
 // ------------------------------------------------------------------------------------------------ grouped (MoE)
 // Expert e owns rows [offsets[e], offsets[e] + counts[e]) of the permuted activations; offsets are multiples of
 // 128 and rows [counts[e], roundup128(counts[e])) are zero padding (written as zeros by every producer).

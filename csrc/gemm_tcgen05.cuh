@@ -52,6 +52,8 @@ struct Params {
   int n_tiles;                 // ceil(N / BN) (kEpiSwiGLU: ceil(F / (BN/2)))
   int m_tiles;                 // kGroupK: ceil(M / 128)
   int max_tiles;               // upper bound used when group sizes are device-side
+  int k_chunk;                 // kGroupK without group_rows: group g reduces rows [g*k_chunk, min(K, (g+1)*k_chunk))
+                               // and writes its own C block (split-K with per-chunk partial outputs)
   // epilogue
   void* out;
   long ldo;
@@ -124,6 +126,10 @@ __device__ __forceinline__ bool tile_info(const Params& p, const int* s_prefix, 
       t.row0 = 0;
       t.rows = 0;
       t.num_kb = kb;
+    } else if (!p.group_rows && p.k_chunk > 0) {
+      t.row0 = g * p.k_chunk;
+      t.rows = min(p.k_chunk, p.K - t.row0);
+      t.num_kb = (t.rows + kBK - 1) / kBK;
     } else {
       const int krows = p.group_rows ? p.group_rows[g] : p.K;
       t.row0 = p.group_off ? p.group_off[g] : 0;

@@ -79,6 +79,18 @@ void router_backward(const float* probs, const int* top_idx, const float* top_w,
                      cudaStream_t stream);
 void router_dx(const float* d_logits, const float* w, int64_t T, int E, int H, float* dx, cudaStream_t stream);
 int router_dw_split(int64_t T);
+// tensor-core router GEMMs (fp32 operands split into bf16 parts); scratch: w3 [3E,H] bf16, out3 [T,3E] fp32,
+// dls [T,3E] bf16, partial [ceil(T/router_dw_chunk) * 2E * H] fp32
+bool router_tc_ok(int64_t T, int H, int E);
+void router_logits_tc(const bf16* x, const float* w, int64_t T, int H, int E, float* logits, bf16* w3, float* out3,
+                      cudaStream_t stream);
+void router_dx_tc(const float* d_logits, const float* w, int64_t T, int E, int H, float* dx, bf16* dls, bf16* w3,
+                  cudaStream_t stream);
+int64_t router_dw_chunk(int64_t T, int H);
+void router_dw_tc(const float* d_logits, const bf16* x, int64_t T, int E, int H, float* dw, bool accumulate,
+                  bf16* dls, float* partial, cudaStream_t stream);
+void linear_wgrad_chunks(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int64_t T, int64_t N, int64_t K,
+                         int64_t chunk, float* partial, cudaStream_t stream);
 void router_dw(const float* d_logits, const bf16* x, int64_t T, int E, int H, float* dw, bool accumulate,
                float* workspace, cudaStream_t stream);
 int routing_status(bool clear);

@@ -698,6 +698,109 @@ void router_dw(const float* d_logits, const bf16* x, int64_t T, int E, int H, fl
                          router_dw_split(T), stream);
 }
 
+// ------------------------------------------------------------------------------------------------ router GEMMs on
+// the tensor cores. An fp32 operand is split into bf16 parts (a = hi + mid + lo to ~24 mantissa bits, or hi + lo to
+// ~16); a bf16 x bf16 product is exact in fp32, so the tcgen05 GEMM over the stacked parts reproduces the fp32 GEMM
+// up to summation order. The MoE input x is bf16 already and needs no split.
+namespace {
+
+__global__ void split_w_kernel(const float* __restrict__ w, int64_t n, bf16* __restrict__ out, int mode) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float a = w[i];
+    const bf16 hi = __float2bfloat16(a);
+    const float r = a - __bfloat162float(hi);
+    const bf16 mid = __float2bfloat16(r);
+    const bf16 lo = __float2bfloat16(r - __bfloat162float(mid));
+    out[i] = hi;
+    out[n + i] = mode == 0 ? mid : hi;   // mode 0: [hi; mid; lo]   mode 1: [hi; hi; mid] (two-term split twice)
+    out[2 * n + i] = mode == 0 ? lo : mid;
+  }
+}
+
+// d[T,E] -> out[T,3E] = [hi | lo | hi]
+__global__ void split_dl_kernel(const float* __restrict__ d, int64_t total, int E, bf16* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / E;
+    const int e = static_cast<int>(i % E);
+    const float a = d[i];
+    const bf16 hi = __float2bfloat16(a);
+    const bf16 lo = __float2bfloat16(a - __bfloat162float(hi));
+    bf16* row = out + t * 3 * E;
+    row[e] = hi;
+    row[E + e] = lo;
+    row[2 * E + e] = hi;
+  }
+}
+
+// logits[t,e] = part_hi + (part_mid + part_lo)
+__global__ void sum3_kernel(const float* __restrict__ in, int64_t total, int E, float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / E;
+    const int e = static_cast<int>(i % E);
+    const float* row = in + t * 3 * E;
+    out[i] = row[e] + (row[E + e] + row[2 * E + e]);
+  }
+}
+
+// dw[e,h] (+)= sum over chunks c in order of (partial[c][e][h] + partial[c][E+e][h])
+__global__ void dw_reduce_kernel(const float* __restrict__ partial, int chunks, int64_t eh, float* __restrict__ dw,
+                                 bool accumulate) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < eh;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc = 0.f;
+    for (int c = 0; c < chunks; ++c) acc += partial[c * 2 * eh + i] + partial[c * 2 * eh + eh + i];
+    dw[i] = accumulate ? dw[i] + acc : acc;
+  }
+}
+
+int elementwise_grid(int64_t n) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4096, (n + 255) / 256))); }
+
+}  // namespace
+
+bool router_tc_ok(int64_t T, int H, int E) { return T >= 256 && H % 64 == 0 && E % 8 == 0; }
+
+void router_logits_tc(const bf16* x, const float* w, int64_t T, int H, int E, float* logits, bf16* w3, float* out3,
+                      cudaStream_t stream) {
+  const int64_t n = static_cast<int64_t>(E) * H;
+  split_w_kernel<<<elementwise_grid(n), 256, 0, stream>>>(w, n, w3, 0);
+  linear_fwd(x, H, w3, H, T, 3 * E, H, nullptr, nullptr, 0, out3, 3 * E, true, stream);
+  sum3_kernel<<<elementwise_grid(T * E), 256, 0, stream>>>(out3, T * E, E, logits);
+  check_cuda(cudaGetLastError(), "router_logits_tc");
+}
+
+void router_dx_tc(const float* d_logits, const float* w, int64_t T, int E, int H, float* dx, bf16* dls, bf16* w3,
+                  cudaStream_t stream) {
+  const int64_t n = static_cast<int64_t>(E) * H;
+  split_dl_kernel<<<elementwise_grid(T * E), 256, 0, stream>>>(d_logits, T * E, E, dls);
+  split_w_kernel<<<elementwise_grid(n), 256, 0, stream>>>(w, n, w3, 1);
+  // dx = [dl_hi | dl_lo | dl_hi] . [W_hi; W_hi; W_lo]
+  linear_dgrad(dls, 3 * E, w3, H, T, 3 * E, H, dx, H, true, false, stream);
+  check_cuda(cudaGetLastError(), "router_dx_tc");
+}
+
+int64_t router_dw_chunk(int64_t T, int H) {
+  // enough chunks that chunks x (H / 256) output tiles cover the 148 SMs about once
+  const int64_t tiles = std::max<int64_t>(1, (H + 255) / 256);
+  const int64_t chunks = std::max<int64_t>(1, 148 / tiles);
+  const int64_t chunk = (T + chunks - 1) / chunks;
+  return std::max<int64_t>(64, (chunk + 63) / 64 * 64);
+}
+
+void router_dw_tc(const float* d_logits, const bf16* x, int64_t T, int E, int H, float* dw, bool accumulate,
+                  bf16* dls, float* partial, cudaStream_t stream) {
+  split_dl_kernel<<<elementwise_grid(T * E), 256, 0, stream>>>(d_logits, T * E, E, dls);
+  const int64_t chunk = router_dw_chunk(T, H);
+  const int chunks = static_cast<int>((T + chunk - 1) / chunk);
+  // partial[c] = [dl_hi | dl_lo]^T . x over the chunk's tokens: 2E x H
+  linear_wgrad_chunks(dls, 3 * E, x, H, T, 2 * E, H, chunk, partial, stream);
+  const int64_t eh = static_cast<int64_t>(E) * H;
+  dw_reduce_kernel<<<elementwise_grid(eh), 256, 0, stream>>>(partial, chunks, eh, dw, accumulate);
+  check_cuda(cudaGetLastError(), "router_dw_tc");
+}
+
 int routing_status(bool clear) { return read_status_word(clear); }
 
 }  // namespace qw

@@ -149,3 +149,28 @@ def test_linear_bias_grad_matches_fp32(M, N):
     b.grad = None
     linear(x, w, b).backward(dy)
     assert torch.equal(b.grad, first)  # deterministic
+
+
+@pytest.mark.parametrize("T,H,E", [(4133, 1024, 64), (300, 256, 8)])
+def test_router_gemms_on_tensor_cores_match_fp64(T, H, E):
+    """Router logits, dX and dW run on the tcgen05 GEMM over bf16 splits of the fp32 operands; against fp64."""
+    C = _ext()
+    torch.manual_seed(3)
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    w = torch.randn(E, H, device="cuda") * 0.02
+    dl = torch.randn(T, E, device="cuda") * 1e-3
+
+    def rel(out, ref):
+        return float((out.double() - ref).abs().max() / ref.abs().max())
+
+    logits = torch.empty(T, E, device="cuda")
+    C.router_logits(x, w, logits)
+    assert rel(logits, x.double() @ w.double().t()) < 5e-6  # three-term split: fp32-level
+    dx = torch.empty(T, H, device="cuda")
+    C.router_dx(dl, w, dx)
+    assert rel(dx, dl.double() @ w.double()) < 1e-4
+    dw = torch.full((E, H), 0.5, device="cuda")
+    ws = torch.empty(C.router_dw_split(T) * E * H, device="cuda")
+    C.router_dw(dl, x, dw, True, ws)
+    assert rel(dw - 0.5, dl.double().t() @ x.double()) < 1e-4
+    assert C.read_status(True) == 0
