@@ -1,0 +1,65 @@
+"""Causal attention kernel timing: forward and backward of ``ops.attention.attention_core`` on one GPU.
+
+    python bench_attention.py --batch 8 --seq 2048 --heads 16 --head-dim 64
+    QW_ATTN_BWD=mma python bench_attention.py ...      # the mma.sync backward instead of the tcgen05 one
+
+Prints one JSON line: median forward / backward milliseconds over ``--iters`` runs (CUDA events on the launching
+stream, after warm-up) and the corresponding TFLOP/s (causal forward = 2 GEMMs over half the S x S scores; backward
+counted as 2.5x the forward).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=2048)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--kv-heads", type=int, default=0, help="0 = same as --heads")
+    ap.add_argument("--head-dim", type=int, default=64)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args()
+
+    from quantaweave_b200.ops import ext
+    from quantaweave_b200.ops.attention import attention_core
+
+    B, S, h, d = args.batch, args.seq, args.heads, args.head_dim
+    hkv = args.kv_heads or h
+    torch.manual_seed(0)
+    qkv = (torch.randn(B * S, (h + 2 * hkv) * d, device="cuda") * 0.5).bfloat16().requires_grad_()
+    grad = torch.randn(B * S, h * d, device="cuda").bfloat16()
+    for _ in range(args.warmup):
+        attention_core(qkv, B, S, h, hkv, d, False, 1e4).backward(grad)
+    torch.cuda.synchronize()
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    fwd, bwd = [], []
+    for _ in range(args.iters):
+        events[0].record()
+        out = attention_core(qkv, B, S, h, hkv, d, False, 1e4)
+        events[1].record()
+        out.backward(grad)
+        events[2].record()
+        torch.cuda.synchronize()
+        fwd.append(events[0].elapsed_time(events[1]))
+        bwd.append(events[1].elapsed_time(events[2]))
+    fwd.sort()
+    bwd.sort()
+    f_ms, b_ms = fwd[len(fwd) // 2], bwd[len(bwd) // 2]
+    flops = 4.0 * B * h * S * S * d / 2
+    print(json.dumps({"backward_path": os.environ.get("QW_ATTN_BWD", "tcgen05"), "batch": B, "seq": S, "heads": h,
+                      "kv_heads": hkv, "head_dim": d, "fwd_ms": round(f_ms, 4), "bwd_ms": round(b_ms, 4),
+                      "fwd_tflops": round(flops / f_ms / 1e9, 1), "bwd_tflops": round(2.5 * flops / b_ms / 1e9, 1)}))
+    if ext().read_status(True) != 0:
+        raise SystemExit("a kernel reported a device-side error status")
+
+
+if __name__ == "__main__":
+    main()
