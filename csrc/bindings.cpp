@@ -48,6 +48,36 @@ void linear_dgrad(Tensor dy, Tensor w, Tensor dx, bool accumulate) {
                    dx.stride(0), fp32, accumulate, stream());
 }
 
+// tensor-parallel partial products into the owners' staging buffers (peer pointers: int64 device tensor [world])
+void linear_fwd_peer(Tensor x, Tensor w, Tensor peer_ptrs, int64_t peer_rows, int64_t slot) {
+  CHECK_CUDA(x); CHECK_ROWS(x); CHECK_DTYPE(x, torch::kBFloat16);
+  CHECK_ROWS(w); CHECK_DTYPE(w, torch::kBFloat16); CHECK_DTYPE(peer_ptrs, torch::kInt64);
+  TORCH_CHECK(w.size(1) == x.size(1) && x.size(0) % peer_rows == 0, "linear_fwd_peer shapes");
+  c10::cuda::CUDAGuard g(x.device());
+  qw::linear_fwd_peer(bptr(x), x.stride(0), bptr(w), w.stride(0), x.size(0), w.size(0), x.size(1),
+                      reinterpret_cast<void* const*>(peer_ptrs.data_ptr<int64_t>()), peer_rows, static_cast<int>(slot),
+                      stream());
+}
+
+void linear_dgrad_peer(Tensor dy, Tensor w, Tensor peer_ptrs, int64_t peer_rows, int64_t slot) {
+  CHECK_CUDA(dy); CHECK_ROWS(dy); CHECK_DTYPE(dy, torch::kBFloat16);
+  CHECK_ROWS(w); CHECK_DTYPE(w, torch::kBFloat16); CHECK_DTYPE(peer_ptrs, torch::kInt64);
+  TORCH_CHECK(w.size(0) == dy.size(1) && dy.size(0) % peer_rows == 0, "linear_dgrad_peer shapes");
+  c10::cuda::CUDAGuard g(dy.device());
+  qw::linear_dgrad_peer(bptr(dy), dy.stride(0), bptr(w), w.stride(0), dy.size(0), dy.size(1), w.size(1),
+                        reinterpret_cast<void* const*>(peer_ptrs.data_ptr<int64_t>()), peer_rows,
+                        static_cast<int>(slot), stream());
+}
+
+void tp_reduce_bcast(Tensor staging, int64_t world, int64_t rows_per_rank, int64_t N, OptT bias, Tensor out_ptrs,
+                     int64_t me) {
+  CHECK_CUDA(staging); CHECK_DTYPE(staging, torch::kBFloat16); CHECK_DTYPE(out_ptrs, torch::kInt64);
+  if (bias) { CHECK_DTYPE(*bias, torch::kFloat32); TORCH_CHECK(bias->numel() == N); }
+  c10::cuda::CUDAGuard g(staging.device());
+  qw::tp_reduce_bcast(bptr(staging), static_cast<int>(world), rows_per_rank, static_cast<int>(N), optptr<float>(bias),
+                      reinterpret_cast<void* const*>(out_ptrs.data_ptr<int64_t>()), static_cast<int>(me), stream());
+}
+
 void linear_wgrad(Tensor dy, Tensor x, Tensor dw, bool accumulate) {
   CHECK_CUDA(dy); CHECK_ROWS(dy); CHECK_DTYPE(dy, torch::kBFloat16);
   CHECK_ROWS(x); CHECK_DTYPE(x, torch::kBFloat16); CHECK_ROWS(dw);
@@ -549,6 +579,7 @@ int64_t read_status(bool clear) {
   if ((t = qw::attention_status(clear)) && !s) s = t;
   if ((t = qw::attention_tc_status(clear)) && !s) s = t;
   if ((t = qw::p2p_status(clear)) && !s) s = t;
+  if ((t = qw::tp_status(clear)) && !s) s = t;
   if ((t = qw::decode_status(clear)) && !s) s = t;
   return s;
 }
@@ -558,6 +589,9 @@ int64_t read_status(bool clear) {
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "QuantaWeave-B200 sm_100a kernels";
   m.def("linear_fwd", &linear_fwd);
+  m.def("linear_fwd_peer", &linear_fwd_peer);
+  m.def("linear_dgrad_peer", &linear_dgrad_peer);
+  m.def("tp_reduce_bcast", &tp_reduce_bcast);
   m.def("linear_dgrad", &linear_dgrad);
   m.def("linear_wgrad", &linear_wgrad);
   m.def("moe_gate_up_fwd", &moe_gate_up_fwd);

@@ -178,6 +178,41 @@ void linear_wgrad(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int6
   launch<BN, kGroupK, kEpiStore, true, true>(ma, mb, p, static_cast<int64_t>(p.m_tiles) * p.n_tiles, stream);
 }
 
+// Tensor-parallel partial products written straight into the owners' staging buffers (peer stores over NVLink):
+// row m of the [M, N] result goes to rank m / peer_rows, slot `peer_slot`. bf16, no bias (the reduction adds it).
+void linear_fwd_peer(const bf16* x, int64_t ldx, const bf16* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                     void* const* peer_out, int64_t peer_rows, int peer_slot, cudaStream_t stream) {
+  if (M == 0 || N == 0) return;
+  constexpr int BN = 256;
+  Params p = base_params();
+  p.M = M; p.N = N; p.K = K;
+  p.num_groups = 1;
+  p.n_tiles = static_cast<int>((N + BN - 1) / BN);
+  p.max_tiles = INT_MAX;
+  p.out = nullptr; p.ldo = N; p.out_fp32 = 0;
+  p.peer_out = peer_out; p.peer_rows = peer_rows; p.peer_slot = peer_slot;
+  auto ma = make_map(x, K, M, ldx, 64, kBM);
+  auto mb = make_map(w, K, N, ldw, 64, BN);
+  launch<BN, kGroupM, kEpiStore, false, false>(ma, mb, p, ((M + kBM - 1) / kBM) * p.n_tiles, stream);
+}
+
+// dx partial [M, K] = dy[M, N] @ w[N, K] into the owners' staging buffers (see linear_fwd_peer)
+void linear_dgrad_peer(const bf16* dy, int64_t lddy, const bf16* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                       void* const* peer_out, int64_t peer_rows, int peer_slot, cudaStream_t stream) {
+  if (M == 0 || K == 0) return;
+  constexpr int BN = 256;
+  Params p = base_params();
+  p.M = M; p.N = K; p.K = N;
+  p.num_groups = 1;
+  p.n_tiles = static_cast<int>((K + BN - 1) / BN);
+  p.max_tiles = INT_MAX;
+  p.out = nullptr; p.ldo = K; p.out_fp32 = 0;
+  p.peer_out = peer_out; p.peer_rows = peer_rows; p.peer_slot = peer_slot;
+  auto ma = make_map(dy, N, M, lddy, 64, kBM);
+  auto mb = make_map(w, K, N, ldw, 64, 64);
+  launch<BN, kGroupM, kEpiStore, false, true>(ma, mb, p, ((M + kBM - 1) / kBM) * p.n_tiles, stream);
+}
+
 // partial[c][N,K] = dy[rows of chunk c, N]^T @ x[rows of chunk c, K] for chunks of `chunk` rows (a multiple of 64):
 // split-K for weight gradients whose output is too small to fill the GPU (the caller reduces the partials)
 void linear_wgrad_chunks(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int64_t T, int64_t N, int64_t K,

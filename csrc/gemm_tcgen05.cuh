@@ -58,6 +58,11 @@ struct Params {
   void* out;
   long ldo;
   long out_group_stride;       // kGroupK: elements between group outputs
+  // fused tensor-parallel reduction (kGroupM, bf16): output row m belongs to rank m / peer_rows and is stored over
+  // NVLink into that rank's staging buffer peer_out[owner] at row peer_slot * peer_rows + m % peer_rows
+  void* const* peer_out;
+  long peer_rows;
+  int peer_slot;
   int out_fp32;
   int accumulate;
   float alpha;
@@ -162,6 +167,12 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const TileInfo& t
     const int n0 = t.n_tile * BN;
     char* base = static_cast<char*>(p.out);
     if (MODE == kGroupK) base += static_cast<long>(t.group) * p.out_group_stride * (p.out_fp32 ? 4 : 2);
+    long dst_row = out_row;
+    if (MODE == kGroupM && p.peer_out && row_write) {
+      const long owner = out_row / p.peer_rows;
+      base = static_cast<char*>(p.peer_out[owner]);
+      dst_row = static_cast<long>(p.peer_slot) * p.peer_rows + (out_row - owner * p.peer_rows);
+    }
 #pragma unroll 1
     for (int c = 0; c < BN; c += 32) {
       float v[32];
@@ -186,7 +197,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const TileInfo& t
           if (full || n0 + c + i < p.N) v[i] += __bfloat162float(r[i]);
       }
       if (p.out_fp32) {
-        float* o = reinterpret_cast<float*>(base) + out_row * p.ldo + n0 + c;
+        float* o = reinterpret_cast<float*>(base) + dst_row * p.ldo + n0 + c;
         if (full && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
@@ -202,7 +213,7 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const TileInfo& t
             if (n0 + c + i < p.N) o[i] = p.accumulate ? o[i] + v[i] : v[i];
         }
       } else {
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(base) + out_row * p.ldo + n0 + c;
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(base) + dst_row * p.ldo + n0 + c;
         if (full && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {

@@ -89,6 +89,15 @@ void router_dx_tc(const float* d_logits, const float* w, int64_t T, int E, int H
 int64_t router_dw_chunk(int64_t T, int H);
 void router_dw_tc(const float* d_logits, const bf16* x, int64_t T, int E, int H, float* dw, bool accumulate,
                   bf16* dls, float* partial, cudaStream_t stream);
+// fused tensor parallelism: GEMMs whose epilogue stores rows into peers' staging buffers, and the reduction that
+// sums the staged partials and stores the result into every rank's output buffer (tp_fused.cu)
+void linear_fwd_peer(const bf16* x, int64_t ldx, const bf16* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                     void* const* peer_out, int64_t peer_rows, int peer_slot, cudaStream_t stream);
+void linear_dgrad_peer(const bf16* dy, int64_t lddy, const bf16* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+                       void* const* peer_out, int64_t peer_rows, int peer_slot, cudaStream_t stream);
+void tp_reduce_bcast(const bf16* staging, int world, int64_t rows_per_rank, int N, const float* bias,
+                     void* const* outs, int me, cudaStream_t stream);
+int tp_status(bool clear);
 void linear_wgrad_chunks(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int64_t T, int64_t N, int64_t K,
                          int64_t chunk, float* partial, cudaStream_t stream);
 void router_dw(const float* d_logits, const bf16* x, int64_t T, int E, int H, float* dw, bool accumulate,

@@ -6,12 +6,17 @@ with a replicated bias) under ``nn.MultiheadAttention`` parameter names (:72-100
 q, k and v heads separately. Expert FFNs are column-parallel for gate/up and row-parallel for down.
 ``shard_state_dict`` / ``merge_state_dicts`` slice and merge full checkpoints (:110-149).
 
-On CUDA the attention runs on the native kernels (tcgen05 GEMMs + flash attention); the TP all-reduce is NCCL.
+On CUDA the attention runs on the native kernels (tcgen05 GEMMs + flash attention). Its two all-reduces are fused
+into the neighbouring GEMMs over NVLink peer memory (``FusedTPReducer``): the row-parallel output projection's GEMM
+stores each partial row straight into the owning rank's staging buffer and a reduction kernel sums the slots and
+stores the result into every rank's output buffer (forward); the column-parallel input projection does the same with
+its dgrad GEMM (backward). ``QW_TP_FUSED=0`` keeps NCCL all-reduces; the expert FFNs' all-reduce stays on NCCL.
 """
 
 from __future__ import annotations
 
 import math
+import os
 import re
 from typing import Optional
 
@@ -56,6 +61,141 @@ def reduce_from_tp(x: Tensor, group) -> Tensor:
     return x if group is None else _ReduceFromTP.apply(x, group)
 
 
+class FusedTPReducer:
+    """All-reduce fused with the producing GEMM over NVLink peer memory (one per (group, device)).
+
+    Buffers come from ``_Channel`` (two parities of symmetric memory, so back-to-back calls never overwrite a slot a
+    slower rank is still reading): ``[0, plane)`` is this rank's staging area ``[world][M/world][N]`` and
+    ``[plane, 2 plane)`` the reduced ``[M, N]`` output. Per call: GEMM with peer-store epilogue -> ready barrier ->
+    ``tp_reduce_bcast`` (fixed-order fp32 sum of the slots + bias, stored into every rank's output) -> done barrier ->
+    copy out. Creating one is collective over the group."""
+
+    _instances: dict = {}
+
+    def __init__(self, group, device: torch.device) -> None:
+        from .p2p import P2PTransport, _Channel
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.transport = P2PTransport.for_group(group, device)
+        self.ready = _Channel(self.transport)
+        self.done = _Channel(self.transport)
+
+    @classmethod
+    def for_group(cls, group, device: torch.device) -> "FusedTPReducer":
+        key = (id(group), device.index)
+        if key not in cls._instances:
+            cls._instances[key] = cls(group, device)
+        return cls._instances[key]
+
+    @staticmethod
+    def usable(x: Tensor, group, width: int) -> bool:
+        if group is None or not x.is_cuda or os.environ.get("QW_TP_FUSED", "1") == "0":
+            return False
+        world = dist.get_world_size(group)
+        return world > 1 and x.size(0) % world == 0 and width % 8 == 0
+
+    def gemm_all_reduce(self, a: Tensor, w: Tensor, bias: Optional[Tensor], transposed: bool) -> Tensor:
+        """``sum over ranks of (a @ w^T)`` (``a @ w`` when ``transposed``) ``+ bias`` as bf16 ``[M, N]``."""
+        from ..ops import ext
+
+        C = ext()
+        M = a.size(0)
+        N = w.size(1) if transposed else w.size(0)
+        rows = M // self.world
+        plane = M * N * 2
+        self.ready.grow(2 * plane)  # same size on every rank: M and N are replicated across the group
+        parity = self.ready.next()
+        buf, _, peers = self.ready.bufs[parity]
+        if transposed:
+            C.linear_dgrad_peer(a, w, peers, rows, self.rank)
+        else:
+            C.linear_fwd_peer(a, w, peers, rows, self.rank)
+        C.ep_signal(self.ready.peer_flags[parity], self.rank, self.ready.epoch)
+        self.ready.wait(parity)  # every rank's partial rows have landed in our staging slots
+        C.tp_reduce_bcast(buf[:plane].view(torch.bfloat16), self.world, rows, N, bias, peers + plane, self.rank)
+        done = self.done.next()
+        C.ep_signal(self.done.peer_flags[done], self.rank, self.done.epoch)
+        self.done.wait(done)  # every rank's reduced rows have landed in our output buffer
+        return buf[plane:2 * plane].view(torch.bfloat16).view(M, N).clone()
+
+
+def _bf16_rows(t: Tensor) -> Tensor:
+    t = t.reshape(-1, t.size(-1)).to(torch.bfloat16)
+    return t if t.stride(-1) == 1 and t.stride(0) % 8 == 0 else t.contiguous()
+
+
+def _local_weight_grads(ctx, g2: Tensor, x2: Tensor, w: Tensor):
+    from ..ops import ext
+
+    C = ext()
+    dw = db = None
+    if ctx.needs_input_grad[1]:
+        dw = torch.empty(w.size(0), w.size(1), device=g2.device, dtype=ctx.weight_dtype
+                         if ctx.weight_dtype in (torch.bfloat16, torch.float32) else torch.float32)
+        C.linear_wgrad(g2, x2, dw, False)
+    if ctx.bias_dtype is not None and ctx.needs_input_grad[2]:
+        db = torch.empty(g2.size(1), device=g2.device, dtype=torch.float32)
+        part = torch.empty(C.bias_grad_slabs(g2.size(0)), g2.size(1), device=g2.device, dtype=torch.float32)
+        C.bias_grad(g2, part, db, False)
+        db = db.to(ctx.bias_dtype)
+    return dw, db
+
+
+class _RowParallelAllReduce(torch.autograd.Function):
+    """``sum_r(x_r W_r^T) + b`` with the all-reduce fused into the GEMM; the backward is local (the conjugate of the
+    all-reduce is the identity)."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, reducer):
+        x2 = _bf16_rows(x)
+        w = weight.to(torch.bfloat16).contiguous()
+        out = reducer.gemm_all_reduce(x2, w, bias.float() if bias is not None else None, False)
+        ctx.save_for_backward(x2, w)
+        ctx.weight_dtype, ctx.bias_dtype = weight.dtype, (bias.dtype if bias is not None else None)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        from ..ops import ext
+
+        x2, w = ctx.saved_tensors
+        g2 = _bf16_rows(grad)
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty(x2.size(0), w.size(1), device=grad.device, dtype=torch.bfloat16)
+            ext().linear_dgrad(g2, w, dx, False)
+        dw, db = _local_weight_grads(ctx, g2, x2, w)
+        return dx, dw, db, None
+
+
+class _ColumnParallelInput(torch.autograd.Function):
+    """``x W_r^T + b_r`` for a replicated ``x``; the backward all-reduce of ``dx = sum_r dy_r W_r`` is fused into the
+    dgrad GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, reducer):
+        from ..ops import ext
+
+        x2 = _bf16_rows(x)
+        w = weight.to(torch.bfloat16).contiguous()
+        out = torch.empty(x2.size(0), w.size(0), device=x.device, dtype=torch.bfloat16)
+        ext().linear_fwd(x2, w, bias.float() if bias is not None else None, None, out)
+        ctx.save_for_backward(x2, w)
+        ctx.reducer = reducer
+        ctx.weight_dtype, ctx.bias_dtype = weight.dtype, (bias.dtype if bias is not None else None)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        x2, w = ctx.saved_tensors
+        g2 = _bf16_rows(grad)
+        dx = ctx.reducer.gemm_all_reduce(g2, w, None, True) if ctx.needs_input_grad[0] else None
+        dw, db = _local_weight_grads(ctx, g2, x2, w)
+        return dx, dw, db, None
+
+
 class _RowParallelOutput(nn.Module):
     """Output projection: weight ``[hidden, local_width]`` (row-parallel slice) and a replicated bias."""
 
@@ -93,6 +233,15 @@ class TensorParallelAttention(nn.Module):
 
     def forward(self, x: Tensor) -> Tensor:
         batch, seq, hidden = x.shape
+        if FusedTPReducer.usable(x.reshape(-1, hidden), self.tp_group, hidden):
+            from ..ops.attention import attention_core
+
+            reducer = FusedTPReducer.for_group(self.tp_group, x.device)
+            qkv = _ColumnParallelInput.apply(x.reshape(-1, hidden), self.in_proj_weight, self.in_proj_bias, reducer)
+            o = attention_core(qkv, batch, seq, self.heads, self.kv_heads, self.head_dim, self.rope,
+                               self.config.rope_theta)
+            out = _RowParallelAllReduce.apply(o, self.out_proj.weight, self.out_proj.bias, reducer)
+            return out.reshape(batch, seq, hidden)
         x = copy_to_tp(x, self.tp_group)
         if x.is_cuda:
             from ..ops.attention import attention_core
