@@ -29,7 +29,7 @@ os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "MoE train tokens/sec"
-BASELINE_VALUE = None  # BASELINE.md publishes no number for this config (published: {})
+BASELINE_VALUE = None  # the reference publishes no tokens/s figure for this config, so vs_baseline is null
 
 CONFIG2 = dict(vocab_size=32000, hidden_size=1024, layers=16, attention_heads=16, num_experts=64, ffn_size=2816,
                top_k=2, capacity_factor=1.25, router_aux_loss_coef=0.01)
