@@ -175,14 +175,60 @@ class QuantaWeaveMoEForCausalLM(nn.Module):
         logits = self.lm_head(normed)
         return F.cross_entropy(logits[:, :-1].reshape(-1, logits.size(-1)), labels[:, 1:].reshape(-1))
 
+    # ---- sequence parallelism (attention TP and expert EP over the same ranks) ------------------------------
+    def _sequence_parallel(self):
+        ep = self.expert_parallel
+        return ep if ep is not None and getattr(ep, "sequence_parallel", False) else None
+
+    def _shard_rows(self, hidden: Tensor, token_domains: Optional[Tensor], ctx):
+        """Keep this rank's contiguous share of the flattened ``batch x sequence`` rows (as a [1, rows, H] batch)."""
+        batch, seq, width = hidden.shape
+        total = batch * seq
+        if total % ctx.world_size:
+            raise ValueError(f"batch x sequence ({total}) must be divisible by the sequence-parallel size "
+                             f"{ctx.world_size}")
+        rows = total // ctx.world_size
+        start = ctx.rank * rows
+        for block in self.blocks:
+            block.attention.sp_shape = (batch, seq)
+        local = hidden.reshape(total, width)[start:start + rows].reshape(1, rows, width)
+        if token_domains is not None:
+            token_domains = token_domains[start:start + rows]
+        return local, token_domains, (start, rows)
+
+    def _sequence_parallel_loss(self, hidden: Tensor, labels: Tensor, ctx, span: tuple) -> Tensor:
+        """This rank's share of the batch-mean next-token CE, scaled so the mean over ranks is the batch mean:
+        ``world * (sum of CE over this rank's rows) / (valid positions in the whole batch)``."""
+        from ..ops import cross_entropy as ce_ops
+
+        start, rows = span
+        ignore = ce_ops.IGNORE_INDEX
+        shifted = torch.cat([labels[:, 1:], labels.new_full((labels.size(0), 1), ignore)], dim=1).reshape(-1)
+        local = shifted[start:start + rows]
+        total_valid = (shifted != ignore).sum().clamp(min=1)
+        normed = self.final_norm(hidden)
+        if normed.is_cuda:
+            mean = ce_ops.linear_cross_entropy(normed, self.lm_head.weight, local.view(1, rows))
+            ce_sum = mean * (local != ignore).sum()
+        else:
+            logits = self.lm_head(normed).reshape(rows, -1)
+            ce_sum = F.cross_entropy(logits.float(), local, ignore_index=ignore, reduction="sum")
+        return ce_sum * ctx.world_size / total_valid
+
     def forward(self, input_ids: Tensor, labels: Optional[Tensor] = None, domain_ids: Optional[Tensor] = None,
                 num_domains: int = 0, return_logits: bool = True) -> dict:
+        """With sequence parallelism every rank gets the same ``input_ids``; it keeps its share of the token rows
+        through the blocks, ``logits`` are this rank's rows (``[1, rows, vocab]``) and ``loss`` is this rank's
+        share scaled so that the mean over ranks is the batch loss."""
         if self.pipeline is not None and getattr(self.pipeline, "num_stages", 1) > 1:
             raise RuntimeError("a pipeline-stage model holds only some layers; drive it with PipelineEngine")
         hidden = self.embed(input_ids)
         token_domains = None
         if domain_ids is not None and self.domain_specialization_coef != 0 and num_domains > 1:
             token_domains = domain_ids.repeat_interleave(input_ids.size(1))
+        sp = self._sequence_parallel()
+        if sp is not None:
+            hidden, token_domains, span = self._shard_rows(hidden, token_domains, sp)
         hidden, balance, dropped, overflow, domain = self.run_blocks(hidden, token_domains, num_domains)
         result: dict = {
             "router_aux_loss": torch.stack(balance).mean(),
@@ -191,7 +237,11 @@ class QuantaWeaveMoEForCausalLM(nn.Module):
             "dropped_routes": torch.stack(dropped).sum(),
             "overflow_routes": torch.stack(overflow).sum(),
         }
-        if return_logits or labels is None or not hidden.is_cuda:
+        if sp is not None:
+            if return_logits or labels is None:
+                result["logits"] = self.head(hidden)
+            ce = self._sequence_parallel_loss(hidden, labels, sp, span) if labels is not None else None
+        elif return_logits or labels is None or not hidden.is_cuda:
             logits = self.head(hidden)
             result["logits"] = logits
             if labels is not None:

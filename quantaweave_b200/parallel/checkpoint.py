@@ -7,6 +7,10 @@ rank 0 adds ``config.json``, tokenizer files and ``metadata.json``; ``layout`` i
 (pipeline shards may also carry ``dp_rank``/``dp_size``). ``consolidate_checkpoint`` merges TP slices, renumbers
 experts globally and concatenates pipeline stages into an ordinary checkpoint with ``"optimizer": None``;
 ``reshard_checkpoint`` splits one checkpoint into ``ep x tp`` weights-only shards.
+
+Sequence-parallel shards (attention tensor-parallel and experts expert-parallel over the same ranks) carry
+``"sequence_parallel": true`` in their ``ep`` layout, with ``tp_rank == ep_rank == rank``: rank r holds attention
+slice r and experts ``[r * E/world, (r+1) * E/world)``, whole.
 """
 
 from __future__ import annotations
@@ -23,7 +27,7 @@ import torch
 
 from ..config import QuantaWeaveConfig
 from ..utils.checkpoint_io import load_checkpoint
-from .tensor_parallel import merge_state_dicts, shard_state_dict
+from .tensor_parallel import is_tp_sharded_shared, merge_state_dicts, merge_tensors, shard_state_dict
 
 EXPERT_KEY = re.compile(r"(experts\.)(\d+)(\.)")
 BLOCK_KEY = re.compile(r"^blocks\.(\d+)\.")
@@ -92,6 +96,40 @@ def _merge_expert_parallel(states: list) -> dict:
     return merged
 
 
+def _merge_sequence_parallel(shards: list, config: Optional[QuantaWeaveConfig]) -> dict:
+    """Attention slices merged over all ranks, experts renumbered by rank, replicated tensors from rank 0."""
+    shards = sorted(shards, key=lambda s: s["layout"]["ep_rank"])
+    qf = None
+    if config is not None and config.num_kv_heads != config.attention_heads:
+        qf = config.attention_heads / (config.attention_heads + 2 * config.num_kv_heads)
+    states = []
+    for shard in shards:
+        state = dict(shard["model"])
+        for key in list(state):
+            if is_tp_sharded_shared(key):
+                state[key] = merge_tensors(key, [s["model"][key] for s in shards], qf)
+        states.append((shard["layout"]["ep_rank"], state))
+    return _merge_expert_parallel(states)
+
+
+def _sequence_parallel_shard(state: dict, rank: int, world: int, config: QuantaWeaveConfig) -> dict:
+    """One rank's sequence-parallel shard of a full state: attention slice ``rank``, its experts whole."""
+    per = config.num_experts // world
+    attention = {k: v for k, v in state.items() if is_tp_sharded_shared(k)}
+    out = shard_state_dict(attention, rank, world, config)
+    for key, tensor in state.items():
+        if key in attention:
+            continue
+        match = EXPERT_KEY.search(key)
+        if match is None:
+            out[key] = tensor
+            continue
+        index = int(match.group(2))
+        if rank * per <= index < (rank + 1) * per:
+            out[EXPERT_KEY.sub(lambda m: f"{m.group(1)}{index - rank * per}{m.group(3)}", key, count=1)] = tensor
+    return out
+
+
 def _merge_pipeline(shards: list) -> dict:
     merged: dict = {}
     for shard in sorted(shards, key=lambda s: s["layout"]["stage"]):
@@ -129,6 +167,8 @@ def consolidate_checkpoint(shards_dir, output_dir) -> None:
         merged = _merge_pipeline(shards)
     elif kind == "dp":
         merged = shards[0]["model"]
+    elif shards[0]["layout"].get("sequence_parallel"):
+        merged = _merge_sequence_parallel(shards, _config(shards_dir))
     else:
         config = _config(shards_dir)
         by_ep: dict = {}
@@ -148,11 +188,33 @@ def consolidate_checkpoint(shards_dir, output_dir) -> None:
             shutil.copy(shards_dir / name, output_dir / name)
 
 
-def reshard_checkpoint(checkpoint_dir, output_dir, ep_size: int, tp_size: int = 1) -> dict:
-    """Split a single-file checkpoint into ``ep_size x tp_size`` weights-only shards (optimizer ``None``)."""
+def reshard_checkpoint(checkpoint_dir, output_dir, ep_size: int, tp_size: int = 1,
+                       sequence_parallel: bool = False) -> dict:
+    """Split a single-file checkpoint into ``ep_size x tp_size`` weights-only shards (optimizer ``None``); with
+    ``sequence_parallel`` into ``ep_size`` shards for the orthogonal mapping (``tp_size`` must equal ``ep_size``)."""
     checkpoint_dir, output_dir = Path(checkpoint_dir), Path(output_dir)
     cfg_dict = json.loads((checkpoint_dir / "config.json").read_text())
     config = QuantaWeaveConfig.from_dict(cfg_dict)
+    if sequence_parallel:
+        if tp_size not in (1, ep_size):
+            raise ValueError("sequence-parallel shards put attention TP and expert EP on the same ranks: "
+                             "tp_size must equal ep_size")
+        if config.num_experts % ep_size or config.attention_heads % ep_size or config.num_kv_heads % ep_size:
+            raise ValueError(f"experts and attention heads must be divisible by {ep_size}")
+        ckpt = load_checkpoint(checkpoint_dir / "model.pt", map_location="cpu")
+        output_dir.mkdir(parents=True, exist_ok=True)
+        for rank in range(ep_size):
+            torch.save({"model": _sequence_parallel_shard(ckpt["model"], rank, ep_size, config), "optimizer": None,
+                        "step": ckpt.get("step", 0), "rng_state": {}, "world_size": ep_size, "rank": rank,
+                        "layout": {"kind": "ep", "ep_rank": rank, "ep_size": ep_size, "tp_rank": rank,
+                                   "tp_size": ep_size, "sequence_parallel": True},
+                        "extra": ckpt.get("extra", {})}, shard_path(output_dir, rank))
+        for name in _COPIED:
+            if (checkpoint_dir / name).exists():
+                shutil.copy(checkpoint_dir / name, output_dir / name)
+        return {"ep_size": ep_size, "tp_size": ep_size, "world_size": ep_size, "sequence_parallel": True,
+                "per_rank_experts": config.num_experts // ep_size,
+                "shards": [str(shard_path(output_dir, r)) for r in range(ep_size)]}
     if config.num_experts % ep_size:
         raise ValueError(f"num_experts {config.num_experts} must be divisible by ep_size {ep_size}")
     if tp_size > 1:

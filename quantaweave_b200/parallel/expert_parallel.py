@@ -49,16 +49,23 @@ class ExpertParallelContext:
     global_rank: int = -1
     global_size: int = -1
     transport: str = "nccl"  # native dispatch: "nccl" (all_to_all), "p2p" (peer-store exchange) or "fused"
+    # orthogonal mapping: attention tensor-parallel and experts expert-parallel over the SAME ranks (tp == ep ==
+    # world). Activations between the attention blocks are sharded by token rows (sequence parallelism); the
+    # experts are not tensor-split.
+    sequence_parallel: bool = False
 
     def __post_init__(self) -> None:
         if self.global_size < 0:
-            self.global_size = self.world_size * self.tp_size
+            self.global_size = self.world_size if self.sequence_parallel else self.world_size * self.tp_size
         if self.global_rank < 0:
-            self.global_rank = self.rank * self.tp_size + self.tp_rank
+            self.global_rank = self.rank if self.sequence_parallel else self.rank * self.tp_size + self.tp_rank
 
     def layout(self) -> dict:
-        return {"kind": "ep", "ep_rank": self.rank, "ep_size": self.world_size, "tp_rank": self.tp_rank,
-                "tp_size": self.tp_size}
+        out = {"kind": "ep", "ep_rank": self.rank, "ep_size": self.world_size, "tp_rank": self.tp_rank,
+               "tp_size": self.tp_size}
+        if self.sequence_parallel:
+            out["sequence_parallel"] = True
+        return out
 
     @property
     def group_root(self) -> int:
@@ -66,12 +73,25 @@ class ExpertParallelContext:
 
 
 def init_expert_parallel(device_arg: str = "auto", tensor_parallel: int = 1,
-                         transport: Optional[str] = None) -> ExpertParallelContext:
-    """Join (or create) the process group from torchrun's environment and build the EP x TP grid."""
+                         transport: Optional[str] = None, sequence_parallel: bool = False) -> ExpertParallelContext:
+    """Join (or create) the process group from torchrun's environment and build the EP x TP grid.
+
+    ``sequence_parallel`` selects the orthogonal mapping instead of the grid: attention tensor-parallel over all
+    ranks and experts expert-parallel over the same ranks (``tensor_parallel`` must equal the world size)."""
     from .groups import ensure_process_group
 
     owns, device = ensure_process_group(device_arg)
     world, rank = dist.get_world_size(), dist.get_rank()
+    if sequence_parallel:
+        if tensor_parallel != world:
+            raise ValueError(f"sequence parallelism maps attention TP and expert EP onto the same ranks: "
+                             f"--tensor-parallel must equal the world size {world} (got {tensor_parallel})")
+        group = dist.new_group(list(range(world)))
+        transport = transport or os.environ.get("QW_EP_TRANSPORT", "auto")
+        if transport == "auto":
+            transport = "fused" if (device.type == "cuda" and world == 2) else "nccl"
+        return ExpertParallelContext(rank, world, device, group, owns, rank, world, group, rank, world, transport,
+                                     sequence_parallel=True)
     if tensor_parallel < 1 or world % tensor_parallel:
         raise ValueError(f"world size {world} is not divisible by --tensor-parallel {tensor_parallel}")
     ep_size = world // tensor_parallel
@@ -274,7 +294,9 @@ class ExpertParallelMoE(TopKMoE):
         if config.num_experts % context.world_size:
             raise ValueError(f"num_experts {config.num_experts} must be divisible by the expert-parallel size "
                              f"{context.world_size}")
-        super().__init__(config, num_local_experts=config.num_experts // context.world_size, tensor_parallel=context)
+        # with sequence parallelism the tensor-parallel ranks are the expert ranks: experts stay whole
+        super().__init__(config, num_local_experts=config.num_experts // context.world_size,
+                         tensor_parallel=None if context.sequence_parallel else context)
         self.context = context
         self.measure_load = False
         self.load_rows = 0
@@ -390,6 +412,8 @@ def broadcast_shared_parameters(model, ctx: ExpertParallelContext) -> None:
         if is_expert_parameter(name):
             continue
         if is_tp_sharded_shared(name) and ctx.tp_size > 1:
+            if ctx.sequence_parallel:
+                continue  # every rank holds a different slice
             if ctx.world_size > 1:
                 dist.broadcast(param.data, src=ctx.group_root, group=ctx.group)
         else:
@@ -407,8 +431,20 @@ def _shared_and_expert(model):
 
 def sync_gradients(model, ctx: ExpertParallelContext, sharded_optimizer=None, optimizer=None) -> None:
     """Average replicated gradients over the expert group (one flat all-reduce per dtype); scale expert gradients
-    by ``1/ep`` (folded into the fused optimizer when it is given, else applied in place)."""
+    by ``1/ep`` (folded into the fused optimizer when it is given, else applied in place).
+
+    With sequence parallelism every rank's loss covers its own token rows of one shared batch, so each rank's
+    autograd already sums every rank's contribution into its attention slices (through the row gathers/scatters)
+    and its experts (through the exchange): those are scaled by ``1/world`` like the experts, and only the
+    replicated tensors are averaged."""
+    from .tensor_parallel import is_tp_sharded_shared
+
     shared, experts = _shared_and_expert(model)
+    if ctx.sequence_parallel:
+        slices = [p for n, p in model.named_parameters() if is_tp_sharded_shared(n)]
+        ids = {id(p) for p in slices}
+        shared = [p for p in shared if id(p) not in ids]
+        experts = experts + slices
     if ctx.world_size > 1:
         if sharded_optimizer is not None:
             sharded_optimizer.reduce_gradients()

@@ -53,6 +53,55 @@ class _ReduceFromTP(torch.autograd.Function):
         return grad, None
 
 
+def _all_gather_rows(x: Tensor, group) -> Tensor:
+    world = dist.get_world_size(group)
+    x = x.contiguous()
+    out = x.new_empty((x.size(0) * world,) + tuple(x.shape[1:]))
+    if x.is_cuda:
+        dist.all_gather_into_tensor(out, x, group=group)
+    else:
+        dist.all_gather(list(out.chunk(world)), x, group=group)
+    return out
+
+
+def _reduce_scatter_rows(x: Tensor, group) -> Tensor:
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    x = x.contiguous()
+    if x.is_cuda:
+        out = x.new_empty((x.size(0) // world,) + tuple(x.shape[1:]))
+        dist.reduce_scatter_tensor(out, x, group=group)
+        return out
+    summed = x.clone()  # gloo has no reduce-scatter
+    dist.all_reduce(summed, group=group)
+    return summed.chunk(world)[rank].contiguous()
+
+
+class _GatherRows(torch.autograd.Function):
+    """Sequence parallelism: token rows sharded over the group -> all rows (backward: reduce-scatter)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return _all_gather_rows(x, group)
+
+    @staticmethod
+    def backward(ctx, grad):
+        return _reduce_scatter_rows(grad, ctx.group), None
+
+
+class _ScatterRows(torch.autograd.Function):
+    """Sequence parallelism: per-rank partial sums of all rows -> this rank's rows, summed (backward: all-gather)."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return _reduce_scatter_rows(x, group)
+
+    @staticmethod
+    def backward(ctx, grad):
+        return _all_gather_rows(grad, ctx.group), None
+
+
 def copy_to_tp(x: Tensor, group) -> Tensor:
     return x if group is None else _CopyToTP.apply(x, group)
 
@@ -215,6 +264,10 @@ class TensorParallelAttention(nn.Module):
             raise ValueError(f"attention heads {heads}/{kv} must be divisible by the tensor-parallel size {tp}")
         self.config = config
         self.tp_group = context.tp_group
+        # sequence parallelism: the input holds this rank's token rows; ``sp_shape`` = (batch, sequence) of the whole
+        # batch is set by the model before each forward
+        self.sequence_parallel = bool(getattr(context, "sequence_parallel", False))
+        self.sp_shape: Optional[tuple] = None
         self.heads = heads // tp
         self.kv_heads = kv // tp
         self.head_dim = config.head_dim
@@ -232,6 +285,8 @@ class TensorParallelAttention(nn.Module):
             nn.init.normal_(self.out_proj.weight, std=config.init_std)
 
     def forward(self, x: Tensor) -> Tensor:
+        if self.sequence_parallel:
+            return self._forward_sequence_parallel(x)
         batch, seq, hidden = x.shape
         if FusedTPReducer.usable(x.reshape(-1, hidden), self.tp_group, hidden):
             from ..ops.attention import attention_core
@@ -269,6 +324,47 @@ class TensorParallelAttention(nn.Module):
             partial = F.linear(o.transpose(1, 2).reshape(batch, seq, self.local_width), self.out_proj.weight)
         out = reduce_from_tp(partial, self.tp_group)
         return out + self.out_proj.bias.to(out.dtype) if self.out_proj.bias is not None else out
+
+    def _heads_partial(self, full: Tensor, batch: int, seq: int) -> Tensor:
+        """This rank's heads over all rows ``full`` [batch*seq, hidden] -> row-parallel partial output (no bias)."""
+        hidden = full.size(-1)
+        if full.is_cuda:
+            from ..ops.attention import attention_core
+            from ..ops.linear import linear
+
+            qkv = linear(full, self.in_proj_weight, self.in_proj_bias)
+            o = attention_core(qkv, batch, seq, self.heads, self.kv_heads, self.head_dim, self.rope,
+                               self.config.rope_theta)
+            return linear(o, self.out_proj.weight)
+        from ..models.layers import apply_rope_reference, rope_tables
+
+        qkv = F.linear(full.reshape(batch, seq, hidden), self.in_proj_weight, self.in_proj_bias)
+        qe, ke = self.heads * self.head_dim, (self.heads + self.kv_heads) * self.head_dim
+        q = qkv[..., :qe].reshape(batch, seq, self.heads, self.head_dim)
+        k = qkv[..., qe:ke].reshape(batch, seq, self.kv_heads, self.head_dim)
+        v = qkv[..., ke:].reshape(batch, seq, self.kv_heads, self.head_dim)
+        if self.rope:
+            cos, sin = rope_tables(torch.arange(seq, device=full.device), self.head_dim, self.config.rope_theta)
+            q, k = apply_rope_reference(q, cos, sin), apply_rope_reference(k, cos, sin)
+        if self.kv_heads != self.heads:
+            k = k.repeat_interleave(self.heads // self.kv_heads, dim=2)
+            v = v.repeat_interleave(self.heads // self.kv_heads, dim=2)
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True)
+        return F.linear(o.transpose(1, 2).reshape(batch * seq, self.local_width), self.out_proj.weight)
+
+    def _forward_sequence_parallel(self, x: Tensor) -> Tensor:
+        """``x``: this rank's token rows (any leading shape, ``rows x hidden``). All-gather the rows, run this rank's
+        heads over the whole batch, reduce-scatter the row-parallel output back to this rank's rows."""
+        if self.sp_shape is None:
+            raise RuntimeError("sequence-parallel attention needs the batch shape (set by the model's forward)")
+        batch, seq = self.sp_shape
+        shape, hidden = x.shape, x.size(-1)
+        full = _GatherRows.apply(x.reshape(-1, hidden), self.tp_group)
+        partial = self._heads_partial(full, batch, seq)
+        out = _ScatterRows.apply(partial, self.tp_group)
+        if self.out_proj.bias is not None:
+            out = out + self.out_proj.bias.to(out.dtype)
+        return out.reshape(shape)
 
 
 # ---- checkpoint slicing (reference key names) ---------------------------------------------------------

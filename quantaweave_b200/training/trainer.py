@@ -201,7 +201,7 @@ def resume_fields(args, config: QuantaWeaveConfig, dataset, tokenizer, world_siz
         curriculum=[args.curriculum, args.curriculum_steps, args.curriculum_start_fraction],
         domain_weights=[args.domain_weights, args.domain_weights_end, args.domain_weights_steps],
         parallel=[bool(args.expert_parallel), args.tensor_parallel, bool(args.pipeline_parallel), args.microbatches,
-                  bool(args.shard_optimizer), args.pipeline_schedule],
+                  bool(args.shard_optimizer), args.pipeline_schedule, bool(getattr(args, "sequence_parallel", False))],
         optimizer=[args.optimizer, args.adam_beta1, args.adam_beta2, args.weight_decay],
     )
     return fields
@@ -301,6 +301,9 @@ def build_parser() -> argparse.ArgumentParser:
     system.add_argument("--auto-batch-target", type=float, default=0.95)
     system.add_argument("--expert-parallel", action="store_true")
     system.add_argument("--tensor-parallel", type=int, default=1)
+    system.add_argument("--sequence-parallel", action="store_true",
+                        help="attention tensor-parallel and experts expert-parallel over the same ranks "
+                             "(--tensor-parallel = world size); token rows are sharded between the attention blocks")
     system.add_argument("--data-parallel", action="store_true", help="plain data parallelism (replicated experts)")
     system.add_argument("--pipeline-parallel", action="store_true")
     system.add_argument("--pipeline-data-parallel", type=int, default=1, help="data-parallel replicas of the pipeline")
@@ -467,6 +470,12 @@ def _validate(args) -> None:
             raise ValueError("--val-fraction needs a full forward pass and is not supported with --pipeline-parallel")
         if args.batch_size % args.microbatches:
             raise ValueError(f"--microbatches {args.microbatches} must divide --batch-size {args.batch_size}")
+    if getattr(args, "sequence_parallel", False):
+        if not args.expert_parallel or args.tensor_parallel < 2:
+            raise ValueError("--sequence-parallel needs --expert-parallel and --tensor-parallel equal to the world size")
+        if args.shard_optimizer:
+            raise ValueError("--shard-optimizer shards replicated tensors across the expert group, which holds "
+                             "different attention slices under --sequence-parallel")
     if args.shard_optimizer and args.optimizer != "adamw":
         raise ValueError(f"--optimizer {args.optimizer} is not combinable with --shard-optimizer")
     if args.curriculum != "none" and args.curriculum_steps <= 0:
@@ -499,7 +508,8 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
     if use_ep:
         from ..parallel.expert_parallel import init_expert_parallel
 
-        ep = init_expert_parallel(args.device, args.tensor_parallel)
+        ep = init_expert_parallel(args.device, args.tensor_parallel,
+                                  sequence_parallel=getattr(args, "sequence_parallel", False))
         device, rank, world_size = ep.device, ep.rank, ep.world_size
         is_main = ep.global_rank == 0
     elif args.pipeline_parallel:
@@ -552,6 +562,8 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
                      "sequence_length"):
             setattr(reproduce_args, name, getattr(args, name))
 
+    # ranks that read distinct batches; under sequence parallelism every rank reads the same one
+    data_rank, data_world = (0, 1) if (ep is not None and ep.sequence_parallel) else (rank, world_size)
     random.seed(args.seed)
     torch.manual_seed(args.seed)
     tokenizer, corpus, redactor = load_data(args, is_main)
@@ -560,7 +572,7 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
     val_dataset = None
     if corpus is None:
         dataset = SyntheticTokenStream(args.vocab_size, args.sequence_length, args.batch_size, args.seed,
-                                       args.synthetic_data, args.zipf_s, rank, world_size)
+                                       args.synthetic_data, args.zipf_s, data_rank, data_world)
         vocab_size = args.vocab_size
     else:
         dataset = WindowDataset(corpus, args.sequence_length)
@@ -615,9 +627,10 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
     if corpus is None:
         stream = dataset
     else:
-        stream = BatchStream(dataset, args.batch_size, args.seed, scores, curriculum, mixture, rank, world_size)
+        stream = BatchStream(dataset, args.batch_size, args.seed, scores, curriculum, mixture, data_rank, data_world)
     domains_active = stream.num_domains > 1
-    val_stream = BatchStream(val_dataset, args.batch_size, args.val_seed, rank=rank, world_size=world_size) if val_dataset else None
+    val_stream = (BatchStream(val_dataset, args.batch_size, args.val_seed, rank=data_rank, world_size=data_world)
+                  if val_dataset else None)
 
     betas = (args.adam_beta1, args.adam_beta2)
     if args.shard_optimizer:
@@ -779,7 +792,7 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
                 loss_value, overflow_fraction = dp.all_reduce_mean([loss_value, overflow_fraction])
         device_metrics = tracker.update(step) if tracker is not None else None
         controller.observe(loss_value, overflow_fraction)
-        pending_tokens += args.batch_size * args.sequence_length * world_size
+        pending_tokens += args.batch_size * args.sequence_length * data_world
         if tracker is not None and collect:
             util = tracker.gather_expert_utilization()
             if monitor is not None:

@@ -149,6 +149,65 @@ def test_tensor_parallel_gqa_attention_matches():
     run_ranks(_tp_case, 2)
 
 
+# ------------------------------------------------------------------------------------------ sequence parallel
+def _sp_case(rank, world):
+    from quantaweave_b200.parallel.expert_parallel import clip_grad_norm_parallel, init_expert_parallel, sync_gradients
+    from quantaweave_b200.parallel.tensor_parallel import is_tp_sharded_shared, shard_state_dict
+
+    # unlimited capacity and no aux loss: per-rank routing statistics would otherwise differ from the full batch's
+    cfg = tiny_config(attention_heads=4, kv_heads=2, capacity_factor=0.0, router_aux_loss_coef=0.0,
+                      attention_bias=True)
+    torch.manual_seed(0)
+    full = QuantaWeaveMoEForCausalLM(cfg)
+    ctx = init_expert_parallel("cpu", world, sequence_parallel=True)
+    model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ctx)
+    per = cfg.num_experts // world
+    state = {}
+    full_state = full.state_dict()
+    attention = {k: v for k, v in full_state.items() if is_tp_sharded_shared(k)}
+    state.update(shard_state_dict(attention, rank, world, cfg))
+    for key, value in full_state.items():
+        if key in attention:
+            continue
+        if ".experts." in key:
+            e = int(key.split(".experts.")[1].split(".")[0])
+            if rank * per <= e < (rank + 1) * per:
+                state[key.replace(f".experts.{e}.", f".experts.{e - rank * per}.")] = value
+        else:
+            state[key] = value
+    model.load_state_dict(state)
+    batch = torch.randint(0, 64, (2, 17), generator=torch.Generator().manual_seed(5))  # the same batch on every rank
+    out = model(batch, labels=batch, return_logits=False)
+    out["loss"].backward()
+    sync_gradients(model, ctx)
+    norm = float(clip_grad_norm_parallel(model, ctx, 1e9))
+    loss = out["loss"].detach().clone()
+    dist.all_reduce(loss)
+    ref = full(batch, labels=batch)
+    ref["loss"].backward()
+    assert abs(float(loss) / world - float(ref["loss"])) < 1e-5, (float(loss) / world, float(ref["loss"]))
+    ref_norm = torch.sqrt(sum(p.grad.double().pow(2).sum() for p in full.parameters())).item()
+    assert abs(norm - ref_norm) < 1e-4 * max(1.0, ref_norm), (norm, ref_norm)
+    ref_grads = {n: p.grad for n, p in full.named_parameters()}
+    qf = cfg.attention_heads / (cfg.attention_heads + 2 * cfg.num_kv_heads)
+    from quantaweave_b200.parallel.tensor_parallel import shard_tensor
+
+    for name, p in model.named_parameters():
+        expect = ref_grads[name]
+        if name.endswith(("w_gate_up", "w_down")):
+            expect = expect[rank * per:(rank + 1) * per]
+        elif is_tp_sharded_shared(name):
+            expect = shard_tensor(name, expect, rank, world, qf)
+        assert torch.allclose(p.grad, expect, atol=1e-5, rtol=1e-4), (name, (p.grad - expect).abs().max())
+    return float(loss)
+
+
+def test_sequence_parallel_attention_tp_and_experts_ep_on_the_same_ranks():
+    """Orthogonal mapping: attention tensor-parallel and experts expert-parallel over the same 2 ranks, token rows
+    sharded between the attention blocks; loss, clip norm and every gradient match the single-process model."""
+    run_ranks(_sp_case, 2)
+
+
 # ------------------------------------------------------------------------------------------ pipeline
 def _pp_case(rank, world, schedule, microbatches):
     from quantaweave_b200.parallel.pipeline_parallel import PipelineEngine, clip_grad_norm_pipeline, init_pipeline_parallel
@@ -253,7 +312,35 @@ def test_consolidate_and_reshard_roundtrip(tmp_path):
         assert torch.equal(merged[key], original[key]), key
 
 
-def _trainer_case(rank, world, tmp, steps):
+def test_sequence_parallel_reshard_roundtrip(tmp_path):
+    """Orthogonal-mapping shards: rank r gets attention slice r and experts [2r, 2r+2) whole; consolidating them
+    restores the original checkpoint exactly, and a shard loads into a sequence-parallel model's parameter shapes."""
+    from quantaweave_b200.parallel.checkpoint import consolidate_checkpoint, reshard_checkpoint
+
+    cfg = tiny_config(attention_heads=4, kv_heads=2, attention_bias=True)
+    torch.manual_seed(0)
+    model = QuantaWeaveMoEForCausalLM(cfg)
+    src = tmp_path / "full"
+    src.mkdir()
+    torch.save({"model": model.state_dict(), "optimizer": None, "step": 3, "extra": {}}, src / "model.pt")
+    cfg.save(src / "config.json")
+    info = reshard_checkpoint(src, tmp_path / "shards", ep_size=2, tp_size=2, sequence_parallel=True)
+    assert info["world_size"] == 2 and info["sequence_parallel"]
+    shard = torch.load(info["shards"][1], weights_only=False)
+    assert shard["layout"]["sequence_parallel"] and shard["layout"]["tp_rank"] == 1
+    assert shard["model"]["blocks.0.attention.out_proj.weight"].shape == (32, 16)
+    assert shard["model"]["blocks.0.moe.experts.1.down.weight"].shape == (32, 64)  # experts stay whole
+    assert torch.equal(shard["model"]["blocks.0.moe.experts.0.down.weight"],
+                       model.state_dict()["blocks.0.moe.experts.2.down.weight"])
+    consolidate_checkpoint(tmp_path / "shards", tmp_path / "merged")
+    merged = torch.load(tmp_path / "merged" / "model.pt", weights_only=False)["model"]
+    original = model.state_dict()
+    assert merged.keys() == original.keys()
+    for key in original:
+        assert torch.equal(merged[key], original[key]), key
+
+
+def _trainer_case(rank, world, tmp, steps, extra=None):
     from pathlib import Path
 
     from quantaweave_b200.training.trainer import default_args, run_training
@@ -263,13 +350,30 @@ def _trainer_case(rank, world, tmp, steps):
                   ffn_size=64, attention_heads=4, total_experts=4, active_experts=2, device="cpu",
                   no_power_tracking=True, expert_parallel=True, checkpoint_interval=2,
                   output=tmp / "out", checkpoint_dir=tmp / "ckpt", metrics_file=tmp / f"m{rank}.jsonl")
+    common.update(extra or {})
     summary = run_training(default_args(steps=steps, **common))
-    return summary["steps"]
+    return summary["steps"], summary.get("final_loss")
+
+
+def test_sequence_parallel_trainer_checkpoints_resumes_and_consolidates(tmp_path):
+    """``--sequence-parallel`` through ``run_training`` on 2 ranks: both ranks report the same loss, the shards carry
+    the orthogonal layout, a fresh launch resumes from them, and the consolidated checkpoint loads into a plain
+    single-process model."""
+    extra = {"tensor_parallel": 2, "sequence_parallel": True, "log_interval": 1}
+    first = run_ranks(_trainer_case, 2, (str(tmp_path), 2, extra))
+    assert first[0][1] is not None and abs(first[0][1] - first[1][1]) < 1e-6, first
+    results = run_ranks(_trainer_case, 2, (str(tmp_path), 4, extra))
+    assert results[0][0] == 4
+    shard = torch.load(tmp_path / "out" / "shards" / "model.rank1.pt", weights_only=False)
+    assert shard["layout"].get("sequence_parallel") and shard["layout"]["tp_rank"] == 1
+    merged = torch.load(tmp_path / "out" / "model.pt", weights_only=False)["model"]
+    cfg = QuantaWeaveConfig.load(tmp_path / "out" / "config.json")
+    QuantaWeaveMoEForCausalLM(cfg).load_state_dict(merged)
 
 
 def test_expert_parallel_trainer_checkpoints_and_resumes(tmp_path):
     run_ranks(_trainer_case, 2, (str(tmp_path), 2))
     results = run_ranks(_trainer_case, 2, (str(tmp_path), 4))  # a fresh launch resumes from the step-2 shards
-    assert results[0] == 4
+    assert results[0][0] == 4
     assert (tmp_path / "out" / "model.pt").exists()
     assert (tmp_path / "out" / "shards" / "model.rank1.pt").exists()
