@@ -103,3 +103,93 @@ def test_fused_tensor_parallel_attention_matches_nccl():
             raise AssertionError(f"rank {rank} failed:\n{payload}")
     for p in procs:
         p.join(timeout=60)
+
+
+def _sp_case(rank, world):
+    """Sequence parallelism on the native kernels: attention TP and experts EP over the same 2 GPUs."""
+    from quantaweave_b200 import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM
+    from quantaweave_b200.ops import ext
+    from quantaweave_b200.parallel.expert_parallel import clip_grad_norm_parallel, init_expert_parallel, sync_gradients
+    from quantaweave_b200.parallel.tensor_parallel import is_tp_sharded_shared, shard_state_dict, shard_tensor
+    from quantaweave_b200.training.native import prepare_model
+
+    torch.cuda.set_device(rank)
+    cfg = QuantaWeaveConfig(vocab_size=512, hidden_size=256, layers=2, ffn_size=256, num_experts=8, top_k=2,
+                            attention_heads=4, kv_heads=2, max_sequence_length=129, capacity_factor=0.0,
+                            router_aux_loss_coef=0.0, norm_type="rmsnorm", position_embedding="rope",
+                            attention_bias=False, init_std=0.02)
+    torch.manual_seed(0)
+    full = QuantaWeaveMoEForCausalLM(cfg).cuda()
+    prepare_model(full, "bf16")
+    ctx = init_expert_parallel("cuda", world, sequence_parallel=True)
+    model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ctx).cuda()
+    prepare_model(model, "bf16")
+    per = cfg.num_experts // world
+    full_state = full.state_dict()
+    attention = {k: v for k, v in full_state.items() if is_tp_sharded_shared(k)}
+    state = shard_state_dict(attention, rank, world, cfg)
+    for key, value in full_state.items():
+        if key in attention:
+            continue
+        if ".experts." in key:
+            e = int(key.split(".experts.")[1].split(".")[0])
+            if rank * per <= e < (rank + 1) * per:
+                state[key.replace(f".experts.{e}.", f".experts.{e - rank * per}.")] = value
+        else:
+            state[key] = value
+    model.load_state_dict(state)
+    batch = torch.randint(0, cfg.vocab_size, (2, 129), generator=torch.Generator().manual_seed(1)).cuda()
+    out = model(batch, labels=batch, return_logits=False)
+    out["loss"].backward()
+    sync_gradients(model, ctx)
+    norm = float(clip_grad_norm_parallel(model, ctx, 1e9))
+    loss = out["loss"].detach().float().clone()
+    dist.all_reduce(loss)
+    ref = full(batch, labels=batch, return_logits=False)
+    ref["loss"].backward()
+    ref_norm = float(torch.sqrt(sum(p.grad.double().pow(2).sum() for p in full.parameters())))
+    assert abs(float(loss) / world - float(ref["loss"])) < 2e-2, (float(loss) / world, float(ref["loss"]))
+    assert abs(norm - ref_norm) < 5e-2 * ref_norm, (norm, ref_norm)
+    qf = cfg.attention_heads / (cfg.attention_heads + 2 * cfg.num_kv_heads)
+    ref_grads = {n: p.grad.float() for n, p in full.named_parameters()}
+    for name, p in model.named_parameters():
+        expect = ref_grads[name]
+        if name.endswith(("w_gate_up", "w_down")):
+            expect = expect[rank * per:(rank + 1) * per]
+        elif is_tp_sharded_shared(name):
+            expect = shard_tensor(name, expect, rank, world, qf)
+        rel = float((p.grad.float() - expect).norm() / (expect.norm() + 1e-12))
+        assert rel < (0.1 if p.dim() >= 2 else 0.3), (name, rel)
+    assert ext().read_status(True) == 0
+    return float(loss)
+
+
+def _sp_worker(rank, world, port, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), QW_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0",
+                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
+    try:
+        queue.put((rank, "ok", _sp_case(rank, world)))
+    except Exception:  # noqa: BLE001
+        queue.put((rank, "error", traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_sequence_parallel_native_matches_single_gpu():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_sp_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for _ in range(world):
+        rank, status, payload = queue.get(timeout=600)
+        if status != "ok":
+            for p in procs:
+                p.join(timeout=30)
+            raise AssertionError(f"rank {rank} failed:\n{payload}")
+    for p in procs:
+        p.join(timeout=60)
