@@ -1,6 +1,9 @@
-"""Fused tensor-parallel attention on 2 B200s: the GEMM + all-reduce kernels over NVLink peer memory (forward
-row-parallel output projection, backward column-parallel input projection) against the NCCL all-reduce path, same
-shards, same inputs."""
+"""Tensor parallelism on 2 B200s.
+
+* Fused tensor-parallel attention: the GEMM + all-reduce kernels over NVLink peer memory (forward row-parallel output
+  projection, backward column-parallel input projection) against the NCCL all-reduce path, same shards, same inputs.
+* Sequence parallelism (attention TP and experts EP over the same GPUs) on the native kernels against the single-GPU
+  model."""
 
 import os
 import socket
