@@ -355,12 +355,14 @@ class FastDecoder:
 
     # ---- prefill -------------------------------------------------------------------------------------
     @torch.no_grad()
-    def _prefill(self, prompts: Tensor) -> None:
-        """Read ``prompts [B, n]`` in one pass (no expert capacity) and leave their keys/values in the cache."""
+    def _prefill(self, prompts: Tensor, first_row: int = 0) -> None:
+        """Read ``prompts [B, n]`` in one pass (no expert capacity) and leave their keys/values in cache rows
+        ``first_row .. first_row + B - 1`` (a continuous batcher fills one slot at a time)."""
         batch, n = prompts.shape
         self.length = n
         if n == 0:
             return
+        rows = slice(first_row, first_row + batch)
         model = self.model
         saved = [(moe.capacity_factor, moe.drop_overflow_tokens) for moe in model.moes()]
         for moe in model.moes():
@@ -372,8 +374,8 @@ class FastDecoder:
                 att = block.attention
                 normed = block.attention_norm(hidden)
                 q, k, v = att.qkv(normed) if not self.native else self._native_qkv(att, normed, batch, n)
-                layer.keys[:batch, :, :n] = k.transpose(1, 2).to(layer.keys.dtype)
-                layer.values[:batch, :, :n] = v.transpose(1, 2).to(layer.values.dtype)
+                layer.keys[rows, :, :n] = k.transpose(1, 2).to(layer.keys.dtype)
+                layer.values[rows, :, :n] = v.transpose(1, 2).to(layer.values.dtype)
                 if self.native:
                     o = self._native_attention(q, k, v, batch, n)
                     from ..ops.linear import linear

@@ -11,6 +11,11 @@ Parity with the reference ``src/serve_quantweave.py`` (routes ``/health``, ``/me
 ``ChatSession`` so a request behaves like the equivalent ``tools.chat -m`` call. The decoder's KV cache is per-request
 state, so requests are serialised behind an asyncio lock and generation runs in a worker thread.
 
+``--batching N`` serves ``/generate`` and ``/generate/stream`` through continuous batching
+(``inference.batching``): up to N requests decode together, joining and leaving between decode steps, with no lock
+around generation. Greedy output matches the serialised path. Seeded sampling is reproducible but draws differently
+(per-request multinomial sampling instead of the session's Gumbel noise). ``/chat`` keeps the serialised session.
+
 Hardening, all opt-in: ``--api-key`` (Bearer or X-API-Key on every route but /health), ``--rate-limit`` per caller per
 ``--rate-limit-window``, ``--max-queue`` (429 once that many wait), ``--request-timeout`` (503 when a request waits
 that long to START; a generation in progress is never cancelled), ``--moderation-blocklist`` (422 on a regex match;
@@ -170,7 +175,8 @@ class Server:
     def __init__(self, checkpoint, adapter, device: torch.device, precision: str, use_cache: bool = True, *,
                  api_key: Optional[str] = None, rate_limit: Optional[int] = None, rate_limit_window: float = 60.0,
                  request_timeout: Optional[float] = None, max_queue: Optional[int] = None,
-                 moderation_patterns: Optional[Path] = None, sessions: Optional[tuple] = None) -> None:
+                 moderation_patterns: Optional[Path] = None, sessions: Optional[tuple] = None,
+                 batching: int = 0) -> None:
         from ..utils.hardware import choose_precision, detect
 
         self.checkpoint, self.adapter, self.device = checkpoint, adapter, device
@@ -191,6 +197,87 @@ class Server:
         self.waiting = 0
         self.moderation = Moderation(moderation_patterns)
         self.metrics = Metrics()
+        self.worker = None
+        if batching > 0:
+            from ..inference.batching import BatchingWorker, ContinuousBatcher
+            from ..inference.fast_decode import FastDecoder
+
+            model = self.complete_session.model
+            self.batch_decoder = FastDecoder(model, device, self.precision, max_batch=batching)
+            self.worker = BatchingWorker(ContinuousBatcher(self.batch_decoder))
+
+    def close(self) -> None:
+        if self.worker is not None:
+            self.worker.close()
+
+    def _admit_batched(self) -> None:
+        from fastapi import HTTPException
+
+        batcher = self.worker.batcher
+        if self.max_queue is not None and batcher.pending() >= batcher.slots + self.max_queue:
+            raise HTTPException(429, f"too many requests already queued (max {self.max_queue})")
+
+    def _batched(self, request: GenerateRequest, on_text=None) -> dict:
+        """One completion through the continuous batcher: the same prompt handling, stop strings (with hold-back
+        when streaming), EOS and reply fields as ``ChatSession.send`` in complete mode."""
+        import random
+
+        from fastapi import HTTPException
+
+        from ..inference.batching import GenerationRequest
+
+        session, dec = self.complete_session, self.batch_decoder
+        tok = session.tokenizer
+        prompt = request.prompt
+        ids = tok.encode(prompt) or [tok.eos_id]
+        budget = max(1, min(request.tokens, dec.capacity - 1))
+        truncated = len(ids) + budget > dec.capacity
+        if truncated:
+            ids = ids[-(dec.capacity - budget):]
+        stops = [x for x in request.stop if x]
+        holdback = max((len(x) for x in stops), default=1) - 1
+        bias = torch.zeros(dec.vocab)
+        if session.valid_ids < dec.vocab:
+            bias[session.valid_ids:] = float("-inf")
+        if tok.unk_id is not None and 0 <= tok.unk_id < dec.vocab:
+            bias[tok.unk_id] = float("-inf")
+        state = {"generated": [], "text": "", "emitted": 0, "reason": "length"}
+        seed = request.seed if request.seed is not None else random.randrange(1 << 31)
+        job = GenerationRequest(ids, budget, request.temperature, request.top_k, request.top_p, seed,
+                                stop_ids=(tok.eos_id,), logit_bias=bias)
+
+        def on_token(token: int) -> None:
+            if token == tok.eos_id:
+                state["reason"] = "eos"
+                return
+            state["generated"].append(token)
+            text = tok.decode(state["generated"])
+            hits = [text.find(x) for x in stops if x in text]
+            if hits:
+                state["text"], state["reason"] = text[: min(hits)], "stop"
+                job.cancelled = True
+                return
+            state["text"] = text
+            if on_text is not None:
+                safe = max(state["emitted"], len(text) - holdback)
+                if safe > state["emitted"]:
+                    on_text(text[state["emitted"]:safe])
+                    state["emitted"] = safe
+
+        job.on_token = on_token
+        started = time.perf_counter()
+        self.worker.submit(job)
+        job.wait()
+        if job.finish_reason and job.finish_reason.startswith("error"):
+            raise HTTPException(500, job.finish_reason)
+        text = state["text"]
+        if on_text is not None and len(text) > state["emitted"]:
+            on_text(text[state["emitted"]:])
+        seconds = time.perf_counter() - started
+        count = len(state["generated"])
+        return {"text": text, "tokens": count, "seconds": seconds,
+                "tokens_per_second": count / seconds if seconds > 0 else 0.0, "stop_reason": state["reason"],
+                "unknown_characters": session.unknown_characters(prompt), "truncated_context": truncated}
 
     def info(self) -> dict:
         s = self.complete_session
@@ -238,6 +325,12 @@ class Server:
 
     async def generate(self, request: GenerateRequest) -> dict:
         self._check(request.prompt, "prompt")
+        if self.worker is not None:
+            self._admit_batched()
+            payload = await asyncio.to_thread(self._batched, request)
+            self.requests_served += 1
+            self.metrics.tokens_generated_total += payload["tokens"]
+            return payload
         await self._acquire()
         try:
             self.complete_session.settings = self._complete_settings(request)
@@ -276,6 +369,27 @@ class Server:
     async def stream_generate(self, request: GenerateRequest):
         """Server-sent events: ``data: {"text": ...}`` per piece, then ``event: done`` with the full reply."""
         self._check(request.prompt, "prompt")
+        if self.worker is not None:
+            self._admit_batched()
+            queue: asyncio.Queue = asyncio.Queue()
+            loop = asyncio.get_running_loop()
+            task = asyncio.ensure_future(asyncio.to_thread(
+                self._batched, request, lambda piece: loop.call_soon_threadsafe(queue.put_nowait, piece)))
+            try:
+                while not (task.done() and queue.empty()):
+                    try:
+                        item = await asyncio.wait_for(queue.get(), timeout=0.05)
+                    except asyncio.TimeoutError:
+                        continue
+                    yield f"data: {json.dumps({'text': item})}\n\n"
+                payload = await task
+            finally:
+                if not task.done():
+                    task.cancel()
+            self.requests_served += 1
+            self.metrics.tokens_generated_total += payload["tokens"]
+            yield f"event: done\ndata: {json.dumps(payload)}\n\n"
+            return
         await self._acquire()
         try:
             self.complete_session.settings = self._complete_settings(request)
@@ -388,6 +502,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
     p.add_argument("--host", default="127.0.0.1")
     p.add_argument("--port", type=int, default=8000)
+    p.add_argument("--batching", type=int, default=0, metavar="N",
+                   help="continuous batching of /generate and /generate/stream over N decoder slots (0 = one "
+                        "request at a time)")
     h = p.add_argument_group("hardening")
     h.add_argument("--api-key", help="require this key (Authorization: Bearer or X-API-Key) on every route but /health")
     h.add_argument("--rate-limit", type=int, help="429 past this many requests per --rate-limit-window per caller")
@@ -409,7 +526,7 @@ def main(argv=None) -> None:
     server = Server(checkpoint, adapter, device, args.precision, use_cache=not args.no_cache, api_key=args.api_key,
                     rate_limit=args.rate_limit, rate_limit_window=args.rate_limit_window,
                     request_timeout=args.request_timeout, max_queue=args.max_queue,
-                    moderation_patterns=args.moderation_blocklist)
+                    moderation_patterns=args.moderation_blocklist, batching=args.batching)
     print(f"model: {checkpoint}" + (f" + adapter {adapter}" if adapter else "")
           + f"  device: {device}  decoding: {server.complete_session.cache_note}")
     if server.api_key is None:

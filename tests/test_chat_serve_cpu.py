@@ -117,3 +117,43 @@ def test_http_server_routes(trained, tmp_path):
     assert 'quantweave_requests_total{route="/generate",status="200"} 1' in metrics
     codes = [client.post("/generate", json={"prompt": "t", "tokens": 1}, headers=auth).status_code for _ in range(4)]
     assert 429 in codes
+
+
+def test_http_server_continuous_batching(trained):
+    """``batching=4``: concurrent /generate requests share decode steps; greedy replies equal the serialised
+    server's, stop strings cut the text, and streaming delivers the same text."""
+    import asyncio
+
+    from fastapi.testclient import TestClient
+
+    from quantaweave_b200.tools.serve import GenerateRequest, Server, build_app
+
+    serial = Server(trained, None, torch.device("cpu"), "fp32")
+    batched = Server(trained, None, torch.device("cpu"), "fp32", batching=4)
+    try:
+        prompts = ["the cat", "a", "the dog sat", "once", "the"]
+        requests = [GenerateRequest(prompt=p, tokens=6 + i, temperature=0) for i, p in enumerate(prompts)]
+
+        async def together():
+            return await asyncio.gather(*(batched.generate(r) for r in requests))
+
+        replies = asyncio.run(together())
+        for r, got in zip(requests, replies):
+            want = asyncio.run(serial.generate(r))
+            assert got["text"] == want["text"] and got["tokens"] == want["tokens"], (r.prompt, got, want)
+            assert got["stop_reason"] == want["stop_reason"]
+        full = replies[0]["text"]
+        if len(full) > 2:
+            cut = asyncio.run(batched.generate(GenerateRequest(prompt="the cat", tokens=6, temperature=0,
+                                                               stop=[full[1:3]])))
+            assert cut["stop_reason"] == "stop" and cut["text"] == full[:1]
+        client = TestClient(build_app(batched))
+        with client.stream("POST", "/generate/stream", json={"prompt": "the cat", "tokens": 6, "temperature": 0}) as resp:
+            body = "".join(resp.iter_text())
+        events = [block.splitlines() for block in body.split("\n\n") if block.strip()]
+        pieces = [json.loads(lines[0][len("data: "):])["text"] for lines in events if lines[0].startswith("data: ")]
+        done = [json.loads(lines[1][len("data: "):]) for lines in events if lines[0] == "event: done"]
+        assert len(done) == 1 and done[0]["text"] == full
+        assert "".join(pieces) == full
+    finally:
+        batched.close()
