@@ -195,6 +195,9 @@ def run_native(args, rank, world, local):
     tokens_per_step = args.seqs_per_gpu * args.seq_len * world
     value = tokens_per_step / (ms_per_step / 1000.0)
     final_loss = float(loss.item())
+    from quantaweave_b200.ops.status import check_device_status
+
+    check_device_status()  # a kernel that gave up on a bounded wait invalidates the measurement
     with torch.no_grad():
         probe = model(dev_batches[-1], labels=dev_batches[-1], return_logits=False)
         routes = args.seqs_per_gpu * (args.seq_len + 1) * cfg.top_k * args.layers

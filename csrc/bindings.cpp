@@ -254,7 +254,7 @@ void moe_permute(Tensor x, int64_t k, Tensor route_row, Tensor top_w, Tensor kep
   qw::moe_permute(bptr(x), route_row.numel(), static_cast<int>(k), static_cast<int>(x.size(1)),
                   route_row.data_ptr<int>(), top_w.data_ptr<float>(), kept.data_ptr<int>(), offsets.data_ptr<int>(),
                   static_cast<int>(kept.numel()), bptr_mut(x_perm), row_token.data_ptr<int>(), row_w.data_ptr<float>(),
-                  stream());
+                  x_perm.size(0), stream());
 }
 
 void moe_pad_zero(Tensor kept, Tensor offsets, Tensor buf) {
@@ -275,14 +275,14 @@ void moe_combine(Tensor y, Tensor route_row, Tensor top_w, OptT resid, int64_t k
   CHECK_CUDA(y); CHECK_CONTIG(y); CHECK_CONTIG(out);
   c10::cuda::CUDAGuard g(y.device());
   qw::moe_combine(bptr(y), route_row.data_ptr<int>(), top_w.data_ptr<float>(), optb(resid), out.size(0),
-                  static_cast<int>(k), static_cast<int>(out.size(1)), bptr_mut(out), stream());
+                  static_cast<int>(k), static_cast<int>(out.size(1)), bptr_mut(out), y.size(0), stream());
 }
 
 void moe_combine_grad(Tensor dx_perm, Tensor route_row, OptT extra, int64_t k, Tensor dx) {
   CHECK_CUDA(dx_perm); CHECK_CONTIG(dx_perm); CHECK_CONTIG(dx);
   c10::cuda::CUDAGuard g(dx.device());
   qw::moe_combine_grad(bptr(dx_perm), route_row.data_ptr<int>(), optptr<float>(extra), dx.size(0), static_cast<int>(k),
-                       static_cast<int>(dx.size(1)), bptr_mut(dx), stream());
+                       static_cast<int>(dx.size(1)), bptr_mut(dx), dx_perm.size(0), stream());
 }
 
 void moe_route_dw(Tensor partial, Tensor route_row, Tensor d_w) {

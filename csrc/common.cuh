@@ -50,6 +50,23 @@ static inline int read_status_word(bool clear) {
   return value;
 }
 
+// Debug bounds checks: in a QW_DEBUG_BOUNDS=1 build an index outside [0, n) records kBoundsError and the caller skips
+// the access; otherwise the check compiles away.
+#ifndef QW_DEBUG_BOUNDS
+#define QW_DEBUG_BOUNDS 0
+#endif
+__device__ __forceinline__ bool in_bounds(int64_t i, int64_t n) {
+#if QW_DEBUG_BOUNDS
+  if (i < 0 || i >= n) {
+    set_status(kBoundsError);
+    return false;
+  }
+#endif
+  (void)i;
+  (void)n;
+  return true;
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const DispatchArgs a) 
     const int row = a.route_row[r];
     if (row < 0) continue;
     const int e = row / a.slot, pos = row % a.slot;
+    if (!in_bounds(e, a.E)) continue;  // QW_DEBUG_BOUNDS: a route past the last expert would write outside a peer
     const int d = e / a.local, le = e % a.local;
     const int64_t rrow = static_cast<int64_t>(a.me * a.local + le) * a.slot + pos;
     const uint4* src = reinterpret_cast<const uint4*>(a.x + (r / a.k) * a.H);

@@ -64,14 +64,15 @@ void moe_plan(const int* top_idx, const float* top_w, const int* counts, int64_t
               int* kept, int* offsets, int* uoffsets, int* meta, int* chunk_hist, int* sorted_routes, int* route_row,
               cudaStream_t stream);
 void moe_permute(const bf16* x, int64_t routes, int k, int H, const int* route_row, const float* top_w, const int* kept,
-                 const int* offsets, int E, bf16* x_perm, int* row_token, float* row_w, cudaStream_t stream);
+                 const int* offsets, int E, bf16* x_perm, int* row_token, float* row_w, int64_t perm_rows,
+                 cudaStream_t stream);
 void moe_pad_zero(const int* kept, const int* offsets, int E, int H, bf16* buf, cudaStream_t stream);
 void moe_gather_rows(const bf16* src, const int* row_token, const int* meta, int64_t max_rows, int H, bf16* dst,
                      cudaStream_t stream);
 void moe_combine(const bf16* y, const int* route_row, const float* top_w, const bf16* resid, int64_t T, int k, int H,
-                 bf16* out, cudaStream_t stream);
+                 bf16* out, int64_t y_rows, cudaStream_t stream);
 void moe_combine_grad(const bf16* dx_perm, const int* route_row, const float* extra, int64_t T, int k, int H, bf16* dx,
-                      cudaStream_t stream);
+                      int64_t perm_rows, cudaStream_t stream);
 void moe_route_dw(const float* partial, int tiles, const int* route_row, int64_t routes, float* d_w,
                   cudaStream_t stream);
 void router_backward(const float* probs, const int* top_idx, const float* top_w, const float* d_w,

@@ -362,13 +362,14 @@ __global__ void __launch_bounds__(1024) select_kernel(const int* __restrict__ co
 // one warp per route; x_perm[row] = x[token]
 __global__ void permute_kernel(const bf16* __restrict__ x, int64_t routes, int k, int H,
                                const int* __restrict__ route_row, const float* __restrict__ top_w,
-                               bf16* __restrict__ x_perm, int* __restrict__ row_token, float* __restrict__ row_w) {
+                               bf16* __restrict__ x_perm, int* __restrict__ row_token, float* __restrict__ row_w,
+                               int64_t perm_rows) {
   const int warps = blockDim.x / 32;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * warps + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (r >= routes) return;
   const int row = route_row[r];
-  if (row < 0) return;
+  if (row < 0 || !in_bounds(row, perm_rows)) return;
   const int64_t t = r / k;
   if (lane == 0) {
     row_token[row] = static_cast<int>(t);
@@ -420,7 +421,7 @@ __global__ void gather_rows_kernel(const bf16* __restrict__ src, const int* __re
 // out[t] = resid[t] + sum_j w_j * y[row(t,j)] ; one warp per token, 8 columns per lane step
 __global__ void combine_kernel(const bf16* __restrict__ y, const int* __restrict__ route_row,
                                const float* __restrict__ top_w, const bf16* __restrict__ resid, int64_t T, int k, int H,
-                               bf16* __restrict__ out) {
+                               bf16* __restrict__ out, int64_t y_rows) {
   const int warps = blockDim.x / 32;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * warps + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -434,7 +435,7 @@ __global__ void combine_kernel(const bf16* __restrict__ y, const int* __restrict
   for (int c = lane * 8; c < H; c += 256) {
     float acc[8] = {};
     for (int j = 0; j < k; ++j) {
-      if (rows[j] < 0) continue;
+      if (rows[j] < 0 || !in_bounds(rows[j], y_rows)) continue;
       uint4 raw = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(rows[j]) * H + c);
       const bf16* v = reinterpret_cast<const bf16*>(&raw);
 #pragma unroll
@@ -455,7 +456,8 @@ __global__ void combine_kernel(const bf16* __restrict__ y, const int* __restrict
 
 // dx[t] = extra[t] (fp32, optional) + sum_j dx_perm[row(t,j)]   (unweighted: the route weight was applied upstream)
 __global__ void combine_grad_kernel(const bf16* __restrict__ dx_perm, const int* __restrict__ route_row,
-                                    const float* __restrict__ extra, int64_t T, int k, int H, bf16* __restrict__ dx) {
+                                    const float* __restrict__ extra, int64_t T, int k, int H, bf16* __restrict__ dx,
+                                    int64_t perm_rows) {
   const int warps = blockDim.x / 32;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * warps + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -469,7 +471,7 @@ __global__ void combine_grad_kernel(const bf16* __restrict__ dx_perm, const int*
       for (int i = 0; i < 8; ++i) acc[i] = extra[t * H + c + i];
     }
     for (int j = 0; j < k; ++j) {
-      if (rows[j] < 0) continue;
+      if (rows[j] < 0 || !in_bounds(rows[j], perm_rows)) continue;
       uint4 raw = *reinterpret_cast<const uint4*>(dx_perm + static_cast<int64_t>(rows[j]) * H + c);
       const bf16* v = reinterpret_cast<const bf16*>(&raw);
 #pragma unroll
@@ -616,12 +618,13 @@ void moe_plan(const int* top_idx, const float* top_w, const int* counts, int64_t
 }
 
 void moe_permute(const bf16* x, int64_t routes, int k, int H, const int* route_row, const float* top_w, const int* kept,
-                 const int* offsets, int E, bf16* x_perm, int* row_token, float* row_w, cudaStream_t stream) {
+                 const int* offsets, int E, bf16* x_perm, int* row_token, float* row_w, int64_t perm_rows,
+                 cudaStream_t stream) {
   if (H % 8) throw std::runtime_error("moe_permute: hidden size must be a multiple of 8");
   if (routes > 0) {
     const int warps = 8;
     permute_kernel<<<static_cast<int>((routes + warps - 1) / warps), warps * 32, 0, stream>>>(
-        x, routes, k, H, route_row, top_w, x_perm, row_token, row_w);
+        x, routes, k, H, route_row, top_w, x_perm, row_token, row_w, perm_rows);
   }
   pad_rows_kernel<<<E, dim3(32, 8), 0, stream>>>(kept, offsets, H, x_perm, row_token, row_w);
   check_cuda(cudaGetLastError(), "moe_permute");
@@ -642,20 +645,22 @@ void moe_gather_rows(const bf16* src, const int* row_token, const int* meta, int
 }
 
 void moe_combine(const bf16* y, const int* route_row, const float* top_w, const bf16* resid, int64_t T, int k, int H,
-                 bf16* out, cudaStream_t stream) {
+                 bf16* out, int64_t y_rows, cudaStream_t stream) {
   if (T == 0) return;
+  if (k > 8) throw std::runtime_error("moe_combine: top_k must be <= 8");
   const int warps = 8;
   combine_kernel<<<static_cast<int>((T + warps - 1) / warps), warps * 32, 0, stream>>>(y, route_row, top_w, resid, T, k,
-                                                                                       H, out);
+                                                                                       H, out, y_rows);
   check_cuda(cudaGetLastError(), "moe_combine");
 }
 
 void moe_combine_grad(const bf16* dx_perm, const int* route_row, const float* extra, int64_t T, int k, int H, bf16* dx,
-                      cudaStream_t stream) {
+                      int64_t perm_rows, cudaStream_t stream) {
   if (T == 0) return;
+  if (k > 8) throw std::runtime_error("moe_combine_grad: top_k must be <= 8");
   const int warps = 8;
   combine_grad_kernel<<<static_cast<int>((T + warps - 1) / warps), warps * 32, 0, stream>>>(dx_perm, route_row, extra,
-                                                                                            T, k, H, dx);
+                                                                                            T, k, H, dx, perm_rows);
   check_cuda(cudaGetLastError(), "moe_combine_grad");
 }
 

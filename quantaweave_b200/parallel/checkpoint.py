@@ -65,9 +65,27 @@ def save_sharded_checkpoint(directory, model, optimizer, step: int, tokenizer, c
 
 
 def load_sharded_checkpoint(directory, model, optimizer, ctx, extra_out: Optional[dict] = None) -> int:
+    """Every rank reads its own shard; the ranks agree on success first (one small all-reduce), so a missing or
+    unreadable shard makes EVERY rank raise the same error instead of leaving the others waiting in a collective."""
+    import torch.distributed as dist
+
     from ..training.trainer import restore_rng
 
-    ckpt = load_checkpoint(shard_path(directory, ctx.global_rank), map_location=ctx.device)
+    path = shard_path(directory, ctx.global_rank)
+    ckpt, problem = None, None
+    try:
+        ckpt = load_checkpoint(path, map_location=ctx.device)
+    except Exception as exc:  # noqa: BLE001 - reported collectively below
+        problem = f"{path}: {type(exc).__name__}: {exc}"
+    if dist.is_initialized() and ctx.global_size > 1:
+        ok = torch.tensor([0 if problem else 1], dtype=torch.int32,
+                          device=ctx.device if ctx.device.type == "cuda" else "cpu")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        if not int(ok.item()) and problem is None:
+            problem = "another rank could not read its shard"
+    if problem is not None:
+        raise RuntimeError(f"cannot resume from the sharded checkpoint in {directory} (rank {ctx.global_rank}): "
+                           f"{problem}")
     if ckpt["world_size"] != ctx.global_size or ckpt.get("layout", ctx.layout()) != ctx.layout():
         raise ValueError(f"checkpoint was written with layout {ckpt.get('layout')} on {ckpt['world_size']} ranks but "
                          f"this run is {ctx.layout()} on {ctx.global_size}")

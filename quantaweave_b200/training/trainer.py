@@ -813,6 +813,10 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
             best_val = val_loss if best_val is None else min(best_val, val_loss)
             say(f"step={step}/{args.steps} val_loss={val_loss:.4f}")
         if step % args.log_interval == 0 or step == args.steps:
+            if device.type == "cuda":
+                from ..ops.status import check_device_status
+
+                check_device_status()  # raises CommTimeoutError / DeviceStatusError if a kernel gave up on a wait
             extra_fields = {}
             if device_metrics:
                 extra_fields.update(time_imbalance=device_metrics["time_imbalance"],

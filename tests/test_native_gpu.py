@@ -269,3 +269,26 @@ def test_adamw_8bit_tracks_fp32_adamw():
     opt_b.load_state_dict(state)
     assert torch.equal(opt_b.state[opt_b.param_groups[0]["params"][0]]["state8"], opt8.state[p8]["state8"])
     _status_ok()
+
+
+def test_peer_flag_timeout_becomes_comm_timeout_error():
+    """A bounded device wait on a flag that nothing sets (this GPU's own memory standing in for a peer's) gives up
+    after its 0.2 s budget and records a status; the host turns it into CommTimeoutError. No fault and no hang: the
+    kernel returns on its own and the context stays usable."""
+    import time
+
+    from quantaweave_b200.ops import ext
+    from quantaweave_b200.ops.status import CommTimeoutError, check_device_status
+
+    C = ext()
+    check_device_status()  # a clean slate
+    flags = torch.zeros(2, dtype=torch.int32, device="cuda")
+    started = time.time()
+    C.p2p_wait(flags, 2, 1, 0.2)
+    torch.cuda.synchronize()
+    assert time.time() - started < 10
+    with pytest.raises(CommTimeoutError):
+        check_device_status()
+    check_device_status()  # the word was cleared
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum()) == 8.0  # the context still works
