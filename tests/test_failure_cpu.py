@@ -34,6 +34,8 @@ def _dying_worker(rank, world, port, queue):
         queue.put((rank, "no error", time.time() - started))
     except Exception as exc:  # noqa: BLE001
         queue.put((rank, type(exc).__name__, time.time() - started))
+    queue.close()
+    queue.join_thread()  # flush the result before the hard exit (the peer is gone, so no orderly shutdown)
     os._exit(0)
 
 
