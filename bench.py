@@ -167,18 +167,24 @@ def run_native(args, rank, world, local):
     stream = SyntheticTokenStream(cfg.vocab_size, args.seq_len, args.seqs_per_gpu, seed=args.seed,
                                   distribution="zipf", zipf_s=1.1, rank=rank, world_size=world)
 
-    def train_step(batch):
-        out = model(batch, labels=batch, return_logits=False)
-        out["loss"].backward()
-        if ep is not None:
-            from quantaweave_b200.parallel.expert_parallel import clip_grad_norm_parallel, sync_gradients
+    from quantaweave_b200.utils.tracing import nvtx_range  # no-ops unless QW_NVTX=1
 
-            sync_gradients(model, ep, None)
-            clip_grad_norm_parallel(model, ep, 1.0, False, opt)
-        else:
-            opt.clip_grad_norm_(1.0)
-        opt.step()
-        opt.zero_grad(set_to_none=True)
+    def train_step(batch):
+        with nvtx_range("forward"):
+            out = model(batch, labels=batch, return_logits=False)
+        with nvtx_range("backward"):
+            out["loss"].backward()
+        with nvtx_range("grad_sync"):
+            if ep is not None:
+                from quantaweave_b200.parallel.expert_parallel import clip_grad_norm_parallel, sync_gradients
+
+                sync_gradients(model, ep, None)
+                clip_grad_norm_parallel(model, ep, 1.0, False, opt)
+            else:
+                opt.clip_grad_norm_(1.0)
+        with nvtx_range("optimizer"):
+            opt.step()
+            opt.zero_grad(set_to_none=True)
         return out["loss"]
 
     host_batches = [stream.batch(i)[0].pin_memory() for i in range(args.warmup + 2 * args.steps + 1)]

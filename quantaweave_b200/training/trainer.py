@@ -39,6 +39,7 @@ from ..data.pipeline import (BatchStream, BPETokenizer, CharTokenizer, Curriculu
                              token_classes)
 from ..models.model import QuantaWeaveMoEForCausalLM
 from ..utils.checkpoint_io import load_checkpoint as load_checkpoint_file
+from ..utils.tracing import nvtx_range
 from ..utils.hardware import choose_precision, detect, find_safe_batch_size, parameter_counts
 from .metrics import MetricsLogger
 from .schedules import ScheduleConfig, TrainingController
@@ -754,31 +755,34 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
             optimizer.zero_grad(set_to_none=True)
             overflow_fraction = overflow_value / max(1, routes_per_step)
         else:
-            with autocast():
+            with autocast(), nvtx_range("forward"):
                 out = model(batch, labels=batch, domain_ids=domain_ids,
                             num_domains=stream.num_domains if domains_active else 0, return_logits=False)
             loss = out["loss"]
             scaled = loss / args.gradient_accumulation_steps
-            (scaler.scale(scaled) if scaler is not None else scaled).backward()
+            with nvtx_range("backward"):
+                (scaler.scale(scaled) if scaler is not None else scaled).backward()
             if step % args.gradient_accumulation_steps == 0 or step == args.steps:
-                if ep is not None:
-                    from ..parallel.expert_parallel import clip_grad_norm_parallel, sync_gradients
+                with nvtx_range("grad_sync"):
+                    if ep is not None:
+                        from ..parallel.expert_parallel import clip_grad_norm_parallel, sync_gradients
 
-                    sync_gradients(model, ep, optimizer if args.shard_optimizer else None)
-                    grad_norm = clip_grad_norm_parallel(model, ep, args.max_grad_norm, bool(args.shard_optimizer), optimizer)
-                elif dp is not None:
-                    dp.sync_gradients(model, optimizer if args.shard_optimizer else None)
-                    grad_norm = dp.clip_grad_norm(model, optimizer, args.max_grad_norm)
-                else:
+                        sync_gradients(model, ep, optimizer if args.shard_optimizer else None)
+                        grad_norm = clip_grad_norm_parallel(model, ep, args.max_grad_norm, bool(args.shard_optimizer), optimizer)
+                    elif dp is not None:
+                        dp.sync_gradients(model, optimizer if args.shard_optimizer else None)
+                        grad_norm = dp.clip_grad_norm(model, optimizer, args.max_grad_norm)
+                    else:
+                        if scaler is not None:
+                            scaler.unscale_(optimizer)
+                        grad_norm = clip_grad_norm(model, optimizer, args.max_grad_norm)
+                with nvtx_range("optimizer"):
                     if scaler is not None:
-                        scaler.unscale_(optimizer)
-                    grad_norm = clip_grad_norm(model, optimizer, args.max_grad_norm)
-                if scaler is not None:
-                    scaler.step(optimizer)
-                    scaler.update()
-                else:
-                    optimizer.step()
-                optimizer.zero_grad(set_to_none=True)
+                        scaler.step(optimizer)
+                        scaler.update()
+                    else:
+                        optimizer.step()
+                    optimizer.zero_grad(set_to_none=True)
             loss_value = float(loss.item())
             aux_value = float(out["router_aux_loss"].item())
             dropped_value, overflow_value = int(out["dropped_routes"].item()), int(out["overflow_routes"].item())
