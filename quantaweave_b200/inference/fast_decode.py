@@ -18,6 +18,12 @@ B200 design:
 * prefill runs the training kernels (tcgen05 GEMMs, flash attention, grouped SwiGLU) over the prompt.
 
 On CPU the same step runs as plain fp32 PyTorch (the oracle the GPU path is tested against).
+
+Expert-parallel models (the reference refuses them, ``src/fast_decode.py:89-90``) decode SPMD: every rank of the
+expert group runs the same prompts and tokens through the replicated layers; at each MoE layer a rank weights only the
+routes to its own experts and one all-reduce over the group sums the partial outputs, so every rank produces the same
+logits (and, with the same seed, the same samples). This path uses the fp32 PyTorch step on the model's device and no
+CUDA graph; the fused decode kernels are single-GPU.
 """
 
 from __future__ import annotations
@@ -65,13 +71,17 @@ class FastDecoder:
                  compile: Optional[bool] = None, max_batch: int = 1, max_length: Optional[int] = None) -> None:
         from ..models.layers import Attention
 
-        if getattr(model, "expert_parallel", None) is not None or getattr(model, "pipeline", None) is not None:
-            raise Unsupported("only a whole single-process QuantaWeave model is supported")
+        ep = getattr(model, "expert_parallel", None)
+        if getattr(model, "pipeline", None) is not None:
+            raise Unsupported("pipeline-stage models hold only some layers")
+        if ep is not None and (getattr(ep, "tp_size", 1) > 1 or getattr(ep, "sequence_parallel", False)):
+            raise Unsupported("tensor-parallel attention")
         cfg = model.config
         self.model = model
         self.config = cfg
         self.device = torch.device(device)
-        self.native = self.device.type == "cuda"
+        self.ep = ep if ep is not None and ep.world_size > 1 else None
+        self.native = self.device.type == "cuda" and self.ep is None
         if self.native:
             # the prefill runs the model's own native modules: bf16 matrices, fp32 router/norms (in place)
             from ..training.native import prepare_model
@@ -213,12 +223,23 @@ class FastDecoder:
             weights = probs.gather(1, chosen)
             weights = weights / weights.sum(-1, keepdim=True)
             f = layer.ffn
+            if self.ep is not None:  # this rank's experts only; the group's partial outputs are summed below
+                local = layer.q_gu.size(0)
+                first = self.ep.rank * local
+                mine = (chosen >= first) & (chosen < first + local)
+                weights = weights * mine
+                chosen = (chosen - first).clamp(0, local - 1)
             wgu = layer.q_gu[chosen].float()          # [B, k, 2F, H]
             wd = layer.q_d[chosen].float()            # [B, k, H, F]
             g = torch.einsum("bkfh,bh->bkf", wgu[:, :, :f], n2)
             u = torch.einsum("bkfh,bh->bkf", wgu[:, :, f:], n2)
             out = torch.einsum("bkhf,bkf->bkh", wd, F.silu(g) * u)
-            x = x + (out * weights[..., None]).sum(1)
+            moe_out = (out * weights[..., None]).sum(1)
+            if self.ep is not None:
+                import torch.distributed as dist
+
+                dist.all_reduce(moe_out, group=self.ep.group)
+            x = x + moe_out
         del rope_tables, rms_norm_reference
         x = self._apply_norm(x, self.final_norm)
         return F.linear(x, self.lm_head.float())
@@ -364,9 +385,11 @@ class FastDecoder:
             return
         rows = slice(first_row, first_row + batch)
         model = self.model
-        saved = [(moe.capacity_factor, moe.drop_overflow_tokens) for moe in model.moes()]
+        saved = [(moe.capacity_factor, moe.drop_overflow_tokens, moe.kernel) for moe in model.moes()]
         for moe in model.moes():
             moe.drop_overflow_tokens = False
+            if self.ep is not None:
+                moe.kernel = "loop"  # expert-parallel prefill: the per-expert exchange path (fp32, any device)
         try:
             hidden = model.embed(prompts.to(self.device))
             hq, hkv, d = self.heads, self.kv_heads, self.head_dim
@@ -393,8 +416,8 @@ class FastDecoder:
                 moe_out = block.moe(block.moe_norm(hidden))[0]
                 hidden = hidden + moe_out
         finally:
-            for moe, (cf, drop) in zip(model.moes(), saved):
-                moe.capacity_factor, moe.drop_overflow_tokens = cf, drop
+            for moe, (cf, drop, kernel) in zip(model.moes(), saved):
+                moe.capacity_factor, moe.drop_overflow_tokens, moe.kernel = cf, drop, kernel
 
     def _native_attention(self, q: Tensor, k: Tensor, v: Tensor, batch: int, n: int) -> Tensor:
         """Causal flash attention over the (already rotated) prompt; q/k/v are views into the packed QKV rows."""
