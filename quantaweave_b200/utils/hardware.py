@@ -235,9 +235,19 @@ def recommend(info: DeviceInfo, config: QuantaWeaveConfig, sequence_length: int,
 
 
 def main(argv=None) -> None:
+    """CLI with the reference's flags (``src/hardware.py:395-430``): describe the device, optionally pick the shape
+    with ``--auto-architecture`` (``--quality``, ``--memory-fraction``), report precision, parameter counts, memory
+    fit and a suggested expert count, and with ``--probe`` run real passes to find a safe batch size."""
     parser = argparse.ArgumentParser(description="Describe this machine and size a QuantaWeave model for it")
-    parser.add_argument("--device", default="auto")
-    parser.add_argument("--probe", action="store_true")
+    parser.add_argument("--device", default="auto", choices=("auto", "cuda", "rocm", "xpu", "cpu"))
+    parser.add_argument("--probe", action="store_true", help="run real passes to find a safe batch size")
+    parser.add_argument("--auto-architecture", action="store_true",
+                        help="pick hidden size, layers, experts and sequence length for this device")
+    parser.add_argument("--quality", default="balanced", choices=("capacity", "balanced", "dense"),
+                        help="--auto-architecture: favour stored capacity, a balance, or a dense (single-expert) model")
+    parser.add_argument("--memory-fraction", type=float, default=0.45,
+                        help="--auto-architecture: share of device memory to target")
+    parser.add_argument("--precision", default="auto", choices=("auto", "bf16", "fp16", "fp32"))
     parser.add_argument("--hidden-size", type=int, default=256)
     parser.add_argument("--layers", type=int, default=4)
     parser.add_argument("--ffn-size", type=int, default=512)
@@ -248,10 +258,22 @@ def main(argv=None) -> None:
     parser.add_argument("--sequence-length", type=int, default=128)
     args = parser.parse_args(argv)
     info = detect(args.device)
+    if args.auto_architecture:
+        shape = auto_architecture(info, args.vocab_size, args.memory_fraction, args.quality)
+        args.hidden_size, args.layers, args.ffn_size = shape["hidden_size"], shape["layers"], shape["ffn_size"]
+        args.total_experts, args.active_experts = shape["total_experts"], shape["active_experts"]
+        args.sequence_length = shape["sequence_length"]
+        args.attention_heads = shape.get("attention_heads", args.attention_heads)
     config = QuantaWeaveConfig(vocab_size=args.vocab_size, hidden_size=args.hidden_size, layers=args.layers,
                                ffn_size=args.ffn_size, num_experts=args.total_experts, top_k=args.active_experts,
                                attention_heads=args.attention_heads, max_sequence_length=args.sequence_length + 1)
-    print(json.dumps(recommend(info, config, args.sequence_length, args.probe), indent=2, default=str))
+    report = recommend(info, config, args.sequence_length, args.probe, preferred_precision=args.precision)
+    report["suggested_num_experts"] = suggest_num_experts(info, args.hidden_size, args.ffn_size, args.layers,
+                                                          args.active_experts, args.vocab_size, args.sequence_length)
+    report["shape"] = {"hidden_size": args.hidden_size, "layers": args.layers, "ffn_size": args.ffn_size,
+                       "total_experts": args.total_experts, "active_experts": args.active_experts,
+                       "sequence_length": args.sequence_length, "attention_heads": args.attention_heads}
+    print(json.dumps(report, indent=2, default=str))
 
 
 if __name__ == "__main__":

@@ -85,3 +85,14 @@ def test_reproduce_command_lists_non_defaults():
     assert "--lr" not in cmd
     full = reproduce_command("quantaweave_b200.train", parser, args, explicit=True)
     assert "--lr 0.0003" in full
+
+
+def test_hardware_cli_auto_architecture(capsys):
+    import json
+
+    from quantaweave_b200.utils.hardware import main
+
+    main(["--device", "cpu", "--auto-architecture", "--quality", "capacity", "--precision", "fp32"])
+    report = json.loads(capsys.readouterr().out)
+    assert report["precision"] == "fp32" and report["shape"]["total_experts"] >= 1
+    assert report["parameters"]["total"] > 0 and report["suggested_num_experts"] >= 1
