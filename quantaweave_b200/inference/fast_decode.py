@@ -56,6 +56,18 @@ def filter_logits(logits: Tensor, top_k: int = 0, top_p: float = 1.0) -> Tensor:
     return logits
 
 
+def layer_weight(module) -> Tensor:
+    """The dense weight a linear-like module applies (reference ``src/fast_decode.py:65-73``): a plain
+    ``nn.Linear``'s weight, a LoRA projection's merged weight, or a quantised projection dequantised."""
+    if isinstance(module, torch.nn.Linear):
+        return module.weight.detach()
+    if hasattr(module, "merged_weight"):
+        return module.merged_weight()
+    if hasattr(module, "dequantize"):
+        return module.dequantize()
+    raise Unsupported(f"cannot read the weights of {type(module).__name__}")
+
+
 def precision_dtype(device: torch.device, precision: str) -> torch.dtype:
     if precision == "auto":
         precision = "bf16" if device.type == "cuda" else "fp32"

@@ -189,6 +189,11 @@ def tokenizer_hash(tokenizer) -> str:
     return hashlib.sha256(text.encode()).hexdigest()[:16]
 
 
+def build_vocab(path: Path, vocab_size: int) -> dict:
+    """Character vocabulary of a JSONL corpus (reference ``src/train_quantweave_moe.py:54-55``)."""
+    return CharTokenizer.build((text for _, text in read_rows([Path(path)])), vocab_size).vocab
+
+
 def tokenizer_payload(tokenizer):
     return tokenizer.vocab if isinstance(tokenizer, CharTokenizer) else tokenizer
 

@@ -96,3 +96,29 @@ def test_hardware_cli_auto_architecture(capsys):
     report = json.loads(capsys.readouterr().out)
     assert report["precision"] == "fp32" and report["shape"]["total_experts"] >= 1
     assert report["parameters"]["total"] > 0 and report["suggested_num_experts"] >= 1
+
+
+def test_reference_helper_names(tmp_path):
+    """``build_vocab`` (trainer) and ``layer_weight`` (decoder) from the reference's public module surface."""
+    import json
+
+    import torch
+
+    from quantaweave_b200.inference.fast_decode import Unsupported, layer_weight
+    from quantaweave_b200.inference.quantization import QuantizedLinear
+    from quantaweave_b200.training.trainer import build_vocab
+
+    corpus = tmp_path / "c.jsonl"
+    corpus.write_text(json.dumps({"text": "abcab"}) + "\n" + json.dumps({"text": "cd"}) + "\n")
+    vocab = build_vocab(corpus, 64)
+    assert {"a", "b", "c", "d"} <= set(vocab)
+    linear = torch.nn.Linear(64, 8, bias=False)
+    assert torch.equal(layer_weight(linear), linear.weight.detach())
+    q = QuantizedLinear.from_linear(linear, 8) if hasattr(QuantizedLinear, "from_linear") else None
+    if q is not None:
+        assert (layer_weight(q) - linear.weight).abs().max() < 0.05
+    try:
+        layer_weight(torch.nn.ReLU())
+        raise AssertionError("expected Unsupported")
+    except Unsupported:
+        pass
