@@ -411,3 +411,34 @@ def test_expert_parallel_decode_matches_single_process():
     single-process decoder's greedy tokens on every rank."""
     results = run_ranks(_ep_decode_case, 2)
     assert results[0] == results[1]
+
+
+# ------------------------------------------------------------------------------------------ straggler control
+def _straggler_case(rank, world):
+    from quantaweave_b200.parallel.expert_parallel import DeviceLoadTracker, init_expert_parallel
+
+    cfg = tiny_config(capacity_factor=0.0, num_experts=4, top_k=1)
+    ep = init_expert_parallel("cpu", 1)
+    torch.manual_seed(0)
+    model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ep).eval()
+    for moe in model.moes():
+        moe.simulated_cost_per_row = 1.0 if rank == 1 else 0.0  # rank 1's experts look slow
+    tracker = DeviceLoadTracker(model, ep, strength=0.5, rate=0.5, interval=1)
+    batch = torch.randint(0, 64, (4, 17), generator=torch.Generator().manual_seed(3))
+    history = []
+    with torch.no_grad():
+        for step in range(1, 9):
+            model(batch, labels=batch)
+            history.append(tracker.update(step))
+    first, last = history[0]["device_rows"], history[-1]["device_rows"]
+    assert tracker.rank_bias[:, 1].mean() < 0 < tracker.rank_bias[:, 0].mean()  # slow rank pushed away
+    assert last[1] < first[1] and last[0] > first[0], (first, last)
+    assert abs(float(tracker.rank_bias.sum())) < 1e-9  # re-centred
+    state = tracker.state_dict()
+    tracker.load_state_dict(state)
+    return last
+
+
+def test_straggler_routing_moves_traffic_off_a_slow_rank():
+    results = run_ranks(_straggler_case, 2)
+    assert results[0] == results[1]  # both ranks see the same gathered loads
