@@ -27,7 +27,8 @@ class CPUOffloadAdamW(torch.optim.Optimizer):
             st["master"] = p.detach().to("cpu", torch.float32).clone()
             if pin:
                 st["master"] = st["master"].pin_memory()
-            st["staging"] = torch.empty(p.shape, dtype=torch.float32, pin_memory=pin)
+        if "staging" not in st:  # a reused transfer buffer; never saved
+            st["staging"] = torch.empty(p.shape, dtype=torch.float32, pin_memory=p.is_cuda)
         return st
 
     @torch.no_grad()
@@ -56,8 +57,8 @@ class CPUOffloadAdamW(torch.optim.Optimizer):
 
     def state_dict(self) -> dict:
         base = super().state_dict()
-        for st in base["state"].values():
-            st.pop("staging", None)
+        # the base class hands out the live per-parameter dicts: filter copies, never the optimizer's own state
+        base["state"] = {idx: {k: v for k, v in st.items() if k != "staging"} for idx, st in base["state"].items()}
         return base
 
     def load_state_dict(self, state_dict: dict) -> None:
