@@ -83,6 +83,8 @@ class FastDecoder:
                  compile: Optional[bool] = None, max_batch: int = 1, max_length: Optional[int] = None) -> None:
         from ..models.layers import Attention
 
+        if not all(hasattr(model, name) for name in ("config", "blocks", "token_embedding", "lm_head")):
+            raise Unsupported(f"{type(model).__name__} is not a QuantaWeave causal LM")
         ep = getattr(model, "expert_parallel", None)
         if getattr(model, "pipeline", None) is not None:
             raise Unsupported("pipeline-stage models hold only some layers")
