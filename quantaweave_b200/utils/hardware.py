@@ -162,42 +162,76 @@ def _is_oom(error: BaseException) -> bool:
     return isinstance(error, torch.OutOfMemoryError) or "out of memory" in str(error).lower()
 
 
+def _peak_bytes(device: torch.device) -> Optional[int]:
+    """Peak device memory since the last reset; on the host, the process's resident set (None without psutil)."""
+    if device.type == "cuda":
+        return torch.cuda.max_memory_allocated(device)
+    try:
+        import psutil
+
+        return psutil.Process().memory_info().rss
+    except ImportError:
+        return None
+
+
+def _reset_peak(device: torch.device) -> None:
+    if device.type == "cuda":
+        torch.cuda.reset_peak_memory_stats(device)
+
+
 def find_safe_batch_size(model, device: torch.device, sequence_length: int, autocast: Callable = None,
-                         start: int = 1, limit: int = 4096, memory_fraction: float = 0.85, target: float = 0.95,
-                         steps: int = 2, peak_fn: Optional[Callable] = None, clock: Callable = time.perf_counter) -> dict:
-    """Double the batch with real forward/backward steps (optimizer moments reserved) until OOM or
-    ``memory_fraction`` of device memory; return the smallest batch reaching ``target`` of the best throughput."""
+                         start: int = 1, limit: int = 256, memory_fraction: float = 0.85, target: float = 0.95,
+                         steps: int = 2, total_memory: Optional[int] = None, peak_fn: Optional[Callable] = None,
+                         clock: Callable = time.perf_counter) -> dict:
+    """Double the batch with real forward/backward/clip steps until a step runs out of memory or its peak passes
+    ``memory_fraction`` of ``total_memory`` (default: the device's, host memory on CPU).
+
+    The optimizer's state is held for the whole search, so an approved batch still fits once training starts: two
+    fp32 AdamW moments per trainable parameter, plus an fp32 master copy of every low-precision one. Weights are never
+    stepped; gradients are cleared and the module's train/eval mode is restored. Any error other than running out of
+    memory propagates. Returns the largest batch that fitted (``batch_size``), the smallest batch whose throughput is
+    within ``target`` of the best (``recommended_batch_size``; ``target=0`` picks the largest) and the measured
+    ``curve`` of ``{batch_size, tokens_per_second, peak_memory_bytes}``."""
     import contextlib
 
     autocast = autocast or contextlib.nullcontext
+    peak_fn = peak_fn or (lambda: _peak_bytes(device))
     vocab = model.config.vocab_size
-    total = torch.cuda.get_device_properties(device).total_memory if device.type == "cuda" else None
-    results = []
+    if total_memory is None:
+        total_memory = (torch.cuda.get_device_properties(device).total_memory if device.type == "cuda"
+                        else _host_memory()[0])
+    trainable = [p for p in model.parameters() if p.requires_grad]
+    reserve = [torch.zeros_like(p, dtype=torch.float32) for p in trainable for _ in range(2)]
+    reserve += [torch.zeros_like(p, dtype=torch.float32) for p in trainable if p.dtype != torch.float32]
+    was_training = model.training
+    model.train()
+    curve = []
     batch = start
-    reserve = [torch.zeros_like(p, dtype=torch.float32) for p in model.parameters()] if device.type == "cuda" else []
     try:
         while batch <= limit:
             try:
-                if device.type == "cuda":
-                    torch.cuda.reset_peak_memory_stats(device)
+                _reset_peak(device)
                 ids = torch.randint(0, vocab, (batch, sequence_length + 1), device=device)
                 began = None
                 for i in range(steps):
-                    if i == 1:
+                    if i == min(1, steps - 1):
                         if device.type == "cuda":
                             torch.cuda.synchronize(device)
                         began = clock()
                     with autocast():
                         loss = model(ids, labels=ids, return_logits=False)["loss"]
                     loss.backward()
+                    torch.nn.utils.clip_grad_norm_(trainable, 1.0)
                     model.zero_grad(set_to_none=True)
                 if device.type == "cuda":
                     torch.cuda.synchronize(device)
-                elapsed = max(clock() - (began or clock()), 1e-9)
-                peak = peak_fn() if peak_fn else (torch.cuda.max_memory_allocated(device) if device.type == "cuda" else 0)
-                results.append({"batch_size": batch, "tokens_per_second": batch * sequence_length * max(1, steps - 1) / elapsed,
-                                "peak_memory_bytes": peak})
-                if total and peak > memory_fraction * total:
+                timed = steps - min(1, steps - 1)
+                elapsed = max(clock() - began, 1e-9)
+                peak = peak_fn()
+                curve.append({"batch_size": batch, "tokens_per_second": batch * sequence_length * timed / elapsed,
+                              "peak_memory_bytes": peak})
+                if peak is not None and total_memory and peak > memory_fraction * total_memory:
+                    curve.pop()  # over the headroom limit: this batch is not safe
                     break
                 batch *= 2
             except Exception as error:  # noqa: BLE001
@@ -209,28 +243,63 @@ def find_safe_batch_size(model, device: torch.device, sequence_length: int, auto
                 break
     finally:
         del reserve
-    if not results:
-        raise RuntimeError("even the smallest batch does not fit on this device")
-    best = max(r["tokens_per_second"] for r in results)
-    chosen = next(r for r in results if r["tokens_per_second"] >= target * best) if target > 0 else results[-1]
-    return {"batch_size": results[-1]["batch_size"], "recommended_batch_size": chosen["batch_size"],
-            "tokens_per_second": chosen["tokens_per_second"], "largest_peak_memory_bytes": results[-1]["peak_memory_bytes"],
-            "probes": results}
+        model.zero_grad(set_to_none=True)
+        model.train(was_training)
+    if not curve:
+        raise RuntimeError("even batch size 1 does not fit on this device")
+    best = max(r["tokens_per_second"] for r in curve)
+    chosen = next(r for r in curve if r["tokens_per_second"] >= target * best) if target > 0 else curve[-1]
+    return {"batch_size": curve[-1]["batch_size"], "recommended_batch_size": chosen["batch_size"],
+            "tokens_per_second": chosen["tokens_per_second"], "peak_memory_bytes": chosen["peak_memory_bytes"],
+            "largest_peak_memory_bytes": curve[-1]["peak_memory_bytes"], "curve": curve, "headroom": memory_fraction}
+
+
+CHECKPOINTING_GAIN = 1.05  # recompute must buy at least 5 % more tokens/s (through a larger batch) to be recommended
 
 
 def recommend(info: DeviceInfo, config: QuantaWeaveConfig, sequence_length: int, probe: bool = False,
-              preferred_precision: str = "auto") -> dict:
+              preferred_precision: str = "auto", autocast: Optional[Callable] = None) -> dict:
+    """Precision, parameter counts and whether the training state fits; with ``probe`` (any device) also the batch
+    probe run twice, without and with activation checkpointing. Checkpointing is recommended only when its best
+    throughput beats the plain model's by ``CHECKPOINTING_GAIN``, or when the plain model does not fit at all; the
+    recommended ``batch_size`` is that of the chosen setting."""
     counts = parameter_counts(config)
     state = counts["total"] * 16
-    out = {"device": asdict(info), "precision": choose_precision(info, preferred_precision), "parameters": counts,
-           "training_state_bytes": state,
-           "fits": info.total_memory_bytes == 0 or state < 0.9 * info.total_memory_bytes,
-           "activation_checkpointing": False}
-    if probe and info.backend != "cpu":
+    precision = choose_precision(info, preferred_precision)
+    memory = info.total_memory_bytes
+    out = {"device": asdict(info), "precision": precision, "parameters": counts, "training_state_bytes": state,
+           "fits_training_state": memory == 0 or state < 0.8 * memory,
+           "max_sequence_length": config.max_sequence_length - 1, "sequence_length": sequence_length,
+           # without a measurement: recompute once the training state alone takes 40 % of the device
+           "activation_checkpointing_recommended": bool(memory and state > 0.4 * memory)}
+    if probe:
         from ..models.model import QuantaWeaveMoEForCausalLM
 
-        model = QuantaWeaveMoEForCausalLM(config).to(info.torch_device)
-        out["probe"] = find_safe_batch_size(model, info.torch_device, sequence_length)
+        device = info.torch_device
+        if autocast is None:
+            from ..training.trainer import autocast_context
+
+            autocast = lambda: autocast_context(device, precision)  # noqa: E731
+        total = memory or None
+        results, errors = {}, {}
+        for checkpointing in (False, True):
+            model = QuantaWeaveMoEForCausalLM(config).to(device)
+            model.activation_checkpointing = checkpointing
+            try:
+                results[checkpointing] = find_safe_batch_size(model, device, sequence_length, autocast,
+                                                              total_memory=total)
+            except RuntimeError as error:
+                errors[checkpointing] = error
+            del model
+        if not results:
+            raise errors[False]
+        plain, recompute = results.get(False), results.get(True)
+        use = recompute is not None and (plain is None or recompute["tokens_per_second"]
+                                         > CHECKPOINTING_GAIN * plain["tokens_per_second"])
+        chosen = recompute if use else plain
+        out.update(activation_checkpointing_recommended=bool(use), batch_size=chosen["recommended_batch_size"],
+                   tokens_per_second=chosen["tokens_per_second"], probe=chosen,
+                   probe_without_checkpointing=plain, probe_with_checkpointing=recompute)
     return out
 
 
