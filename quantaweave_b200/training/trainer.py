@@ -484,6 +484,8 @@ def _validate(args) -> None:
                              "different attention slices under --sequence-parallel")
     if args.shard_optimizer and args.optimizer != "adamw":
         raise ValueError(f"--optimizer {args.optimizer} is not combinable with --shard-optimizer")
+    if args.val_fraction is not None and args.val_interval < 1:
+        raise ValueError("--val-fraction needs --val-interval >= 1 (steps between validation passes)")
     if args.curriculum != "none" and args.curriculum_steps <= 0:
         raise ValueError("--curriculum needs --curriculum-steps > 0")
 

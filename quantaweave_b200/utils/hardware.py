@@ -109,53 +109,106 @@ def suggest_num_experts(info: DeviceInfo, hidden_size: int, ffn_size: int, layer
     return best
 
 
-# (parameter budget, hidden, layers, ffn multiplier x10, heads) anchors, interpolated in log-budget space
-_SHAPE_ANCHORS = (
-    (2e6, 64, 2, 20, 4),
-    (2e7, 256, 4, 20, 4),
-    (2e8, 512, 8, 24, 8),
-    (2e9, 1024, 16, 27, 16),
-    (2e10, 2048, 24, 27, 16),
-    (2e11, 4096, 32, 35, 32),
-)
+# Depth and FFN width as functions of the model width: (hidden, layers, ffn multiplier), interpolated in log(hidden).
+_WIDTH_ANCHORS = ((64, 2, 2.0), (256, 4, 2.0), (512, 8, 2.5), (1024, 16, 2.75), (2048, 24, 2.75), (4096, 32, 3.5),
+                  (8192, 48, 3.5))
+# quality -> (starting expert count, routed experts per token)
+_QUALITIES = {"capacity": (64, 1), "balanced": (16, 2), "dense": (1, 1)}
+_MAX_EXPERTS = 256
+_MAX_WIDTH = 16384
 
 
-def _interpolate_shape(budget: float) -> tuple[int, int, int, int]:
-    pts = _SHAPE_ANCHORS
-    if budget <= pts[0][0]:
-        _, h, l, f, a = pts[0]
-        return h, l, h * f // 10, a
-    for lo, hi in zip(pts, pts[1:]):
-        if budget <= hi[0]:
-            t = (math.log(budget) - math.log(lo[0])) / (math.log(hi[0]) - math.log(lo[0]))
-            h = int(round((lo[1] + t * (hi[1] - lo[1])) / 64) * 64) or 64
-            layers = max(1, int(round(lo[2] + t * (hi[2] - lo[2]))))
-            fm = lo[3] + t * (hi[3] - lo[3])
-            heads = lo[4] if t < 0.5 else hi[4]
-            while h % heads:
-                heads //= 2
-            return h, layers, int(round(h * fm / 10 / 64) * 64) or 64, max(1, heads)
-    _, h, l, f, a = pts[-1]
-    return h, l, h * f // 10, a
+def _depth_and_ffn(hidden: int) -> tuple[int, int]:
+    pts = _WIDTH_ANCHORS
+    if hidden <= pts[0][0]:
+        layers, mult = pts[0][1], pts[0][2]
+    elif hidden >= pts[-1][0]:
+        layers, mult = pts[-1][1], pts[-1][2]
+    else:
+        lo, hi = next((a, b) for a, b in zip(pts, pts[1:]) if hidden <= b[0])
+        t = (math.log(hidden) - math.log(lo[0])) / (math.log(hi[0]) - math.log(lo[0]))
+        layers, mult = round(lo[1] + t * (hi[1] - lo[1])), lo[2] + t * (hi[2] - lo[2])
+    return max(1, int(layers)), max(64, int(round(hidden * mult / 64)) * 64)
 
 
-def auto_architecture(info: DeviceInfo, vocab_size: int, memory_fraction: float = 0.45, quality: str = "balanced") -> dict:
-    """Pick a shape whose training state fills about ``memory_fraction`` of device memory."""
-    if quality not in {"capacity", "balanced", "dense"}:
+def _sequence_length(hidden: int) -> int:
+    return 256 if hidden <= 256 else 512 if hidden <= 1024 else 2048
+
+
+def _linear_counts(vocab: int, hidden: int, ffn: int, seq: int) -> tuple[int, int, int]:
+    """(fixed, per layer with one expert, per extra expert per layer) parameter counts, read off three meta-device
+    builds: the model's size is affine in the layer count and, per layer, in the expert count."""
+    def total(layers: int, experts: int) -> int:
+        return parameter_counts(QuantaWeaveConfig(vocab_size=vocab, hidden_size=hidden, layers=layers, ffn_size=ffn,
+                                                  num_experts=experts, top_k=1, attention_heads=max(1, hidden // 64),
+                                                  max_sequence_length=seq + 1))["total"]
+
+    one = total(1, 1)
+    per_layer = total(2, 1) - one
+    per_expert = total(1, 2) - one
+    return one - per_layer, per_layer, per_expert
+
+
+def auto_architecture(info: DeviceInfo, vocab_size: int = 7168, memory_fraction: float = 0.45,
+                      quality: str = "balanced") -> dict:
+    """The largest model whose training state (16 B per parameter) fits ``memory_fraction`` of the device.
+
+    Width sets depth and FFN width (``_WIDTH_ANCHORS``); the widest shape that fits with the quality's starting
+    expert count is taken, then the rest of the budget is filled: ``capacity`` and ``balanced`` add experts (up to
+    256), ``dense`` widens its single FFN. ``capacity`` routes each token to one of many experts (most parameters,
+    fewest active), ``balanced`` to two of a moderate pool, ``dense`` is a plain transformer. A budget below the
+    smallest shape still returns that shape when it fits the device; one that fits no device memory at all raises."""
+    if quality not in _QUALITIES:
         raise ValueError("quality must be capacity, balanced or dense")
-    budget_bytes = max(info.total_memory_bytes, 1 << 30) * memory_fraction
-    params = budget_bytes / 16
-    experts, active = {"capacity": (64, 2), "balanced": (16, 2), "dense": (1, 1)}[quality]
-    dense_equiv = params / max(1.0, experts / 4)
-    hidden, layers, ffn, heads = _interpolate_shape(dense_equiv)
-    config = QuantaWeaveConfig(vocab_size=vocab_size, hidden_size=hidden, layers=layers, ffn_size=ffn,
-                               num_experts=experts, top_k=active, attention_heads=heads)
-    while training_state_bytes(config) > budget_bytes and config.num_experts > active:
-        config.num_experts = max(active, config.num_experts // 2)
-    seq = 256 if hidden <= 256 else 512 if hidden <= 1024 else 2048
-    return {"hidden_size": hidden, "layers": layers, "ffn_size": ffn, "attention_heads": heads,
-            "total_experts": config.num_experts, "active_experts": active, "sequence_length": seq,
-            "training_state_fraction_of_budget": training_state_bytes(config) / budget_bytes}
+    if not 0 < memory_fraction <= 1:
+        raise ValueError("memory_fraction must be in (0, 1]")
+    if info.total_memory_bytes <= 0:
+        raise ValueError("the device's memory size is unknown; auto-architecture needs it")
+    budget = info.total_memory_bytes * memory_fraction
+    start_experts, active = _QUALITIES[quality]
+
+    def shape(hidden: int) -> dict:
+        layers, ffn = _depth_and_ffn(hidden)
+        seq = _sequence_length(hidden)
+        fixed, per_layer, per_expert = _linear_counts(vocab_size, hidden, ffn, seq)
+        return dict(hidden=hidden, layers=layers, ffn=ffn, seq=seq, fixed=fixed, per_layer=per_layer,
+                    per_expert=per_expert)
+
+    def state(sh: dict, experts: int, ffn_extra: int = 0) -> int:
+        params = sh["fixed"] + sh["layers"] * (sh["per_layer"] + (experts - 1) * sh["per_expert"])
+        params += sh["layers"] * experts * 3 * sh["hidden"] * ffn_extra
+        return params * 16
+
+    lo, hi = 1, _MAX_WIDTH // 64  # widths are multiples of 64 (one 64-wide head each)
+    best = shape(64)
+    if state(best, start_experts) > 0.9 * info.total_memory_bytes:
+        raise ValueError(f"no architecture fits this device: even hidden 64 needs {state(best, start_experts):,} "
+                         f"bytes of training state, {info.total_memory_bytes:,} available")
+    while lo < hi:  # training state grows with width: the widest shape within the budget
+        mid = (lo + hi + 1) // 2
+        candidate = shape(64 * mid)
+        if state(candidate, start_experts) <= budget:
+            lo, best = mid, candidate
+        else:
+            hi = mid - 1
+    experts, extra = start_experts, 0
+    if quality == "dense":
+        while extra < 8 * best["hidden"] and state(best, 1, extra + 64) <= budget:
+            extra += 64
+    else:
+        while experts < _MAX_EXPERTS and state(best, experts + 1) <= budget:
+            experts += 1
+    hidden, ffn = best["hidden"], best["ffn"] + extra
+    config = QuantaWeaveConfig(vocab_size=vocab_size, hidden_size=hidden, layers=best["layers"], ffn_size=ffn,
+                               num_experts=experts, top_k=active, attention_heads=max(1, hidden // 64),
+                               max_sequence_length=best["seq"] + 1)
+    counts = parameter_counts(config)
+    state_bytes = counts["total"] * 16
+    return {"quality": quality, "memory_fraction": memory_fraction, "vocab_size": vocab_size, "hidden_size": hidden,
+            "layers": config.layers, "ffn_size": ffn, "attention_heads": config.attention_heads,
+            "total_experts": experts, "active_experts": active, "sequence_length": best["seq"],
+            "total_parameters": counts["total"], "active_parameters": counts["active"],
+            "training_state_bytes": state_bytes, "training_state_fraction_of_budget": state_bytes / budget}
 
 
 def _is_oom(error: BaseException) -> bool:
@@ -332,13 +385,15 @@ def main(argv=None) -> None:
         args.hidden_size, args.layers, args.ffn_size = shape["hidden_size"], shape["layers"], shape["ffn_size"]
         args.total_experts, args.active_experts = shape["total_experts"], shape["active_experts"]
         args.sequence_length = shape["sequence_length"]
-        args.attention_heads = shape.get("attention_heads", args.attention_heads)
+        args.attention_heads = shape["attention_heads"]
     config = QuantaWeaveConfig(vocab_size=args.vocab_size, hidden_size=args.hidden_size, layers=args.layers,
                                ffn_size=args.ffn_size, num_experts=args.total_experts, top_k=args.active_experts,
                                attention_heads=args.attention_heads, max_sequence_length=args.sequence_length + 1)
     report = recommend(info, config, args.sequence_length, args.probe, preferred_precision=args.precision)
     report["suggested_num_experts"] = suggest_num_experts(info, args.hidden_size, args.ffn_size, args.layers,
                                                           args.active_experts, args.vocab_size, args.sequence_length)
+    if args.auto_architecture:
+        report["auto_architecture"] = shape
     report["shape"] = {"hidden_size": args.hidden_size, "layers": args.layers, "ffn_size": args.ffn_size,
                        "total_experts": args.total_experts, "active_experts": args.active_experts,
                        "sequence_length": args.sequence_length, "attention_heads": args.attention_heads}
