@@ -12,6 +12,7 @@ from quantaweave_b200.training.trainer import build_parser, default_args, run_tr
 
 def _corpus(path: Path, rows: int = 120) -> Path:
     words = ["the cat sat on the mat", "a dog ran far away", "numbers 12 34 56", "sun and moon, stars!"]
+    path.parent.mkdir(parents=True, exist_ok=True)
     with path.open("w") as fh:
         for i in range(rows):
             fh.write(json.dumps({"text": f"{words[i % 4]} {i}", "domain": "story" if i % 2 else "code"}) + "\n")
