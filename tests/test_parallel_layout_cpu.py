@@ -4,7 +4,6 @@ partitioning, the launcher-environment requirement, consolidation renumbering ex
 and 2-rank gloo training that resumes exactly, keeps replicated weights identical and, with the sharded optimizer,
 trains like the unsharded one while holding less state per rank."""
 
-
 import pytest
 import torch
 import torch.distributed as dist
