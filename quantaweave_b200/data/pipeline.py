@@ -20,6 +20,7 @@ import hashlib
 import json
 import math
 import shutil
+import unicodedata
 from array import array
 from dataclasses import dataclass
 from pathlib import Path
@@ -212,27 +213,33 @@ def load_tokenizer(directory: Path):
     return CharTokenizer(json.loads((directory / "vocab.json").read_text()))
 
 
-def token_classes(tokenizer) -> dict[str, list[int]]:
-    """Token ids grouped into coarse classes (letters, digits, whitespace, punctuation, special) for diagnostics."""
-    classes: dict[str, list[int]] = {"special": [], "whitespace": [], "digit": [], "alpha": [], "punct": [], "other": []}
-    size = tokenizer.vocab_size
-    for index in range(size):
+TOKEN_CLASS_NAMES = ("special", "letter", "digit", "space", "punct", "other")
+
+
+def token_classes(tokenizer) -> tuple[Tensor, list[str]]:
+    """Coarse class of every token id for routing-specialisation maps, as ``(class index per id [vocab], names)``
+    with the names special, letter, digit, space, punct and other (reference ``src/data_pipeline.py:199-223``).
+    A token is judged by the first visible character of its text; all-whitespace tokens are ``space``."""
+    names = list(TOKEN_CLASS_NAMES)
+    classes = torch.full((tokenizer.vocab_size,), names.index("other"), dtype=torch.long)
+    for index in range(tokenizer.vocab_size):
         if index in (tokenizer.unk_id, tokenizer.eos_id):
-            classes["special"].append(index)
+            classes[index] = names.index("special")
             continue
         text = tokenizer.decode([index])
         stripped = text.strip()
         if not stripped:
-            classes["whitespace"].append(index)
-        elif stripped.isdigit():
-            classes["digit"].append(index)
-        elif stripped.isalpha():
-            classes["alpha"].append(index)
-        elif all(not ch.isalnum() for ch in stripped):
-            classes["punct"].append(index)
+            label = "space" if text else "other"
+        elif stripped[0].isalpha():
+            label = "letter"
+        elif stripped[0].isdigit():
+            label = "digit"
+        elif unicodedata.category(stripped[0])[0] in "PS":
+            label = "punct"
         else:
-            classes["other"].append(index)
-    return {name: ids for name, ids in classes.items() if ids}
+            label = "other"
+        classes[index] = names.index(label)
+    return classes, names
 
 
 # ------------------------------------------------------------------------------------------ corpora

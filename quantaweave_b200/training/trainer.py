@@ -675,7 +675,7 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
     if diagnostics_interval and is_main:
         from ..utils.routing_diagnostics import RoutingMonitor
 
-        classes = token_classes(tokenizer) if tokenizer is not None else {}
+        classes = token_classes(tokenizer) if tokenizer is not None else None
         monitor = RoutingMonitor(config.layers, config.num_experts, config.top_k,
                                  getattr(dataset, "domains", ["synthetic"]), classes, args.diagnostics_dir)
     logger = MetricsLogger(args.metrics_file if is_main else None, counts["total"], counts["active"])

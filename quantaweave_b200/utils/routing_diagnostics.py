@@ -26,9 +26,9 @@ class RoutingMonitor:
                  token_classes: Optional[tuple[Tensor, list[str]]] = None, out_dir: Optional[Path] = None) -> None:
         self.num_layers, self.num_experts, self.top_k = num_layers, num_experts, top_k
         self.domains = list(domains)
-        if isinstance(token_classes, dict):  # {class name: [token ids]} as produced by data.pipeline.token_classes
+        if isinstance(token_classes, dict):  # {class name: [token ids]} is accepted too
             token_classes = _class_table(token_classes) if token_classes else None
-        self.token_classes = token_classes if token_classes else None
+        self.token_classes = token_classes if token_classes is not None and len(token_classes[1]) else None
         self.out_dir = Path(out_dir) if out_dir is not None else None
         if self.out_dir is not None:
             self.out_dir.mkdir(parents=True, exist_ok=True)

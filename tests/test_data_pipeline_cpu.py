@@ -34,9 +34,11 @@ def test_char_tokenizer_roundtrip_save_load_and_token_classes(tmp_path):
     tok.save(tmp_path)
     again = load_tokenizer(tmp_path)
     assert again.vocab == tok.vocab
-    classes = token_classes(tok)
-    assert {"special", "alpha", "digit", "whitespace", "punct"} <= set(classes)
-    assert tok.eos_id in classes["special"]
+    classes, names = token_classes(tok)
+    assert classes.shape == (tok.vocab_size,)
+    label = lambda ch: names[int(classes[tok.vocab[ch]])]  # noqa: E731
+    assert (label("h"), label("1"), label(" "), label("!")) == ("letter", "digit", "space", "punct")
+    assert names[int(classes[tok.eos_id])] == names[int(classes[tok.unk_id])] == "special"
 
 
 def test_bpe_and_sentencepiece_train_save_and_roundtrip(tmp_path):
@@ -133,3 +135,50 @@ def test_pii_redaction_in_rows(tmp_path):
     assert rows[1] == "nothing to see here"
     assert sum(redactor.report().values()) >= 2
     assert [t for _, t in read_rows([path])][0].startswith("mail me at jane.doe")
+
+
+def test_a_vocabulary_without_tokenizer_metadata_loads_as_characters(tmp_path):
+    tok = CharTokenizer.build(["hello world"], 32)
+    (tmp_path / "vocab.json").write_text(json.dumps(tok.vocab))  # an older checkpoint: no tokenizer_meta.json
+    again = load_tokenizer(tmp_path)
+    assert isinstance(again, CharTokenizer) and again.vocab == tok.vocab
+
+
+def test_windows_stay_inside_one_domain_and_drop_partial_tails(tmp_path):
+    data = _jsonl(tmp_path / "d.jsonl", [{"text": "aaaa", "domain": "x"}, {"text": "bbbbbbbbb", "domain": "y"},
+                                          {"text": "aa", "domain": "x"}])
+    tok = CharTokenizer.build(["ab"], 8)
+    ds = WindowDataset(build_corpus([data], tok), 3)  # windows of 4 tokens
+    a, b, eos = tok.vocab["a"], tok.vocab["b"], tok.eos_id
+    # x: a a a a <eos> a a <eos> (8 tokens, 2 windows); y: 9 b's and <eos> (10 tokens, 2 windows, 2 left over)
+    assert ds.domains == ["x", "y"] and ds.window_domains.tolist() == [0, 0, 1, 1]
+    assert ds[0].tolist() == [a] * 4 and ds[1].tolist() == [eos, a, a, eos] and ds[2].tolist() == [b] * 4
+    one = _jsonl(tmp_path / "stories.jsonl", [{"text": "aaaaaaaa"}])
+    two = _jsonl(tmp_path / "code.jsonl", [{"text": "bbbbbbbb"}])
+    assert build_corpus([one, two], tok).domains == ["stories", "code"]  # several files: the stem is the domain
+
+
+def test_repetitive_windows_score_easier_and_the_stream_reports_its_stage():
+    from quantaweave_b200.data.pipeline import Segment, TokenCorpus
+
+    tok = CharTokenizer.build(["abcdefgh"], 16)
+    text = "aaaaaaaa" + "abcdefgh"
+    ds = WindowDataset(TokenCorpus(torch.tensor(tok.encode(text), dtype=torch.int32), [Segment("default", 0, 16)]),
+                       7)
+    assert len(ds) == 2
+    for method in ("rarity", "entropy"):
+        scores = difficulty_scores(ds, method, tok.vocab_size)
+        assert scores[0] <= scores[1], method
+    stream = BatchStream(ds, 4, seed=3, scores=difficulty_scores(ds, "entropy", tok.vocab_size),
+                         curriculum=CurriculumConfig("entropy", start_fraction=0.5, steps=10))
+    state = stream.state(5)
+    assert state["samples_consumed"] == 20 and state["domain_weights"] == {"default": 1.0}
+    assert 1 <= state["curriculum_stage"] <= 4
+
+
+def test_an_empty_stream_is_refused(tmp_path):
+    data = _jsonl(tmp_path / "d.jsonl", [{"text": "ab"}])
+    ds = WindowDataset(build_corpus([data], CharTokenizer.build(["ab"], 8)), 32)
+    assert len(ds) == 0
+    with pytest.raises(ValueError):
+        BatchStream(ds, 2)
