@@ -1,0 +1,105 @@
+"""A checkpoint in the reference's layout loads unchanged (reference: ``src/quantweave_moe_model.py:51-60, 275-340``
+module names; ``src/train_quantweave_moe.py`` checkpoint payload). The checkpoint is written by hand here: a
+``config.json`` with only the reference's fourteen fields, a ``model.pt`` payload with per-expert
+``experts.{e}.{gate,up,down}.weight`` tensors in ``nn.Linear`` layout, ``nn.MultiheadAttention`` packed projections
+and LayerNorms, and a character ``vocab.json`` without tokenizer metadata."""
+
+import json
+
+import torch
+import torch.nn.functional as F
+
+from quantaweave_b200 import QuantaWeaveConfig
+from quantaweave_b200.tools.common import load_model
+
+REFERENCE_CONFIG = dict(vocab_size=40, hidden_size=16, layers=2, ffn_size=24, num_experts=3, top_k=2,
+                        attention_heads=2, max_sequence_length=12, router_aux_loss_coef=0.01, capacity_factor=0.0,
+                        min_expert_capacity=4, drop_overflow_tokens=True, overflow_policy="drop",
+                        router_temperature=1.0)
+
+
+def _reference_state(cfg: dict) -> dict:
+    g = torch.Generator().manual_seed(0)
+    H, F_, V, E = cfg["hidden_size"], cfg["ffn_size"], cfg["vocab_size"], cfg["num_experts"]
+    r = lambda *shape: 0.1 * torch.randn(*shape, generator=g)  # noqa: E731
+    state = {"token_embedding.weight": r(V, H), "position_embedding.weight": r(cfg["max_sequence_length"], H)}
+    for layer in range(cfg["layers"]):
+        p = f"blocks.{layer}."
+        state.update({p + "attention_norm.weight": 1 + r(H), p + "attention_norm.bias": r(H),
+                      p + "attention.in_proj_weight": r(3 * H, H), p + "attention.in_proj_bias": r(3 * H),
+                      p + "attention.out_proj.weight": r(H, H), p + "attention.out_proj.bias": r(H),
+                      p + "moe_norm.weight": 1 + r(H), p + "moe_norm.bias": r(H), p + "moe.router.weight": r(E, H)})
+        for e in range(E):
+            q = f"{p}moe.experts.{e}."
+            state.update({q + "gate.weight": r(F_, H), q + "up.weight": r(F_, H), q + "down.weight": r(H, F_)})
+    state.update({"final_norm.weight": 1 + r(H), "final_norm.bias": r(H), "lm_head.weight": r(V, H)})
+    return state
+
+
+def _write(tmp_path):
+    state = _reference_state(REFERENCE_CONFIG)
+    (tmp_path / "config.json").write_text(json.dumps(REFERENCE_CONFIG))
+    vocab = {"<unk>": 0, "<eos>": 1, **{ch: i + 2 for i, ch in enumerate("abcdefghijklmnopqrstuvwxyz .,!?")}}
+    (tmp_path / "vocab.json").write_text(json.dumps(vocab))
+    torch.save({"model": state, "optimizer": None, "step": 5, "rng_state": {}, "extra": {}}, tmp_path / "model.pt")
+    return state
+
+
+def _layer_norm(x, w, b):
+    return F.layer_norm(x, (x.size(-1),), w, b, 1e-5)
+
+
+@torch.no_grad()
+def _reference_forward(state: dict, cfg: dict, ids: torch.Tensor) -> torch.Tensor:
+    """The reference architecture restated in plain fp32 PyTorch, without expert capacity (capacity_factor 0)."""
+    H, heads, E, k = cfg["hidden_size"], cfg["attention_heads"], cfg["num_experts"], cfg["top_k"]
+    T = ids.size(1)
+    h = state["token_embedding.weight"][ids] + state["position_embedding.weight"][:T]
+    mask = torch.triu(torch.ones(T, T, dtype=torch.bool), 1)
+    for layer in range(cfg["layers"]):
+        p = f"blocks.{layer}."
+        a = _layer_norm(h, state[p + "attention_norm.weight"], state[p + "attention_norm.bias"])
+        qkv = a @ state[p + "attention.in_proj_weight"].T + state[p + "attention.in_proj_bias"]
+        q, kk, v = (t.view(1, T, heads, H // heads).transpose(1, 2) for t in qkv.split(H, -1))
+        scores = (q @ kk.transpose(-1, -2)) / (H // heads) ** 0.5
+        o = scores.masked_fill(mask, float("-inf")).softmax(-1) @ v
+        o = o.transpose(1, 2).reshape(1, T, H)
+        h = h + o @ state[p + "attention.out_proj.weight"].T + state[p + "attention.out_proj.bias"]
+        m = _layer_norm(h, state[p + "moe_norm.weight"], state[p + "moe_norm.bias"])[0]
+        probs = (m @ state[p + "moe.router.weight"].T).softmax(-1)
+        w, idx = probs.topk(k, -1)
+        w = w / w.sum(-1, keepdim=True)
+        out = torch.zeros_like(m)
+        for t in range(T):
+            for j in range(k):
+                q_ = f"{p}moe.experts.{int(idx[t, j])}."
+                x = m[t]
+                y = (F.silu(state[q_ + "gate.weight"] @ x) * (state[q_ + "up.weight"] @ x)) @ state[q_ + "down.weight"].T
+                out[t] += w[t, j] * y
+        h = h + out[None]
+    h = _layer_norm(h, state["final_norm.weight"], state["final_norm.bias"])
+    return h @ state["lm_head.weight"].T
+
+
+def test_a_reference_layout_checkpoint_loads_and_computes_the_reference_function(tmp_path):
+    state = _write(tmp_path)
+    config = QuantaWeaveConfig.load(tmp_path / "config.json")
+    assert (config.norm_type, config.position_embedding, config.attention_bias, config.kv_heads) == (
+        "layernorm", "learned", True, None)  # the additions default to the reference architecture
+    model = load_model(tmp_path, torch.device("cpu")).eval()
+    saved = model.state_dict()
+    assert saved.keys() == state.keys() and all(torch.equal(saved[k], state[k]) for k in state)  # same key layout
+    ids = torch.tensor([[3, 7, 1, 12, 5, 9, 2, 20, 4, 6, 8]])
+    with torch.no_grad():
+        got = model(ids)["logits"]
+    assert torch.allclose(got, _reference_forward(state, REFERENCE_CONFIG, ids), atol=1e-5)
+
+
+def test_the_chat_loader_reads_a_reference_character_vocabulary(tmp_path):
+    from quantaweave_b200.tools.chat import ChatSession, Settings, load_for_chat
+
+    _write(tmp_path)
+    model, tokenizer = load_for_chat(tmp_path, None, 0, torch.device("cpu"))
+    assert tokenizer.kind == "char" and tokenizer.vocab_size == 33
+    reply = ChatSession(model, tokenizer, torch.device("cpu"), "fp32", Settings(temperature=0, tokens=4)).send("ab")
+    assert reply.tokens <= 4
