@@ -2,7 +2,8 @@
 module names; ``src/train_quantweave_moe.py`` checkpoint payload). The checkpoint is written by hand here: a
 ``config.json`` with only the reference's fourteen fields, a ``model.pt`` payload with per-expert
 ``experts.{e}.{gate,up,down}.weight`` tensors in ``nn.Linear`` layout, ``nn.MultiheadAttention`` packed projections
-and LayerNorms, and a character ``vocab.json`` without tokenizer metadata."""
+and LayerNorms, and a character ``vocab.json`` without tokenizer metadata. The reference's ``model.int{b}.pt``
+payload (``src/quantization.py:105-117``: per-expert ``qweight``/``scales`` with fp32 scales) loads too."""
 
 import json
 
@@ -103,3 +104,58 @@ def test_the_chat_loader_reads_a_reference_character_vocabulary(tmp_path):
     assert tokenizer.kind == "char" and tokenizer.vocab_size == 33
     reply = ChatSession(model, tokenizer, torch.device("cpu"), "fp32", Settings(temperature=0, tokens=4)).send("ab")
     assert reply.tokens <= 4
+
+
+def _reference_quantize(weight: torch.Tensor, bits: int, group: int):
+    """The reference payload's per-layer encoding, restated: symmetric per-group codes (int8 in [-127, 127]; int4 in
+    [-8, 7] stored +8, two per byte, low nibble = even column) with fp32 scales, input padded to the group."""
+    out, cols = weight.shape
+    padded = -(-cols // group) * group
+    grouped = F.pad(weight, (0, padded - cols)).reshape(out, -1, group)
+    limit = 127 if bits == 8 else 7
+    scales = (grouped.abs().amax(-1) / limit).clamp(min=1e-8)
+    codes = torch.round(grouped / scales[..., None]).clamp(-limit - (bits == 4), limit).reshape(out, -1)
+    if bits == 8:
+        return codes.to(torch.int8), scales
+    unsigned = (codes + 8).to(torch.uint8)
+    return unsigned[:, 0::2] | (unsigned[:, 1::2] << 4), scales
+
+
+def _reference_dequantize(q: torch.Tensor, scales: torch.Tensor, bits: int, group: int, cols: int):
+    if bits == 8:
+        values = q.float()
+    else:
+        values = torch.stack([(q & 0xF).float() - 8, (q >> 4).float() - 8], -1).reshape(q.size(0), -1)
+    return (values.reshape(q.size(0), -1, group) * scales[..., None]).reshape(q.size(0), -1)[:, :cols]
+
+
+def test_a_reference_quantized_payload_loads_and_dequantizes_to_the_same_weights(tmp_path):
+    import pytest
+
+    from quantaweave_b200.inference.quantization import dequantized_expert, load_quantized
+
+    for bits, group in ((8, None), (4, 8)):
+        state = _reference_state(REFERENCE_CONFIG)
+        expected = {}
+        for key in [k for k in state if ".experts." in k]:
+            weight = state.pop(key)
+            g = group or weight.size(1)  # int8 without a group size: one scale per output row
+            q, s = _reference_quantize(weight, bits, g)
+            state[key.replace(".weight", ".qweight")], state[key.replace(".weight", ".scales")] = q, s
+            expected[key] = _reference_dequantize(q, s, bits, g, weight.size(1))
+        payload = {"config": REFERENCE_CONFIG, "bits": bits, "group_size": group, "quantize_lm_head": False,
+                   "state_dict": state}
+        torch.save(payload, tmp_path / f"model.int{bits}.pt")
+        model = load_quantized(tmp_path / f"model.int{bits}.pt")
+        for layer, moe in enumerate(model.moes()):
+            for e in range(moe.num_local_experts):
+                wgu, wd = dequantized_expert(moe, e)
+                p = f"blocks.{layer}.moe.experts.{e}."
+                want = torch.cat([expected[p + "gate.weight"], expected[p + "up.weight"]])
+                # scales are held as fp16 for the decode kernels: a relative difference of at most 2^-11
+                assert torch.allclose(wgu, want, rtol=1e-3, atol=1e-6), (bits, p)
+                assert torch.allclose(wd, expected[p + "down.weight"], rtol=1e-3, atol=1e-6), (bits, p)
+        dense = {k: v for k, v in model.state_dict().items() if ".experts." not in k}
+        assert all(torch.equal(dense[k], state[k]) for k in dense if k in state)
+        with pytest.raises(Exception):
+            load_quantized(tmp_path / "missing.pt")
