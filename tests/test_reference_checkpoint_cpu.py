@@ -3,7 +3,8 @@ module names; ``src/train_quantweave_moe.py`` checkpoint payload). The checkpoin
 ``config.json`` with only the reference's fourteen fields, a ``model.pt`` payload with per-expert
 ``experts.{e}.{gate,up,down}.weight`` tensors in ``nn.Linear`` layout, ``nn.MultiheadAttention`` packed projections
 and LayerNorms, and a character ``vocab.json`` without tokenizer metadata. The reference's ``model.int{b}.pt``
-payload (``src/quantization.py:105-117``: per-expert ``qweight``/``scales`` with fp32 scales) loads too."""
+payload (``src/quantization.py:105-117``: per-expert ``qweight``/``scales`` with fp32 scales) and its LoRA adapter
+file (``src/lora.py:86-104``: ``{state, info, base_checkpoint}`` with ``...{proj}.lora_a``/``lora_b``) load too."""
 
 import json
 
@@ -159,3 +160,29 @@ def test_a_reference_quantized_payload_loads_and_dequantizes_to_the_same_weights
         assert all(torch.equal(dense[k], state[k]) for k in dense if k in state)
         with pytest.raises(Exception):
             load_quantized(tmp_path / "missing.pt")
+
+
+def test_a_reference_lora_adapter_file_loads_and_merges_to_the_same_weights(tmp_path):
+    from quantaweave_b200.tools.lora import add_lora, load_adapter, merge_lora_state
+
+    base = _write(tmp_path)
+    rank, alpha = 4, 8.0
+    g = torch.Generator().manual_seed(3)
+    adapter, merged_want = {}, dict(base)
+    for key in [k for k in base if ".experts." in k] + ["lm_head.weight"]:
+        out_f, in_f = base[key].shape
+        a, b = torch.randn(rank, in_f, generator=g), 0.1 * torch.randn(out_f, rank, generator=g)
+        stem = key[: -len(".weight")]
+        adapter[stem + ".lora_a"], adapter[stem + ".lora_b"] = a, b  # the reference's per-projection names
+        merged_want[key] = base[key] + (alpha / rank) * (b @ a)
+    adapter["blocks.0.moe.router.weight"] = base["blocks.0.moe.router.weight"] + 0.5  # an unfrozen router
+    merged_want["blocks.0.moe.router.weight"] = adapter["blocks.0.moe.router.weight"]
+    info = {"rank": rank, "alpha": alpha, "include_lm_head": True}
+    torch.save({"state": adapter, "info": info, "base_checkpoint": str(tmp_path)}, tmp_path / "adapter.pt")
+    model = load_model(tmp_path, torch.device("cpu"))
+    add_lora(model, rank=rank, alpha=alpha, include_lm_head=True, train_router=True)
+    assert load_adapter(model, tmp_path / "adapter.pt") == info
+    merged = merge_lora_state(model)
+    assert merged.keys() == merged_want.keys()
+    for key, want in merged_want.items():
+        assert torch.allclose(merged[key], want, atol=1e-5), key
