@@ -4,7 +4,8 @@ module names; ``src/train_quantweave_moe.py`` checkpoint payload). The checkpoin
 ``experts.{e}.{gate,up,down}.weight`` tensors in ``nn.Linear`` layout, ``nn.MultiheadAttention`` packed projections
 and LayerNorms, and a character ``vocab.json`` without tokenizer metadata. The reference's ``model.int{b}.pt``
 payload (``src/quantization.py:105-117``: per-expert ``qweight``/``scales`` with fp32 scales) and its LoRA adapter
-file (``src/lora.py:86-104``: ``{state, info, base_checkpoint}`` with ``...{proj}.lora_a``/``lora_b``) load too."""
+file (``src/lora.py:86-104``: ``{state, info, base_checkpoint}`` with ``...{proj}.lora_a``/``lora_b``) load too, and
+its ``model.rank{r}.pt`` expert- and pipeline-parallel shards (``src/expert_parallel.py:396-544``) consolidate."""
 
 import json
 
@@ -186,3 +187,58 @@ def test_a_reference_lora_adapter_file_loads_and_merges_to_the_same_weights(tmp_
     assert merged.keys() == merged_want.keys()
     for key, want in merged_want.items():
         assert torch.allclose(merged[key], want, atol=1e-5), key
+
+
+def test_reference_expert_and_pipeline_shards_consolidate_into_the_full_model(tmp_path):
+    import re
+
+    from quantaweave_b200.parallel.checkpoint import consolidate_checkpoint
+    from quantaweave_b200.utils.checkpoint_io import load_checkpoint
+
+    config = {**REFERENCE_CONFIG, "num_experts": 4}
+    full = _reference_state(config)
+    expert = re.compile(r"(\.experts\.)(\d+)(\.)")
+
+    def shard(ep_rank, experts, layout):
+        state = {}
+        for key, value in full.items():
+            m = expert.search(key)
+            if m is None:
+                state[key] = value  # replicated tensors: every rank holds a copy
+            elif int(m.group(2)) in experts:  # local expert numbering on each rank
+                state[expert.sub(lambda mm: f"{mm.group(1)}{int(mm.group(2)) - experts[0]}{mm.group(3)}", key)] = value
+        payload = {"model": state, "optimizer": None, "step": 9, "rng_state": {}, "world_size": 2, "rank": ep_rank,
+                   "extra": {"note": "reference"}}
+        if layout:
+            payload["layout"] = {"kind": "ep", "ep_rank": ep_rank, "ep_size": 2, "tp_rank": 0, "tp_size": 1}
+        return payload
+
+    for with_layout in (True, False):  # older reference shards carry no "layout": expert parallelism is assumed
+        root = tmp_path / f"ep{int(with_layout)}"
+        root.mkdir()
+        (root / "config.json").write_text(json.dumps(config))
+        for rank, experts in ((0, [0, 1]), (1, [2, 3])):
+            torch.save(shard(rank, experts, with_layout), root / f"model.rank{rank}.pt")
+        consolidate_checkpoint(root, root / "merged")
+        merged = load_checkpoint(root / "merged" / "model.pt")
+        assert merged["step"] == 9 and merged["extra"] == {"note": "reference"}
+        assert merged["model"].keys() == full.keys()
+        assert all(torch.equal(merged["model"][k], full[k]) for k in full)
+    pipe = tmp_path / "pp"
+    pipe.mkdir()
+    block = re.compile(r"^blocks\.(\d+)\.")
+    for stage, (start, end) in enumerate(((0, 1), (1, 2))):
+        state = {}
+        for key, value in full.items():
+            m = block.match(key)
+            if m and start <= int(m.group(1)) < end:
+                state[f"blocks.{int(m.group(1)) - start}." + key[m.end():]] = value
+            elif not m and (key.startswith(("token_", "position_")) if stage == 0 else
+                             key.startswith(("final_norm", "lm_head"))):
+                state[key] = value
+        torch.save({"model": state, "optimizer": None, "step": 2, "rng_state": {}, "world_size": 2, "rank": stage,
+                    "layout": {"kind": "pp", "stage": stage, "stages": 2, "layer_start": start, "layer_end": end},
+                    "extra": {}}, pipe / f"model.rank{stage}.pt")
+    consolidate_checkpoint(pipe, pipe / "merged")
+    merged = load_checkpoint(pipe / "merged" / "model.pt")["model"]
+    assert merged.keys() == full.keys() and all(torch.equal(merged[k], full[k]) for k in full)
