@@ -2,16 +2,18 @@
 
 Public API (names kept from jorgenep/QuantaWeave):
 
-* model: ``QuantaWeaveConfig``, ``QuantaWeaveMoEForCausalLM``, ``TopKMoE``, ``SparseSwiGLU``;
+* model: ``QuantaWeaveConfig``, ``QuantaWeaveMoEForCausalLM``, ``QuantaWeaveBlock``, ``TopKMoE``, ``SparseSwiGLU``;
+* data: ``CharTokenizer``, ``BPETokenizer``, ``SentencePieceTokenizer``, ``load_tokenizer``;
 * training: ``run_training``, ``default_args``, ``build_parser``, ``save_checkpoint``, ``load_checkpoint``,
   ``TrainingController``, ``ScheduleConfig``, ``MetricsLogger``;
-* inference: ``FastDecoder``, ``QuantizedLinear``, ``quantize_model``;
+* inference and adaptation: ``FastDecoder``, ``QuantizedLinear``, ``quantize_model``, ``save_quantized``,
+  ``load_quantized``, ``add_lora``, ``CPUOffloadAdamW``;
 * parallelism: ``init_expert_parallel``, ``ShardedAdamW``, ``PipelineEngine``, ``consolidate_checkpoint``,
   ``reshard_checkpoint``.
 """
 
 from .config import PRESETS, QuantaWeaveConfig, preset
-from .models import QuantaWeaveMoEForCausalLM, SparseSwiGLU, TopKMoE
+from .models import QuantaWeaveBlock, QuantaWeaveMoEForCausalLM, SparseSwiGLU, TopKMoE
 
 __version__ = "0.1.0"
 
@@ -24,7 +26,15 @@ _LAZY = {
     "TrainingController": ("training.schedules", "TrainingController"),
     "ScheduleConfig": ("training.schedules", "ScheduleConfig"),
     "MetricsLogger": ("training.metrics", "MetricsLogger"),
+    "CharTokenizer": ("data.pipeline", "CharTokenizer"),
+    "BPETokenizer": ("data.pipeline", "BPETokenizer"),
+    "SentencePieceTokenizer": ("data.pipeline", "SentencePieceTokenizer"),
+    "load_tokenizer": ("data.pipeline", "load_tokenizer"),
     "FastDecoder": ("inference.fast_decode", "FastDecoder"),
+    "save_quantized": ("inference.quantization", "save_quantized"),
+    "load_quantized": ("inference.quantization", "load_quantized"),
+    "add_lora": ("tools.lora", "add_lora"),
+    "CPUOffloadAdamW": ("optim.cpu_offload", "CPUOffloadAdamW"),
     "QuantizedLinear": ("inference.quantization", "QuantizedLinear"),
     "quantize_model": ("inference.quantization", "quantize_model"),
     "init_expert_parallel": ("parallel.expert_parallel", "init_expert_parallel"),
@@ -44,5 +54,5 @@ def __getattr__(name):
     raise AttributeError(name)
 
 
-__all__ = ["PRESETS", "QuantaWeaveConfig", "preset", "QuantaWeaveMoEForCausalLM", "SparseSwiGLU", "TopKMoE",
-           *_LAZY]
+__all__ = ["PRESETS", "QuantaWeaveConfig", "preset", "QuantaWeaveBlock", "QuantaWeaveMoEForCausalLM", "SparseSwiGLU",
+           "TopKMoE", *_LAZY]

@@ -130,3 +130,11 @@ def test_the_l_preset_is_the_30b_total_1b_active_target():
 
     spec = make_spec("moe", "l")
     assert 29e9 < spec.total_params < 32e9 and 0.9e9 < spec.active_params < 1.2e9
+
+
+def test_every_public_name_resolves():
+    import quantaweave_b200 as package
+
+    for name in package.__all__:
+        assert getattr(package, name) is not None, name
+    assert {"QuantaWeaveBlock", "SparseSwiGLU", "TopKMoE", "load_tokenizer", "add_lora"} <= set(package.__all__)
