@@ -92,7 +92,13 @@ class ContinuousBatcher:
                 request = self.waiting.popleft()
             slot = free[0]
             prompt = list(request.prompt)
-            self.decoder._prefill(torch.tensor([prompt[:-1]], dtype=torch.long), first_row=slot)
+            try:
+                self.decoder._prefill(torch.tensor([prompt[:-1]], dtype=torch.long), first_row=slot)
+            except BaseException as exc:
+                # the request left the queue but never reached a slot: finish it here so its waiter returns
+                request.finish_reason = f"error: {exc}"
+                request.done.set()
+                raise
             self._position[slot] = len(prompt) - 1
             self._next_token[slot] = prompt[-1]
             self._generators[slot] = torch.Generator().manual_seed(request.seed)
@@ -159,6 +165,8 @@ class BatchingWorker:
         self._thread.start()
 
     def submit(self, request: GenerationRequest) -> GenerationRequest:
+        if self._stop.is_set():
+            raise RuntimeError("the batching worker is closed")
         self.batcher.submit(request)
         self._wake.set()
         return request
@@ -173,15 +181,20 @@ class BatchingWorker:
                 self.batcher.step()
             except BaseException as exc:  # noqa: BLE001 - fail every waiting request instead of hanging them
                 self.error = exc
-                with self.batcher.lock:
-                    stuck = list(self.batcher.active.values()) + list(self.batcher.waiting)
-                    self.batcher.active.clear()
-                    self.batcher.waiting.clear()
-                for request in stuck:
-                    request.finish_reason = f"error: {exc}"
-                    request.done.set()
+                self._fail_all(f"error: {exc}")
+
+    def _fail_all(self, reason: str) -> None:
+        with self.batcher.lock:
+            stuck = list(self.batcher.active.values()) + list(self.batcher.waiting)
+            self.batcher.active.clear()
+            self.batcher.waiting.clear()
+        for request in stuck:
+            request.finish_reason = reason
+            request.done.set()
 
     def close(self) -> None:
+        """Stop stepping; requests still queued or in flight finish with reason ``closed``."""
         self._stop.set()
         self._wake.set()
         self._thread.join(timeout=5)
+        self._fail_all("closed")

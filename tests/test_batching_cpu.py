@@ -88,3 +88,31 @@ def test_worker_thread_serves_concurrent_submitters():
         _run(model, [r])
         expected.append(r.tokens)
     assert [results[i] for i in range(len(PROMPTS))] == expected
+
+
+def test_a_failing_prefill_and_closing_the_worker_never_leave_a_request_waiting(monkeypatch):
+    import pytest
+
+    model = _model()
+    worker = BatchingWorker(ContinuousBatcher(FastDecoder(model, torch.device("cpu"), max_batch=2)))
+    original = worker.batcher.decoder._prefill
+
+    def prefill(prompts, first_row=0):
+        if 63 in prompts.tolist()[0]:
+            raise RuntimeError("bad prompt")
+        return original(prompts, first_row)
+
+    monkeypatch.setattr(worker.batcher.decoder, "_prefill", prefill)
+    bad = worker.submit(GenerationRequest([63, 1, 2], 4))
+    bad.wait(timeout=30)
+    assert bad.finish_reason.startswith("error") and "bad prompt" in bad.finish_reason
+    assert isinstance(worker.error, RuntimeError)
+    good = worker.submit(GenerationRequest([1, 2], 3))
+    assert len(good.wait(timeout=30)) == 3 and good.finish_reason == "length"  # the worker keeps serving
+    worker._stop.set()  # stop stepping first, so the next request stays queued until close
+    worker._thread.join(timeout=5)
+    queued = worker.batcher.submit(GenerationRequest([1, 2], 3))
+    worker.close()
+    assert queued.wait(timeout=1) == [] and queued.finish_reason == "closed"
+    with pytest.raises(RuntimeError, match="closed"):
+        worker.submit(GenerationRequest([1], 1))
