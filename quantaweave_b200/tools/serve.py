@@ -268,6 +268,8 @@ class Server:
         started = time.perf_counter()
         self.worker.submit(job)
         job.wait()
+        if job.finish_reason == "closed":
+            raise HTTPException(503, "the server is shutting down")
         if job.finish_reason and job.finish_reason.startswith("error"):
             raise HTTPException(500, job.finish_reason)
         text = state["text"]
