@@ -3,6 +3,12 @@
     python bench_decode.py --batch 1 --bits 4
     python bench_decode.py --batch 32 --bits 4
     python bench_decode.py --impl reference --batch 1
+    python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 bench_decode.py --batch 1
+
+Launched on N ranks, the experts are spread expert-parallel over the N GPUs (N must divide 64) and every rank
+decodes the same prompts; each MoE layer sums the ranks' partial outputs with one all-reduce. That path runs the
+PyTorch decode step (the fused single-GPU decode kernels and CUDA graph are not used); the reported time is the max
+over ranks.
 
 Config 5: the config-2 architecture (vocab 32000, d1024, 16 layers, 16 heads, 64 SwiGLU experts h2816, top-2) with
 random-init N(0, 0.02) weights, experts quantised to int4 (group 128, fp16 scales, symmetric) or int8 per-channel;
@@ -38,6 +44,8 @@ def main():
     import torch
 
     args = parse()
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        return run_expert_parallel(args)
     torch.manual_seed(args.seed)
     gen = torch.Generator().manual_seed(args.seed)
     prompts = torch.randint(0, CONFIG["vocab_size"], (args.batch, args.prompt), generator=gen)
@@ -140,3 +148,72 @@ def run_reference(args, prompts, group):
 
 if __name__ == "__main__":
     main()
+
+
+def run_expert_parallel(args):
+    """Decode with the experts sharded over the ranks of one node (``torch.distributed.run``)."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, ROOT)
+    from quantaweave_b200 import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM
+    from quantaweave_b200.inference.fast_decode import FastDecoder
+    from quantaweave_b200.inference.quantization import quantize_model
+    from quantaweave_b200.parallel.expert_parallel import broadcast_shared_parameters, init_expert_parallel
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dist.init_process_group("nccl", timeout=timedelta(seconds=float(os.environ.get("QW_PG_TIMEOUT_S", "300"))),
+                            device_id=torch.device("cuda", local))
+    try:
+        ep = init_expert_parallel("cuda", 1, transport="nccl")
+        group = 128 if args.bits == 4 else None
+        prompts = torch.randint(0, CONFIG["vocab_size"], (args.batch, args.prompt),
+                                generator=torch.Generator().manual_seed(args.seed))  # the same prompts on every rank
+        cfg = QuantaWeaveConfig(**CONFIG, max_sequence_length=args.prompt + max(args.new, 8) + 1,
+                                norm_type="layernorm", position_embedding="learned", attention_bias=True,
+                                init_std=0.02)
+        torch.manual_seed(args.seed + ep.rank)
+        with torch.device("cuda"):
+            model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ep).eval()
+        broadcast_shared_parameters(model, ep)
+        if args.bits != 16:
+            quantize_model(model, args.bits, group)  # this rank's experts
+        dec = FastDecoder(model, torch.device("cuda"), max_batch=args.batch)
+        prompts = prompts.cuda()
+        dec.generate(prompts, 8)  # warm-up
+        dist.barrier()
+        torch.cuda.synchronize()
+        start, mid = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        dec._prefill(prompts[:, :-1])
+        mid.record()
+        token = prompts[:, -1]
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(args.new + 1)]
+        events[0].record()
+        for i in range(args.new):
+            pos = torch.full((args.batch,), args.prompt - 1 + i, dtype=torch.int32, device="cuda")
+            token = dec.run_step(token, pos).argmax(-1)
+            events[i + 1].record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        timing = torch.tensor([events[0].elapsed_time(events[-1]), start.elapsed_time(mid)], device="cuda")
+        dist.all_reduce(timing, op=dist.ReduceOp.MAX)
+        step_ms = [events[i].elapsed_time(events[i + 1]) for i in range(args.new)]
+        if ep.rank == 0:
+            decode_ms, prefill_ms = (float(v) for v in timing)
+            print(json.dumps({
+                "metric": "int4 decode tokens/sec" if args.bits == 4 else f"int{args.bits} decode tokens/sec",
+                "value": args.batch * args.new / (decode_ms / 1000.0), "unit": "tokens/s", "n_gpus": ep.world_size,
+                "batch": args.batch, "prompt": args.prompt, "new_tokens": args.new,
+                "p50_token_latency_ms": statistics.median(step_ms), "prefill_ms": prefill_ms,
+                "higher_is_better": True, "impl": "native", "parallelism": f"ep{ep.world_size} (SPMD, all-reduce "
+                "of the MoE partial outputs per layer, PyTorch decode step)",
+                "weights": f"int{args.bits}" + (f" g{group} fp16 scales" if args.bits == 4 else
+                                                " per-channel" if args.bits == 8 else " bf16"),
+                "data": "synthetic seeded uniform prompt, random-init N(0,0.02) weights"}), flush=True)
+    finally:
+        dist.destroy_process_group()

@@ -141,9 +141,15 @@ def dequantized_expert(moe, index: int) -> tuple[Tensor, Tensor]:
 
 
 def quantize_model(model, bits: int = 8, group_size: Optional[int] = None, quantize_lm_head: bool = False) -> dict:
-    """Quantise every expert (and optionally the LM head) in place. Returns size statistics."""
-    if getattr(model, "expert_parallel", None) is not None:
-        raise ValueError("consolidate an expert-parallel model before quantizing it")
+    """Quantise every expert (and optionally the LM head) in place. Returns size statistics.
+
+    An expert-parallel model quantises the experts it holds (each row is quantised on its own, so a rank's experts
+    come out exactly as they would in the consolidated model); this serves expert-parallel decoding. Such a model
+    cannot be saved as a quantised file, which must hold every expert (``save_quantized``)."""
+    ep = getattr(model, "expert_parallel", None)
+    if ep is not None and getattr(ep, "tp_size", 1) > 1:
+        raise ValueError("tensor-parallel experts hold slices of each weight; consolidate the model before "
+                         "quantizing it")
     before = after = replaced = 0
     for block in model.blocks:
         b, a = quantize_moe(block.moe, bits, group_size)
@@ -163,6 +169,9 @@ def quantize_model(model, bits: int = 8, group_size: Optional[int] = None, quant
 
 
 def save_quantized(model, path: Path, stats: dict, quantize_lm_head: bool = False) -> None:
+    if getattr(model, "expert_parallel", None) is not None:
+        raise ValueError("a quantised file holds every expert: consolidate the expert-parallel model, then quantize "
+                         "and save it")
     torch.save({"config": dict(model.config.__dict__), "bits": stats["bits"], "group_size": stats["group_size"],
                 "quantize_lm_head": quantize_lm_head, "state_dict": model.state_dict()}, path)
 
