@@ -217,9 +217,10 @@ class Server:
         if self.max_queue is not None and batcher.pending() >= batcher.slots + self.max_queue:
             raise HTTPException(429, f"too many requests already queued (max {self.max_queue})")
 
-    def _batched(self, request: GenerateRequest, on_text=None) -> dict:
+    def _batched(self, request: GenerateRequest, on_text=None, handle: Optional[list] = None) -> dict:
         """One completion through the continuous batcher: the same prompt handling, stop strings (with hold-back
-        when streaming), EOS and reply fields as ``ChatSession.send`` in complete mode."""
+        when streaming), EOS and reply fields as ``ChatSession.send`` in complete mode. ``handle`` (a list) receives
+        the queued job, so a caller whose client went away can cancel it."""
         import random
 
         from fastapi import HTTPException
@@ -265,6 +266,8 @@ class Server:
                     state["emitted"] = safe
 
         job.on_token = on_token
+        if handle is not None:
+            handle.append(job)
         started = time.perf_counter()
         self.worker.submit(job)
         job.wait()
@@ -375,8 +378,9 @@ class Server:
             self._admit_batched()
             queue: asyncio.Queue = asyncio.Queue()
             loop = asyncio.get_running_loop()
+            handle: list = []
             task = asyncio.ensure_future(asyncio.to_thread(
-                self._batched, request, lambda piece: loop.call_soon_threadsafe(queue.put_nowait, piece)))
+                self._batched, request, lambda piece: loop.call_soon_threadsafe(queue.put_nowait, piece), handle))
             try:
                 while not (task.done() and queue.empty()):
                     try:
@@ -386,7 +390,9 @@ class Server:
                     yield f"data: {json.dumps({'text': item})}\n\n"
                 payload = await task
             finally:
-                if not task.done():
+                if not task.done():  # the client went away mid-stream: retire its job at the next decode step
+                    for job in handle:
+                        job.cancelled = True
                     task.cancel()
             self.requests_served += 1
             self.metrics.tokens_generated_total += payload["tokens"]

@@ -116,3 +116,34 @@ def test_a_failing_prefill_and_closing_the_worker_never_leave_a_request_waiting(
     assert queued.wait(timeout=1) == [] and queued.finish_reason == "closed"
     with pytest.raises(RuntimeError, match="closed"):
         worker.submit(GenerationRequest([1], 1))
+
+
+def test_a_stream_closed_early_cancels_its_batched_job(tmp_path):
+    import asyncio
+    import time
+
+    from test_tools_cpu import _train
+
+    from quantaweave_b200.tools.serve import GenerateRequest, Server
+
+    _train(tmp_path, steps=1)
+    server = Server(tmp_path / "out", None, torch.device("cpu"), "fp32", batching=2)
+    jobs = []
+    submit = server.worker.submit
+    server.worker.submit = lambda job: jobs.append(job) or submit(job)
+    try:
+        async def first_piece_then_leave():
+            stream = server.stream_generate(GenerateRequest(prompt="the", tokens=60, temperature=0.0, stop=[]))
+            async for _ in stream:
+                break  # the client disconnects after the first event
+            await stream.aclose()
+
+        asyncio.run(first_piece_then_leave())
+        deadline = time.time() + 10
+        while server.worker.batcher.pending() and time.time() < deadline:
+            time.sleep(0.02)
+        assert server.worker.batcher.pending() == 0
+        assert jobs[0].done.is_set() and jobs[0].cancelled
+        assert len(jobs[0].tokens) < jobs[0].max_new  # retired early, not decoded to its budget
+    finally:
+        server.close()
