@@ -78,6 +78,17 @@ class ContinuousBatcher:
             self.waiting.append(request)
         return request
 
+    def withdraw(self, request: GenerationRequest) -> bool:
+        """Take a request that has not reached a slot yet back out of the queue; False once it is decoding."""
+        with self.lock:
+            try:
+                self.waiting.remove(request)
+            except ValueError:
+                return False
+        request.finish_reason = "withdrawn"
+        request.done.set()
+        return True
+
     def pending(self) -> int:
         with self.lock:
             return len(self.waiting) + len(self.active)

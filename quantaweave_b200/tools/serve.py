@@ -270,6 +270,10 @@ class Server:
             handle.append(job)
         started = time.perf_counter()
         self.worker.submit(job)
+        if self.request_timeout is not None and not job.done.wait(self.request_timeout):
+            if self.worker.batcher.withdraw(job):  # still queued behind busy slots after the start timeout
+                raise HTTPException(503, f"timed out after {self.request_timeout}s waiting to start "
+                                         "(every decode slot is busy)")
         job.wait()
         if job.finish_reason == "closed":
             raise HTTPException(503, "the server is shutting down")

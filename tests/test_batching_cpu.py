@@ -147,3 +147,35 @@ def test_a_stream_closed_early_cancels_its_batched_job(tmp_path):
         assert len(jobs[0].tokens) < jobs[0].max_new  # retired early, not decoded to its budget
     finally:
         server.close()
+
+
+def test_queued_requests_can_be_withdrawn_and_the_server_times_out_waiting_ones(tmp_path):
+    import asyncio
+    import time
+
+    import pytest
+    from fastapi import HTTPException
+    from test_tools_cpu import _train
+
+    from quantaweave_b200.tools.serve import GenerateRequest, Server
+
+    batcher = ContinuousBatcher(FastDecoder(_model(), torch.device("cpu"), max_batch=1))
+    first, second = GenerationRequest([1, 2], 3), GenerationRequest([3], 3)
+    batcher.submit(first)
+    batcher.submit(second)
+    batcher.step()  # `first` holds the only slot
+    assert batcher.withdraw(second) and second.finish_reason == "withdrawn" and second.done.is_set()
+    assert not batcher.withdraw(first)  # already decoding: it runs to the end
+    batcher.run_until_idle()
+    assert first.finish_reason == "length"
+
+    _train(tmp_path, steps=1)
+    server = Server(tmp_path / "out", None, torch.device("cpu"), "fp32", batching=1, request_timeout=0.2)
+    try:
+        # a worker whose slots never free up: every step makes no progress, so requests stay queued
+        server.worker.batcher.step = lambda: time.sleep(0.01)
+        with pytest.raises(HTTPException) as waited:
+            asyncio.run(server.generate(GenerateRequest(prompt="the", tokens=2, temperature=0.0)))
+        assert waited.value.status_code == 503 and server.worker.batcher.pending() == 0
+    finally:
+        server.close()
