@@ -296,7 +296,8 @@ class Server:
                 "context_length": s.model.config.max_sequence_length - 1,
                 "uptime_seconds": time.time() - self.started_at, "requests_served": self.requests_served,
                 "auth_required": self.api_key is not None, "rate_limit": self.rate_limiter.limit,
-                "request_timeout": self.request_timeout, "max_queue": self.max_queue}
+                "request_timeout": self.request_timeout, "max_queue": self.max_queue,
+                "batching_slots": self.worker.batcher.slots if self.worker is not None else 0}
 
     async def _acquire(self) -> None:
         """Take the generation lock. A request that finds it free always proceeds (even ``max_queue=0``); one that

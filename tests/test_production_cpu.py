@@ -250,4 +250,4 @@ def test_health_reports_the_hardening_configuration(checkpoint):
         "/health").json()
     assert info["status"] == "ok" and info["auth_required"] is True
     assert (info["rate_limit"], info["request_timeout"], info["max_queue"]) == (5, 2.5, 3)
-    assert info["context_length"] > 0 and "KV cache" in info["decoding"]
+    assert info["context_length"] > 0 and "KV cache" in info["decoding"] and info["batching_slots"] == 0
