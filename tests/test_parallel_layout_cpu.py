@@ -154,3 +154,24 @@ def test_pipeline_training_resumes_exactly_and_consolidates(tmp_path):
     assert all(torch.equal(a[k], b[k]) for k in a)
     config = QuantaWeaveConfig.load(tmp_path / "straight" / "out" / "config.json")
     QuantaWeaveMoEForCausalLM(config).load_state_dict(a)  # every layer, one plain model
+
+
+def test_the_pipeline_engine_checks_its_schedule_and_micro_batches():
+    from quantaweave_b200.parallel.pipeline_parallel import PipelineContext, PipelineEngine
+
+    ctx = PipelineContext(0, 1, torch.device("cpu"), 0, 2, False, 0, 1, None, None)
+    model = QuantaWeaveMoEForCausalLM(_config())
+    with pytest.raises(ValueError, match="schedule"):
+        PipelineEngine(model, ctx, 2, schedule="zigzag")
+    with pytest.raises(ValueError, match="microbatches"):
+        PipelineEngine(model, ctx, 0)
+
+
+def test_1f1b_training_runs_repeated_steps_and_resumes_exactly(tmp_path):
+    extra = {"pipeline_parallel": True, "expert_parallel": False, "microbatches": 2, "pipeline_schedule": "1f1b"}
+    run_ranks(_trainer_case, 2, (str(tmp_path / "straight"), 5, extra))
+    run_ranks(_trainer_case, 2, (str(tmp_path / "split"), 2, extra))
+    run_ranks(_trainer_case, 2, (str(tmp_path / "split"), 5, extra))
+    a = _weights(tmp_path / "straight" / "out" / "model.pt")
+    b = _weights(tmp_path / "split" / "out" / "model.pt")
+    assert all(torch.equal(a[k], b[k]) for k in a)
