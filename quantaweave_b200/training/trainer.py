@@ -136,6 +136,35 @@ def select_device(requested: str) -> torch.device:
     return torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
 
 
+class StepScalars:
+    """Per-step scalars (loss, aux, dropped, overflow, domain loss, overflow fraction) held on the device until a
+    flush point, so steps between logging, controller and checkpoint steps never wait for the device (survey
+    collective C12: device-side accumulation, the host reads at log intervals only)."""
+
+    COLUMNS = 6
+    REDUCED = (0, 5)  # loss and overflow fraction are averaged over the ranks that saw different tokens
+
+    def __init__(self) -> None:
+        self.rows: list = []
+
+    def push(self, step: int, values: torch.Tensor, reduce: bool) -> None:
+        self.rows.append((step, values, reduce))
+
+    def flush(self, mean_over_ranks) -> list:
+        """[(step, [6 floats])] in step order, with one device->host copy and at most one collective."""
+        if not self.rows:
+            return []
+        stacked = torch.stack([v.to(self.rows[0][1].device) for _, v, _ in self.rows]).cpu().tolist()
+        pick = [(i, c) for i, (_, _, reduce) in enumerate(self.rows) if reduce for c in self.REDUCED]
+        if pick:
+            averaged = mean_over_ranks([stacked[i][c] for i, c in pick])
+            for (i, c), value in zip(pick, averaged):
+                stacked[i][c] = value
+        out = [(step, row) for (step, _, _), row in zip(self.rows, stacked)]
+        self.rows.clear()
+        return out
+
+
 def autocast_context(device: torch.device, precision: str = "auto"):
     """CPU: optional bf16 autocast of the oracle path. CUDA: the native kernels choose their own dtypes (bf16
     operands, fp32 accumulation), so no autocast region is opened."""
@@ -742,6 +771,18 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
     model.train()
     optimizer.zero_grad(set_to_none=True)
     routes_per_step = args.batch_size * args.sequence_length * config.layers * config.top_k
+    scalars = StepScalars()
+
+    def mean_over_ranks(values: list) -> list:
+        """Average loss and overflow fraction over the ranks that saw different tokens (one collective per flush;
+        every rank flushes at the same steps)."""
+        if ctx is not None and ep is not None:
+            from ..parallel.expert_parallel import all_reduce_mean
+
+            return all_reduce_mean(values, ep)
+        if dp is not None:
+            return dp.all_reduce_mean(values)
+        return values
     window_metrics = {"imbalance": None, "active_fraction": None}
     pending_tokens = 0
     last_log: dict = {}
@@ -755,12 +796,14 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
         grad_norm = None
         if engine is not None:
             result = engine.train_step(batch)
-            loss_value, aux_value = result["loss"], result["router_aux_loss"]
-            dropped_value, overflow_value, domain_value = result["dropped_routes"], result["overflow_routes"], 0.0
             grad_norm = engine.clip_and_sync(optimizer, args.max_grad_norm)
             optimizer.step()
             optimizer.zero_grad(set_to_none=True)
-            overflow_fraction = overflow_value / max(1, routes_per_step)
+            # the engine has already reduced these over the pipeline (host values): nothing left to all-reduce
+            scalars.push(step, torch.tensor([result["loss"], result["router_aux_loss"], result["dropped_routes"],
+                                             result["overflow_routes"], 0.0,
+                                             result["overflow_routes"] / max(1, routes_per_step)],
+                                            dtype=torch.float64), reduce=False)
         else:
             with autocast(), nvtx_range("forward"):
                 out = model(batch, labels=batch, domain_ids=domain_ids,
@@ -790,20 +833,21 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
                     else:
                         optimizer.step()
                     optimizer.zero_grad(set_to_none=True)
-            loss_value = float(loss.item())
-            aux_value = float(out["router_aux_loss"].item())
-            dropped_value, overflow_value = int(out["dropped_routes"].item()), int(out["overflow_routes"].item())
-            domain_value = float(out["domain_loss"].item())
-            overflow_fraction = overflow_value / max(1, routes_per_step)
-            if ctx is not None and ep is not None:
-                from ..parallel.expert_parallel import all_reduce_mean
-
-                loss_value, overflow_fraction = all_reduce_mean([loss_value, overflow_fraction], ep)
-            elif dp is not None:
-                loss_value, overflow_fraction = dp.all_reduce_mean([loss_value, overflow_fraction])
+            # kept on the device: read back (and averaged over ranks) in one transfer at the next flush point
+            overflow = out["overflow_routes"].detach().double()
+            scalars.push(step, torch.stack([loss.detach().double(), out["router_aux_loss"].detach().double(),
+                                            out["dropped_routes"].detach().double(), overflow,
+                                            out["domain_loss"].detach().double(),
+                                            overflow / max(1, routes_per_step)]), reduce=True)
         device_metrics = tracker.update(step) if tracker is not None else None
-        controller.observe(loss_value, overflow_fraction)
         pending_tokens += args.batch_size * args.sequence_length * data_world
+        flush_now = (step % args.log_interval == 0 or step == args.steps or controller.should_update(step)
+                     or (args.checkpoint_interval > 0 and step % args.checkpoint_interval == 0))
+        if flush_now:
+            for _, (loss_value, aux_value, dropped, overflow_count, domain_value, overflow_fraction) in \
+                    scalars.flush(mean_over_ranks):
+                controller.observe(loss_value, overflow_fraction)
+            dropped_value, overflow_value = int(dropped), int(overflow_count)
         if tracker is not None and collect:
             util = tracker.gather_expert_utilization()
             if monitor is not None:

@@ -129,3 +129,25 @@ def test_the_expert_suggestion_grows_with_memory_and_respects_its_cap():
 
     assert 2 <= suggest(1) <= suggest(4) <= suggest(16) and suggest(1) < suggest(16)
     assert suggest(1000, cap=32) == 32
+
+
+def test_step_values_are_read_back_only_at_flush_points_with_the_same_results(tmp_path, monkeypatch):
+    from quantaweave_b200.training import trainer
+
+    every = run_training(_args(tmp_path / "every", steps=10, log_interval=1, metrics_file=tmp_path / "a.jsonl"))
+    flushes = []
+    original = trainer.StepScalars.flush
+
+    def counting(self, reduce):
+        flushes.append([step for step, _, _ in self.rows])
+        return original(self, reduce)
+
+    monkeypatch.setattr(trainer.StepScalars, "flush", counting)
+    sparse = run_training(_args(tmp_path / "sparse", steps=10, log_interval=5, controller_interval=50,
+                                metrics_file=tmp_path / "b.jsonl"))
+    assert flushes == [[1, 2, 3, 4, 5], [6, 7, 8, 9, 10]]  # two transfers instead of ten
+    dense_rows = {r["step"]: r for r in map(json.loads, (tmp_path / "a.jsonl").read_text().splitlines())}
+    for row in map(json.loads, (tmp_path / "b.jsonl").read_text().splitlines()):
+        assert row["loss"] == dense_rows[row["step"]]["loss"]
+        assert row["overflow_routes"] == dense_rows[row["step"]]["overflow_routes"]
+    assert sparse["last_log"]["loss"] == every["last_log"]["loss"]  # (final_loss averages the logged tail)
