@@ -251,3 +251,27 @@ def test_health_reports_the_hardening_configuration(checkpoint):
     assert info["status"] == "ok" and info["auth_required"] is True
     assert (info["rate_limit"], info["request_timeout"], info["max_queue"]) == (5, 2.5, 3)
     assert info["context_length"] > 0 and "KV cache" in info["decoding"] and info["batching_slots"] == 0
+
+
+def test_generate_matches_the_chat_session_and_concurrent_requests_never_mix(checkpoint):
+    from quantaweave_b200.tools.chat import ChatSession, Settings, load_for_chat
+    from quantaweave_b200.tools.serve import GenerateRequest
+
+    server = _server(checkpoint)
+    model, tokenizer = load_for_chat(checkpoint, None, 0, torch.device("cpu"))
+    session = ChatSession(model, tokenizer, torch.device("cpu"), "fp32", Settings(temperature=0.0, tokens=8))
+    prompts = ["the cat", "a dog", "numbers 1", "sun and"]
+    expected = [session.send(p).response for p in prompts]
+    single = asyncio.run(server.generate(GenerateRequest(prompt=prompts[0], tokens=8, temperature=0.0)))
+    assert single["text"] == expected[0]
+
+    async def together():
+        return await asyncio.gather(*(server.generate(GenerateRequest(prompt=p, tokens=8, temperature=0.0))
+                                      for p in prompts))
+
+    replies = asyncio.run(together())  # serialised behind the lock, each on a fresh decoder state
+    assert [r["text"] for r in replies] == expected
+    with pytest.raises(Exception):
+        GenerateRequest(prompt="x", tokens=0)  # validated before it reaches the model
+    with pytest.raises(Exception):
+        GenerateRequest(prompt="x", temperature=-1)
