@@ -251,6 +251,101 @@ def diff_fields(saved: dict, current: dict) -> dict:
 
 
 # ------------------------------------------------------------------------------------------ CLI
+# Help text of every trainer option, attached in ``build_parser`` (defaults are appended there).
+_HELP = {
+    "data": "JSONL training files (one text per row, optional \"domain\"); several files: the file stem is the domain",
+    "zipf_s": "exponent of the Zipf distribution of --synthetic-data zipf",
+    "tokenizer": "character tokenizer, or a byte-level BPE / SentencePiece tokenizer trained at --tokenizer-path",
+    "tokenizer_path": "directory of the BPE/SentencePiece tokenizer: reused if present, otherwise trained and saved",
+    "tokenizer_algorithm": "SentencePiece model type",
+    "examples": "rows read from each data file; later rows stay unseen (held-out benchmark in the run archive)",
+    "redact_pii": "replace e-mail addresses, phone, SSN and card numbers and IPv4 addresses before tokenising",
+    "sequence_length": "tokens per training window (the model gets one more position for the shifted labels)",
+    "vocab_size": "vocabulary size (character tokenizer: at least the characters seen; BPE/SentencePiece target)",
+    "curriculum": "order windows from easy to hard by this difficulty score",
+    "curriculum_steps": "steps over which the curriculum widens from --curriculum-start-fraction to all windows",
+    "curriculum_start_fraction": "share of the easiest windows drawn from at step 0",
+    "domain_weights": "sampling weights per domain, e.g. \"prose=3,code=1\" (default: proportional to size)",
+    "domain_weights_end": "weights reached after --domain-weights-steps (linear blend)",
+    "domain_weights_steps": "steps of the blend from --domain-weights to --domain-weights-end",
+    "domain_specialization_coef": "weight of the loss that pushes different domains onto different experts",
+    "val_fraction": "hold out this share of each domain's windows for validation",
+    "val_interval": "steps between validation passes",
+    "val_batches": "batches per validation pass",
+    "val_seed": "seed of the validation split and batches",
+    "auto_architecture": "pick hidden size, layers, FFN width and experts to fill part of this device's memory",
+    "auto_architecture_quality": "capacity: many experts, one active; balanced: a moderate pool, two active; "
+                                 "dense: one expert",
+    "auto_architecture_memory_fraction": "share of device memory the training state may fill",
+    "hidden_size": "model width", "layers": "transformer blocks", "ffn_size": "hidden width of each SwiGLU expert",
+    "attention_heads": "query heads",
+    "norm_type": "normalisation", "position_embedding": "learned absolute positions or rotary embeddings",
+    "attention_bias": "biases on the QKV and output projections",
+    "total_experts": "experts per MoE layer", "active_experts": "experts each token is routed to (top-k)",
+    "capacity_factor": "per-expert capacity = capacity_factor x tokens x k / experts (0: unlimited)",
+    "min_expert_capacity": "lower bound of the per-expert capacity",
+    "drop_overflow_tokens": "enforce the capacity (off: every route reaches its expert)",
+    "overflow_policy": "drop: routes over capacity contribute nothing and are reported as dropped; residual: they "
+                       "are skipped the same way (the residual stream carries the token) but not counted as dropped",
+    "router_temperature": "softmax temperature of the router",
+    "router_aux_coef": "weight of the load-balancing auxiliary loss",
+    "steps": "optimizer steps to train to (a resumed run continues up to this step)",
+    "schedule_steps": "length of the learning-rate schedule (default: --steps)",
+    "batch_size": "sequences per step (per data-parallel group)",
+    "gradient_accumulation_steps": "micro-steps accumulated before each optimizer step",
+    "lr": "peak learning rate", "adam_beta1": "AdamW beta1", "adam_beta2": "AdamW beta2",
+    "weight_decay": "AdamW decoupled weight decay", "max_grad_norm": "clip the global gradient norm to this value",
+    "warmup_steps": "linear warm-up steps", "lr_decay": "decay after warm-up, down to --min-lr-ratio x --lr",
+    "min_lr_ratio": "floor of the decayed learning rate, as a share of --lr",
+    "plateau_patience": "controller intervals without improvement before the learning rate is reduced (0: off)",
+    "aux_coef_end": "anneal the aux-loss weight linearly to this value over the schedule",
+    "aux_adapt": "raise the aux-loss weight while routing is imbalanced, lower it when balanced",
+    "capacity_adapt": "grow the capacity factor while routes are dropped, shrink it otherwise",
+    "capacity_min": "lower bound of the adapted capacity factor", "capacity_max": "upper bound of it",
+    "drop_threshold": "dropped-route share above which the capacity grows",
+    "capacity_release_step": "stop enforcing the capacity from this step (0: never)",
+    "temperature_start": "router temperature at step 0, annealed to --router-temperature",
+    "temperature_steps": "steps of the router-temperature anneal",
+    "temperature_adapt": "warm the router temperature while experts sit idle",
+    "controller_interval": "steps between closed-loop controller updates",
+    "optimizer": "AdamW (fused sm_100a kernel on CUDA), with 8-bit moments, or with moments in host memory",
+    "device": "where to train (auto: CUDA when available)",
+    "precision": "compute precision (CUDA: bf16 operands with fp32 accumulation and fp32 master weights)",
+    "activation_checkpointing": "recompute each block's activations in backward to save memory",
+    "auto_batch_size": "probe the largest batch that fits (optimizer state included) before training",
+    "auto_batch_target": "use the smallest probed batch within this share of the best throughput (0: largest)",
+    "expert_parallel": "shard the experts over the ranks of torchrun (replicated layers are averaged)",
+    "tensor_parallel": "split each attention layer (and expert FFN) over this many ranks",
+    "pipeline_parallel": "split the layers into contiguous stages, one per rank",
+    "microbatches": "micro-batches per pipeline step",
+    "pipeline_schedule": "GPipe (all forwards, then all backwards) or 1F1B",
+    "shard_optimizer": "ZeRO-style: each rank keeps the AdamW state of its share of the replicated parameters",
+    "straggler_routing": "bias routing away from ranks whose experts run slower",
+    "straggler_capacity": "scale each rank's expert capacity by its measured speed",
+    "straggler_capacity_min": "lower bound of the per-rank capacity scale",
+    "straggler_capacity_max": "upper bound of the per-rank capacity scale",
+    "straggler_strength": "gain of the routing-bias controller", "straggler_max_bias": "bound of the routing bias",
+    "straggler_interval": "steps between straggler measurements",
+    "device_metrics": "log per-rank expert time and row imbalance",
+    "seed": "seed of the initialisation and of the batch order",
+    "output": "directory of the final model (model.pt, config.json, tokenizer)",
+    "checkpoint_dir": "directory of the resumable checkpoint",
+    "checkpoint_interval": "steps between checkpoints (0: only at the end)",
+    "resume": "continue from --checkpoint-dir when it holds a checkpoint of the same run configuration",
+    "allow_config_change": "resume even if the run configuration changed",
+    "metrics_file": "append one JSON line of metrics per logged step",
+    "electricity_rate_usd_kwh": "price used for the energy cost in the metrics",
+    "no_power_tracking": "do not read GPU energy counters",
+    "log_interval": "steps between metric reads and log lines (values are read back from the device only then)",
+    "diagnostics_dir": "write routing diagnostics (snapshots, SVG charts, index.html) here",
+    "diagnostics_interval": "steps between routing snapshots (0: off unless a controller needs them)",
+    "archive_dir": "archive the finished run (weights, data manifest, benchmarks, reproduce.sh) under this folder",
+    "no_archive": "do not archive the run", "archive_data_limit_mb": "copy the data into the archive up to this size",
+    "archive_benchmark_examples": "rows per benchmark in the archive",
+    "data_card": "JSON describing the data's source, licence and provenance, embedded in the archive manifest",
+}
+
+
 def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     data = p.add_argument_group("data")
@@ -375,6 +470,13 @@ def build_parser() -> argparse.ArgumentParser:
     io.add_argument("--archive-data-limit-mb", type=float, default=200.0)
     io.add_argument("--archive-benchmark-examples", type=int, default=500)
     io.add_argument("--data-card", type=Path)
+    for action in p._actions:
+        if action.help is None and action.dest in _HELP:
+            default = action.default
+            shown = "" if default in (None, False) or isinstance(default, bool) else f" (default: {default})"
+            if isinstance(default, list):
+                shown = " (default: " + " ".join(map(str, default)) + ")"
+            action.help = _HELP[action.dest] + shown
     return p
 
 
