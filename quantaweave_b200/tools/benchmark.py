@@ -65,6 +65,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--output", type=Path, help="JSON report path; a .md report is written beside it")
     p.add_argument("--training-metrics", type=Path, help="metrics.jsonl from training, for stability metrics")
     p.add_argument("--no-routing-stats", action="store_true", help="skip the routing/compute diagnostic pass")
+    from .common import describe_options
+
+    describe_options(p)
     return p
 
 

@@ -428,6 +428,9 @@ def build_parser() -> argparse.ArgumentParser:
     g.add_argument("--no-cache", action="store_true", help="plain forward pass per token instead of the KV cache")
     g.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")
     g.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
+    from .common import describe_options
+
+    describe_options(p)
     return p
 
 

@@ -45,3 +45,52 @@ def load_model(directory: Path, device: torch.device, precision: str = "auto", w
 def synchronize(device: torch.device) -> None:
     if device.type == "cuda":
         torch.cuda.synchronize(device)
+
+
+# Help text shared by the command-line tools, by option name; ``describe_options`` attaches it (with the default).
+OPTION_HELP = {
+    "checkpoint": "checkpoint directory (model.pt, config.json, tokenizer files)",
+    "student": "checkpoint directory of the student model",
+    "teacher_data": "JSONL text the student is distilled on",
+    "data": "JSONL rows to read",
+    "output": "directory written with the result",
+    "checkpoint_dir": "directory of the resumable checkpoint",
+    "runs_dir": "folder of archived runs (searched by --run and --latest)",
+    "mode": "complete: continue the text; chat: User/Assistant turns with history",
+    "top_k": "sample only from the k most likely tokens (0: off)",
+    "top_p": "sample only from the smallest set of tokens whose probability reaches p (1: off)",
+    "temperature": "sampling temperature (0: greedy)",
+    "prompt": "text to continue",
+    "tokens": "tokens to generate",
+    "precision": "compute precision (auto: bf16 on CUDA, fp32 on CPU)",
+    "device": "where to run (auto: CUDA when available)",
+    "host": "interface to listen on",
+    "port": "TCP port",
+    "rate_limit_window": "seconds of the --rate-limit sliding window",
+    "log_format": "request log lines as text or one JSON object per line",
+    "group_size": "quantisation group size (default: per row for int8, 32 for int4)",
+    "rank": "LoRA rank",
+    "alpha": "LoRA scaling numerator (the update is scaled by alpha / rank)",
+    "include_lm_head": "also adapt the LM head",
+    "train_router": "also train the routers",
+    "train_norms": "also train the normalisation weights",
+    "optimizer": "AdamW, or AdamW with 8-bit moments (CUDA)",
+    "steps": "optimizer steps",
+    "checkpoint_interval": "steps between checkpoints (0: only at the end)",
+    "batch_size": "sequences per step",
+    "sequence_length": "tokens per training window",
+    "examples": "rows read from each data file",
+    "lr": "learning rate",
+    "seed": "random seed",
+    "resume": "continue from --checkpoint-dir when it holds a checkpoint",
+}
+
+
+def describe_options(parser, extra: dict | None = None) -> None:
+    """Give every option of ``parser`` that has no help text the shared (or ``extra``) description."""
+    table = {**OPTION_HELP, **(extra or {})}
+    for action in parser._actions:
+        if action.help is None and action.dest in table:
+            default = action.default
+            shown = "" if default in (None, False) or isinstance(default, bool) else f" (default: {default})"
+            action.help = table[action.dest] + shown

@@ -67,6 +67,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
     p.add_argument("--resume", action=argparse.BooleanOptionalAction, default=True)
     add_archive_arguments(p)
+    from .common import describe_options
+
+    describe_options(p)
     return p
 
 

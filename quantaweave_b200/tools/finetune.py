@@ -91,6 +91,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")
     p.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
     add_archive_arguments(p)
+    from .common import describe_options
+
+    describe_options(p)
     return p
 
 

@@ -42,6 +42,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--temperature", type=float, default=0.8)
     p.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")
     p.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
+    from .common import describe_options
+
+    describe_options(p)
     return p
 
 

@@ -526,6 +526,9 @@ def build_parser() -> argparse.ArgumentParser:
     h.add_argument("--max-queue", type=int, help="429 once this many requests are already waiting to start")
     h.add_argument("--moderation-blocklist", type=Path, help="regex patterns (one per line); a match is a 422")
     h.add_argument("--log-format", choices=("text", "json"), default="text")
+    from .common import describe_options
+
+    describe_options(p)
     return p
 
 

@@ -123,3 +123,16 @@ def test_reference_helper_names(tmp_path):
         raise AssertionError("expected Unsupported")
     except Unsupported:
         pass
+
+
+def test_every_command_line_option_is_documented():
+    import importlib
+
+    from quantaweave_b200.training.trainer import build_parser as train_parser
+
+    parsers = {"train": train_parser()}
+    for name in ("chat", "serve", "finetune", "distill", "benchmark", "generate"):
+        parsers[name] = importlib.import_module(f"quantaweave_b200.tools.{name}").build_parser()
+    for name, parser in parsers.items():
+        bare = [a.option_strings[-1] for a in parser._actions if a.option_strings and a.dest != "help" and not a.help]
+        assert not bare, (name, bare)
