@@ -1,4 +1,4 @@
-"""Headline benchmark: MoE training tokens/sec on N GPUs of one node.
+"""Headline benchmark: MoE training tokens/sec (benchmark configuration 2) on N GPUs of one node.
 
     python bench.py --gpus 1 --steps 10 --warmup 3
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
@@ -233,7 +233,7 @@ def run_native(args, rank, world, local):
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None, "dtype": "bf16",
         "data": "synthetic: seeded Zipf(1.1) token ids, random-init N(0,0.02) weights",
-        "config": {"model": "moe-1b-e64 (BASELINE config 2: vocab 32000, d1024, 16 layers, 16 heads, 64 experts "
+        "config": {"model": "moe-1b-e64 (benchmark configuration 2: vocab 32000, d1024, 16 layers, 16 heads, 64 experts "
                             "h2816, top2, cf1.25; reference layout: LayerNorm, learned positions, biased MHA)"
                             if args.layers == 16 else
                             f"DEBUG {args.layers}-layer variant of config 2",

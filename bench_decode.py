@@ -1,4 +1,4 @@
-"""Second headline metric: int4 weight-only MoE decode tokens/sec on one B200.
+"""Second headline metric: int4 weight-only MoE decode tokens/sec (benchmark configuration 5) on one B200.
 
     python bench_decode.py --batch 1 --bits 4
     python bench_decode.py --batch 32 --bits 4

@@ -4,12 +4,12 @@
         bench_parallel.py --config tp-ep --steps 5 --warmup 3
     python -m torch.distributed.run ... bench_parallel.py --config pp-zero --steps 5 --warmup 3
 
-``tp-ep``: the Mixtral-shaped model (vocab 32000, d4096, 32 layers, 32 query / 8 KV heads,
+``tp-ep`` (benchmark configuration 3): the Mixtral-shaped model (vocab 32000, d4096, 32 layers, 32 query / 8 KV heads,
 8 experts h14336, top-2, capacity 1.0) with attention tensor-parallel and experts expert-parallel over the SAME
 ranks (sequence parallelism: token rows sharded between the attention blocks), activation checkpointing, 4
 sequences of 4096 per step, seeded uniform token ids. One data-parallel group, so tokens/step = 4 x 4096.
 
-``pp-zero``: vocab 50304, d2048, 24 layers, 16 heads, 16 experts h5632, top-2, as 4 pipeline
+``pp-zero`` (benchmark configuration 4): vocab 50304, d2048, 24 layers, 16 heads, 16 experts h5632, top-2, as 4 pipeline
 stages x 2 data-parallel replicas, GPipe with 8 micro-batches of 4 x 2048 tokens per replica, the sharded AdamW
 over the data-parallel group. tokens/step = 8 x 4 x 2048 x 2.
 
@@ -120,7 +120,7 @@ def _tp_ep(args, rank, world, device):
         opt.zero_grad(set_to_none=True)
         return out["loss"]
 
-    description = {"model": "mixtral-8x7b shape (BASELINE config 3)" if not args.tiny else "tiny tp-ep wiring check",
+    description = {"model": "mixtral-8x7b shape (benchmark configuration 3)" if not args.tiny else "tiny tp-ep wiring check",
                    "global_batch": seqs, "seq_len": seq,
                    "parallelism": f"sp: attention tp{world} + experts ep{world} on the same ranks",
                    "activation_checkpointing": True, "ep_transport": ep.transport}
@@ -166,7 +166,7 @@ def _pp_zero(args, rank, world, device):
         opt.zero_grad(set_to_none=True)
         return result["loss"]
 
-    description = {"model": "moe-pp-e16 (BASELINE config 4)" if not args.tiny else "tiny pp-zero wiring check",
+    description = {"model": "moe-pp-e16 (benchmark configuration 4)" if not args.tiny else "tiny pp-zero wiring check",
                    "global_batch": micro * per_micro * pp.dp_size, "seq_len": seq,
                    "parallelism": f"pp{pp.num_stages} x dp{pp.dp_size}, gpipe, {micro} micro-batches",
                    "optimizer": "sharded AdamW over the data-parallel group" if pp.dp_size > 1 else "AdamW"}

@@ -4,7 +4,7 @@ The field names, defaults and validation of the first fourteen fields follow the
 ``QuantaWeaveConfig`` (``src/quantweave_moe_model.py:15-48``) so that a reference ``config.json`` loads
 unchanged and reproduces the reference layout (LayerNorm, learned absolute positions, biased MHA).
 
-The remaining fields are additions needed by the BASELINE configurations and by the B200 engine:
+The remaining fields are additions needed by the benchmark configurations and by the B200 engine:
 
 * ``norm_type``: ``"layernorm"`` (reference) or ``"rmsnorm"``;
 * ``position_embedding``: ``"learned"`` (reference) or ``"rope"``;
@@ -102,19 +102,19 @@ class QuantaWeaveConfig:
 
 # Named architectures from the benchmark configurations (tests and bench.py use these).
 PRESETS: dict[str, dict] = {
-    # CPU fp32 exact-resume gate.
+    # benchmark configuration 1: CPU fp32 exact-resume gate.
     "tiny-cpu": dict(vocab_size=512, hidden_size=128, layers=4, attention_heads=4, num_experts=8, ffn_size=256,
                      top_k=2, capacity_factor=1.25, router_aux_loss_coef=0.01, norm_type="rmsnorm",
                      position_embedding="rope", attention_bias=False),
-    # expert-parallel MoE training (the headline metric).
+    # benchmark configuration 2: expert-parallel MoE training (the headline metric).
     "moe-1b-e64": dict(vocab_size=32000, hidden_size=1024, layers=16, attention_heads=16, num_experts=64,
                        ffn_size=2816, top_k=2, capacity_factor=1.25, router_aux_loss_coef=0.01,
                        norm_type="rmsnorm", position_embedding="rope", attention_bias=False, init_std=0.02),
-    # Mixtral-shaped TP+EP.
+    # benchmark configuration 3: Mixtral-shaped TP+EP.
     "mixtral-8x7b": dict(vocab_size=32000, hidden_size=4096, layers=32, attention_heads=32, kv_heads=8,
                          num_experts=8, ffn_size=14336, top_k=2, capacity_factor=1.0, norm_type="rmsnorm",
                          position_embedding="rope", attention_bias=False, init_std=0.02, rope_theta=1e6),
-    # pipeline + ZeRO.
+    # benchmark configuration 4: pipeline + ZeRO.
     "moe-pp-e16": dict(vocab_size=50304, hidden_size=2048, layers=24, attention_heads=16, num_experts=16,
                        ffn_size=5632, top_k=2, capacity_factor=1.25, norm_type="rmsnorm",
                        position_embedding="rope", attention_bias=False, init_std=0.02),

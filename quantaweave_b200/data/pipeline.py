@@ -10,7 +10,7 @@ Behavioural parity with the reference ``src/data_pipeline.py``:
   ``seed * 1_000_003 + step`` draws one global batch and each rank takes its disjoint slice (:517-590). The same
   seeding rule is kept so that resumed runs draw the same windows.
 
-Additions: ``SyntheticTokenStream`` (seeded uniform or Zipf token ids, the BASELINE benchmark inputs) with the same
+Additions: ``SyntheticTokenStream`` (seeded uniform or Zipf token ids, the benchmark inputs) with the same
 ``batch(step)`` / ``state(step)`` contract, and a pinned-host staging helper for the end-to-end bench path.
 """
 

@@ -1,4 +1,4 @@
-"""The multi-GPU benchmark script for BASELINE configs 3 and 4 (``bench_parallel.py``) runs end to end on gloo ranks
+"""The multi-GPU benchmark script for benchmark configurations 3 and 4 (``bench_parallel.py``) runs end to end on gloo ranks
 with tiny models of the same layouts: sequence-parallel TP+EP, and pipeline x data parallel with the sharded
 optimizer. This checks the wiring only; the timing it prints on CPU is not a measurement."""
 

@@ -1,4 +1,4 @@
-"""CPU fp32 tiny MoE (RoPE + RMSNorm), 20 AdamW steps (lr 3e-4, betas 0.9/0.95, wd 0.1),
+"""benchmark configuration 1: CPU fp32 tiny MoE (RoPE + RMSNorm), 20 AdamW steps (lr 3e-4, betas 0.9/0.95, wd 0.1),
 checkpoint at step 10, resume, and compare weights/loss/routing bit-exactly against an uninterrupted run."""
 
 import json
