@@ -83,13 +83,33 @@ OPTION_HELP = {
     "lr": "learning rate",
     "seed": "random seed",
     "resume": "continue from --checkpoint-dir when it holds a checkpoint",
+    "config": "YAML or JSON configuration file",
+    "name": "name of the run (default: the config's name)",
+    "runs": "run directories to compare",
+    "metric": "dotted path of the value to rank by (lower is better)",
+    "markdown": "also write the comparison table to this file",
+    "vocab_size": "vocabulary size",
+    "hidden_size": "model width",
+    "layers": "transformer blocks",
+    "ffn_size": "hidden width of each expert",
+    "total_experts": "experts per MoE layer",
+    "active_experts": "experts per token (top-k)",
+    "attention_heads": "attention heads",
+    "capacity_factor": "per-expert capacity factor (0: unlimited)",
+    "min_expert_capacity": "lower bound of the per-expert capacity",
 }
 
 
 def describe_options(parser, extra: dict | None = None) -> None:
     """Give every option of ``parser`` that has no help text the shared (or ``extra``) description."""
+    import argparse
+
     table = {**OPTION_HELP, **(extra or {})}
     for action in parser._actions:
+        if isinstance(action, argparse._SubParsersAction):
+            for sub in action.choices.values():
+                describe_options(sub, extra)
+            continue
         if action.help is None and action.dest in table:
             default = action.default
             shown = "" if default in (None, False) or isinstance(default, bool) else f" (default: {default})"

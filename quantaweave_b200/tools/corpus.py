@@ -113,6 +113,9 @@ def main(argv=None) -> None:
     c.add_argument("--total-tokens", type=int, default=2_500_000_000)
     c.add_argument("--code-fraction", type=float, default=0.85)
     c.add_argument("--output", type=Path, default=Path("data/raw/quantweave-code-corpus.jsonl"))
+    from .common import describe_options
+
+    describe_options(p, {'total_tokens': 'approximate token budget of the corpus', 'code_fraction': 'share of code among the tokens', 'output': 'JSONL file to write'})
     args = p.parse_args(argv)
     if args.command == "smoke":
         if args.examples < 1:

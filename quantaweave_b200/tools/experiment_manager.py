@@ -314,6 +314,9 @@ def main(argv=None) -> None:
     cmp.add_argument("--objectives", nargs="+", help="2+ dotted.path:min|max entries (Pareto ranking)")
     cmp.add_argument("--markdown", type=Path)
     cmp.add_argument("--charts-dir", type=Path, help="write loss_curves.svg and metric_bars.svg here")
+    from .common import describe_options
+
+    describe_options(p, {'runs_dir': 'folder of tracked runs'})
     args = p.parse_args(argv)
     if args.command == "run":
         summary = run_experiment(load_config(args.config), args.runs_dir, args.name)

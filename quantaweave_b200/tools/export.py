@@ -180,6 +180,9 @@ def main(argv=None) -> None:
     p.add_argument("--group-size", type=int, help="quantisation group (default: per row for int8, 32 for int4)")
     p.add_argument("--onnx", action="store_true", help="also try an ONNX export (needs the onnx package)")
     p.add_argument("--benchmark-data", type=Path, help="record loss/perplexity/throughput of the source checkpoint")
+    from .common import describe_options
+
+    describe_options(p, {'output': 'directory of the export bundle'})
     args = p.parse_args(argv)
     meta = export_bundle(args.checkpoint, args.output, args.quantize, args.onnx, args.benchmark_data,
                          args.group_size)

@@ -147,6 +147,9 @@ def main(argv=None) -> None:
     p.add_argument("--capacity-factor", type=float, default=1.25)
     p.add_argument("--min-expert-capacity", type=int, default=4)
     p.add_argument("--b200-plan", action="store_true", help="add the per-B200 memory / expert-parallel plan")
+    from .common import describe_options
+
+    describe_options(p, {'mode': 'dense or mixture-of-experts architecture', 'size': 'preset size from the architecture table', 'output': 'write the manifest JSON here', 'num_experts': 'experts per MoE layer (overrides the preset)', 'top_k': 'experts per token (overrides the preset)', 'ffn_multiplier': 'FFN width as a multiple of the model width', 'tied_embeddings': 'share the input embedding with the LM head'})
     args = p.parse_args(argv)
     try:
         spec = make_spec(args.mode, args.size, hidden_size=args.hidden_size, layers=args.layers,

@@ -35,6 +35,9 @@ def build_parser() -> argparse.ArgumentParser:
             c.add_argument("--vocab-size", type=int, default=4096)
         if name == "sentencepiece":
             c.add_argument("--algorithm", choices=("unigram", "bpe"), default="unigram")
+    from .common import describe_options
+
+    describe_options(p, {"data": "JSONL files to read", "output": "directory to write", "algorithm": "SentencePiece model type"})
     return p
 
 

@@ -211,6 +211,9 @@ def main(argv=None) -> None:
     p.add_argument("--config", type=Path, required=True)
     p.add_argument("--runs-dir", type=Path, default=DEFAULT_RUNS_DIR)
     p.add_argument("--dry-run", action="store_true", help="list what would run without training")
+    from .common import describe_options
+
+    describe_options(p, {'runs_dir': "folder the sweep's runs are written to"})
     args = p.parse_args(argv)
     outcome = run_sweep(load_config(args.config), args.runs_dir, args.dry_run)
     print(json.dumps({k: v for k, v in outcome.items() if k not in {"ranking", "skipped"}}, indent=2, default=str))

@@ -378,6 +378,9 @@ def main(argv=None) -> None:
     parser.add_argument("--attention-heads", type=int, default=4)
     parser.add_argument("--vocab-size", type=int, default=7168)
     parser.add_argument("--sequence-length", type=int, default=128)
+    from ..tools.common import describe_options
+
+    describe_options(parser, {'sequence_length': 'tokens per training sequence', 'device': 'device to describe'})
     args = parser.parse_args(argv)
     info = detect(args.device)
     if args.auto_architecture:
