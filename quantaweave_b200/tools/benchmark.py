@@ -18,6 +18,8 @@ from typing import Optional
 
 import torch
 
+from .common import synchronize  # noqa: F401  (the reference exposes it from its benchmark module)
+
 
 def process_rss_bytes() -> Optional[int]:
     try:

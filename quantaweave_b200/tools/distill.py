@@ -25,6 +25,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor
 
+from .common import load_model  # noqa: F401  (the reference exposes it from its distillation module)
 from .run_bundle import add_archive_arguments, create_run_bundle, reproduce_command, resolve_archive_dir
 
 
