@@ -13,9 +13,16 @@ import torch
 
 
 class CPUOffloadAdamW(torch.optim.Optimizer):
-    def __init__(self, params: Iterable, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
+    def __init__(self, parameters: Iterable, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.01) -> None:
-        super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
+        items = list(parameters)
+        if items and not isinstance(items[0], dict):
+            items = [p for p in items if p.requires_grad]  # frozen parameters hold no optimizer state
+        super().__init__(items, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay))
+
+    def state_numel(self) -> int:
+        """Elements of optimizer state (the two AdamW moments) kept in host memory instead of device memory."""
+        return sum(st["exp_avg"].numel() + st["exp_avg_sq"].numel() for st in self.state.values() if "exp_avg" in st)
 
     def _host_state(self, p: torch.Tensor) -> dict:
         st = self.state[p]

@@ -20,13 +20,13 @@ def read_config(directory: Path) -> QuantaWeaveConfig:
     return QuantaWeaveConfig.from_dict(json.loads((Path(directory) / "config.json").read_text()))
 
 
-def load_model(directory: Path, device: torch.device, precision: str = "auto", with_payload: bool = False):
-    """Build the model of ``directory`` on ``device`` and load its weights (quantised checkpoints included)."""
+def load_model(checkpoint: Path, device: torch.device, precision: str = "auto", with_payload: bool = False):
+    """Build the model of ``checkpoint`` on ``device`` and load its weights (quantised checkpoints included)."""
     from ..models.model import QuantaWeaveMoEForCausalLM
 
-    directory = Path(directory)
-    config = read_config(directory)
-    payload = load_checkpoint(directory / "model.pt", map_location="cpu")
+    checkpoint = Path(checkpoint)
+    config = read_config(checkpoint)
+    payload = load_checkpoint(checkpoint / "model.pt", map_location="cpu")
     state = payload["model"] if "model" in payload else payload["state_dict"]
     model = QuantaWeaveMoEForCausalLM(config)
     if "bits" in payload:  # a quantised export

@@ -113,13 +113,13 @@ def load_checkpoint(path: Path, model, optimizer, device: torch.device, extra_ou
     return int(ckpt["step"])
 
 
-def restore_rng(state: dict, device: torch.device) -> None:
-    if "python" in state:
-        random.setstate(state["python"])
-    if "torch" in state:
-        torch.set_rng_state(state["torch"].cpu())
-    if "accelerator" in state and device.type == "cuda":
-        torch.cuda.set_rng_state(state["accelerator"].cpu(), device)
+def restore_rng(rng_state: dict, device: torch.device) -> None:
+    if "python" in rng_state:
+        random.setstate(rng_state["python"])
+    if "torch" in rng_state:
+        torch.set_rng_state(rng_state["torch"].cpu())
+    if "accelerator" in rng_state and device.type == "cuda":
+        torch.cuda.set_rng_state(rng_state["accelerator"].cpu(), device)
 
 
 def checkpoint_exists(path: Path) -> bool:

@@ -233,14 +233,16 @@ def _reset_peak(device: torch.device) -> None:
 
 
 def find_safe_batch_size(model, device: torch.device, sequence_length: int, autocast: Callable = None,
-                         start: int = 1, limit: int = 256, memory_fraction: float = 0.85, target: float = 0.95,
+                         start: int = 1, limit: int = 256, headroom: float = 0.85, target: float = 0.95,
+                         optimizer_state_copies: int = 2,
                          steps: int = 2, total_memory: Optional[int] = None, peak_fn: Optional[Callable] = None,
                          clock: Callable = time.perf_counter) -> dict:
     """Double the batch with real forward/backward/clip steps until a step runs out of memory or its peak passes
-    ``memory_fraction`` of ``total_memory`` (default: the device's, host memory on CPU).
+    ``headroom`` of ``total_memory`` (default: the device's, host memory on CPU).
 
-    The optimizer's state is held for the whole search, so an approved batch still fits once training starts: two
-    fp32 AdamW moments per trainable parameter, plus an fp32 master copy of every low-precision one. Weights are never
+    The optimizer's state is held for the whole search, so an approved batch still fits once training starts:
+    ``optimizer_state_copies`` fp32 copies per trainable parameter (2: the AdamW moments), plus an fp32 master copy
+    of every low-precision one. Weights are never
     stepped; gradients are cleared and the module's train/eval mode is restored. Any error other than running out of
     memory propagates. Returns the largest batch that fitted (``batch_size``), the smallest batch whose throughput is
     within ``target`` of the best (``recommended_batch_size``; ``target=0`` picks the largest) and the measured
@@ -254,7 +256,7 @@ def find_safe_batch_size(model, device: torch.device, sequence_length: int, auto
         total_memory = (torch.cuda.get_device_properties(device).total_memory if device.type == "cuda"
                         else _host_memory()[0])
     trainable = [p for p in model.parameters() if p.requires_grad]
-    reserve = [torch.zeros_like(p, dtype=torch.float32) for p in trainable for _ in range(2)]
+    reserve = [torch.zeros_like(p, dtype=torch.float32) for p in trainable for _ in range(optimizer_state_copies)]
     reserve += [torch.zeros_like(p, dtype=torch.float32) for p in trainable if p.dtype != torch.float32]
     was_training = model.training
     model.train()
@@ -283,7 +285,7 @@ def find_safe_batch_size(model, device: torch.device, sequence_length: int, auto
                 peak = peak_fn()
                 curve.append({"batch_size": batch, "tokens_per_second": batch * sequence_length * timed / elapsed,
                               "peak_memory_bytes": peak})
-                if peak is not None and total_memory and peak > memory_fraction * total_memory:
+                if peak is not None and total_memory and peak > headroom * total_memory:
                     curve.pop()  # over the headroom limit: this batch is not safe
                     break
                 batch *= 2
@@ -304,7 +306,7 @@ def find_safe_batch_size(model, device: torch.device, sequence_length: int, auto
     chosen = next(r for r in curve if r["tokens_per_second"] >= target * best) if target > 0 else curve[-1]
     return {"batch_size": curve[-1]["batch_size"], "recommended_batch_size": chosen["batch_size"],
             "tokens_per_second": chosen["tokens_per_second"], "peak_memory_bytes": chosen["peak_memory_bytes"],
-            "largest_peak_memory_bytes": curve[-1]["peak_memory_bytes"], "curve": curve, "headroom": memory_fraction}
+            "largest_peak_memory_bytes": curve[-1]["peak_memory_bytes"], "curve": curve, "headroom": headroom}
 
 
 CHECKPOINTING_GAIN = 1.05  # recompute must buy at least 5 % more tokens/s (through a larger batch) to be recommended

@@ -32,6 +32,10 @@ def test_cpu_offload_adamw_matches_torch_adamw_step_for_step_and_round_trips():
             opt.step()
     for p, q in zip(a.parameters(), b.parameters()):
         assert torch.allclose(p, q, atol=1e-6)
+    assert ours.state_numel() == 2 * sum(p.numel() for p in a.parameters())  # both moments, on the host
+    frozen = torch.nn.Linear(4, 4)
+    frozen.bias.requires_grad_(False)
+    assert len(CPUOffloadAdamW(parameters=frozen.parameters()).param_groups[0]["params"]) == 1  # trainable only
     again = CPUOffloadAdamW(a.parameters(), lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1)
     again.load_state_dict(ours.state_dict())
     assert json.dumps(again.state_dict(), default=str) == json.dumps(ours.state_dict(), default=str)
