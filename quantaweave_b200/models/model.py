@@ -45,7 +45,11 @@ class QuantaWeaveBlock(nn.Module):
             self.moe = ExpertParallelMoE(config, expert_parallel)
         del tp_rank
 
-    def forward(self, hidden: Tensor, token_domains: Optional[Tensor] = None, num_domains: int = 0):
+    def forward(self, hidden: Tensor, causal_mask: Optional[Tensor] = None, token_domains: Optional[Tensor] = None,
+                num_domains: int = 0):
+        """``causal_mask`` keeps the reference's argument order (``src/quantweave_moe_model.py:293``); attention here
+        is always causal, so the mask itself is not needed."""
+        del causal_mask
         if hidden.is_cuda and type(self.attention) is Attention:
             from ..ops.attention import self_attention
 
@@ -151,9 +155,9 @@ class QuantaWeaveMoEForCausalLM(nn.Module):
         balance, dropped, overflow, domain = [], [], [], []
         for block in self.blocks:
             if self.activation_checkpointing and self.training:
-                hidden, b, d, o, dom = checkpoint(block, hidden, token_domains, num_domains, use_reentrant=False)
+                hidden, b, d, o, dom = checkpoint(block, hidden, None, token_domains, num_domains, use_reentrant=False)
             else:
-                hidden, b, d, o, dom = block(hidden, token_domains, num_domains)
+                hidden, b, d, o, dom = block(hidden, None, token_domains, num_domains)
             balance.append(b)
             dropped.append(d)
             overflow.append(o)

@@ -138,3 +138,15 @@ def test_every_public_name_resolves():
     for name in package.__all__:
         assert getattr(package, name) is not None, name
     assert {"QuantaWeaveBlock", "SparseSwiGLU", "TopKMoE", "load_tokenizer", "add_lora"} <= set(package.__all__)
+
+
+def test_a_block_takes_the_reference_argument_order():
+    torch.manual_seed(0)
+    model = QuantaWeaveMoEForCausalLM(_cfg(capacity_factor=0.0))
+    block = model.blocks[0]
+    x = torch.randn(2, 5, 16)
+    mask = torch.triu(torch.ones(5, 5, dtype=torch.bool), diagonal=1)  # what the reference passes
+    with torch.no_grad():
+        with_mask = block(x, mask)[0]
+        without = block(x)[0]
+    assert torch.equal(with_mask, without)
