@@ -64,9 +64,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--batch-size", type=int, default=2)
     p.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
     p.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")
-    p.add_argument("--output", type=Path, help="JSON report path; a .md report is written beside it")
-    p.add_argument("--training-metrics", type=Path, help="metrics.jsonl from training, for stability metrics")
-    p.add_argument("--no-routing-stats", action="store_true", help="skip the routing/compute diagnostic pass")
+    p.add_argument("--output", type=Path, help="write the report as JSON here, with a Markdown copy next to it")
+    p.add_argument("--training-metrics", type=Path, help="the training run's metrics.jsonl, to add loss-stability figures")
+    p.add_argument("--no-routing-stats", action="store_true", help="leave out the per-layer routing and expert-time pass")
     from .common import describe_options
 
     describe_options(p)

@@ -403,28 +403,28 @@ def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     m = p.add_argument_group("which model")
     m.add_argument("--checkpoint", type=Path, help=f"a checkpoint directory (default {DEFAULT_CHECKPOINT})")
-    m.add_argument("--run", help="an archived run: its epoch id under artifacts/runs, or the folder path")
-    m.add_argument("--latest", action="store_true", help="the newest archived run that contains a model")
-    m.add_argument("--adapter", type=Path, help="a QLoRA adapter directory (applied over --checkpoint)")
+    m.add_argument("--run", help="archived run to load, by its epoch-second name under --runs-dir or by path")
+    m.add_argument("--latest", action="store_true", help="load the most recent archived run that holds a model")
+    m.add_argument("--adapter", type=Path, help="QLoRA adapter folder, applied on top of --checkpoint")
     m.add_argument("--quantize", type=int, choices=(0, 4, 8), default=0, help="quantise the experts in memory")
     m.add_argument("--runs-dir", type=Path, default=RUNS_DIR)
     s = p.add_argument_group("sending messages")
-    s.add_argument("-m", "--message", action="append", default=[], help="send this message (repeatable)")
+    s.add_argument("-m", "--message", action="append", default=[], help="a message to send; give it several times for several messages")
     s.add_argument("--messages-file", type=Path, help=".txt (one per line) or .jsonl ({message, expect, ...})")
     s.add_argument("--conversation", action="store_true", help="batch mode keeps the history between messages")
-    s.add_argument("--json", action="store_true", help="print one JSON object per reply instead of text")
-    s.add_argument("--transcript", type=Path, help="append every exchange to this JSONL file")
+    s.add_argument("--json", action="store_true", help="write each reply as a JSON line rather than plain text")
+    s.add_argument("--transcript", type=Path, help="log each message and reply as a line in this JSONL file")
     s.add_argument("--interactive", action="store_true", help="always run the interactive session (even on a pipe)")
-    s.add_argument("--quiet", action="store_true", help="no statistics or notes")
+    s.add_argument("--quiet", action="store_true", help="print replies only, without timing lines or notes")
     g = p.add_argument_group("generation")
     g.add_argument("--mode", choices=("complete", "chat"), default="complete")
-    g.add_argument("--system", default="", help="chat mode: text placed before the conversation")
-    g.add_argument("--tokens", type=int, default=200, help="maximum new tokens per reply")
-    g.add_argument("--temperature", type=float, default=0.8, help="0 = greedy and deterministic")
+    g.add_argument("--system", default="", help="system text that opens the conversation (chat mode)")
+    g.add_argument("--tokens", type=int, default=200, help="upper limit of generated tokens for each reply")
+    g.add_argument("--temperature", type=float, default=0.8, help="sampling temperature; 0 always takes the most likely token")
     g.add_argument("--top-k", type=int, default=0)
     g.add_argument("--top-p", type=float, default=1.0)
-    g.add_argument("--seed", type=int, help="make sampling reproducible")
-    g.add_argument("--stop", action="append", default=[], help="stop when this text appears (repeatable)")
+    g.add_argument("--seed", type=int, help="seed for the sampler, for repeatable replies")
+    g.add_argument("--stop", action="append", default=[], help="end the reply at this text; may be given several times")
     g.add_argument("--no-cache", action="store_true", help="plain forward pass per token instead of the KV cache")
     g.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")
     g.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")

@@ -49,11 +49,11 @@ def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--student", type=Path, default=Path("artifacts/outputs/quantweave-moe-out"))
     p.add_argument("--teacher-data", type=Path, required=True)
-    p.add_argument("--teacher-checkpoint", type=Path, help="enable logit-level distillation from this checkpoint")
-    p.add_argument("--hf-teacher", help="Hugging Face causal LM (directory or hub id) with its own tokenizer")
+    p.add_argument("--teacher-checkpoint", type=Path, help="distil towards the logits of this model (same tokenizer)")
+    p.add_argument("--hf-teacher", help="a Hugging Face causal language model (folder or hub name) that brings its own tokenizer")
     p.add_argument("--cross-loss", choices=("auto", "marginal", "uld"), default="auto",
-                   help="loss for --hf-teacher: exact next-character marginal (char students) or sorted-distribution L1")
-    p.add_argument("--alpha", type=float, default=1.0, help="weight of the KL / cross-tokenizer term")
+                   help="how --hf-teacher is matched: the next-character marginal (character students) or the ULD sorted-probability distance")
+    p.add_argument("--alpha", type=float, default=1.0, help="multiplier of the distillation term added to the language-model loss")
     p.add_argument("--temperature", type=float, default=2.0, help="softmax temperature of the KL term")
     p.add_argument("--output", type=Path, default=Path("artifacts/outputs/quantweave-moe-distilled"))
     p.add_argument("--checkpoint-dir", type=Path, default=Path("artifacts/checkpoints/quantweave-distill"))

@@ -302,18 +302,18 @@ def loss_curves_svg(summaries: list[dict]) -> str:
 def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     sub = p.add_subparsers(dest="command", required=True)
-    run = sub.add_parser("run", help="execute a config bundle as a tracked run")
+    run = sub.add_parser("run", help="train one configuration file as a tracked run")
     run.add_argument("--config", type=Path, required=True)
     run.add_argument("--name")
     run.add_argument("--runs-dir", type=Path, default=DEFAULT_RUNS_DIR)
-    listing = sub.add_parser("list", help="list runs and the best one")
+    listing = sub.add_parser("list", help="show the tracked runs and which one is best")
     listing.add_argument("--runs-dir", type=Path, default=DEFAULT_RUNS_DIR)
-    cmp = sub.add_parser("compare", help="rank runs and draw comparison charts")
+    cmp = sub.add_parser("compare", help="order runs by a metric and draw charts of them")
     cmp.add_argument("runs", type=Path, nargs="+")
     cmp.add_argument("--metric", default="benchmark.loss")
     cmp.add_argument("--objectives", nargs="+", help="2+ dotted.path:min|max entries (Pareto ranking)")
     cmp.add_argument("--markdown", type=Path)
-    cmp.add_argument("--charts-dir", type=Path, help="write loss_curves.svg and metric_bars.svg here")
+    cmp.add_argument("--charts-dir", type=Path, help="folder for the loss-curve and metric-bar SVG charts")
     from .common import describe_options
 
     describe_options(p, {'runs_dir': 'folder of tracked runs'})

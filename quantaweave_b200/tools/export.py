@@ -176,10 +176,10 @@ def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--checkpoint", type=Path, default=Path("artifacts/outputs/quantweave-moe-out"))
     p.add_argument("--output", type=Path, required=True)
-    p.add_argument("--quantize", type=int, choices=(4, 8), help="also write a weight-only int4/int8 copy")
+    p.add_argument("--quantize", type=int, choices=(4, 8), help="add a copy with int4 or int8 expert weights")
     p.add_argument("--group-size", type=int, help="quantisation group (default: per row for int8, 32 for int4)")
-    p.add_argument("--onnx", action="store_true", help="also try an ONNX export (needs the onnx package)")
-    p.add_argument("--benchmark-data", type=Path, help="record loss/perplexity/throughput of the source checkpoint")
+    p.add_argument("--onnx", action="store_true", help="attempt an ONNX file as well (requires the onnx package)")
+    p.add_argument("--benchmark-data", type=Path, help="measure the source model's loss, perplexity and speed on these rows")
     from .common import describe_options
 
     describe_options(p, {'output': 'directory of the export bundle'})

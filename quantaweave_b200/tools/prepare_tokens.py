@@ -25,12 +25,12 @@ def build_parser() -> argparse.ArgumentParser:
                        ("pack", "tokenize JSONL into tokens.bin + meta.json")):
         c = sub.add_parser(name, help=text)
         c.add_argument("--data", type=Path, nargs="+", required=True)
-        c.add_argument("--examples", type=int, help="max JSONL rows read per file")
+        c.add_argument("--examples", type=int, help="read at most this many rows from each JSONL file")
         c.add_argument("--output", type=Path, required=True)
         c.add_argument("--redact-pii", action="store_true", help="best-effort PII redaction first")
         if name == "pack":
             c.add_argument("--tokenizer", default="char", help="'char' or a directory saved by bpe/sentencepiece")
-            c.add_argument("--vocab-size", type=int, default=7168, help="character vocabulary size (char only)")
+            c.add_argument("--vocab-size", type=int, default=7168, help="vocabulary size of the character tokenizer")
         else:
             c.add_argument("--vocab-size", type=int, default=4096)
         if name == "sentencepiece":

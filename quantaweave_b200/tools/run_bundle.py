@@ -39,14 +39,14 @@ FULL_HASH_LIMIT = 512 << 20
 def add_archive_arguments(parser: argparse.ArgumentParser) -> None:
     g = parser.add_argument_group("run archive")
     g.add_argument("--archive-dir", type=Path,
-                   help="save weights, data, benchmarks and more in ARCHIVE_DIR/<epoch seconds>/ "
-                        "(the command line uses artifacts/runs unless --no-archive)")
-    g.add_argument("--no-archive", action="store_true", help="do not create a run archive")
+                   help="keep the finished run (weights, data manifest, benchmarks, reproduce script) in "
+                        "ARCHIVE_DIR/<epoch seconds>/; from the command line this defaults to artifacts/runs")
+    g.add_argument("--no-archive", action="store_true", help="skip the run archive")
     g.add_argument("--archive-data-limit-mb", type=float, default=200.0,
-                   help="copy the data into the archive if it is at most this big (0 = never)")
-    g.add_argument("--archive-benchmark-examples", type=int, default=500, help="rows per benchmark in the archive")
+                   help="largest data size copied into the archive, in MB (0: record hashes only)")
+    g.add_argument("--archive-benchmark-examples", type=int, default=500, help="rows each archived benchmark reads")
     g.add_argument("--data-card", type=Path,
-                   help="JSON describing the data's source/license/provenance, embedded in data/manifest.json")
+                   help="JSON file about the data (origin, licence, provenance) copied into the archive's manifest")
 
 
 def resolve_archive_dir(args: argparse.Namespace, default: Path = Path("artifacts/runs")) -> None:

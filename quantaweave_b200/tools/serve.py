@@ -506,9 +506,9 @@ def build_app(server: Server):
 def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--checkpoint", type=Path, help=f"a checkpoint directory (default {DEFAULT_CHECKPOINT})")
-    p.add_argument("--run", help="an archived run: its epoch id under artifacts/runs, or the folder path")
-    p.add_argument("--latest", action="store_true", help="the newest archived run that contains a model")
-    p.add_argument("--adapter", type=Path, help="a QLoRA adapter directory")
+    p.add_argument("--run", help="archived run to load, by its epoch-second name under --runs-dir or by path")
+    p.add_argument("--latest", action="store_true", help="load the most recent archived run that holds a model")
+    p.add_argument("--adapter", type=Path, help="QLoRA adapter folder, applied on top of --checkpoint")
     p.add_argument("--runs-dir", type=Path, default=Path("artifacts/runs"))
     p.add_argument("--no-cache", action="store_true", help="plain forward pass per token instead of the KV cache")
     p.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")

@@ -210,7 +210,7 @@ def main(argv=None) -> None:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--config", type=Path, required=True)
     p.add_argument("--runs-dir", type=Path, default=DEFAULT_RUNS_DIR)
-    p.add_argument("--dry-run", action="store_true", help="list what would run without training")
+    p.add_argument("--dry-run", action="store_true", help="print the planned trials and stop before training")
     from .common import describe_options
 
     describe_options(p, {'runs_dir': "folder the sweep's runs are written to"})

@@ -341,7 +341,7 @@ _HELP = {
     "diagnostics_interval": "steps between routing snapshots (0: off unless a controller needs them)",
     "archive_dir": "archive the finished run (weights, data manifest, benchmarks, reproduce.sh) under this folder",
     "no_archive": "do not archive the run", "archive_data_limit_mb": "copy the data into the archive up to this size",
-    "archive_benchmark_examples": "rows per benchmark in the archive",
+    "archive_benchmark_examples": "rows each archived benchmark reads",
     "data_card": "JSON describing the data's source, licence and provenance, embedded in the archive manifest",
 }
 

@@ -364,7 +364,7 @@ def main(argv=None) -> None:
     fit and a suggested expert count, and with ``--probe`` run real passes to find a safe batch size."""
     parser = argparse.ArgumentParser(description="Describe this machine and size a QuantaWeave model for it")
     parser.add_argument("--device", default="auto", choices=("auto", "cuda", "rocm", "xpu", "cpu"))
-    parser.add_argument("--probe", action="store_true", help="run real passes to find a safe batch size")
+    parser.add_argument("--probe", action="store_true", help="time real training steps to find the largest safe batch")
     parser.add_argument("--auto-architecture", action="store_true",
                         help="pick hidden size, layers, experts and sequence length for this device")
     parser.add_argument("--quality", default="balanced", choices=("capacity", "balanced", "dense"),
