@@ -1,18 +1,24 @@
-"""Send messages to a model: an interactive session, one-off messages, or a batch of test messages.
+"""Talk to a trained model: an interactive session, one-off messages, or a file of test messages.
 
     python -m quantaweave_b200.tools.chat --latest                      # interactive, newest archived run
     python -m quantaweave_b200.tools.chat --checkpoint DIR -m "Once upon a time"
     python -m quantaweave_b200.tools.chat --latest --messages-file tests.jsonl --json
     printf 'Once upon a time\\n' | python -m quantaweave_b200.tools.chat --latest
 
-Parity with the reference ``src/chat_quantweave_moe.py`` (``choose_token`` :54, ``Settings`` :62, ``Reply`` :80,
-``ChatSession`` :96-188, ``resolve_model`` :216-232, ``read_messages`` :251-273, ``run_batch`` :276-296, ``repl``
-:329-395, CLI :407-494; exit code 1 when an expectation fails). ``complete`` mode continues the message as text (what
-a base model does); ``chat`` mode wraps the conversation in ``User:`` / ``Assistant:`` turns and stops at the next
-``User:`` line. Sampling is restricted to ids the tokenizer has, never emits ``<unk>``; temperature 0 is greedy.
+Same names, options and behaviour as the reference's ``src/chat_quantweave_moe.py`` (``choose_token``, ``Settings``,
+``Reply``, ``ChatSession``, ``resolve_model``, ``read_messages``, ``run_batch``, ``repl`` and the command line, whose
+exit code is 1 when an expectation fails).
 
-Decoding runs on ``FastDecoder`` (KV cache; on CUDA the sm_100a decode kernels captured in a CUDA graph); ``--no-cache``
-falls back to a full forward pass per token. The usable context is ``max_sequence_length - 1`` tokens.
+How it works here:
+
+* A reply is produced by a token source (the KV-cache ``FastDecoder`` stream, or one full forward pass per token
+  with ``--no-cache``) feeding a ``_StopScanner``. The scanner owns the reply text: it cuts at the earliest stop
+  string and releases streamed text only once no stop string can still begin inside it, so a caller never sees part
+  of a stop string.
+* ``complete`` mode continues the message; ``chat`` mode renders the conversation as ``User:`` / ``Assistant:``
+  turns after an optional system line and stops at the next turn marker.
+* Only ids the tokenizer can decode are ever sampled, and never ``<unk>``; temperature 0 is greedy. At most
+  ``max_sequence_length - 1`` tokens of context are read (the last position of a training window is never trained).
 """
 
 from __future__ import annotations
@@ -22,7 +28,7 @@ import json
 import re
 import sys
 import time
-from dataclasses import asdict, dataclass, field
+from dataclasses import asdict, dataclass, field, fields, replace
 from pathlib import Path
 from typing import Callable, Iterator, Optional, Sequence
 
@@ -30,19 +36,22 @@ import torch
 
 RUNS_DIR = Path("artifacts/runs")
 DEFAULT_CHECKPOINT = Path("artifacts/outputs/quantweave-moe-out")
-CHAT_STOPS = ("\nUser:", "\nSystem:")
+CHAT_STOPS = ("\nUser:", "\nSystem:")  # the next turn marker ends an assistant reply
 
 
+# ---- sampling ----------------------------------------------------------------------------------------------------
 def choose_token(logits: torch.Tensor, temperature: float, top_k: int, top_p: float,
                  generator: Optional[torch.Generator]) -> int:
+    """Greedy at temperature 0, otherwise a draw from the top-k / nucleus-filtered softmax."""
     from ..inference.fast_decode import filter_logits
 
     if temperature <= 0:
-        return int(logits.argmax())
-    probs = filter_logits(logits / temperature, top_k, top_p).softmax(dim=-1)
-    return int(torch.multinomial(probs, 1, generator=generator))
+        return int(torch.argmax(logits))
+    weights = torch.softmax(filter_logits(logits / temperature, top_k, top_p), dim=-1)
+    return int(torch.multinomial(weights, 1, generator=generator).item())
 
 
+# ---- settings and replies ------------------------------------------------------------------------------------------
 @dataclass
 class Settings:
     mode: str = "complete"
@@ -55,10 +64,19 @@ class Settings:
     system: str = ""
 
     def validate(self) -> None:
-        if self.mode not in {"complete", "chat"}:
-            raise ValueError("mode must be complete or chat")
-        if self.tokens < 1 or self.temperature < 0 or self.top_k < 0 or not 0 < self.top_p <= 1:
-            raise ValueError("tokens must be >= 1, temperature >= 0, top_k >= 0, and top_p in (0, 1]")
+        problems = []
+        if self.mode not in ("complete", "chat"):
+            problems.append("mode must be complete or chat")
+        if self.tokens < 1:
+            problems.append("tokens must be at least 1")
+        if self.temperature < 0:
+            problems.append("temperature cannot be negative")
+        if self.top_k < 0:
+            problems.append("top_k cannot be negative")
+        if not 0.0 < self.top_p <= 1.0:
+            problems.append("top_p must lie in (0, 1]")
+        if problems:
+            raise ValueError("; ".join(problems))
 
 
 @dataclass
@@ -68,7 +86,7 @@ class Reply:
     response: str
     tokens: int
     seconds: float
-    stop_reason: str  # eos | stop | length
+    stop_reason: str  # "eos", "stop" or "length"
     unknown_characters: list[str] = field(default_factory=list)
     truncated_context: bool = False
 
@@ -77,133 +95,174 @@ class Reply:
         return self.tokens / self.seconds if self.seconds > 0 else 0.0
 
 
+class _StopScanner:
+    """Accumulates reply text, finds the first stop string, and decides how much text is safe to stream."""
+
+    def __init__(self, stops: Sequence[str]) -> None:
+        self.stops = [s for s in stops if s]
+        self.reserve = max((len(s) for s in self.stops), default=1) - 1
+        self.text = ""
+        self.shown = 0
+        self.stopped = False
+
+    def extend(self, text: str) -> None:
+        self.text = text
+        cut = min((i for i in (text.find(s) for s in self.stops) if i >= 0), default=-1)
+        if cut >= 0:
+            self.text, self.stopped = text[:cut], True
+
+    def release(self, final: bool = False) -> str:
+        """Text not yet shown that can no longer turn into the start of a stop string (all of it when ``final``)."""
+        limit = len(self.text) if (final or self.stopped) else max(self.shown, len(self.text) - self.reserve)
+        piece, self.shown = self.text[self.shown:limit], max(self.shown, limit)
+        return piece
+
+
+# ---- the session -----------------------------------------------------------------------------------------------------
 class ChatSession:
     def __init__(self, model, tokenizer, device: torch.device, precision: str, settings: Settings,
                  use_cache: bool = True) -> None:
         from ..inference.fast_decode import FastDecoder, Unsupported
 
         settings.validate()
-        self.model, self.tokenizer, self.device = model, tokenizer, device
-        self.precision, self.settings = precision, settings
+        self.model, self.tokenizer, self.device, self.precision = model.eval(), tokenizer, device, precision
+        self.settings = settings
         self.history: list[tuple[str, str]] = []
-        self.valid_ids = tokenizer.vocab_size
-        model.eval()
+        self.valid_ids = tokenizer.vocab_size  # the model may score ids the tokenizer never produces
         self.decoder = None
         self.cache_note = "no cache (full forward pass per token)"
-        if use_cache:
-            try:
-                self.decoder = FastDecoder(model, device, precision)
-                self.decoder.warm(settings.temperature, settings.top_k, settings.top_p)
-                self.cache_note = self.decoder.description
-            except Unsupported as error:
-                self.cache_note = f"no cache ({error})"
+        if not use_cache:
+            return
+        try:
+            self.decoder = FastDecoder(model, device, precision)
+        except Unsupported as why:
+            self.cache_note = f"no cache ({why})"
+            return
+        self.decoder.warm(settings.temperature, settings.top_k, settings.top_p)
+        self.cache_note = self.decoder.description
 
     def reset(self) -> None:
-        self.history.clear()
+        self.history = []
 
     def format_prompt(self, message: str) -> str:
-        if self.settings.mode == "complete":
+        if self.settings.mode != "chat":
             return message
-        parts = [f"System: {self.settings.system}\n"] if self.settings.system else []
-        parts += [f"User: {u}\nAssistant: {a}\n" for u, a in self.history]
-        parts.append(f"User: {message}\nAssistant:")
-        return "".join(parts)
+        turns = [f"User: {user}\nAssistant: {answer}\n" for user, answer in self.history]
+        opening = [f"System: {self.settings.system}\n"] if self.settings.system else []
+        return "".join(opening + turns) + f"User: {message}\nAssistant:"
 
     def unknown_characters(self, text: str) -> list[str]:
-        vocab = getattr(self.tokenizer, "vocab", None)
-        if self.tokenizer.kind != "char" or vocab is None:
-            return []
-        return sorted({ch for ch in text if ch not in vocab})
+        vocab = getattr(self.tokenizer, "vocab", None) if self.tokenizer.kind == "char" else None
+        return sorted(set(text) - set(vocab)) if vocab is not None else []
 
-    def _plain_tokens(self, ids: list[int], generated: list[int], generator, usable: int) -> Iterator[int]:
-        """No cache: one full forward pass over the last ``usable`` tokens per new token."""
+    def _context_limit(self) -> int:
+        return self.decoder.capacity if self.decoder is not None else self.model.config.max_sequence_length - 1
+
+    def _uncached(self, ids: list[int], generator) -> Iterator[int]:
+        """One full forward pass over the newest ``_context_limit()`` tokens per generated token."""
         from ..training.trainer import autocast_context
 
-        s, tok = self.settings, self.tokenizer
+        s, limit = self.settings, self._context_limit()
+        banned = torch.zeros(0, dtype=torch.long)
+        if self.tokenizer.unk_id is not None and self.tokenizer.unk_id < self.valid_ids:
+            banned = torch.tensor([self.tokenizer.unk_id])
+        context = list(ids)
         while True:
-            window = torch.tensor([(ids + generated)[-usable:]], dtype=torch.long, device=self.device)
+            window = torch.tensor([context[-limit:]], dtype=torch.long, device=self.device)
             with autocast_context(self.device, self.precision):
-                logits = self.model(window)["logits"][0, -1].float()
-            logits[self.valid_ids:] = float("-inf")
-            if tok.unk_id is not None and tok.unk_id < self.valid_ids:
-                logits[tok.unk_id] = float("-inf")
-            yield choose_token(logits, s.temperature, s.top_k, s.top_p, generator)
+                scores = self.model(window)["logits"][0, -1].float()
+            scores[self.valid_ids:] = float("-inf")
+            scores[banned.to(scores.device)] = float("-inf")
+            token = choose_token(scores, s.temperature, s.top_k, s.top_p, generator)
+            context.append(token)
+            yield token
+
+    def _cached(self, ids: list[int], generator) -> Iterator[int]:
+        s = self.settings
+        return self.decoder.stream(ids, s.tokens, temperature=s.temperature, top_k=s.top_k, top_p=s.top_p,
+                                   valid_ids=self.valid_ids, unk_id=self.tokenizer.unk_id, generator=generator)
 
     @torch.inference_mode()
     def send(self, message: str, on_text: Optional[Callable[[str], None]] = None) -> Reply:
-        """Generate a reply; ``on_text`` receives it as produced, never a partial stop string."""
-        s, tok, dec = self.settings, self.tokenizer, self.decoder
+        """Generate a reply to ``message``; ``on_text`` receives the reply piece by piece, never part of a stop."""
+        s, tok = self.settings, self.tokenizer
         prompt = self.format_prompt(message)
-        stops = [x for x in ([*CHAT_STOPS] if s.mode == "chat" else []) + list(s.stop) if x]
         ids = tok.encode(prompt) or [tok.eos_id]
-        usable = dec.capacity if dec is not None else self.model.config.max_sequence_length - 1
-        generator = torch.Generator(device=self.device).manual_seed(s.seed) if s.seed is not None else None
-        holdback = max((len(x) for x in stops), default=1) - 1
-        generated: list[int] = []
-        text, emitted, reason = "", 0, "length"
-        per_char = tok.kind == "char"  # a character's text never depends on its neighbours
+        stops = list(s.stop) + (list(CHAT_STOPS) if s.mode == "chat" else [])
+        scanner = _StopScanner(stops)
+        generator = None if s.seed is None else torch.Generator(device=self.device).manual_seed(s.seed)
+        source = (self._cached if self.decoder is not None else self._uncached)(ids, generator)
+        produced: list[int] = []
+        reason = "length"
+        character_level = tok.kind == "char"  # a character's text does not depend on its neighbours
         started = time.perf_counter()
-        if dec is not None:
-            source = dec.stream(ids, s.tokens, temperature=s.temperature, top_k=s.top_k, top_p=s.top_p,
-                                valid_ids=self.valid_ids, unk_id=tok.unk_id, generator=generator)
-        else:
-            source = self._plain_tokens(ids, generated, generator, usable)
-        for step, token in enumerate(source):
-            if step >= s.tokens:
-                break
-            if token == tok.eos_id:
-                reason = "eos"
-                break
-            generated.append(token)
-            text = text + tok.inverse.get(token, "?") if per_char else tok.decode(generated)
-            hits = [text.find(x) for x in stops if x in text]
-            if hits:
-                text, reason = text[: min(hits)], "stop"
-                break
-            if on_text is not None:
-                safe = max(emitted, len(text) - holdback)
-                if safe > emitted:
-                    on_text(text[emitted:safe])
-                    emitted = safe
-        source.close()
-        if on_text is not None and len(text) > emitted:
-            on_text(text[emitted:])
-        seconds = time.perf_counter() - started
-        response = text.strip() if s.mode == "chat" else text
+        try:
+            for token in source:
+                if len(produced) >= s.tokens:
+                    break
+                if token == tok.eos_id:
+                    reason = "eos"
+                    break
+                produced.append(token)
+                text = scanner.text + tok.inverse.get(token, "?") if character_level else tok.decode(produced)
+                scanner.extend(text)
+                if scanner.stopped:
+                    reason = "stop"
+                    break
+                if on_text is not None:
+                    piece = scanner.release()
+                    if piece:
+                        on_text(piece)
+        finally:
+            source.close()
+        if on_text is not None:
+            rest = scanner.release(final=True)
+            if rest:
+                on_text(rest)
+        elapsed = time.perf_counter() - started
+        response = scanner.text.strip() if s.mode == "chat" else scanner.text
         if s.mode == "chat":
             self.history.append((message, response))
-        return Reply(message, prompt, response, len(generated), seconds, reason, self.unknown_characters(prompt),
-                     len(ids) > usable)
+        return Reply(message=message, prompt=prompt, response=response, tokens=len(produced), seconds=elapsed,
+                     stop_reason=reason, unknown_characters=self.unknown_characters(prompt),
+                     truncated_context=len(ids) > self._context_limit())
 
 
-# ---- which model --------------------------------------------------------------------------------------------
+# ---- choosing a model -----------------------------------------------------------------------------------------------
+_RUN_NAME = re.compile(r"(\d+)(?:-(\d+))?")
+
+
 def run_folders(root: Path = RUNS_DIR) -> list[Path]:
-    """Archived runs (``<epoch>`` or ``<epoch>-<n>``), oldest first."""
+    """Archived runs, oldest first: folders named ``<epoch seconds>`` or ``<epoch seconds>-<n>``."""
     root = Path(root)
     if not root.is_dir():
         return []
-    keyed = []
-    for path in root.iterdir():
-        m = re.fullmatch(r"(\d+)(?:-(\d+))?", path.name)
-        if path.is_dir() and m:
-            keyed.append(((int(m.group(1)), int(m.group(2) or 0)), path))
-    return [p for _, p in sorted(keyed)]
+    runs = []
+    for entry in root.iterdir():
+        match = _RUN_NAME.fullmatch(entry.name)
+        if match and entry.is_dir():
+            runs.append((int(match[1]), int(match[2] or 0), entry))
+    return [path for *_, path in sorted(runs)]
 
 
 def usable_model(run: Path) -> Optional[tuple[Path, Optional[Path]]]:
-    """(checkpoint dir, adapter dir) of an archived run, or None when it holds no model."""
+    """(checkpoint, adapter) held by an archived run: its trained or merged model, else its adapter over the base the
+    adapter names; None when the run holds none of them."""
     run = Path(run)
-    for sub in ("model", "merged"):
-        if (run / sub / "model.pt").exists():
-            return run / sub, None
-    if (run / "adapter" / "adapter.pt").exists():
-        meta = json.loads((run / "adapter" / "finetune_metadata.json").read_text())
-        return Path(meta["base_checkpoint"]), run / "adapter"
+    for folder in (run / "model", run / "merged"):
+        if (folder / "model.pt").exists():
+            return folder, None
+    adapter = run / "adapter"
+    if (adapter / "adapter.pt").exists():
+        base = json.loads((adapter / "finetune_metadata.json").read_text())["base_checkpoint"]
+        return Path(base), adapter
     return None
 
 
 def resolve_model(checkpoint: Optional[Path], adapter: Optional[Path], run: Optional[str], latest: bool,
                   root: Path = RUNS_DIR) -> tuple[Path, Optional[Path]]:
+    """An explicit checkpoint wins; then a named run (epoch name under ``root`` or a path); then the newest run that
+    holds a model; otherwise the default output folder."""
     if checkpoint is not None:
         return Path(checkpoint), adapter
     if run is not None:
@@ -213,16 +272,16 @@ def resolve_model(checkpoint: Optional[Path], adapter: Optional[Path], run: Opti
             raise FileNotFoundError(f"no model found in run '{run}' (looked in {folder})")
         return found
     if latest:
-        for folder in reversed(run_folders(root)):
-            found = usable_model(folder)
-            if found is not None:
-                return found
-        raise FileNotFoundError(f"no archived run with a model under {root}")
+        found = next(filter(None, map(usable_model, reversed(run_folders(root)))), None)
+        if found is None:
+            raise FileNotFoundError(f"no archived run with a model under {root}")
+        return found
     return DEFAULT_CHECKPOINT, adapter
 
 
 def load_for_chat(checkpoint: Path, adapter: Optional[Path], quantize: int, device: torch.device):
-    """(model, tokenizer): an adapter over its (quantised) base, or the checkpoint, optionally quantised in memory."""
+    """(model, tokenizer): the adapter applied over its base, or the checkpoint, with experts quantised in memory when
+    ``quantize`` is 4 or 8."""
     from ..data.pipeline import load_tokenizer
 
     if adapter is not None:
@@ -241,122 +300,131 @@ def load_for_chat(checkpoint: Path, adapter: Optional[Path], quantize: int, devi
     return model.eval(), load_tokenizer(checkpoint)
 
 
-# ---- batches of test messages --------------------------------------------------------------------------------
+# ---- batches of test messages ----------------------------------------------------------------------------------------
+_OVERRIDABLE = ("mode", "tokens", "temperature", "top_k", "top_p", "seed")
+
+
 def read_messages(path: Path) -> list[dict]:
-    """``.jsonl``: ``{"message"|"prompt", "expect"?: str|list, "tokens", "temperature", "mode", ...}`` per line;
-    anything else: one message per line. Blank lines and ``#`` comments are skipped."""
+    """Messages to send. A ``.jsonl`` file holds one object per line with ``message`` (or ``prompt``), optional
+    ``expect`` (a string or a list of strings that must appear in the reply) and per-message settings; any other
+    file holds one message per line. Blank lines and lines starting with ``#`` are skipped."""
     path = Path(path)
+    structured = path.suffix == ".jsonl"
     items = []
-    for number, line in enumerate(path.read_text(encoding="utf-8").splitlines(), start=1):
-        if not line.strip() or line.lstrip().startswith("#"):
+    for number, raw in enumerate(path.read_text(encoding="utf-8").splitlines(), start=1):
+        if not raw.strip() or raw.lstrip().startswith("#"):
             continue
-        if path.suffix == ".jsonl":
-            try:
-                item = json.loads(line)
-            except json.JSONDecodeError as error:
-                raise ValueError(f"{path}:{number}: not valid JSON ({error})") from error
-            message = item.get("message", item.get("prompt"))
-            if message is None:
-                raise ValueError(f"{path}:{number}: needs a 'message' field")
-            item["message"] = message
-        else:
-            item = {"message": line}
-        expect = item.get("expect")
-        item["expect"] = [expect] if isinstance(expect, str) else list(expect or [])
-        items.append(item)
+        if not structured:
+            items.append({"message": raw, "expect": []})
+            continue
+        try:
+            item = json.loads(raw)
+        except json.JSONDecodeError as error:
+            raise ValueError(f"{path}:{number}: not valid JSON ({error})") from error
+        text = item["message"] if "message" in item else item.get("prompt")
+        if text is None:
+            raise ValueError(f"{path}:{number}: needs a 'message' field")
+        wanted = item.get("expect") or []
+        items.append({**item, "message": text, "expect": [wanted] if isinstance(wanted, str) else list(wanted)})
     return items
 
 
 def run_batch(session: ChatSession, items: Sequence[dict], conversation: bool,
               emit: Callable[[dict], None]) -> list[dict]:
-    """Send each message (per-message settings override the session's for that message only)."""
+    """Send every message; a message's own settings apply to it alone. Each result records whether every expected
+    string appeared (``passed`` is None when nothing was expected)."""
+    base = session.settings
     results = []
-    base = asdict(session.settings)
     for item in items:
         if not conversation:
             session.reset()
-        overrides = {k: item[k] for k in ("mode", "tokens", "temperature", "top_k", "top_p", "seed") if k in item}
-        session.settings = Settings(**{**base, **overrides})
+        session.settings = replace(base, **{k: item[k] for k in _OVERRIDABLE if k in item})
         try:
             reply = session.send(item["message"])
         finally:
-            session.settings = Settings(**base)
+            session.settings = base
         missing = [needle for needle in item["expect"] if needle not in reply.response]
-        result = {**asdict(reply), "tokens_per_second": reply.tokens_per_second, "expect": item["expect"],
-                  "passed": None if not item["expect"] else not missing, "missing": missing}
-        results.append(result)
+        result = dict(asdict(reply), tokens_per_second=reply.tokens_per_second, expect=item["expect"],
+                      passed=(not missing) if item["expect"] else None, missing=missing)
         emit(result)
+        results.append(result)
     return results
 
 
-# ---- interactive session -------------------------------------------------------------------------------------
+# ---- interactive session ---------------------------------------------------------------------------------------------
 HELP = """commands:
-  /help                  this text
-  /reset                 forget the conversation (chat mode)
-  /mode complete|chat    switch modes
-  /set NAME VALUE        temperature, top_k, top_p, tokens, seed (a number or "none"), system (text)
-  /show                  current settings
-  /history               the conversation so far
-  /save FILE             write the conversation as JSON lines
-  /quit                  leave (also Ctrl-D)
-anything else is sent to the model."""
+  /help                  show this list
+  /reset                 start the conversation over (chat mode)
+  /mode complete|chat    change mode (and start over)
+  /set NAME VALUE        temperature, top_k, top_p, tokens, seed (a number or "none") or system (text)
+  /show                  print the current settings
+  /history               print the conversation so far
+  /save FILE             write the conversation to FILE as JSON lines
+  /quit                  leave (Ctrl-D works too)
+any other line is sent to the model."""
+
+_SETTING_TYPES = {"temperature": float, "top_p": float, "top_k": int, "tokens": int,
+                  "seed": lambda v: None if v.lower() == "none" else int(v), "system": str}
 
 
 def apply_setting(settings: Settings, name: str, value: str) -> None:
-    """Change one setting; a value that fails validation leaves the settings untouched."""
-    casts = {"temperature": float, "top_p": float, "top_k": int, "tokens": int}
-    trial = Settings(**asdict(settings))
-    if name == "seed":
-        trial.seed = None if value.lower() == "none" else int(value)
-    elif name == "system":
-        trial.system = value
-    elif name in casts:
-        setattr(trial, name, casts[name](value))
-    else:
-        raise ValueError(f"unknown setting '{name}' (try: temperature, top_k, top_p, tokens, seed, system)")
-    trial.validate()
-    setattr(settings, name, getattr(trial, name))
+    """Change one setting in place; a value that does not parse or validate leaves every setting as it was."""
+    if name not in _SETTING_TYPES:
+        raise ValueError(f"unknown setting '{name}' (try: {', '.join(_SETTING_TYPES)})")
+    candidate = replace(settings, **{name: _SETTING_TYPES[name](value)})
+    candidate.validate()
+    setattr(settings, name, getattr(candidate, name))
 
 
-def _command(session: ChatSession, command: str, rest: str, out) -> bool:
-    """Run one ``/command``; returns False to leave the session."""
-    if command in {"quit", "exit"}:
-        return False
-    if command == "help":
-        print(HELP, file=out)
-    elif command == "reset":
-        session.reset()
-        print("conversation cleared", file=out)
-    elif command == "mode":
-        mode = rest.strip()
-        Settings(**{**asdict(session.settings), "mode": mode}).validate()
-        session.settings.mode = mode
-        session.reset()
-        print(f"mode: {mode}", file=out)
-    elif command == "set":
-        name, _, value = rest.strip().partition(" ")
-        apply_setting(session.settings, name, value.strip())
-        print(f"{name} = {getattr(session.settings, name)!r}", file=out)
-    elif command == "show":
-        print(json.dumps(asdict(session.settings)), file=out)
-    elif command == "history":
-        for user, reply in session.history:
-            print(f"you: {user}\nmodel: {reply}", file=out)
-    elif command == "save":
-        target = Path(rest.strip())
-        target.write_text("".join(json.dumps({"user": u, "assistant": a}) + "\n" for u, a in session.history))
-        print(f"saved {len(session.history)} turns to {target}", file=out)
-    else:
-        print(f"unknown command /{command}; /help lists them", file=out)
-    return True
+def _cmd_help(session, rest, out):
+    print(HELP, file=out)
+
+
+def _cmd_reset(session, rest, out):
+    session.reset()
+    print("conversation cleared", file=out)
+
+
+def _cmd_mode(session, rest, out):
+    mode = rest.strip()
+    replace(session.settings, mode=mode).validate()
+    session.settings.mode = mode
+    session.reset()
+    print(f"mode: {mode}", file=out)
+
+
+def _cmd_set(session, rest, out):
+    name, _, value = rest.strip().partition(" ")
+    apply_setting(session.settings, name, value.strip())
+    print(f"{name} = {getattr(session.settings, name)!r}", file=out)
+
+
+def _cmd_show(session, rest, out):
+    print(json.dumps(asdict(session.settings)), file=out)
+
+
+def _cmd_history(session, rest, out):
+    for user, answer in session.history:
+        print(f"you: {user}\nmodel: {answer}", file=out)
+
+
+def _cmd_save(session, rest, out):
+    target = Path(rest.strip())
+    target.write_text("".join(json.dumps({"user": u, "assistant": a}) + "\n" for u, a in session.history))
+    print(f"saved {len(session.history)} turns to {target}", file=out)
+
+
+_COMMANDS = {"help": _cmd_help, "reset": _cmd_reset, "mode": _cmd_mode, "set": _cmd_set, "show": _cmd_show,
+             "history": _cmd_history, "save": _cmd_save}
 
 
 def repl(session: ChatSession, out=None, ask: Optional[Callable[[str], str]] = None,
          transcript: Optional[Callable[[dict], None]] = None, show_stats: bool = True) -> None:
+    """Read lines until ``/quit`` or end of input; ``/commands`` change the session, other lines are sent."""
     out = sys.stdout if out is None else out
     ask = input if ask is None else ask
     try:
-        import readline  # noqa: F401  (line editing where available)
+        import readline  # noqa: F401  (line editing where the platform has it)
     except ImportError:
         pass
     print(f"QuantaWeave chat ({session.settings.mode} mode). /help for commands, /quit to leave.", file=out)
@@ -369,10 +437,15 @@ def repl(session: ChatSession, out=None, ask: Optional[Callable[[str], str]] = N
         if not line.strip():
             continue
         if line.startswith("/"):
-            command, _, rest = line[1:].partition(" ")
+            name, _, rest = line[1:].partition(" ")
+            if name in ("quit", "exit"):
+                return
+            handler = _COMMANDS.get(name)
+            if handler is None:
+                print(f"unknown command /{name}; /help lists them", file=out)
+                continue
             try:
-                if not _command(session, command, rest, out):
-                    return
+                handler(session, rest, out)
             except (ValueError, OSError) as error:
                 print(f"error: {error}", file=out)
             continue
@@ -382,13 +455,55 @@ def repl(session: ChatSession, out=None, ask: Optional[Callable[[str], str]] = N
         print(file=out)
         if reply.unknown_characters:
             print("  note: not in this model's vocabulary and replaced by <unk>: "
-                  + " ".join(map(repr, reply.unknown_characters)), file=out)
+                  + " ".join(repr(c) for c in reply.unknown_characters), file=out)
         if show_stats:
             print(f"  [{reply.tokens} tokens, {reply.tokens_per_second:.0f} tok/s, stopped: {reply.stop_reason}]",
                   file=out)
         if transcript is not None:
-            transcript({**asdict(reply), "tokens_per_second": reply.tokens_per_second,
-                        "settings": asdict(session.settings)})
+            transcript(dict(asdict(reply), tokens_per_second=reply.tokens_per_second,
+                            settings=asdict(session.settings)))
+
+
+# ---- command line ----------------------------------------------------------------------------------------------------
+def build_parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    which = p.add_argument_group("which model")
+    which.add_argument("--checkpoint", type=Path, help=f"checkpoint directory to load (default {DEFAULT_CHECKPOINT})")
+    which.add_argument("--run", help="archived run to load, by its epoch-second name under --runs-dir or by path")
+    which.add_argument("--latest", action="store_true", help="load the most recent archived run that holds a model")
+    which.add_argument("--adapter", type=Path, help="QLoRA adapter folder, applied on top of --checkpoint")
+    which.add_argument("--quantize", type=int, choices=(0, 4, 8), default=0,
+                       help="quantise the experts to int4 or int8 after loading (0: keep them as saved)")
+    which.add_argument("--runs-dir", type=Path, default=RUNS_DIR)
+    send = p.add_argument_group("what to send")
+    send.add_argument("-m", "--message", action="append", default=[],
+                      help="a message to send; give it several times for several messages")
+    send.add_argument("--messages-file", type=Path,
+                      help="messages to send: one per line, or JSON lines with message, expect and settings")
+    send.add_argument("--conversation", action="store_true", help="keep the history between the messages of a batch")
+    send.add_argument("--json", action="store_true", help="write each reply as a JSON line rather than plain text")
+    send.add_argument("--transcript", type=Path, help="log each message and reply as a line in this JSONL file")
+    send.add_argument("--interactive", action="store_true",
+                      help="start the interactive session even when standard input is not a terminal")
+    send.add_argument("--quiet", action="store_true", help="print replies only, without timing lines or notes")
+    gen = p.add_argument_group("generation")
+    gen.add_argument("--mode", choices=("complete", "chat"), default="complete")
+    gen.add_argument("--system", default="", help="system text that opens the conversation (chat mode)")
+    gen.add_argument("--tokens", type=int, default=200, help="upper limit of generated tokens for each reply")
+    gen.add_argument("--temperature", type=float, default=0.8,
+                     help="sampling temperature; 0 always takes the most likely token")
+    gen.add_argument("--top-k", type=int, default=0)
+    gen.add_argument("--top-p", type=float, default=1.0)
+    gen.add_argument("--seed", type=int, help="seed for the sampler, for repeatable replies")
+    gen.add_argument("--stop", action="append", default=[], help="end the reply at this text; may be given several times")
+    gen.add_argument("--no-cache", action="store_true",
+                     help="run a full forward pass per token instead of decoding with the KV cache")
+    gen.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")
+    gen.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
+    from .common import describe_options
+
+    describe_options(p)
+    return p
 
 
 class _NullStream:
@@ -399,39 +514,26 @@ class _NullStream:
         pass
 
 
-def build_parser() -> argparse.ArgumentParser:
-    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    m = p.add_argument_group("which model")
-    m.add_argument("--checkpoint", type=Path, help=f"a checkpoint directory (default {DEFAULT_CHECKPOINT})")
-    m.add_argument("--run", help="archived run to load, by its epoch-second name under --runs-dir or by path")
-    m.add_argument("--latest", action="store_true", help="load the most recent archived run that holds a model")
-    m.add_argument("--adapter", type=Path, help="QLoRA adapter folder, applied on top of --checkpoint")
-    m.add_argument("--quantize", type=int, choices=(0, 4, 8), default=0, help="quantise the experts in memory")
-    m.add_argument("--runs-dir", type=Path, default=RUNS_DIR)
-    s = p.add_argument_group("sending messages")
-    s.add_argument("-m", "--message", action="append", default=[], help="a message to send; give it several times for several messages")
-    s.add_argument("--messages-file", type=Path, help=".txt (one per line) or .jsonl ({message, expect, ...})")
-    s.add_argument("--conversation", action="store_true", help="batch mode keeps the history between messages")
-    s.add_argument("--json", action="store_true", help="write each reply as a JSON line rather than plain text")
-    s.add_argument("--transcript", type=Path, help="log each message and reply as a line in this JSONL file")
-    s.add_argument("--interactive", action="store_true", help="always run the interactive session (even on a pipe)")
-    s.add_argument("--quiet", action="store_true", help="print replies only, without timing lines or notes")
-    g = p.add_argument_group("generation")
-    g.add_argument("--mode", choices=("complete", "chat"), default="complete")
-    g.add_argument("--system", default="", help="system text that opens the conversation (chat mode)")
-    g.add_argument("--tokens", type=int, default=200, help="upper limit of generated tokens for each reply")
-    g.add_argument("--temperature", type=float, default=0.8, help="sampling temperature; 0 always takes the most likely token")
-    g.add_argument("--top-k", type=int, default=0)
-    g.add_argument("--top-p", type=float, default=1.0)
-    g.add_argument("--seed", type=int, help="seed for the sampler, for repeatable replies")
-    g.add_argument("--stop", action="append", default=[], help="end the reply at this text; may be given several times")
-    g.add_argument("--no-cache", action="store_true", help="plain forward pass per token instead of the KV cache")
-    g.add_argument("--precision", choices=("auto", "bf16", "fp16", "fp32"), default="auto")
-    g.add_argument("--device", choices=("auto", "cuda", "rocm", "xpu", "cpu"), default="auto")
-    from .common import describe_options
+def _batch_printer(args, status, session, write):
+    def emit(result: dict) -> None:
+        if write is not None:
+            write(dict(result, settings=asdict(session.settings)))
+        if args.json:
+            print(json.dumps(result), flush=True)
+            return
+        print(f"> {result['message']}\n{result['response']}")
+        if args.quiet:
+            return
+        if result["unknown_characters"]:
+            print("  note: replaced by <unk>: " + " ".join(map(repr, result["unknown_characters"])), file=status)
+        if result["passed"] is None:
+            verdict = ""
+        else:
+            verdict = "  PASS" if result["passed"] else f"  FAIL (missing {result['missing']})"
+        print(f"  [{result['tokens']} tokens, {result['tokens_per_second']:.0f} tok/s, "
+              f"stopped: {result['stop_reason']}]{verdict}", file=status)
 
-    describe_options(p)
-    return p
+    return emit
 
 
 def main(argv: Optional[Sequence[str]] = None) -> int:
@@ -440,14 +542,14 @@ def main(argv: Optional[Sequence[str]] = None) -> int:
 
     parser = build_parser()
     args = parser.parse_args(argv)
-    settings = Settings(mode=args.mode, tokens=args.tokens, temperature=args.temperature, top_k=args.top_k,
-                        top_p=args.top_p, seed=args.seed, stop=list(args.stop), system=args.system)
+    chosen = {f.name: getattr(args, f.name) for f in fields(Settings) if f.name != "stop"}
+    settings = Settings(**chosen, stop=list(args.stop))
     try:
         settings.validate()
         checkpoint, adapter = resolve_model(args.checkpoint, args.adapter, args.run, args.latest, args.runs_dir)
-        items = [{"message": msg, "expect": []} for msg in args.message]
+        items = [{"message": text, "expect": []} for text in args.message]
         if args.messages_file is not None:
-            items += read_messages(args.messages_file)
+            items.extend(read_messages(args.messages_file))
         if args.interactive and items:
             parser.error("--interactive cannot be combined with --message/--messages-file")
         if not items and not args.interactive and not sys.stdin.isatty():
@@ -458,47 +560,35 @@ def main(argv: Optional[Sequence[str]] = None) -> int:
     model, tokenizer = load_for_chat(checkpoint, adapter, args.quantize, device)
     precision = choose_precision(detect(device.type), args.precision)
     session = ChatSession(model, tokenizer, device, precision, settings, use_cache=not args.no_cache)
-    status = sys.stderr if not args.quiet else _NullStream()
-    print(f"model: {checkpoint}" + (f" + adapter {adapter}" if adapter else "")
-          + f"  device: {device}  precision: {precision}"
-          + (f"  experts quantized to int{args.quantize}" if args.quantize and adapter is None else "")
-          + f"  decoding: {session.cache_note}", file=status)
+    status = _NullStream() if args.quiet else sys.stderr
+    described = f"model: {checkpoint}" + (f" + adapter {adapter}" if adapter else "")
+    described += f"  device: {device}  precision: {precision}"
+    if args.quantize and adapter is None:
+        described += f"  experts quantized to int{args.quantize}"
+    print(described + f"  decoding: {session.cache_note}", file=status)
     log = None
     if args.transcript is not None:
         args.transcript.parent.mkdir(parents=True, exist_ok=True)
         log = args.transcript.open("a", encoding="utf-8")
-    write = (lambda entry: (log.write(json.dumps(entry) + "\n"), log.flush())) if log else None
+
+    def write(entry: dict) -> None:
+        log.write(json.dumps(entry) + "\n")
+        log.flush()
+
     try:
         if not items:
-            repl(session, transcript=write, show_stats=not args.quiet)
+            repl(session, transcript=write if log else None, show_stats=not args.quiet)
             return 0
-
-        def emit(result: dict) -> None:
-            if write:
-                write({**result, "settings": asdict(session.settings)})
-            if args.json:
-                print(json.dumps(result), flush=True)
-                return
-            print(f"> {result['message']}")
-            print(result["response"])
-            if args.quiet:
-                return
-            if result["unknown_characters"]:
-                print(f"  note: replaced by <unk>: {' '.join(map(repr, result['unknown_characters']))}", file=status)
-            verdict = "" if result["passed"] is None else (
-                "  PASS" if result["passed"] else f"  FAIL (missing {result['missing']})")
-            print(f"  [{result['tokens']} tokens, {result['tokens_per_second']:.0f} tok/s, "
-                  f"stopped: {result['stop_reason']}]{verdict}", file=status)
-
-        results = run_batch(session, items, args.conversation, emit)
+        results = run_batch(session, items, args.conversation,
+                            _batch_printer(args, status, session, write if log else None))
     finally:
-        if log:
+        if log is not None:
             log.close()
-    failed = [r for r in results if r["passed"] is False]
     checked = [r for r in results if r["passed"] is not None]
+    failures = sum(1 for r in checked if not r["passed"])
     if checked and not args.quiet:
-        print(f"{len(checked) - len(failed)}/{len(checked)} checks passed", file=status)
-    return 1 if failed else 0
+        print(f"{len(checked) - failures}/{len(checked)} checks passed", file=status)
+    return 1 if failures else 0
 
 
 if __name__ == "__main__":
