@@ -119,45 +119,50 @@ class RoutingMonitor:
         self.window_updates += 1
 
     # ---- window metrics ---------------------------------------------------------------------------
-    def imbalance(self) -> Optional[float]:
-        """Mean over layers of the coefficient of variation of the routed load (0 = perfectly even)."""
+    def _window_shares(self) -> Optional[Tensor]:
+        """Each expert's share of the routes its layer's router asked for in this window: ``[layers, experts]``,
+        rows summing to 1 (None before any update)."""
         if not self.window_updates:
             return None
-        counts = self.window_assigned.double()
-        return float((counts.std(dim=1, unbiased=False) / counts.mean(dim=1).clamp(min=1e-9)).mean())
+        wanted = self.window_assigned.double()
+        return wanted / wanted.sum(dim=1, keepdim=True).clamp(min=1)
+
+    def imbalance(self) -> Optional[float]:
+        """How unevenly routes are spread, averaged over layers: the spread (population standard deviation) of the
+        experts' shares relative to the mean share; 0 when every expert gets as many routes as the others."""
+        shares = self._window_shares()
+        if shares is None:
+            return None
+        mean = shares.mean(dim=1, keepdim=True)
+        spread = (shares - mean).square().mean(dim=1).sqrt()
+        return float((spread / mean.squeeze(1).clamp(min=1e-9)).mean())
 
     def active_fraction(self, floor: float = 0.1) -> Optional[float]:
-        """Share of experts that receive at least ``floor`` of an even share of the routes."""
-        if not self.window_updates:
+        """Fraction of (layer, expert) pairs whose share of the routes is at least ``floor`` times the share every
+        expert would get under perfectly even routing."""
+        shares = self._window_shares()
+        if shares is None:
             return None
-        counts = self.window_assigned.double()
-        even = counts.sum(dim=1, keepdim=True) / self.num_experts
-        return float((counts >= floor * even).double().mean())
+        return float((shares * self.num_experts >= floor).double().mean())
 
     def snapshot(self, step: int, reset: bool = True) -> dict:
+        """Summarise the window per layer, append it to ``snapshots`` (and to routing_log.jsonl), then start a new
+        window unless ``reset`` is False."""
         if not self.window_updates:
             return {}
-        n = self.window_updates
-        assigned = self.window_assigned.double().cpu()
-        load = self.window_load.double().cpu()
-        entropy = (self.window_entropy / n).cpu().tolist()
-        confidence = (self.window_confidence / n).cpu().tolist()
-        hist = (self.window_confidence_hist / n).cpu().tolist()
-        drops = self.window_drops_by_expert.cpu().tolist()
-        routes = assigned.sum(dim=1).clamp(min=1)
-        layers = []
-        for layer in range(self.num_layers):
-            layers.append({
-                "utilization": (load[layer] / load[layer].sum().clamp(min=1)).tolist(),
-                "requested_share": (assigned[layer] / routes[layer]).tolist(),
-                "entropy": entropy[layer],
-                "entropy_max": math.log(self.num_experts),
-                "confidence": confidence[layer],
-                "confidence_hist": hist[layer],
-                "drop_rate": float(1 - load[layer].sum() / routes[layer]),
-                "drops_by_expert": drops[layer],
-                "dead_experts": int((assigned[layer] == 0).sum()),
-            })
+        windows = self.window_updates
+        wanted = self.window_assigned.double().cpu()
+        served = self.window_load.double().cpu()
+        routes = wanted.sum(dim=1).clamp(min=1)
+        per_layer = zip(served / served.sum(dim=1, keepdim=True).clamp(min=1), wanted / routes[:, None],
+                        (self.window_entropy / windows).cpu().tolist(), (self.window_confidence / windows).cpu().tolist(),
+                        (self.window_confidence_hist / windows).cpu().tolist(), 1 - served.sum(dim=1) / routes,
+                        self.window_drops_by_expert.cpu().tolist(), (wanted == 0).sum(dim=1).tolist())
+        ceiling = math.log(self.num_experts)
+        layers = [{"utilization": used.tolist(), "requested_share": asked.tolist(), "entropy": entropy,
+                   "entropy_max": ceiling, "confidence": confidence, "confidence_hist": histogram,
+                   "drop_rate": float(dropped), "drops_by_expert": drops, "dead_experts": int(dead)}
+                  for used, asked, entropy, confidence, histogram, dropped, drops, dead in per_layer]
         record = {"step": step, "layers": layers, "imbalance": self.imbalance(),
                   "active_fraction": self.active_fraction(), "drops_by_token_class": self.window_drops_by_class}
         self.snapshots.append(record)

@@ -68,3 +68,14 @@ def test_svg_helpers_render_valid_markup():
                 bar_chart_svg({"x": 1.0, "y": 2.0}, "t")):
         assert svg.startswith("<svg") and svg.rstrip().endswith("</svg>")
     assert bar_chart_svg({"x": 1.0, "y": 2.0, "z": 3.0}, "t").count("<rect") >= 3
+
+
+def test_window_imbalance_and_active_fraction_values():
+    monitor = RoutingMonitor(2, 2, 1)
+    monitor.window_updates = 1
+    monitor.window_assigned = torch.tensor([[5, 5], [30, 10]])
+    # layer 0 is even (0); layer 1 has shares 0.75 / 0.25: spread 0.25 over a mean share of 0.5 -> 0.5
+    assert monitor.imbalance() == pytest.approx(0.25)
+    monitor.window_assigned = torch.tensor([[100, 0], [95, 5]])
+    # an even share is 0.5; at floor 0.1 an expert needs 5 % of the routes: 3 of the 4 (layer, expert) pairs
+    assert monitor.active_fraction(0.1) == pytest.approx(0.75)
