@@ -224,23 +224,31 @@ class PipelineEngine:
 
 
 def clip_grad_norm_pipeline(model, ctx: PipelineContext, max_norm: float, optimizer=None):
-    """Global gradient norm across stages (every parameter lives on exactly one stage), applied identically."""
+    """Clip by the norm of the whole model's gradient and return that norm (before clipping).
+
+    Each parameter lives on exactly one stage, so the squared norm of the full gradient is the sum of the stages'
+    squared norms: one all-reduce over the pipeline group. With a sharded optimizer the replicas of a stage hold
+    disjoint gradient shards; their squared norms are summed over the data-parallel group first, and the clip factor
+    is handed to the optimizer, which applies it inside its update."""
     if optimizer is not None and hasattr(optimizer, "shard_sumsq"):
-        sq = optimizer.shard_sumsq()
+        squared = optimizer.shard_sumsq()
         if ctx.dp_size > 1:
-            dist.all_reduce(sq, group=ctx.dp_group)
+            dist.all_reduce(squared, group=ctx.dp_group)
+        grads = []
     else:
-        sq = torch.zeros((), dtype=torch.float64, device=ctx.device)
-        for p in model.parameters():
-            if p.grad is not None:
-                sq = sq + p.grad.detach().double().pow(2).sum()
-    dist.all_reduce(sq, group=ctx.pp_group)
-    total = sq.sqrt()
-    coef = torch.clamp(max_norm / (total + 1e-6), max=1.0)
+        grads = [p.grad for p in model.parameters() if p.grad is not None]
+        per_tensor = [torch.linalg.vector_norm(g, dtype=torch.float64) for g in grads]
+        squared = (torch.stack(per_tensor).square().sum() if per_tensor
+                   else torch.zeros((), dtype=torch.float64, device=ctx.device))
+    dist.all_reduce(squared, group=ctx.pp_group)
+    norm = squared.sqrt()
+    factor = (max_norm / (norm + 1e-6)).clamp(max=1.0)
     if optimizer is not None and hasattr(optimizer, "set_clip_coefficient"):
-        optimizer.set_clip_coefficient(coef, total)
-        return float(total)
-    for p in model.parameters():
-        if p.grad is not None:
-            p.grad.mul_(coef.to(p.grad.dtype))
-    return float(total)
+        optimizer.set_clip_coefficient(factor, norm)
+        return float(norm)
+    by_dtype: dict = {}
+    for g in grads:
+        by_dtype.setdefault(g.dtype, []).append(g)
+    for dtype, group in by_dtype.items():
+        torch._foreach_mul_(group, factor.to(dtype))
+    return float(norm)
