@@ -1,27 +1,24 @@
 """Tokenizers, domain-tagged token corpora, window datasets, curriculum, domain mixtures and batch streams.
 
-Behavioural parity with the reference ``src/data_pipeline.py``:
+The data formats and public names follow the reference's ``src/data_pipeline.py``: JSONL rows with an optional
+``domain`` field; character, byte-level BPE and SentencePiece tokenizers with ``<unk>`` = 0 and ``<eos>`` = 1 and
+their saved files; packed corpora as ``tokens.bin`` + ``meta.json`` + ``tokenizer/``.
 
-* JSONL rows with an optional ``domain`` field (``read_rows`` :32); char / byte-level BPE / SentencePiece tokenizers
-  with ``<unk>``=0, ``<eos>``=1 (:55-198); per-domain token corpora in memory or memmapped from ``tokens.bin`` +
-  ``meta.json`` (:234-335); non-overlapping ``seq+1`` windows that never cross a domain (:338-409);
-  curriculum difficulty scores (:420); domain mixtures (:490).
-* ``BatchStream.batch(step)`` is a pure function of (seed, step, rank layout): a ``torch.Generator`` seeded with
-  ``seed * 1_000_003 + step`` draws one global batch and each rank takes its disjoint slice (:517-590). The same
-  seeding rule is kept so that resumed runs draw the same windows.
-
-Additions: ``SyntheticTokenStream`` (seeded uniform or Zipf token ids, the benchmark inputs) with the same
-``batch(step)`` / ``state(step)`` contract, and a pinned-host staging helper for the end-to-end bench path.
+Here a corpus is one flat token array cut into per-domain segments; windows of ``sequence_length + 1`` tokens are
+laid out inside segments only; ``BatchStream.batch(step)`` is a pure function of (seed, step, rank layout), so a
+resumed run draws exactly the windows an uninterrupted one would. ``SyntheticTokenStream`` (seeded uniform or Zipf
+token ids, the benchmark inputs) follows the same ``batch(step)`` / ``state(step)`` contract.
 """
 
 from __future__ import annotations
 
+import copy
 import hashlib
+import itertools
 import json
 import math
-import shutil
+import re
 import unicodedata
-from array import array
 from dataclasses import dataclass
 from pathlib import Path
 from typing import Iterable, Iterator, Optional, Sequence
@@ -251,108 +248,119 @@ class Segment:
 
 
 class TokenCorpus:
-    """One flat token stream split into per-domain segments (in memory or memmapped)."""
+    """All token ids in one flat array (a tensor, or a read-only memmap for packed corpora), cut into one segment per
+    domain. Every document ends with ``<eos>``; segments never overlap."""
 
     def __init__(self, data, segments: list[Segment]) -> None:
         self._data = data
         self.segments = segments
-        self.domains: list[str] = []
-        for seg in segments:
-            if seg.domain not in self.domains:
-                self.domains.append(seg.domain)
+        self.domains = list(dict.fromkeys(seg.domain for seg in segments))
 
     def read(self, start: int, stop: int) -> Tensor:
-        if isinstance(self._data, Tensor):
-            return self._data[start:stop].long()
+        piece = self._data[start:stop]
+        if isinstance(piece, Tensor):
+            return piece.long()
         import numpy as np
 
-        return torch.from_numpy(np.asarray(self._data[start:stop], dtype=np.int64))
+        return torch.from_numpy(np.array(piece, dtype=np.int64))
 
     def __len__(self) -> int:
         return sum(seg.length for seg in self.segments)
 
 
-def build_corpus(paths: Sequence[Path], tokenizer, limit: Optional[int] = None, redactor=None) -> TokenCorpus:
-    """Tokenise JSONL rows into per-domain streams, each document followed by ``<eos>``."""
-    streams: dict[str, array] = {}
+def _documents(paths: Sequence[Path], tokenizer, limit: Optional[int], redactor) -> Iterator[tuple[str, list[int]]]:
+    """(domain, token ids ending with ``<eos>``) for every row."""
     for domain, text in read_rows(paths, limit, redactor):
-        stream = streams.setdefault(domain, array("i"))
-        stream.extend(tokenizer.encode(text))
-        stream.append(tokenizer.eos_id)
-    joined = array("i")
-    segments = []
-    for domain, stream in streams.items():
-        segments.append(Segment(domain, len(joined), len(stream)))
-        joined.extend(stream)
-    data = torch.tensor(joined, dtype=torch.int32) if len(joined) else torch.empty(0, dtype=torch.int32)
-    return TokenCorpus(data, segments)
+        yield domain, tokenizer.encode(text) + [tokenizer.eos_id]
 
 
-def write_token_bin(paths: Sequence[Path], tokenizer, out_dir: Path, limit: Optional[int] = None, redactor=None) -> dict:
-    """Tokenise JSONL into a memmappable ``tokens.bin`` (uint16/uint32) plus ``meta.json`` and the tokenizer."""
+def build_corpus(paths: Sequence[Path], tokenizer, limit: Optional[int] = None, redactor=None) -> TokenCorpus:
+    """Tokenise the rows in memory: the documents of each domain back to back, domains in order of first row."""
+    per_domain: dict[str, list[int]] = {}
+    for domain, ids in _documents(paths, tokenizer, limit, redactor):
+        per_domain.setdefault(domain, []).extend(ids)
+    lengths = [len(ids) for ids in per_domain.values()]
+    offsets = [0, *itertools.accumulate(lengths)]
+    segments = [Segment(domain, offsets[i], lengths[i]) for i, domain in enumerate(per_domain)]
+    flat = [token for ids in per_domain.values() for token in ids]
+    return TokenCorpus(torch.tensor(flat, dtype=torch.int32), segments)
+
+
+class _Spool:
+    """Token ids of one domain appended to a temporary file as they are produced (bounded memory)."""
+
+    def __init__(self, path: Path, dtype) -> None:
+        self.path, self.dtype, self.length = path, dtype, 0
+        self.handle = path.open("wb")
+
+    def add(self, ids: list[int]) -> None:
+        import numpy as np
+
+        np.asarray(ids, dtype=self.dtype).tofile(self.handle)
+        self.length += len(ids)
+
+
+def write_token_bin(paths: Sequence[Path], tokenizer, out_dir: Path, limit: Optional[int] = None,
+                    redactor=None) -> dict:
+    """Pack the rows into ``tokens.bin`` (uint16, or uint32 for vocabularies over 65,536 ids) with ``meta.json``
+    describing the per-domain segments, and the tokenizer beside them, for memory-mapped training."""
     import numpy as np
 
     out_dir = Path(out_dir)
     out_dir.mkdir(parents=True, exist_ok=True)
-    dtype = np.uint16 if tokenizer.vocab_size <= 2 ** 16 else np.uint32
-    parts: dict[str, Path] = {}
-    handles: dict = {}
-    lengths: dict[str, int] = {}
+    dtype = np.dtype(np.uint16 if tokenizer.vocab_size <= 1 << 16 else np.uint32)
+    spools: dict[str, _Spool] = {}
     try:
-        for domain, text in read_rows(paths, limit, redactor):
-            if domain not in handles:
-                parts[domain] = out_dir / f".tokens.{len(parts)}.part"
-                handles[domain] = parts[domain].open("wb")
-                lengths[domain] = 0
-            ids = np.asarray(tokenizer.encode(text) + [tokenizer.eos_id], dtype=dtype)
-            ids.tofile(handles[domain])
-            lengths[domain] += int(ids.size)
+        for domain, ids in _documents(paths, tokenizer, limit, redactor):
+            if domain not in spools:
+                spools[domain] = _Spool(out_dir / f".spool-{len(spools)}.bin", dtype)
+            spools[domain].add(ids)
     finally:
-        for handle in handles.values():
-            handle.close()
-    segments = []
-    itemsize = np.dtype(dtype).itemsize
-    with (out_dir / "tokens.bin").open("wb") as target:
-        for domain, part in parts.items():
-            segments.append({"domain": domain, "start": target.tell() // itemsize, "length": lengths[domain]})
-            with part.open("rb") as source:
-                shutil.copyfileobj(source, target)
-            part.unlink()
+        for spool in spools.values():
+            spool.handle.close()
+    segments, position = [], 0
+    with (out_dir / "tokens.bin").open("wb") as packed:
+        for domain, spool in spools.items():
+            segments.append({"domain": domain, "start": position, "length": spool.length})
+            position += spool.length
+            packed.write(spool.path.read_bytes())
+            spool.path.unlink()
     tokenizer.save(out_dir / "tokenizer")
-    meta = {"format": 1, "dtype": np.dtype(dtype).name, "tokenizer": tokenizer.kind, "vocab_size": tokenizer.vocab_size,
-            "eos_id": tokenizer.eos_id, "segments": segments, "total_tokens": sum(lengths.values())}
+    meta = {"format": 1, "dtype": dtype.name, "tokenizer": tokenizer.kind, "vocab_size": tokenizer.vocab_size,
+            "eos_id": tokenizer.eos_id, "segments": segments, "total_tokens": position}
     (out_dir / "meta.json").write_text(json.dumps(meta, indent=2) + "\n")
     return meta
 
 
 def load_token_bin(directory: Path) -> tuple[TokenCorpus, object]:
+    """(corpus, tokenizer) of a packed directory; the tokens stay on disk, memory-mapped."""
     import numpy as np
 
     directory = Path(directory)
     meta = json.loads((directory / "meta.json").read_text())
     tokenizer = load_tokenizer(directory / "tokenizer")
-    if meta["total_tokens"] == 0:
-        return TokenCorpus(torch.empty(0, dtype=torch.int32), []), tokenizer
-    data = np.memmap(directory / "tokens.bin", dtype=np.dtype(meta["dtype"]), mode="r")
     segments = [Segment(s["domain"], s["start"], s["length"]) for s in meta["segments"]]
-    return TokenCorpus(data, segments), tokenizer
+    if not meta["total_tokens"]:
+        return TokenCorpus(torch.empty(0, dtype=torch.int32), []), tokenizer
+    return TokenCorpus(np.memmap(directory / "tokens.bin", dtype=np.dtype(meta["dtype"]), mode="r"), segments), tokenizer
 
 
 # ------------------------------------------------------------------------------------------ windows
 class WindowDataset(Dataset):
-    """Non-overlapping windows of ``sequence_length + 1`` tokens that never cross a domain boundary."""
+    """Consecutive, non-overlapping windows of ``sequence_length + 1`` tokens inside each domain's segment (a
+    partial window at the end of a segment is dropped), so no window mixes two domains."""
 
     def __init__(self, corpus: TokenCorpus, sequence_length: int) -> None:
-        self.corpus = corpus
-        self.window = sequence_length + 1
-        self.domains = corpus.domains
-        starts, owners = [], []
-        for seg in corpus.segments:
-            count = seg.length // self.window
-            starts.append(seg.start + torch.arange(count, dtype=torch.long) * self.window)
-            owners.append(torch.full((count,), self.domains.index(seg.domain), dtype=torch.long))
-        self.starts = torch.cat(starts) if starts else torch.empty(0, dtype=torch.long)
-        self.window_domains = torch.cat(owners) if owners else torch.empty(0, dtype=torch.long)
+        self.corpus, self.window, self.domains = corpus, sequence_length + 1, corpus.domains
+        counts = torch.tensor([seg.length // self.window for seg in corpus.segments], dtype=torch.long)
+        firsts = torch.tensor([seg.start for seg in corpus.segments], dtype=torch.long)
+        owners = torch.tensor([self.domains.index(seg.domain) for seg in corpus.segments], dtype=torch.long)
+        total = int(counts.sum())
+        segment_of = torch.repeat_interleave(torch.arange(len(corpus.segments)), counts)
+        before = torch.cumsum(counts, 0) - counts  # windows in earlier segments
+        rank_in_segment = torch.arange(total) - before[segment_of] if total else torch.zeros(0, dtype=torch.long)
+        self.starts = firsts[segment_of] + rank_in_segment * self.window if total else torch.zeros(0, dtype=torch.long)
+        self.window_domains = owners[segment_of] if total else torch.zeros(0, dtype=torch.long)
 
     def __len__(self) -> int:
         return int(self.starts.numel())
@@ -360,8 +368,8 @@ class WindowDataset(Dataset):
     def __getitem__(self, index: int) -> Tensor:
         if not 0 <= index < len(self):
             raise IndexError(index)
-        start = int(self.starts[index])
-        return self.corpus.read(start, start + self.window)
+        first = int(self.starts[index])
+        return self.corpus.read(first, first + self.window)
 
     def batch(self, indices: Sequence[int]) -> Tensor:
         return torch.stack([self[int(i)] for i in indices])
@@ -369,34 +377,28 @@ class WindowDataset(Dataset):
     def fingerprint(self) -> str:
         return hashlib.sha256(f"{len(self)}|{self.window}|{self.domains}".encode()).hexdigest()[:16]
 
-    @classmethod
-    def _view(cls, corpus, window, domains, starts, window_domains) -> "WindowDataset":
-        view = cls.__new__(cls)
-        view.corpus, view.window, view.domains = corpus, window, domains
-        view.starts, view.window_domains = starts, window_domains
-        return view
+    def _subset(self, keep: Tensor) -> "WindowDataset":
+        part = copy.copy(self)
+        part.starts, part.window_domains = self.starts[keep], self.window_domains[keep]
+        return part
 
     def split_train_val(self, val_fraction: float = 0.02, seed: int = 0, min_val_windows_per_domain: int = 1):
-        """Domain-stratified deterministic (train, val) split; the two views never overlap."""
+        """(train, val) views that never share a window. Each domain gives ``val_fraction`` of its windows (at least
+        ``min_val_windows_per_domain``) to validation, drawn by a generator seeded with ``seed``."""
         if not 0 < val_fraction < 1:
             raise ValueError("val_fraction must be in (0, 1)")
         gen = torch.Generator().manual_seed(seed)
-        train_parts, val_parts = [], []
-        for d in range(len(self.domains)):
-            where = (self.window_domains == d).nonzero(as_tuple=True)[0]
-            if where.numel() == 0:
+        held = torch.zeros(len(self), dtype=torch.bool)
+        for d, name in enumerate(self.domains):
+            members = torch.nonzero(self.window_domains == d).flatten()
+            if not members.numel():
                 continue
-            shuffled = where[torch.randperm(where.numel(), generator=gen)]
-            held = max(min_val_windows_per_domain, round(where.numel() * val_fraction))
-            if held >= where.numel():
-                raise ValueError(f"domain '{self.domains[d]}' has only {where.numel()} window(s), too few to both "
-                                 f"train on and hold out {held} for validation; lower val_fraction or add data")
-            val_parts.append(shuffled[:held])
-            train_parts.append(shuffled[held:])
-        tr = torch.cat(train_parts).sort().values
-        va = torch.cat(val_parts).sort().values
-        return (self._view(self.corpus, self.window, self.domains, self.starts[tr], self.window_domains[tr]),
-                self._view(self.corpus, self.window, self.domains, self.starts[va], self.window_domains[va]))
+            take = max(min_val_windows_per_domain, round(members.numel() * val_fraction))
+            if take >= members.numel():
+                raise ValueError(f"domain '{name}' has only {members.numel()} window(s), too few to both train on "
+                                 f"and hold out {take} for validation; lower val_fraction or add data")
+            held[members[torch.randperm(members.numel(), generator=gen)[:take]]] = True
+        return self._subset(~held), self._subset(held)
 
 
 class CharacterDataset(WindowDataset):
@@ -405,37 +407,43 @@ class CharacterDataset(WindowDataset):
 
 
 # ------------------------------------------------------------------------------------------ curriculum
+def _blocks(dataset: WindowDataset, size: int) -> Iterator[tuple[int, Tensor]]:
+    for first in range(0, len(dataset), size):
+        yield first, dataset.batch(range(first, min(len(dataset), first + size)))
+
+
 def difficulty_scores(dataset: WindowDataset, method: str, vocab_size: int, chunk: int = 4096) -> Tensor:
-    """Per-window difficulty (higher = harder): ``rarity`` mean -log unigram frequency, ``entropy`` histogram
-    entropy, ``uncommon`` share of tokens in the rarest 10% by corpus frequency."""
-    if method not in {"rarity", "entropy", "uncommon"}:
+    """One difficulty per window, higher is harder: ``rarity`` is the mean surprisal of its tokens under the corpus
+    unigram distribution, ``entropy`` the entropy of its own token histogram, ``uncommon`` the share of its tokens
+    that are among the rarest tenth of the token types seen."""
+    if method not in ("rarity", "entropy", "uncommon"):
         raise ValueError("curriculum method must be rarity, entropy or uncommon")
-    total = len(dataset)
-    counts = torch.zeros(vocab_size, dtype=torch.float64)
-    for lo in range(0, total, chunk):
-        rows = dataset.batch(range(lo, min(total, lo + chunk)))
-        counts += torch.bincount(rows.reshape(-1), minlength=vocab_size).double()
-    freq = counts / counts.sum().clamp(min=1)
-    neg_log = -(freq.clamp_min(1e-12)).log()
-    seen = counts[counts > 0]
-    cutoff = torch.quantile(seen, 0.1) if seen.numel() else torch.tensor(0.0, dtype=torch.float64)
-    scores = torch.empty(total, dtype=torch.float64)
-    for lo in range(0, total, chunk):
-        rows = dataset.batch(range(lo, min(total, lo + chunk)))
+    frequency = torch.zeros(vocab_size, dtype=torch.float64)
+    for _, rows in _blocks(dataset, chunk):
+        frequency.index_add_(0, rows.flatten(), torch.ones(rows.numel(), dtype=torch.float64))
+    surprisal = -torch.log((frequency / frequency.sum().clamp(min=1)).clamp(min=1e-12))
+    present = frequency[frequency > 0]
+    rare_limit = torch.quantile(present, 0.1) if present.numel() else torch.tensor(0.0, dtype=torch.float64)
+    out = torch.empty(len(dataset), dtype=torch.float64)
+    for first, rows in _blocks(dataset, chunk):
+        span = slice(first, first + rows.size(0))
         if method == "rarity":
-            scores[lo: lo + len(rows)] = neg_log[rows].mean(dim=1)
+            out[span] = surprisal[rows].mean(dim=1)
         elif method == "uncommon":
-            scores[lo: lo + len(rows)] = (counts[rows] <= cutoff).double().mean(dim=1)
+            out[span] = (frequency[rows] <= rare_limit).double().mean(dim=1)
         else:
-            for r, toks in enumerate(rows):
-                hist = torch.bincount(toks).double()
-                p = hist[hist > 0] / toks.numel()
-                scores[lo + r] = -(p * p.log()).sum()
-    return scores.float()
+            for offset, row in enumerate(rows):
+                _, counts = torch.unique(row, return_counts=True)
+                p = counts.double() / row.numel()
+                out[first + offset] = -(p * p.log()).sum()
+    return out.float()
 
 
 @dataclass
 class CurriculumConfig:
+    """Start from the easiest ``start_fraction`` of each domain's windows and widen linearly to all of them over
+    ``steps`` steps (``steps`` 0: no curriculum)."""
+
     method: str = "rarity"
     start_fraction: float = 0.25
     steps: int = 0
@@ -447,54 +455,74 @@ class CurriculumConfig:
     def fraction(self, step: int) -> float:
         if not self.enabled:
             return 1.0
-        return min(1.0, self.start_fraction + (1.0 - self.start_fraction) * step / self.steps)
+        progress = min(1.0, step / self.steps)
+        return self.start_fraction + (1.0 - self.start_fraction) * progress
 
     def stage(self, step: int, tiers: int = 4) -> int:
+        """Which quarter (by default) of the difficulty range the sampler has reached, 1..tiers."""
         return max(1, math.ceil(self.fraction(step) * tiers - 1e-9))
 
 
+_WEIGHT_ITEM = re.compile(r"\s*([^=,\s][^=,]*?)\s*=\s*([^,]+?)\s*$")
+
+
 def parse_domain_weights(spec: Optional[str]) -> Optional[dict[str, float]]:
+    """``"prose=3, code=1"`` -> ``{"prose": 3.0, "code": 1.0}``; None for an empty spec."""
     if not spec:
         return None
-    weights: dict[str, float] = {}
+    weights = {}
     for item in spec.split(","):
-        name, _, value = item.partition("=")
-        name = name.strip()
-        if not name or not value:
+        match = _WEIGHT_ITEM.match(item)
+        if match is None:
             raise ValueError(f"bad domain weight '{item}', expected name=weight")
-        weights[name] = float(value)
-        if weights[name] < 0:
-            raise ValueError("domain weights must be non-negative")
+        weights[match[1]] = float(match[2])
+    if any(w < 0 for w in weights.values()):
+        raise ValueError("domain weights must be non-negative")
     return weights
 
 
 class DomainMixture:
-    def __init__(self, domains: Sequence[str], start: dict[str, float], end: Optional[dict[str, float]] = None, steps: int = 0):
-        for weights in (start, end or {}):
-            unknown = set(weights) - set(domains)
-            if unknown:
-                raise ValueError(f"unknown domains {sorted(unknown)}; dataset has {list(domains)}")
-            missing = set(domains) - set(weights)
-            if weights and missing:
-                raise ValueError(f"domain weights must cover every domain; missing {sorted(missing)}")
+    """Sampling weights per domain, fixed or blended linearly from ``start`` to ``end`` over ``steps`` steps."""
+
+    def __init__(self, domains: Sequence[str], start: dict[str, float], end: Optional[dict[str, float]] = None,
+                 steps: int = 0):
         self.domains = list(domains)
-        self.start = torch.tensor([start[d] for d in domains], dtype=torch.double)
-        self.end = torch.tensor([end[d] for d in domains], dtype=torch.double) if end else None
+        self.start = self._vector(start)
+        self.end = self._vector(end) if end else None
         self.steps = steps
-        if self.start.sum() <= 0 or (self.end is not None and self.end.sum() <= 0):
+
+    def _vector(self, weights: dict[str, float]) -> Tensor:
+        unknown = sorted(set(weights) - set(self.domains))
+        if unknown:
+            raise ValueError(f"unknown domains {unknown}; dataset has {self.domains}")
+        missing = sorted(set(self.domains) - set(weights))
+        if missing:
+            raise ValueError(f"domain weights must cover every domain; missing {missing}")
+        vector = torch.tensor([weights[d] for d in self.domains], dtype=torch.double)
+        if vector.sum() <= 0:
             raise ValueError("domain weights must not all be zero")
+        return vector / vector.sum()
 
     def weights(self, step: int) -> Tensor:
         if self.end is None or self.steps <= 0:
-            return self.start / self.start.sum()
-        mix = min(1.0, step / self.steps)
-        blended = (1 - mix) * self.start / self.start.sum() + mix * self.end / self.end.sum()
-        return blended / blended.sum()
+            return self.start.clone()
+        t = min(1.0, step / self.steps)
+        blend = torch.lerp(self.start, self.end, t)
+        return blend / blend.sum()
 
 
 # ------------------------------------------------------------------------------------------ batch streams
+def _step_seed(seed: int, step: int) -> int:
+    """A generator seed for (run seed, step): the same pair always gives the same batch, on every rank."""
+    return (seed * 0x9E3779B1 + step * 0x85EBCA77 + 1) % (1 << 62)
+
+
 class BatchStream:
-    """Deterministic batches: ``batch(step)`` depends only on (seed, step, rank, world_size)."""
+    """``batch(step)`` draws one global batch from a generator seeded by (seed, step) alone and gives each rank its
+    own slice, so a resumed or differently launched run sees exactly the same windows at every step.
+
+    Each sample first picks a domain (by the mixture, else in proportion to the domain's windows), then one of the
+    domain's windows; with a curriculum only the easiest ``fraction(step)`` of that domain's windows can be picked."""
 
     def __init__(self, dataset: WindowDataset, batch_size: int, seed: int = 0, scores: Optional[Tensor] = None,
                  curriculum: Optional[CurriculumConfig] = None, mixture: Optional[DomainMixture] = None,
@@ -503,55 +531,47 @@ class BatchStream:
             raise ValueError("dataset holds fewer tokens than one training window")
         if curriculum is not None and curriculum.enabled and scores is None:
             raise ValueError("a curriculum needs difficulty scores")
-        self.dataset = dataset
-        self.batch_size = batch_size
-        self.seed = seed
+        self.dataset, self.batch_size, self.seed = dataset, batch_size, seed
         self.curriculum = curriculum or CurriculumConfig()
         self.mixture = mixture
         self.rank, self.world_size = rank, world_size
-        self.pools: list[Tensor] = []
+        self.pools = []  # per domain: its windows, easiest first when there are scores
         for d in range(len(dataset.domains)):
-            idx = (dataset.window_domains == d).nonzero(as_tuple=True)[0]
-            if scores is not None and idx.numel():
-                idx = idx[torch.argsort(scores[idx], stable=True)]
-            self.pools.append(idx)
+            members = torch.nonzero(dataset.window_domains == d).flatten()
+            if scores is not None and members.numel():
+                members = members[torch.argsort(scores[members], stable=True)]
+            self.pools.append(members)
         self.natural = torch.tensor([p.numel() for p in self.pools], dtype=torch.double)
+        self._flat = torch.cat(self.pools)
+        self._pool_start = torch.cumsum(self.natural.long(), 0) - self.natural.long()
 
     @property
     def num_domains(self) -> int:
         return len(self.dataset.domains)
 
     def domain_weights(self, step: int) -> Tensor:
-        weights = (self.mixture.weights(step) if self.mixture is not None else self.natural).clone()
-        weights[self.natural == 0] = 0
+        base = self.mixture.weights(step) if self.mixture is not None else self.natural
+        weights = torch.where(self.natural > 0, base, torch.zeros_like(base))
         if weights.sum() <= 0:
             raise ValueError("no sampleable domain has non-zero weight")
         return weights / weights.sum()
 
     def batch(self, step: int) -> tuple[Tensor, Tensor]:
-        total = self.batch_size * self.world_size
-        gen = torch.Generator().manual_seed(self.seed * 1_000_003 + step)
-        domains = torch.multinomial(self.domain_weights(step), total, replacement=True, generator=gen)
-        uniform = torch.rand(total, generator=gen, dtype=torch.double)
-        fraction = self.curriculum.fraction(step)
-        chosen = []
-        for d, u in zip(domains.tolist(), uniform.tolist()):
-            pool = self.pools[d]
-            reach = max(1, math.ceil(fraction * pool.numel()))
-            chosen.append(int(pool[min(int(u * reach), reach - 1)]))
+        count = self.batch_size * self.world_size
+        gen = torch.Generator().manual_seed(_step_seed(self.seed, step))
+        domains = torch.multinomial(self.domain_weights(step), count, replacement=True, generator=gen)
+        reach = torch.ceil(self.curriculum.fraction(step) * self.natural[domains]).long().clamp(min=1)
+        position = (torch.rand(count, generator=gen, dtype=torch.double) * reach).long().clamp(max=reach - 1)
+        windows = self._flat[self._pool_start[domains] + position]
         mine = slice(self.rank * self.batch_size, (self.rank + 1) * self.batch_size)
-        return self.dataset.batch(chosen[mine]), domains[mine]
+        return self.dataset.batch(windows[mine].tolist()), domains[mine]
 
     def state(self, step: int) -> dict:
-        return {
-            "seed": self.seed,
-            "step": step,
-            "samples_consumed": step * self.batch_size * self.world_size,
-            "fingerprint": self.dataset.fingerprint(),
-            "curriculum_fraction": self.curriculum.fraction(step),
-            "curriculum_stage": self.curriculum.stage(step) if self.curriculum.enabled else None,
-            "domain_weights": {d: float(w) for d, w in zip(self.dataset.domains, self.domain_weights(step))},
-        }
+        curriculum = self.curriculum
+        return {"seed": self.seed, "step": step, "samples_consumed": step * self.batch_size * self.world_size,
+                "fingerprint": self.dataset.fingerprint(), "curriculum_fraction": curriculum.fraction(step),
+                "curriculum_stage": curriculum.stage(step) if curriculum.enabled else None,
+                "domain_weights": dict(zip(self.dataset.domains, map(float, self.domain_weights(step))))}
 
 
 class SyntheticTokenStream:
@@ -586,7 +606,7 @@ class SyntheticTokenStream:
 
     def global_batch(self, step: int) -> Tensor:
         total = self.batch_size * self.world_size
-        gen = torch.Generator().manual_seed(self.seed * 1_000_003 + step)
+        gen = torch.Generator().manual_seed(_step_seed(self.seed, step))
         shape = (total, self.sequence_length + 1)
         if self.distribution == "uniform":
             return torch.randint(0, self.vocab_size, shape, generator=gen, dtype=torch.long)
