@@ -112,23 +112,26 @@ def init_expert_parallel(device_arg: str = "auto", tensor_parallel: int = 1,
 
 
 # ------------------------------------------------------------------------------------------ reference-style exchange
+def _exchange(x: Tensor, send: list, recv: list, group) -> Tensor:
+    """Uneven row exchange: ``send[r]`` leading rows of ``x`` go to rank ``r``; ``recv[r]`` rows arrive from it."""
+    x = x.contiguous()
+    out = x.new_empty((sum(recv), *x.shape[1:]))
+    dist.all_to_all_single(out, x, output_split_sizes=recv, input_split_sizes=send, group=group)
+    return out
+
+
 class _AllToAll(torch.autograd.Function):
-    """Uneven all_to_all_single whose backward is the reverse exchange (CPU / gloo oracle path)."""
+    """Differentiable :func:`_exchange` (CPU / gloo oracle path): the gradient takes the same route backwards, so the
+    backward is the exchange with the two split lists swapped."""
 
     @staticmethod
-    def forward(ctx, x: Tensor, in_splits: list, out_splits: list, group):
-        ctx.in_splits, ctx.out_splits, ctx.group = in_splits, out_splits, group
-        x = x.contiguous()
-        out = x.new_empty((sum(out_splits),) + tuple(x.shape[1:]))
-        dist.all_to_all_single(out, x, out_splits, in_splits, group=group)
-        return out
+    def forward(ctx, x: Tensor, send: list, recv: list, group):
+        ctx.route = (recv, send, group)
+        return _exchange(x, send, recv, group)
 
     @staticmethod
     def backward(ctx, grad: Tensor):
-        grad = grad.contiguous()
-        out = grad.new_empty((sum(ctx.in_splits),) + tuple(grad.shape[1:]))
-        dist.all_to_all_single(out, grad, ctx.in_splits, ctx.out_splits, group=ctx.group)
-        return out, None, None, None
+        return _exchange(grad, *ctx.route), None, None, None
 
 
 def _even_exchange(x: Tensor, group) -> Tensor:
@@ -353,52 +356,66 @@ class ExpertParallelMoE(TopKMoE):
 
     # ---- reference algorithm (CPU / gloo, and the profiling/straggler paths) ----
     def _execute(self, flat_hidden: Tensor, tokens: Tensor, weights: Tensor, kept_counts: Tensor) -> Tensor:
+        """Route the kept rows to the ranks that own their experts, run the local experts, route the results back.
+
+        ``kept_counts`` is this rank's ``[world * local]`` per-expert row count in destination-major order, and
+        ``tokens`` lists the source row of every kept slot in the same order. The exchanged counts tell every
+        received row its local expert (the buffer arrives grouped by source rank, then by expert), so one stable
+        sort by expert id gives each expert one contiguous slice.
+        """
         ctx, group = self.context, self.context.group
         world, local = ctx.world_size, self.num_local_experts
-        counts = kept_counts.tolist()
-        send_splits = [sum(counts[r * local:(r + 1) * local]) for r in range(world)]
         recv_counts = torch.empty_like(kept_counts)
         dist.all_to_all_single(recv_counts, kept_counts.contiguous(), group=group)
-        per_source = recv_counts.reshape(world, local).tolist()
-        recv_splits = [sum(row) for row in per_source]
-        received = self._tp_in(_AllToAll.apply(flat_hidden[tokens], send_splits, recv_splits, group))
-        offset, positions = 0, [[] for _ in range(local)]
-        for source in range(world):
-            for e in range(local):
-                n = per_source[source][e]
-                positions[e].append(torch.arange(offset, offset + n, device=received.device))
-                offset += n
-        started = self._start_clock(received) if self.measure_load else None
-        processed = received.new_zeros(received.shape)
-        for e in range(local):
-            rows = torch.cat(positions[e])
-            if rows.numel():
-                processed = processed.index_copy(0, rows, self.expert_forward(e, received[rows]).to(received.dtype))
-        if started is not None:
-            self.load_rows += received.size(0)
-            self.load_seconds += self._stop_clock(received, started) + received.size(0) * self.simulated_cost_per_row
-        returned = _AllToAll.apply(self._tp_out(processed), recv_splits, send_splits, group)
-        output = torch.zeros_like(flat_hidden)
-        output.index_add_(0, tokens, (returned * weights[:, None]).to(output.dtype))
-        return output
+        send = kept_counts.view(world, local).sum(dim=1).tolist()
+        recv = recv_counts.view(world, local).sum(dim=1).tolist()
+        received = self._tp_in(_AllToAll.apply(flat_hidden[tokens], send, recv, group))
+        expert_of_row = torch.arange(local, device=received.device).repeat(world).repeat_interleave(
+            recv_counts.to(received.device))
+        order = torch.argsort(expert_of_row, stable=True)
+        bounds = [0] + torch.bincount(expert_of_row, minlength=local).cumsum(0).tolist()
+        with _LoadClock(self, received):
+            grouped = received[order]
+            pieces = [self.expert_forward(e, grouped[bounds[e]:bounds[e + 1]]).to(received.dtype)
+                      for e in range(local) if bounds[e + 1] > bounds[e]]
+            processed = torch.empty_like(received)
+            if pieces:
+                processed = processed.index_copy(0, order, torch.cat(pieces))
+        returned = _AllToAll.apply(self._tp_out(processed), recv, send, group)
+        return torch.zeros_like(flat_hidden).index_add_(0, tokens, (returned * weights[:, None]).to(flat_hidden.dtype))
 
     def _run_expert(self, index: int, inputs: Tensor) -> Tensor:
         return self.expert_forward(index, inputs)
 
-    @staticmethod
-    def _start_clock(reference: Tensor) -> float:
-        if reference.is_cuda:
-            torch.cuda.synchronize()
-        return time.perf_counter()
-
-    @staticmethod
-    def _stop_clock(reference: Tensor, started: float) -> float:
-        if reference.is_cuda:
-            torch.cuda.synchronize()
-        return time.perf_counter() - started
 
 
-# ------------------------------------------------------------------------------------------ parameter classes
+class _LoadClock:
+    """Charges the expert work inside the ``with`` block to ``moe.load_seconds`` / ``moe.load_rows`` when the layer
+    is measured. The device is synchronised on both sides so the wall clock covers the kernels, and the layer's
+    ``simulated_cost_per_row`` (a test hook that makes a rank look slow) is added per row."""
+
+    def __init__(self, moe, rows: Tensor) -> None:
+        self.moe, self.rows, self.started = moe, rows, None
+
+    def _sync(self) -> None:
+        if self.rows.is_cuda:
+            torch.cuda.synchronize(self.rows.device)
+
+    def __enter__(self):
+        if self.moe.measure_load:
+            self._sync()
+            self.started = time.perf_counter()
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self.started is None or exc[0] is not None:
+            return
+        self._sync()
+        n = self.rows.size(0)
+        self.moe.load_rows += n
+        self.moe.load_seconds += time.perf_counter() - self.started + n * self.moe.simulated_cost_per_row
+
+
 def is_expert_parameter(name: str) -> bool:
     return name.endswith(("moe.w_gate_up", "moe.w_down")) or ".moe.experts." in name
 
@@ -557,18 +574,19 @@ def finish(ctx) -> None:
 class DeviceLoadTracker:
     """Per-rank expert time/rows controller (reference ``DeviceLoadTracker``, ``src/expert_parallel.py:280-384``).
 
-    Every ``interval`` steps the accumulated per-layer expert seconds and rows are gathered; the routing bias is an
-    integral controller ``bias_r -= rate * strength * log(t_r / mean)``, clamped to ``max_bias`` and re-centred, added to
-    the router logits for selection only. ``adapt_capacity`` additionally sets each rank's ``capacity_scale`` to
-    ``clamp(mean / t_r)``. Measuring per-expert time synchronises the device, so tracked layers take the reference
-    (per-expert) path.
+    Every ``interval`` steps the per-layer expert seconds and rows each rank accumulated are collected into one
+    ``[layers, ranks]`` table (one all-reduce of a rank-slotted slab, after a mean over the tensor-parallel group).
+    The routing bias is an integral controller ``bias_r -= rate * strength * log(t_r / mean)``, clamped to
+    ``max_bias`` and re-centred, added to the router logits for selection only. ``adapt_capacity`` additionally sets
+    each rank's ``capacity_scale`` to ``clamp(mean / t_r)``. Measuring per-expert time synchronises the device, so
+    tracked layers take the reference (per-expert) path.
     """
 
     def __init__(self, model, ctx: ExpertParallelContext, strength: float = 0.5, max_bias: float = 2.0,
                  rate: float = 0.5, interval: int = 10, adapt_capacity: bool = False,
                  capacity_scale_min: float = 0.5, capacity_scale_max: float = 2.0) -> None:
-        self.model, self.ctx = model, ctx
-        self.strength, self.max_bias, self.rate, self.interval = strength, max_bias, rate, interval
+        self.model, self.ctx, self.interval = model, ctx, interval
+        self.strength, self.rate, self.max_bias = strength, rate, max_bias
         self.adapt_capacity = adapt_capacity
         self.capacity_scale_min, self.capacity_scale_max = capacity_scale_min, capacity_scale_max
         self.layers = len(model.moes())
@@ -577,64 +595,84 @@ class DeviceLoadTracker:
         for moe in model.moes():
             moe.measure_load = True
 
-    def _gather(self):
-        local = torch.tensor([[moe.load_seconds, float(moe.load_rows)] for moe in self.model.moes()],
-                             dtype=torch.float64, device=self.ctx.device)
-        for moe in self.model.moes():
-            moe.load_seconds, moe.load_rows = 0.0, 0
+    # ---- collection ----
+    def _table(self, local: Tensor) -> Tensor:
+        """``local[layer, ...]`` of every rank as ``[layer, rank, ...]`` on the host: each rank writes its own slot
+        of a zero slab and one sum-all-reduce over the expert-parallel group fills in the others."""
+        local = local.to(self.ctx.device, torch.float64)
         if self.ctx.tp_size > 1:
             dist.all_reduce(local, group=self.ctx.tp_group)
-            local /= self.ctx.tp_size
-        gathered = [torch.zeros_like(local) for _ in range(self.ctx.world_size)]
-        dist.all_gather(gathered, local, group=self.ctx.group)
-        stacked = torch.stack(gathered, dim=1).cpu()
-        return stacked[..., 0], stacked[..., 1]
+            local = local / self.ctx.tp_size
+        slab = local.new_zeros((self.ctx.world_size, *local.shape))
+        slab[self.ctx.rank] = local
+        dist.all_reduce(slab, group=self.ctx.group)
+        return slab.transpose(0, 1).cpu()
+
+    def _drain(self) -> Tensor:
+        moes = self.model.moes()
+        local = torch.tensor([[moe.load_seconds, moe.load_rows] for moe in moes], dtype=torch.float64)
+        for moe in moes:
+            moe.load_seconds, moe.load_rows = 0.0, 0
+        return self._table(local)
+
+    # ---- control ----
+    @staticmethod
+    def _imbalance(per_rank: Tensor) -> float:
+        return float(per_rank.max() / per_rank.mean().clamp(min=1e-9))
+
+    def _next_bias(self, seconds: Tensor) -> Tensor:
+        """One integral step on the log of each rank's time relative to its layer's mean; only the differences
+        between ranks matter, so the result is re-centred per layer."""
+        log_ratio = (seconds / seconds.mean(dim=1, keepdim=True).clamp(min=1e-12)).clamp(min=0.05).log()
+        bias = (self.rank_bias - self.rate * self.strength * log_ratio).clamp(-self.max_bias, self.max_bias)
+        return bias - bias.mean(dim=1, keepdim=True)
+
+    def _capacity_scale(self, seconds: Tensor) -> Tensor:
+        mean = seconds.mean(dim=1, keepdim=True).clamp(min=1e-12)
+        return (mean / seconds.clamp(min=1e-12)).clamp(self.capacity_scale_min, self.capacity_scale_max)
 
     def update(self, step: int) -> Optional[dict]:
         if step % self.interval:
             return None
-        seconds, rows = self._gather()
-        per_rank_seconds, per_rank_rows = seconds.sum(dim=0), rows.sum(dim=0)
-        metrics = {"step": step, "device_rows": per_rank_rows.tolist(), "device_seconds": per_rank_seconds.tolist(),
-                   "rows_imbalance": float(per_rank_rows.max() / per_rank_rows.mean().clamp(min=1e-9)),
-                   "time_imbalance": float(per_rank_seconds.max() / per_rank_seconds.mean().clamp(min=1e-9))}
-        if self.strength > 0 and float(seconds.sum()) > 0:
-            relative = seconds / seconds.mean(dim=1, keepdim=True).clamp(min=1e-12)
-            correction = -self.strength * torch.log(relative.clamp(min=0.05))
-            bias = (self.rank_bias + self.rate * correction).clamp(-self.max_bias, self.max_bias)
-            self.rank_bias = bias - bias.mean(dim=1, keepdim=True)
+        table = self._drain()
+        seconds, rows = table[..., 0], table[..., 1]
+        metrics = {"step": step, "device_rows": rows.sum(dim=0).tolist(),
+                   "device_seconds": seconds.sum(dim=0).tolist(),
+                   "rows_imbalance": self._imbalance(rows.sum(dim=0)),
+                   "time_imbalance": self._imbalance(seconds.sum(dim=0))}
+        measured = float(seconds.sum()) > 0
+        if measured and self.strength > 0:
+            self.rank_bias = self._next_bias(seconds)
             self._apply()
         metrics["rank_bias"] = self.rank_bias.mean(dim=0).tolist()
-        if self.adapt_capacity and float(seconds.sum()) > 0:
-            mean_time = seconds.mean(dim=1, keepdim=True).clamp(min=1e-12)
-            scale = (mean_time / seconds.clamp(min=1e-12)).clamp(self.capacity_scale_min, self.capacity_scale_max)
-            for layer, moe in enumerate(self.model.moes()):
-                moe.capacity_scale = float(scale[layer, self.ctx.rank])
+        if measured and self.adapt_capacity:
+            scale = self._capacity_scale(seconds)
+            for moe, value in zip(self.model.moes(), scale[:, self.ctx.rank].tolist()):
+                moe.capacity_scale = value
             metrics["capacity_scale"] = scale.mean(dim=0).tolist()
         self.history.append(metrics)
         return metrics
 
     def _apply(self) -> None:
-        per_rank = self.model.moes()[0].num_local_experts
-        for layer, moe in enumerate(self.model.moes()):
-            moe.expert_bias = self.rank_bias[layer].repeat_interleave(per_rank).to(torch.float32).to(self.ctx.device)
+        """Expand the per-rank bias to every expert a rank holds (experts are laid out rank-major)."""
+        moes = self.model.moes()
+        per_expert = self.rank_bias.repeat_interleave(moes[0].num_local_experts, dim=1)
+        per_expert = per_expert.to(device=self.ctx.device, dtype=torch.float32)
+        for moe, row in zip(moes, per_expert):
+            moe.expert_bias = row
 
     def gather_expert_utilization(self) -> Tensor:
-        local = torch.stack([moe.last_stats["expert_load"].to(torch.float64) for moe in self.model.moes()])
-        local = local.to(self.ctx.device)
-        if self.ctx.tp_size > 1:
-            dist.all_reduce(local, group=self.ctx.tp_group)
-            local /= self.ctx.tp_size
-        gathered = [torch.zeros_like(local) for _ in range(self.ctx.world_size)]
-        dist.all_gather(gathered, local, group=self.ctx.group)
-        return torch.stack(gathered).cpu()
+        """``[rank, layer, expert]`` routed-row shares of the last step, as each rank saw them."""
+        local = torch.stack([moe.last_stats["expert_load"].double().cpu() for moe in self.model.moes()])
+        return self._table(local).transpose(0, 1).contiguous()
 
+    # ---- checkpoint ----
     def state_dict(self) -> dict:
         return {"rank_bias": self.rank_bias.tolist()}
 
     def load_state_dict(self, state: dict) -> None:
         self.rank_bias = torch.tensor(state["rank_bias"], dtype=torch.float64)
-        if bool(self.rank_bias.abs().sum() > 0):
+        if bool(self.rank_bias.ne(0).any()):
             self._apply()
 
 
