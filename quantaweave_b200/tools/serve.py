@@ -24,12 +24,15 @@ a keyword guardrail, not a safety system).
 
 import argparse
 import asyncio
+import bisect
+import contextlib
+import hmac
 import json
 import logging
 import re
 import time
 import uuid
-from collections import defaultdict, deque
+from collections import Counter, defaultdict
 from pathlib import Path
 from typing import Optional
 
@@ -88,23 +91,28 @@ def configure_logging(log_format: str) -> None:
 
 
 class RateLimiter:
-    """At most ``limit`` calls per ``window`` seconds per key (sliding window, in memory); ``None`` disables it."""
+    """At most ``limit`` calls per ``window`` seconds per key (sliding window, in memory); ``None`` disables it.
+
+    Each key keeps the sorted monotonic times of its admitted calls; expired times are cut with one bisection, and a
+    key whose window has emptied is forgotten, so memory stays bounded by the callers active in the last window.
+    """
 
     def __init__(self, limit: Optional[int], window: float = 60.0) -> None:
         self.limit, self.window = limit, window
-        self.hits: dict[str, deque] = defaultdict(deque)
+        self.hits: dict[str, list[float]] = {}
 
     def allow(self, key: str) -> bool:
         if self.limit is None:
             return True
         now = time.monotonic()
-        recent = self.hits[key]
-        while recent and now - recent[0] > self.window:
-            recent.popleft()
-        if len(recent) >= self.limit:
-            return False
-        recent.append(now)
-        return True
+        times = self.hits.pop(key, [])
+        del times[:bisect.bisect_left(times, now - self.window)]
+        admitted = len(times) < self.limit
+        if admitted:
+            times.append(now)
+        if times:
+            self.hits[key] = times
+        return admitted
 
 
 class Moderation:
@@ -122,19 +130,45 @@ class Moderation:
         return next((p.pattern for p in self.patterns if p.search(text)), None)
 
 
+def _sample(name: str, value, **labels) -> str:
+    """One exposition line: ``quantweave_<name>{k="v",...} value`` (floats with 6 decimals)."""
+    label_text = "{" + ",".join(f'{k}="{v}"' for k, v in labels.items()) + "}" if labels else ""
+    return f"quantweave_{name}{label_text} {value:.6f}" if isinstance(value, float) else \
+        f"quantweave_{name}{label_text} {value}"
+
+
 class Metrics:
-    """Prometheus text exposition: requests by route/status, errors, request seconds, tokens, in-flight gauge."""
+    """Prometheus text exposition: requests by route/status, errors, request seconds, tokens, in-flight gauge.
+
+    ``_FAMILIES`` lists each metric family once (name, type, help, and how its samples are read off this object);
+    :meth:`render` writes the ``# HELP`` / ``# TYPE`` header and the samples of every family in that order.
+    """
+
+    _FAMILIES = (
+        ("requests_total", "counter", "Total requests by route and status.",
+         lambda m: [_sample("requests_total", n, route=r, status=c) for (r, c), n in sorted(m.requests_total.items())]),
+        ("errors_total", "counter", "Total error responses (status >= 400) by route.",
+         lambda m: [_sample("errors_total", n, route=r) for r, n in sorted(m.errors_total.items())]),
+        ("request_seconds_sum", "counter", "Total request handling seconds by route.",
+         lambda m: [line for r in sorted(m.seconds_sum)
+                    for line in (_sample("request_seconds_sum", m.seconds_sum[r], route=r),
+                                 _sample("request_seconds_count", m.seconds_count[r], route=r))]),
+        ("tokens_generated_total", "counter", "Total tokens generated across all requests.",
+         lambda m: [_sample("tokens_generated_total", m.tokens_generated_total)]),
+        ("requests_in_flight", "gauge", "Requests currently being handled.",
+         lambda m: [_sample("requests_in_flight", m.requests_in_flight)]),
+    )
 
     def __init__(self) -> None:
-        self.requests_total: dict[tuple[str, int], int] = defaultdict(int)
-        self.errors_total: dict[str, int] = defaultdict(int)
+        self.requests_total: Counter = Counter()
+        self.errors_total: Counter = Counter()
         self.seconds_sum: dict[str, float] = defaultdict(float)
-        self.seconds_count: dict[str, int] = defaultdict(int)
+        self.seconds_count: Counter = Counter()
         self.tokens_generated_total = 0
         self.requests_in_flight = 0
 
     def observe(self, route: str, status: int, seconds: float, tokens: int = 0) -> None:
-        self.requests_total[(route, status)] += 1
+        self.requests_total[route, status] += 1
         if status >= 400:
             self.errors_total[route] += 1
         self.seconds_sum[route] += seconds
@@ -142,25 +176,10 @@ class Metrics:
         self.tokens_generated_total += tokens
 
     def render(self) -> str:
-        out = ["# HELP quantweave_requests_total Total requests by route and status.",
-               "# TYPE quantweave_requests_total counter"]
-        out += [f'quantweave_requests_total{{route="{r}",status="{s}"}} {n}'
-                for (r, s), n in sorted(self.requests_total.items())]
-        out += ["# HELP quantweave_errors_total Total error responses (status >= 400) by route.",
-                "# TYPE quantweave_errors_total counter"]
-        out += [f'quantweave_errors_total{{route="{r}"}} {n}' for r, n in sorted(self.errors_total.items())]
-        out += ["# HELP quantweave_request_seconds_sum Total request handling seconds by route.",
-                "# TYPE quantweave_request_seconds_sum counter"]
-        for r in sorted(self.seconds_sum):
-            out.append(f'quantweave_request_seconds_sum{{route="{r}"}} {self.seconds_sum[r]:.6f}')
-            out.append(f'quantweave_request_seconds_count{{route="{r}"}} {self.seconds_count[r]}')
-        out += ["# HELP quantweave_tokens_generated_total Total tokens generated across all requests.",
-                "# TYPE quantweave_tokens_generated_total counter",
-                f"quantweave_tokens_generated_total {self.tokens_generated_total}",
-                "# HELP quantweave_requests_in_flight Requests currently being handled.",
-                "# TYPE quantweave_requests_in_flight gauge",
-                f"quantweave_requests_in_flight {self.requests_in_flight}"]
-        return "\n".join(out) + "\n"
+        lines = []
+        for name, kind, text, samples in self._FAMILIES:
+            lines += [f"# HELP quantweave_{name} {text}", f"# TYPE quantweave_{name} {kind}", *samples(self)]
+        return "\n".join(lines) + "\n"
 
 
 def reply_payload(reply) -> dict:
@@ -376,59 +395,59 @@ class Server:
         self.metrics.tokens_generated_total += reply.tokens
         return reply_payload(reply)
 
+    async def _relay(self, produce, cancel=None):
+        """Server-sent events from a blocking producer: ``produce(on_text)`` runs in a worker thread and returns the
+        reply payload; every piece it hands to ``on_text`` is sent as ``data: {"text": ...}`` as soon as it exists,
+        and the payload follows as ``event: done``. A sentinel queued when the producer returns (or raises) ends the
+        stream. If the client goes away first, ``cancel`` is called and the task is abandoned."""
+        loop = asyncio.get_running_loop()
+        pieces: asyncio.Queue = asyncio.Queue()
+        finished = object()
+
+        def work():
+            try:
+                return produce(lambda piece: loop.call_soon_threadsafe(pieces.put_nowait, piece))
+            finally:
+                loop.call_soon_threadsafe(pieces.put_nowait, finished)
+
+        task = asyncio.ensure_future(asyncio.to_thread(work))
+        try:
+            while (piece := await pieces.get()) is not finished:
+                yield f"data: {json.dumps({'text': piece})}\n\n"
+            payload = await task
+        finally:
+            if not task.done():
+                if cancel is not None:
+                    cancel()
+                task.cancel()
+        self.requests_served += 1
+        self.metrics.tokens_generated_total += payload["tokens"]
+        yield f"event: done\ndata: {json.dumps(payload)}\n\n"
+
     async def stream_generate(self, request: GenerateRequest):
-        """Server-sent events: ``data: {"text": ...}`` per piece, then ``event: done`` with the full reply."""
+        """Server-sent events: ``data: {"text": ...}`` per piece, then ``event: done`` with the full reply. With the
+        batching worker the request joins the shared decode; otherwise it holds the session lock while it streams."""
         self._check(request.prompt, "prompt")
         if self.worker is not None:
             self._admit_batched()
-            queue: asyncio.Queue = asyncio.Queue()
-            loop = asyncio.get_running_loop()
             handle: list = []
-            task = asyncio.ensure_future(asyncio.to_thread(
-                self._batched, request, lambda piece: loop.call_soon_threadsafe(queue.put_nowait, piece), handle))
-            try:
-                while not (task.done() and queue.empty()):
-                    try:
-                        item = await asyncio.wait_for(queue.get(), timeout=0.05)
-                    except asyncio.TimeoutError:
-                        continue
-                    yield f"data: {json.dumps({'text': item})}\n\n"
-                payload = await task
-            finally:
-                if not task.done():  # the client went away mid-stream: retire its job at the next decode step
-                    for job in handle:
-                        job.cancelled = True
-                    task.cancel()
-            self.requests_served += 1
-            self.metrics.tokens_generated_total += payload["tokens"]
-            yield f"event: done\ndata: {json.dumps(payload)}\n\n"
+
+            def retire() -> None:  # the client went away mid-stream: retire its job at the next decode step
+                for job in handle:
+                    job.cancelled = True
+
+            events = self._relay(lambda on_text: self._batched(request, on_text, handle), retire)
+            async with contextlib.aclosing(events):
+                async for event in events:
+                    yield event
             return
         await self._acquire()
         try:
             self.complete_session.settings = self._complete_settings(request)
-            queue: asyncio.Queue = asyncio.Queue()
-            loop = asyncio.get_running_loop()
-            done = object()
-
-            def on_text(piece: str) -> None:
-                loop.call_soon_threadsafe(queue.put_nowait, piece)
-
-            async def run():
-                reply = await asyncio.to_thread(self.complete_session.send, request.prompt, on_text)
-                loop.call_soon_threadsafe(queue.put_nowait, done)
-                return reply
-
-            task = asyncio.ensure_future(run())
-            try:
-                while (item := await queue.get()) is not done:
-                    yield f"data: {json.dumps({'text': item})}\n\n"
-                reply = await task
-                self.requests_served += 1
-                self.metrics.tokens_generated_total += reply.tokens
-                yield f"event: done\ndata: {json.dumps(reply_payload(reply))}\n\n"
-            finally:
-                if not task.done():
-                    task.cancel()
+            events = self._relay(lambda on_text: reply_payload(self.complete_session.send(request.prompt, on_text)))
+            async with contextlib.aclosing(events):
+                async for event in events:
+                    yield event
         finally:
             self.lock.release()
 
@@ -440,11 +459,12 @@ def build_app(server: Server):
     app = FastAPI(title="QuantaWeave-B200 inference server")
 
     def require_auth(request: Request) -> None:
+        """Bearer token or ``X-API-Key``; compared in constant time so the key cannot be probed by timing."""
         if server.api_key is None:
             return
-        header = request.headers.get("authorization", "")
-        key = header[7:] if header.lower().startswith("bearer ") else request.headers.get("x-api-key", "")
-        if key != server.api_key:
+        scheme, _, token = request.headers.get("authorization", "").partition(" ")
+        presented = token.strip() if scheme.lower() == "bearer" else request.headers.get("x-api-key", "")
+        if not hmac.compare_digest(presented.encode(), server.api_key.encode()):
             raise HTTPException(401, "invalid or missing API key (Authorization: Bearer <key> or X-API-Key: <key>)")
 
     def require_rate_limit(request: Request) -> None:

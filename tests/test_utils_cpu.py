@@ -124,3 +124,18 @@ def test_rate_limiter_window_per_key_and_disabled():
     assert limiter.allow("a")  # the window slid
     assert all(RateLimiter(None).allow("x") for _ in range(100))
     assert Moderation(None).blocked("anything at all") is None
+
+
+def test_rate_limiter_forgets_callers_whose_window_emptied():
+    from quantaweave_b200.tools.serve import RateLimiter
+
+    limiter = RateLimiter(1, window=0.02)
+    assert all(limiter.allow(f"client-{i}") for i in range(50))
+    assert len(limiter.hits) == 50 and not limiter.allow("client-0")
+    time.sleep(0.03)
+    assert limiter.allow("client-0")  # its old call expired, so it is admitted again
+    assert len(limiter.hits["client-0"]) == 1
+    assert all(limiter.allow(f"client-{i}") for i in range(1, 50))
+    limiter.limit = 0  # refuse everything: a caller with no admitted call in the window leaves no entry behind
+    time.sleep(0.03)
+    assert not limiter.allow("client-7") and "client-7" not in limiter.hits
