@@ -275,52 +275,69 @@ def routing_and_compute(model, batches, device, precision, config) -> tuple[dict
     return routing, compute
 
 
+def _megabytes(count) -> str:
+    return "n/a" if count is None else f"{count / 1e6:,.1f} MB"
+
+
+# (section title, [(row label, cell text from the report)]): the two-column summary tables of the report.
+_SUMMARY = (
+    ("Quality", (
+        ("loss", lambda r: f"{r['loss']:.4f}"),
+        ("perplexity", lambda r: f"{r['perplexity']:.2f}"),
+        ("tokens evaluated", lambda r: f"{r['tokens']:,}"))),
+    ("Speed and memory", (
+        ("tokens / second", lambda r: f"{r['tokens_per_second']:,.0f}"),
+        ("seconds / batch", lambda r: f"{r['seconds_per_batch']:.4f}"),
+        ("parameter memory", lambda r: _megabytes(r["memory"]["parameter_bytes"])),
+        ("memory per expert (all layers)", lambda r: _megabytes(r["memory"]["bytes_per_expert"])),
+        ("peak device memory", lambda r: _megabytes(r["memory"]["peak_device_bytes"])),
+        ("process RSS", lambda r: _megabytes(r["memory"]["process_rss_bytes"])))),
+    ("Parameters", (
+        ("total", lambda r: f"{r['total_parameters']:,}"),
+        ("active per token", lambda r: f"{r['active_parameters_per_token_estimate']:,}"),
+        ("active / total", lambda r: f"{r['active_parameter_ratio']:.1%}"),
+        ("experts (total / active)", lambda r: f"{r['num_experts']} / {r['active_experts_per_token']}"))),
+    ("Routing", (
+        ("aux (balance) loss", lambda r: f"{r['router_aux_loss']:.4f}"),
+        ("overflow routes", lambda r: f"{r['overflow_routes']:,} ({r['overflow_route_fraction']:.2%})"),
+        ("dropped routes", lambda r: f"{r['dropped_routes']:,} ({r['dropped_route_fraction']:.2%})"),
+        ("capacity factor", lambda r: f"{r['capacity_factor']}"),
+        ("expert utilization min / mean / max", lambda r: " / ".join(
+            f"{r[f'expert_utilization_{k}']:.4f}" for k in ("min", "mean", "max"))))),
+)
+
+_PER_LAYER = ("layer", "entropy (norm.)", "confidence", "load CV", "dead", "underused", "drop rate")
+
+
+def _table(header, rows) -> list[str]:
+    """A Markdown table followed by a blank line."""
+    return ["| " + " | ".join(header) + " |", "|" + "---|" * len(header),
+            *("| " + " | ".join(str(cell) for cell in row) + " |" for row in rows), ""]
+
+
+def _layer_cells(index: int, layer: dict) -> tuple:
+    return (index, f"{layer['entropy']:.3f} ({layer['entropy_normalized']:.0%})", f"{layer['confidence_mean']:.3f}",
+            f"{layer['load_cv']:.3f}", layer["dead_experts"], layer["underused_experts"], f"{layer['drop_rate']:.2%}")
+
+
 def render_markdown(report: dict) -> str:
-    mb = lambda b: "n/a" if b is None else f"{b / 1e6:,.1f} MB"  # noqa: E731
-    mem = report["memory"]
-    out = [
-        f"# Benchmark: {report['checkpoint']}", "",
-        f"- device: {report['device_name']} ({report['device']}), precision {report['precision']}, "
-        f"tokenizer {report['tokenizer']}",
-        f"- checkpoint step: {report['training_step_in_checkpoint']}", "",
-        "## Quality", "", "| metric | value |", "|---|---|",
-        f"| loss | {report['loss']:.4f} |", f"| perplexity | {report['perplexity']:.2f} |",
-        f"| tokens evaluated | {report['tokens']:,} |", "",
-        "## Speed and memory", "", "| metric | value |", "|---|---|",
-        f"| tokens / second | {report['tokens_per_second']:,.0f} |",
-        f"| seconds / batch | {report['seconds_per_batch']:.4f} |",
-        f"| parameter memory | {mb(mem['parameter_bytes'])} |",
-        f"| memory per expert (all layers) | {mb(mem['bytes_per_expert'])} |",
-        f"| peak device memory | {mb(mem['peak_device_bytes'])} |",
-        f"| process RSS | {mb(mem['process_rss_bytes'])} |", "",
-        "## Parameters", "", "| metric | value |", "|---|---|",
-        f"| total | {report['total_parameters']:,} |",
-        f"| active per token | {report['active_parameters_per_token_estimate']:,} |",
-        f"| active / total | {report['active_parameter_ratio']:.1%} |",
-        f"| experts (total / active) | {report['num_experts']} / {report['active_experts_per_token']} |", "",
-        "## Routing", "", "| metric | value |", "|---|---|",
-        f"| aux (balance) loss | {report['router_aux_loss']:.4f} |",
-        f"| overflow routes | {report['overflow_routes']:,} ({report['overflow_route_fraction']:.2%}) |",
-        f"| dropped routes | {report['dropped_routes']:,} ({report['dropped_route_fraction']:.2%}) |",
-        f"| capacity factor | {report['capacity_factor']} |",
-        f"| expert utilization min / mean / max | {report['expert_utilization_min']:.4f} / "
-        f"{report['expert_utilization_mean']:.4f} / {report['expert_utilization_max']:.4f} |", "",
-    ]
+    """The benchmark report as Markdown: header bullets, the summary tables of ``_SUMMARY``, then the per-layer
+    routing table and the expert-compute line when the routing pass ran, then the training-stability table when a
+    metrics file was given."""
+    out = [f"# Benchmark: {report['checkpoint']}", "",
+           f"- device: {report['device_name']} ({report['device']}), precision {report['precision']}, "
+           f"tokenizer {report['tokenizer']}",
+           f"- checkpoint step: {report['training_step_in_checkpoint']}", ""]
+    for title, rows in _SUMMARY:
+        out += [f"## {title}", "", *_table(("metric", "value"), ((label, cell(report)) for label, cell in rows))]
     if "routing" in report:
-        out += ["### Per layer", "",
-                "| layer | entropy (norm.) | confidence | load CV | dead | underused | drop rate |",
-                "|---|---|---|---|---|---|---|"]
-        for i, layer in enumerate(report["routing"]["per_layer"]):
-            out.append(f"| {i} | {layer['entropy']:.3f} ({layer['entropy_normalized']:.0%}) | "
-                       f"{layer['confidence_mean']:.3f} | {layer['load_cv']:.3f} | {layer['dead_experts']} | "
-                       f"{layer['underused_experts']} | {layer['drop_rate']:.2%} |")
-        c = report["expert_compute"]
-        out += ["", f"MoE layers spent {c['moe_seconds_total']:.3f}s across experts "
-                    f"({(c['moe_share_of_forward'] or 0):.0%} of the profiled pass).", ""]
+        out += ["### Per layer", "", *_table(_PER_LAYER, (_layer_cells(i, layer) for i, layer in
+                                                          enumerate(report["routing"]["per_layer"])))]
+        compute = report["expert_compute"]
+        out += [f"MoE layers spent {compute['moe_seconds_total']:.3f}s across experts "
+                f"({(compute['moe_share_of_forward'] or 0):.0%} of the profiled pass).", ""]
     if "training_stability" in report:
-        out += ["## Training stability", "", "| metric | value |", "|---|---|"]
-        out += [f"| {k} | {v} |" for k, v in report["training_stability"].items()]
-        out.append("")
+        out += ["## Training stability", "", *_table(("metric", "value"), report["training_stability"].items())]
     return "\n".join(out)
 
 
