@@ -248,12 +248,87 @@ def run_native(args, rank, world, local):
 
 
 # ================================================================================================ reference arm
+REFERENCE_MODULE = "quantweave_moe_model.py"  # the reference's model module; its directory holds all its modules
+
+
+def _module_dir(path: str):
+    return path if path and os.path.isfile(os.path.join(path, REFERENCE_MODULE)) else None
+
+
+def locate_reference_src(root: str = ROOT, environ=None):
+    """Find the directory that holds the unmodified reference's top-level modules.
+
+    The reference is a flat collection of modules (``quantweave_moe_model.py``, ``moe_kernels.py``,
+    ``expert_parallel.py``, ...) that import each other by bare name, and its ``pyproject.toml`` declares
+    ``py-modules = []``, so a ``pip install --target baseline/_ref`` lays down only a ``*.dist-info`` folder. The
+    modules are therefore looked up, in order, at:
+
+    1. ``$QW_REFERENCE_SRC`` (an explicit override);
+    2. any directory under ``baseline/_ref`` (four levels deep at most) that contains the model module;
+    3. the source tree recorded by the install: ``direct_url.json`` of each ``baseline/_ref/*.dist-info`` holds a
+       ``file://`` URL of the installed project, whose ``src/`` (or root) holds the modules;
+    4. the current import path (a ``PYTHONPATH`` that already exposes the modules).
+
+    Returns ``(directory or None, searched)``; ``searched`` lists every place looked at, for the error line.
+    """
+    import glob
+    import importlib.util
+    from urllib.parse import unquote, urlparse
+
+    environ = os.environ if environ is None else environ
+    searched = []
+    explicit = environ.get("QW_REFERENCE_SRC")
+    if explicit:
+        searched.append(f"$QW_REFERENCE_SRC={explicit}")
+        if _module_dir(explicit):
+            return explicit, searched
+    base = os.path.join(root, "baseline", "_ref")
+    searched.append(f"{base}/**/{REFERENCE_MODULE}")
+    if os.path.isdir(base):
+        for dirpath, dirnames, filenames in os.walk(base):
+            depth = dirpath[len(base):].count(os.sep)
+            dirnames[:] = sorted(d for d in dirnames if not d.startswith(".") and d != "__pycache__") if depth < 4 else []
+            if REFERENCE_MODULE in filenames:
+                return dirpath, searched
+        for info in sorted(glob.glob(os.path.join(base, "*.dist-info", "direct_url.json"))):
+            try:
+                with open(info) as f:
+                    url = json.load(f).get("url", "")
+            except (OSError, ValueError):
+                searched.append(f"{info} (unreadable)")
+                continue
+            parsed = urlparse(url)
+            if parsed.scheme != "file":
+                searched.append(f"{info}: {url} (not a local path)")
+                continue
+            project = unquote(parsed.path)
+            for candidate in (os.path.join(project, "src"), project):
+                searched.append(f"{candidate} (from {os.path.relpath(info, root)})")
+                if _module_dir(candidate):
+                    return candidate, searched
+    spec = importlib.util.find_spec(REFERENCE_MODULE[:-3])
+    searched.append("sys.path")
+    if spec is not None and spec.origin:
+        return os.path.dirname(spec.origin), searched
+    return None, searched
+
+
+def _listing(path: str, limit: int = 12) -> str:
+    if not os.path.isdir(path):
+        return f"{os.path.relpath(path, ROOT)} does not exist"
+    names = sorted(os.listdir(path))
+    more = f" (+{len(names) - limit} more)" if len(names) > limit else ""
+    return f"{os.path.relpath(path, ROOT)}: [{', '.join(names[:limit])}]{more}"
+
+
 def run_reference(args, rank, world, local):
     import torch
 
-    ref_src = os.path.join(ROOT, "baseline", "_ref", "src")
-    if not os.path.isdir(ref_src):
-        emit(rank, {"impl": "reference", "unavailable": "baseline/_ref/src is missing (reference not installed)"})
+    ref_src, searched = locate_reference_src()
+    if ref_src is None:
+        emit(rank, {"impl": "reference",
+                    "unavailable": f"reference modules not found; searched {'; '.join(searched)}; "
+                                   f"{_listing(os.path.join(ROOT, 'baseline', '_ref'))}"})
         return
     sys.path.insert(0, ref_src)
     from quantweave_moe_model import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM  # the reference's own modules
@@ -336,6 +411,7 @@ def run_reference(args, rank, world, local):
                     "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                     "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "impl": "reference",
                     "data": "synthetic: seeded Zipf(1.1) token ids, random-init N(0,0.02) weights",
+                    "reference_src": os.path.relpath(ref_src, ROOT),
                     "config": {"model": "reference architecture at config-2 shape (LayerNorm, learned positions, MHA)",
                                "global_batch": args.seqs_per_gpu * world, "seq_len": args.seq_len,
                                "parallelism": f"ep{world}" if world > 1 else "single-gpu",

@@ -12,8 +12,16 @@
 // Contract:
 //   * dy, x: bf16 [rows, hidden] row-major; weight: fp32 [hidden]; rstd: fp32 [rows] (1/sqrt(mean(x^2)+eps) from
 //     the forward pass); dx: bf16 [rows, hidden] (written); dweight: fp32 [hidden] (overwritten, not accumulated).
-//   * hidden must be a multiple of 8; ceil(rows / 256) * hidden must not exceed QW_NOALLOC_SCRATCH_FLOATS
-//     (4,194,304 floats = 16 MiB); larger problems are rejected with QW_NOALLOC_TOO_LARGE before anything runs.
+//   * hidden must be a multiple of 8, and dy, x and dx must start on a 16-byte boundary (rows are read and written
+//     as 16-byte vectors); weight, rstd and dweight must be 4-byte aligned. Anything else is rejected with
+//     QW_NOALLOC_BAD_ARGUMENT before anything runs, so a view at an odd element offset gets an error code, not a
+//     misaligned-address fault.
+//   * ceil(rows / 256) * hidden must not exceed QW_NOALLOC_SCRATCH_FLOATS (4,194,304 floats = 16 MiB); larger
+//     problems are rejected with QW_NOALLOC_TOO_LARGE before anything runs.
+//   * rows == 0 is valid: nothing is read and dweight is set to zero.
+//   * A CUDA error already pending on the calling thread (from earlier, unrelated work) is left in place and the
+//     call returns QW_NOALLOC_PENDING_ERROR without launching, so it never reports or clears an error it did not
+//     cause; QW_NOALLOC_CUDA_ERROR means that this call's own set-up or launch failed.
 //   * The first call on a device looks up the device address of the scratch array for that device
 //     (cudaGetSymbolAddress, with that device current); make that first call before any stream capture.
 //   * Every call shares the one scratch array, which keeps the last call's partial sums. Calls that can overlap on
@@ -120,10 +128,15 @@ extern "C" QW_NOALLOC_API int qw_rmsnorm_backward_noalloc(const void* dy, const 
                                                           long long rows, int hidden, void* stream) {
   if (!dy || !x || !weight || !rstd || !dx || !dweight || rows < 0 || hidden <= 0 || hidden % 8)
     return QW_NOALLOC_BAD_ARGUMENT;
+  const auto misaligned = [](const void* p, uintptr_t to) { return reinterpret_cast<uintptr_t>(p) % to != 0; };
+  if (misaligned(dy, 16) || misaligned(x, 16) || misaligned(dx, 16) || misaligned(weight, 4) ||
+      misaligned(rstd, 4) || misaligned(dweight, 4))
+    return QW_NOALLOC_BAD_ARGUMENT;
   const long long blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
   if (blocks * static_cast<long long>(hidden) > QW_NOALLOC_SCRATCH_FLOATS) return QW_NOALLOC_TOO_LARGE;
   const size_t smem = static_cast<size_t>(kWarps) * hidden * sizeof(float);
   if (smem > 227 * 1024) return QW_NOALLOC_TOO_LARGE;
+  if (cudaPeekAtLastError() != cudaSuccess) return QW_NOALLOC_PENDING_ERROR;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) return QW_NOALLOC_CUDA_ERROR;
   float* scratch = nullptr;
@@ -148,6 +161,7 @@ extern "C" QW_NOALLOC_API int qw_rmsnorm_backward_noalloc(const void* dy, const 
     rms_bwd_partials<<<static_cast<unsigned>(blocks), kWarps * 32, smem, s>>>(
         static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x), weight, rstd,
         static_cast<__nv_bfloat16*>(dx), scratch, rows, hidden);
+    if (cudaGetLastError() != cudaSuccess) return QW_NOALLOC_CUDA_ERROR;  // nothing was pending on entry
   }
   rms_bwd_reduce<<<(hidden + 255) / 256, 256, 0, s>>>(scratch, static_cast<int>(blocks), hidden, dweight);
   return cudaGetLastError() == cudaSuccess ? QW_NOALLOC_OK : QW_NOALLOC_CUDA_ERROR;
@@ -156,10 +170,14 @@ extern "C" QW_NOALLOC_API int qw_rmsnorm_backward_noalloc(const void* dy, const 
 extern "C" QW_NOALLOC_API const char* qw_noalloc_error_message(int code) {
   switch (code) {
     case QW_NOALLOC_OK: return "ok";
-    case QW_NOALLOC_BAD_ARGUMENT: return "bad argument: null pointer, negative rows, or hidden not a positive multiple of 8";
+    case QW_NOALLOC_BAD_ARGUMENT:
+      return "bad argument: null pointer, negative rows, hidden not a positive multiple of 8, dy/x/dx not 16-byte "
+             "aligned, or weight/rstd/dweight not 4-byte aligned";
     case QW_NOALLOC_TOO_LARGE:
       return "problem too large: ceil(rows/256) * hidden exceeds the 4,194,304-float (16 MiB) static scratch array";
-    case QW_NOALLOC_CUDA_ERROR: return "CUDA error during set-up or launch (see cudaGetLastError)";
+    case QW_NOALLOC_CUDA_ERROR: return "CUDA error during this call's set-up or launch (see cudaGetLastError)";
+    case QW_NOALLOC_PENDING_ERROR:
+      return "an earlier CUDA error is pending on this thread; nothing was launched and the error was left in place";
     default: return "unknown error code";
   }
 }

@@ -2,7 +2,9 @@
 //
 // For callers that may not allocate device memory: every buffer is passed in, and the only scratch space is a
 // fixed-size static device array (QW_NOALLOC_SCRATCH_FLOATS floats) that each GPU loading the library keeps until
-// the process exits. See noalloc.cu for the full contract (size limit, first-call set-up, shared scratch).
+// the process exits. Two rules follow from that array: calls that can overlap on the GPU (streams with no order
+// between them) race on it, and the first call on each device looks up the array's device address, so it must
+// come before any stream capture. dy, x and dx must be 16-byte aligned. See noalloc.cu for the full contract.
 #pragma once
 
 #define QW_NOALLOC_API __attribute__((visibility("default")))
@@ -13,6 +15,7 @@
 #define QW_NOALLOC_BAD_ARGUMENT 1
 #define QW_NOALLOC_TOO_LARGE 2
 #define QW_NOALLOC_CUDA_ERROR 3
+#define QW_NOALLOC_PENDING_ERROR 4
 
 #ifdef __cplusplus
 extern "C" {

@@ -575,7 +575,8 @@ class DeviceLoadTracker:
     """Per-rank expert time/rows controller (reference ``DeviceLoadTracker``, ``src/expert_parallel.py:280-384``).
 
     Every ``interval`` steps the per-layer expert seconds and rows each rank accumulated are collected into one
-    ``[layers, ranks]`` table (one all-reduce of a rank-slotted slab, after a mean over the tensor-parallel group).
+    ``[layers, ranks]`` table (one all-reduce of a rank-slotted slab, after a mean over the tensor-parallel group
+    on the EP x TP grid; not under sequence parallelism, where every rank holds different experts).
     The routing bias is an integral controller ``bias_r -= rate * strength * log(t_r / mean)``, clamped to
     ``max_bias`` and re-centred, added to the router logits for selection only. ``adapt_capacity`` additionally sets
     each rank's ``capacity_scale`` to ``clamp(mean / t_r)``. Measuring per-expert time synchronises the device, so
@@ -600,7 +601,10 @@ class DeviceLoadTracker:
         """``local[layer, ...]`` of every rank as ``[layer, rank, ...]`` on the host: each rank writes its own slot
         of a zero slab and one sum-all-reduce over the expert-parallel group fills in the others."""
         local = local.to(self.ctx.device, torch.float64)
-        if self.ctx.tp_size > 1:
+        # on the EP x TP grid the tensor-parallel ranks share one expert slice and measured the same work, so their
+        # figures are averaged; with sequence parallelism the tensor-parallel ranks ARE the expert ranks, each with
+        # its own experts, and averaging would erase exactly the differences the controller acts on
+        if self.ctx.tp_size > 1 and not self.ctx.sequence_parallel:
             dist.all_reduce(local, group=self.ctx.tp_group)
             local = local / self.ctx.tp_size
         slab = local.new_zeros((self.ctx.world_size, *local.shape))

@@ -30,6 +30,7 @@ import hmac
 import json
 import logging
 import re
+import threading
 import time
 import uuid
 from collections import Counter, defaultdict
@@ -42,6 +43,10 @@ from pydantic import BaseModel, Field
 from .chat import DEFAULT_CHECKPOINT, ChatSession, Settings, load_for_chat, resolve_model
 
 logger = logging.getLogger("quantaweave_b200.serve")
+
+
+class ClientDisconnected(Exception):
+    """Raised inside a streaming producer's worker thread once its client has gone away, to end the generation."""
 
 
 class GenerateRequest(BaseModel):
@@ -395,18 +400,30 @@ class Server:
         self.metrics.tokens_generated_total += reply.tokens
         return reply_payload(reply)
 
-    async def _relay(self, produce, cancel=None):
+    async def _relay(self, produce, cancel=None, interrupt: bool = False):
         """Server-sent events from a blocking producer: ``produce(on_text)`` runs in a worker thread and returns the
         reply payload; every piece it hands to ``on_text`` is sent as ``data: {"text": ...}`` as soon as it exists,
         and the payload follows as ``event: done``. A sentinel queued when the producer returns (or raises) ends the
-        stream. If the client goes away first, ``cancel`` is called and the task is abandoned."""
+        stream.
+
+        If the client goes away first, ``cancel`` is called and, with ``interrupt``, the next ``on_text`` call raises
+        :class:`ClientDisconnected` inside the worker thread, which ends the producer early. A thread cannot be
+        stopped from outside, so the generator then waits until the worker has actually returned: whatever the
+        producer uses (the session and its KV cache, guarded by the caller's lock) is free by the time the caller
+        releases that lock."""
         loop = asyncio.get_running_loop()
         pieces: asyncio.Queue = asyncio.Queue()
         finished = object()
+        gone = threading.Event()
+
+        def on_text(piece: str) -> None:
+            if interrupt and gone.is_set():
+                raise ClientDisconnected("the streaming client went away")
+            loop.call_soon_threadsafe(pieces.put_nowait, piece)
 
         def work():
             try:
-                return produce(lambda piece: loop.call_soon_threadsafe(pieces.put_nowait, piece))
+                return produce(on_text)
             finally:
                 loop.call_soon_threadsafe(pieces.put_nowait, finished)
 
@@ -417,9 +434,16 @@ class Server:
             payload = await task
         finally:
             if not task.done():
+                gone.set()
                 if cancel is not None:
                     cancel()
-                task.cancel()
+                while not task.done():  # asyncio.wait never cancels the task it waits on
+                    try:
+                        await asyncio.wait({task})
+                    except asyncio.CancelledError:
+                        continue
+                if not task.cancelled():
+                    task.exception()  # retrieved: the producer's ClientDisconnected is expected here
         self.requests_served += 1
         self.metrics.tokens_generated_total += payload["tokens"]
         yield f"event: done\ndata: {json.dumps(payload)}\n\n"
@@ -444,7 +468,8 @@ class Server:
         await self._acquire()
         try:
             self.complete_session.settings = self._complete_settings(request)
-            events = self._relay(lambda on_text: reply_payload(self.complete_session.send(request.prompt, on_text)))
+            events = self._relay(lambda on_text: reply_payload(self.complete_session.send(request.prompt, on_text)),
+                                 interrupt=True)
             async with contextlib.aclosing(events):
                 async for event in events:
                     yield event

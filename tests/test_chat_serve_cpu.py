@@ -157,3 +157,47 @@ def test_http_server_continuous_batching(trained):
         assert "".join(pieces) == full
     finally:
         batched.close()
+
+
+def test_stream_disconnect_waits_for_the_worker_thread(trained):
+    """A streaming client that goes away mid-reply ends the producer inside its worker thread, and the relay returns
+    only after that thread has returned, so the session lock is never released while the session is still in use."""
+    import asyncio
+    import threading
+
+    from quantaweave_b200.tools.serve import ClientDisconnected, GenerateRequest, Server
+
+    server = Server(trained, None, torch.device("cpu"), "fp32")
+    release, worker_done, outcome = threading.Event(), threading.Event(), []
+
+    def produce(on_text):
+        try:
+            on_text("a")
+            release.wait(10)
+            on_text("b")  # the client is gone by now: this raises inside the worker
+            outcome.append("kept going")
+        except ClientDisconnected:
+            outcome.append("stopped")
+            raise
+        finally:
+            worker_done.set()
+
+    async def disconnecting_client():
+        events = server._relay(produce, interrupt=True)
+        assert '"a"' in await events.__anext__()
+        threading.Timer(0.3, release.set).start()
+        await events.aclose()
+        assert worker_done.is_set()  # aclose came back only after the worker returned
+
+    asyncio.run(disconnecting_client())
+    assert outcome == ["stopped"]
+
+    async def stream_then_generate():
+        events = server.stream_generate(GenerateRequest(prompt="the", tokens=64, temperature=0))
+        await events.__anext__()  # first piece arrives; the client then disconnects
+        await events.aclose()
+        assert not server.lock.locked()
+        reply = await server.generate(GenerateRequest(prompt="the", tokens=4, temperature=0))
+        assert reply["tokens"] <= 4
+
+    asyncio.run(stream_then_generate())

@@ -43,6 +43,15 @@ def _only_bundle(root: Path) -> Path:
     return bundles[0]
 
 
+@pytest.fixture(autouse=True)
+def _private_tempdir(tmp_path, monkeypatch):
+    """Each test gets its own temporary directory, so files that concurrently running tests leave in the shared
+    one are never counted as this test's leftovers."""
+    private = tmp_path / "tempdir"
+    private.mkdir()
+    monkeypatch.setattr(tempfile, "tempdir", str(private))
+
+
 def _temp_leftovers() -> set:
     root = Path(tempfile.gettempdir())
     return {p.name for p in root.glob("diagnostics-*")} | {p.name for p in root.glob("tmp*.jsonl")}

@@ -87,3 +87,33 @@ def test_a_weights_only_resharded_checkpoint_loads_across_ranks(tmp_path):
     info = reshard_checkpoint(tmp_path / "full", tmp_path / "shards", ep_size=2)
     assert info["world_size"] == 2 and (tmp_path / "shards" / "config.json").exists()
     assert run_ranks(_resharded_case, 2, (str(tmp_path),)) == {0: 7, 1: 7}
+
+
+def _sequence_parallel_capacity_case(rank, world):
+    """Under sequence parallelism the tensor-parallel ranks are the expert ranks; a slow rank must still show up as
+    slow (its timings are not averaged away over the tensor-parallel group). One controller step is checked: later
+    steps route traffic off the slow rank, which then stops being slow."""
+    from quantaweave_b200.parallel.expert_parallel import DeviceLoadTracker, init_expert_parallel
+
+    ep = init_expert_parallel("cpu", world, sequence_parallel=True)
+    torch.manual_seed(0)
+    model = QuantaWeaveMoEForCausalLM(tiny_config(capacity_factor=1.0, num_experts=4, top_k=1),
+                                      expert_parallel=ep).eval()
+    for moe in model.moes():
+        moe.simulated_cost_per_row = 2e-3 if rank == 1 else 0.0
+    tracker = DeviceLoadTracker(model, ep, strength=0.5, interval=1, adapt_capacity=True, capacity_scale_min=0.5,
+                                capacity_scale_max=2.0)
+    batch = torch.randint(0, 64, (4, 17), generator=torch.Generator().manual_seed(5))
+    with torch.no_grad():
+        model(batch, labels=batch)
+        metrics = tracker.update(1)
+    return [moe.capacity_scale for moe in model.moes()], metrics["time_imbalance"], metrics["rank_bias"]
+
+
+def test_straggler_control_acts_under_sequence_parallelism():
+    results = run_ranks(_sequence_parallel_capacity_case, 2)
+    fast, slow = results[0][0], results[1][0]
+    assert all(s < 1.0 for s in slow) and all(f > 1.0 for f in fast), (fast, slow)
+    assert results[0][1] > 1.0
+    bias = results[0][2]
+    assert bias[1] < bias[0]  # routing is biased away from the slow rank's experts

@@ -51,6 +51,31 @@ def _case(ext, rows, hidden, seed):
     return x, dy, w, rstd, dx_ref, dw_ref
 
 
+def _fp32_rmsnorm_backward(x, dy, w, eps=1e-5):
+    """Plain PyTorch fp32 RMSNorm backward (autograd through y = x * rsqrt(mean(x^2) + eps) * w)."""
+    xf = x.float().requires_grad_(True)
+    wf = w.float().clone().requires_grad_(True)
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * wf
+    y.backward(dy.float())
+    return xf.grad, wf.grad
+
+
+def test_noalloc_rmsnorm_backward_matches_fp32_pytorch():
+    lib, ext = _lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    for seed, (rows, hidden) in enumerate([(777, 512), (300, 1024)]):  # two calls in a row, shared scratch
+        x, dy, w, rstd, _, _ = _case(ext, rows, hidden, 100 + seed)
+        dx = torch.empty_like(x)
+        dw = torch.full((hidden,), float("nan"), device="cuda")
+        code = lib.qw_rmsnorm_backward_noalloc(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr(),
+                                               dx.data_ptr(), dw.data_ptr(), rows, hidden, stream)
+        assert code == 0, lib.qw_noalloc_error_message(code).decode()
+        torch.cuda.synchronize()
+        dx_ref, dw_ref = _fp32_rmsnorm_backward(x, dy, w)
+        _close(dx, dx_ref, 3e-2)
+        _close(dw, dw_ref, 1e-2)
+
+
 def test_noalloc_rmsnorm_backward_matches_regular_entry_point():
     lib, ext = _lib()
     stream = torch.cuda.current_stream().cuda_stream
@@ -68,6 +93,36 @@ def test_noalloc_rmsnorm_backward_matches_regular_entry_point():
 
 def test_noalloc_rejects_oversized_problems():
     lib, _ = _lib()
-    code = lib.qw_rmsnorm_backward_noalloc(1, 1, 1, 1, 1, 1, 10_000_000, 4096, None)
+    code = lib.qw_rmsnorm_backward_noalloc(256, 256, 256, 256, 256, 256, 10_000_000, 4096, None)  # never read
     assert code == 2
     assert b"too large" in lib.qw_noalloc_error_message(code)
+
+
+def test_noalloc_rejects_misaligned_rows_before_launching():
+    lib, _ = _lib()
+    rows, hidden = 16, 256
+    buf = torch.zeros(rows * hidden + 8, device="cuda", dtype=torch.bfloat16)
+    ok = buf[: rows * hidden]
+    odd = buf[1: 1 + rows * hidden]  # a legal view at an odd bf16 offset: 2 bytes past a 16-byte boundary
+    w = torch.ones(hidden, device="cuda")
+    rstd = torch.ones(rows, device="cuda")
+    dw = torch.zeros(hidden, device="cuda")
+    for dy, x, dx in ((odd, ok, ok), (ok, odd, ok), (ok, ok, odd)):
+        code = lib.qw_rmsnorm_backward_noalloc(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr(),
+                                               dx.data_ptr(), dw.data_ptr(), rows, hidden, None)
+        assert code == 1
+        assert b"16-byte" in lib.qw_noalloc_error_message(code)
+    torch.cuda.synchronize()  # nothing was launched, so the context is untouched
+
+
+def test_noalloc_zero_rows_zeroes_the_weight_gradient():
+    lib, _ = _lib()
+    hidden = 256
+    buf = torch.zeros(hidden, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(hidden, device="cuda")
+    dw = torch.full((hidden,), float("nan"), device="cuda")
+    code = lib.qw_rmsnorm_backward_noalloc(buf.data_ptr(), buf.data_ptr(), w.data_ptr(), w.data_ptr(), buf.data_ptr(),
+                                           dw.data_ptr(), 0, hidden, torch.cuda.current_stream().cuda_stream)
+    assert code == 0
+    torch.cuda.synchronize()
+    assert torch.equal(dw, torch.zeros_like(dw))
