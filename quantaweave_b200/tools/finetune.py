@@ -4,11 +4,13 @@
         --data new_domain.jsonl --output artifacts/outputs/qlora --bits 4 --rank 8 --steps 500 \\
         --merge-output artifacts/outputs/qlora-merged
 
-Parity with the reference ``src/finetune_quantweave_moe.py`` (``load_base`` :34, ``evaluate`` :41-53,
-``load_finetuned`` :54-65, CLI :68-91, ``run_finetune`` :92-181): experts quantised to int4/int8 and frozen, only the
-adapters (and optionally routers/norms) train; the output directory holds ``adapter.pt``,
-``finetune_metadata.json`` and the config/tokenizer files so ``load_finetuned`` rebuilds the model from the untouched
-base checkpoint; ``--merge-output`` writes an ordinary full-precision checkpoint with the adapters folded in.
+Same CLI, public functions and output files as the reference ``src/finetune_quantweave_moe.py`` (``load_base`` :34,
+``evaluate`` :41-53, ``load_finetuned`` :54-65, CLI :68-91, ``run_finetune`` :92-181): the base experts are quantised
+to int4/int8 and frozen, and only the adapters (optionally also the routers and norms) train. The output directory
+holds ``adapter.pt``, ``finetune_metadata.json`` and the config/tokenizer files, so ``load_finetuned`` rebuilds the
+model from the untouched base checkpoint; ``--merge-output`` writes an ordinary full-precision checkpoint with the
+adapters folded in. A run is a :class:`_FineTune` object whose stages run in order: prepare, measure, train,
+measure again, write the outputs, archive.
 """
 
 from __future__ import annotations
@@ -40,18 +42,20 @@ def load_base(checkpoint: Path, device: torch.device):
 
 @torch.no_grad()
 def evaluate(model, dataset, device: torch.device, precision: str, batch_size: int = 8, batches: int = 8) -> float:
-    """Mean loss over the first ``batches`` batches of windows (fixed, so before/after numbers compare)."""
+    """Row-weighted mean loss over a fixed prefix of the dataset (its first ``batch_size * batches`` windows),
+    so numbers taken before and after training compare like for like. Leaves the model in training mode."""
     from ..training.trainer import autocast_context
 
     model.eval()
-    total, count = 0.0, 0
-    for start in range(0, min(len(dataset), batch_size * batches), batch_size):
-        batch = dataset.batch(range(start, min(len(dataset), start + batch_size))).to(device)
+    rows = range(min(len(dataset), batch_size * batches))
+    weighted, seen = 0.0, 0
+    for first in rows[::batch_size]:
+        chunk = dataset.batch(range(first, min(rows.stop, first + batch_size))).to(device)
         with autocast_context(device, precision):
-            total += float(model(batch, labels=batch)["loss"]) * batch.size(0)
-        count += batch.size(0)
+            weighted += float(model(chunk, labels=chunk)["loss"]) * len(chunk)
+        seen += len(chunk)
     model.train()
-    return total / max(1, count)
+    return weighted / seen if seen else 0.0
 
 
 def load_finetuned(base_checkpoint: Path, adapter_dir: Path, device: Optional[torch.device] = None):
@@ -97,90 +101,140 @@ def build_parser() -> argparse.ArgumentParser:
     return p
 
 
-def run_finetune(args) -> dict:
-    from ..data.pipeline import BatchStream, WindowDataset, build_corpus, load_tokenizer
-    from ..inference.quantization import quantize_model
-    from ..training.trainer import autocast_context, build_optimizer, select_device, write_checkpoint_metadata
-    from ..utils.hardware import choose_precision, detect
-    from .common import read_config
+QUANTISED_BUFFERS = ("qweight", "scales", "q_gate_up", "s_gate_up", "q_down", "s_down")
+COPIED_FILES = ("config.json", "vocab.json", "tokenizer.json", "tokenizer_meta.json", "tokenizer.model")
 
-    started_at = time.time()
-    device = select_device(args.device)
-    random.seed(args.seed)
-    torch.manual_seed(args.seed)
-    tokenizer = load_tokenizer(args.checkpoint)
-    model = load_base(args.checkpoint, device)
-    if args.sequence_length + 1 > model.config.max_sequence_length:
-        raise ValueError(f"--sequence-length {args.sequence_length} exceeds the checkpoint's context "
-                         f"{model.config.max_sequence_length - 1}")
-    dataset = WindowDataset(build_corpus([args.data], tokenizer, args.examples), args.sequence_length)
-    if len(dataset) == 0:
-        raise ValueError("the fine-tuning data holds fewer tokens than one window")
-    precision = choose_precision(detect(device.type), args.precision)
-    fp32_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
-    quant = quantize_model(model, args.bits, args.group_size) if args.bits else None
-    info = add_lora(model, args.rank, args.alpha, args.include_lm_head, args.train_router, args.train_norms)
-    base_loss = evaluate(model, dataset, device, precision)
-    quantized_bytes = sum(p.numel() * p.element_size() for p in model.parameters()) + sum(
-        b.numel() * b.element_size() for n, b in model.named_buffers()
-        if n.split(".")[-1] in ("qweight", "scales", "q_gate_up", "s_gate_up", "q_down", "s_down"))
-    trainable = [p for p in model.parameters() if p.requires_grad]
-    optimizer = build_optimizer(args.optimizer, trainable, args.lr, device=device)
-    stream = BatchStream(dataset, args.batch_size, args.seed)
-    model.train()
-    losses = []
-    started = time.perf_counter()
-    for step in range(1, args.steps + 1):
-        batch, _ = stream.batch(step)
-        batch = batch.to(device)
-        with autocast_context(device, precision):
-            loss = model(batch, labels=batch)["loss"]
-        optimizer.zero_grad(set_to_none=True)
-        loss.backward()
-        torch.nn.utils.clip_grad_norm_(trainable, 1.0)
-        optimizer.step()
-        losses.append(float(loss.detach()))
-        if step % 10 == 0 or step == args.steps:
-            print(f"finetune step={step}/{args.steps} loss={losses[-1]:.4f}")
-    final_loss = evaluate(model, dataset, device, precision)
 
-    args.output.mkdir(parents=True, exist_ok=True)
-    metadata = {
-        "base_checkpoint": str(args.checkpoint), "bits": args.bits, "group_size": args.group_size, "rank": args.rank,
-        "alpha": args.alpha, "include_lm_head": args.include_lm_head, "train_router": args.train_router,
-        "train_norms": args.train_norms, "optimizer": args.optimizer, "steps": args.steps,
-        "trainable_parameters": info["trainable_parameters"], "total_parameters": info["total_parameters"],
-        "trainable_fraction": info["trainable_parameters"] / info["total_parameters"],
-        "fp32_parameter_bytes": fp32_bytes, "quantized_model_bytes": quantized_bytes, "quantization": quant,
-        "loss_before": base_loss, "loss_after": final_loss, "seconds": time.perf_counter() - started,
-        "peak_device_bytes": torch.cuda.max_memory_allocated(device) if device.type == "cuda" else None,
-    }
-    save_adapter(model, args.output / "adapter.pt", info, str(args.checkpoint))
-    (args.output / "finetune_metadata.json").write_text(json.dumps(metadata, indent=2, default=str) + "\n")
-    for name in ("config.json", "vocab.json", "tokenizer.json", "tokenizer_meta.json", "tokenizer.model"):
-        if (args.checkpoint / name).exists():
-            shutil.copy(args.checkpoint / name, args.output / name)
-    if args.merge_output is not None:
-        merged = merge_lora_state(model)
-        args.merge_output.mkdir(parents=True, exist_ok=True)
-        torch.save({"model": {k: v.cpu() for k, v in merged.items()}, "optimizer": None, "step": None,
-                    "rng_state": {}, "extra": {"merged_from": str(args.output)}}, args.merge_output / "model.pt")
-        write_checkpoint_metadata(args.merge_output, read_config(args.checkpoint),
-                                  tokenizer.vocab if tokenizer.kind == "char" else tokenizer, 0, None)
-    if getattr(args, "archive_dir", None) is not None and not args.no_archive:
-        models = {"adapter": args.output, **({"merged": args.merge_output} if args.merge_output is not None else {})}
-        bundle = create_run_bundle(
-            args.archive_dir, kind="finetune", model_dirs=models, benchmark_model=args.merge_output,
-            data_paths=[args.data], options=vars(args),
-            summary={**metadata, "final_loss": metadata["loss_after"], "steps": args.steps}, started=started_at,
-            finished=time.time(),
-            reproduce=reproduce_command("quantaweave_b200.tools.finetune", build_parser(), args,
-                                        skip=("archive_dir", "no_archive")),
-            skip_rows=args.examples, benchmark_examples=args.archive_benchmark_examples, device=args.device,
-            precision=args.precision, data_limit_mb=args.archive_data_limit_mb, data_card=args.data_card)
-        metadata["archive"] = str(bundle)
+def _bytes(tensors) -> int:
+    return sum(t.numel() * t.element_size() for t in tensors)
+
+
+class _FineTune:
+    """One fine-tuning run, stage by stage; ``record`` becomes ``finetune_metadata.json``."""
+
+    def __init__(self, args) -> None:
+        self.args = args
+        self.record: dict = {}
+
+    def prepare(self) -> None:
+        from ..data.pipeline import WindowDataset, build_corpus, load_tokenizer
+        from ..inference.quantization import quantize_model
+        from ..training.trainer import select_device
+        from ..utils.hardware import choose_precision, detect
+
+        a = self.args
+        self.device = select_device(a.device)
+        random.seed(a.seed)
+        torch.manual_seed(a.seed)
+        self.tokenizer = load_tokenizer(a.checkpoint)
+        self.model = load_base(a.checkpoint, self.device)
+        context = self.model.config.max_sequence_length - 1
+        if a.sequence_length > context:
+            raise ValueError(f"--sequence-length {a.sequence_length} exceeds the checkpoint's context {context}")
+        self.dataset = WindowDataset(build_corpus([a.data], self.tokenizer, a.examples), a.sequence_length)
+        if len(self.dataset) == 0:
+            raise ValueError("the fine-tuning data holds fewer tokens than one window")
+        self.precision = choose_precision(detect(self.device.type), a.precision)
+        full_bytes = _bytes(self.model.parameters())
+        quantisation = quantize_model(self.model, a.bits, a.group_size) if a.bits else None
+        self.adapters = add_lora(self.model, a.rank, a.alpha, a.include_lm_head, a.train_router, a.train_norms)
+        packed = [b for name, b in self.model.named_buffers() if name.rsplit(".", 1)[-1] in QUANTISED_BUFFERS]
+        total = self.adapters["total_parameters"]
+        self.record.update(
+            base_checkpoint=str(a.checkpoint), bits=a.bits, group_size=a.group_size, rank=a.rank, alpha=a.alpha,
+            include_lm_head=a.include_lm_head, train_router=a.train_router, train_norms=a.train_norms,
+            optimizer=a.optimizer, steps=a.steps, trainable_parameters=self.adapters["trainable_parameters"],
+            total_parameters=total, trainable_fraction=self.adapters["trainable_parameters"] / total,
+            fp32_parameter_bytes=full_bytes,
+            quantized_model_bytes=_bytes(self.model.parameters()) + _bytes(packed), quantization=quantisation)
+
+    def measure(self, key: str) -> None:
+        self.record[key] = evaluate(self.model, self.dataset, self.device, self.precision)
+
+    def train(self) -> None:
+        from ..data.pipeline import BatchStream
+        from ..training.trainer import autocast_context, build_optimizer
+
+        a = self.args
+        params = [p for p in self.model.parameters() if p.requires_grad]
+        optimizer = build_optimizer(a.optimizer, params, a.lr, device=self.device)
+        batches = BatchStream(self.dataset, a.batch_size, a.seed)
+        self.model.train()
+        clock = time.perf_counter()
+        for step in range(1, a.steps + 1):
+            tokens = batches.batch(step)[0].to(self.device)
+            with autocast_context(self.device, self.precision):
+                loss = self.model(tokens, labels=tokens)["loss"]
+            optimizer.zero_grad(set_to_none=True)
+            loss.backward()
+            torch.nn.utils.clip_grad_norm_(params, 1.0)
+            optimizer.step()
+            if step == a.steps or step % 10 == 0:
+                print(f"finetune step={step}/{a.steps} loss={float(loss.detach()):.4f}")
+        self.record["seconds"] = time.perf_counter() - clock
+        on_gpu = self.device.type == "cuda"
+        self.record["peak_device_bytes"] = torch.cuda.max_memory_allocated(self.device) if on_gpu else None
+
+    def write(self) -> None:
+        from ..training.trainer import write_checkpoint_metadata
+        from .common import read_config
+
+        a = self.args
+        a.output.mkdir(parents=True, exist_ok=True)
+        save_adapter(self.model, a.output / "adapter.pt", self.adapters, str(a.checkpoint))
+        ordered = {key: self.record[key] for key in METADATA_KEYS}
+        (a.output / "finetune_metadata.json").write_text(json.dumps(ordered, indent=2, default=str) + "\n")
+        for name in COPIED_FILES:
+            if (a.checkpoint / name).exists():
+                shutil.copy(a.checkpoint / name, a.output / name)
+        if a.merge_output is None:
+            return
+        weights = {name: tensor.cpu() for name, tensor in merge_lora_state(self.model).items()}
+        a.merge_output.mkdir(parents=True, exist_ok=True)
+        torch.save({"model": weights, "optimizer": None, "step": None, "rng_state": {},
+                    "extra": {"merged_from": str(a.output)}}, a.merge_output / "model.pt")
+        vocab = self.tokenizer.vocab if self.tokenizer.kind == "char" else self.tokenizer
+        write_checkpoint_metadata(a.merge_output, read_config(a.checkpoint), vocab, 0, None)
+
+    def archive(self, started_at: float) -> None:
+        a = self.args
+        if getattr(a, "archive_dir", None) is None or a.no_archive:
+            return
+        models = {"adapter": a.output}
+        if a.merge_output is not None:
+            models["merged"] = a.merge_output
+        summary = {**self.record, "final_loss": self.record["loss_after"], "steps": a.steps}
+        command = reproduce_command("quantaweave_b200.tools.finetune", build_parser(), a,
+                                    skip=("archive_dir", "no_archive"))
+        bundle = create_run_bundle(a.archive_dir, kind="finetune", model_dirs=models, benchmark_model=a.merge_output,
+                                   data_paths=[a.data], options=vars(a), summary=summary, started=started_at,
+                                   finished=time.time(), reproduce=command, skip_rows=a.examples,
+                                   benchmark_examples=a.archive_benchmark_examples, device=a.device,
+                                   precision=a.precision, data_limit_mb=a.archive_data_limit_mb,
+                                   data_card=a.data_card)
+        self.record["archive"] = str(bundle)
         print(f"archived run to {bundle}")
-    return metadata
+
+
+# the keys of finetune_metadata.json, in file order
+METADATA_KEYS = ("base_checkpoint", "bits", "group_size", "rank", "alpha", "include_lm_head", "train_router",
+                 "train_norms", "optimizer", "steps", "trainable_parameters", "total_parameters",
+                 "trainable_fraction", "fp32_parameter_bytes", "quantized_model_bytes", "quantization",
+                 "loss_before", "loss_after", "seconds", "peak_device_bytes")
+
+
+def run_finetune(args) -> dict:
+    """Quantise, attach adapters, train them, and write the adapter directory (plus optional merged checkpoint
+    and run archive). Returns the metadata record."""
+    started_at = time.time()
+    run = _FineTune(args)
+    run.prepare()
+    run.measure("loss_before")
+    run.train()
+    run.measure("loss_after")
+    run.write()
+    run.archive(started_at)
+    return run.record
 
 
 def main(argv=None) -> None:

@@ -1,9 +1,10 @@
-"""Plain full-context sampling from a checkpoint (no KV cache).
+"""Plain full-context sampling from a checkpoint, without a KV cache.
 
-Parity with the reference ``src/generate_quantweave_moe.py`` (``sample_text`` :16-33, CLI :36-51): encode the prompt
-(``unk`` if empty), keep the last ``max_sequence_length - 1`` tokens as context, mask logits of ids beyond the
-tokenizer's vocabulary, sample from ``softmax(logits / max(T, 0.01))`` and stop at ``<eos>``. For cached decoding use
-``quantaweave_b200.inference.fast_decode.FastDecoder``.
+Same behaviour and CLI as the reference ``src/generate_quantweave_moe.py`` (``sample_text`` :16-33, ``main``
+:36-51): the prompt's ids (the tokenizer's ``unk`` id when it encodes to nothing) seed the sequence; every step
+re-runs the model on the newest ``max_sequence_length - 1`` ids (the trainer never trains the last position of a
+window), excludes ids the tokenizer cannot produce, samples from ``softmax(logits / max(T, 0.01))`` and stops
+after ``<eos>``. This is the simple reference loop; ``inference.fast_decode.FastDecoder`` is the cached decoder.
 """
 
 from __future__ import annotations
@@ -14,24 +15,34 @@ from pathlib import Path
 import torch
 
 
+def _producible(logit_count: int, tokenizer_vocab: int, device) -> torch.Tensor:
+    """Additive logit mask: 0 for ids the tokenizer can emit, -inf for the model's extra (never trained) rows."""
+    mask = torch.zeros(logit_count, device=device)
+    mask[tokenizer_vocab:] = float("-inf")
+    return mask
+
+
 def sample_text(model, tokenizer, prompt: str, tokens: int, temperature: float, device: torch.device,
                 precision: str = "auto") -> str:
+    """Sample up to ``tokens`` ids after ``prompt`` and return the decoded prompt plus continuation."""
     from ..training.trainer import autocast_context
 
-    generated = tokenizer.encode(prompt) or [tokenizer.unk_id]
-    context = model.config.max_sequence_length - 1  # the last position of a training window is never trained
+    sequence = torch.tensor(tokenizer.encode(prompt) or [tokenizer.unk_id], dtype=torch.long, device=device)
+    window = model.config.max_sequence_length - 1
+    inverse_temperature = 1.0 / max(temperature, 0.01)
+    mask = None
     with torch.inference_mode():
         for _ in range(tokens):
-            window = torch.tensor([generated[-context:]], dtype=torch.long, device=device)
             with autocast_context(device, precision):
-                logits = model(window)["logits"][:, -1, :].float()
-            logits[:, tokenizer.vocab_size:] = float("-inf")  # ids the tokenizer never produced are untrained
-            probs = (logits / max(temperature, 0.01)).softmax(dim=-1)
-            next_id = int(torch.multinomial(probs, 1).item())
-            generated.append(next_id)
-            if next_id == tokenizer.eos_id:
+                last = model(sequence[-window:].unsqueeze(0))["logits"][0, -1].float()
+            if mask is None:
+                mask = _producible(last.numel(), tokenizer.vocab_size, device)
+            probabilities = torch.softmax((last + mask) * inverse_temperature, dim=-1)
+            chosen = torch.multinomial(probabilities, 1)
+            sequence = torch.cat((sequence, chosen))
+            if int(chosen) == tokenizer.eos_id:
                 break
-    return tokenizer.decode(generated)
+    return tokenizer.decode(sequence.tolist())
 
 
 def build_parser() -> argparse.ArgumentParser:
@@ -56,8 +67,8 @@ def main(argv=None) -> None:
     args = build_parser().parse_args(argv)
     device = select_device(args.device)
     model = load_model(args.checkpoint, device, args.precision)
-    tokenizer = load_tokenizer(args.checkpoint)
-    print(sample_text(model, tokenizer, args.prompt, args.tokens, args.temperature, device, args.precision))
+    print(sample_text(model, load_tokenizer(args.checkpoint), args.prompt, args.tokens, args.temperature, device,
+                      args.precision))
 
 
 if __name__ == "__main__":
