@@ -118,6 +118,43 @@ void moe_down_fwd(Tensor h, Tensor w, Tensor counts, Tensor offsets, Tensor y) {
                    stream());
 }
 
+// peer_ptrs: int64 [world] base address of every rank's receive buffer (bf16 [world * peer_rows, H]); row r of the
+// result goes to rank r / peer_rows at row peer_slot * peer_rows + r % peer_rows
+static void* const* peer_table(const Tensor& peer_ptrs, int64_t peer_rows, int64_t R) {
+  CHECK_CUDA(peer_ptrs);
+  CHECK_DTYPE(peer_ptrs, torch::kInt64);
+  TORCH_CHECK(peer_rows > 0 && R == peer_ptrs.numel() * peer_rows, "peer table: rows must be world * peer_rows");
+  return reinterpret_cast<void* const*>(peer_ptrs.data_ptr<int64_t>());
+}
+
+void moe_down_fwd_peer(Tensor h, Tensor w, Tensor counts, Tensor offsets, Tensor peer_ptrs, int64_t peer_rows,
+                       int64_t peer_slot) {
+  CHECK_CUDA(h); CHECK_CONTIG(h); CHECK_CONTIG(w);
+  const int64_t E = w.size(0), H = w.size(1), F = w.size(2), R = h.size(0);
+  TORCH_CHECK(h.size(1) == F, "moe_down_fwd_peer shapes");
+  const int64_t G = counts.numel();
+  check_groups(counts, offsets, G);
+  TORCH_CHECK(G % E == 0, "groups must be a multiple of the expert count");
+  TORCH_CHECK(peer_slot >= 0 && peer_slot < peer_ptrs.numel(), "peer slot out of range");
+  c10::cuda::CUDAGuard g(h.device());
+  qw::moe_down_fwd(bptr(h), bptr(w), counts.data_ptr<int>(), offsets.data_ptr<int>(), R, G, E, H, F, nullptr,
+                   stream(), peer_table(peer_ptrs, peer_rows, R), peer_rows, static_cast<int>(peer_slot));
+}
+
+void moe_gate_up_dgrad_peer(Tensor dgu, Tensor w, Tensor counts, Tensor offsets, Tensor peer_ptrs, int64_t peer_rows,
+                            int64_t peer_slot) {
+  CHECK_CUDA(dgu); CHECK_CONTIG(dgu); CHECK_CONTIG(w);
+  const int64_t E = w.size(0), F = w.size(1) / 2, H = w.size(2), R = dgu.size(0);
+  TORCH_CHECK(dgu.size(1) == 2 * F, "moe_gate_up_dgrad_peer shapes");
+  const int64_t G = counts.numel();
+  check_groups(counts, offsets, G);
+  TORCH_CHECK(G % E == 0, "groups must be a multiple of the expert count");
+  TORCH_CHECK(peer_slot >= 0 && peer_slot < peer_ptrs.numel(), "peer slot out of range");
+  c10::cuda::CUDAGuard g(dgu.device());
+  qw::moe_gate_up_dgrad(bptr(dgu), bptr(w), counts.data_ptr<int>(), offsets.data_ptr<int>(), R, G, E, H, F, nullptr,
+                        stream(), peer_table(peer_ptrs, peer_rows, R), peer_rows, static_cast<int>(peer_slot));
+}
+
 void moe_down_bwd(Tensor dy, Tensor w, Tensor counts, Tensor offsets, Tensor gu, Tensor route_w, Tensor dgu,
                   OptT h_weighted, Tensor dw_partial) {
   CHECK_CUDA(dy); CHECK_CONTIG(dy); CHECK_CONTIG(w); CHECK_CONTIG(gu); CHECK_CONTIG(dgu); CHECK_CONTIG(dw_partial);
@@ -460,15 +497,6 @@ void ep_signal(Tensor peer_flags, int64_t me, int64_t epoch) {
                 static_cast<int>(me), static_cast<int>(epoch), stream());
 }
 
-void ep_gather(Tensor peer_rows, Tensor route_row, OptT top_w, OptT extra, OptT resid, int64_t k, int64_t local,
-               int64_t slot, int64_t me, Tensor out) {
-  CHECK_CUDA(out); CHECK_CONTIG(out);
-  c10::cuda::CUDAGuard g(out.device());
-  qw::ep_gather(reinterpret_cast<const qw::bf16* const*>(peer_rows.data_ptr<int64_t>()), route_row.data_ptr<int>(),
-                optptr<float>(top_w), optptr<float>(extra), optb(resid), out.size(0), static_cast<int>(k),
-                static_cast<int>(out.size(1)), static_cast<int>(local), static_cast<int>(slot), static_cast<int>(me),
-                bptr_mut(out), stream());
-}
 
 // ------------------------------------------------------------------------------------------------ fused ZeRO
 int64_t zero_rs_blocks(int64_t per) { return qw::zero_rs_blocks(per); }
@@ -598,6 +626,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_down_fwd", &moe_down_fwd);
   m.def("moe_down_bwd", &moe_down_bwd);
   m.def("moe_gate_up_dgrad", &moe_gate_up_dgrad);
+  m.def("moe_down_fwd_peer", &moe_down_fwd_peer);
+  m.def("moe_gate_up_dgrad_peer", &moe_gate_up_dgrad_peer);
   m.def("moe_wgrad", &moe_wgrad, py::arg("a"), py::arg("b"), py::arg("counts"), py::arg("offsets"), py::arg("out"),
         py::arg("accumulate"), py::arg("segments") = 1, py::arg("alpha") = 1.0);
   m.def("moe_dw_tiles", [](int64_t F) { return static_cast<int64_t>(qw::moe_dw_tiles(F)); });
@@ -639,7 +669,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("zero_adamw_gather", &zero_adamw_gather);
   m.def("ep_pad", &ep_pad);
   m.def("ep_signal", &ep_signal);
-  m.def("ep_gather", &ep_gather);
   m.def("bias_grad_slabs", &bias_grad_slabs);
   m.def("bias_grad", &bias_grad);
   m.def("decode_combine_norm", &decode_combine_norm);

@@ -7,11 +7,9 @@
 //            `epoch` into every peer's flag[me] with a system-scope release store.
 //  pad fix:  after the flag wait, the receiver zeroes each segment's rows [count, round_up(count, 128)) so the
 //            128-row GEMM tiles read zeros (and zero weights) past the last routed row.
-//  signal:   after a local kernel filled this rank's return buffer (expert outputs or input gradients), release
-//            flags to every peer.
-//  gather:   the source rank pulls the rows of its own routes from the expert ranks' return buffers with peer loads
-//            and reduces them in a fixed order: out[t] = resid + extra + sum_j w_j * row(t, j). This replaces the
-//            return all-to-all and the combine.
+//  signal:   after the expert GEMM's peer-store epilogue (gemm_tcgen05.cuh) pushed every output row into its source
+//            rank's return buffer, release flags to every peer; each source then reduces its top-k rows locally
+//            (combine_kernel / combine_grad_kernel in moe_routing.cu) once every expert rank has signalled.
 // Only plain loads and stores to peer memory are used (no multimem, no TMA). Flag waits are p2p_wait (bounded).
 #include <algorithm>
 
@@ -96,55 +94,6 @@ __global__ void ep_signal_kernel(int* const* __restrict__ peer_flags, int world,
   if (d < world) st_release_sys(peer_flags[d] + me, epoch);
 }
 
-// out[t] = resid[t] + extra[t] + sum_j w_j * peer_rows[d(t,j)][(me*local + le) * slot + pos]; warp per token
-__global__ void __launch_bounds__(256) ep_gather_kernel(const bf16* const* __restrict__ peer_rows,
-                                                        const int* __restrict__ route_row,
-                                                        const float* __restrict__ top_w,
-                                                        const float* __restrict__ extra,
-                                                        const bf16* __restrict__ resid, int64_t T, int k, int H,
-                                                        int local, int slot, int me, bf16* __restrict__ out) {
-  const int warps = blockDim.x / 32;
-  const int64_t t = static_cast<int64_t>(blockIdx.x) * warps + threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  if (t >= T) return;
-  const bf16* src[8];
-  float ws[8];
-  for (int j = 0; j < k; ++j) {
-    const int row = route_row[t * k + j];
-    src[j] = nullptr;
-    ws[j] = top_w ? top_w[t * k + j] : 1.f;
-    if (row >= 0) {
-      const int e = row / slot, pos = row % slot;
-      const int d = e / local, le = e % local;
-      src[j] = peer_rows[d] + (static_cast<int64_t>(me * local + le) * slot + pos) * H;
-    }
-  }
-  for (int c = lane * 8; c < H; c += 256) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (extra) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = extra[t * H + c + i];
-    }
-    if (resid) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(resid + t * H + c);
-      const bf16* v = reinterpret_cast<const bf16*>(&raw);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += __bfloat162float(v[i]);
-    }
-    for (int j = 0; j < k; ++j) {
-      if (!src[j]) continue;
-      const uint4 raw = *reinterpret_cast<const uint4*>(src[j] + c);  // NVLink load from the expert rank
-      const bf16* v = reinterpret_cast<const bf16*>(&raw);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] += ws[j] * __bfloat162float(v[i]);
-    }
-    uint4 o;
-    o.x = pack_bf16(acc[0], acc[1]); o.y = pack_bf16(acc[2], acc[3]);
-    o.z = pack_bf16(acc[4], acc[5]); o.w = pack_bf16(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(out + t * H + c) = o;
-  }
-}
-
 }  // namespace
 
 void ep_dispatch(const bf16* x, int64_t T, int k, int H, const int* route_row, const float* top_w, const int* kept,
@@ -169,17 +118,6 @@ void ep_pad(const int* counts, int groups, int slot, int H, bf16* rows, float* w
 void ep_signal(int* const* peer_flags, int world, int me, int epoch, cudaStream_t stream) {
   ep_signal_kernel<<<1, 32, 0, stream>>>(peer_flags, world, me, epoch);
   check_cuda(cudaGetLastError(), "ep_signal");
-}
-
-void ep_gather(const bf16* const* peer_rows, const int* route_row, const float* top_w, const float* extra,
-               const bf16* resid, int64_t T, int k, int H, int local, int slot, int me, bf16* out,
-               cudaStream_t stream) {
-  if (T == 0) return;
-  if (H % 8 || k > 8) throw std::runtime_error("ep_gather: hidden size % 8 and top-k <= 8 required");
-  const int warps = 8;
-  ep_gather_kernel<<<static_cast<int>((T + warps - 1) / warps), warps * 32, 0, stream>>>(
-      peer_rows, route_row, top_w, extra, resid, T, k, H, local, slot, me, out);
-  check_cuda(cudaGetLastError(), "ep_gather");
 }
 
 }  // namespace qw

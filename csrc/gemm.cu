@@ -261,9 +261,13 @@ void moe_gate_up_fwd(const bf16* x, const bf16* w_gate_up, const int* counts, co
   launch<BN, kGroupM, kEpiSwiGLU, false, false>(ma, mb, p, p.max_tiles, stream);
 }
 
-// y[R,H] = h[R,F] @ w_down[e]^T   (w_down [E, H, F])
+// y[R,H] = h[R,F] @ w_down[e]^T   (w_down [E, H, F]). With `peer_out`, row r is stored over NVLink into rank
+// r / peer_rows's buffer at row peer_slot * peer_rows + r % peer_rows instead (the expert-parallel combine push:
+// rows are laid out [source rank][local expert][slot], so peer_rows = local * slot and peer_slot = this rank);
+// padding rows are not written then.
 void moe_down_fwd(const bf16* h, const bf16* w_down, const int* counts, const int* offsets, int64_t R, int64_t G,
-                  int64_t E, int64_t H, int64_t F, bf16* y, cudaStream_t stream) {
+                  int64_t E, int64_t H, int64_t F, bf16* y, cudaStream_t stream, void* const* peer_out,
+                  int64_t peer_rows, int peer_slot) {
   if (R == 0) return;
   constexpr int BN = 256;
   Params p = base_params();
@@ -275,7 +279,8 @@ void moe_down_fwd(const bf16* h, const bf16* w_down, const int* counts, const in
   p.n_tiles = static_cast<int>((H + BN - 1) / BN);
   p.max_tiles = static_cast<int>(((R + kBM - 1) / kBM) * p.n_tiles);
   p.out = y; p.ldo = H;
-  p.zero_pad_rows = 1;
+  p.zero_pad_rows = peer_out ? 0 : 1;
+  p.peer_out = peer_out; p.peer_rows = peer_rows; p.peer_slot = peer_slot;
   auto ma = make_map(h, F, R, F, 64, kBM);
   auto mb = make_map(w_down, F, E * H, F, 64, BN);
   launch<BN, kGroupM, kEpiStore, false, false>(ma, mb, p, p.max_tiles, stream);
@@ -310,9 +315,10 @@ void moe_down_bwd(const bf16* dy, const bf16* w_down, const int* counts, const i
 
 int moe_dw_tiles(int64_t F) { return static_cast<int>((F + 255) / 256); }
 
-// dx[R,H] = dgu[R,2F] @ w_gate_up[e]
+// dx[R,H] = dgu[R,2F] @ w_gate_up[e]; `peer_out` as in moe_down_fwd (the expert-parallel input-gradient push)
 void moe_gate_up_dgrad(const bf16* dgu, const bf16* w_gate_up, const int* counts, const int* offsets, int64_t R,
-                       int64_t G, int64_t E, int64_t H, int64_t F, bf16* dx, cudaStream_t stream) {
+                       int64_t G, int64_t E, int64_t H, int64_t F, bf16* dx, cudaStream_t stream,
+                       void* const* peer_out, int64_t peer_rows, int peer_slot) {
   if (R == 0) return;
   constexpr int BN = 256;
   Params p = base_params();
@@ -324,7 +330,8 @@ void moe_gate_up_dgrad(const bf16* dgu, const bf16* w_gate_up, const int* counts
   p.n_tiles = static_cast<int>((H + BN - 1) / BN);
   p.max_tiles = static_cast<int>(((R + kBM - 1) / kBM) * p.n_tiles);
   p.out = dx; p.ldo = H;
-  p.zero_pad_rows = 1;
+  p.zero_pad_rows = peer_out ? 0 : 1;
+  p.peer_out = peer_out; p.peer_rows = peer_rows; p.peer_slot = peer_slot;
   auto ma = make_map(dgu, 2 * F, R, 2 * F, 64, kBM);
   auto mb = make_map(w_gate_up, H, E * 2 * F, H, 64, 64);
   launch<BN, kGroupM, kEpiStore, false, true>(ma, mb, p, p.max_tiles, stream);

@@ -534,6 +534,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
+    // rows stored into peers' memory are made visible at system scope before the kernel ends, so the flag that a
+    // later kernel releases to the peers orders them
+    if (p.peer_out) __threadfence_system();
   }
 
   tc_fence_before();

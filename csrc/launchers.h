@@ -29,13 +29,15 @@ void linear_wgrad(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int6
 void moe_gate_up_fwd(const bf16* x, const bf16* w_gate_up, const int* counts, const int* offsets, int64_t R, int64_t G,
                      int64_t E, int64_t H, int64_t F, bf16* h, bf16* gu, cudaStream_t stream);
 void moe_down_fwd(const bf16* h, const bf16* w_down, const int* counts, const int* offsets, int64_t R, int64_t G,
-                  int64_t E, int64_t H, int64_t F, bf16* y, cudaStream_t stream);
+                  int64_t E, int64_t H, int64_t F, bf16* y, cudaStream_t stream, void* const* peer_out = nullptr,
+                  int64_t peer_rows = 0, int peer_slot = 0);
 void moe_down_bwd(const bf16* dy, const bf16* w_down, const int* counts, const int* offsets, int64_t R, int64_t G,
                   int64_t E, int64_t H, int64_t F, const bf16* gu, const float* route_w, bf16* dgu, bf16* h_weighted,
                   float* dw_partial, int dw_tiles, cudaStream_t stream);
 int moe_dw_tiles(int64_t F);
 void moe_gate_up_dgrad(const bf16* dgu, const bf16* w_gate_up, const int* counts, const int* offsets, int64_t R,
-                       int64_t G, int64_t E, int64_t H, int64_t F, bf16* dx, cudaStream_t stream);
+                       int64_t G, int64_t E, int64_t H, int64_t F, bf16* dx, cudaStream_t stream, void* const* peer_out = nullptr,
+                       int64_t peer_rows = 0, int peer_slot = 0);
 // out[e] (+)= sum over the `segments` row groups s*E + e of a^T b   (segments = sources in expert parallelism)
 void moe_wgrad(const bf16* a, const bf16* b, const int* counts, const int* offsets, int64_t R, int64_t E, int segments,
                int64_t M, int64_t N, void* out, bool out_fp32, bool accumulate, float alpha, cudaStream_t stream);
@@ -161,10 +163,6 @@ void ep_dispatch(const bf16* x, int64_t T, int k, int H, const int* route_row, c
                  int* const* peer_flags, int epoch, unsigned int* done, cudaStream_t stream);
 void ep_pad(const int* counts, int groups, int slot, int H, bf16* rows, float* w, cudaStream_t stream);
 void ep_signal(int* const* peer_flags, int world, int me, int epoch, cudaStream_t stream);
-void ep_gather(const bf16* const* peer_rows, const int* route_row, const float* top_w, const float* extra,
-               const bf16* resid, int64_t T, int k, int H, int local, int slot, int me, bf16* out,
-               cudaStream_t stream);
-
 // ---- zero_fused.cu (ZeRO reduce-scatter and AdamW + all-gather over peer memory) ----
 int zero_rs_blocks(int64_t per);
 void zero_reduce_scatter(const void* const* peers, int world, int dtype, int64_t start, int64_t per, float* shard,

@@ -163,9 +163,11 @@ class _SlotDispatch(torch.autograd.Function):
         rows = E * slot
         transport = moe.transport()
         fused = getattr(transport, "dispatch", None) is not None
-        if fused:  # permute + exchange in one kernel, straight into the owners' receive buffers
-            rx, rw, rc = transport.dispatch(x, plan.route_row, plan.top_w, plan.kept, k, E, local, slot)
-            x_recv, w_recv, recv_counts = rx.clone(), rw.clone(), rc.clone()  # saved for backward
+        store = None
+        if fused:  # permute + exchange in one kernel, straight into the owners' persistent layer stores
+            store = transport.store_for(id(moe), rows, H, world * local, hold=any(ctx.needs_input_grad[:4]))
+            x_recv, w_recv, recv_counts = transport.dispatch(x, plan.route_row, plan.top_w, plan.kept, k, E, local,
+                                                             slot, store=store)
             row_token = torch.empty(0, device=dev, dtype=torch.int32)
         else:
             send = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
@@ -180,12 +182,13 @@ class _SlotDispatch(torch.autograd.Function):
         gu = None if moe.recompute_activations else torch.empty(rows, F2, device=dev, dtype=torch.bfloat16)
         C.moe_gate_up_fwd(x_recv, w_gate_up, recv_counts, offsets, h, gu)
         out = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
-        if fused:  # expert outputs land in this rank's return buffer; each source pulls and combines its rows
-            y = transport.return_buffer(rows, H)
-            C.moe_down_fwd(h, w_down, recv_counts, offsets, y)
+        if fused:  # the down GEMM stores each expert output row into its source rank's return buffer
+            y_back, peers = transport.return_buffer(rows, H)
+            C.moe_down_fwd_peer(h, w_down, recv_counts, offsets, peers, local * slot, transport.me)
             del h
             transport.publish()
-            transport.gather(plan.route_row, plan.top_w, None, k, local, slot, out)
+            transport.wait_returned()
+            C.moe_combine(y_back, plan.route_row, plan.top_w, None, k, out)
         else:
             y = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
             C.moe_down_fwd(h, w_down, recv_counts, offsets, y)
@@ -198,6 +201,7 @@ class _SlotDispatch(torch.autograd.Function):
             saved.append(gu)
         ctx.save_for_backward(*saved)
         ctx.moe, ctx.slot = moe, slot
+        ctx.store = _StoreHold(transport, store) if store is not None and store.held else None
         ctx.mark_non_differentiable(plan.top_idx, plan.counts, plan.kept, plan.meta, plan.route_row)
         return out, plan.probs, plan.top_idx, plan.counts, plan.kept, plan.meta, plan.route_row
 
@@ -248,16 +252,21 @@ class _SlotDispatch(torch.autograd.Function):
         del hw, dy_recv
         d_w_gate_up = torch.empty_like(w_gate_up)
         C.moe_wgrad(dgu, x_recv, recv_counts, offsets, d_w_gate_up, False, world, 1.0)
-        dx_recv = transport.return_buffer(rows, H) if fused else torch.empty(rows, H, device=dev,
-                                                                                dtype=torch.bfloat16)
-        C.moe_gate_up_dgrad(dgu, w_gate_up, recv_counts, offsets, dx_recv)
-        del dgu
-        if fused:
+        if fused:  # the input-gradient GEMM stores each row into its source rank's return buffer
+            dx_back, peers = transport.return_buffer(rows, H)
+            C.moe_gate_up_dgrad_peer(dgu, w_gate_up, recv_counts, offsets, peers, local * slot, transport.me)
+            del dgu
             transport.publish()
-            dx_send = None
+            partial_back = transport.exchange(partial)
+            transport.wait_returned()
+            if ctx.store is not None:
+                ctx.store.release()
         else:
-            dx_send = transport.exchange(dx_recv)
-        partial_back = transport.exchange(partial)
+            dx_recv = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
+            C.moe_gate_up_dgrad(dgu, w_gate_up, recv_counts, offsets, dx_recv)
+            del dgu
+            dx_back = transport.exchange(dx_recv)
+            partial_back = transport.exchange(partial)
         d_w = torch.empty(T * k, device=dev, dtype=torch.float32)
         C.moe_route_dw(partial_back, route_row, d_w)
         d_logits = torch.empty_like(probs)
@@ -271,12 +280,24 @@ class _SlotDispatch(torch.autograd.Function):
         d_router = torch.empty(moe.num_experts, H, device=dev, dtype=torch.float32)
         C.router_dw(d_logits, x, d_router, False, workspace)
         dx = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
-        if fused:  # pull the input-gradient rows of this rank's routes from the expert ranks
-            transport.gather(route_row, None, dx_router, k, local, slot, dx)
-        else:
-            C.moe_combine_grad(dx_send, route_row, dx_router, k, dx)
-        del local
+        C.moe_combine_grad(dx_back, route_row, dx_router, k, dx)
         return dx, d_router.to(router_weight.dtype), d_w_gate_up, d_w_down, None, None
+
+
+class _StoreHold:
+    """Keeps a layer's persistent receive store marked busy until its backward has read it, or until the autograd
+    graph holding it is freed without a backward (then the store is free for the next forward)."""
+
+    def __init__(self, transport, store) -> None:
+        self.transport, self.store = transport, store
+
+    def release(self) -> None:
+        if self.store is not None:
+            self.transport.release(self.store)
+            self.store = None
+
+    def __del__(self) -> None:
+        self.release()
 
 
 class NcclTransport:

@@ -145,18 +145,43 @@ class _Channel:
         ext().p2p_wait(self.flags[parity * w:(parity + 1) * w], w, self.epoch, self.t.timeout_s)
 
 
-class FusedTransport(P2PTransport):
-    """Expert-parallel exchange fused into the routing kernels (``csrc/ep_fused.cu``).
+class _RowStore:
+    """A persistent symmetric receive buffer that one layer's forward dispatch writes into and its backward reads
+    (the rows, routing weights and counts of every source). It stays mapped in every peer; ``held`` is set while a
+    pending backward still needs its contents."""
 
-    ``dispatch`` stores each routed row (and its weight and the per-expert counts) straight into the owning rank's
-    receive buffer; ``return_buffer`` / ``publish`` / ``gather`` let the expert rank's GEMM write its output into its
-    own symmetric buffer and each source rank pull and reduce its rows with NVLink loads. Plain ``exchange`` (used for
-    small tensors) is the P2P push of ``P2PTransport``."""
+    def __init__(self, transport: "P2PTransport", nbytes: int) -> None:
+        t = transport
+        self.nbytes = nbytes
+        self.buf = t.symm.empty(nbytes, dtype=torch.uint8, device=t.device)
+        self.handle = t.symm.rendezvous(self.buf, t._group_name())
+        self.peers = torch.tensor([int(p) for p in self.handle.buffer_ptrs], dtype=torch.int64, device=t.device)
+        self.held = False
+
+
+class FusedTransport(P2PTransport):
+    """Expert-parallel exchange fused into the routing kernels and the expert GEMMs (``csrc/ep_fused.cu``,
+    ``csrc/gemm_tcgen05.cuh`` peer-store epilogue).
+
+    * ``dispatch`` (the permute): each routed row, its routing weight and this rank's per-expert counts are stored
+      straight into the owning rank's receive buffer. In the forward pass that buffer is the layer's own persistent
+      :class:`_RowStore`, so the rows the backward needs are never copied; the backward's gradient rows use the
+      two-parity send channel.
+    * combine: the expert rank's down-projection GEMM (forward) or input-gradient GEMM (backward) stores each output
+      row over NVLink into the SOURCE rank's return buffer, at the row the source's own routing plan names
+      (``route_row``); ``publish`` releases a flag to every peer, ``wait_returned`` waits for all expert ranks, and
+      the source reduces its top-k rows locally in a fixed order. Only routed rows cross NVLink.
+
+    Store reuse is safe without extra synchronisation: a rank finishes a layer's forward only after every expert
+    rank pushed that layer's outputs, which each does after its GEMMs finished reading the layer's store; a backward
+    reads the store before it pushes the layer's input gradients, which every source waits for.
+    """
 
     def __init__(self, group, device: torch.device, capacity_bytes: int = 1 << 20) -> None:
         super().__init__(group, device, capacity_bytes)
         self.send = _Channel(self)
         self.back = _Channel(self)
+        self._stores: dict = {}
         dist.barrier(group=self.group, device_ids=[device.index] if device.type == "cuda" else None)
 
     @classmethod
@@ -172,11 +197,28 @@ class FusedTransport(P2PTransport):
         c_off = (w_off + rows * 4 + 255) // 256 * 256
         return w_off, c_off, c_off + groups * 4
 
+    def store_for(self, key, rows: int, H: int, groups: int, hold: bool) -> _RowStore:
+        """The first free persistent store of layer ``key`` that fits (a new one, collectively, if none does);
+        ``hold`` marks it busy until :meth:`release`. Every rank takes the same path, so allocations match."""
+        need = self._layout(rows, H, groups)[2]
+        pool = self._stores.setdefault(key, [])
+        store = next((s for s in pool if not s.held and s.nbytes >= need), None)
+        if store is None:
+            torch.cuda.synchronize(self.device)
+            store = _RowStore(self, (need + (1 << 20) - 1) // (1 << 20) * (1 << 20))
+            pool.append(store)
+        store.held = hold
+        return store
+
+    @staticmethod
+    def release(store: _RowStore) -> None:
+        store.held = False
+
     def dispatch(self, x: Tensor, route_row: Tensor, top_w, kept, k: int, E: int, local: int, slot: int,
-                 pad_counts: Tensor | None = None):
-        """Rows (and, when given, weights and counts) of this rank's routes into the owners' receive buffers.
-        Returns views of this rank's receive buffer: rows [world*local*slot, H] bf16, weights [rows] fp32, counts
-        [world*local] int32 (valid until the next dispatch of the other parity)."""
+                 pad_counts: Tensor | None = None, store: _RowStore | None = None):
+        """Rows (and, when given, weights and counts) of this rank's routes into the owners' receive buffers: the
+        layer ``store`` when given, else the send channel's current parity. Returns views of this rank's receive
+        buffer: rows [world*local*slot, H] bf16, weights [rows] fp32, counts [world*local] int32."""
         from ..ops import ext
 
         C = ext()
@@ -185,9 +227,12 @@ class FusedTransport(P2PTransport):
         rows = groups * slot
         w_off, c_off, total = self._layout(rows, H, groups)
         ch = self.send
-        ch.grow(total)
         parity = ch.next()
-        buf, _, peers = ch.bufs[parity]
+        if store is None:
+            ch.grow(total)
+            buf, _, peers = ch.bufs[parity]
+        else:
+            buf, peers = store.buf, store.peers
         C.ep_dispatch(x.contiguous(), route_row, top_w, kept, k, E, local, slot, self.me, peers, w_off, c_off,
                       ch.peer_flags[parity], ch.epoch, ch.done)
         ch.wait(parity)
@@ -198,23 +243,22 @@ class FusedTransport(P2PTransport):
         C.ep_pad(counts_for_pad, slot, rows_t, w_t if top_w is not None else None)
         return rows_t, w_t, counts
 
-    def return_buffer(self, rows: int, H: int) -> Tensor:
+    def return_buffer(self, rows: int, H: int) -> tuple[Tensor, Tensor]:
+        """(this rank's return buffer [rows, H] bf16 for the next combine, every rank's buffer address): the expert
+        GEMM's peer-store epilogue writes into the addresses, this rank reduces from its own buffer."""
         ch = self.back
         ch.grow(rows * H * 2)
         self._back_parity = ch.next()
-        buf = ch.bufs[self._back_parity][0]
-        return buf[: rows * H * 2].view(torch.bfloat16).view(rows, H)
+        buf, _, peers = ch.bufs[self._back_parity]
+        return buf[: rows * H * 2].view(torch.bfloat16).view(rows, H), peers
 
     def publish(self) -> None:
+        """Release this rank's pushed rows to every peer (after the pushing GEMM, in stream order)."""
         from ..ops import ext
 
         ch = self.back
         ext().ep_signal(ch.peer_flags[self._back_parity], self.me, ch.epoch)
 
-    def gather(self, route_row: Tensor, top_w, extra, k: int, local: int, slot: int, out: Tensor) -> Tensor:
-        from ..ops import ext
-
-        ch = self.back
-        ch.wait(self._back_parity)
-        ext().ep_gather(ch.bufs[self._back_parity][2], route_row, top_w, extra, None, k, local, slot, self.me, out)
-        return out
+    def wait_returned(self) -> None:
+        """Wait (bounded) until every expert rank has published its rows into this rank's return buffer."""
+        self.back.wait(self._back_parity)

@@ -1,4 +1,5 @@
-"""Expert parallelism on 2+ B200s (NCCL): the native slot-dispatch MoE against the single-GPU native model."""
+"""Expert parallelism on 2+ B200s: the native slot-dispatch MoE against the single-GPU native model, and the fused
+NVLink exchange (peer-store dispatch, GEMM-epilogue combine push) against the NCCL all-to-all exchange."""
 
 import os
 import socket
@@ -83,23 +84,44 @@ def _case(rank, world, transport):
         rel = float((grad - r).norm() / (r.norm() + 1e-12))
         assert rel < (0.1 if grad.dim() >= 2 else 0.3), (name, rel)
     assert ext().read_status(True) == 0
-    return float(out["loss"])
+    digest = [float(got[n].double().pow(2).sum()) for n in sorted(got)]
+    return float(out["loss"]), norm, digest
 
 
-@pytest.mark.parametrize("transport", ["nccl", "p2p", "fused"])
-def test_expert_parallel_native_matches_single_gpu(transport):
-    world = 2
+def _run(world, transport):
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, transport, queue)) for r in range(world)]
     for p in procs:
         p.start()
+    results = {}
     for _ in range(world):
         rank, status, payload = queue.get(timeout=600)
         if status != "ok":
             for p in procs:
                 p.join(timeout=30)
             raise AssertionError(f"rank {rank} failed:\n{payload}")
+        results[rank] = payload
     for p in procs:
         p.join(timeout=60)
+    return results
+
+
+@pytest.mark.parametrize("transport", ["nccl", "p2p", "fused"])
+def test_expert_parallel_native_matches_single_gpu(transport):
+    _run(2, transport)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_fused_exchange_matches_nccl_exchange(world):
+    """The fused transport moves the same rows through the same kernels as the NCCL all-to-all, so every rank's
+    loss, clip norm and gradients agree to rounding (they are normally bit-identical)."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} B200s")
+    nccl, fused = _run(world, "nccl"), _run(world, "fused")
+    for rank in range(world):
+        (l0, n0, d0), (l1, n1, d1) = nccl[rank], fused[rank]
+        assert abs(l0 - l1) <= 1e-6 * abs(l0) and abs(n0 - n1) <= 1e-6 * n0, (rank, l0, l1, n0, n1)
+        for a, b in zip(d0, d1):
+            assert abs(a - b) <= 1e-5 * (abs(a) + 1e-12), (rank, a, b)
