@@ -45,10 +45,14 @@ def parse():
     p.add_argument("--seqs-per-gpu", type=int, default=32)
     p.add_argument("--seq-len", type=int, default=2048)
     p.add_argument("--layers", type=int, default=CONFIG2["layers"], help="debug override (the metric needs 16)")
-    p.add_argument("--recompute", choices=("auto", "on", "off"), default="auto")
+    p.add_argument("--recompute", choices=("auto", "on", "off"), default="on",
+                   help="recompute the expert gate/up activations in backward (on at every N by default, so the "
+                        "scaling curve compares steps doing the same work; auto: only with more than 16 local "
+                        "experts)")
     p.add_argument("--transport", choices=("auto", "fused", "p2p", "nccl"), default=os.environ.get("QW_EP_TRANSPORT", "auto"),
-                   help="expert-parallel exchange: fused (permute/combine kernels with NVLink peer stores and "
-                        "loads), p2p (peer-store exchange), nccl (all_to_all), auto (fused at 2 ranks, else nccl)")
+                   help="expert-parallel exchange: fused (dispatch kernel and expert-GEMM epilogue store rows "
+                        "into peers over NVLink), p2p (peer-store exchange of padded buffers), nccl (all_to_all), "
+                        "auto (fused on CUDA)")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-launch-count", action="store_true",
                    help="skip the profiler-based launch count (for runs under an external profiler)")

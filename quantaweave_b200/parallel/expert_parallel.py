@@ -89,7 +89,7 @@ def init_expert_parallel(device_arg: str = "auto", tensor_parallel: int = 1,
         group = dist.new_group(list(range(world)))
         transport = transport or os.environ.get("QW_EP_TRANSPORT", "auto")
         if transport == "auto":
-            transport = "fused" if (device.type == "cuda" and world == 2) else "nccl"
+            transport = "fused" if device.type == "cuda" else "nccl"
         return ExpertParallelContext(rank, world, device, group, owns, rank, world, group, rank, world, transport,
                                      sequence_parallel=True)
     if tensor_parallel < 1 or world % tensor_parallel:
@@ -105,8 +105,8 @@ def init_expert_parallel(device_arg: str = "auto", tensor_parallel: int = 1,
             g = dist.new_group([row * tensor_parallel + column for column in range(tensor_parallel)])
             tp_group = g if row == ep_rank else tp_group
     transport = transport or os.environ.get("QW_EP_TRANSPORT", "auto")
-    if transport == "auto":  # measured on B200 (moe-1b-e64): fused is faster at 2 ranks, NCCL at 8; 4 uses NCCL
-        transport = "fused" if (device.type == "cuda" and ep_size == 2) else "nccl"
+    if transport == "auto":  # measured on 8 B200s (moe-1b-e64): the fused exchange beats the NCCL all-to-all
+        transport = "fused" if device.type == "cuda" else "nccl"
     return ExpertParallelContext(ep_rank, ep_size, device, ep_group, owns, tp_rank, tensor_parallel, tp_group, rank,
                                  world, transport)
 
