@@ -2,6 +2,7 @@
 
     python bench_attention.py --batch 8 --seq 2048 --heads 16 --head-dim 64
     QW_ATTN_BWD=mma python bench_attention.py ...      # the mma.sync backward instead of the tcgen05 one
+    QW_ATTN_FWD=mma python bench_attention.py ...      # the mma.sync forward instead of the tcgen05 one
 
 Prints one JSON line: median forward / backward milliseconds over ``--iters`` runs (CUDA events on the launching
 stream, after warm-up) and the corresponding TFLOP/s (causal forward = 2 GEMMs over half the S x S scores; backward
@@ -54,7 +55,8 @@ def main() -> None:
     bwd.sort()
     f_ms, b_ms = fwd[len(fwd) // 2], bwd[len(bwd) // 2]
     flops = 4.0 * B * h * S * S * d / 2
-    print(json.dumps({"backward_path": os.environ.get("QW_ATTN_BWD", "tcgen05"), "batch": B, "seq": S, "heads": h,
+    print(json.dumps({"forward_path": os.environ.get("QW_ATTN_FWD", "tcgen05" if d == 64 else "mma"),
+                      "backward_path": os.environ.get("QW_ATTN_BWD", "tcgen05"), "batch": B, "seq": S, "heads": h,
                       "kv_heads": hkv, "head_dim": d, "fwd_ms": round(f_ms, 4), "bwd_ms": round(b_ms, 4),
                       "fwd_tflops": round(flops / f_ms / 1e9, 1), "bwd_tflops": round(2.5 * flops / b_ms / 1e9, 1)}))
     if ext().read_status(True) != 0:

@@ -155,6 +155,8 @@ def _pp_zero(args, rank, world, device):
     opt = ShardedAdamW(model, pp, lr=3e-4, betas=(0.9, 0.95), weight_decay=0.1) if pp.dp_size > 1 else \
         _optimizer(model, device)
     engine = PipelineEngine(model, pp, micro, contextlib.nullcontext, schedule="gpipe")
+    if hasattr(opt, "arm_overlap"):  # the sharded AdamW reduce-scatters bucket by bucket during the last backward
+        engine.before_last_backward = opt.arm_overlap
     gen = torch.Generator().manual_seed(args.seed * 1000 + pp.dp_rank)  # each replica its own sequences
     batches = [torch.randint(0, cfg.vocab_size, (micro * per_micro, seq + 1), generator=gen).to(device)
                for _ in range(args.warmup + args.steps)]

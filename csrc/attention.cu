@@ -498,6 +498,15 @@ void set_smem(K kernel, size_t bytes) {
 void flash_attn_fwd(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv, bf16* o,
                     int64_t ldo, float* lse, int B, int S, int Hq, int Hkv, int D, float scale, cudaStream_t stream) {
   if (B == 0 || S == 0) return;
+  // head_dim 64 runs on the tcgen05 kernel (attention_fwd_tc.cu); QW_ATTN_FWD=mma keeps the mma.sync kernel below
+  static const bool use_mma = [] {
+    const char* e = std::getenv("QW_ATTN_FWD");
+    return e && std::string(e) == "mma";
+  }();
+  if (D == 64 && !use_mma) {
+    flash_attn_fwd_tc(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hkv, D, scale, stream);
+    return;
+  }
   dim3 grid((S + 127) / 128, B * Hq);
   if (D == 32) {
     const size_t smem = (128 + 4 * 64) * 32 * sizeof(bf16);

@@ -1,0 +1,409 @@
+// Causal flash-attention forward on the Blackwell tensor cores (head_dim 64): tcgen05.mma with TMEM accumulators,
+// Q/K/V staged by TMA into 128-byte-swizzled shared memory, grouped-query attention read in place from the packed
+// QKV rows.
+//
+// One CTA owns 256 queries of one (batch, q-head) as two 128-row Q tiles, and walks the 128-key K/V tiles up to the
+// diagonal. Each Q tile has its own softmax warpgroup, so while one group turns its scores into probabilities the
+// tensor core works on the other group's tiles (ping-pong):
+//
+//   S_g  = Q_g K_j^T                       (TMEM, 128 x 128 fp32 per group)
+//   P_g  = exp2(S_g * scale*log2e - m_g)   (softmax warps -> bf16, K-major swizzled shared memory)
+//   O_g += P_g V_j                          (TMEM, 128 x 64 fp32 per group, accumulated by the tensor core)
+//
+// Lazy rescaling: m_g is the row maximum the accumulator O_g is expressed against. A new tile only moves it when its
+// own maximum exceeds m_g by more than 2^8 (so probabilities stay below 256, well inside bf16 and fp32 range);
+// then the warp reads O_g out of TMEM, scales it by 2^(m_old - m_new) and writes it back before the next P V
+// accumulates. After the first few tiles of a row this almost never happens, so the softmax touches each score once
+// (one TMEM read of the row) and never waits for the previous P V except to reuse the P buffer. At the end
+// O_g / l is stored in bf16 and lse = ln(sum exp(scale * s)) in fp32 (the backward's input).
+//
+// Roles (320 threads, one CTA per SM — the shared-memory request guarantees it, so the 512 TMEM columns never
+// contend):
+//   warp 0      TMA: both Q tiles once, then K_j | V_j through a ring of 3 stages.
+//   warp 1      MMA issuer (one thread), polling: per group, S_g(j+1) as soon as tile j+1 has landed and the group
+//               has read S_g(j) out of TMEM (so the next scores are computed while the group exponentiates), and
+//               O_g += P_g(j) V_j once P_g(j) is written; a K/V stage is released when both groups' MMAs for that
+//               tile are issued.
+//   warps 2-5   softmax group 0 (Q tile 0), warps 6-9 group 1 (Q tile 1). Warp w reads TMEM lanes 32*(w%4)..+31.
+//
+// TMEM columns: [0,128) S_0, [128,256) S_1, [256,320) O_0, [320,384) O_1.
+// Every mbarrier wait is bounded (common.cuh): on a timeout all roles stop, in-flight TMA loads and MMAs are waited
+// for (bounded), TMEM is freed and the status word records the cause.
+#include <algorithm>
+#include <stdexcept>
+
+#include "common.cuh"
+#include "launchers.h"
+
+namespace qw {
+
+CUtensorMap make_bf16_map_3d(const void* ptr, int64_t inner, int64_t rows, int64_t batches, int64_t ld,
+                             int64_t batch_stride, int box_rows);
+
+namespace attn_fwd_tc {
+
+constexpr int kTile = 128;                    // queries per Q tile and keys per K/V tile
+constexpr int kGroups = 2;                    // Q tiles per CTA, one softmax warpgroup each
+constexpr int kThreads = 64 + 128 * kGroups;  // TMA warp, MMA warp, softmax warpgroups
+constexpr int kStages = 3;
+constexpr int kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleLog2 = 8.f;  // move the reference maximum only when a row grows by more than 2^8
+
+template <int D>
+struct Layout {
+  static constexpr int kBoxes = D / 64;                      // 64-wide (128-byte) boxes per row
+  static constexpr int kTileBytes = kBoxes * kTile * 128;    // one [128 x D] bf16 tile
+  static constexpr int kPBytes = 2 * kTile * 128;            // one [128 x 128] bf16 P tile: two 64-key boxes
+  static constexpr int kQ = 0;
+  static constexpr int kKV = kGroups * kTileBytes;           // stages of [K | V]
+  static constexpr int kP = kKV + kStages * 2 * kTileBytes;
+  static constexpr int kBar = kP + kGroups * kPBytes;
+  static constexpr int kTotal = kBar + 256 + 1024;           // barriers, and slack to align the base to 1 KB
+  static constexpr int kTmemO = 2 * kTile;                   // first column of the partial outputs
+};
+
+struct Params {
+  bf16* o;
+  int64_t ldo;
+  float* lse;  // [B, Hq, S]
+  int S, Hq, Hkv;
+  float scale_log2;  // softmax scale * log2(e)
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ int kv_tiles_of(const Params& p, int q_start) {
+  if (q_start >= p.S) return 0;
+  return min((p.S + kTile - 1) / kTile, q_start / kTile + 1);
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                       const __grid_constant__ CUtensorMap map_v, Params p) {
+  using L = Layout<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* kv_full = q_full + 1;           // [kStages]
+  uint64_t* kv_empty = kv_full + kStages;   // [kStages]
+  uint64_t* s_full = kv_empty + kStages;    // [kGroups] S_g of the group's next tile is in TMEM
+  uint64_t* s_free = s_full + kGroups;      // [kGroups] the group has read S_g out of TMEM
+  uint64_t* p_full = s_free + kGroups;      // [kGroups] P_g written (and O_g rescaled if it had to be)
+  uint64_t* o_full = p_full + kGroups;      // [kGroups] O_g += P_g V_j has completed
+  uint64_t* teardown = o_full + kGroups;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(teardown + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int b = blockIdx.x / p.Hq, hq = blockIdx.x % p.Hq;
+  const int hk = hq / (p.Hq / p.Hkv);
+  const int q0 = (gridDim.y - 1 - blockIdx.y) * (kTile * kGroups);  // the latest queries see the most keys: first
+  const int n0 = kv_tiles_of(p, q0), n1 = kv_tiles_of(p, q0 + kTile);
+  const int nk = max(n0, n1);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int g = 0; g < kGroups; ++g) {
+      mbar_init(&s_full[g], 1);
+      mbar_init(&s_free[g], 4);  // one arrival per warp of the group
+      mbar_init(&p_full[g], 4);
+      mbar_init(&o_full[g], 1);
+    }
+    mbar_init(teardown, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_k);
+    tma_prefetch_desc(&map_v);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      // phase of the last load issued into each stage (-1: none), packed 2 bits per stage to stay in a register
+      uint32_t issued = 0;  // bit 2s: stage s used, bit 2s+1: its phase
+      mbar_arrive_expect_tx(q_full, kGroups * L::kTileBytes);
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+        for (int c = 0; c < L::kBoxes; ++c)
+          tma_load_3d(smem + L::kQ + g * L::kTileBytes + c * kTile * 128, &map_q, q_full, hq * D + c * 64,
+                      q0 + g * kTile, b);
+      for (int j = 0; j < nk; ++j) {
+        const int st = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        if (!mbar_sleep_wait(&kv_empty[st], ph ^ 1, kTimeoutEmpty) || *abort_flag) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&kv_full[st], 2 * L::kTileBytes);
+        issued = (issued & ~(3u << (2 * st))) | ((1u | (ph << 1)) << (2 * st));
+        uint8_t* sk = smem + L::kKV + st * 2 * L::kTileBytes;
+#pragma unroll
+        for (int c = 0; c < L::kBoxes; ++c) {
+          tma_load_3d(sk + c * kTile * 128, &map_k, &kv_full[st], hk * D + c * 64, j * kTile, b);
+          tma_load_3d(sk + L::kTileBytes + c * kTile * 128, &map_v, &kv_full[st], hk * D + c * 64, j * kTile, b);
+        }
+      }
+      // drain: every load issued above has landed before the CTA may exit
+      mbar_sleep_wait(q_full, 0, kTimeoutFull);
+      for (int s = 0; s < kStages; ++s)
+        if ((issued >> (2 * s)) & 1u) mbar_sleep_wait(&kv_full[s], (issued >> (2 * s + 1)) & 1u, kTimeoutFull);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16(kTile, kTile, false, false);
+      constexpr uint32_t id_o = idesc_bf16(kTile, D, false, true);
+      int ns0 = 0, ns1 = 0;  // next S to issue, per group
+      int no0 = 0, no1 = 0;  // next O' to issue, per group
+      int released = 0;      // K/V tiles whose stage went back to the producer
+      auto issue_s = [&](int g, int j) {
+        const int st = j % kStages;
+        tc_fence_after();
+        const uint32_t sq = smem_u32(smem + L::kQ + g * L::kTileBytes);
+        const uint32_t sk = smem_u32(smem + L::kKV + st * 2 * L::kTileBytes);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const uint32_t off = (k / 4) * (kTile * 128) + (k % 4) * 32;
+          umma_bf16(tmem + g * kTile, smem_desc_sw128(sq + off, 16, 1024), smem_desc_sw128(sk + off, 16, 1024),
+                    id_s, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[g]);
+      };
+      auto issue_o = [&](int g, int j) {
+        const int st = j % kStages;
+        tc_fence_after();
+        const uint32_t sp = smem_u32(smem + L::kP + g * L::kPBytes);
+        const uint32_t sv = smem_u32(smem + L::kKV + st * 2 * L::kTileBytes + L::kTileBytes);
+#pragma unroll
+        for (int k = 0; k < kTile / 16; ++k) {
+          // A = P (K-major, keys in two 64-wide boxes); B = V read MN-major: 16 keys = 16 rows of 128 B per step,
+          // 64-wide head-dim blocks one box apart
+          const uint64_t a = smem_desc_sw128(sp + (k / 4) * (kTile * 128) + (k % 4) * 32, 16, 1024);
+          const uint64_t bv = smem_desc_sw128(sv + k * 2048, kTile * 128, 1024);
+          umma_bf16(tmem + L::kTmemO + g * D, a, bv, id_o, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&o_full[g]);
+      };
+      bool ok = mbar_sleep_wait(q_full, 0, kTimeoutFull);
+      tc_fence_after();
+      int idle = 0;
+      uint64_t idle_start = 0;
+      // one group's step: O_g += P_g(j) V_j once the group has written P_g(j); S_g(j) once tile j has landed and
+      // the group has read S_g(j-1) out of the TMEM columns this MMA overwrites
+      auto step = [&](int g, int n, int& ns, int& no) -> bool {
+        bool moved = false;
+        if (no < ns && mbar_test(&p_full[g], no & 1)) {
+          issue_o(g, no++);
+          moved = true;
+        }
+        if (ns < n && (ns == 0 || mbar_test(&s_free[g], (ns - 1) & 1)) &&
+            mbar_test(&kv_full[ns % kStages], (ns / kStages) & 1)) {
+          issue_s(g, ns++);
+          moved = true;
+        }
+        return moved;
+      };
+      while (ok && (no0 < n0 || no1 < n1)) {
+        bool progress = step(0, n0, ns0, no0);
+        progress = step(1, n1, ns1, no1) || progress;
+        while (released < nk && (released >= n0 || no0 > released) && (released >= n1 || no1 > released)) {
+          umma_commit(&kv_empty[released % kStages]);  // fires when the MMAs reading that stage are done
+          ++released;
+          progress = true;
+        }
+        if (progress) {
+          idle = 0;
+          continue;
+        }
+        __nanosleep(32);
+        if ((++idle & 255) == 0) {  // bounded: give up after the wait budget without progress
+          if (*abort_flag) { ok = false; break; }
+          const uint64_t now = globaltimer();
+          if (idle == 256) idle_start = now;
+          else if (now - idle_start > QW_WAIT_TIMEOUT_NS) { set_status(kTimeoutAccum); ok = false; break; }
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(teardown);  // fires once every MMA issued above has completed
+      mbar_sleep_wait(teardown, 0, kTimeoutAccum);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warpgroups (warps 2..9)
+    const int g = (warp - 2) / 4;
+    const int quarter = warp % 4;
+    const int row = quarter * 32 + lane;
+    const int q_start = q0 + g * kTile;
+    const int q = q_start + row;
+    const int n = g == 0 ? n0 : n1;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t ts = tmem + lane_off + g * kTile;
+    const uint32_t to = tmem + lane_off + L::kTmemO + g * D;
+    uint8_t* prow = smem + L::kP + g * L::kPBytes + row * 128;
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY;  // the maximum O_g is expressed against (base-2, scaled)
+    float l_sum = 0.f;        // row sum of the probabilities, relative to m_ref
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_sleep_wait(&s_full[g], j & 1, kTimeoutAccum))) { ok = false; break; }
+      tc_fence_after();
+      float v[kTile];
+      tmem_ld32_pair(ts, ts + 32, v, v + 32);
+      tmem_ld32_pair(ts + 64, ts + 96, v + 64, v + 96);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[g]);  // the issuer may compute the next scores into these columns
+      const int k0 = j * kTile;
+      // the diagonal tile and a tile past the end of the sequence need masking
+      const bool masked = (k0 + kTile > q_start) || (k0 + kTile > p.S);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kTile; ++i) {
+        const int key = k0 + i;
+        v[i] *= sl2;
+        if (masked && (key > q || key >= p.S)) v[i] = -INFINITY;
+        mx = fmaxf(mx, v[i]);
+      }
+      // O_g += P_g(j-1) V_{j-1} must have finished before its P buffer is rewritten or O_g is rescaled
+      if (j > 0 && !__all_sync(0xffffffffu, mbar_sleep_wait(&o_full[g], (j - 1) & 1, kTimeoutAccum))) {
+        ok = false;
+        break;
+      }
+      // the reference maximum moves only when some row of the warp grew by more than 2^8 (warp-uniform decision:
+      // TMEM access is warp-collective); rows whose maximum barely moved then get a factor close to 1
+      float factor = 1.f;
+      bool rescale = false;
+      if (j == 0) {
+        m_ref = mx;  // key 0 is visible to every row, so the first tile's maximum is finite
+      } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleLog2)) {
+        const float m_new = fmaxf(m_ref, mx);
+        factor = ex2(m_ref - m_new);
+        m_ref = m_new;
+        rescale = true;
+      }
+      float tile_sum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < kTile / 8; ++c8) {  // 8 keys -> one 16-byte chunk of P
+        uint32_t w[4];
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const float a = ex2(v[8 * c8 + 2 * e2] - m_ref);  // exp2(-inf) = 0 for masked keys
+          const float b2 = ex2(v[8 * c8 + 2 * e2 + 1] - m_ref);
+          tile_sum += a + b2;
+          w[e2] = pack_bf16(a, b2);
+        }
+        const int box = c8 / 8;
+        const int swz = (c8 % 8) ^ (row & 7);
+        *reinterpret_cast<uint4*>(prow + box * (kTile * 128) + swz * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l_sum = fmaf(l_sum, factor, tile_sum);
+      if (rescale) {  // O_g to the new reference before the next P V accumulates into it
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          float o[32];
+          tmem_ld32(to + c, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= factor;
+          tmem_st32(to + c, o);
+        }
+        tmem_st_wait();
+      }
+      tc_fence_before();
+      fence_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[g]);
+    }
+    if (ok && n > 0 && !__all_sync(0xffffffffu, mbar_sleep_wait(&o_full[g], (n - 1) & 1, kTimeoutAccum))) ok = false;
+    if (!ok) {
+      *abort_flag = 1;
+    } else if (n > 0) {
+      tc_fence_after();
+      const float inv = 1.f / l_sum;
+      bf16* out = p.o + (static_cast<int64_t>(b) * p.S + q) * p.ldo + hq * D;
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        float o[32];
+        tmem_ld32(to + c, o);  // warp-collective: every lane loads, only rows inside the sequence store
+        if (q < p.S) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack_bf16(o[i] * inv, o[i + 1] * inv);
+            w.y = pack_bf16(o[i + 2] * inv, o[i + 3] * inv);
+            w.z = pack_bf16(o[i + 4] * inv, o[i + 5] * inv);
+            w.w = pack_bf16(o[i + 6] * inv, o[i + 7] * inv);
+            *reinterpret_cast<uint4*>(out + c + i) = w;
+          }
+        }
+      }
+      if (q < p.S) p.lse[(static_cast<int64_t>(b) * p.Hq + hq) * p.S + q] = (m_ref + __log2f(l_sum)) * kLn2;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+template <int D>
+void run(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv, bf16* o, int64_t ldo,
+         float* lse, int B, int S, int Hq, int Hkv, float scale, cudaStream_t stream) {
+  auto kernel = attn_fwd_tc_kernel<D>;
+  static bool configured = false;
+  if (!configured) {
+    check_cuda(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<D>::kTotal),
+               "attention forward tc smem");
+    configured = true;
+  }
+  Params p{};
+  p.o = o;
+  p.ldo = ldo;
+  p.lse = lse;
+  p.S = S;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale_log2 = scale * kLog2e;
+  auto mq = make_bf16_map_3d(q, static_cast<int64_t>(Hq) * D, S, B, ldq, S * ldq, kTile);
+  auto mk = make_bf16_map_3d(k, static_cast<int64_t>(Hkv) * D, S, B, ldk, S * ldk, kTile);
+  auto mv = make_bf16_map_3d(v, static_cast<int64_t>(Hkv) * D, S, B, ldv, S * ldv, kTile);
+  dim3 grid(B * Hq, (S + kTile * kGroups - 1) / (kTile * kGroups));
+  kernel<<<grid, kThreads, Layout<D>::kTotal, stream>>>(mq, mk, mv, p);
+  check_cuda(cudaGetLastError(), "attention forward tc launch");
+}
+
+}  // namespace attn_fwd_tc
+
+void flash_attn_fwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv, bf16* o,
+                       int64_t ldo, float* lse, int B, int S, int Hq, int Hkv, int D, float scale,
+                       cudaStream_t stream) {
+  if (B == 0 || S == 0) return;
+  if (D != 64) throw std::runtime_error("flash_attn_fwd_tc: head_dim must be 64");
+  if (Hq % Hkv) throw std::runtime_error("flash_attn_fwd_tc: query heads must be a multiple of kv heads");
+  attn_fwd_tc::run<64>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hkv, scale, stream);
+}
+
+int attention_fwd_tc_status(bool clear) { return read_status_word(clear); }
+
+}  // namespace qw

@@ -87,65 +87,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Bounded wait that parks the thread: try_wait with a suspend-time hint sleeps until the phase completes (or the
-// hint elapses), so waiting warps take no issue slots from the softmax warps sharing their SM sub-partition.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return done != 0;
-}
-
-__device__ __forceinline__ bool mbar_sleep_wait(uint64_t* bar, uint32_t parity, int code) {
-  if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
-  const uint64_t start = globaltimer();
-  while (!mbar_try_wait_hint(bar, parity, 1000000u)) {
-    if (globaltimer() - start > QW_WAIT_TIMEOUT_NS) {
-      set_status(code);
-      return false;
-    }
-  }
-  return true;
-}
-
-// Non-blocking probe of an mbarrier phase (the MMA issuer polls two kinds of barriers and must not park on either).
-__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Two 32-column TMEM loads (32 lanes x 32 bit each) issued back to back with one wait, in one asm block so no use of
-// the results can be scheduled before the wait.
-__device__ __forceinline__ void tmem_ld32_pair(uint32_t taddr_a, uint32_t taddr_b, float* fa, float* fb) {
-  uint32_t a[32], b[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3]), "=r"(a[4]), "=r"(a[5]), "=r"(a[6]), "=r"(a[7]), "=r"(a[8]), "=r"(a[9]), "=r"(a[10]), "=r"(a[11]), "=r"(a[12]), "=r"(a[13]), "=r"(a[14]), "=r"(a[15]), "=r"(a[16]), "=r"(a[17]), "=r"(a[18]), "=r"(a[19]), "=r"(a[20]), "=r"(a[21]), "=r"(a[22]), "=r"(a[23]), "=r"(a[24]), "=r"(a[25]), "=r"(a[26]), "=r"(a[27]), "=r"(a[28]), "=r"(a[29]), "=r"(a[30]), "=r"(a[31]), "=r"(b[0]), "=r"(b[1]), "=r"(b[2]), "=r"(b[3]), "=r"(b[4]), "=r"(b[5]), "=r"(b[6]), "=r"(b[7]), "=r"(b[8]), "=r"(b[9]), "=r"(b[10]), "=r"(b[11]), "=r"(b[12]), "=r"(b[13]), "=r"(b[14]), "=r"(b[15]), "=r"(b[16]), "=r"(b[17]), "=r"(b[18]), "=r"(b[19]), "=r"(b[20]), "=r"(b[21]), "=r"(b[22]), "=r"(b[23]), "=r"(b[24]), "=r"(b[25]), "=r"(b[26]), "=r"(b[27]), "=r"(b[28]), "=r"(b[29]), "=r"(b[30]), "=r"(b[31])
-      : "r"(taddr_a), "r"(taddr_b)
-      : "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    fa[i] = __uint_as_float(a[i]);
-    fb[i] = __uint_as_float(b[i]);
-  }
-}
-
 __device__ __forceinline__ void store_row16(bf16* dst, const float* v, float mul) {
 #pragma unroll
   for (int i = 0; i < 16; i += 8) {

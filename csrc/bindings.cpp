@@ -69,6 +69,15 @@ void linear_dgrad_peer(Tensor dy, Tensor w, Tensor peer_ptrs, int64_t peer_rows,
                         static_cast<int>(slot), stream());
 }
 
+void tp_reduce_rows(Tensor staging, int64_t world, int64_t rows_per_rank, int64_t N, OptT bias, Tensor out) {
+  CHECK_CUDA(staging); CHECK_DTYPE(staging, torch::kBFloat16); CHECK_DTYPE(out, torch::kBFloat16); CHECK_CONTIG(out);
+  TORCH_CHECK(out.numel() == rows_per_rank * N, "tp_reduce_rows: output size");
+  if (bias) { CHECK_DTYPE(*bias, torch::kFloat32); TORCH_CHECK(bias->numel() == N); }
+  c10::cuda::CUDAGuard g(staging.device());
+  qw::tp_reduce_rows(bptr(staging), static_cast<int>(world), rows_per_rank, static_cast<int>(N), optptr<float>(bias),
+                     bptr_mut(out), stream());
+}
+
 void tp_reduce_bcast(Tensor staging, int64_t world, int64_t rows_per_rank, int64_t N, OptT bias, Tensor out_ptrs,
                      int64_t me) {
   CHECK_CUDA(staging); CHECK_DTYPE(staging, torch::kBFloat16); CHECK_DTYPE(out_ptrs, torch::kInt64);
@@ -453,6 +462,16 @@ void flash_attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor dout, Tensor 
 
 // ------------------------------------------------------------------------------------------------ p2p
 // peer_bufs / peer_flags: int64 device tensors of raw peer addresses (from the symmetric-memory rendezvous)
+void p2p_broadcast(Tensor src, Tensor peer_bufs, Tensor peer_flags, int64_t me, int64_t epoch, Tensor done) {
+  CHECK_CUDA(src); CHECK_CONTIG(src);
+  c10::cuda::CUDAGuard g(src.device());
+  qw::p2p_broadcast(src.data_ptr(), src.numel() * src.element_size(),
+                    reinterpret_cast<void* const*>(peer_bufs.data_ptr<int64_t>()),
+                    reinterpret_cast<int* const*>(peer_flags.data_ptr<int64_t>()), static_cast<int>(peer_bufs.numel()),
+                    static_cast<int>(me), static_cast<int>(epoch), reinterpret_cast<unsigned int*>(done.data_ptr<int>()),
+                    stream());
+}
+
 void p2p_push(Tensor src, int64_t block_bytes, Tensor peer_bufs, Tensor peer_flags, int64_t me, int64_t epoch,
               Tensor done) {
   CHECK_CUDA(src); CHECK_CONTIG(src);
@@ -587,6 +606,61 @@ void decode_combine_norm(OptT x, OptT tokens, OptT tok_emb, OptT pos_emb, OptT p
                           bptr_mut(n_out), stream());
 }
 
+// expert-parallel decode: routing over every expert, active list restricted to this rank's [first, first + local)
+void decode_route_local(Tensor x, Tensor wr, OptT ebias, int64_t k, double temperature, Tensor logits, Tensor cnt,
+                        Tensor off, Tensor order, Tensor route_slot, Tensor top_w, Tensor active, Tensor ticket,
+                        int64_t first, int64_t local) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DTYPE(wr, torch::kFloat32);
+  TORCH_CHECK(first >= 0 && local > 0 && first + local <= wr.size(0), "decode_route_local: expert range");
+  c10::cuda::CUDAGuard g(x.device());
+  qw::decode_route(bptr(x), wr.data_ptr<float>(), optptr<float>(ebias), static_cast<int>(x.size(0)),
+                   static_cast<int>(x.size(1)), static_cast<int>(wr.size(0)), static_cast<int>(k),
+                   static_cast<float>(temperature), logits.data_ptr<float>(), cnt.data_ptr<int>(), off.data_ptr<int>(),
+                   order.data_ptr<int>(), route_slot.data_ptr<int>(), top_w.data_ptr<float>(), active.data_ptr<int>(),
+                   ticket.data_ptr<int>(), stream(), static_cast<int>(first), static_cast<int>(local));
+}
+
+// norm of x + sum over ranks of the expert-parallel partial MoE outputs (plane of `layer` for the current step)
+void decode_combine_norm_parts(Tensor x, Tensor parts, Tensor step, int64_t layer, int64_t layers, int64_t world,
+                               int64_t tstride, Tensor w, OptT bias, double eps, bool rms, OptT x_out, Tensor n_out) {
+  CHECK_CUDA(n_out); CHECK_CONTIG(n_out); CHECK_CONTIG(x); CHECK_DTYPE(w, torch::kFloat32);
+  CHECK_DTYPE(parts, torch::kFloat32); CHECK_DTYPE(step, torch::kInt32);
+  TORCH_CHECK(parts.numel() >= 2 * layers * world * tstride * n_out.size(1), "decode_combine_norm_parts: planes");
+  c10::cuda::CUDAGuard g(n_out.device());
+  qw::decode_combine_norm(bptr(x), nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0,
+                          static_cast<int>(n_out.size(0)), static_cast<int>(n_out.size(1)), w.data_ptr<float>(),
+                          optptr<float>(bias), static_cast<float>(eps), rms, optb_mut(x_out), bptr_mut(n_out),
+                          stream(), parts.data_ptr<float>(), step.data_ptr<int>(), static_cast<int>(layer),
+                          static_cast<int>(layers), static_cast<int>(world), static_cast<int>(tstride));
+}
+
+void ep_decode_tick(Tensor step) {
+  CHECK_CUDA(step); CHECK_DTYPE(step, torch::kInt32);
+  c10::cuda::CUDAGuard g(step.device());
+  qw::ep_decode_tick(step.data_ptr<int>(), stream());
+}
+
+void ep_decode_push(Tensor y, Tensor slot, Tensor top_w, int64_t k, int64_t tstride, Tensor peers, int64_t plane_floats,
+                    int64_t layer, int64_t layers, int64_t me, Tensor peer_flags, Tensor step, Tensor done) {
+  CHECK_CUDA(y); CHECK_CONTIG(y); CHECK_DTYPE(peers, torch::kInt64); CHECK_DTYPE(peer_flags, torch::kInt64);
+  const int T = static_cast<int>(top_w.size(0));
+  TORCH_CHECK(T <= tstride, "ep_decode_push: more tokens than the exchange planes hold");
+  c10::cuda::CUDAGuard g(y.device());
+  qw::ep_decode_push(bptr(y), slot.data_ptr<int>(), top_w.data_ptr<float>(), static_cast<int>(k), T,
+                     static_cast<int>(y.size(1)), static_cast<int>(tstride),
+                     reinterpret_cast<float* const*>(peers.data_ptr<int64_t>()), plane_floats, static_cast<int>(layer),
+                     static_cast<int>(layers), static_cast<int>(me), static_cast<int>(peers.numel()),
+                     reinterpret_cast<int* const*>(peer_flags.data_ptr<int64_t>()), step.data_ptr<int>(),
+                     reinterpret_cast<unsigned int*>(done.data_ptr<int>()), stream());
+}
+
+void ep_decode_wait(Tensor flags, int64_t world, Tensor step, int64_t layer, int64_t layers, double timeout_s) {
+  CHECK_CUDA(flags); CHECK_DTYPE(flags, torch::kInt32);
+  c10::cuda::CUDAGuard g(flags.device());
+  qw::ep_decode_wait(flags.data_ptr<int>(), static_cast<int>(world), step.data_ptr<int>(), static_cast<int>(layer),
+                     static_cast<int>(layers), timeout_s, stream());
+}
+
 void rope_append(Tensor qkv, Tensor pos, int64_t Hq, int64_t Hkv, Tensor cos_t, Tensor sin_t, bool rope, Tensor q_out,
                  Tensor kc, Tensor vc) {
   CHECK_CUDA(qkv); CHECK_CONTIG(qkv);
@@ -606,6 +680,9 @@ int64_t read_status(bool clear) {
   if ((t = qw::optim_status(clear)) && !s) s = t;
   if ((t = qw::attention_status(clear)) && !s) s = t;
   if ((t = qw::attention_tc_status(clear)) && !s) s = t;
+  if ((t = qw::attention_fwd_tc_status(clear)) && !s) s = t;
+  if ((t = qw::ep_status(clear)) && !s) s = t;
+  if ((t = qw::ep_decode_status(clear)) && !s) s = t;
   if ((t = qw::p2p_status(clear)) && !s) s = t;
   if ((t = qw::tp_status(clear)) && !s) s = t;
   if ((t = qw::decode_status(clear)) && !s) s = t;
@@ -620,6 +697,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_fwd_peer", &linear_fwd_peer);
   m.def("linear_dgrad_peer", &linear_dgrad_peer);
   m.def("tp_reduce_bcast", &tp_reduce_bcast);
+  m.def("tp_reduce_rows", &tp_reduce_rows);
   m.def("linear_dgrad", &linear_dgrad);
   m.def("linear_wgrad", &linear_wgrad);
   m.def("moe_gate_up_fwd", &moe_gate_up_fwd);
@@ -672,7 +750,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("bias_grad_slabs", &bias_grad_slabs);
   m.def("bias_grad", &bias_grad);
   m.def("decode_combine_norm", &decode_combine_norm);
+  m.def("decode_combine_norm_parts", &decode_combine_norm_parts);
+  m.def("decode_route_local", &decode_route_local);
+  m.def("ep_decode_tick", &ep_decode_tick);
+  m.def("ep_decode_push", &ep_decode_push);
+  m.def("ep_decode_wait", &ep_decode_wait);
   m.def("p2p_push", &p2p_push);
+  m.def("p2p_broadcast", &p2p_broadcast);
   m.def("p2p_wait", &p2p_wait);
   m.def("read_status", &read_status, py::arg("clear") = true);
 }

@@ -430,7 +430,9 @@ __global__ void __launch_bounds__(256) combine_norm_kernel(const bf16* __restric
                                                            const float* __restrict__ top_w, int k, int H,
                                                            const float* __restrict__ w, const float* __restrict__ bias,
                                                            float eps, int rms, bf16* __restrict__ x_out,
-                                                           bf16* __restrict__ n_out) {
+                                                           bf16* __restrict__ n_out, const float* __restrict__ parts,
+                                                           const int* __restrict__ part_step, int part_layer,
+                                                           int part_layers, int part_world, int part_tstride) {
   extern __shared__ float v[];  // [H]
   __shared__ float red[2][8];
   griddep_wait();
@@ -447,6 +449,12 @@ __global__ void __launch_bounds__(256) combine_norm_kernel(const bf16* __restric
       float add = 0.f;
       for (int j = 0; j < k; ++j)
         add += top_w[t * k + j] * __bfloat162float(y[static_cast<int64_t>(slot[t * k + j]) * H + h]);
+      val = __bfloat162float(__float2bfloat16(val + add));
+    } else if (parts) {  // expert-parallel decode: every rank's partial MoE output, summed in rank order
+      const int64_t plane = (*part_step & 1) * part_layers + part_layer;
+      const float* base = parts + plane * part_world * static_cast<int64_t>(part_tstride) * H;
+      float add = 0.f;
+      for (int r = 0; r < part_world; ++r) add += base[(static_cast<int64_t>(r) * part_tstride + t) * H + h];
       val = __bfloat162float(__float2bfloat16(val + add));
     }
     if (x_out) x_out[static_cast<int64_t>(t) * H + h] = __float2bfloat16(val);
@@ -491,7 +499,7 @@ __global__ void __launch_bounds__(256) decode_route_kernel(const bf16* __restric
                                                            int* __restrict__ cnt, int* __restrict__ off,
                                                            int* __restrict__ order, int* __restrict__ route_slot,
                                                            float* __restrict__ top_w, int* __restrict__ active,
-                                                           int* __restrict__ ticket) {
+                                                           int* __restrict__ ticket, int first, int local) {
   extern __shared__ float sh[];
   __shared__ int s_last;
   const int e_blk = blockIdx.x;
@@ -575,7 +583,8 @@ __global__ void __launch_bounds__(256) decode_route_kernel(const bf16* __restric
       off[e] = acc;
       cnt[e] = s_cnt[e];
       acc += s_cnt[e];
-      if (s_cnt[e] > 0 && n_active < slots) active[n_active++] = e;
+      // the active list names the experts this rank holds (all of them unless expert-parallel), relative to `first`
+      if (s_cnt[e] > 0 && e >= first && e < first + local && n_active < slots) active[n_active++] = e - first;
       s_cnt[e] = 0;
     }
     for (int i = n_active; i < slots; ++i) active[i] = -1;
@@ -643,26 +652,28 @@ void rope_append(const bf16* qkv, const int* pos, int B, int Hq, int Hkv, int D,
 void decode_combine_norm(const bf16* x, const int64_t* tokens, const bf16* tok_emb, const bf16* pos_emb,
                          const int* positions, const bf16* y, const int* slot, const float* top_w, int k, int T, int H,
                          const float* w, const float* bias, float eps, bool rms, bf16* x_out, bf16* n_out,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, const float* parts, const int* part_step, int part_layer,
+                         int part_layers, int part_world, int part_tstride) {
   if (T == 0) return;
   const size_t smem = static_cast<size_t>(H) * sizeof(float);
   if (smem > 48 * 1024)
     check_cuda(cudaFuncSetAttribute(combine_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     static_cast<int>(smem)), "combine_norm smem");
   launch_pdl(combine_norm_kernel, dim3(T), dim3(256), smem, stream, "decode_combine_norm", x, tokens, tok_emb,
-             pos_emb, positions, y, slot, top_w, k, H, w, bias, eps, rms ? 1 : 0, x_out, n_out);
+             pos_emb, positions, y, slot, top_w, k, H, w, bias, eps, rms ? 1 : 0, x_out, n_out, parts, part_step,
+             part_layer, part_layers, part_world, part_tstride);
 }
 
 void decode_route(const bf16* x, const float* wr, const float* ebias, int T, int H, int E, int k, float temperature,
                   float* logits, int* cnt, int* off, int* order, int* route_slot, float* top_w, int* active,
-                  int* ticket, cudaStream_t stream) {
+                  int* ticket, cudaStream_t stream, int first, int local) {
   if (T > 64 || k > 8) throw std::runtime_error("decode_route: at most 64 tokens and top-8");
   if (H % 128) throw std::runtime_error("decode_route: hidden size must be a multiple of 128");
   const size_t smem = static_cast<size_t>(T) * E * sizeof(float) + (static_cast<size_t>(T) * k + E) * sizeof(int);
   check_cuda(cudaFuncSetAttribute(decode_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   static_cast<int>(std::max<size_t>(smem, 1024))), "decode_route smem");
   launch_pdl(decode_route_kernel, dim3(E), dim3(256), smem, stream, "decode_route", x, wr, ebias, T, H, E, k,
-             temperature, logits, cnt, off, order, route_slot, top_w, active, ticket);
+             temperature, logits, cnt, off, order, route_slot, top_w, active, ticket, first, local < 0 ? E : local);
 }
 
 int decode_status(bool clear) { return read_status_word(clear); }

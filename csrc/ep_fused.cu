@@ -120,4 +120,6 @@ void ep_signal(int* const* peer_flags, int world, int me, int epoch, cudaStream_
   check_cuda(cudaGetLastError(), "ep_signal");
 }
 
+int ep_status(bool clear) { return read_status_word(clear); }
+
 }  // namespace qw

@@ -98,6 +98,8 @@ void linear_fwd_peer(const bf16* x, int64_t ldx, const bf16* w, int64_t ldw, int
                      void* const* peer_out, int64_t peer_rows, int peer_slot, cudaStream_t stream);
 void linear_dgrad_peer(const bf16* dy, int64_t lddy, const bf16* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
                        void* const* peer_out, int64_t peer_rows, int peer_slot, cudaStream_t stream);
+void tp_reduce_rows(const bf16* staging, int world, int64_t rows_per_rank, int N, const float* bias, bf16* out,
+                    cudaStream_t stream);
 void tp_reduce_bcast(const bf16* staging, int world, int64_t rows_per_rank, int N, const float* bias,
                      void* const* outs, int me, cudaStream_t stream);
 int tp_status(bool clear);
@@ -150,8 +152,16 @@ void flash_attn_bwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, c
                        bf16* dk, int64_t lddk, bf16* dv, int64_t lddv, int B, int S, int Hq, int Hkv, int D,
                        float scale, cudaStream_t stream);
 int attention_tc_status(bool clear);
+// tcgen05 causal flash-attention forward, head_dim 64 (attention_fwd_tc.cu)
+void flash_attn_fwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv, bf16* o,
+                       int64_t ldo, float* lse, int B, int S, int Hq, int Hkv, int D, float scale,
+                       cudaStream_t stream);
+int attention_fwd_tc_status(bool clear);
+int ep_status(bool clear);
 
 // ---- p2p.cu ----
+void p2p_broadcast(const void* src, int64_t block_bytes, void* const* peer_bufs, int* const* peer_flags, int world,
+                   int me, int epoch, unsigned int* done, cudaStream_t stream);
 void p2p_push(const void* src, int64_t block_bytes, void* const* peer_bufs, int* const* peer_flags, int world, int me,
               int epoch, unsigned int* done, cudaStream_t stream);
 void p2p_wait(const int* flags, int world, int epoch, double timeout_s, cudaStream_t stream);
@@ -178,18 +188,29 @@ void grouped_gemv(const bf16* x, int64_t ldx, const void* w, const void* scales,
                   const float* bias, const bf16* resid, int64_t ldr, const int* active, int active_slots,
                   cudaStream_t stream);
 int decode_attn_chunks(int Lmax);
+// first/local: the experts this rank holds (expert-parallel decode); `active` lists them relative to `first`
 void decode_route(const bf16* x, const float* wr, const float* ebias, int T, int H, int E, int k, float temperature,
                   float* logits, int* cnt, int* off, int* order, int* route_slot, float* top_w, int* active,
-                  int* ticket, cudaStream_t stream);
+                  int* ticket, cudaStream_t stream, int first = 0, int local = -1);
 void decode_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* lens, int B, int Hq, int Hkv, int D,
                       int Lmax, float scale, float* part_o, float* part_ml, int* tickets, bf16* out,
                       cudaStream_t stream);
 void rope_append(const bf16* qkv, const int* pos, int B, int Hq, int Hkv, int D, int Lmax, const float* cos_t,
                  const float* sin_t, bool rope, bf16* q_out, bf16* kc, bf16* vc, cudaStream_t stream);
+// parts: expert-parallel partial MoE outputs (ep_decode.cu planes) summed in rank order instead of y/slot/top_w
 void decode_combine_norm(const bf16* x, const int64_t* tokens, const bf16* tok_emb, const bf16* pos_emb,
                          const int* positions, const bf16* y, const int* slot, const float* top_w, int k, int T, int H,
                          const float* w, const float* bias, float eps, bool rms, bf16* x_out, bf16* n_out,
-                         cudaStream_t stream);
+                         cudaStream_t stream, const float* parts = nullptr, const int* part_step = nullptr,
+                         int part_layer = 0, int part_layers = 1, int part_world = 1, int part_tstride = 0);
 int decode_status(bool clear);
+// expert-parallel decode exchange (ep_decode.cu)
+void ep_decode_tick(int* step, cudaStream_t stream);
+void ep_decode_push(const bf16* y, const int* slot, const float* top_w, int k, int T, int H, int tstride,
+                    float* const* peers, int64_t plane_floats, int layer, int layers, int me, int world,
+                    int* const* peer_flags, const int* step, unsigned int* done, cudaStream_t stream);
+void ep_decode_wait(const int* flags, int world, const int* step, int layer, int layers, double timeout_s,
+                    cudaStream_t stream);
+int ep_decode_status(bool clear);
 
 }  // namespace qw

@@ -20,10 +20,12 @@ B200 design:
 On CPU the same step runs as plain fp32 PyTorch (the oracle the GPU path is tested against).
 
 Expert-parallel models (the reference refuses them, ``src/fast_decode.py:89-90``) decode SPMD: every rank of the
-expert group runs the same prompts and tokens through the replicated layers; at each MoE layer a rank weights only the
-routes to its own experts and one all-reduce over the group sums the partial outputs, so every rank produces the same
-logits (and, with the same seed, the same samples). This path uses the fp32 PyTorch step on the model's device and no
-CUDA graph; the fused decode kernels are single-GPU.
+expert group runs the same prompts and tokens through the replicated layers; at each MoE layer a rank runs only the
+routes to its own experts, so every rank produces the same logits (and, with the same seed, the same samples). On
+CUDA this is the native graph-captured step: the routing kernel lists only this rank's experts, the grouped GEMVs run
+them, and ``csrc/ep_decode.cu`` stores each token's partial MoE output into every rank's exchange plane with NVLink
+peer stores and a release flag; the next layer's norm kernel sums the planes in rank order. On CPU the partial outputs
+are summed with one all-reduce (the oracle).
 """
 
 from __future__ import annotations
@@ -95,7 +97,7 @@ class FastDecoder:
         self.config = cfg
         self.device = torch.device(device)
         self.ep = ep if ep is not None and ep.world_size > 1 else None
-        self.native = self.device.type == "cuda" and self.ep is None
+        self.native = self.device.type == "cuda"
         if self.native:
             # the prefill runs the model's own native modules: bf16 matrices, fp32 router/norms (in place)
             from ..training.native import prepare_model
@@ -142,6 +144,8 @@ class FastDecoder:
             self.cos, self.sin = cos.contiguous(), sin.contiguous()
         else:
             self.cos = self.sin = torch.zeros(1, device=dev)
+        if self.native and self.ep is not None:
+            self._setup_ep_exchange()
         # static step inputs/outputs (graph-safe)
         self.tokens_in = torch.zeros(max_batch, dtype=torch.long, device=dev)
         self.positions_in = torch.zeros(max_batch, dtype=torch.int32, device=dev)
@@ -161,6 +165,35 @@ class FastDecoder:
         self.graph_enabled = self.native if use_graph is None else bool(use_graph and self.native)
         if self.graph_enabled:
             self._capture()
+
+    def _setup_ep_exchange(self) -> None:
+        """Symmetric buffers of the expert-parallel decode exchange (collective over the expert group): two planes per
+        layer of ``[world][max_batch][hidden]`` fp32 partial outputs, one flag word per peer, a device step counter."""
+        import torch.distributed as dist
+
+        from ..parallel.p2p import P2PTransport
+
+        ep, dev = self.ep, self.device
+        transport = P2PTransport.for_group(ep.group, dev)
+        symm, name = transport.symm, transport._group_name()
+        local = self.layers[0].q_gu.size(0)
+        self._ep_first, self._ep_local = ep.rank * local, local
+        self._ep_me, self._ep_world = transport.me, transport.world
+        self._ep_plane = self._ep_world * self.max_batch * self.hidden
+        self._ep_parts = symm.empty(2 * len(self.layers) * self._ep_plane, dtype=torch.float32, device=dev)
+        self._ep_parts.zero_()
+        parts_handle = symm.rendezvous(self._ep_parts, name)
+        self._ep_flags = symm.empty(self._ep_world, dtype=torch.int32, device=dev)
+        self._ep_flags.zero_()
+        flags_handle = symm.rendezvous(self._ep_flags, name)
+        self._ep_handles = (parts_handle, flags_handle)
+        self._ep_peers = torch.tensor([int(p) for p in parts_handle.buffer_ptrs], dtype=torch.int64, device=dev)
+        self._ep_peer_flags = torch.tensor([int(p) for p in flags_handle.buffer_ptrs], dtype=torch.int64, device=dev)
+        self._ep_step = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._ep_done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._ep_timeout = transport.timeout_s
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=ep.group, device_ids=[dev.index])
 
     # ---- weight extraction -----------------------------------------------------------------------
     def _norm(self, norm):
@@ -293,7 +326,9 @@ class FastDecoder:
         chunks = C.decode_attn_chunks(self.capacity)
         tickets = self._tickets
         x = None
-        pending = None  # (y, slot, top_w, k) of the previous layer's MoE
+        pending = None  # (y, slot, top_w, k) of the previous layer's MoE, or its layer index (expert-parallel)
+        if self.ep is not None:
+            C.ep_decode_tick(self._ep_step)  # a fresh exchange target for this step (also on every graph replay)
         for li, layer in enumerate(self.layers):
             w1, b1, eps1, kind1 = layer.norm1
             n1 = torch.empty(batch, H, device=dev, dtype=bf)
@@ -302,10 +337,8 @@ class FastDecoder:
                 C.decode_combine_norm(None, tokens, self.tok_emb, self.pos_emb if self.learned else None, positions,
                                       None, None, None, 0, w1, b1, eps1, kind1 == "rmsnorm", x, n1)
             else:
-                y, slot, top_w, k = pending
                 x_res = torch.empty_like(x)
-                C.decode_combine_norm(x, None, None, None, None, y, slot, top_w, k, w1, b1, eps1, kind1 == "rmsnorm",
-                                      x_res, n1)
+                self._combine_norm(x, pending, layer.norm1, x_res, n1)
                 x = x_res
             qkv = torch.empty(batch, (hq + 2 * hkv) * d, device=dev, dtype=bf)
             C.grouped_gemv(n1, layer.wqkv, None, qkv.size(1), H, 0, 0, False, None, None, None, 1, batch,
@@ -326,20 +359,33 @@ class FastDecoder:
             n2 = torch.empty_like(x)
             C.decode_combine_norm(x, None, None, None, None, None, None, None, 0, w2, b2, eps2, kind2 == "rmsnorm",
                                   None, n2)
-            pending = self._moe_native(layer, n2, batch)
-        y, slot, top_w, k = pending
-        wf, bfn, epsf, kindf = self.final_norm
+            pending = self._moe_native(layer, n2, batch, li)
         xf = torch.empty_like(x)
-        C.decode_combine_norm(x, None, None, None, None, y, slot, top_w, k, wf, bfn, epsf, kindf == "rmsnorm", None, xf)
+        self._combine_norm(x, pending, self.final_norm, None, xf)
         logits = torch.empty(batch, self.vocab, device=dev, dtype=bf)
         C.grouped_gemv(xf, self.lm_head, None, self.vocab, H, 0, 0, False, None, None, None, 1, batch, logits,
                        False, None, None, None)
         return logits.float()
 
-    def _moe_native(self, layer, n2: Tensor, batch: int):
+    def _combine_norm(self, x: Tensor, pending, norm, x_out: Optional[Tensor], n_out: Tensor) -> None:
+        """x (+ the previous layer's MoE output) -> (x_out, norm(x_out)). Single GPU: weighted rows of the routed
+        expert outputs; expert-parallel: every rank's partial outputs from the exchange planes, in rank order."""
+        w, b, eps, kind = norm
+        if self.ep is not None:
+            self._C.decode_combine_norm_parts(x, self._ep_parts, self._ep_step, pending, len(self.layers),
+                                              self._ep_world, self.max_batch, w, b, eps, kind == "rmsnorm", x_out,
+                                              n_out)
+            return
+        y, slot, top_w, k = pending
+        self._C.decode_combine_norm(x, None, None, None, None, y, slot, top_w, k, w, b, eps, kind == "rmsnorm", x_out,
+                                    n_out)
+
+    def _moe_native(self, layer, n2: Tensor, batch: int, index: int = 0):
         """Fused decode routing (no capacity) -> grouped dequant SwiGLU GEMV -> grouped down GEMV.
 
-        Returns (y [routes, H] route-major, route_slot, top_w, k); the combine happens in the next norm."""
+        Returns (y [routes, H] route-major, route_slot, top_w, k); the combine happens in the next norm. Expert-parallel:
+        only this rank's experts run (the other routes' rows stay zero), the per-token partial outputs are pushed into
+        every rank's exchange plane and the wait for all peers' planes follows; returns the layer index."""
         C = self._C
         dev = n2.device
         E, k, f = layer.num_experts, layer.top_k, layer.ffn
@@ -351,15 +397,29 @@ class FastDecoder:
         top_w = torch.empty(batch, k, device=dev, dtype=torch.float32)
         logits = torch.empty(batch, E, device=dev, dtype=torch.float32)
         active = torch.empty(min(E, routes), device=dev, dtype=torch.int32)
-        C.decode_route(n2, layer.router, layer.bias, k, layer.temperature, logits, cnt, off, order, slot, top_w,
-                       active, self._tickets)
+        first, groups = 0, E
+        if self.ep is not None:
+            first, groups = self._ep_first, self._ep_local
+            C.decode_route_local(n2, layer.router, layer.bias, k, layer.temperature, logits, cnt, off, order, slot,
+                                 top_w, active, self._tickets, first, groups)
+        else:
+            C.decode_route(n2, layer.router, layer.bias, k, layer.temperature, logits, cnt, off, order, slot, top_w,
+                           active, self._tickets)
+        cnt_l, off_l = cnt[first:first + groups], off[first:first + groups]
         h = torch.empty(routes, f, device=dev, dtype=torch.bfloat16)
-        C.grouped_gemv(n2, layer.q_gu, layer.s_gu, f, self.hidden, layer.group_in, layer.fmt, True, order, off, cnt,
-                       E, 0, h, True, None, None, active)
-        y = torch.empty(routes, self.hidden, device=dev, dtype=torch.bfloat16)
-        C.grouped_gemv(h, layer.q_d, layer.s_d, self.hidden, f, layer.group_down, layer.fmt, False, None, off, cnt,
-                       E, 0, y, True, None, None, active)
-        return y, slot, top_w, k
+        C.grouped_gemv(n2, layer.q_gu, layer.s_gu, f, self.hidden, layer.group_in, layer.fmt, True, order, off_l,
+                       cnt_l, groups, 0, h, True, None, None, active)
+        alloc = torch.zeros if self.ep is not None else torch.empty  # routes to other ranks' experts add zero
+        y = alloc(routes, self.hidden, device=dev, dtype=torch.bfloat16)
+        C.grouped_gemv(h, layer.q_d, layer.s_d, self.hidden, f, layer.group_down, layer.fmt, False, None, off_l,
+                       cnt_l, groups, 0, y, True, None, None, active)
+        if self.ep is None:
+            return y, slot, top_w, k
+        layers = len(self.layers)
+        C.ep_decode_push(y, slot, top_w, k, self.max_batch, self._ep_peers, self._ep_plane, index, layers,
+                         self._ep_me, self._ep_peer_flags, self._ep_step, self._ep_done)
+        C.ep_decode_wait(self._ep_flags, self._ep_world, self._ep_step, index, layers, self._ep_timeout)
+        return index
 
     # ---- graphs ------------------------------------------------------------------------------------
     @torch.no_grad()

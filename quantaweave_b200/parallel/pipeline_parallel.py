@@ -114,6 +114,10 @@ class PipelineEngine:
         self.model, self.ctx, self.microbatches, self.autocast, self.schedule = model, ctx, microbatches, autocast, schedule
         self._totals = {"ce": 0.0, "aux": 0.0, "dropped": 0, "overflow": 0}
         self._pending: list = []
+        # called right before the step's last micro-batch backward (a sharded optimizer's ``arm_overlap``, so its
+        # gradient reduce-scatter runs bucket by bucket during that backward)
+        self.before_last_backward: Optional[Callable] = None
+        self._backwards = 0
 
     def _isend(self, tensor: Tensor, stage: int) -> None:
         self._pending.append((dist.isend(tensor, dst=self.ctx.peer(stage)), tensor))
@@ -160,6 +164,9 @@ class PipelineEngine:
 
     def _backward_step(self, saved) -> None:
         ctx = self.ctx
+        self._backwards += 1
+        if self._backwards == self.microbatches and self.before_last_backward is not None:
+            self.before_last_backward()
         hidden_in, output, aux_term = saved
         if ctx.is_last:
             output.backward()
@@ -177,6 +184,7 @@ class PipelineEngine:
         size = batch.size(0) // M
         zero = torch.zeros((), dtype=torch.float64, device=ctx.device)
         self._totals = {"ce": zero.clone(), "aux": zero.clone(), "dropped": zero.clone(), "overflow": zero.clone()}
+        self._backwards = 0
         if self.schedule == "1f1b":
             self._run_1f1b(batch, size)
         else:

@@ -16,6 +16,14 @@ On CUDA with more than one rank the collectives are fused into the optimizer ker
 packs its gradients into a symmetric staging buffer, the reduce-scatter kernel sums its shard straight from the
 peers' buffers (fixed rank order, cast and 1/world scale fused, sums of squares for the clip norm), and the AdamW
 kernel stores each updated value into every rank's parameter buffer, which is the all-gather.
+
+Overlap with backward (fused path, ``QW_ZERO_OVERLAP=1`` by default): the staging buffer is cut into buckets of
+about ``bucket_elems`` elements in reverse parameter order (the order backward produces gradients). Calling
+:meth:`arm_overlap` before the step's last backward makes each parameter's post-accumulate hook copy its finished
+gradient into the staging buffer and free it; when every parameter touching a bucket is staged, a side stream runs
+that bucket's barrier and the reduce-scatter of this rank's part of it while backward continues on the main stream.
+:meth:`reduce_gradients` then only flushes the buckets whose gradients never arrived (unused parameters) and joins
+the side stream.
 """
 
 from __future__ import annotations
@@ -31,7 +39,8 @@ from .expert_parallel import is_expert_parameter
 
 class ShardedAdamW:
     def __init__(self, model, ctx, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
-                 weight_decay: float = 1e-2, group=None) -> None:
+                 weight_decay: float = 1e-2, group=None, bucket_elems: int = 1 << 24) -> None:
+        self.bucket_elems = bucket_elems
         self.model, self.ctx = model, ctx
         self.group = group if group is not None else getattr(ctx, "group", None) or getattr(ctx, "dp_group", None)
         self.world = dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -46,7 +55,8 @@ class ShardedAdamW:
         self.shards: dict = {}
         for dtype, params in self._groups.items():
             total = sum(p.numel() for p in params)
-            per = (total + self.world - 1) // self.world
+            # shards are padded to a multiple of 8 elements, so the fused kernels move 16-byte vectors
+            per = ((total + self.world - 1) // self.world + 7) // 8 * 8
             start = self.rank * per
             flat = torch.cat([p.detach().reshape(-1).float() for p in params])
             flat = torch.nn.functional.pad(flat, (0, per * self.world - total))
@@ -101,6 +111,126 @@ class ShardedAdamW:
                       code=0 if dtype == torch.float32 else 1)
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group, device_ids=[device.index])
+        self._armed = False
+        self._overlap = os.environ.get("QW_ZERO_OVERLAP", "1") != "0"
+        if self._overlap:
+            self._setup_buckets(device)
+
+    # ---- overlap of the reduce-scatter with backward ------------------------------------------------
+    def _setup_buckets(self, device) -> None:
+        """Cut every dtype's staging buffer into 8-aligned buckets, from the end (backward's order), and hook the
+        parameters. ``self._buckets``: (dtype, lo, hi, number of parameters touching it), in launch order."""
+        self._comm = torch.cuda.Stream(device)
+        self._buckets: list = []
+        self._param_buckets: dict = {}  # id(param) -> (dtype, offset, bucket indices)
+        for dtype, params in self._groups.items():
+            sh = self.shards[dtype]
+            end = sh["per"] * self.world
+            offsets, offset = [], 0
+            for p in params:
+                offsets.append(offset)
+                offset += p.numel()
+            cuts = [end]
+            for off in reversed(offsets):
+                if cuts[-1] - off >= self.bucket_elems:
+                    cut = off // 8 * 8
+                    if 0 < cut < cuts[-1]:
+                        cuts.append(cut)
+            cuts.append(0)
+            cuts = sorted(set(cuts), reverse=True)  # descending: the first bucket covers the buffer's end
+            first = len(self._buckets)
+            for hi, lo in zip(cuts, cuts[1:]):
+                self._buckets.append([dtype, lo, hi, 0])
+            for p, off in zip(params, offsets):
+                touched = [first + b for b, (hi, lo) in enumerate(zip(cuts, cuts[1:])) if off < hi and off + p.numel() > lo]
+                for b in touched:
+                    self._buckets[b][3] += 1
+                self._param_buckets[id(p)] = (dtype, off, touched)
+                p.register_post_accumulate_grad_hook(self._on_grad)
+
+    def arm_overlap(self) -> None:
+        """Stage gradients and reduce-scatter them bucket by bucket during the next backward (the step's last)."""
+        if not (self.fused and self._overlap):
+            return
+        device = self.shared[0].device
+        self._armed = True
+        self._pending = [b[3] for b in self._buckets]
+        self._staged: set = set()
+        self._launched = [False] * len(self._buckets)
+        self._next_launch = 0
+        for dtype in self._groups:
+            sh = self.shards[dtype]
+            sh["grad"] = torch.empty(sh["per"], device=device, dtype=torch.float32)
+        from ..ops import ext
+
+        C = ext()
+        self._bucket_span = []
+        total = 0
+        for dtype, lo, hi, _ in self._buckets:
+            per = self.shards[dtype]["per"]
+            a, e = max(lo, self.rank * per), min(hi, (self.rank + 1) * per)
+            blocks = C.zero_rs_blocks(e - a) if e > a else 0
+            self._bucket_span.append((a, e, total, blocks))
+            total += blocks
+        self._partial = torch.zeros(max(total, 1), device=device, dtype=torch.float64)
+        self._launch_ready()
+
+    def _on_grad(self, p) -> None:
+        if not self._armed or id(p) in self._staged:
+            return
+        dtype, off, touched = self._param_buckets[id(p)]
+        self.shards[dtype]["gbuf"][off:off + p.numel()].copy_(p.grad.reshape(-1))
+        p.grad = None
+        self._staged.add(id(p))
+        for b in touched:
+            self._pending[b] -= 1
+        self._launch_ready()
+
+    def _launch_ready(self) -> None:
+        """Launch, in bucket order, every bucket whose parameters are all staged (same order on every rank)."""
+        while self._next_launch < len(self._buckets) and self._pending[self._next_launch] == 0:
+            self._launch(self._next_launch)
+            self._next_launch += 1
+
+    def _launch(self, b: int) -> None:
+        from ..ops import ext
+
+        dtype = self._buckets[b][0]
+        sh = self.shards[dtype]
+        a, e, first_block, blocks = self._bucket_span[b]
+        staged = torch.cuda.Event()
+        staged.record()
+        with torch.cuda.stream(self._comm):
+            self._comm.wait_event(staged)
+            self._barrier(self._ready)  # every rank has staged this bucket
+            if e > a:
+                base = self.rank * sh["per"]
+                ext().zero_reduce_scatter(sh["gpeers"], sh["code"], a, sh["grad"][a - base:e - base],
+                                          self._partial[first_block:first_block + blocks])
+        self._launched[b] = True
+
+    def _finish_overlap(self) -> None:
+        """Stage the gradients that never arrived (unused parameters: zeros), launch what is left, join."""
+        for dtype, params in self._groups.items():
+            gbuf = self.shards[dtype]["gbuf"]
+            for p in params:
+                if id(p) in self._staged:
+                    continue
+                _, off, touched = self._param_buckets[id(p)]
+                if p.grad is None:
+                    gbuf[off:off + p.numel()].zero_()
+                else:
+                    gbuf[off:off + p.numel()].copy_(p.grad.reshape(-1))
+                    p.grad = None
+                self._staged.add(id(p))
+                for b in touched:
+                    self._pending[b] -= 1
+        self._launch_ready()
+        torch.cuda.current_stream().wait_stream(self._comm)
+        total = self._partial.sum()
+        for i, dtype in enumerate(self._groups):
+            self.shards[dtype]["sumsq"] = total if i == 0 else torch.zeros_like(total)
+        self._armed = False
 
     def _barrier(self, channel) -> None:
         from ..ops import ext
@@ -134,6 +264,9 @@ class ShardedAdamW:
 
     # ---- gradients ------------------------------------------------------------------------------
     def reduce_gradients(self) -> None:
+        if self.fused and self._armed:
+            self._finish_overlap()
+            return
         if self.fused:
             self._reduce_fused()
             return

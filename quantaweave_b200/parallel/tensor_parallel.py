@@ -10,7 +10,9 @@ On CUDA the attention runs on the native kernels (tcgen05 GEMMs + flash attentio
 into the neighbouring GEMMs over NVLink peer memory (``FusedTPReducer``): the row-parallel output projection's GEMM
 stores each partial row straight into the owning rank's staging buffer and a reduction kernel sums the slots and
 stores the result into every rank's output buffer (forward); the column-parallel input projection does the same with
-its dgrad GEMM (backward). ``QW_TP_FUSED=0`` keeps NCCL all-reduces; the expert FFNs' all-reduce stays on NCCL.
+its dgrad GEMM (backward). Under sequence parallelism the all-gather of the token rows is done by NVLink peer stores
+and the reduce-scatter is fused into the producing GEMM the same way (each rank reduces only its own rows).
+``QW_TP_FUSED=0`` keeps NCCL collectives; the expert FFNs' all-reduce stays on NCCL.
 """
 
 from __future__ import annotations
@@ -130,6 +132,7 @@ class FusedTPReducer:
         self.transport = P2PTransport.for_group(group, device)
         self.ready = _Channel(self.transport)
         self.done = _Channel(self.transport)
+        self._arrivals = torch.zeros(self.world, dtype=torch.int32, device=device)  # per-destination block counters
 
     @classmethod
     def for_group(cls, group, device: torch.device) -> "FusedTPReducer":
@@ -168,6 +171,45 @@ class FusedTPReducer:
         C.ep_signal(self.done.peer_flags[done], self.rank, self.done.epoch)
         self.done.wait(done)  # every rank's reduced rows have landed in our output buffer
         return buf[plane:2 * plane].view(torch.bfloat16).view(M, N).clone()
+
+    def gemm_reduce_scatter(self, a: Tensor, w: Tensor, bias: Optional[Tensor], transposed: bool) -> Tensor:
+        """This rank's rows of ``sum over ranks of (a @ w^T)`` (``a @ w`` when ``transposed``) ``+ bias``: the GEMM
+        epilogue stores every partial row into its owner's staging slot over NVLink; after the ready barrier each rank
+        sums its own rows over the slots in a fixed rank order. ``[M / world, N]`` bf16."""
+        from ..ops import ext
+
+        C = ext()
+        M = a.size(0)
+        N = w.size(1) if transposed else w.size(0)
+        rows = M // self.world
+        plane = M * N * 2
+        self.ready.grow(plane)
+        parity = self.ready.next()
+        buf, _, peers = self.ready.bufs[parity]
+        if transposed:
+            C.linear_dgrad_peer(a, w, peers, rows, self.rank)
+        else:
+            C.linear_fwd_peer(a, w, peers, rows, self.rank)
+        C.ep_signal(self.ready.peer_flags[parity], self.rank, self.ready.epoch)
+        self.ready.wait(parity)  # every rank's partial rows of our block have landed
+        out = torch.empty(rows, N, device=a.device, dtype=torch.bfloat16)
+        C.tp_reduce_rows(buf[:plane].view(torch.bfloat16), self.world, rows, N, bias, out)
+        return out
+
+    def all_gather_rows(self, x: Tensor) -> Tensor:
+        """``[rows, H]`` of every rank, rank-major ``[world * rows, H]``: each rank stores its rows into every peer's
+        buffer with NVLink stores and releases a flag; after the wait the gathered rows are copied out of the
+        two-parity buffer (they outlive its next reuse when autograd saves them)."""
+        from ..ops import ext
+
+        x = x.contiguous()
+        nbytes = x.numel() * x.element_size()
+        self.ready.grow(nbytes * self.world)
+        parity = self.ready.next()
+        buf, _, peers = self.ready.bufs[parity]
+        ext().p2p_broadcast(x, peers, self.ready.peer_flags[parity], self.rank, self.ready.epoch, self._arrivals)
+        self.ready.wait(parity)
+        return buf[:nbytes * self.world].view(x.dtype).view(self.world * x.size(0), *x.shape[1:]).clone()
 
 
 def _bf16_rows(t: Tensor) -> Tensor:
@@ -243,6 +285,63 @@ class _ColumnParallelInput(torch.autograd.Function):
         dx = ctx.reducer.gemm_all_reduce(g2, w, None, True) if ctx.needs_input_grad[0] else None
         dw, db = _local_weight_grads(ctx, g2, x2, w)
         return dx, dw, db, None
+
+
+class _SPGatherLinear(torch.autograd.Function):
+    """Sequence parallelism, column-parallel input projection: ``(all rows of x) @ W_r^T + b_r`` where each rank holds
+    only its token rows of ``x``. The row all-gather is done by NVLink peer stores into symmetric memory (no NCCL);
+    in backward the dgrad GEMM stores each partial input-gradient row into its owner's staging slot and every rank
+    reduces its own rows — the reduce-scatter is fused into the GEMM."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, reducer):
+        from ..ops import ext
+
+        full = reducer.all_gather_rows(_bf16_rows(x))
+        w = weight.to(torch.bfloat16).contiguous()
+        out = torch.empty(full.size(0), w.size(0), device=x.device, dtype=torch.bfloat16)
+        ext().linear_fwd(full, w, bias.float() if bias is not None else None, None, out)
+        ctx.save_for_backward(full, w)
+        ctx.reducer = reducer
+        ctx.weight_dtype, ctx.bias_dtype = weight.dtype, (bias.dtype if bias is not None else None)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        full, w = ctx.saved_tensors
+        g2 = _bf16_rows(grad)
+        dx = ctx.reducer.gemm_reduce_scatter(g2, w, None, True) if ctx.needs_input_grad[0] else None
+        dw, db = _local_weight_grads(ctx, g2, full, w)
+        return dx, dw, db, None
+
+
+class _SPLinearScatter(torch.autograd.Function):
+    """Sequence parallelism, row-parallel output projection: ``o_r @ W_r^T`` over all rows, reduce-scattered to this
+    rank's rows inside the GEMM (peer-store epilogue + fixed-order local reduction); in backward the row gradients
+    are all-gathered by NVLink peer stores and the dgrad / wgrad GEMMs run locally."""
+
+    @staticmethod
+    def forward(ctx, o, weight, reducer):
+        o2 = _bf16_rows(o)
+        w = weight.to(torch.bfloat16).contiguous()
+        out = reducer.gemm_reduce_scatter(o2, w, None, False)
+        ctx.save_for_backward(o2, w)
+        ctx.reducer = reducer
+        ctx.weight_dtype, ctx.bias_dtype = weight.dtype, None
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        from ..ops import ext
+
+        o2, w = ctx.saved_tensors
+        g_full = ctx.reducer.all_gather_rows(_bf16_rows(grad))
+        do = None
+        if ctx.needs_input_grad[0]:
+            do = torch.empty(o2.size(0), w.size(1), device=grad.device, dtype=torch.bfloat16)
+            ext().linear_dgrad(g_full, w, do, False)
+        dw, _ = _local_weight_grads(ctx, g_full, o2, w)
+        return do, dw, None
 
 
 class _RowParallelOutput(nn.Module):
@@ -359,6 +458,18 @@ class TensorParallelAttention(nn.Module):
             raise RuntimeError("sequence-parallel attention needs the batch shape (set by the model's forward)")
         batch, seq = self.sp_shape
         shape, hidden = x.shape, x.size(-1)
+        rows = x.reshape(-1, hidden)
+        if FusedTPReducer.usable(rows, self.tp_group, hidden):
+            from ..ops.attention import attention_core
+
+            reducer = FusedTPReducer.for_group(self.tp_group, x.device)
+            qkv = _SPGatherLinear.apply(rows, self.in_proj_weight, self.in_proj_bias, reducer)
+            o = attention_core(qkv, batch, seq, self.heads, self.kv_heads, self.head_dim, self.rope,
+                               self.config.rope_theta)
+            out = _SPLinearScatter.apply(o, self.out_proj.weight, reducer)
+            if self.out_proj.bias is not None:
+                out = out + self.out_proj.bias.to(out.dtype)
+            return out.reshape(shape)
         full = _GatherRows.apply(x.reshape(-1, hidden), self.tp_group)
         partial = self._heads_partial(full, batch, seq)
         out = _ScatterRows.apply(partial, self.tp_group)

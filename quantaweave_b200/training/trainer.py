@@ -798,6 +798,8 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
         from ..parallel.pipeline_parallel import PipelineEngine
 
         engine = PipelineEngine(model, pp, args.microbatches, autocast, schedule=args.pipeline_schedule)
+        if hasattr(optimizer, "arm_overlap"):  # sharded AdamW: reduce-scatter during the last backward
+            engine.before_last_backward = optimizer.arm_overlap
     counts = parameter_counts(config)
     controller = TrainingController(schedule_config_from(args), base_temperature=args.router_temperature)
     adaptive = args.aux_adapt or args.temperature_adapt
@@ -912,6 +914,9 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
                             num_domains=stream.num_domains if domains_active else 0, return_logits=False)
             loss = out["loss"]
             scaled = loss / args.gradient_accumulation_steps
+            last_micro = step % args.gradient_accumulation_steps == 0 or step == args.steps
+            if last_micro and args.shard_optimizer and scaler is None and hasattr(optimizer, "arm_overlap"):
+                optimizer.arm_overlap()  # reduce-scatter the gradient buckets while this backward runs
             with nvtx_range("backward"):
                 (scaler.scale(scaled) if scaler is not None else scaled).backward()
             if step % args.gradient_accumulation_steps == 0 or step == args.steps:

@@ -85,6 +85,33 @@ def test_attention(B, S, hq, hkv, d):
     _status_ok()
 
 
+@pytest.mark.parametrize("B,S,hq,hkv", [(2, 2048, 4, 4), (1, 4096, 2, 1), (3, 333, 4, 2), (1, 1, 2, 2),
+                                        (1, 130, 2, 2), (2, 256, 16, 16)])
+def test_attention_forward_tcgen05_and_lse_match_fp32(B, S, hq, hkv):
+    """The tcgen05 forward (head_dim 64) against a plain fp32 causal softmax(QK^T)V, including lse = ln sum exp."""
+    from quantaweave_b200.ops import ext
+
+    d = 64
+    torch.manual_seed(3)
+    T = B * S
+    qkv = (torch.randn(T, (hq + 2 * hkv) * d, device="cuda") * 0.7).bfloat16()
+    q, k, v = qkv[:, : hq * d], qkv[:, hq * d:(hq + hkv) * d], qkv[:, (hq + hkv) * d:]
+    o = torch.empty(T, hq * d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.full((B, hq, S), float("nan"), device="cuda")
+    ext().flash_attn_fwd(q, k, v, o, lse, B, S, hq, hkv, d, 1.0 / math.sqrt(d))
+    torch.cuda.synchronize()
+    qf = q.float().reshape(B, S, hq, d).transpose(1, 2)
+    kf = k.float().reshape(B, S, hkv, d).repeat_interleave(hq // hkv, dim=2).transpose(1, 2)
+    vf = v.float().reshape(B, S, hkv, d).repeat_interleave(hq // hkv, dim=2).transpose(1, 2)
+    scores = (qf @ kf.transpose(-1, -2)) / math.sqrt(d)
+    scores = scores.masked_fill(torch.ones(S, S, device="cuda", dtype=torch.bool).triu(1), float("-inf"))
+    ref_lse = torch.logsumexp(scores, dim=-1)
+    ref = (torch.softmax(scores, dim=-1) @ vf).transpose(1, 2).reshape(T, hq * d)
+    _close(o, ref, 2e-2)
+    assert float((lse - ref_lse).abs().max()) < 2e-2
+    _status_ok()
+
+
 def _moe_module(E=8, H=128, F_=256, k=2, cf=1.25):
     from quantaweave_b200 import QuantaWeaveConfig
     from quantaweave_b200.models.moe import TopKMoE

@@ -167,10 +167,10 @@ def _sp_case(rank, world):
     return float(loss)
 
 
-def _sp_worker(rank, world, port, queue):
+def _sp_worker(rank, world, port, queue, fused):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), QW_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0",
-                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
+                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1", QW_TP_FUSED=fused)
     try:
         queue.put((rank, "ok", _sp_case(rank, world)))
     except Exception:  # noqa: BLE001
@@ -180,12 +180,14 @@ def _sp_worker(rank, world, port, queue):
             dist.destroy_process_group()
 
 
-def test_sequence_parallel_native_matches_single_gpu():
+@pytest.mark.parametrize("fused", ["1", "0"])
+def test_sequence_parallel_native_matches_single_gpu(fused):
+    """fused "1": row all-gather by NVLink peer stores and reduce-scatter inside the projection GEMMs; "0": NCCL."""
     world = 2
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_sp_worker, args=(r, world, port, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_sp_worker, args=(r, world, port, queue, fused)) for r in range(world)]
     for p in procs:
         p.start()
     for _ in range(world):

@@ -22,7 +22,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _case(rank, fused):
+def _case(rank, mode):
     from quantaweave_b200 import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM
     from quantaweave_b200.ops import ext
     from quantaweave_b200.parallel.expert_parallel import (broadcast_shared_parameters, clip_grad_norm_parallel,
@@ -30,7 +30,9 @@ def _case(rank, fused):
     from quantaweave_b200.parallel.sharded_optimizer import ShardedAdamW
     from quantaweave_b200.training.native import prepare_model
 
+    fused = mode != "nccl"
     os.environ["QW_ZERO_FUSED"] = "1" if fused else "0"
+    os.environ["QW_ZERO_OVERLAP"] = "1" if mode == "overlap" else "0"
     torch.cuda.set_device(rank)
     ctx = init_expert_parallel("cuda", 1, transport="nccl")
     cfg = QuantaWeaveConfig(vocab_size=512, hidden_size=256, layers=2, ffn_size=256, num_experts=8, top_k=2,
@@ -40,12 +42,15 @@ def _case(rank, fused):
     model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ctx).cuda()
     prepare_model(model, "bf16")
     broadcast_shared_parameters(model, ctx)
-    opt = ShardedAdamW(model, ctx, lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)
+    # small buckets, so the overlapped reduce-scatter runs as several bucket launches during backward
+    opt = ShardedAdamW(model, ctx, lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1, bucket_elems=1 << 16)
     assert opt.fused == fused
     norms, first = [], {}
     for step in range(3):
         g = torch.Generator().manual_seed(100 * step + rank)
         batch = torch.randint(0, cfg.vocab_size, (2, 129), generator=g).cuda()
+        if mode == "overlap":
+            opt.arm_overlap()
         model(batch, labels=batch, return_logits=False)["loss"].backward()
         sync_gradients(model, ctx, opt)
         if step == 0:
@@ -62,11 +67,11 @@ def _case(rank, fused):
     return {"norms": norms, "shared": shared, "first": first}
 
 
-def _worker(rank, world, port, fused, queue):
+def _worker(rank, world, port, mode, queue):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
                       LOCAL_RANK=str(rank), QW_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0")
     try:
-        queue.put((rank, "ok", _case(rank, fused)))
+        queue.put((rank, "ok", _case(rank, mode)))
     except Exception:  # noqa: BLE001
         queue.put((rank, "error", traceback.format_exc()))
     finally:
@@ -74,12 +79,12 @@ def _worker(rank, world, port, fused, queue):
             dist.destroy_process_group()
 
 
-def _run(fused):
+def _run(mode):
     world = 2
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, fused, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, queue)) for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -95,9 +100,12 @@ def _run(fused):
     return results
 
 
-def test_fused_zero_matches_nccl_zero():
+@pytest.mark.parametrize("mode", ["fused", "overlap"])
+def test_fused_zero_matches_nccl_zero(mode):
+    """``fused``: peer-load reduce-scatter after backward; ``overlap``: the same kernels launched bucket by bucket on
+    a side stream while backward runs. Both against the NCCL reduce_scatter / all_gather path."""
     lr, steps = 1e-3, 3
-    fused, plain = _run(True), _run(False)
+    fused, plain = _run(mode), _run("nccl")
     for rank in (0, 1):
         # step 1, same inputs: the peer-load reduce-scatter is the fp32 sum of two values, exactly what NCCL computes
         for key, value in plain[rank]["first"]["grad"].items():
