@@ -6,9 +6,9 @@
     python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 bench_decode.py --batch 1
 
 Launched on N ranks, the experts are spread expert-parallel over the N GPUs (N must divide 64) and every rank
-decodes the same prompts; each MoE layer sums the ranks' partial outputs with one all-reduce. That path runs the
-PyTorch decode step (the fused single-GPU decode kernels and CUDA graph are not used); the reported time is the max
-over ranks.
+decodes the same prompts with the native graph-captured step: each rank runs the experts it holds and stores its
+per-token partial MoE outputs into every rank's exchange buffer over NVLink (csrc/ep_decode.cu); the reported time is
+the max over ranks.
 
 Config 5: the config-2 architecture (vocab 32000, d1024, 16 layers, 16 heads, 64 SwiGLU experts h2816, top-2) with
 random-init N(0, 0.02) weights, experts quantised to int4 (group 128, fp16 scales, symmetric) or int8 per-channel;
@@ -37,7 +37,29 @@ def parse():
     p.add_argument("--new", type=int, default=256)
     p.add_argument("--impl", choices=("native", "reference"), default="native")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--kernel-breakdown", action="store_true",
+                   help="after timing, profile 8 more decode steps and print per-kernel device time per step")
     return p.parse_args()
+
+
+def kernel_breakdown(step, steps: int = 8) -> None:
+    """Device time per decode step of every kernel (torch profiler; shares only, never a reported number)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(steps):
+            step()
+        torch.cuda.synchronize()
+    totals: dict = {}
+    for e in prof.events():
+        if e.device_type == torch.autograd.DeviceType.CUDA:
+            t, n = totals.get(e.name[:100], (0.0, 0))
+            totals[e.name[:100]] = (t + e.device_time_total, n + 1)
+    grand = sum(t for t, _ in totals.values()) or 1.0
+    print(f"decode kernel breakdown: {grand / steps:.1f} us of device time per step", file=sys.stderr)
+    for name, (t, n) in sorted(totals.items(), key=lambda kv: -kv[1][0])[:25]:
+        print(f"  {100 * t / grand:5.1f}%  {t / steps:8.2f} us/step  x{n // steps:<4d} {name}", file=sys.stderr)
 
 
 def main():
@@ -82,6 +104,9 @@ def main():
     torch.cuda.synchronize()
     step_ms = [events[i].elapsed_time(events[i + 1]) for i in range(args.new)]
     decode_ms = events[0].elapsed_time(events[-1])
+    if args.kernel_breakdown:
+        pos = torch.full((args.batch,), args.prompt - 1, dtype=torch.int32, device="cuda")
+        kernel_breakdown(lambda: dec.run_step(token, pos))
     print(json.dumps({
         "metric": "int4 decode tokens/sec" if args.bits == 4 else f"int{args.bits} decode tokens/sec",
         "value": args.batch * args.new / (decode_ms / 1000.0), "unit": "tokens/s", "n_gpus": 1,
@@ -96,9 +121,13 @@ def main():
 def run_reference(args, prompts, group):
     import torch
 
-    src = os.path.join(ROOT, "baseline", "_ref", "src")
-    if not os.path.isdir(src):
-        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref/src is missing"}))
+    sys.path.insert(0, ROOT)
+    from bench import locate_reference_src
+
+    src, searched = locate_reference_src(ROOT)
+    if src is None:
+        print(json.dumps({"impl": "reference", "unavailable": "reference modules not found; searched "
+                          + "; ".join(searched)}))
         return
     sys.path.insert(0, src)
     from fast_decode import FastDecoder
@@ -144,10 +173,6 @@ def run_reference(args, prompts, group):
         "n_gpus": 1, "batch": 1, "prompt": args.prompt, "new_tokens": args.new,
         "p50_token_latency_ms": statistics.median(s.elapsed_time(e) for s, e in steps), "impl": "reference",
         "description": dec.description}))
-
-
-if __name__ == "__main__":
-    main()
 
 
 def run_expert_parallel(args):
@@ -200,6 +225,15 @@ def run_expert_parallel(args):
             events[i + 1].record()
         torch.cuda.synchronize()
         dist.barrier()
+        if args.kernel_breakdown:  # every rank runs the steps (they exchange); rank 0's profile is printed
+            pos = torch.full((args.batch,), args.prompt - 1, dtype=torch.int32, device="cuda")
+            if ep.rank == 0:
+                kernel_breakdown(lambda: dec.run_step(token, pos))
+            else:
+                for _ in range(8):
+                    dec.run_step(token, pos)
+            torch.cuda.synchronize()
+            dist.barrier()
         timing = torch.tensor([events[0].elapsed_time(events[-1]), start.elapsed_time(mid)], device="cuda")
         dist.all_reduce(timing, op=dist.ReduceOp.MAX)
         step_ms = [events[i].elapsed_time(events[i + 1]) for i in range(args.new)]
@@ -210,10 +244,15 @@ def run_expert_parallel(args):
                 "value": args.batch * args.new / (decode_ms / 1000.0), "unit": "tokens/s", "n_gpus": ep.world_size,
                 "batch": args.batch, "prompt": args.prompt, "new_tokens": args.new,
                 "p50_token_latency_ms": statistics.median(step_ms), "prefill_ms": prefill_ms,
-                "higher_is_better": True, "impl": "native", "parallelism": f"ep{ep.world_size} (SPMD, all-reduce "
-                "of the MoE partial outputs per layer, PyTorch decode step)",
+                "higher_is_better": True, "impl": "native", "graph": dec.uses_graph,
+                "parallelism": f"ep{ep.world_size} (SPMD native graph step; per-token partial MoE outputs exchanged "
+                "by NVLink peer stores)" if dec.native else f"ep{ep.world_size} (PyTorch step, all-reduce)",
                 "weights": f"int{args.bits}" + (f" g{group} fp16 scales" if args.bits == 4 else
                                                 " per-channel" if args.bits == 8 else " bf16"),
                 "data": "synthetic seeded uniform prompt, random-init N(0,0.02) weights"}), flush=True)
     finally:
         dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -41,6 +41,8 @@ def parse():
     p.add_argument("--device", choices=("cuda", "cpu"), default="cuda")
     p.add_argument("--tiny", action="store_true", help="a small model of the same layout (wiring check)")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--layers", type=int, default=0, help="debug override of the layer count (the metric needs the "
+                                                           "configuration's own)")
     return p.parse_args()
 
 
@@ -94,6 +96,8 @@ def _tp_ep(args, rank, world, device):
     if args.tiny:
         overrides.update(vocab_size=256, hidden_size=8 * world, layers=2, attention_heads=world, kv_heads=world,
                          num_experts=world, ffn_size=32)
+    if args.layers:
+        overrides["layers"] = args.layers
     cfg = preset("mixtral-8x7b", **overrides)
     ep = init_expert_parallel(device.type, tensor_parallel=world, sequence_parallel=True)
     torch.manual_seed(args.seed + rank)
@@ -120,7 +124,9 @@ def _tp_ep(args, rank, world, device):
         opt.zero_grad(set_to_none=True)
         return out["loss"]
 
-    description = {"model": "mixtral-8x7b shape (benchmark configuration 3)" if not args.tiny else "tiny tp-ep wiring check",
+    description = {"model": ("mixtral-8x7b shape (benchmark configuration 3)" if not args.layers else
+                             f"DEBUG {args.layers}-layer variant of the mixtral-8x7b shape")
+                   if not args.tiny else "tiny tp-ep wiring check",
                    "global_batch": seqs, "seq_len": seq,
                    "parallelism": f"sp: attention tp{world} + experts ep{world} on the same ranks",
                    "activation_checkpointing": True, "ep_transport": ep.transport}
@@ -140,6 +146,8 @@ def _pp_zero(args, rank, world, device):
     if args.tiny:
         overrides.update(vocab_size=256, hidden_size=32, layers=2 * (world // dp), attention_heads=4, num_experts=4,
                          ffn_size=32)
+    if args.layers:
+        overrides["layers"] = args.layers
     cfg = preset("moe-pp-e16", **overrides)
     pp = init_pipeline_parallel(device.type, cfg.layers, data_parallel=dp)
     torch.manual_seed(args.seed + pp.stage)
@@ -168,7 +176,9 @@ def _pp_zero(args, rank, world, device):
         opt.zero_grad(set_to_none=True)
         return result["loss"]
 
-    description = {"model": "moe-pp-e16 (benchmark configuration 4)" if not args.tiny else "tiny pp-zero wiring check",
+    description = {"model": ("moe-pp-e16 (benchmark configuration 4)" if not args.layers else
+                             f"DEBUG {args.layers}-layer variant of moe-pp-e16") if not args.tiny else
+                   "tiny pp-zero wiring check",
                    "global_batch": micro * per_micro * pp.dp_size, "seq_len": seq,
                    "parallelism": f"pp{pp.num_stages} x dp{pp.dp_size}, gpipe, {micro} micro-batches",
                    "optimizer": "sharded AdamW over the data-parallel group" if pp.dp_size > 1 else "AdamW"}

@@ -7,7 +7,8 @@
 // tensor core works on the other group's tiles (ping-pong):
 //
 //   S_g  = Q_g K_j^T                       (TMEM, 128 x 128 fp32 per group)
-//   P_g  = exp2(S_g * scale*log2e - m_g)   (softmax warps -> bf16, K-major swizzled shared memory)
+//   P_g  = exp2(S_g * scale*log2e - m_g)   (softmax warps, packed f16x2 exponentials -> bf16, K-major swizzled
+//                                           shared memory)
 //   O_g += P_g V_j                          (TMEM, 128 x 64 fp32 per group, accumulated by the tensor core)
 //
 // Lazy rescaling: m_g is the row maximum the accumulator O_g is expressed against. A new tile only moves it when its
@@ -307,10 +308,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t w[4];
 #pragma unroll
         for (int e2 = 0; e2 < 4; ++e2) {
-          const float a = ex2(v[8 * c8 + 2 * e2] - m_ref);  // exp2(-inf) = 0 for masked keys
-          const float b2 = ex2(v[8 * c8 + 2 * e2 + 1] - m_ref);
-          tile_sum += a + b2;
-          w[e2] = pack_bf16(a, b2);
+          // two exponentials per instruction in half precision: the exponent lies in [-inf, 8] (lazy rescale), so
+          // the f16 input keeps ~11 bits where the probabilities are large, and the bf16 probabilities need 8
+          const __half2 e = h2exp2(__floats2half2_rn(v[8 * c8 + 2 * e2] - m_ref, v[8 * c8 + 2 * e2 + 1] - m_ref));
+          const float2 f = __half22float2(e);  // exp2(-inf) = 0 for masked keys
+          tile_sum += f.x + f.y;
+          w[e2] = pack_bf16(f.x, f.y);
         }
         const int box = c8 / 8;
         const int swz = (c8 % 8) ^ (row & 7);

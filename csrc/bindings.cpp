@@ -93,8 +93,20 @@ void linear_wgrad(Tensor dy, Tensor x, Tensor dw, bool accumulate) {
   TORCH_CHECK(x.size(0) == dy.size(0) && dw.size(0) == dy.size(1) && dw.size(1) == x.size(1), "linear_wgrad shapes");
   const bool fp32 = dw.scalar_type() == torch::kFloat32;
   c10::cuda::CUDAGuard g(dy.device());
-  qw::linear_wgrad(bptr(dy), dy.stride(0), bptr(x), x.stride(0), dy.size(0), dy.size(1), x.size(1), dw.data_ptr(),
-                   dw.stride(0), fp32, accumulate, stream());
+  const int64_t T = dy.size(0), N = dy.size(1), K = x.size(1);
+  const int split = qw::wgrad_split(T, N, K);
+  if (split > 1) {  // too few output tiles to fill the GPU: split the token reduction, then a fixed-order sum
+    const int64_t chunk = ((T + split - 1) / split + 63) / 64 * 64;
+    const int chunks = static_cast<int>((T + chunk - 1) / chunk);
+    auto partial = torch::empty({chunks, N, K}, dy.options().dtype(torch::kFloat32));
+    qw::linear_wgrad_chunks(bptr(dy), dy.stride(0), bptr(x), x.stride(0), T, N, K, chunk, partial.data_ptr<float>(),
+                            stream());
+    qw::splitk_reduce(partial.data_ptr<float>(), chunks, N, K, dw.data_ptr(), dw.stride(0), fp32, accumulate,
+                      stream());
+    return;
+  }
+  qw::linear_wgrad(bptr(dy), dy.stride(0), bptr(x), x.stride(0), T, N, K, dw.data_ptr(), dw.stride(0), fp32,
+                   accumulate, stream());
 }
 
 void check_groups(const Tensor& counts, const Tensor& offsets, int64_t E) {
@@ -634,6 +646,17 @@ void decode_combine_norm_parts(Tensor x, Tensor parts, Tensor step, int64_t laye
                           static_cast<int>(layers), static_cast<int>(world), static_cast<int>(tstride));
 }
 
+void dequant_rows(Tensor q, Tensor scales, int64_t K, int64_t group, int64_t fmt, Tensor out) {
+  CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(scales); CHECK_CONTIG(out);
+  TORCH_CHECK(scales.scalar_type() == torch::kFloat16 && out.scalar_type() == torch::kBFloat16, "dequant_rows dtypes");
+  TORCH_CHECK(fmt == 1 || fmt == 2, "dequant_rows: fmt 1 (int8) or 2 (int4)");
+  const int64_t rows = out.numel() / K;
+  TORCH_CHECK(q.numel() == rows * (fmt == 2 ? K / 2 : K), "dequant_rows: packed size");
+  c10::cuda::CUDAGuard g(q.device());
+  qw::dequant_rows(q.data_ptr(), scales.data_ptr(), rows, static_cast<int>(K), static_cast<int>(group),
+                   static_cast<int>(fmt), bptr_mut(out), stream());
+}
+
 void ep_decode_tick(Tensor step) {
   CHECK_CUDA(step); CHECK_DTYPE(step, torch::kInt32);
   c10::cuda::CUDAGuard g(step.device());
@@ -753,6 +776,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_combine_norm_parts", &decode_combine_norm_parts);
   m.def("decode_route_local", &decode_route_local);
   m.def("ep_decode_tick", &ep_decode_tick);
+  m.def("dequant_rows", &dequant_rows);
   m.def("ep_decode_push", &ep_decode_push);
   m.def("ep_decode_wait", &ep_decode_wait);
   m.def("p2p_push", &p2p_push);

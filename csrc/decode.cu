@@ -678,4 +678,54 @@ void decode_route(const bf16* x, const float* wr, const float* ebias, int T, int
 
 int decode_status(bool clear) { return read_status_word(clear); }
 
+
+
+// ------------------------------------------------------------------------------------------------ dequantisation
+// bf16 copy of packed weight rows, for the tensor-core GEMMs that serve many tokens at once (prefill): int4 (fmt 2,
+// two values per byte, low nibble = even column, value = (nibble - 8) * scale of its group of `group` columns) or
+// int8 (fmt 1, one scale per row). One thread writes 8 consecutive bf16 (one 16-byte store).
+namespace {
+__global__ void __launch_bounds__(256) dequant_rows_kernel(const uint8_t* __restrict__ q, const __half* __restrict__ s,
+                                                           int64_t rows, int K, int group, int fmt,
+                                                           bf16* __restrict__ out) {
+  const int vecs_per_row = K / 8;
+  const int64_t total = rows * vecs_per_row;
+  const int spr = fmt == 2 ? K / group : 1;  // scales per row
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / vecs_per_row;
+    const int k0 = static_cast<int>(i % vecs_per_row) * 8;
+    const float scale = __half2float(s[r * spr + (fmt == 2 ? k0 / group : 0)]);
+    float v[8];
+    if (fmt == 2) {
+      const uint32_t packed = *reinterpret_cast<const uint32_t*>(q + r * (K / 2) + k0 / 2);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = static_cast<float>(static_cast<int>((packed >> (4 * j)) & 0xFu) - 8) * scale;
+    } else {
+      const uint2 packed = *reinterpret_cast<const uint2*>(q + r * K + k0);
+      const int8_t* b = reinterpret_cast<const int8_t*>(&packed);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = static_cast<float>(b[j]) * scale;
+    }
+    uint4 w;
+    w.x = pack_bf16(v[0], v[1]);
+    w.y = pack_bf16(v[2], v[3]);
+    w.z = pack_bf16(v[4], v[5]);
+    w.w = pack_bf16(v[6], v[7]);
+    *reinterpret_cast<uint4*>(out + r * K + k0) = w;
+  }
+}
+}  // namespace
+
+void dequant_rows(const void* q, const void* scales, int64_t rows, int K, int group, int fmt, bf16* out,
+                  cudaStream_t stream) {
+  if (rows == 0) return;
+  if (K % 8 || (fmt == 2 && (group % 8 || K % group))) throw std::runtime_error("dequant_rows: K / group layout");
+  const int64_t total = rows * (K / 8);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(148 * 16, (total + 255) / 256)));
+  dequant_rows_kernel<<<grid, 256, 0, stream>>>(static_cast<const uint8_t*>(q), static_cast<const __half*>(scales),
+                                                rows, K, group, fmt, out);
+  check_cuda(cudaGetLastError(), "dequant_rows");
+}
+
 }  // namespace qw

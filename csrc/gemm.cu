@@ -357,6 +357,47 @@ void moe_wgrad(const bf16* a, const bf16* b, const int* counts, const int* offse
   launch<BN, kGroupK, kEpiStore, true, true>(ma, mb, p, static_cast<int64_t>(p.m_tiles) * p.n_tiles * E, stream);
 }
 
+namespace {
+// out[r, c] (+)= sum over chunks (fixed order) of partial[chunk][r][c]: the tail of a split-K weight gradient
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ partial, int chunks, int rows,
+                                                            int cols, void* __restrict__ out, int64_t ldo,
+                                                            int out_fp32, int accumulate) {
+  const int64_t total = static_cast<int64_t>(rows) * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc = 0.f;
+    for (int c = 0; c < chunks; ++c) acc += partial[c * total + i];
+    const int64_t at = (i / cols) * ldo + i % cols;
+    if (out_fp32) {
+      float* o = static_cast<float*>(out) + at;
+      *o = accumulate ? *o + acc : acc;
+    } else {
+      bf16* o = static_cast<bf16*>(out) + at;
+      *o = __float2bfloat16(accumulate ? __bfloat162float(*o) + acc : acc);
+    }
+  }
+}
+}  // namespace
+
+// Split-K factor for a dense weight gradient whose output tiles cannot fill the GPU (1 = no split): enough row
+// chunks for about two waves of output tiles, each chunk at least 1024 rows.
+int wgrad_split(int64_t T, int64_t N, int64_t K) {
+  const int64_t tiles = ((N + kBM - 1) / kBM) * ((K + 255) / 256);
+  if (tiles >= num_sms() || T < 4096) return 1;
+  const int64_t want = (2 * num_sms() + tiles - 1) / tiles;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, T / 1024)));
+}
+
+void splitk_reduce(const float* partial, int chunks, int64_t rows, int64_t cols, void* out, int64_t ldo,
+                   bool out_fp32, bool accumulate, cudaStream_t stream) {
+  const int64_t total = rows * cols;
+  if (total == 0) return;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(4 * num_sms(), (total + 255) / 256)));
+  splitk_reduce_kernel<<<grid, 256, 0, stream>>>(partial, chunks, static_cast<int>(rows), static_cast<int>(cols), out,
+                                                 ldo, out_fp32 ? 1 : 0, accumulate ? 1 : 0);
+  check_cuda(cudaGetLastError(), "splitk_reduce");
+}
+
 int gemm_status(bool clear) { return read_status_word(clear); }
 
 }  // namespace qw

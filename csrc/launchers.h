@@ -42,6 +42,9 @@ void moe_gate_up_dgrad(const bf16* dgu, const bf16* w_gate_up, const int* counts
 void moe_wgrad(const bf16* a, const bf16* b, const int* counts, const int* offsets, int64_t R, int64_t E, int segments,
                int64_t M, int64_t N, void* out, bool out_fp32, bool accumulate, float alpha, cudaStream_t stream);
 int gemm_status(bool clear);
+int wgrad_split(int64_t T, int64_t N, int64_t K);
+void splitk_reduce(const float* partial, int chunks, int64_t rows, int64_t cols, void* out, int64_t ldo,
+                   bool out_fp32, bool accumulate, cudaStream_t stream);
 
 // ---- norm_rope.cu ----
 void norm_fwd(const bf16* x, const bf16* delta, bf16* x_out, const float* w, const float* b, bf16* y, float* mean,
@@ -204,6 +207,9 @@ void decode_combine_norm(const bf16* x, const int64_t* tokens, const bf16* tok_e
                          cudaStream_t stream, const float* parts = nullptr, const int* part_step = nullptr,
                          int part_layer = 0, int part_layers = 1, int part_world = 1, int part_tstride = 0);
 int decode_status(bool clear);
+// bf16 copy of int4 (fmt 2, grouped fp16 scales) / int8 (fmt 1, per-row fp16 scale) weight rows
+void dequant_rows(const void* q, const void* scales, int64_t rows, int K, int group, int fmt, bf16* out,
+                  cudaStream_t stream);
 // expert-parallel decode exchange (ep_decode.cu)
 void ep_decode_tick(int* step, cudaStream_t stream);
 void ep_decode_push(const bf16* y, const int* slot, const float* top_w, int k, int T, int H, int tstride,

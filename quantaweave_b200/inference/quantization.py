@@ -127,7 +127,9 @@ def quantize_moe(moe, bits: int, group_size: Optional[int]) -> tuple[int, int]:
     moe.register_buffer("q_down", q_d.to(device))
     moe.register_buffer("s_down", s_d.to(device))
     moe.quant = {"bits": bits, "group_in": g_in, "group_down": g_dn}
-    moe.kernel = "loop"
+    # training and the per-expert path dequantise one expert at a time; without gradients on CUDA the layer expands
+    # the packed stacks to bf16 in one kernel and runs the tcgen05 grouped GEMMs ("auto")
+    moe.kernel = "auto"
     after = sum(t.numel() * t.element_size() for t in (q_gu, s_gu, q_d, s_d))
     return before, after
 

@@ -181,7 +181,7 @@ class TopKMoE(nn.Module):
         batch, sequence, width = hidden.shape
         flat = hidden.reshape(-1, width)
         num_tokens = flat.size(0)
-        if hidden.is_cuda and self._native_ok():
+        if hidden.is_cuda and (self._native_ok() or self._quantized_native_ok()):
             from ..ops import moe as moe_ops
 
             self._last_counts = None
@@ -217,6 +217,18 @@ class TopKMoE(nn.Module):
             counts = torch.bincount(top_indices.reshape(-1), minlength=self.num_experts)
         assignments = counts.float() / top_indices.numel()
         return self.num_experts * (importance * assignments).sum()
+
+    def _quantized_native_ok(self) -> bool:
+        """Quantised experts on many tokens at once (prefill, evaluation): without gradients, the packed weights are
+        expanded to bf16 by one kernel and the tcgen05 grouped GEMMs run over all routed rows."""
+        if getattr(self, "quant", None) is None or torch.is_grad_enabled() or self.tp_size > 1:
+            return False
+        if self.kernel == "loop" or self.static_dispatch or self.profile_experts or getattr(self, "lora", None):
+            return False
+        from ..ops import native_required
+
+        native_required()
+        return True
 
     def _native_ok(self) -> bool:
         if self.kernel == "loop" or self.static_dispatch or self.profile_experts:

@@ -160,11 +160,32 @@ class _MoEFn(torch.autograd.Function):
         return dx, d_router.to(rw_dtype), d_w_gate_up, d_w_down, None, None, None, None, None
 
 
+def dequantized_stacks(moe) -> tuple[Tensor, Tensor]:
+    """bf16 ``w_gate_up [E, 2F, H]`` and ``w_down [E, H, F]`` expanded from a quantised MoE's packed buffers by the
+    ``dequant_rows`` kernel (int4 groups or int8 rows with fp16 scales)."""
+    C = ext()
+    q = moe.quant
+    fmt = 2 if q["bits"] == 4 else 1
+    E, F2 = moe.q_gate_up.shape[0], moe.q_gate_up.shape[1]
+    H = moe.hidden_size
+    F = F2 // 2
+    w_gate_up = torch.empty(E, F2, H, device=moe.q_gate_up.device, dtype=torch.bfloat16)
+    w_down = torch.empty(E, H, F, device=moe.q_down.device, dtype=torch.bfloat16)
+    C.dequant_rows(moe.q_gate_up, moe.s_gate_up, H, q["group_in"] if fmt == 2 else H, fmt, w_gate_up)
+    C.dequant_rows(moe.q_down, moe.s_down, F, q["group_down"] if fmt == 2 else F, fmt, w_down)
+    return w_gate_up, w_down
+
+
 def moe_forward(moe, flat: Tensor, capacity: int):
-    """Native forward of ``models.moe.TopKMoE``; returns (output, probs, top_idx, overflow, kept_counts, dropped)."""
+    """Native forward of ``models.moe.TopKMoE``; returns (output, probs, top_idx, overflow, kept_counts, dropped).
+    Quantised experts (inference only) are expanded to bf16 first."""
     recompute = getattr(moe, "recompute_activations", False)
+    if getattr(moe, "quant", None) is not None:
+        w_gate_up, w_down = dequantized_stacks(moe)
+    else:
+        w_gate_up, w_down = moe.w_gate_up, moe.w_down
     out, probs, top_idx, counts, kept, meta, route_row = _MoEFn.apply(
-        flat, moe.router.weight, moe.w_gate_up, moe.w_down, int(capacity), moe.top_k, float(moe.router_temperature),
+        flat, moe.router.weight, w_gate_up, w_down, int(capacity), moe.top_k, float(moe.router_temperature),
         moe.expert_bias, recompute)
     moe._last_counts = counts
     overflow = meta[1].long()

@@ -189,12 +189,16 @@ class _SlotDispatch(torch.autograd.Function):
             transport.publish()
             transport.wait_returned()
             C.moe_combine(y_back, plan.route_row, plan.top_w, None, k, out)
+            if moe.tp_size > 1:  # EP x TP grid: each rank's experts hold a slice of F, so the outputs are partial
+                dist.all_reduce(out, group=ep.tp_group)
         else:
             y = torch.empty(rows, H, device=dev, dtype=torch.bfloat16)
             C.moe_down_fwd(h, w_down, recv_counts, offsets, y)
             del h
             y_back = transport.exchange(y)
             C.moe_combine(y_back, plan.route_row, plan.top_w, None, k, out)
+            if moe.tp_size > 1:
+                dist.all_reduce(out, group=ep.tp_group)
         saved = [x, router_weight, w_gate_up, w_down, plan.probs, plan.top_idx, plan.top_w, plan.meta, plan.route_row,
                  row_token, recv_counts, offsets, x_recv, w_recv]
         if gu is not None:
@@ -247,6 +251,8 @@ class _SlotDispatch(torch.autograd.Function):
         partial = torch.zeros(rows, tiles, device=dev, dtype=torch.float32)
         C.moe_down_bwd(dy_recv, w_down, recv_counts, offsets, gu, w_recv, dgu, hw, partial)
         del gu
+        if moe.tp_size > 1:  # <dH, H> per row summed over the F slices of the tensor-parallel row of ranks
+            dist.all_reduce(partial, group=ep.tp_group)
         d_w_down = torch.empty_like(w_down)
         C.moe_wgrad(dy_recv, hw, recv_counts, offsets, d_w_down, False, world, 1.0)
         del hw, dy_recv
@@ -280,7 +286,12 @@ class _SlotDispatch(torch.autograd.Function):
         d_router = torch.empty(moe.num_experts, H, device=dev, dtype=torch.float32)
         C.router_dw(d_logits, x, d_router, False, workspace)
         dx = torch.empty(T, H, device=dev, dtype=torch.bfloat16)
-        C.moe_combine_grad(dx_back, route_row, dx_router, k, dx)
+        if moe.tp_size > 1:  # the expert part of dx is partial over the F slices; the router part is replicated
+            C.moe_combine_grad(dx_back, route_row, None, k, dx)
+            dist.all_reduce(dx, group=ep.tp_group)
+            dx += dx_router.to(torch.bfloat16)
+        else:
+            C.moe_combine_grad(dx_back, route_row, dx_router, k, dx)
         return dx, d_router.to(router_weight.dtype), d_w_gate_up, d_w_down, None, None
 
 
@@ -349,8 +360,13 @@ class ExpertParallelMoE(TopKMoE):
             self._offsets_cache[key] = torch.arange(groups, device=device, dtype=torch.int32) * slot
         return self._offsets_cache[key]
 
+    def _native_ok(self) -> bool:
+        # the single-GPU native MoE would run only this rank's experts with no exchange: the slot dispatch below is
+        # the native path here, and every other case takes the reference exchange algorithm (``_execute``)
+        return False
+
     def forward(self, hidden: Tensor, token_domains: Optional[Tensor] = None, num_domains: int = 0):
-        if not (hidden.is_cuda and self.kernel != "loop" and self.tp_size == 1 and not self.static_dispatch
+        if not (hidden.is_cuda and self.kernel != "loop" and not self.static_dispatch
                 and not self.profile_experts and not self.simulated_cost_per_row and not self.measure_load):
             return super().forward(hidden, token_domains, num_domains)
         from ..ops import native_required

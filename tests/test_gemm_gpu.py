@@ -42,8 +42,10 @@ def test_linear_fwd(M, N, K):
     assert C.read_status(True) == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (130, 1024, 320)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (130, 1024, 320), (8200, 1024, 1024), (65536, 1024, 256)])
 def test_linear_dgrad_wgrad(M, N, K):
+    """The last two shapes have too few output tiles to fill the GPU, so the weight gradient is split over token
+    chunks and reduced in a fixed order (fp32 partials)."""
     C = _ext()
     g = torch.Generator(device="cuda").manual_seed(1)
     dy = torch.randn(M, N, device="cuda", generator=g).bfloat16()
@@ -57,6 +59,9 @@ def test_linear_dgrad_wgrad(M, N, K):
     _close(dw, dy.float().t() @ x.float(), 1e-3)
     C.linear_wgrad(dy, x, dw, True)  # accumulate
     _close(dw, 2 * dy.float().t() @ x.float(), 1e-3)
+    dwb = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)  # bf16 gradient output (the split path casts)
+    C.linear_wgrad(dy, x, dwb, False)
+    _close(dwb, dy.float().t() @ x.float(), 1e-2)
     assert C.read_status(True) == 0
 
 

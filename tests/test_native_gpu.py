@@ -319,3 +319,21 @@ def test_peer_flag_timeout_becomes_comm_timeout_error():
     check_device_status()  # the word was cleared
     x = torch.ones(4, device="cuda")
     assert float((x * 2).sum()) == 8.0  # the context still works
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_quantized_moe_prefill_on_tensor_cores_matches_per_expert_path(bits):
+    """Without gradients on CUDA, a quantised MoE expands its packed experts to bf16 with one kernel and runs the
+    tcgen05 grouped GEMMs; its output matches the per-expert dequantise-and-multiply path in fp32."""
+    from quantaweave_b200.inference.quantization import quantize_moe
+
+    moe = _moe_module(E=8, H=256, F_=512, k=2, cf=0.0).cuda()
+    quantize_moe(moe, bits, 128 if bits == 4 else None)
+    x = torch.randn(3, 100, 256, device="cuda").bfloat16()
+    with torch.no_grad():
+        assert moe._quantized_native_ok()
+        fast = moe(x)[0].float()
+        moe.kernel = "loop"
+        ref = moe(x.float())[0].float()
+    _close(fast, ref, 3e-2)
+    _status_ok()

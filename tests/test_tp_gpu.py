@@ -198,3 +198,100 @@ def test_sequence_parallel_native_matches_single_gpu(fused):
             raise AssertionError(f"rank {rank} failed:\n{payload}")
     for p in procs:
         p.join(timeout=60)
+
+
+def _grid_case(rank, world):
+    """The EP x TP grid at tensor-parallel 2 on the native kernels: attention heads and every expert's F dimension
+    split over the two GPUs (one expert-parallel rank), against the single-GPU model with the full weights."""
+    from quantaweave_b200 import QuantaWeaveConfig, QuantaWeaveMoEForCausalLM
+    from quantaweave_b200.ops import ext
+    from quantaweave_b200.parallel.expert_parallel import clip_grad_norm_parallel, init_expert_parallel, sync_gradients
+    from quantaweave_b200.parallel.tensor_parallel import is_tp_sharded, shard_state_dict, shard_tensor
+    from quantaweave_b200.training.native import prepare_model
+
+    torch.cuda.set_device(rank)
+    cfg = QuantaWeaveConfig(vocab_size=512, hidden_size=256, layers=2, ffn_size=512, num_experts=4, top_k=2,
+                            attention_heads=4, kv_heads=2, max_sequence_length=129, capacity_factor=1.25,
+                            norm_type="rmsnorm", position_embedding="rope", attention_bias=False, init_std=0.02)
+    torch.manual_seed(0)
+    full = QuantaWeaveMoEForCausalLM(cfg).cuda()
+    prepare_model(full, "bf16")
+    ctx = init_expert_parallel("cuda", world)  # tensor-parallel over both ranks, expert-parallel size 1
+    model = QuantaWeaveMoEForCausalLM(cfg, expert_parallel=ctx).cuda()
+    prepare_model(model, "bf16")
+    model.load_state_dict(shard_state_dict(full.state_dict(), ctx.tp_rank, ctx.tp_size, cfg))
+    batch = torch.randint(0, cfg.vocab_size, (2, 129), generator=torch.Generator().manual_seed(1)).cuda()
+    out = model(batch, labels=batch, return_logits=False)
+    out["loss"].backward()
+    sync_gradients(model, ctx)
+    norm = float(clip_grad_norm_parallel(model, ctx, 1e9))
+    ref = full(batch, labels=batch, return_logits=False)
+    ref["loss"].backward()
+    ref_norm = float(torch.sqrt(sum(p.grad.double().pow(2).sum() for p in full.parameters())))
+    assert abs(float(out["loss"]) - float(ref["loss"])) < 2e-2, (float(out["loss"]), float(ref["loss"]))
+    assert abs(norm - ref_norm) < 5e-2 * ref_norm, (norm, ref_norm)
+    qf = cfg.attention_heads / (cfg.attention_heads + 2 * cfg.num_kv_heads)
+    full_grads = {}
+    for name, p in full.named_parameters():  # expert stacks -> per-expert keys so they slice like the checkpoint
+        if name.endswith("w_gate_up"):
+            f = cfg.ffn_size
+            for e in range(cfg.num_experts):
+                full_grads[name.replace("w_gate_up", f"experts.{e}.gate.weight")] = p.grad[e, :f].float()
+                full_grads[name.replace("w_gate_up", f"experts.{e}.up.weight")] = p.grad[e, f:].float()
+        elif name.endswith("w_down"):
+            for e in range(cfg.num_experts):
+                full_grads[name.replace("w_down", f"experts.{e}.down.weight")] = p.grad[e].float()
+        else:
+            full_grads[name] = p.grad.float()
+    for name, p in model.named_parameters():
+        if name.endswith(("w_gate_up", "w_down")):
+            f = cfg.ffn_size // world
+            for e in range(cfg.num_experts):
+                if name.endswith("w_gate_up"):
+                    pieces = {"gate": p.grad[e, :f], "up": p.grad[e, f:]}
+                else:
+                    pieces = {"down": p.grad[e]}
+                for proj, got in pieces.items():
+                    key = name.replace("w_gate_up" if proj != "down" else "w_down", f"experts.{e}.{proj}.weight")
+                    expect = shard_tensor(key, full_grads[key], rank, world, qf)
+                    rel = float((got.float() - expect).norm() / (expect.norm() + 1e-12))
+                    assert rel < 0.1, (key, rel)
+            continue
+        expect = full_grads[name]
+        if is_tp_sharded(name):
+            expect = shard_tensor(name, expect, rank, world, qf)
+        rel = float((p.grad.float() - expect).norm() / (expect.norm() + 1e-12))
+        assert rel < (0.1 if p.dim() >= 2 else 0.3), (name, rel)
+    assert ext().read_status(True) == 0
+    return float(out["loss"])
+
+
+def _grid_worker(rank, world, port, queue):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), QW_PG_TIMEOUT_S="120", NCCL_NVLS_ENABLE="0",
+                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
+    try:
+        queue.put((rank, "ok", _grid_case(rank, world)))
+    except Exception:  # noqa: BLE001
+        queue.put((rank, "error", traceback.format_exc()))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_tensor_parallel_experts_on_the_grid_match_single_gpu():
+    world = 2
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_grid_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for _ in range(world):
+        rank, status, payload = queue.get(timeout=600)
+        if status != "ok":
+            for p in procs:
+                p.join(timeout=30)
+            raise AssertionError(f"rank {rank} failed:\n{payload}")
+    for p in procs:
+        p.join(timeout=60)
