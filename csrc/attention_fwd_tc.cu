@@ -285,11 +285,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (masked && (key > q || key >= p.S)) v[i] = -INFINITY;
         mx = fmaxf(mx, v[i]);
       }
-      // O_g += P_g(j-1) V_{j-1} must have finished before its P buffer is rewritten or O_g is rescaled
-      if (j > 0 && !__all_sync(0xffffffffu, mbar_sleep_wait(&o_full[g], (j - 1) & 1, kTimeoutAccum))) {
-        ok = false;
-        break;
-      }
       // the reference maximum moves only when some row of the warp grew by more than 2^8 (warp-uniform decision:
       // TMEM access is warp-collective); rows whose maximum barely moved then get a factor close to 1
       float factor = 1.f;
@@ -302,22 +297,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = m_new;
         rescale = true;
       }
+      // probabilities in registers first (two exponentials per instruction in half precision: the exponent lies in
+      // [-inf, 8] thanks to the lazy rescale, so the f16 input keeps ~11 bits where the probabilities are large,
+      // and the bf16 probabilities need 8), so the wait for the previous P V below overlaps this work
       float tile_sum = 0.f;
+      uint32_t pk[kTile / 2];
 #pragma unroll
-      for (int c8 = 0; c8 < kTile / 8; ++c8) {  // 8 keys -> one 16-byte chunk of P
-        uint32_t w[4];
+      for (int i = 0; i < kTile / 2; ++i) {
+        const __half2 e = h2exp2(__floats2half2_rn(v[2 * i] - m_ref, v[2 * i + 1] - m_ref));
+        const float2 f = __half22float2(e);  // exp2(-inf) = 0 for masked keys
+        tile_sum += f.x + f.y;
+        pk[i] = pack_bf16(f.x, f.y);
+      }
+      // O_g += P_g(j-1) V_{j-1} must have finished before its P buffer is rewritten or O_g is rescaled
+      if (j > 0 && !__all_sync(0xffffffffu, mbar_sleep_wait(&o_full[g], (j - 1) & 1, kTimeoutAccum))) {
+        ok = false;
+        break;
+      }
 #pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) {
-          // two exponentials per instruction in half precision: the exponent lies in [-inf, 8] (lazy rescale), so
-          // the f16 input keeps ~11 bits where the probabilities are large, and the bf16 probabilities need 8
-          const __half2 e = h2exp2(__floats2half2_rn(v[8 * c8 + 2 * e2] - m_ref, v[8 * c8 + 2 * e2 + 1] - m_ref));
-          const float2 f = __half22float2(e);  // exp2(-inf) = 0 for masked keys
-          tile_sum += f.x + f.y;
-          w[e2] = pack_bf16(f.x, f.y);
-        }
+      for (int c8 = 0; c8 < kTile / 8; ++c8) {  // 8 keys -> one 16-byte chunk of the K-major swizzled P tile
         const int box = c8 / 8;
         const int swz = (c8 % 8) ^ (row & 7);
-        *reinterpret_cast<uint4*>(prow + box * (kTile * 128) + swz * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(prow + box * (kTile * 128) + swz * 16) =
+            make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
       }
       l_sum = fmaf(l_sum, factor, tile_sum);
       if (rescale) {  // O_g to the new reference before the next P V accumulates into it
