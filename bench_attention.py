@@ -55,7 +55,7 @@ def main() -> None:
     bwd.sort()
     f_ms, b_ms = fwd[len(fwd) // 2], bwd[len(bwd) // 2]
     flops = 4.0 * B * h * S * S * d / 2
-    print(json.dumps({"forward_path": os.environ.get("QW_ATTN_FWD", "tcgen05" if d == 64 else "mma"),
+    print(json.dumps({"forward_path": os.environ.get("QW_ATTN_FWD", "tcgen05" if d in (64, 128) else "mma"),
                       "backward_path": os.environ.get("QW_ATTN_BWD", "tcgen05"), "batch": B, "seq": S, "heads": h,
                       "kv_heads": hkv, "head_dim": d, "fwd_ms": round(f_ms, 4), "bwd_ms": round(b_ms, 4),
                       "fwd_tflops": round(flops / f_ms / 1e9, 1), "bwd_tflops": round(2.5 * flops / b_ms / 1e9, 1)}))

@@ -82,11 +82,36 @@ def cases(torch, C):
     }
 
 
+def trace_summary(torch, C, run) -> dict:
+    """Median per-tile phase lengths (SM clocks) of CTA 0 over one launch: producer streaming time, the issuer's wait
+    for a free accumulator, its wait for the first k-block, its k-loop, the epilogue, and the tile period."""
+    buf = torch.zeros(64 * 8, dtype=torch.int64, device="cuda")
+    C.gemm_trace(buf)
+    run()
+    torch.cuda.synchronize()
+    C.gemm_trace(None)
+    t = buf.view(64, 8).cpu().tolist()
+    t = [row for row in t if row[3] and row[7]]
+    med = lambda xs: statistics.median(xs) if xs else None  # noqa: E731
+    return {
+        "tiles": len(t),
+        "producer": med([r[1] - r[0] for r in t]),
+        "acc_wait": med([r[3] - r[2] for r in t]),
+        "first_kblock_wait": med([r[4] - r[3] for r in t]),
+        "mainloop": med([r[5] - r[3] for r in t]),
+        "epilogue": med([r[7] - r[6] for r in t]),
+        "epilogue_wait": med([r[6] - r[5] for r in t]),
+        "period": med([b[5] - a[5] for a, b in zip(t, t[1:])]),
+    }
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--case", default="all")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--trace", action="store_true",
+                    help="also print per-tile SM-clock timestamps of CTA 0 (producer, MMA issuer, epilogue)")
     args = ap.parse_args()
     import torch
 
@@ -110,6 +135,8 @@ def main() -> None:
             end.synchronize()
             times.append(start.elapsed_time(end))
         ms = statistics.median(times)
+        if args.trace:
+            print(json.dumps({"case": name, "trace": trace_summary(torch, C, run)}), flush=True)
         tflops = flops / ms / 1e9
         print(json.dumps({"case": name, "ms": round(ms, 4), "tflops": round(tflops, 1),
                           "fraction_of_measured_bf16": round(tflops / peak, 3)}), flush=True)

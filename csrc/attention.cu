@@ -498,12 +498,13 @@ void set_smem(K kernel, size_t bytes) {
 void flash_attn_fwd(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, int64_t ldv, bf16* o,
                     int64_t ldo, float* lse, int B, int S, int Hq, int Hkv, int D, float scale, cudaStream_t stream) {
   if (B == 0 || S == 0) return;
-  // head_dim 64 runs on the tcgen05 kernel (attention_fwd_tc.cu); QW_ATTN_FWD=mma keeps the mma.sync kernel below
+  // head_dim 64 and 128 run on the tcgen05 kernel (attention_fwd_tc.cu); QW_ATTN_FWD=mma keeps the mma.sync kernels
+  // below (and head_dim 32 always uses them)
   static const bool use_mma = [] {
     const char* e = std::getenv("QW_ATTN_FWD");
     return e && std::string(e) == "mma";
   }();
-  if (D == 64 && !use_mma) {
+  if ((D == 64 || D == 128) && !use_mma) {
     flash_attn_fwd_tc(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hkv, D, scale, stream);
     return;
   }

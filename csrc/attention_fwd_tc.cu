@@ -1,15 +1,16 @@
-// Causal flash-attention forward on the Blackwell tensor cores (head_dim 64): tcgen05.mma with TMEM accumulators,
-// Q/K/V staged by TMA into 128-byte-swizzled shared memory, grouped-query attention read in place from the packed
-// QKV rows.
+// Causal flash-attention forward on the Blackwell tensor cores (head_dim 64 and 128): tcgen05.mma with TMEM
+// accumulators, Q/K/V staged by TMA into 128-byte-swizzled shared memory, grouped-query attention read in place from
+// the packed QKV rows.
 //
-// One CTA owns 256 queries of one (batch, q-head) as two 128-row Q tiles, and walks the 128-key K/V tiles up to the
-// diagonal. Each Q tile has its own softmax warpgroup, so while one group turns its scores into probabilities the
-// tensor core works on the other group's tiles (ping-pong):
+// One CTA owns 256 queries of one (batch, q-head) as two 128-row Q tiles, and walks the KT-key K/V tiles up to the
+// diagonal (KT = 128 keys at head_dim 64; 64 keys at head_dim 128, so that three K/V stages, both Q tiles and both
+// P tiles still fit in shared memory). Each Q tile has its own softmax warpgroup, so while one group turns its
+// scores into probabilities the tensor core works on the other group's tiles (ping-pong):
 //
-//   S_g  = Q_g K_j^T                       (TMEM, 128 x 128 fp32 per group)
+//   S_g  = Q_g K_j^T                       (TMEM, 128 x KT fp32 per group)
 //   P_g  = exp2(S_g * scale*log2e - m_g)   (softmax warps, packed f16x2 exponentials -> bf16, K-major swizzled
 //                                           shared memory)
-//   O_g += P_g V_j                          (TMEM, 128 x 64 fp32 per group, accumulated by the tensor core)
+//   O_g += P_g V_j                          (TMEM, 128 x D fp32 per group, accumulated by the tensor core)
 //
 // Lazy rescaling: m_g is the row maximum the accumulator O_g is expressed against. A new tile only moves it when its
 // own maximum exceeds m_g by more than 2^8 (so probabilities stay below 256, well inside bf16 and fp32 range);
@@ -27,7 +28,7 @@
 //               tile are issued.
 //   warps 2-5   softmax group 0 (Q tile 0), warps 6-9 group 1 (Q tile 1). Warp w reads TMEM lanes 32*(w%4)..+31.
 //
-// TMEM columns: [0,128) S_0, [128,256) S_1, [256,320) O_0, [320,384) O_1.
+// TMEM columns: [0,KT) S_0, [KT,2KT) S_1, then O_0 and O_1 (D columns each): 384 of the 512 at either head_dim.
 // Every mbarrier wait is bounded (common.cuh): on a timeout all roles stop, in-flight TMA loads and MMAs are waited
 // for (bounded), TMEM is freed and the status word records the cause.
 #include <algorithm>
@@ -43,7 +44,7 @@ CUtensorMap make_bf16_map_3d(const void* ptr, int64_t inner, int64_t rows, int64
 
 namespace attn_fwd_tc {
 
-constexpr int kTile = 128;                    // queries per Q tile and keys per K/V tile
+constexpr int kTile = 128;                    // queries per Q tile
 constexpr int kGroups = 2;                    // Q tiles per CTA, one softmax warpgroup each
 constexpr int kThreads = 64 + 128 * kGroups;  // TMA warp, MMA warp, softmax warpgroups
 constexpr int kStages = 3;
@@ -54,15 +55,22 @@ constexpr float kRescaleLog2 = 8.f;  // move the reference maximum only when a r
 
 template <int D>
 struct Layout {
+  static constexpr int KT = D == 64 ? 128 : 64;             // keys per K/V tile
   static constexpr int kBoxes = D / 64;                      // 64-wide (128-byte) boxes per row
-  static constexpr int kTileBytes = kBoxes * kTile * 128;    // one [128 x D] bf16 tile
-  static constexpr int kPBytes = 2 * kTile * 128;            // one [128 x 128] bf16 P tile: two 64-key boxes
+  static constexpr int kQBytes = kBoxes * kTile * 128;       // one [128 x D] bf16 Q tile
+  static constexpr int kKVBytes = kBoxes * KT * 128;         // one [KT x D] bf16 K or V tile
+  static constexpr int kPBytes = (KT / 64) * kTile * 128;    // one [128 x KT] bf16 P tile: 64-key boxes
   static constexpr int kQ = 0;
-  static constexpr int kKV = kGroups * kTileBytes;           // stages of [K | V]
-  static constexpr int kP = kKV + kStages * 2 * kTileBytes;
-  static constexpr int kBar = kP + kGroups * kPBytes;
+  static constexpr int kKV = kGroups * kQBytes;              // stages of [K | V]
+  static constexpr int kP = kKV + kStages * 2 * kKVBytes;
+  static constexpr int kOnes = kP + kGroups * kPBytes;      // [16 x KT] K-major B operand: row 0 ones, rows 1-15 zero
+  static constexpr int kOnesBytes = (KT / 64) * 16 * 128;
+  static constexpr int kBar = kOnes + kOnesBytes;
   static constexpr int kTotal = kBar + 256 + 1024;           // barriers, and slack to align the base to 1 KB
-  static constexpr int kTmemO = 2 * kTile;                   // first column of the partial outputs
+  static constexpr int kTmemO = 2 * KT;                      // first column of the partial outputs
+  static constexpr int kTmemL = kTmemO + kGroups * D;        // row sums: P times the ones row, 16 columns per group
+  static_assert(kTmemL + kGroups * 16 <= kTmemCols, "TMEM columns");
+  static_assert(kTotal <= 227 * 1024, "shared memory per CTA");
 };
 
 struct Params {
@@ -79,16 +87,34 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// (2^x, 2^y) through one packed half-precision exponential (ex2.approx.f16x2), widened back to fp32
+__device__ __forceinline__ float2 exp2_f16x2(float x, float y) {
+  const __half2 h = __floats2half2_rn(x, y);
+  uint32_t e;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(*reinterpret_cast<const uint32_t*>(&h)));
+  return __half22float2(*reinterpret_cast<const __half2*>(&e));
+}
+
+// K/V tiles of KT keys that the 128 queries from q_start see (causal: keys up to the last query of the tile)
+template <int KT>
 __device__ __forceinline__ int kv_tiles_of(const Params& p, int q_start) {
   if (q_start >= p.S) return 0;
-  return min((p.S + kTile - 1) / kTile, q_start / kTile + 1);
+  return (min(p.S, q_start + kTile) + KT - 1) / KT;
 }
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __maxnreg__(200)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v, Params p) {
   using L = Layout<D>;
+  constexpr int KT = L::KT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::kBar);
@@ -106,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = blockIdx.x / p.Hq, hq = blockIdx.x % p.Hq;
   const int hk = hq / (p.Hq / p.Hkv);
   const int q0 = (gridDim.y - 1 - blockIdx.y) * (kTile * kGroups);  // the latest queries see the most keys: first
-  const int n0 = kv_tiles_of(p, q0), n1 = kv_tiles_of(p, q0 + kTile);
+  const int n0 = kv_tiles_of<KT>(p, q0), n1 = kv_tiles_of<KT>(p, q0 + kTile);
   const int nk = max(n0, n1);
 
   if (threadIdx.x == 0) {
@@ -125,6 +151,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
+  // the ones operand of the row-sum MMA: row 0 of each 64-key box is all ones (the swizzle only permutes 16-byte
+  // chunks inside a row, so a row of ones needs none), rows 1-15 are zero
+  for (int i = threadIdx.x; i < L::kOnesBytes / 16; i += kThreads) {
+    const uint32_t one = (i % 128) < 8 ? 0x3F803F80u : 0u;
+    reinterpret_cast<uint4*>(smem + L::kOnes)[i] = make_uint4(one, one, one, one);
+  }
+  fence_async_smem();
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_k);
@@ -141,12 +174,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // phase of the last load issued into each stage (-1: none), packed 2 bits per stage to stay in a register
       uint32_t issued = 0;  // bit 2s: stage s used, bit 2s+1: its phase
-      mbar_arrive_expect_tx(q_full, kGroups * L::kTileBytes);
+      mbar_arrive_expect_tx(q_full, kGroups * L::kQBytes);
 #pragma unroll
       for (int g = 0; g < kGroups; ++g)
 #pragma unroll
         for (int c = 0; c < L::kBoxes; ++c)
-          tma_load_3d(smem + L::kQ + g * L::kTileBytes + c * kTile * 128, &map_q, q_full, hq * D + c * 64,
+          tma_load_3d(smem + L::kQ + g * L::kQBytes + c * kTile * 128, &map_q, q_full, hq * D + c * 64,
                       q0 + g * kTile, b);
       for (int j = 0; j < nk; ++j) {
         const int st = j % kStages;
@@ -155,13 +188,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
           break;
         }
-        mbar_arrive_expect_tx(&kv_full[st], 2 * L::kTileBytes);
+        mbar_arrive_expect_tx(&kv_full[st], 2 * L::kKVBytes);
         issued = (issued & ~(3u << (2 * st))) | ((1u | (ph << 1)) << (2 * st));
-        uint8_t* sk = smem + L::kKV + st * 2 * L::kTileBytes;
+        uint8_t* sk = smem + L::kKV + st * 2 * L::kKVBytes;
 #pragma unroll
         for (int c = 0; c < L::kBoxes; ++c) {
-          tma_load_3d(sk + c * kTile * 128, &map_k, &kv_full[st], hk * D + c * 64, j * kTile, b);
-          tma_load_3d(sk + L::kTileBytes + c * kTile * 128, &map_v, &kv_full[st], hk * D + c * 64, j * kTile, b);
+          tma_load_3d(sk + c * KT * 128, &map_k, &kv_full[st], hk * D + c * 64, j * KT, b);
+          tma_load_3d(sk + L::kKVBytes + c * KT * 128, &map_v, &kv_full[st], hk * D + c * 64, j * KT, b);
         }
       }
       // drain: every load issued above has landed before the CTA may exit
@@ -172,20 +205,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t id_s = idesc_bf16(kTile, kTile, false, false);
+      constexpr uint32_t id_s = idesc_bf16(kTile, KT, false, false);
       constexpr uint32_t id_o = idesc_bf16(kTile, D, false, true);
+      constexpr uint32_t id_l = idesc_bf16(kTile, 16, false, false);
+      const uint32_t sones = smem_u32(smem + L::kOnes);
       int ns0 = 0, ns1 = 0;  // next S to issue, per group
       int no0 = 0, no1 = 0;  // next O' to issue, per group
       int released = 0;      // K/V tiles whose stage went back to the producer
       auto issue_s = [&](int g, int j) {
         const int st = j % kStages;
         tc_fence_after();
-        const uint32_t sq = smem_u32(smem + L::kQ + g * L::kTileBytes);
-        const uint32_t sk = smem_u32(smem + L::kKV + st * 2 * L::kTileBytes);
+        const uint32_t sq = smem_u32(smem + L::kQ + g * L::kQBytes);
+        const uint32_t sk = smem_u32(smem + L::kKV + st * 2 * L::kKVBytes);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k / 4) * (kTile * 128) + (k % 4) * 32;
-          umma_bf16(tmem + g * kTile, smem_desc_sw128(sq + off, 16, 1024), smem_desc_sw128(sk + off, 16, 1024),
+        for (int k = 0; k < D / 16; ++k) {  // 16 head-dim columns per MMA: 32 bytes inside a 128-byte box
+          const uint32_t oq = (k / 4) * (kTile * 128) + (k % 4) * 32;
+          const uint32_t ok_ = (k / 4) * (KT * 128) + (k % 4) * 32;
+          umma_bf16(tmem + g * KT, smem_desc_sw128(sq + oq, 16, 1024), smem_desc_sw128(sk + ok_, 16, 1024),
                     id_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[g]);
@@ -194,14 +230,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % kStages;
         tc_fence_after();
         const uint32_t sp = smem_u32(smem + L::kP + g * L::kPBytes);
-        const uint32_t sv = smem_u32(smem + L::kKV + st * 2 * L::kTileBytes + L::kTileBytes);
+        const uint32_t sv = smem_u32(smem + L::kKV + st * 2 * L::kKVBytes + L::kKVBytes);
 #pragma unroll
-        for (int k = 0; k < kTile / 16; ++k) {
-          // A = P (K-major, keys in two 64-wide boxes); B = V read MN-major: 16 keys = 16 rows of 128 B per step,
-          // 64-wide head-dim blocks one box apart
+        for (int k = 0; k < KT / 16; ++k) {
+          // A = P (K-major, keys in 64-wide boxes); B = V read MN-major: 16 keys = 16 rows of 128 B per step,
+          // 64-wide head-dim blocks one box (KT rows) apart
           const uint64_t a = smem_desc_sw128(sp + (k / 4) * (kTile * 128) + (k % 4) * 32, 16, 1024);
-          const uint64_t bv = smem_desc_sw128(sv + k * 2048, kTile * 128, 1024);
+          const uint64_t bv = smem_desc_sw128(sv + k * 2048, KT * 128, 1024);
           umma_bf16(tmem + L::kTmemO + g * D, a, bv, id_o, (j > 0 || k > 0) ? 1u : 0u);
+          // l_g += P_g 1: the row sums, from the same A operand and the K-major ones row
+          const uint64_t b1 = smem_desc_sw128(sones + (k / 4) * (16 * 128) + (k % 4) * 32, 16, 1024);
+          umma_bf16(tmem + L::kTmemL + g * 16, a, b1, id_l, (j > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&o_full[g]);
       };
@@ -257,34 +296,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = q_start + row;
     const int n = g == 0 ? n0 : n1;
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
-    const uint32_t ts = tmem + lane_off + g * kTile;
+    const uint32_t ts = tmem + lane_off + g * KT;
     const uint32_t to = tmem + lane_off + L::kTmemO + g * D;
+    const uint32_t tl = tmem + lane_off + L::kTmemL + g * 16;
     uint8_t* prow = smem + L::kP + g * L::kPBytes + row * 128;
     const float sl2 = p.scale_log2;
-    float m_ref = -INFINITY;  // the maximum O_g is expressed against (base-2, scaled)
-    float l_sum = 0.f;        // row sum of the probabilities, relative to m_ref
+    float m_ref = -INFINITY;  // the maximum O_g and l_g are expressed against (base-2, scaled)
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
       if (!__all_sync(0xffffffffu, mbar_sleep_wait(&s_full[g], j & 1, kTimeoutAccum))) { ok = false; break; }
       tc_fence_after();
-      float v[kTile];
-      tmem_ld32_pair(ts, ts + 32, v, v + 32);
-      tmem_ld32_pair(ts + 64, ts + 96, v + 64, v + 96);
+      float v[KT];
+#pragma unroll
+      for (int c = 0; c < KT; c += 64) tmem_ld32_pair(ts + c, ts + c + 32, v + c, v + c + 32);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[g]);  // the issuer may compute the next scores into these columns
-      const int k0 = j * kTile;
-      // the diagonal tile and a tile past the end of the sequence need masking
-      const bool masked = (k0 + kTile > q_start) || (k0 + kTile > p.S);
-      float mx = -INFINITY;
+      const int k0 = j * KT;
+      // tiles that reach past the group's first query, and a tile past the end of the sequence, need masking; the
+      // others (all but one or two per row) take the loop below without any per-key test
+      if ((k0 + KT - 1 > q_start) || (k0 + KT > p.S)) {
+        const int lim = min(q + 1, p.S) - k0;  // keys [k0, k0 + lim) are visible to this row
 #pragma unroll
-      for (int i = 0; i < kTile; ++i) {
-        const int key = k0 + i;
-        v[i] *= sl2;
-        if (masked && (key > q || key >= p.S)) v[i] = -INFINITY;
-        mx = fmaxf(mx, v[i]);
+        for (int i = 0; i < KT; ++i)
+          if (i >= lim) v[i] = -INFINITY;
       }
+      // row maximum of the raw scores (the scale is positive), three at a time
+      float mx = v[0];
+#pragma unroll
+      for (int i = 1; i + 1 < KT; i += 2) mx = fmax3(mx, v[i], v[i + 1]);
+      mx = fmaxf(mx, v[KT - 1]) * sl2;
       // the reference maximum moves only when some row of the warp grew by more than 2^8 (warp-uniform decision:
       // TMEM access is warp-collective); rows whose maximum barely moved then get a factor close to 1
       float factor = 1.f;
@@ -297,17 +339,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = m_new;
         rescale = true;
       }
-      // probabilities in registers first (two exponentials per instruction in half precision: the exponent lies in
-      // [-inf, 8] thanks to the lazy rescale, so the f16 input keeps ~11 bits where the probabilities are large,
-      // and the bf16 probabilities need 8), so the wait for the previous P V below overlaps this work
-      float tile_sum = 0.f;
-      uint32_t pk[kTile / 2];
+      // probabilities, two per instruction in half precision: the exponent s*scale*log2e - m_ref lies in [-inf, 8]
+      // thanks to the lazy rescale, so its f16 rounding keeps ~11 bits where the probabilities are large (the bf16
+      // probabilities keep 8). The row sum is not formed here: the tensor core accumulates it (P times a ones row).
+      const float neg_m = -m_ref;
+      uint32_t pk[KT / 2];
 #pragma unroll
-      for (int i = 0; i < kTile / 2; ++i) {
-        const __half2 e = h2exp2(__floats2half2_rn(v[2 * i] - m_ref, v[2 * i + 1] - m_ref));
-        const float2 f = __half22float2(e);  // exp2(-inf) = 0 for masked keys
-        tile_sum += f.x + f.y;
-        pk[i] = pack_bf16(f.x, f.y);
+      for (int i = 0; i < KT / 2; ++i) {
+        const float2 e = exp2_f16x2(fmaf(v[2 * i], sl2, neg_m), fmaf(v[2 * i + 1], sl2, neg_m));
+        pk[i] = pack_bf16(e.x, e.y);  // exp2(-inf) = 0 for masked keys
       }
       // O_g += P_g(j-1) V_{j-1} must have finished before its P buffer is rewritten or O_g is rescaled
       if (j > 0 && !__all_sync(0xffffffffu, mbar_sleep_wait(&o_full[g], (j - 1) & 1, kTimeoutAccum))) {
@@ -315,14 +355,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
 #pragma unroll
-      for (int c8 = 0; c8 < kTile / 8; ++c8) {  // 8 keys -> one 16-byte chunk of the K-major swizzled P tile
+      for (int c8 = 0; c8 < KT / 8; ++c8) {  // 8 keys -> one 16-byte chunk of the K-major swizzled P tile
         const int box = c8 / 8;
         const int swz = (c8 % 8) ^ (row & 7);
         *reinterpret_cast<uint4*>(prow + box * (kTile * 128) + swz * 16) =
             make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
       }
-      l_sum = fmaf(l_sum, factor, tile_sum);
-      if (rescale) {  // O_g to the new reference before the next P V accumulates into it
+      if (rescale) {  // O_g and l_g to the new reference before the next P V accumulates into them
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < D; c += 32) {
@@ -332,6 +371,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) o[i] *= factor;
           tmem_st32(to + c, o);
         }
+        float l[16];
+        tmem_ld16(tl, l);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) l[i] *= factor;
+        tmem_st16(tl, l);
         tmem_st_wait();
       }
       tc_fence_before();
@@ -344,6 +388,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       *abort_flag = 1;
     } else if (n > 0) {
       tc_fence_after();
+      float l[16];
+      tmem_ld16(tl, l);  // column 0: the row sum of the probabilities, relative to m_ref
+      const float l_sum = l[0];
       const float inv = 1.f / l_sum;
       bf16* out = p.o + (static_cast<int64_t>(b) * p.S + q) * p.ldo + hq * D;
 #pragma unroll
@@ -391,8 +438,8 @@ void run(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, 
   p.Hkv = Hkv;
   p.scale_log2 = scale * kLog2e;
   auto mq = make_bf16_map_3d(q, static_cast<int64_t>(Hq) * D, S, B, ldq, S * ldq, kTile);
-  auto mk = make_bf16_map_3d(k, static_cast<int64_t>(Hkv) * D, S, B, ldk, S * ldk, kTile);
-  auto mv = make_bf16_map_3d(v, static_cast<int64_t>(Hkv) * D, S, B, ldv, S * ldv, kTile);
+  auto mk = make_bf16_map_3d(k, static_cast<int64_t>(Hkv) * D, S, B, ldk, S * ldk, Layout<D>::KT);
+  auto mv = make_bf16_map_3d(v, static_cast<int64_t>(Hkv) * D, S, B, ldv, S * ldv, Layout<D>::KT);
   dim3 grid(B * Hq, (S + kTile * kGroups - 1) / (kTile * kGroups));
   kernel<<<grid, kThreads, Layout<D>::kTotal, stream>>>(mq, mk, mv, p);
   check_cuda(cudaGetLastError(), "attention forward tc launch");
@@ -404,9 +451,10 @@ void flash_attn_fwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, c
                        int64_t ldo, float* lse, int B, int S, int Hq, int Hkv, int D, float scale,
                        cudaStream_t stream) {
   if (B == 0 || S == 0) return;
-  if (D != 64) throw std::runtime_error("flash_attn_fwd_tc: head_dim must be 64");
+  if (D != 64 && D != 128) throw std::runtime_error("flash_attn_fwd_tc: head_dim must be 64 or 128");
   if (Hq % Hkv) throw std::runtime_error("flash_attn_fwd_tc: query heads must be a multiple of kv heads");
-  attn_fwd_tc::run<64>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hkv, scale, stream);
+  if (D == 64) attn_fwd_tc::run<64>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hkv, scale, stream);
+  else attn_fwd_tc::run<128>(q, ldq, k, ldk, v, ldv, o, ldo, lse, B, S, Hq, Hkv, scale, stream);
 }
 
 int attention_fwd_tc_status(bool clear) { return read_status_word(clear); }

@@ -400,4 +400,10 @@ void splitk_reduce(const float* partial, int chunks, int64_t rows, int64_t cols,
 
 int gemm_status(bool clear) { return read_status_word(clear); }
 
+// Arms (buf != null: kTraceTiles x 8 int64 slots) or disarms the per-tile timestamps of CTA 0 of every GEMM launch.
+void gemm_trace(void* buf) {
+  unsigned long long* ptr = static_cast<unsigned long long*>(buf);
+  check_cuda(cudaMemcpyToSymbol(g_gemm_trace, &ptr, sizeof(ptr)), "gemm trace");
+}
+
 }  // namespace qw

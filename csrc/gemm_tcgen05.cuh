@@ -89,6 +89,16 @@ struct Smem {
   static constexpr int kTotal = kDataBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// Optional per-tile timestamps of CTA 0 (clock64 of its SM) for tuning: null unless armed from the host
+// (gemm_trace). Slots per tile: 0/1 producer first wait / last load issued, 2/3 issuer before / after the
+// accumulator-free wait, 4 first k-block landed, 5 last MMA committed, 6/7 epilogue start / end.
+constexpr int kTraceTiles = 64;
+static __device__ unsigned long long* g_gemm_trace;
+
+__device__ __forceinline__ void trace_mark(unsigned long long* tr, int local_tile, int slot) {
+  if (tr && local_tile < kTraceTiles) tr[local_tile * 8 + slot] = clock64();
+}
+
 struct TileInfo {
   int group;
   int m_tile;
@@ -379,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int ngroups = p.num_groups;
+  unsigned long long* const trace = blockIdx.x == 0 ? g_gemm_trace : nullptr;
 
   // group prefix (tiles before each group) for kGroupM
   if (MODE == kGroupM && threadIdx.x == 0) {
@@ -422,8 +433,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < kStages; ++s) issued_phase[s] = -1;
       TileInfo t;
+      int local = 0;
       for (int tile = blockIdx.x; !*abort_flag && tile_info<BN, MODE>(p, s_prefix, ngroups, tile, t);
-           tile += gridDim.x) {
+           tile += gridDim.x, ++local) {
+        trace_mark(trace, local, 0);
         for (int kb = 0; kb < t.num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, kTimeoutEmpty)) { *abort_flag = 1; break; }
           uint8_t* sa = smem + stage * S::kStageBytes;
@@ -473,6 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
+        trace_mark(trace, local, 1);
       }
       // drain: every stage this thread filled must have landed before the CTA may exit
       for (int s = 0; s < kStages; ++s)
@@ -487,14 +501,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       TileInfo t;
+      int local = 0;
       for (int tile = blockIdx.x; !*abort_flag && tile_info<BN, MODE>(p, s_prefix, ngroups, tile, t);
-           tile += gridDim.x) {
+           tile += gridDim.x, ++local) {
+        trace_mark(trace, local, 2);
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, kTimeoutAccumFree)) { *abort_flag = 1; break; }
+        trace_mark(trace, local, 3);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
         for (int kb = 0; kb < t.num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, kTimeoutFull)) { *abort_flag = 1; ok = false; break; }
+          if (kb == 0) trace_mark(trace, local, 4);
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
           const uint32_t sb = sa + S::kABytes;
@@ -511,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
         umma_commit(&acc_full[acc]);
+        trace_mark(trace, local, 5);
         if (!ok) break;
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
@@ -525,11 +544,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     TileInfo t;
-    for (int tile = blockIdx.x; tile_info<BN, MODE>(p, s_prefix, ngroups, tile, t); tile += gridDim.x) {
+    unsigned long long* const etrace = threadIdx.x == 64 ? trace : nullptr;
+    int local = 0;
+    for (int tile = blockIdx.x; tile_info<BN, MODE>(p, s_prefix, ngroups, tile, t); tile += gridDim.x, ++local) {
       if (*abort_flag) break;
       if (!mbar_wait(&acc_full[acc], acc_phase, kTimeoutAccum)) { *abort_flag = 1; break; }
+      trace_mark(etrace, local, 6);
       tc_fence_after();
       epilogue_tile<BN, MODE, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base);
+      trace_mark(etrace, local, 7);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }

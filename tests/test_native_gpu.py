@@ -58,7 +58,8 @@ def test_norm(kind, H):
 
 
 @pytest.mark.parametrize("B,S,hq,hkv,d", [(2, 200, 4, 4, 64), (1, 333, 8, 2, 128), (2, 128, 2, 1, 64),
-                                         (1, 1024, 4, 2, 64), (1, 640, 2, 2, 128)])
+                                         (1, 1024, 4, 2, 64), (1, 640, 2, 2, 128), (1, 2048, 4, 2, 128),
+                                         (1, 4096, 2, 1, 64), (1, 4096, 2, 2, 128)])
 def test_attention(B, S, hq, hkv, d):
     from quantaweave_b200.models.layers import apply_rope_reference, rope_tables
     from quantaweave_b200.ops.attention import attention_core
@@ -85,13 +86,14 @@ def test_attention(B, S, hq, hkv, d):
     _status_ok()
 
 
+@pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("B,S,hq,hkv", [(2, 2048, 4, 4), (1, 4096, 2, 1), (3, 333, 4, 2), (1, 1, 2, 2),
-                                        (1, 130, 2, 2), (2, 256, 16, 16)])
-def test_attention_forward_tcgen05_and_lse_match_fp32(B, S, hq, hkv):
-    """The tcgen05 forward (head_dim 64) against a plain fp32 causal softmax(QK^T)V, including lse = ln sum exp."""
+                                        (1, 130, 2, 2), (2, 256, 16, 16), (1, 200, 2, 1)])
+def test_attention_forward_tcgen05_and_lse_match_fp32(B, S, hq, hkv, d):
+    """The tcgen05 forward (head_dim 64: 128-key tiles; 128: 64-key tiles) against a plain fp32 causal
+    softmax(QK^T)V, including lse = ln sum exp."""
     from quantaweave_b200.ops import ext
 
-    d = 64
     torch.manual_seed(3)
     T = B * S
     qkv = (torch.randn(T, (hq + 2 * hkv) * d, device="cuda") * 0.7).bfloat16()
@@ -253,23 +255,29 @@ def test_model_native_matches_cpu_oracle():
     # accumulation orders, move individual gradients by a few percent; a real bug moves them by ~100%
     assert max(rels.values()) < 0.3, rels
     assert sorted(rels.values())[len(rels) // 2] < 0.05, rels
-    # per expert: every expert that no routing flip touched must match closely, so a bug confined to one
-    # rarely-routed expert cannot hide inside a whole-tensor norm
+    # per expert, so a bug confined to one rarely-routed expert cannot hide inside a whole-tensor norm. A token whose
+    # top-2 set differs between the two runs (a near tie flipped by bf16 activations) adds or removes one rank-1 term
+    # of an expert's weight gradient, which moves it by about 1/sqrt(rows of that expert) per flip; the tolerance
+    # grows with that, and an expert whose rows are mostly flipped is not checked. A wrong tile or row mapping moves
+    # an expert's gradient by ~100%.
     checked = 0
+    params = dict(gpu.named_parameters())
     for layer, (mg, mc) in enumerate(zip(gpu.moes(), cpu.moes())):
         ig, ic = mg.last_top_indices.cpu().reshape(-1, mg.top_k), mc.last_top_indices.reshape(-1, mc.top_k)
         flipped = (ig.sort(dim=1).values != ic.sort(dim=1).values).any(dim=1)
-        touched = set(ig[flipped].reshape(-1).tolist()) | set(ic[flipped].reshape(-1).tolist())
-        for stack in ("w_gate_up", "w_down"):
-            name = f"blocks.{layer}.moe.{stack}"
-            got, want = dict(gpu.named_parameters())[name].grad.float().cpu(), cpu_grads[name].grad
-            for e in range(mg.num_experts):
-                if e in touched or float(want[e].norm()) == 0.0:
-                    continue
-                rel = float((got[e] - want[e]).norm() / want[e].norm())
-                assert rel < 0.08, (name, e, rel)
+        for e in range(mg.num_experts):
+            rows = int((ic == e).any(dim=1).sum())
+            flips = int((((ig == e).any(dim=1) | (ic == e).any(dim=1)) & flipped).sum())
+            tol = 0.08 + 1.5 * math.sqrt(flips / max(rows, 1))
+            if rows == 0 or tol > 0.6:
+                continue
+            for stack in ("w_gate_up", "w_down"):
+                name = f"blocks.{layer}.moe.{stack}"
+                got, want = params[name].grad[e].float().cpu(), cpu_grads[name].grad[e]
+                rel = float((got - want).norm() / want.norm())
+                assert rel < tol, (name, e, rel, flips, rows)
                 checked += 1
-    assert checked >= cfg.layers * cfg.num_experts  # most experts are untouched by flips and were checked
+    assert checked >= cfg.layers * cfg.num_experts  # most experts were checked
     _status_ok()
 
 
