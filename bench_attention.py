@@ -27,6 +27,8 @@ def main() -> None:
     ap.add_argument("--head-dim", type=int, default=64)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--trace", action="store_true",
+                    help="also print the forward's per-tile timeline (SM clocks) of its first CTA")
     args = ap.parse_args()
 
     from quantaweave_b200.ops import ext
@@ -59,6 +61,18 @@ def main() -> None:
                       "backward_path": os.environ.get("QW_ATTN_BWD", "tcgen05"), "batch": B, "seq": S, "heads": h,
                       "kv_heads": hkv, "head_dim": d, "fwd_ms": round(f_ms, 4), "bwd_ms": round(b_ms, 4),
                       "fwd_tflops": round(flops / f_ms / 1e9, 1), "bwd_tflops": round(2.5 * flops / b_ms / 1e9, 1)}))
+    if args.trace:
+        buf = torch.zeros(32 * 2 * 8, dtype=torch.int64, device="cuda")
+        ext().attn_fwd_trace(buf)
+        attention_core(qkv, B, S, h, hkv, d, False, 1e4)
+        torch.cuda.synchronize()
+        ext().attn_fwd_trace(None)
+        t = buf.view(32, 2, 8).cpu().tolist()
+        t0 = min(v for tile in t for grp in tile for v in grp if v)
+        rows = [[[v - t0 if v else None for v in grp[:6]] for grp in tile] for tile in t if any(tile[0][:6])]
+        print(json.dumps({"forward_timeline": "per tile j, per group: [scores ready, probabilities computed, previous "
+                                              "PV done, P written, S(j) issued, O(j) issued] in SM clocks",
+                          "tiles": rows}))
     if ext().read_status(True) != 0:
         raise SystemExit("a kernel reported a device-side error status")
 

@@ -87,6 +87,16 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Optional timeline of the CTA at blockIdx (0, 0) (clock64 of its SM) for tuning: null unless armed from the host
+// (attn_fwd_trace). Slots of (tile j, group g) at 8 * (2j + g): 0 scores ready, 1 probabilities computed,
+// 2 previous P V done, 3 P written, 4 S(j) issued, 5 O(j) issued.
+constexpr int kTraceTiles = 32;
+static __device__ unsigned long long* g_attn_fwd_trace;
+
+__device__ __forceinline__ void trace_mark(unsigned long long* tr, int j, int g, int slot) {
+  if (tr && j < kTraceTiles) tr[(2 * j + g) * 8 + slot] = clock64();
+}
+
 // max(a, b, c) in one instruction (three-input max.f32, sm_100)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
@@ -110,7 +120,7 @@ __device__ __forceinline__ int kv_tiles_of(const Params& p, int q_start) {
 }
 
 template <int D>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                        const __grid_constant__ CUtensorMap map_v, Params p) {
   using L = Layout<D>;
@@ -129,6 +139,7 @@ __global__ void __maxnreg__(200)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  unsigned long long* const trace = (blockIdx.x == 0 && blockIdx.y == 0) ? g_attn_fwd_trace : nullptr;
   const int b = blockIdx.x / p.Hq, hq = blockIdx.x % p.Hq;
   const int hk = hq / (p.Hq / p.Hkv);
   const int q0 = (gridDim.y - 1 - blockIdx.y) * (kTile * kGroups);  // the latest queries see the most keys: first
@@ -225,6 +236,7 @@ __global__ void __maxnreg__(200)
                     id_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[g]);
+        trace_mark(trace, j, g, 4);
       };
       auto issue_o = [&](int g, int j) {
         const int st = j % kStages;
@@ -243,6 +255,7 @@ __global__ void __maxnreg__(200)
           umma_bf16(tmem + L::kTmemL + g * 16, a, b1, id_l, (j > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(&o_full[g]);
+        trace_mark(trace, j, g, 5);
       };
       bool ok = mbar_sleep_wait(q_full, 0, kTimeoutFull);
       tc_fence_after();
@@ -275,11 +288,11 @@ __global__ void __maxnreg__(200)
           idle = 0;
           continue;
         }
-        __nanosleep(32);
-        if ((++idle & 255) == 0) {  // bounded: give up after the wait budget without progress
+        // spin without sleeping: a sleeping issuer woke up to a microsecond late, stalling both groups
+        if ((++idle & 1023) == 0) {  // bounded: give up after the wait budget without progress
           if (*abort_flag) { ok = false; break; }
           const uint64_t now = globaltimer();
-          if (idle == 256) idle_start = now;
+          if (idle == 1024) idle_start = now;
           else if (now - idle_start > QW_WAIT_TIMEOUT_NS) { set_status(kTimeoutAccum); ok = false; break; }
         }
       }
@@ -300,12 +313,14 @@ __global__ void __maxnreg__(200)
     const uint32_t to = tmem + lane_off + L::kTmemO + g * D;
     const uint32_t tl = tmem + lane_off + L::kTmemL + g * 16;
     uint8_t* prow = smem + L::kP + g * L::kPBytes + row * 128;
+    unsigned long long* const gtrace = (quarter == 2 && lane == 0) ? trace : nullptr;
     const float sl2 = p.scale_log2;
     float m_ref = -INFINITY;  // the maximum O_g and l_g are expressed against (base-2, scaled)
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
       if (!__all_sync(0xffffffffu, mbar_sleep_wait(&s_full[g], j & 1, kTimeoutAccum))) { ok = false; break; }
+      trace_mark(gtrace, j, g, 0);
       tc_fence_after();
       float v[KT];
 #pragma unroll
@@ -349,11 +364,13 @@ __global__ void __maxnreg__(200)
         const float2 e = exp2_f16x2(fmaf(v[2 * i], sl2, neg_m), fmaf(v[2 * i + 1], sl2, neg_m));
         pk[i] = pack_bf16(e.x, e.y);  // exp2(-inf) = 0 for masked keys
       }
+      trace_mark(gtrace, j, g, 1);
       // O_g += P_g(j-1) V_{j-1} must have finished before its P buffer is rewritten or O_g is rescaled
       if (j > 0 && !__all_sync(0xffffffffu, mbar_sleep_wait(&o_full[g], (j - 1) & 1, kTimeoutAccum))) {
         ok = false;
         break;
       }
+      trace_mark(gtrace, j, g, 2);
 #pragma unroll
       for (int c8 = 0; c8 < KT / 8; ++c8) {  // 8 keys -> one 16-byte chunk of the K-major swizzled P tile
         const int box = c8 / 8;
@@ -382,6 +399,7 @@ __global__ void __maxnreg__(200)
       fence_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[g]);
+      trace_mark(gtrace, j, g, 3);
     }
     if (ok && n > 0 && !__all_sync(0xffffffffu, mbar_sleep_wait(&o_full[g], (n - 1) & 1, kTimeoutAccum))) ok = false;
     if (!ok) {
@@ -458,5 +476,11 @@ void flash_attn_fwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, c
 }
 
 int attention_fwd_tc_status(bool clear) { return read_status_word(clear); }
+
+// Arms (buf: 2 * kTraceTiles * 8 int64 slots) or disarms (null) the forward's timeline trace.
+void attn_fwd_trace(void* buf) {
+  unsigned long long* ptr = static_cast<unsigned long long*>(buf);
+  check_cuda(cudaMemcpyToSymbol(attn_fwd_tc::g_attn_fwd_trace, &ptr, sizeof(ptr)), "attention trace");
+}
 
 }  // namespace qw

@@ -317,13 +317,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           idle = 0;
           continue;
         }
-        // nothing ready: a short sleep, then poll both conditions again. (Parking on the oldest tile's P/dS
-        // barrier would leave a next S/dP that becomes ready first waiting behind the other group's whole softmax.)
-        __nanosleep(20);
-        if ((++idle & 255) == 0) {  // bounded: give up after the wait budget without progress
+        // nothing ready: poll both conditions again at once. (Parking on the oldest tile's P/dS barrier would leave
+        // a next S/dP that becomes ready first waiting behind the other group's whole softmax, and a sleeping
+        // issuer woke up to a microsecond late.)
+        if ((++idle & 1023) == 0) {  // bounded: give up after the wait budget without progress
           if (*abort_flag) { ok = false; break; }
           const uint64_t now = globaltimer();
-          if (idle == 256) idle_start = now;
+          if (idle == 1024) idle_start = now;
           else if (now - idle_start > QW_WAIT_TIMEOUT_NS) { set_status(kTimeoutAccum); ok = false; break; }
         }
       }

@@ -2,6 +2,7 @@
 // Raw-pointer API (no torch headers here); argument validation lives in bindings.cpp.
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -101,9 +102,31 @@ static int num_sms() {
   return n;
 }
 
+// Maps of the TMA epilogue (output, residual, raw gate|up); unused ones stay zero.
+struct OutMaps {
+  CUtensorMap out{}, res{}, gu{};
+};
+
+// Whether bf16 outputs go through TMA boxes (the default); QW_GEMM_TMA_EPI=0 keeps the per-thread stores.
+static bool tma_epilogue_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("QW_GEMM_TMA_EPI");
+    return !(e && std::string(e) == "0");
+  }();
+  return on;
+}
+
+// A [rows, cols] bf16 map with 32-row x 64-column boxes for the epilogue, or false when the buffer's alignment
+// rules one out (then the per-thread epilogue runs).
+static bool epi_map(CUtensorMap& m, const void* ptr, int64_t cols, int64_t rows, int64_t ld) {
+  if (!ptr || rows <= 0 || (reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16) return false;
+  m = make_map(ptr, cols, rows, ld, 64, 32);
+  return true;
+}
+
 template <int BN, int MODE, int EPI, bool A_MN, bool B_MN>
 static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int64_t total_tiles_bound,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const OutMaps& outs = OutMaps{}) {
   auto kernel = gemm_kernel<BN, MODE, EPI, A_MN, B_MN>;
   static bool configured = false;
   const int smem = Smem<BN>::kTotal;
@@ -112,7 +135,7 @@ static void launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p
     configured = true;
   }
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_sms(), total_tiles_bound)));
-  kernel<<<grid, kThreads, smem, stream>>>(ma, mb, p);
+  kernel<<<grid, kThreads, smem, stream>>>(ma, mb, outs.out, outs.res, outs.gu, p);
   check_cuda(cudaGetLastError(), "gemm launch");
 }
 
@@ -143,7 +166,10 @@ void linear_fwd(const bf16* x, int64_t ldx, const bf16* w, int64_t ldw, int64_t 
   p.residual = residual; p.ldr = ldr;
   auto ma = make_map(x, K, M, ldx, 64, kBM);
   auto mb = make_map(w, K, N, ldw, 64, BN);
-  launch<BN, kGroupM, kEpiStore, false, false>(ma, mb, p, ((M + kBM - 1) / kBM) * p.n_tiles, stream);
+  OutMaps outs;
+  p.tma_out = tma_epilogue_enabled() && !out_fp32 && epi_map(outs.out, out, N, M, ldo) &&
+              (!residual || epi_map(outs.res, residual, N, M, ldr));
+  launch<BN, kGroupM, kEpiStore, false, false>(ma, mb, p, ((M + kBM - 1) / kBM) * p.n_tiles, stream, outs);
 }
 
 // dx[M,K] (+)= dy[M,N] @ w[N,K]
@@ -159,7 +185,9 @@ void linear_dgrad(const bf16* dy, int64_t lddy, const bf16* w, int64_t ldw, int6
   p.out = dx; p.ldo = lddx; p.out_fp32 = out_fp32; p.accumulate = accumulate;
   auto ma = make_map(dy, N, M, lddy, 64, kBM);
   auto mb = make_map(w, K, N, ldw, 64, 64);
-  launch<BN, kGroupM, kEpiStore, false, true>(ma, mb, p, ((M + kBM - 1) / kBM) * p.n_tiles, stream);
+  OutMaps outs;
+  p.tma_out = tma_epilogue_enabled() && !out_fp32 && !accumulate && epi_map(outs.out, dx, K, M, lddx);
+  launch<BN, kGroupM, kEpiStore, false, true>(ma, mb, p, ((M + kBM - 1) / kBM) * p.n_tiles, stream, outs);
 }
 
 // dw[N,K] (+)= dy[T,N]^T @ x[T,K]
@@ -258,7 +286,10 @@ void moe_gate_up_fwd(const bf16* x, const bf16* w_gate_up, const int* counts, co
   p.gu_out = gu;
   auto ma = make_map(x, H, R, H, 64, kBM);
   auto mb = make_map(w_gate_up, H, E * 2 * F, H, 64, BN / 2);
-  launch<BN, kGroupM, kEpiSwiGLU, false, false>(ma, mb, p, p.max_tiles, stream);
+  OutMaps outs;
+  p.tma_out = tma_epilogue_enabled() && F % 8 == 0 && epi_map(outs.out, h, F, R, F) &&
+              (!gu || epi_map(outs.gu, gu, 2 * F, R, 2 * F));
+  launch<BN, kGroupM, kEpiSwiGLU, false, false>(ma, mb, p, p.max_tiles, stream, outs);
 }
 
 // y[R,H] = h[R,F] @ w_down[e]^T   (w_down [E, H, F]). With `peer_out`, row r is stored over NVLink into rank
@@ -283,7 +314,9 @@ void moe_down_fwd(const bf16* h, const bf16* w_down, const int* counts, const in
   p.peer_out = peer_out; p.peer_rows = peer_rows; p.peer_slot = peer_slot;
   auto ma = make_map(h, F, R, F, 64, kBM);
   auto mb = make_map(w_down, F, E * H, F, 64, BN);
-  launch<BN, kGroupM, kEpiStore, false, false>(ma, mb, p, p.max_tiles, stream);
+  OutMaps outs;
+  p.tma_out = tma_epilogue_enabled() && !peer_out && epi_map(outs.out, y, H, R, H);
+  launch<BN, kGroupM, kEpiStore, false, false>(ma, mb, p, p.max_tiles, stream, outs);
 }
 
 // a = dy @ w_down[e] ; dgu = [w*a*u*silu'(g) | w*a*silu(g)] ; h_w = w*silu(g)*u ; dw_partial[r,t] = <a,h> per tile
@@ -334,7 +367,9 @@ void moe_gate_up_dgrad(const bf16* dgu, const bf16* w_gate_up, const int* counts
   p.peer_out = peer_out; p.peer_rows = peer_rows; p.peer_slot = peer_slot;
   auto ma = make_map(dgu, 2 * F, R, 2 * F, 64, kBM);
   auto mb = make_map(w_gate_up, H, E * 2 * F, H, 64, 64);
-  launch<BN, kGroupM, kEpiStore, false, true>(ma, mb, p, p.max_tiles, stream);
+  OutMaps outs;
+  p.tma_out = tma_epilogue_enabled() && !peer_out && epi_map(outs.out, dx, H, R, H);
+  launch<BN, kGroupM, kEpiStore, false, true>(ma, mb, p, p.max_tiles, stream, outs);
 }
 
 // out[e][M,N] (+)= a[rows_e, M]^T @ b[rows_e, N]

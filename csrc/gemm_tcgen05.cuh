@@ -10,6 +10,11 @@
 //              last k-block of a tile it commits `accum_full[b]`.
 //   warps 2-5  epilogue: tcgen05.ld the 128 x BN accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows),
 //              apply the fused epilogue and store to global memory, then release the buffer (`accum_empty[b]`).
+//              bf16 outputs go out through TMA: the warp writes its 32 rows x 64 columns into a 128-byte-swizzled
+//              shared-memory box and one lane issues a bulk tensor store (a residual is brought in the same way by a
+//              TMA load into that box). One thread per row storing 16 bytes to 32 different rows per instruction
+//              left the epilogue at ~2.5x the k-loop time of a K = 1024 tile; the bulk store writes whole lines.
+//              fp32 outputs, read-modify-write accumulation and stores into peers' memory keep the per-thread path.
 //
 // Tile schedules (device-side, no host synchronisation):
 //   kGroupM  grouped over rows: group g owns rows [row_off[g], row_off[g]+rows[g]) of A and C, and its own B
@@ -77,7 +82,10 @@ struct Params {
   const float* route_w;        // kEpiSwiGLUBwd: per-row route weight
   __nv_bfloat16* h_out;        // kEpiSwiGLUBwd: optional H = silu(g)*u, ld = F
   float* dw_partial;           // kEpiSwiGLUBwd: [rows, n_tiles] partial <dH_raw, H>
+  int tma_out;                 // kGroupM store / SwiGLU epilogues: bf16 out (and residual, gu) through TMA boxes
 };
+
+constexpr int kStgBytes = 32 * 128;  // one epilogue warp's TMA box: 32 rows x 64 bf16, 128-byte swizzle
 
 template <int BN>
 struct Smem {
@@ -86,8 +94,53 @@ struct Smem {
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kDataBytes = kStages * kStageBytes;
-  static constexpr int kTotal = kDataBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kStg = kDataBytes;                    // 4 epilogue warps x one box each
+  static constexpr int kBarOff = kStg + 4 * kStgBytes;
+  static constexpr int kTotal = kBarOff + 1024 /*align*/ + 256 /*barriers*/;
 };
+
+// TMA stores from shared memory (bulk async-groups of the issuing thread)
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               :: "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(src)), "r"(x), "r"(y) : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void tma_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// One epilogue warp's staging box: 64 bf16 of row `lane` in 16-byte chunks at the 128-byte-swizzled positions the
+// tensor map expects (chunk q of row r at q ^ (r % 8); the box is 1024-byte aligned).
+struct StageBox {
+  uint8_t* base;
+  int lane;
+  __device__ __forceinline__ uint4* chunk(int q) const {
+    return reinterpret_cast<uint4*>(base + lane * 128 + ((q ^ (lane & 7)) << 4));
+  }
+};
+
+// Per-warp state of the TMA epilogue: the staging box, the maps and the residual barrier's phase.
+struct TmaEpi {
+  StageBox box;
+  const CUtensorMap* map_out;
+  const CUtensorMap* map_res;
+  const CUtensorMap* map_gu;
+  uint64_t* res_bar;
+  uint32_t res_phase;
+  int row;  // first output row of this warp's 32 rows
+};
+
+// Make the warp's box free for new data (the previous bulk store from it has finished reading it).
+__device__ __forceinline__ void box_acquire(int lane) {
+  if (lane == 0) tma_store_wait_read();
+  __syncwarp();
+}
+
+// Publish the box written by the warp's lanes and store it at (x, row) through `map`.
+__device__ __forceinline__ void box_release(const TmaEpi& e, const CUtensorMap* map, int x, int lane) {
+  fence_async_smem();  // generic-proxy writes -> visible to the TMA (async proxy)
+  __syncwarp();
+  if (lane == 0) tma_store_2d(map, e.box.base, x, e.row);
+}
 
 // Optional per-tile timestamps of CTA 0 (clock64 of its SM) for tuning: null unless armed from the host
 // (gemm_trace). Slots per tile: 0/1 producer first wait / last load issued, 2/3 issuer before / after the
@@ -158,6 +211,99 @@ __device__ __forceinline__ bool tile_info(const Params& p, const int* s_prefix, 
 // ---------------------------------------------------------------------------------------------------------
 // epilogue: one thread = one accumulator row, 32 columns at a time
 // ---------------------------------------------------------------------------------------------------------
+// TMA variant of the store and SwiGLU epilogues (bf16 out, no read-modify-write accumulation, local memory)
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile_tma(const Params& p, const TileInfo& t, uint32_t tmem_acc,
+                                                  int row_in_tile, int warp_lane_base, TmaEpi& e, int lane) {
+  const bool row_ok = row_in_tile < t.rows;
+  const uint32_t tbase = tmem_acc + (static_cast<uint32_t>(warp_lane_base) << 16);
+  if (EPI == kEpiStore) {
+    const bool empty_k = (t.num_kb == 0);
+    const int n0 = t.n_tile * BN;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 64) {
+      float v[64];
+      if (!empty_k) {
+        tmem_ld32_pair(tbase + c, tbase + c + 32, v, v + 32);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = 0.f;
+      }
+      if (n0 + c >= p.N) continue;  // warp-uniform: the whole box lies past the last column
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        float x = row_ok ? v[i] * p.alpha : 0.f;
+        if (row_ok && p.bias) x += (n0 + c + i < p.N) ? p.bias[n0 + c + i] : 0.f;
+        v[i] = x;
+      }
+      box_acquire(lane);
+      if (p.residual) {  // the residual box comes in through the same shared memory
+        if (lane == 0) {
+          mbar_arrive_expect_tx(e.res_bar, kStgBytes);
+          tma_load_2d(e.box.base, e.map_res, e.res_bar, n0 + c, e.row);
+        }
+        const bool landed = mbar_wait(e.res_bar, e.res_phase, kTimeoutFull);
+        e.res_phase ^= 1;
+        if (landed && row_ok) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 r = *e.box.chunk(q);
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&r);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * q + i] += __bfloat162float(rb[i]);
+          }
+        }
+        __syncwarp();
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *e.box.chunk(q) = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                                     pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+      box_release(e, e.map_out, n0 + c, lane);
+    }
+  } else {  // kEpiSwiGLU: acc columns [0, BN/2) = gate, [BN/2, BN) = up for FFN columns f0 + [0, BN/2)
+    constexpr int HALF = BN / 2;
+    const int f0 = t.n_tile * HALF;
+#pragma unroll 1
+    for (int c = 0; c < HALF; c += 64) {
+      float g[64], u[64];
+      tmem_ld32_pair(tbase + c, tbase + c + 32, g, g + 32);
+      tmem_ld32_pair(tbase + HALF + c, tbase + HALF + c + 32, u, u + 32);
+      if (f0 + c >= p.ffn) continue;
+      if (!row_ok) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) { g[i] = 0.f; u[i] = 0.f; }
+      }
+      box_acquire(lane);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float hv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float gv = g[8 * q + i];
+          hv[i] = __fdividef(gv, 1.0f + __expf(-gv)) * u[8 * q + i];
+        }
+        *e.box.chunk(q) = make_uint4(pack_bf16(hv[0], hv[1]), pack_bf16(hv[2], hv[3]), pack_bf16(hv[4], hv[5]),
+                                     pack_bf16(hv[6], hv[7]));
+      }
+      box_release(e, e.map_out, f0 + c, lane);
+      if (p.gu_out) {  // raw gate and up halves, two more boxes through the same staging
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          const float* src = half ? u : g;
+          box_acquire(lane);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *e.box.chunk(q) = make_uint4(pack_bf16(src[8 * q], src[8 * q + 1]), pack_bf16(src[8 * q + 2], src[8 * q + 3]),
+                                         pack_bf16(src[8 * q + 4], src[8 * q + 5]),
+                                         pack_bf16(src[8 * q + 6], src[8 * q + 7]));
+          box_release(e, e.map_gu, half * p.ffn + f0 + c, lane);
+        }
+      }
+    }
+  }
+}
+
 template <int BN, int MODE, int EPI>
 __device__ __forceinline__ void epilogue_tile(const Params& p, const TileInfo& t, uint32_t tmem_acc, int row_in_tile,
                                               int warp_lane_base) {
@@ -372,17 +518,20 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, const TileInfo& t
 // ---------------------------------------------------------------------------------------------------------
 template <int BN, int MODE, int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_out, const __grid_constant__ CUtensorMap map_res,
+                const __grid_constant__ CUtensorMap map_gu, Params p) {
   using S = Smem<BN>;
   constexpr int kStages = S::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kDataBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOff);
   uint64_t* empty = full + kStages;
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* teardown = acc_empty + 2;
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(teardown + 1);
+  uint64_t* res_full = teardown + 1;  // [4] residual boxes of the epilogue warps
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(res_full + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
   __shared__ int s_prefix[1025];
 
@@ -411,12 +560,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_empty[b], 128);
     }
     mbar_init(teardown, 1);
+    for (int w = 0; w < 4; ++w) mbar_init(&res_full[w], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
+    if (p.tma_out) {
+      tma_prefetch_desc(&map_out);
+      if (p.residual) tma_prefetch_desc(&map_res);
+      if (p.gu_out) tma_prefetch_desc(&map_gu);
+    }
   }
   if (warp == 1) tmem_alloc(tmem_base_slot, 2 * BN);
   tc_fence_before();
@@ -541,6 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int lane_base = 32 * (warp % 4);
     const int row_in_tile = lane_base + lane;
+    TmaEpi te{{smem + S::kStg + (warp % 4) * kStgBytes, lane}, &map_out, &map_res, &map_gu, &res_full[warp % 4], 0u, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
     TileInfo t;
@@ -551,7 +707,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&acc_full[acc], acc_phase, kTimeoutAccum)) { *abort_flag = 1; break; }
       trace_mark(etrace, local, 6);
       tc_fence_after();
-      epilogue_tile<BN, MODE, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base);
+      if constexpr (MODE == kGroupM && EPI != kEpiSwiGLUBwd) {
+        if (p.tma_out) {
+          te.row = t.row0 + lane_base;
+          epilogue_tile_tma<BN, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base, te, lane);
+        } else {
+          epilogue_tile<BN, MODE, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base);
+        }
+      } else {
+        epilogue_tile<BN, MODE, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base);
+      }
       trace_mark(etrace, local, 7);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
@@ -560,6 +725,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // rows stored into peers' memory are made visible at system scope before the kernel ends, so the flag that a
     // later kernel releases to the peers orders them
     if (p.peer_out) __threadfence_system();
+    if (p.tma_out && lane == 0) tma_store_wait_all();  // bulk stores complete before the CTA (and its smem) is gone
   }
 
   tc_fence_before();

@@ -42,7 +42,8 @@ void moe_gate_up_dgrad(const bf16* dgu, const bf16* w_gate_up, const int* counts
 void moe_wgrad(const bf16* a, const bf16* b, const int* counts, const int* offsets, int64_t R, int64_t E, int segments,
                int64_t M, int64_t N, void* out, bool out_fp32, bool accumulate, float alpha, cudaStream_t stream);
 int gemm_status(bool clear);
-void gemm_trace(void* buf);  // per-tile clock64 timestamps of CTA 0 (null disarms)
+void gemm_trace(void* buf);
+void attn_fwd_trace(void* buf);  // timeline of the forward's CTA (0, 0) (null disarms)  // per-tile clock64 timestamps of CTA 0 (null disarms)
 int wgrad_split(int64_t T, int64_t N, int64_t K);
 void splitk_reduce(const float* partial, int chunks, int64_t rows, int64_t cols, void* out, int64_t ldo,
                    bool out_fp32, bool accumulate, cudaStream_t stream);
