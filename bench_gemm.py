@@ -10,6 +10,8 @@ Cases (H = 1024, F = 2816, 64 experts, 32 x 2048 tokens, top-2):
 * ``gate_up_zipf``: the same GEMM with per-expert rows drawn from a Zipf(1.1) over the experts and cut at capacity
   (the load the benchmark's Zipf tokens produce);
 * ``down_balanced``: grouped down projection, every expert at capacity;
+* ``gate_up_wgrad_balanced`` / ``gate_up_wgrad_zipf``: the gate|up weight gradient, reduced over each expert's rows
+  (every expert's [2F x H] block is written, also for experts with few rows);
 * ``qkv_fwd``: dense [65536 x 1024] @ [3072 x 1024]^T; ``qkv_wgrad``: its weight gradient (split-K);
 * ``lm_head``: dense [16384 x 1024] @ [32000 x 1024]^T (one chunk of the chunked cross-entropy).
 
@@ -62,6 +64,15 @@ def cases(torch, C):
         out = torch.empty(rows, F, device=dev, dtype=torch.bfloat16)
         return (lambda: C.moe_gate_up_fwd(x, w, cnt, offsets, out, None)), 2.0 * useful * 2 * F * H
 
+    def grouped_wgrad(counts):
+        rows = E * CAP
+        offsets = torch.arange(E, device=dev, dtype=torch.int32) * CAP
+        cnt = torch.tensor(counts, device=dev, dtype=torch.int32)
+        dgu = torch.randn(rows, 2 * F, device=dev, generator=g).bfloat16()
+        x = torch.randn(rows, H, device=dev, generator=g).bfloat16()
+        dw = torch.empty(E, 2 * F, H, device=dev, dtype=torch.bfloat16)
+        return (lambda: C.moe_wgrad(dgu, x, cnt, offsets, dw, False, 1, 1.0)), 2.0 * sum(counts) * 2 * F * H
+
     def dense(M, N, K, wgrad=False):
         a = torch.randn(M, K, device=dev, generator=g).bfloat16()
         if wgrad:
@@ -76,6 +87,8 @@ def cases(torch, C):
         "gate_up_balanced": lambda: grouped([CAP] * E, False),
         "gate_up_zipf": lambda: grouped(_zipf_counts(), False),
         "down_balanced": lambda: grouped([CAP] * E, True),
+        "gate_up_wgrad_balanced": lambda: grouped_wgrad([CAP] * E),
+        "gate_up_wgrad_zipf": lambda: grouped_wgrad(_zipf_counts()),
         "qkv_fwd": lambda: dense(65536, 3072, 1024),
         "qkv_wgrad": lambda: dense(65536, 3072, 1024, wgrad=True),
         "lm_head": lambda: dense(16384, 32000, 1024),

@@ -3,14 +3,18 @@
 // the packed QKV rows.
 //
 // One CTA owns 256 queries of one (batch, q-head) as two 128-row Q tiles, and walks the KT-key K/V tiles up to the
-// diagonal (KT = 128 keys at head_dim 64; 64 keys at head_dim 128, so that three K/V stages, both Q tiles and both
-// P tiles still fit in shared memory). Each Q tile has its own softmax warpgroup, so while one group turns its
-// scores into probabilities the tensor core works on the other group's tiles (ping-pong):
+// diagonal (KT = 128 keys at head_dim 64; 64 keys at head_dim 128, so that S, O and P of both tiles fit the 512
+// TMEM columns). Each Q tile has its own softmax warpgroup, so while one group turns its scores into probabilities
+// the tensor core works on the other group's tiles (ping-pong):
 //
-//   S_g  = Q_g K_j^T                       (TMEM, 128 x KT fp32 per group)
-//   P_g  = exp2(S_g * scale*log2e - m_g)   (softmax warps, packed f16x2 exponentials -> bf16, K-major swizzled
+//   S_g  = Q_g K_j^T                       (TMEM, 128 x KT fp32 per group; Q and K from shared memory)
+//   P_g  = exp2(S_g * scale*log2e - m_g)   (softmax warps, packed f16x2 exponentials -> bf16, stored to TMEM)
+//   O_g += P_g V_j                          (TMEM, 128 x D fp32 per group; A = P_g read from TMEM, B = V_j from
 //                                           shared memory)
-//   O_g += P_g V_j                          (TMEM, 128 x D fp32 per group, accumulated by the tensor core)
+//
+// Shared-memory bandwidth (128 B per clock) is what an M = 128, N <= 128 MMA with both operands in shared memory
+// runs into: P in shared memory cost a store and a re-read of 32 KB per group and tile on top of the operand reads.
+// With P in TMEM the P V MMA reads only V from shared memory.
 //
 // Lazy rescaling: m_g is the row maximum the accumulator O_g is expressed against. A new tile only moves it when its
 // own maximum exceeds m_g by more than 2^8 (so probabilities stay below 256, well inside bf16 and fp32 range);
@@ -21,14 +25,15 @@
 //
 // Roles (320 threads, one CTA per SM — the shared-memory request guarantees it, so the 512 TMEM columns never
 // contend):
-//   warp 0      TMA: both Q tiles once, then K_j | V_j through a ring of 3 stages.
+//   warp 0      TMA: both Q tiles once, then K_j | V_j through a ring of stages.
 //   warp 1      MMA issuer (one thread), polling: per group, S_g(j+1) as soon as tile j+1 has landed and the group
 //               has read S_g(j) out of TMEM (so the next scores are computed while the group exponentiates), and
 //               O_g += P_g(j) V_j once P_g(j) is written; a K/V stage is released when both groups' MMAs for that
 //               tile are issued.
 //   warps 2-5   softmax group 0 (Q tile 0), warps 6-9 group 1 (Q tile 1). Warp w reads TMEM lanes 32*(w%4)..+31.
 //
-// TMEM columns: [0,KT) S_0, [KT,2KT) S_1, then O_0 and O_1 (D columns each): 384 of the 512 at either head_dim.
+// TMEM columns: [0,KT) S_0, [KT,2KT) S_1, then O_0 and O_1 (D columns each), P_0 and P_1 (KT/2 columns each); the
+// softmax warps add the row sums up themselves.
 // Every mbarrier wait is bounded (common.cuh): on a timeout all roles stop, in-flight TMA loads and MMAs are waited
 // for (bounded), TMEM is freed and the status word records the cause.
 #include <algorithm>
@@ -47,7 +52,6 @@ namespace attn_fwd_tc {
 constexpr int kTile = 128;                    // queries per Q tile
 constexpr int kGroups = 2;                    // Q tiles per CTA, one softmax warpgroup each
 constexpr int kThreads = 64 + 128 * kGroups;  // TMA warp, MMA warp, softmax warpgroups
-constexpr int kStages = 3;
 constexpr int kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -56,20 +60,24 @@ constexpr float kRescaleLog2 = 8.f;  // move the reference maximum only when a r
 template <int D>
 struct Layout {
   static constexpr int KT = D == 64 ? 128 : 64;             // keys per K/V tile
+  // Row sums on the tensor core (P times a ones row, N = 16) cost as many MMA instructions as P V itself, and an
+  // M = 128 MMA instruction takes about the same time at N = 16 as at N = 128; the softmax warps add them up with
+  // packed fp32 adds instead. (TMEM would have room for them at head_dim 128.)
+  static constexpr bool kRowSumMma = false;
+  static constexpr int kStages = D == 64 ? 4 : 3;
   static constexpr int kBoxes = D / 64;                      // 64-wide (128-byte) boxes per row
   static constexpr int kQBytes = kBoxes * kTile * 128;       // one [128 x D] bf16 Q tile
   static constexpr int kKVBytes = kBoxes * KT * 128;         // one [KT x D] bf16 K or V tile
-  static constexpr int kPBytes = (KT / 64) * kTile * 128;    // one [128 x KT] bf16 P tile: 64-key boxes
   static constexpr int kQ = 0;
   static constexpr int kKV = kGroups * kQBytes;              // stages of [K | V]
-  static constexpr int kP = kKV + kStages * 2 * kKVBytes;
-  static constexpr int kOnes = kP + kGroups * kPBytes;      // [16 x KT] K-major B operand: row 0 ones, rows 1-15 zero
-  static constexpr int kOnesBytes = (KT / 64) * 16 * 128;
+  static constexpr int kOnes = kKV + kStages * 2 * kKVBytes; // [16 x KT] K-major B operand: row 0 ones, rows 1-15 zero
+  static constexpr int kOnesBytes = kRowSumMma ? (KT / 64) * 16 * 128 : 0;
   static constexpr int kBar = kOnes + kOnesBytes;
   static constexpr int kTotal = kBar + 256 + 1024;           // barriers, and slack to align the base to 1 KB
   static constexpr int kTmemO = 2 * KT;                      // first column of the partial outputs
-  static constexpr int kTmemL = kTmemO + kGroups * D;        // row sums: P times the ones row, 16 columns per group
-  static_assert(kTmemL + kGroups * 16 <= kTmemCols, "TMEM columns");
+  static constexpr int kTmemP = kTmemO + kGroups * D;        // P_g: 128 x KT bf16, two per 32-bit column
+  static constexpr int kTmemL = kTmemP + kGroups * (KT / 2); // row sums (head_dim 128), 16 columns per group
+  static_assert(kTmemL + (kRowSumMma ? kGroups * 16 : 0) <= kTmemCols, "TMEM columns");
   static_assert(kTotal <= 227 * 1024, "shared memory per CTA");
 };
 
@@ -112,6 +120,23 @@ __device__ __forceinline__ float2 exp2_f16x2(float x, float y) {
   return __half22float2(*reinterpret_cast<const __half2*>(&e));
 }
 
+// packed fp32 pairs (one instruction for two lanes of work, sm_100)
+__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
+        "l"(*reinterpret_cast<const uint64_t*>(&c)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+
 // K/V tiles of KT keys that the 128 queries from q_start see (causal: keys up to the last query of the tile)
 template <int KT>
 __device__ __forceinline__ int kv_tiles_of(const Params& p, int q_start) {
@@ -125,6 +150,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                        const __grid_constant__ CUtensorMap map_v, Params p) {
   using L = Layout<D>;
   constexpr int KT = L::KT;
+  constexpr int kStages = L::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* q_full = reinterpret_cast<uint64_t*>(smem + L::kBar);
@@ -164,11 +190,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   // the ones operand of the row-sum MMA: row 0 of each 64-key box is all ones (the swizzle only permutes 16-byte
   // chunks inside a row, so a row of ones needs none), rows 1-15 are zero
-  for (int i = threadIdx.x; i < L::kOnesBytes / 16; i += kThreads) {
-    const uint32_t one = (i % 128) < 8 ? 0x3F803F80u : 0u;
-    reinterpret_cast<uint4*>(smem + L::kOnes)[i] = make_uint4(one, one, one, one);
+  if constexpr (L::kRowSumMma) {
+    for (int i = threadIdx.x; i < L::kOnesBytes / 16; i += kThreads) {
+      const uint32_t one = (i % 128) < 8 ? 0x3F803F80u : 0u;
+      reinterpret_cast<uint4*>(smem + L::kOnes)[i] = make_uint4(one, one, one, one);
+    }
+    fence_async_smem();
   }
-  fence_async_smem();
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&map_q);
     tma_prefetch_desc(&map_k);
@@ -223,36 +251,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       int ns0 = 0, ns1 = 0;  // next S to issue, per group
       int no0 = 0, no1 = 0;  // next O' to issue, per group
       int released = 0;      // K/V tiles whose stage went back to the producer
+      // The issuer shares its SM sub-partition with two softmax warps, so it gets a fraction of the issue slots:
+      // every descriptor below is a precomputed base plus a constant (the 14-bit address field holds bytes / 16),
+      // leaving about one add and the MMA itself per instruction.
+      const uint64_t dq0 = smem_desc_sw128(smem_u32(smem + L::kQ), 16, 1024);
+      const uint64_t dk0 = smem_desc_sw128(smem_u32(smem + L::kKV), 16, 1024);
+      const uint64_t dv0 = smem_desc_sw128(smem_u32(smem + L::kKV + L::kKVBytes), KT * 128, 1024);
+      const uint64_t d1 = smem_desc_sw128(sones, 16, 1024);
       auto issue_s = [&](int g, int j) {
-        const int st = j % kStages;
+        const uint64_t dq = dq0 + static_cast<uint32_t>(g * (L::kQBytes >> 4));
+        const uint64_t dk = dk0 + static_cast<uint32_t>((j % kStages) * ((2 * L::kKVBytes) >> 4));
+        const uint32_t d = tmem + g * KT;
         tc_fence_after();
-        const uint32_t sq = smem_u32(smem + L::kQ + g * L::kQBytes);
-        const uint32_t sk = smem_u32(smem + L::kKV + st * 2 * L::kKVBytes);
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) {  // 16 head-dim columns per MMA: 32 bytes inside a 128-byte box
-          const uint32_t oq = (k / 4) * (kTile * 128) + (k % 4) * 32;
-          const uint32_t ok_ = (k / 4) * (KT * 128) + (k % 4) * 32;
-          umma_bf16(tmem + g * KT, smem_desc_sw128(sq + oq, 16, 1024), smem_desc_sw128(sk + ok_, 16, 1024),
+        for (int k = 0; k < D / 16; ++k)  // 16 head-dim columns per MMA: 32 bytes inside a 128-byte box
+          umma_bf16(d, dq + (((k / 4) * (kTile * 128) + (k % 4) * 32) >> 4), dk + (((k / 4) * (KT * 128) + (k % 4) * 32) >> 4),
                     id_s, k > 0 ? 1u : 0u);
-        }
         umma_commit(&s_full[g]);
         trace_mark(trace, j, g, 4);
       };
       auto issue_o = [&](int g, int j) {
-        const int st = j % kStages;
+        const uint64_t dv = dv0 + static_cast<uint32_t>((j % kStages) * ((2 * L::kKVBytes) >> 4));
+        const uint32_t a0 = tmem + L::kTmemP + g * (KT / 2);
+        const uint32_t d = tmem + L::kTmemO + g * D;
+        const uint32_t first = j > 0 ? 1u : 0u;
         tc_fence_after();
-        const uint32_t sp = smem_u32(smem + L::kP + g * L::kPBytes);
-        const uint32_t sv = smem_u32(smem + L::kKV + st * 2 * L::kKVBytes + L::kKVBytes);
 #pragma unroll
         for (int k = 0; k < KT / 16; ++k) {
-          // A = P (K-major, keys in 64-wide boxes); B = V read MN-major: 16 keys = 16 rows of 128 B per step,
-          // 64-wide head-dim blocks one box (KT rows) apart
-          const uint64_t a = smem_desc_sw128(sp + (k / 4) * (kTile * 128) + (k % 4) * 32, 16, 1024);
-          const uint64_t bv = smem_desc_sw128(sv + k * 2048, KT * 128, 1024);
-          umma_bf16(tmem + L::kTmemO + g * D, a, bv, id_o, (j > 0 || k > 0) ? 1u : 0u);
-          // l_g += P_g 1: the row sums, from the same A operand and the K-major ones row
-          const uint64_t b1 = smem_desc_sw128(sones + (k / 4) * (16 * 128) + (k % 4) * 32, 16, 1024);
-          umma_bf16(tmem + L::kTmemL + g * 16, a, b1, id_l, (j > 0 || k > 0) ? 1u : 0u);
+          // A = P_g from TMEM (16 keys = 8 columns per step); B = V read MN-major: 16 keys = 16 rows of 128 B per
+          // step, 64-wide head-dim blocks one box (KT rows) apart
+          umma_bf16_ts(d, a0 + k * 8, dv + ((k * 2048) >> 4), id_o, k > 0 ? 1u : first);
+          if constexpr (L::kRowSumMma)  // l_g += P_g 1: the row sums, from the same A and the K-major ones row
+            umma_bf16_ts(tmem + L::kTmemL + g * 16, a0 + k * 8, d1 + ((((k / 4) * (16 * 128) + (k % 4) * 32)) >> 4), id_l,
+                         k > 0 ? 1u : first);
         }
         umma_commit(&o_full[g]);
         trace_mark(trace, j, g, 5);
@@ -312,10 +343,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t ts = tmem + lane_off + g * KT;
     const uint32_t to = tmem + lane_off + L::kTmemO + g * D;
     const uint32_t tl = tmem + lane_off + L::kTmemL + g * 16;
-    uint8_t* prow = smem + L::kP + g * L::kPBytes + row * 128;
+    const uint32_t tp = tmem + lane_off + L::kTmemP + g * (KT / 2);
     unsigned long long* const gtrace = (quarter == 2 && lane == 0) ? trace : nullptr;
     const float sl2 = p.scale_log2;
     float m_ref = -INFINITY;  // the maximum O_g and l_g are expressed against (base-2, scaled)
+    float l_sum = 0.f;        // row sum of the probabilities (head_dim 64; at 128 the tensor core forms it)
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       if (__any_sync(0xffffffffu, *abort_flag != 0)) { ok = false; break; }
@@ -356,14 +388,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // probabilities, two per instruction in half precision: the exponent s*scale*log2e - m_ref lies in [-inf, 8]
       // thanks to the lazy rescale, so its f16 rounding keeps ~11 bits where the probabilities are large (the bf16
-      // probabilities keep 8). The row sum is not formed here: the tensor core accumulates it (P times a ones row).
-      const float neg_m = -m_ref;
+      // probabilities keep 8)
+      const float2 scale2 = make_float2(sl2, sl2), neg_m2 = make_float2(-m_ref, -m_ref);
       uint32_t pk[KT / 2];
+      float2 sum2 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int i = 0; i < KT / 2; ++i) {
-        const float2 e = exp2_f16x2(fmaf(v[2 * i], sl2, neg_m), fmaf(v[2 * i + 1], sl2, neg_m));
+        const float2 x = fma_f32x2(make_float2(v[2 * i], v[2 * i + 1]), scale2, neg_m2);
+        const float2 e = exp2_f16x2(x.x, x.y);
         pk[i] = pack_bf16(e.x, e.y);  // exp2(-inf) = 0 for masked keys
+        if constexpr (!L::kRowSumMma) sum2 = add_f32x2(sum2, e);
       }
+      const float tile_sum = sum2.x + sum2.y;
       trace_mark(gtrace, j, g, 1);
       // O_g += P_g(j-1) V_{j-1} must have finished before its P buffer is rewritten or O_g is rescaled
       if (j > 0 && !__all_sync(0xffffffffu, mbar_sleep_wait(&o_full[g], (j - 1) & 1, kTimeoutAccum))) {
@@ -371,13 +407,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       trace_mark(gtrace, j, g, 2);
+      tc_fence_after();
 #pragma unroll
-      for (int c8 = 0; c8 < KT / 8; ++c8) {  // 8 keys -> one 16-byte chunk of the K-major swizzled P tile
-        const int box = c8 / 8;
-        const int swz = (c8 % 8) ^ (row & 7);
-        *reinterpret_cast<uint4*>(prow + box * (kTile * 128) + swz * 16) =
-            make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
-      }
+      for (int c = 0; c < KT / 2; c += 32) tmem_st32u(tp + c, pk + c);  // P_g(j): row = lane, key pairs = columns
+      if constexpr (!L::kRowSumMma) l_sum = fmaf(l_sum, factor, tile_sum);
       if (rescale) {  // O_g and l_g to the new reference before the next P V accumulates into them
         tc_fence_after();
 #pragma unroll
@@ -388,15 +421,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) o[i] *= factor;
           tmem_st32(to + c, o);
         }
-        float l[16];
-        tmem_ld16(tl, l);
+        if constexpr (L::kRowSumMma) {
+          float l[16];
+          tmem_ld16(tl, l);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) l[i] *= factor;
-        tmem_st16(tl, l);
-        tmem_st_wait();
+          for (int i = 0; i < 16; ++i) l[i] *= factor;
+          tmem_st16(tl, l);
+        }
       }
+      tmem_st_wait();  // P (and the rescaled O) are in TMEM before the issuer may read them
       tc_fence_before();
-      fence_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[g]);
       trace_mark(gtrace, j, g, 3);
@@ -406,9 +440,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       *abort_flag = 1;
     } else if (n > 0) {
       tc_fence_after();
-      float l[16];
-      tmem_ld16(tl, l);  // column 0: the row sum of the probabilities, relative to m_ref
-      const float l_sum = l[0];
+      if constexpr (L::kRowSumMma) {
+        float l[16];
+        tmem_ld16(tl, l);  // column 0: the row sum of the probabilities, relative to m_ref
+        l_sum = l[0];
+      }
       const float inv = 1.f / l_sum;
       bf16* out = p.o + (static_cast<int64_t>(b) * p.S + q) * p.ldo + hq * D;
 #pragma unroll

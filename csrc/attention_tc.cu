@@ -87,6 +87,17 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Optional timeline of CTA (0, 0) (clock64 of its SM) for tuning: null unless armed from the host (attn_bwd_trace).
+// Slots of tile t of pass m (0 dK/dV, 1 dQ) at 4 * (32 m + t): 0 S/dP issued, 1 scores ready (softmax), 2 P/dS
+// written, 3 accumulation issued.
+constexpr int kTraceTiles = 32;
+static __device__ unsigned long long* g_attn_bwd_trace;
+
+template <int MODE>
+__device__ __forceinline__ void trace_mark(unsigned long long* tr, int t, int slot) {
+  if (tr && t < kTraceTiles) tr[4 * (MODE * kTraceTiles + t) + slot] = clock64();
+}
+
 __device__ __forceinline__ void store_row16(bf16* dst, const float* v, float mul) {
 #pragma unroll
   for (int i = 0; i < 16; i += 8) {
@@ -123,6 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  unsigned long long* const trace = (blockIdx.x == 0 && blockIdx.y == 0) ? g_attn_bwd_trace : nullptr;
   const int group = p.Hq / p.Hkv;
   int b, hk, hq, row0, n, per_head;
   if (MODE == kDKDV) {
@@ -257,45 +269,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         return mbar_test(&full[t % kStages], (t / kStages) & 1) &&
                (t < 2 || mbar_test(&s_empty[t & 1], ((t >> 1) - 1) & 1));
       };
+      // The issuer shares its SM sub-partition with four softmax warps, so it gets a fraction of the issue slots:
+      // every descriptor below is a precomputed base plus a constant (the 14-bit address field holds bytes / 16),
+      // leaving about one add and the MMA itself per instruction.
+      const uint64_t dx1 = smem_desc_sw128(sx1, 16, 1024), dx2 = smem_desc_sw128(sx2, 16, 1024);
+      const uint64_t dy0 = smem_desc_sw128(smem_u32(smem + L::kY), 16, 1024);             // stage 0 Y1, K-major
+      const uint64_t dyt0 = smem_desc_sw128(smem_u32(smem + L::kY), kCols * 128, 1024);  // stage 0 Y1, MN-major
+      const uint64_t do0 = smem_desc_sw128(smem_u32(smem + L::kO), 16, 1024);
+      constexpr uint32_t kY2 = L::kYBytes >> 4;
       auto issue_s = [&](int t) {
-        const int st = t % kStages;
         const int buf = t & 1;
-        tc_fence_after();
-        const uint32_t sy1 = smem_u32(smem + L::kY + st * 2 * L::kYBytes), sy2 = sy1 + L::kYBytes;
+        const uint32_t ys = static_cast<uint32_t>((t % kStages) * ((2 * L::kYBytes) >> 4));
         const uint32_t ts = tmem + buf * kCols, tdp = tmem + 128 + buf * kCols;
+        tc_fence_after();
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t ox = (k / 4) * (kRows * 128) + (k % 4) * 32;
-          const uint32_t oy = (k / 4) * (kCols * 128) + (k % 4) * 32;
-          umma_bf16(ts, smem_desc_sw128(sx1 + ox, 16, 1024), smem_desc_sw128(sy1 + oy, 16, 1024), id_s,
-                    k > 0 ? 1u : 0u);
-          umma_bf16(tdp, smem_desc_sw128(sx2 + ox, 16, 1024), smem_desc_sw128(sy2 + oy, 16, 1024), id_s,
-                    k > 0 ? 1u : 0u);
+          const uint32_t ox = ((k / 4) * (kRows * 128) + (k % 4) * 32) >> 4;
+          const uint32_t oy = ((k / 4) * (kCols * 128) + (k % 4) * 32) >> 4;
+          umma_bf16(ts, dx1 + ox, dy0 + ys + oy, id_s, k > 0 ? 1u : 0u);
+          umma_bf16(tdp, dx2 + ox, dy0 + ys + kY2 + oy, id_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[buf]);
+        trace_mark<MODE>(trace, t, 0);
       };
       // accumulation of tile j once the softmax group has written its P/dS operands
       auto issue_acc = [&](int j) {
         const int buf = j & 1;
         const int st = j % kStages;
+        const uint64_t b1 = dyt0 + static_cast<uint32_t>(st * ((2 * L::kYBytes) >> 4)), b2 = b1 + kY2;
+        const uint64_t a0 = do0 + static_cast<uint32_t>(buf * ((L::kONum * L::kOBytes) >> 4));
+        const uint32_t first = j > 0 ? 1u : 0u;
         tc_fence_after();
-        const uint32_t sy1 = smem_u32(smem + L::kY + st * 2 * L::kYBytes), sy2 = sy1 + L::kYBytes;
-        const uint32_t so = smem_u32(smem + L::kO + buf * L::kONum * L::kOBytes);
 #pragma unroll
         for (int k = 0; k < kCols / 16; ++k) {
-          const uint32_t acc = (j > 0 || k > 0) ? 1u : 0u;
+          const uint32_t acc = k > 0 ? 1u : first;
           // B operands are the column tiles read MN-major: 64-wide MN blocks one box apart, K rows of 128 B
-          const uint64_t b1 = smem_desc_sw128(sy1 + k * 2048, kCols * 128, 1024);
-          const uint64_t b2 = smem_desc_sw128(sy2 + k * 2048, kCols * 128, 1024);
+          const uint32_t ob = (k * 2048) >> 4, oa = (k * 32) >> 4;
           if (MODE == kDKDV) {
-            umma_bf16(tmem + 256, smem_desc_sw128(so + k * 32, 16, 1024), b2, id_acc, acc);                  // dV
-            umma_bf16(tmem + 256 + D, smem_desc_sw128(so + L::kOBytes + k * 32, 16, 1024), b1, id_acc, acc);  // dK
+            umma_bf16(tmem + 256, a0 + oa, b2 + ob, id_acc, acc);                               // dV
+            umma_bf16(tmem + 256 + D, a0 + (L::kOBytes >> 4) + oa, b1 + ob, id_acc, acc);       // dK
           } else {
-            umma_bf16(tmem + 256, smem_desc_sw128(so + k * 32, 16, 1024), b1, id_acc, acc);  // dQ
+            umma_bf16(tmem + 256, a0 + oa, b1 + ob, id_acc, acc);  // dQ
           }
         }
         umma_commit(&empty[st]);
         umma_commit(&p_empty[buf]);
+        trace_mark<MODE>(trace, j, 3);
       };
       bool ok = mbar_sleep_wait(x_full, 0, kTimeoutFull);
       tc_fence_after();
@@ -357,6 +376,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = grp;
       const uint32_t use = (j >> 1) & 1;
       if (!__all_sync(0xffffffffu, mbar_sleep_wait(&s_full[buf], use, kTimeoutAccum))) { *abort_flag = 1; ok = false; break; }
+      if (sw % 8 == 0 && lane == 0) trace_mark<MODE>(trace, j, 1);
       tc_fence_after();
       float s[32], dp[32];
       tmem_ld32_pair(tmem + lane_off + buf * kCols + half * 32, tmem + lane_off + 128 + buf * kCols + half * 32, s, dp);
@@ -429,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_async_smem();  // generic-proxy stores -> visible to the tensor core's async proxy
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[buf]);
+      if (sw % 8 == 0 && lane == 0) trace_mark<MODE>(trace, j, 2);
     }
     // epilogue: accumulators -> bf16 rows (dK and dQ carry the softmax scale). dK/dV: group 0 stores dV, group 1
     // dK, each half of the columns; dQ: each (group, half) a quarter of the columns.
@@ -539,5 +560,11 @@ void flash_attn_bwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, c
 }
 
 int attention_tc_status(bool clear) { return read_status_word(clear); }
+
+// Arms (buf: 2 * 4 * kTraceTiles int64 slots) or disarms (null) the backward's timeline trace.
+void attn_bwd_trace(void* buf) {
+  unsigned long long* ptr = static_cast<unsigned long long*>(buf);
+  check_cuda(cudaMemcpyToSymbol(attn_tc::g_attn_bwd_trace, &ptr, sizeof(ptr)), "attention backward trace");
+}
 
 }  // namespace qw

@@ -783,6 +783,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_broadcast", &p2p_broadcast);
   m.def("p2p_wait", &p2p_wait);
   m.def("read_status", &read_status, py::arg("clear") = true);
+  m.def("attn_bwd_trace", [](c10::optional<torch::Tensor> buf) {
+    if (buf) {
+      TORCH_CHECK(buf->is_cuda() && buf->dtype() == torch::kInt64 && buf->numel() >= 64 * 4 && buf->is_contiguous(),
+                  "attn_bwd_trace: a contiguous CUDA int64 tensor of at least 256 elements");
+      qw::attn_bwd_trace(buf->data_ptr());
+    } else {
+      qw::attn_bwd_trace(nullptr);
+    }
+  });
   m.def("attn_fwd_trace", [](c10::optional<torch::Tensor> buf) {
     if (buf) {
       TORCH_CHECK(buf->is_cuda() && buf->dtype() == torch::kInt64 && buf->numel() >= 32 * 2 * 8 && buf->is_contiguous(),

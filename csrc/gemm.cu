@@ -102,26 +102,33 @@ static int num_sms() {
   return n;
 }
 
-// Maps of the TMA epilogue (output, residual, raw gate|up); unused ones stay zero.
-struct OutMaps {
-  CUtensorMap out{}, res{}, gu{};
-};
-
-// Whether bf16 outputs go through TMA boxes (the default); QW_GEMM_TMA_EPI=0 keeps the per-thread stores.
-static bool tma_epilogue_enabled() {
+// Whether bf16 outputs go through the staged (coalesced) epilogue, the default; QW_GEMM_STAGED_EPI=0 keeps the
+// per-thread stores.
+static bool staged_epilogue_enabled() {
   static const bool on = [] {
-    const char* e = std::getenv("QW_GEMM_TMA_EPI");
+    const char* e = std::getenv("QW_GEMM_STAGED_EPI");
     return !(e && std::string(e) == "0");
   }();
   return on;
 }
 
-// A [rows, cols] bf16 map with 32-row x 64-column boxes for the epilogue, or false when the buffer's alignment
-// rules one out (then the per-thread epilogue runs).
+// Maps of the TMA epilogue (output, residual, raw gate|up); unused ones stay zero.
+struct OutMaps {
+  CUtensorMap out{}, res{}, gu{};
+};
+
+// A [rows, cols] bf16 map with 32-row x 64-column boxes (128-byte swizzle) for the TMA epilogue, or false when the
+// buffer's alignment rules one out.
 static bool epi_map(CUtensorMap& m, const void* ptr, int64_t cols, int64_t rows, int64_t ld) {
   if (!ptr || rows <= 0 || (reinterpret_cast<uintptr_t>(ptr) & 15) || (ld * 2) % 16) return false;
   m = make_map(ptr, cols, rows, ld, 64, 32);
   return true;
+}
+
+// The staged epilogue moves 16-byte chunks: the buffer and its row stride (ld elements of esize bytes) must be
+// 16-byte aligned.
+static bool aligned16(const void* ptr, int64_t ld, int esize = 2) {
+  return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && (ld * esize) % 16 == 0;
 }
 
 template <int BN, int MODE, int EPI, bool A_MN, bool B_MN>
@@ -167,8 +174,10 @@ void linear_fwd(const bf16* x, int64_t ldx, const bf16* w, int64_t ldw, int64_t 
   auto ma = make_map(x, K, M, ldx, 64, kBM);
   auto mb = make_map(w, K, N, ldw, 64, BN);
   OutMaps outs;
-  p.tma_out = tma_epilogue_enabled() && !out_fp32 && epi_map(outs.out, out, N, M, ldo) &&
+  p.tma_out = staged_epilogue_enabled() && !out_fp32 && epi_map(outs.out, out, N, M, ldo) &&
               (!residual || epi_map(outs.res, residual, N, M, ldr));
+  p.staged_out = !p.tma_out && staged_epilogue_enabled() && N % 8 == 0 && aligned16(out, ldo, out_fp32 ? 4 : 2) &&
+                 (!residual || (!out_fp32 && aligned16(residual, ldr)));
   launch<BN, kGroupM, kEpiStore, false, false>(ma, mb, p, ((M + kBM - 1) / kBM) * p.n_tiles, stream, outs);
 }
 
@@ -186,7 +195,9 @@ void linear_dgrad(const bf16* dy, int64_t lddy, const bf16* w, int64_t ldw, int6
   auto ma = make_map(dy, N, M, lddy, 64, kBM);
   auto mb = make_map(w, K, N, ldw, 64, 64);
   OutMaps outs;
-  p.tma_out = tma_epilogue_enabled() && !out_fp32 && !accumulate && epi_map(outs.out, dx, K, M, lddx);
+  p.tma_out = staged_epilogue_enabled() && !out_fp32 && !accumulate && epi_map(outs.out, dx, K, M, lddx);
+  p.staged_out = !p.tma_out && staged_epilogue_enabled() && (out_fp32 || !accumulate) && K % 8 == 0 &&
+                 aligned16(dx, lddx, out_fp32 ? 4 : 2);
   launch<BN, kGroupM, kEpiStore, false, true>(ma, mb, p, ((M + kBM - 1) / kBM) * p.n_tiles, stream, outs);
 }
 
@@ -201,6 +212,8 @@ void linear_wgrad(const bf16* dy, int64_t lddy, const bf16* x, int64_t ldx, int6
   p.m_tiles = static_cast<int>((N + kBM - 1) / kBM);
   p.n_tiles = static_cast<int>((K + BN - 1) / BN);
   p.out = dw; p.ldo = lddw; p.out_fp32 = out_fp32; p.accumulate = accumulate;
+  p.staged_out = staged_epilogue_enabled() && (out_fp32 || !accumulate) && K % 8 == 0 &&
+                 aligned16(dw, lddw, out_fp32 ? 4 : 2);
   auto ma = make_map(dy, N, std::max<int64_t>(T, 1), lddy, 64, 64);
   auto mb = make_map(x, K, std::max<int64_t>(T, 1), ldx, 64, 64);
   launch<BN, kGroupK, kEpiStore, true, true>(ma, mb, p, static_cast<int64_t>(p.m_tiles) * p.n_tiles, stream);
@@ -256,6 +269,7 @@ void linear_wgrad_chunks(const bf16* dy, int64_t lddy, const bf16* x, int64_t ld
   p.n_tiles = static_cast<int>((K + BN - 1) / BN);
   p.out = partial; p.ldo = K; p.out_fp32 = 1;
   p.out_group_stride = N * K;
+  p.staged_out = staged_epilogue_enabled() && K % 8 == 0 && aligned16(partial, K, 4);
   auto ma = make_map(dy, N, T, lddy, 64, 64);
   auto mb = make_map(x, K, T, ldx, 64, 64);
   launch<BN, kGroupK, kEpiStore, true, true>(ma, mb, p,
@@ -287,8 +301,10 @@ void moe_gate_up_fwd(const bf16* x, const bf16* w_gate_up, const int* counts, co
   auto ma = make_map(x, H, R, H, 64, kBM);
   auto mb = make_map(w_gate_up, H, E * 2 * F, H, 64, BN / 2);
   OutMaps outs;
-  p.tma_out = tma_epilogue_enabled() && F % 8 == 0 && epi_map(outs.out, h, F, R, F) &&
+  p.tma_out = staged_epilogue_enabled() && F % 8 == 0 && epi_map(outs.out, h, F, R, F) &&
               (!gu || epi_map(outs.gu, gu, 2 * F, R, 2 * F));
+  p.staged_out = !p.tma_out && staged_epilogue_enabled() && F % 64 == 0 && aligned16(h, F) &&
+                 (!gu || aligned16(gu, 2 * F));
   launch<BN, kGroupM, kEpiSwiGLU, false, false>(ma, mb, p, p.max_tiles, stream, outs);
 }
 
@@ -315,7 +331,7 @@ void moe_down_fwd(const bf16* h, const bf16* w_down, const int* counts, const in
   auto ma = make_map(h, F, R, F, 64, kBM);
   auto mb = make_map(w_down, F, E * H, F, 64, BN);
   OutMaps outs;
-  p.tma_out = tma_epilogue_enabled() && !peer_out && epi_map(outs.out, y, H, R, H);
+  p.tma_out = staged_epilogue_enabled() && !peer_out && epi_map(outs.out, y, H, R, H);
   launch<BN, kGroupM, kEpiStore, false, false>(ma, mb, p, p.max_tiles, stream, outs);
 }
 
@@ -368,7 +384,7 @@ void moe_gate_up_dgrad(const bf16* dgu, const bf16* w_gate_up, const int* counts
   auto ma = make_map(dgu, 2 * F, R, 2 * F, 64, kBM);
   auto mb = make_map(w_gate_up, H, E * 2 * F, H, 64, 64);
   OutMaps outs;
-  p.tma_out = tma_epilogue_enabled() && !peer_out && epi_map(outs.out, dx, H, R, H);
+  p.tma_out = staged_epilogue_enabled() && !peer_out && epi_map(outs.out, dx, H, R, H);
   launch<BN, kGroupM, kEpiStore, false, true>(ma, mb, p, p.max_tiles, stream, outs);
 }
 
@@ -387,6 +403,8 @@ void moe_wgrad(const bf16* a, const bf16* b, const int* counts, const int* offse
   p.out = out; p.ldo = N;
   p.out_group_stride = M * N;
   p.out_fp32 = out_fp32; p.accumulate = accumulate;
+  p.staged_out = staged_epilogue_enabled() && (out_fp32 || !accumulate) && N % 8 == 0 &&
+                 aligned16(out, N, out_fp32 ? 4 : 2);
   auto ma = make_map(a, M, std::max<int64_t>(R, 1), M, 64, 64);
   auto mb = make_map(b, N, std::max<int64_t>(R, 1), N, 64, 64);
   launch<BN, kGroupK, kEpiStore, true, true>(ma, mb, p, static_cast<int64_t>(p.m_tiles) * p.n_tiles * E, stream);

@@ -10,11 +10,11 @@
 //              last k-block of a tile it commits `accum_full[b]`.
 //   warps 2-5  epilogue: tcgen05.ld the 128 x BN accumulator (warp w owns TMEM lanes 32*(w%4)..+31 = tile rows),
 //              apply the fused epilogue and store to global memory, then release the buffer (`accum_empty[b]`).
-//              bf16 outputs go out through TMA: the warp writes its 32 rows x 64 columns into a 128-byte-swizzled
-//              shared-memory box and one lane issues a bulk tensor store (a residual is brought in the same way by a
-//              TMA load into that box). One thread per row storing 16 bytes to 32 different rows per instruction
-//              left the epilogue at ~2.5x the k-loop time of a K = 1024 tile; the bulk store writes whole lines.
-//              fp32 outputs, read-modify-write accumulation and stores into peers' memory keep the per-thread path.
+//              bf16 outputs go through a per-warp shared-memory box: each lane writes its row, then the warp
+//              stores 4 whole 128-byte rows per instruction (a residual comes in the same way). One thread per row
+//              storing 16 bytes to 32 different rows per instruction left the epilogue at ~2.5x the k-loop time of
+//              a K = 1024 tile. fp32 outputs, read-modify-write accumulation and stores into peers' memory keep the
+//              per-thread path.
 //
 // Tile schedules (device-side, no host synchronisation):
 //   kGroupM  grouped over rows: group g owns rows [row_off[g], row_off[g]+rows[g]) of A and C, and its own B
@@ -82,10 +82,11 @@ struct Params {
   const float* route_w;        // kEpiSwiGLUBwd: per-row route weight
   __nv_bfloat16* h_out;        // kEpiSwiGLUBwd: optional H = silu(g)*u, ld = F
   float* dw_partial;           // kEpiSwiGLUBwd: [rows, n_tiles] partial <dH_raw, H>
-  int tma_out;                 // kGroupM store / SwiGLU epilogues: bf16 out (and residual, gu) through TMA boxes
+  int staged_out;              // store / SwiGLU epilogues: out through a shared-memory box, coalesced stores
+  int tma_out;                 // kGroupM store / SwiGLU, bf16: out (and residual, gu) through TMA boxes instead
 };
 
-constexpr int kStgBytes = 32 * 128;  // one epilogue warp's TMA box: 32 rows x 64 bf16, 128-byte swizzle
+constexpr int kStgBytes = 32 * 128;  // one epilogue warp's staging box: 32 rows x 64 bf16 (128-byte rows)
 
 template <int BN>
 struct Smem {
@@ -141,6 +142,69 @@ __device__ __forceinline__ void box_release(const TmaEpi& e, const CUtensorMap* 
   __syncwarp();
   if (lane == 0) tma_store_2d(map, e.box.base, x, e.row);
 }
+
+// Staged epilogue of one warp: its 32 rows x 64 columns pass through a shared-memory box so that global memory sees
+// whole 128-byte lines. Lane r owns accumulator row r and writes it into the box (16-byte chunk q at q ^ (r % 8),
+// so the 32 lanes' chunks fall on distinct banks); then lane l moves chunk l % 8 of rows l / 8 + 4i, i < 8: one
+// 16-byte load or store instruction covers 4 full rows.
+struct StagedEpi {
+  uint8_t* box;  // 4 KB
+  int lane;
+  long out_rows;  // rows of the output that exist (dense tail); grouped tiles write their padded rows
+  __device__ __forceinline__ uint4* own(int q) const {  // chunk q of the lane's own row
+    return reinterpret_cast<uint4*>(box + lane * 128 + ((q ^ (lane & 7)) << 4));
+  }
+  __device__ __forceinline__ uint4* moved(int i) const {  // the chunk this lane moves in step i
+    const int r = lane / 8 + 4 * i;
+    return reinterpret_cast<uint4*>(box + r * 128 + (((lane & 7) ^ (r & 7)) << 4));
+  }
+  __device__ __forceinline__ void put(const float* v) const {  // 64 values of the lane's row, rounded to bf16
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *own(q) = make_uint4(pack_bf16(v[8 * q], v[8 * q + 1]), pack_bf16(v[8 * q + 2], v[8 * q + 3]),
+                           pack_bf16(v[8 * q + 4], v[8 * q + 5]), pack_bf16(v[8 * q + 6], v[8 * q + 7]));
+  }
+  __device__ __forceinline__ void put_f32(const float* v) const {  // 32 fp32 values of the lane's row
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      *own(q) = make_uint4(__float_as_uint(v[4 * q]), __float_as_uint(v[4 * q + 1]), __float_as_uint(v[4 * q + 2]),
+                           __float_as_uint(v[4 * q + 3]));
+  }
+  // box -> 128 bytes at out + (row0 + r) * ld_bytes + col_bytes for rows below out_rows; chunks at or past
+  // lim_bytes (the end of the row) are skipped. fp32_add: add the existing fp32 values (read-modify-write).
+  __device__ __forceinline__ void flush(char* out, long ld_bytes, long row0, long col_bytes, long lim_bytes,
+                                        bool fp32_add = false) const {
+    __syncwarp();
+    const long cb = col_bytes + (lane & 7) * 16;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const long r = row0 + lane / 8 + 4 * i;
+      if (r < out_rows && cb < lim_bytes) {
+        uint4* dst = reinterpret_cast<uint4*>(out + r * ld_bytes + cb);
+        uint4 val = *moved(i);
+        if (fp32_add) {
+          const uint4 old = *dst;
+          val = make_uint4(__float_as_uint(__uint_as_float(val.x) + __uint_as_float(old.x)),
+                           __float_as_uint(__uint_as_float(val.y) + __uint_as_float(old.y)),
+                           __float_as_uint(__uint_as_float(val.z) + __uint_as_float(old.z)),
+                           __float_as_uint(__uint_as_float(val.w) + __uint_as_float(old.w)));
+        }
+        *dst = val;
+      }
+    }
+    __syncwarp();  // the box is free again
+  }
+  // 128 bytes of res rows row0 + r at col_bytes -> box, read back by the row owners with own()
+  __device__ __forceinline__ void fetch(const char* res, long ld_bytes, long row0, long col_bytes) const {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const long r = row0 + lane / 8 + 4 * i;
+      *moved(i) = r < out_rows ? *reinterpret_cast<const uint4*>(res + r * ld_bytes + col_bytes + (lane & 7) * 16)
+                               : make_uint4(0, 0, 0, 0);
+    }
+    __syncwarp();
+  }
+};
 
 // Optional per-tile timestamps of CTA 0 (clock64 of its SM) for tuning: null unless armed from the host
 // (gemm_trace). Slots per tile: 0/1 producer first wait / last load issued, 2/3 issuer before / after the
@@ -209,7 +273,7 @@ __device__ __forceinline__ bool tile_info(const Params& p, const int* s_prefix, 
 }
 
 // ---------------------------------------------------------------------------------------------------------
-// epilogue: one thread = one accumulator row, 32 columns at a time
+// epilogues: one thread = one accumulator row
 // ---------------------------------------------------------------------------------------------------------
 // TMA variant of the store and SwiGLU epilogues (bf16 out, no read-modify-write accumulation, local memory)
 template <int BN, int EPI>
@@ -300,6 +364,95 @@ __device__ __forceinline__ void epilogue_tile_tma(const Params& p, const TileInf
           box_release(e, e.map_gu, half * p.ffn + f0 + c, lane);
         }
       }
+    }
+  }
+}
+
+// Staged variant of the store and SwiGLU epilogues (N a multiple of 8; bf16 out without read-modify-write, or fp32
+// out with or without it; local memory). kGroupK writes group g's block at out + g * out_group_stride.
+template <int BN, int MODE, int EPI>
+__device__ __forceinline__ void epilogue_tile_staged(const Params& p, const TileInfo& t, uint32_t tmem_acc,
+                                                     int row_in_tile, int warp_lane_base, const StagedEpi& e) {
+  const uint32_t tbase = tmem_acc + (static_cast<uint32_t>(warp_lane_base) << 16);
+  if (EPI == kEpiStore) {
+    const bool empty_k = (t.num_kb == 0);
+    const int n0 = t.n_tile * BN;
+    const long row0 = (MODE == kGroupM ? t.row0 : static_cast<long>(t.m_tile) * kBM) + warp_lane_base;
+    const bool row_ok = MODE == kGroupM ? row_in_tile < t.rows : row0 + (row_in_tile - warp_lane_base) < p.M;
+    const int esize = p.out_fp32 ? 4 : 2;
+    char* out = static_cast<char*>(p.out);
+    if (MODE == kGroupK) out += static_cast<long>(t.group) * p.out_group_stride * esize;
+    const long ld_bytes = p.ldo * esize, lim_bytes = static_cast<long>(p.N) * esize;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 64) {
+      float v[64];
+      if (!empty_k) {
+        tmem_ld32_pair(tbase + c, tbase + c + 32, v, v + 32);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) v[i] = 0.f;
+      }
+      const int col = n0 + c;
+      if (col >= p.N) continue;  // warp-uniform: the box lies past the last column
+      const bool full = col + 64 <= p.N;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        float x = row_ok ? v[i] * p.alpha : 0.f;
+        if (row_ok && p.bias) x += (full || col + i < p.N) ? p.bias[col + i] : 0.f;
+        v[i] = x;
+      }
+      if (p.out_fp32) {  // two boxes of 32 fp32 columns
+        e.put_f32(v);
+        e.flush(out, ld_bytes, row0, static_cast<long>(col) * 4, lim_bytes, p.accumulate != 0);
+        if (col + 32 < p.N) {
+          e.put_f32(v + 32);
+          e.flush(out, ld_bytes, row0, static_cast<long>(col + 32) * 4, lim_bytes, p.accumulate != 0);
+        }
+        continue;
+      }
+      if (p.residual) {  // the residual box comes in through the same shared memory, coalesced
+        e.fetch(reinterpret_cast<const char*>(p.residual), p.ldr * 2, row0, static_cast<long>(col) * 2);
+        if (row_ok) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 r = *e.own(q);
+            const __nv_bfloat16* rb = reinterpret_cast<const __nv_bfloat16*>(&r);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * q + i] += __bfloat162float(rb[i]);
+          }
+        }
+        __syncwarp();
+      }
+      e.put(v);
+      e.flush(out, ld_bytes, row0, static_cast<long>(col) * 2, lim_bytes);
+    }
+  } else {  // kEpiSwiGLU: acc columns [0, BN/2) = gate, [BN/2, BN) = up for FFN columns f0 + [0, BN/2)
+    constexpr int HALF = BN / 2;
+    const int f0 = t.n_tile * HALF;
+    const bool row_ok = row_in_tile < t.rows;
+    const long row0 = t.row0 + warp_lane_base;
+    char* h = static_cast<char*>(p.out);
+#pragma unroll 1
+    for (int c = 0; c < HALF; c += 64) {
+      if (f0 + c >= p.ffn) break;  // warp-uniform (F is a multiple of 64 on this path)
+      float g[64], u[64];
+      tmem_ld32_pair(tbase + c, tbase + c + 32, g, g + 32);
+      tmem_ld32_pair(tbase + HALF + c, tbase + HALF + c + 32, u, u + 32);
+      if (!row_ok) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) { g[i] = 0.f; u[i] = 0.f; }
+      }
+      if (p.gu_out) {  // raw gate and up rows first (g and u are overwritten below)
+        char* gu = reinterpret_cast<char*>(p.gu_out);
+        e.put(g);
+        e.flush(gu, 4L * p.ffn, row0, 2L * (f0 + c), 4L * p.ffn);
+        e.put(u);
+        e.flush(gu, 4L * p.ffn, row0, 2L * (p.ffn + f0 + c), 4L * p.ffn);
+      }
+#pragma unroll
+      for (int i = 0; i < 64; ++i) g[i] = __fdividef(g[i], 1.0f + __expf(-g[i])) * u[i];
+      e.put(g);
+      e.flush(h, p.ldo * 2, row0, 2L * (f0 + c), 2L * p.ffn);
     }
   }
 }
@@ -530,7 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + kStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* teardown = acc_empty + 2;
-  uint64_t* res_full = teardown + 1;  // [4] residual boxes of the epilogue warps
+  uint64_t* res_full = teardown + 1;  // [4] residual boxes of the epilogue warps (TMA epilogue)
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(res_full + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
   __shared__ int s_prefix[1025];
@@ -696,6 +849,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int lane_base = 32 * (warp % 4);
     const int row_in_tile = lane_base + lane;
+    const StagedEpi se{smem + S::kStg + (warp % 4) * kStgBytes, lane,
+                       (MODE == kGroupM && p.group_rows) ? LONG_MAX : static_cast<long>(p.M)};
     TmaEpi te{{smem + S::kStg + (warp % 4) * kStgBytes, lane}, &map_out, &map_res, &map_gu, &res_full[warp % 4], 0u, 0};
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -711,6 +866,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.tma_out) {
           te.row = t.row0 + lane_base;
           epilogue_tile_tma<BN, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base, te, lane);
+          trace_mark(etrace, local, 7);
+          tc_fence_before();
+          mbar_arrive(&acc_empty[acc]);
+          if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+          continue;
+        }
+      }
+      if constexpr (EPI == kEpiStore || (MODE == kGroupM && EPI == kEpiSwiGLU)) {
+        if (p.staged_out) {
+          epilogue_tile_staged<BN, MODE, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base, se);
         } else {
           epilogue_tile<BN, MODE, EPI>(p, t, tmem_base + acc * BN, row_in_tile, lane_base);
         }

@@ -43,7 +43,8 @@ void moe_wgrad(const bf16* a, const bf16* b, const int* counts, const int* offse
                int64_t M, int64_t N, void* out, bool out_fp32, bool accumulate, float alpha, cudaStream_t stream);
 int gemm_status(bool clear);
 void gemm_trace(void* buf);
-void attn_fwd_trace(void* buf);  // timeline of the forward's CTA (0, 0) (null disarms)  // per-tile clock64 timestamps of CTA 0 (null disarms)
+void attn_fwd_trace(void* buf);
+void attn_bwd_trace(void* buf);  // timeline of the backward's CTA (0, 0) (null disarms)  // timeline of the forward's CTA (0, 0) (null disarms)  // per-tile clock64 timestamps of CTA 0 (null disarms)
 int wgrad_split(int64_t T, int64_t N, int64_t K);
 void splitk_reduce(const float* partial, int chunks, int64_t rows, int64_t cols, void* out, int64_t ldo,
                    bool out_fp32, bool accumulate, cudaStream_t stream);
