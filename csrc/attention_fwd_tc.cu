@@ -105,38 +105,6 @@ __device__ __forceinline__ void trace_mark(unsigned long long* tr, int j, int g,
   if (tr && j < kTraceTiles) tr[(2 * j + g) * 8 + slot] = clock64();
 }
 
-// max(a, b, c) in one instruction (three-input max.f32, sm_100)
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float r;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-  return r;
-}
-
-// (2^x, 2^y) through one packed half-precision exponential (ex2.approx.f16x2), widened back to fp32
-__device__ __forceinline__ float2 exp2_f16x2(float x, float y) {
-  const __half2 h = __floats2half2_rn(x, y);
-  uint32_t e;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(*reinterpret_cast<const uint32_t*>(&h)));
-  return __half22float2(*reinterpret_cast<const __half2*>(&e));
-}
-
-// packed fp32 pairs (one instruction for two lanes of work, sm_100)
-__device__ __forceinline__ float2 fma_f32x2(float2 a, float2 b, float2 c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
-        "l"(*reinterpret_cast<const uint64_t*>(&c)));
-  return *reinterpret_cast<const float2*>(&d);
-}
-__device__ __forceinline__ float2 add_f32x2(float2 a, float2 b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)));
-  return *reinterpret_cast<const float2*>(&d);
-}
-
 // K/V tiles of KT keys that the 128 queries from q_start see (causal: keys up to the last query of the tile)
 template <int KT>
 __device__ __forceinline__ int kv_tiles_of(const Params& p, int q_start) {

@@ -419,24 +419,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 8; ++e) { lv[e] = row_lse2; dv[e] = row_delta; }
         }
 #pragma unroll
-        for (int e2 = 0; e2 < 4; ++e2) {  // column pairs
-          float pv[2], ds[2];
+        for (int e2 = 0; e2 < 4; ++e2) {  // column pairs: packed fp32x2 math, one f16x2 exponential per pair (the
+                                          // exponent s*scale*log2e - lse is <= 0 here: P <= 1, and its f16
+                                          // rounding keeps ~11 bits where P is large; P and dS go out in bf16)
+          const int e = 2 * e2, c = 8 * q + e;
+          const float2 arg = fma_f32x2(make_float2(s[c], s[c + 1]), make_float2(sl2, sl2),
+                                       make_float2(-lv[e], -lv[e + 1]));
+          float2 x = exp2_f16x2(arg.x, arg.y);
+          if (need_mask) {
 #pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int e = 2 * e2 + h2;
-            const int c = 8 * q + e;
-            float x = ex2(fmaf(s[c], sl2, -lv[e]));
-            if (need_mask) {
-              const int other = col0 + c;  // query (dK/dV) or key (dQ) index of this column
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int other = col0 + c + h2;  // query (dK/dV) or key (dQ) index of this column
               const bool bad = MODE == kDKDV ? (other < grow || other >= p.S || grow >= p.S)
                                              : (other > grow || other >= p.S || grow >= p.S);
-              if (bad) x = 0.f;
+              if (bad) (h2 ? x.y : x.x) = 0.f;
             }
-            pv[h2] = x;
-            ds[h2] = x * (dp[c] - dv[e]);
           }
-          pw[e2] = pack_bf16(pv[0], pv[1]);
-          dw[e2] = pack_bf16(ds[0], ds[1]);
+          const float2 ds = mul_f32x2(x, add_f32x2(make_float2(dp[c], dp[c + 1]), make_float2(-dv[e], -dv[e + 1])));
+          pw[e2] = pack_bf16(x.x, x.y);
+          dw[e2] = pack_bf16(ds.x, ds.y);
         }
         const int chunk = (half * 4 + q) ^ (row & 7);
         if (MODE == kDKDV) {

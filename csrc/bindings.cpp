@@ -684,6 +684,20 @@ void ep_decode_wait(Tensor flags, int64_t world, Tensor step, int64_t layer, int
                      static_cast<int>(layers), timeout_s, stream());
 }
 
+void decode_attention_rope(Tensor qkv, Tensor pos, Tensor cos_t, Tensor sin_t, bool rope, Tensor kc, Tensor vc,
+                           int64_t Hq, double scale, Tensor part_o, Tensor part_ml, Tensor tickets, Tensor out) {
+  CHECK_CUDA(qkv); CHECK_CONTIG(qkv); CHECK_CONTIG(kc); CHECK_CONTIG(vc); CHECK_CONTIG(out);
+  const int B = static_cast<int>(qkv.size(0)), Hkv = static_cast<int>(kc.size(1)), Lmax = static_cast<int>(kc.size(2));
+  const int D = static_cast<int>(kc.size(3));
+  TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * D, "decode_attention_rope: qkv width");
+  TORCH_CHECK(kc.size(0) >= B && pos.numel() >= B, "decode_attention_rope: batch");
+  c10::cuda::CUDAGuard g(qkv.device());
+  qw::decode_attention_rope(bptr(qkv), pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), rope,
+                            bptr_mut(kc), bptr_mut(vc), B, static_cast<int>(Hq), Hkv, D, Lmax,
+                            static_cast<float>(scale), part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+                            tickets.data_ptr<int>(), bptr_mut(out), stream());
+}
+
 void rope_append(Tensor qkv, Tensor pos, int64_t Hq, int64_t Hkv, Tensor cos_t, Tensor sin_t, bool rope, Tensor q_out,
                  Tensor kc, Tensor vc) {
   CHECK_CUDA(qkv); CHECK_CONTIG(qkv);
@@ -764,6 +778,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_route", &decode_route);
   m.def("decode_attention", &decode_attention);
   m.def("rope_append", &rope_append);
+  m.def("decode_attention_rope", &decode_attention_rope);
   m.def("ep_dispatch", &ep_dispatch);
   m.def("zero_rs_blocks", &zero_rs_blocks);
   m.def("zero_reduce_scatter", &zero_reduce_scatter);

@@ -131,13 +131,45 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
   const int n0 = (blockIdx.x * kGemvWarps + warp) * kGemvRows;
   const int64_t rb = F::row_bytes(a.K);
   const bool routed = a.active != nullptr || a.cnt != nullptr;
-  if (!routed && n0 < a.N) {  // weights do not depend on the previous kernel: start pulling them into L2
+  const int spr = (FMT == 2) ? a.K / a.group : 1;  // scales per row
+  const uint8_t* wrow[NW];
+  const __half* srow[NW];
+  bool ok[NW];
+  auto rows_of = [&](int g) {
 #pragma unroll
     for (int r = 0; r < NW; ++r) {
       const int n = n0 + r % kGemvRows;
-      if (n >= a.N) continue;
-      const uint8_t* row = a.w + (n + static_cast<int64_t>(r / kGemvRows) * a.N) * rb;
-      for (int64_t b = static_cast<int64_t>(lane) * 128; b < rb; b += 32 * 128) prefetch_l2(row + b);
+      ok[r] = n < a.N;
+      const int64_t wn = ok[r] ? n + static_cast<int64_t>(r / kGemvRows) * a.N : 0;
+      wrow[r] = a.w + static_cast<int64_t>(g) * a.wgb + wn * rb;
+      srow[r] = a.s ? a.s + static_cast<int64_t>(g) * a.sge + wn * spr : nullptr;
+    }
+  };
+  auto load = [&](int kb, uint4 (&wv)[KU][NW], float (&sc)[KU][NW]) {
+#pragma unroll
+    for (int u = 0; u < KU; ++u) {
+      const int k = kb + u * 32 * F::kVals;
+#pragma unroll
+      for (int r = 0; r < NW; ++r) {
+        const bool live = ok[r] && k < a.K;
+        wv[u][r] = live ? __ldg(reinterpret_cast<const uint4*>(wrow[r] + F::byte_off(k))) : make_uint4(0, 0, 0, 0);
+        sc[u][r] = (FMT == 0 || !live) ? 1.f : __half2float(srow[r][FMT == 2 ? k / a.group : 0]);
+      }
+    }
+  };
+  // Dense rows do not depend on the previous kernel: the first k-block of this warp's weights is loaded into
+  // registers before the programmatic-launch wait (for a 1024-wide bf16 row that is the whole row), the rest is
+  // pulled into L2.
+  const bool pre = !routed && n0 < a.N;
+  uint4 wpre[KU][NW];
+  float spre[KU][NW];
+  if (pre) {
+    rows_of(blockIdx.y);
+    load(lane * F::kVals, wpre, spre);
+#pragma unroll
+    for (int r = 0; r < NW; ++r) {
+      if (!ok[r]) continue;
+      for (int64_t b = static_cast<int64_t>(lane) * 128 + KU * 32 * 16; b < rb; b += 32 * 128) prefetch_l2(wrow[r] + b);
     }
   }
   griddep_wait();
@@ -147,18 +179,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
   const int count = a.cnt ? a.cnt[g] : a.dense_rows;
   if (count <= 0) return;
   const int base = a.off ? a.off[g] : 0;
-  const int spr = (FMT == 2) ? a.K / a.group : 1;  // scales per row
-  const uint8_t* wrow[NW];
-  const __half* srow[NW];
-  bool ok[NW];
-#pragma unroll
-  for (int r = 0; r < NW; ++r) {
-    const int n = n0 + r % kGemvRows;
-    ok[r] = n < a.N;
-    const int64_t wn = ok[r] ? n + static_cast<int64_t>(r / kGemvRows) * a.N : 0;
-    wrow[r] = a.w + static_cast<int64_t>(g) * a.wgb + wn * rb;
-    srow[r] = a.s ? a.s + static_cast<int64_t>(g) * a.sge + wn * spr : nullptr;
-  }
+  if (!pre) rows_of(g);
   for (int c0 = 0; c0 < count; c0 += kGemvTok) {
     const int tc = min(kGemvTok, count - c0);
     const bf16* xr[kGemvTok];
@@ -175,15 +196,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
     for (int kb = lane * F::kVals; kb < a.K; kb += KU * 32 * F::kVals) {
       uint4 wv[KU][NW];
       float sc[KU][NW];
+      if (pre && c0 == 0 && kb == lane * F::kVals) {
 #pragma unroll
-      for (int u = 0; u < KU; ++u) {
-        const int k = kb + u * 32 * F::kVals;
+        for (int u = 0; u < KU; ++u)
 #pragma unroll
-        for (int r = 0; r < NW; ++r) {
-          const bool live = ok[r] && k < a.K;
-          wv[u][r] = live ? __ldg(reinterpret_cast<const uint4*>(wrow[r] + F::byte_off(k))) : make_uint4(0, 0, 0, 0);
-          sc[u][r] = (FMT == 0 || !live) ? 1.f : __half2float(srow[r][FMT == 2 ? k / a.group : 0]);
-        }
+          for (int r = 0; r < NW; ++r) { wv[u][r] = wpre[u][r]; sc[u][r] = spre[u][r]; }
+      } else {
+        load(kb, wv, sc);
       }
 #pragma unroll
       for (int u = 0; u < KU; ++u) {
@@ -359,6 +378,196 @@ __global__ void __launch_bounds__(128) decode_attn_kernel(const bf16* __restrict
     part_ml[(pidx + threadIdx.x * chunks) * 2 + 1] = stats[threadIdx.x][1];
   }
   // the last chunk block of this (batch, kv head) merges the chunks
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&tickets[blockIdx.y], 1) == used - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i % D;
+    const int64_t hb = (static_cast<int64_t>(b) * Hq + hk * G + g) * chunks;
+    float M = -INFINITY;
+    for (int cc = 0; cc < used; ++cc) M = fmaxf(M, __ldcg(part_ml + (hb + cc) * 2));
+    float L = 0.f, o = 0.f;
+    for (int cc = 0; cc < used; ++cc) {
+      const float f = __expf(__ldcg(part_ml + (hb + cc) * 2) - M);
+      L += f * __ldcg(part_ml + (hb + cc) * 2 + 1);
+      o += f * __ldcg(part_o + (hb + cc) * D + d);
+    }
+    out[(static_cast<int64_t>(b) * Hq + hk * G + g) * D + d] = __float2bfloat16(L > 0.f ? o / L : 0.f);
+  }
+  if (threadIdx.x == 0) tickets[blockIdx.y] = 0;
+}
+
+// Decode attention straight from the QKV GEMV output, with RoPE and the KV-cache append of the new token folded in
+// (one launch instead of rope_append + decode_attn_kernel). The cached keys and values of the chunk, which the
+// previous kernel does not write, are loaded before the programmatic-launch wait; after it each block rotates its q
+// heads (lanes li and li ^ LPK/2 hold the two halves of a rotation pair), and the block whose chunk holds the new
+// position rotates the new key, writes key and value into the caches (one writer per batch x kv head) and uses them
+// in place of the cache rows. Chunk merge as in decode_attn_kernel.
+template <int D>
+__global__ void __launch_bounds__(128) decode_attn_rope_kernel(
+    const bf16* __restrict__ qkv, const int* __restrict__ pos, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, int rope, bf16* __restrict__ kc, bf16* __restrict__ vc, int Hq, int Hkv,
+    int Lmax, float scale, float* __restrict__ part_o, float* __restrict__ part_ml, int chunks,
+    int* __restrict__ tickets, bf16* __restrict__ out) {
+  constexpr int LPK = D / 8;        // lanes per key (8 head dims each)
+  constexpr int KPS = 32 / LPK;     // keys per warp step
+  constexpr int STEPS = 16 / KPS;   // a warp owns 16 keys of the chunk
+  constexpr int HALF = D / 2;
+  __shared__ float ps[kMaxG][kKeyChunk];
+  __shared__ float po[4][kMaxG][D];
+  __shared__ float stats[kMaxG][2];
+  __shared__ int s_last;
+  const int c = blockIdx.x;
+  const int b = blockIdx.y / Hkv, hk = blockIdx.y % Hkv;
+  const int G = Hq / Hkv;
+  const int p = pos[b];  // written before the step, not by the previous kernel
+  const int len = p + 1;
+  const int used = (len + kKeyChunk - 1) / kKeyChunk;
+  if (c >= used) return;
+  const int k0 = c * kKeyChunk;
+  const int nk = min(kKeyChunk, len - k0);
+  const int jnew = p - k0;  // the new key's slot in this chunk (in range only for the last chunk)
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int kg = lane / LPK, li = lane % LPK;
+  const int64_t cache_row = (static_cast<int64_t>(b) * Hkv + hk) * Lmax;
+  const bf16* kbase = kc + (cache_row + k0) * D + li * 8;
+  const bf16* vbase = vc + (cache_row + k0) * D + li * 8;
+  // cached keys and values (everything before the new position): independent of the previous kernel
+  uint4 kraw[STEPS], vraw[STEPS];
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s) {
+    const int jl = warp * 16 + s * KPS + kg;
+    const bool cached = jl < nk && jl != jnew;
+    kraw[s] = cached ? __ldg(reinterpret_cast<const uint4*>(kbase + static_cast<int64_t>(jl) * D))
+                     : make_uint4(0, 0, 0, 0);
+    vraw[s] = cached ? __ldg(reinterpret_cast<const uint4*>(vbase + static_cast<int64_t>(jl) * D))
+                     : make_uint4(0, 0, 0, 0);
+  }
+  griddep_wait();
+  griddep_launch();
+  const int width = (Hq + 2 * Hkv) * D;
+  const bf16* row = qkv + static_cast<int64_t>(b) * width;
+  // rotation of the 8 dims d = li*8 + e of a head row; the partner dims d +- D/2 live in lane li ^ LPK/2
+  auto rotate = [&](float* x) {
+    if (!rope) return;
+    const bool first = li < LPK / 2;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, x[e], LPK / 2);
+      const int j = (li * 8 + e) % HALF;
+      const float cs = cos_t[static_cast<int64_t>(p) * HALF + j], sn = sin_t[static_cast<int64_t>(p) * HALF + j];
+      x[e] = first ? x[e] * cs - other * sn : x[e] * cs + other * sn;
+    }
+  };
+  float qr[kMaxG][8];
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) {
+    if (g < G) {
+      bf16x8_to_float(*reinterpret_cast<const uint4*>(row + (hk * G + g) * D + li * 8), qr[g]);
+      rotate(qr[g]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qr[g][e] *= scale;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) qr[g][e] = 0.f;
+    }
+  }
+  if (jnew >= 0 && jnew < kKeyChunk) {  // block-uniform: this chunk holds the new position
+    float kn[8];
+    bf16x8_to_float(*reinterpret_cast<const uint4*>(row + (Hq + hk) * D + li * 8), kn);
+    rotate(kn);
+    uint4 knew;
+    knew.x = pack_bf16(kn[0], kn[1]); knew.y = pack_bf16(kn[2], kn[3]);
+    knew.z = pack_bf16(kn[4], kn[5]); knew.w = pack_bf16(kn[6], kn[7]);
+    const uint4 vnew = *reinterpret_cast<const uint4*>(row + (Hq + Hkv + hk) * D + li * 8);
+#pragma unroll
+    for (int s = 0; s < STEPS; ++s) {
+      if (warp * 16 + s * KPS + kg == jnew) {  // the LPK lanes of the new key's group
+        kraw[s] = knew;
+        vraw[s] = vnew;
+        *reinterpret_cast<uint4*>(kc + (cache_row + p) * D + li * 8) = knew;
+        *reinterpret_cast<uint4*>(vc + (cache_row + p) * D + li * 8) = vnew;
+      }
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s) {
+    const int jl = warp * 16 + s * KPS + kg;
+    float kv[8];
+    bf16x8_to_float(kraw[s], kv);
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+      if (g < G) {
+        float sc = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sc += qr[g][e] * kv[e];
+#pragma unroll
+        for (int o = LPK / 2; o > 0; o >>= 1) sc += __shfl_xor_sync(0xffffffffu, sc, o);
+        if (li == 0 && jl < nk) ps[g][jl] = sc;
+      }
+    }
+  }
+  __syncthreads();
+  for (int g = warp; g < G; g += 4) {
+    float m = -INFINITY;
+    for (int j = lane; j < nk; j += 32) m = fmaxf(m, ps[g][j]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int j = lane; j < nk; j += 32) {
+      const float pv = __expf(ps[g][j] - m);
+      ps[g][j] = pv;
+      l += pv;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      stats[g][0] = m;
+      stats[g][1] = l;
+    }
+  }
+  __syncthreads();
+  float acc[kMaxG][8];
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[g][e] = 0.f;
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s) {
+    const int jl = warp * 16 + s * KPS + kg;
+    if (jl < nk) {
+      float vv[8];
+      bf16x8_to_float(vraw[s], vv);
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g)
+        if (g < G) {
+          const float pr = ps[g][jl];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[g][e] += pr * vv[e];
+        }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g)
+    if (g < G)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float v = acc[g][e];
+#pragma unroll
+        for (int o = LPK; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (kg == 0) po[warp][g][li * 8 + e] = v;
+      }
+  __syncthreads();
+  const int64_t pidx = (static_cast<int64_t>(b) * Hq + hk * G) * chunks + c;
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i % D;
+    part_o[(pidx + g * chunks) * D + d] = po[0][g][d] + po[1][g][d] + po[2][g][d] + po[3][g][d];
+  }
+  if (threadIdx.x < G) {
+    part_ml[(pidx + threadIdx.x * chunks) * 2] = stats[threadIdx.x][0];
+    part_ml[(pidx + threadIdx.x * chunks) * 2 + 1] = stats[threadIdx.x][1];
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(&tickets[blockIdx.y], 1) == used - 1;
@@ -636,6 +845,22 @@ void decode_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* 
 #define QW_ATTN(DIM)                                                                                               \
   launch_pdl(decode_attn_kernel<DIM>, grid, dim3(128), 0, stream, "decode_attention", q, kc, vc, lens, Hq, Hkv, Lmax, \
              scale, part_o, part_ml, chunks, tickets, out)
+  if (D == 64) QW_ATTN(64);
+  else if (D == 128) QW_ATTN(128);
+  else if (D == 32) QW_ATTN(32);
+  else throw std::runtime_error("decode attention: head_dim must be 32, 64 or 128");
+#undef QW_ATTN
+}
+
+void decode_attention_rope(const bf16* qkv, const int* pos, const float* cos_t, const float* sin_t, bool rope,
+                           bf16* kc, bf16* vc, int B, int Hq, int Hkv, int D, int Lmax, float scale, float* part_o,
+                           float* part_ml, int* tickets, bf16* out, cudaStream_t stream) {
+  if (Hq % Hkv || Hq / Hkv > kMaxG) throw std::runtime_error("decode attention: at most 8 q heads per kv head");
+  const int chunks = decode_attn_chunks(Lmax);
+  dim3 grid(chunks, B * Hkv);
+#define QW_ATTN(DIM)                                                                                               \
+  launch_pdl(decode_attn_rope_kernel<DIM>, grid, dim3(128), 0, stream, "decode_attention_rope", qkv, pos, cos_t,   \
+             sin_t, rope ? 1 : 0, kc, vc, Hq, Hkv, Lmax, scale, part_o, part_ml, chunks, tickets, out)
   if (D == 64) QW_ATTN(64);
   else if (D == 128) QW_ATTN(128);
   else if (D == 32) QW_ATTN(32);

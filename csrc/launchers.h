@@ -201,6 +201,10 @@ void decode_route(const bf16* x, const float* wr, const float* ebias, int T, int
 void decode_attention(const bf16* q, const bf16* kc, const bf16* vc, const int* lens, int B, int Hq, int Hkv, int D,
                       int Lmax, float scale, float* part_o, float* part_ml, int* tickets, bf16* out,
                       cudaStream_t stream);
+// decode attention from the raw QKV row with RoPE and the KV-cache append of the new token (pos[b]) folded in
+void decode_attention_rope(const bf16* qkv, const int* pos, const float* cos_t, const float* sin_t, bool rope,
+                           bf16* kc, bf16* vc, int B, int Hq, int Hkv, int D, int Lmax, float scale, float* part_o,
+                           float* part_ml, int* tickets, bf16* out, cudaStream_t stream);
 void rope_append(const bf16* qkv, const int* pos, int B, int Hq, int Hkv, int D, int Lmax, const float* cos_t,
                  const float* sin_t, bool rope, bf16* q_out, bf16* kc, bf16* vc, cudaStream_t stream);
 // parts: expert-parallel partial MoE outputs (ep_decode.cu planes) summed in rank order instead of y/slot/top_w

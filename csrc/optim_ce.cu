@@ -281,6 +281,89 @@ __global__ void __launch_bounds__(256) ce_kernel(bf16* __restrict__ logits, int6
   }
 }
 
+// Register-resident variant for rows of at most 8 * 256 * CPT columns (16-byte aligned rows, V a multiple of 8): the
+// row is read once with 16-byte loads and kept in registers, the maximum and the sum of exponentials are block
+// reductions over it, and the gradient is written back with 16-byte stores. One read and one write per element,
+// against two reads, one write and a data-dependent branch per element in ce_kernel above.
+template <int CPT>
+__global__ void __launch_bounds__(256) ce_row_kernel(bf16* __restrict__ logits, int64_t ld, int V,
+                                                     const int64_t* __restrict__ labels, float grad_scale,
+                                                     float* __restrict__ loss_out, int ignore_index) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  bf16* l = logits + row * ld;
+  const int64_t label = labels[row];
+  const int chunks = V / 8;
+  uint4 raw[CPT];
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    const int i = threadIdx.x + c * 256;
+    raw[c] = i < chunks ? reinterpret_cast<const uint4*>(l)[i] : make_uint4(0, 0, 0, 0);
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  auto block_reduce = [&](float v, bool is_max) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = is_max ? fmaxf(v, w) : v + w;
+    }
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float r = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) r = is_max ? fmaxf(r, red[i]) : r + red[i];
+    __syncthreads();  // red is reused by the next reduction
+    return r;
+  };
+  float m = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    if (threadIdx.x + c * 256 >= chunks) break;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[c]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      m = fmax3(m, f.x, f.y);
+    }
+  }
+  m = block_reduce(m, true);
+  const float ml2 = m * kLog2e;
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    if (threadIdx.x + c * 256 >= chunks) break;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[c]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      s += exp2f_approx(fmaf(f.x, kLog2e, -ml2)) + exp2f_approx(fmaf(f.y, kLog2e, -ml2));
+    }
+  }
+  s = block_reduce(s, false);
+  const bool ignored = (label == ignore_index);
+  if (threadIdx.x == 0) loss_out[row] = ignored ? 0.f : m + __logf(s) - __bfloat162float(l[label]);
+  const float scale = ignored ? 0.f : grad_scale / s;
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    const int i = threadIdx.x + c * 256;
+    if (i >= chunks) break;
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[c]);
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      float g0 = exp2f_approx(fmaf(f.x, kLog2e, -ml2)) * scale;
+      float g1 = exp2f_approx(fmaf(f.y, kLog2e, -ml2)) * scale;
+      const int64_t col = 8 * static_cast<int64_t>(i) + 2 * j;
+      if (!ignored && col == label) g0 -= grad_scale;
+      if (!ignored && col + 1 == label) g1 -= grad_scale;
+      o[j] = pack_bf16(g0, g1);
+    }
+    reinterpret_cast<uint4*>(l)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 __global__ void scale_bf16_kernel(bf16* __restrict__ x, int64_t n, const float* __restrict__ scale) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i < n) x[i] = __float2bfloat16(__bfloat162float(x[i]) * scale[0]);
@@ -317,7 +400,16 @@ void adam_step(const AdamTensor* tensors, const int* chunk_tensor, const int64_t
 void cross_entropy_chunk(bf16* logits, int64_t rows, int64_t ld, int V, const int64_t* labels, float grad_scale,
                          float* loss_out, int ignore_index, cudaStream_t stream) {
   if (rows == 0) return;
-  ce_kernel<<<static_cast<int>(rows), 256, 0, stream>>>(logits, ld, V, labels, grad_scale, loss_out, ignore_index);
+  const bool vec = V % 8 == 0 && (ld * 2) % 16 == 0 && (reinterpret_cast<uintptr_t>(logits) & 15) == 0;
+  if (vec && V <= 8 * 256 * 8) {
+    ce_row_kernel<8><<<static_cast<int>(rows), 256, 0, stream>>>(logits, ld, V, labels, grad_scale, loss_out,
+                                                                 ignore_index);
+  } else if (vec && V <= 8 * 256 * 16) {
+    ce_row_kernel<16><<<static_cast<int>(rows), 256, 0, stream>>>(logits, ld, V, labels, grad_scale, loss_out,
+                                                                  ignore_index);
+  } else {
+    ce_kernel<<<static_cast<int>(rows), 256, 0, stream>>>(logits, ld, V, labels, grad_scale, loss_out, ignore_index);
+  }
   check_cuda(cudaGetLastError(), "cross_entropy_chunk");
 }
 

@@ -309,12 +309,12 @@ class FastDecoder:
         return y
 
     def _step_native(self, batch: int) -> Tensor:
-        """One decode step on the native kernels: 9 launches per layer, all with programmatic dependent launch.
+        """One decode step on the native kernels: 8 launches per layer, all with programmatic dependent launch.
 
-        combine(previous MoE output) + norm1 -> QKV GEMV (+bias) -> RoPE + cache append -> split-K attention (chunk
-        merge in the same launch) -> out-proj GEMV (+bias +residual) -> norm2 -> routing (logits + top-k + lists) ->
-        SwiGLU grouped GEMV over the routed experts -> down grouped GEMV. The last layer's MoE output is combined
-        inside the final norm."""
+        combine(previous MoE output) + norm1 -> QKV GEMV (+bias) -> split-K attention with RoPE and the cache append
+        of the new token folded in (chunk merge in the same launch) -> out-proj GEMV (+bias +residual) -> norm2 ->
+        routing (logits + top-k + lists) -> SwiGLU grouped GEMV over the routed experts -> down grouped GEMV. The
+        last layer's MoE output is combined inside the final norm."""
         from ..ops import ext
 
         C = self._C = ext()
@@ -322,7 +322,6 @@ class FastDecoder:
         tokens, positions = self.tokens_in[:batch], self.positions_in[:batch]
         hq, hkv, d, H = self.heads, self.kv_heads, self.head_dim, self.hidden
         bf = torch.bfloat16
-        lens = positions + 1
         chunks = C.decode_attn_chunks(self.capacity)
         tickets = self._tickets
         x = None
@@ -343,14 +342,12 @@ class FastDecoder:
             qkv = torch.empty(batch, (hq + 2 * hkv) * d, device=dev, dtype=bf)
             C.grouped_gemv(n1, layer.wqkv, None, qkv.size(1), H, 0, 0, False, None, None, None, 1, batch,
                            qkv, False, layer.bqkv, None, None)
-            qbuf = torch.empty(batch, hq, d, device=dev, dtype=bf)
-            C.rope_append(qkv, positions, hq, hkv, self.cos, self.sin, not self.learned, qbuf,
-                          layer.keys[:batch], layer.values[:batch])
             part_o = torch.empty(batch * hq * chunks * d, device=dev, dtype=torch.float32)
             part_ml = torch.empty(batch * hq * chunks * 2, device=dev, dtype=torch.float32)
             att = torch.empty(batch, hq * d, device=dev, dtype=bf)
-            C.decode_attention(qbuf, layer.keys[:batch], layer.values[:batch], lens, 1.0 / math.sqrt(d), part_o,
-                               part_ml, tickets, att)
+            # RoPE and the cache append of the new token happen inside the attention launch
+            C.decode_attention_rope(qkv, positions, self.cos, self.sin, not self.learned, layer.keys[:batch],
+                                    layer.values[:batch], hq, 1.0 / math.sqrt(d), part_o, part_ml, tickets, att)
             x_new = torch.empty_like(x)  # out-projection with bias and the residual add in the GEMV epilogue
             C.grouped_gemv(att, layer.wo, None, H, hq * d, 0, 0, False, None, None, None, 1, batch, x_new,
                            False, layer.bo, x, None)
