@@ -73,17 +73,18 @@ def main() -> None:
         print(json.dumps({"forward_timeline": "per tile j, per group: [scores ready, probabilities computed, previous "
                                               "PV done, P written, S(j) issued, O(j) issued] in SM clocks",
                           "tiles": rows}))
-        buf = torch.zeros(64 * 4, dtype=torch.int64, device="cuda")
+        buf = torch.zeros(2 * 32 * 16, dtype=torch.int64, device="cuda")
         ext().attn_bwd_trace(buf)
         out = attention_core(qkv, B, S, h, hkv, d, False, 1e4)
         out.backward(grad)
         torch.cuda.synchronize()
         ext().attn_bwd_trace(None)
         for m, name in enumerate(("dkdv", "dq")):
-            t = buf.view(2, 32, 4)[m].cpu().tolist()
+            t = buf.view(2, 32, 16)[m].cpu().tolist()
             t0 = min((v for row in t for v in row if v), default=0)
             print(json.dumps({"backward_timeline": name, "columns": "per tile t: [S/dP issued, scores ready, P/dS "
-                                                                    "written, accumulation issued] in SM clocks",
+                                                                    "written (first warp), accumulation issued, P/dS "
+                                                                    "written by warps 0-7 of the group] in SM clocks",
                               "tiles": [[v - t0 if v else None for v in row] for row in t if any(row)]}))
     if ext().read_status(True) != 0:
         raise SystemExit("a kernel reported a device-side error status")

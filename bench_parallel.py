@@ -43,6 +43,9 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--layers", type=int, default=0, help="debug override of the layer count (the metric needs the "
                                                            "configuration's own)")
+    p.add_argument("--kernel-breakdown", action="store_true",
+                   help="after the timed steps, every rank runs one more step under the torch profiler and rank 0 "
+                        "prints its per-kernel device time (shares only, to stderr)")
     return p.parse_args()
 
 
@@ -219,6 +222,10 @@ def main() -> None:
                         loss = step(batches[args.warmup + i])
             check_device_status()
             clock_summary = clocks.summary()
+            if args.kernel_breakdown:  # every rank steps (collectives), rank 0 reports
+                from bench import kernel_breakdown
+
+                kernel_breakdown(lambda: step(batches[-1]), report=rank == 0)
         else:
             with _WallTimer() as timer:
                 for i in range(args.steps):

@@ -283,6 +283,40 @@ __global__ void attn_delta_kernel(const bf16* __restrict__ o, int64_t ldo, const
   }
 }
 
+// delta = rowsum(dO * O) with 16-byte loads: CPR = D / 8 consecutive lanes share a (token, head) row, one 8-wide
+// chunk each (16-byte aligned rows, D in {32, 64, 128})
+template <int CPR>
+__global__ void __launch_bounds__(256) attn_delta_vec_kernel(const bf16* __restrict__ o, int64_t ldo,
+                                                             const bf16* __restrict__ dout, int64_t lddo,
+                                                             float* __restrict__ delta, int B, int S, int Hq) {
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t idx = t / CPR;  // (token, head) row
+  const int c = static_cast<int>(t % CPR);
+  const bool live = idx < static_cast<int64_t>(B) * S * Hq;
+  float s = 0.f;
+  if (live) {
+    const int64_t tok = idx / Hq;
+    const int h = static_cast<int>(idx % Hq);
+    const uint4 a = *reinterpret_cast<const uint4*>(o + tok * ldo + (h * CPR + c) * 8);
+    const uint4 g = *reinterpret_cast<const uint4*>(dout + tok * lddo + (h * CPR + c) * 8);
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&a);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x = __bfloat1622float2(a2[i]), y = __bfloat1622float2(g2[i]);
+      s = fmaf(x.x, y.x, fmaf(x.y, y.y, s));
+    }
+  }
+#pragma unroll
+  for (int off = CPR / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (live && c == 0) {
+    const int64_t tok = idx / Hq;
+    const int h = static_cast<int>(idx % Hq);
+    const int b = static_cast<int>(tok / S), sidx = static_cast<int>(tok % S);
+    delta[(static_cast<int64_t>(b) * Hq + h) * S + sidx] = s;
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ dK, dV
 // CTA = 64 keys (4 warps x 16) of one (batch, kv-head); loops over the group's q-heads and the query tiles.
 template <int D, int BR>
@@ -533,7 +567,17 @@ void flash_attn_bwd(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, cons
                     float scale, cudaStream_t stream) {
   if (B == 0 || S == 0) return;
   const int64_t rows = static_cast<int64_t>(B) * S * Hq;
-  attn_delta_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, stream>>>(o, ldo, dout, lddo, delta, B, S, Hq, D);
+  const bool vec = (D == 32 || D == 64 || D == 128) && (ldo * 2) % 16 == 0 && (lddo * 2) % 16 == 0 &&
+                   (reinterpret_cast<uintptr_t>(o) & 15) == 0 && (reinterpret_cast<uintptr_t>(dout) & 15) == 0;
+  if (vec) {
+    const int64_t threads = rows * (D / 8);
+    const int blocks = static_cast<int>((threads + 255) / 256);
+    if (D == 64) attn_delta_vec_kernel<8><<<blocks, 256, 0, stream>>>(o, ldo, dout, lddo, delta, B, S, Hq);
+    else if (D == 128) attn_delta_vec_kernel<16><<<blocks, 256, 0, stream>>>(o, ldo, dout, lddo, delta, B, S, Hq);
+    else attn_delta_vec_kernel<4><<<blocks, 256, 0, stream>>>(o, ldo, dout, lddo, delta, B, S, Hq);
+  } else {
+    attn_delta_kernel<<<static_cast<int>((rows + 7) / 8), 256, 0, stream>>>(o, ldo, dout, lddo, delta, B, S, Hq, D);
+  }
   // head_dim 64 / 128 run on the tcgen05 kernels (attention_tc.cu); QW_ATTN_BWD=mma keeps the mma.sync kernels
   // below for comparison
   static const bool use_mma = [] {

@@ -37,6 +37,8 @@
 // Every mbarrier wait is bounded (common.cuh): on a timeout all roles stop, in-flight TMA loads and MMAs are waited
 // for (bounded), TMEM is freed and the status word records the cause.
 #include <algorithm>
+#include <cstdlib>
+#include <string>
 #include <stdexcept>
 
 #include "common.cuh"
@@ -87,6 +89,7 @@ struct Params {
   float* lse;  // [B, Hq, S]
   int S, Hq, Hkv;
   float scale_log2;  // softmax scale * log2(e)
+  int park;          // idle MMA issuer: 1 = suspend on a pending P barrier (hinted try_wait), 0 = spin
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -287,7 +290,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           idle = 0;
           continue;
         }
-        // spin without sleeping: a sleeping issuer woke up to a microsecond late, stalling both groups
+        // nothing ready: by default suspend on a pending P barrier with a short hint (the thread wakes when that
+        // barrier completes or the hint runs out), so the idle issuer takes no issue slots from the softmax warps
+        // sharing its SM sub-partition; QW_ATTN_ISSUER=spin polls
+        if (p.park) {
+          if (no0 < ns0) mbar_try_wait_hint(&p_full[0], no0 & 1, 256u);
+          else if (no1 < ns1) mbar_try_wait_hint(&p_full[1], no1 & 1, 256u);
+        }
         if ((++idle & 1023) == 0) {  // bounded: give up after the wait budget without progress
           if (*abort_flag) { ok = false; break; }
           const uint64_t now = globaltimer();
@@ -459,6 +468,11 @@ void run(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, 
   p.Hq = Hq;
   p.Hkv = Hkv;
   p.scale_log2 = scale * kLog2e;
+  static const int park = [] {
+    const char* e = std::getenv("QW_ATTN_ISSUER");
+    return (e && std::string(e) == "spin") ? 0 : 1;
+  }();
+  p.park = park;
   auto mq = make_bf16_map_3d(q, static_cast<int64_t>(Hq) * D, S, B, ldq, S * ldq, kTile);
   auto mk = make_bf16_map_3d(k, static_cast<int64_t>(Hkv) * D, S, B, ldk, S * ldk, Layout<D>::KT);
   auto mv = make_bf16_map_3d(v, static_cast<int64_t>(Hkv) * D, S, B, ldv, S * ldv, Layout<D>::KT);

@@ -29,6 +29,7 @@
 // Every mbarrier wait is bounded (common.cuh): on a timeout all roles stop, in-flight TMA loads and MMAs are
 // waited for (bounded), TMEM is freed and the status word records the cause.
 #include <algorithm>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -79,6 +80,7 @@ struct Params {
   int64_t ld2;
   int S, Hq, Hkv;
   float scale;
+  int park;  // idle MMA issuer: 1 = suspend on the oldest pending P/dS barrier (hinted try_wait), 0 = spin
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -88,14 +90,14 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // Optional timeline of CTA (0, 0) (clock64 of its SM) for tuning: null unless armed from the host (attn_bwd_trace).
-// Slots of tile t of pass m (0 dK/dV, 1 dQ) at 4 * (32 m + t): 0 S/dP issued, 1 scores ready (softmax), 2 P/dS
-// written, 3 accumulation issued.
+// Slots of tile t of pass m (0 dK/dV, 1 dQ) at 16 * (32 m + t): 0 S/dP issued, 1 scores ready (softmax), 2 P/dS
+// written (first warp of the group), 3 accumulation issued, 4 + w P/dS written by warp w of the group.
 constexpr int kTraceTiles = 32;
 static __device__ unsigned long long* g_attn_bwd_trace;
 
 template <int MODE>
 __device__ __forceinline__ void trace_mark(unsigned long long* tr, int t, int slot) {
-  if (tr && t < kTraceTiles) tr[4 * (MODE * kTraceTiles + t) + slot] = clock64();
+  if (tr && t < kTraceTiles) tr[16 * (MODE * kTraceTiles + t) + slot] = clock64();
 }
 
 __device__ __forceinline__ void store_row16(bf16* dst, const float* v, float mul) {
@@ -336,9 +338,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           idle = 0;
           continue;
         }
-        // nothing ready: poll both conditions again at once. (Parking on the oldest tile's P/dS barrier would leave
-        // a next S/dP that becomes ready first waiting behind the other group's whole softmax, and a sleeping
-        // issuer woke up to a microsecond late.)
+        // nothing ready: by default suspend on the oldest tile's P/dS barrier with a short hint (the thread wakes
+        // when that barrier completes or the hint runs out, then polls both conditions again), so the idle issuer
+        // takes no issue slots from the softmax warps sharing its SM sub-partition; QW_ATTN_ISSUER=spin polls
+        if (p.park && na < ns) mbar_try_wait_hint(&p_full[na & 1], (na >> 1) & 1, 256u);
         if ((++idle & 1023) == 0) {  // bounded: give up after the wait budget without progress
           if (*abort_flag) { ok = false; break; }
           const uint64_t now = globaltimer();
@@ -451,6 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[buf]);
       if (sw % 8 == 0 && lane == 0) trace_mark<MODE>(trace, j, 2);
+      if (lane == 0) trace_mark<MODE>(trace, j, 4 + sw % 8);
     }
     // epilogue: accumulators -> bf16 rows (dK and dQ carry the softmax scale). dK/dV: group 0 stores dV, group 1
     // dK, each half of the columns; dQ: each (group, half) a quarter of the columns.
@@ -517,6 +521,11 @@ void run(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, const bf16* v, 
   p.Hq = Hq;
   p.Hkv = Hkv;
   p.scale = scale;
+  static const int park = [] {
+    const char* e = std::getenv("QW_ATTN_ISSUER");
+    return (e && std::string(e) == "spin") ? 0 : 1;
+  }();
+  p.park = park;
   // dK/dV: K, V are 128-row tiles; Q, dO 64-row tiles
   {
     auto mq = make_bf16_map_3d(q, static_cast<int64_t>(Hq) * D, S, B, ldq, S * ldq, kCols);
@@ -562,7 +571,7 @@ void flash_attn_bwd_tc(const bf16* q, int64_t ldq, const bf16* k, int64_t ldk, c
 
 int attention_tc_status(bool clear) { return read_status_word(clear); }
 
-// Arms (buf: 2 * 4 * kTraceTiles int64 slots) or disarms (null) the backward's timeline trace.
+// Arms (buf: 2 * 16 * kTraceTiles int64 slots) or disarms (null) the backward's timeline trace.
 void attn_bwd_trace(void* buf) {
   unsigned long long* ptr = static_cast<unsigned long long*>(buf);
   check_cuda(cudaMemcpyToSymbol(attn_tc::g_attn_bwd_trace, &ptr, sizeof(ptr)), "attention backward trace");

@@ -800,8 +800,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_status", &read_status, py::arg("clear") = true);
   m.def("attn_bwd_trace", [](c10::optional<torch::Tensor> buf) {
     if (buf) {
-      TORCH_CHECK(buf->is_cuda() && buf->dtype() == torch::kInt64 && buf->numel() >= 64 * 4 && buf->is_contiguous(),
-                  "attn_bwd_trace: a contiguous CUDA int64 tensor of at least 256 elements");
+      TORCH_CHECK(buf->is_cuda() && buf->dtype() == torch::kInt64 && buf->numel() >= 2 * 32 * 16 && buf->is_contiguous(),
+                  "attn_bwd_trace: a contiguous CUDA int64 tensor of at least 1024 elements");
       qw::attn_bwd_trace(buf->data_ptr());
     } else {
       qw::attn_bwd_trace(nullptr);
