@@ -141,6 +141,24 @@ class QuantaWeaveMoEForCausalLM(nn.Module):
     def routing_stats(self) -> list[dict[str, Tensor]]:
         return [moe.last_stats for moe in self.moes()]
 
+    def parameter_parts(self) -> list:
+        """``(module, parameters)`` pairs in the order the forward first uses the parameters: the model itself
+        (embeddings, and every parameter not listed later), each block, then the final norm (final norm and LM
+        head, unless tied to the embedding). An optimizer that overlaps its update with the next forward waits for a
+        part's update in a forward pre-hook on that part's module."""
+        first = {id(p) for m in (self.token_embedding, self.position_embedding) if m is not None
+                 for p in m.parameters()}
+        blocks = [(b, [p for p in b.parameters() if id(p) not in first]) for b in self.blocks]
+        taken = set(first) | {id(p) for _, ps in blocks for p in ps}
+        final = [] if self.final_norm is None else [
+            p for m in (self.final_norm, self.lm_head) if m is not None for p in m.parameters() if id(p) not in taken]
+        taken |= {id(p) for p in final}
+        head = [p for p in self.parameters() if id(p) not in taken or id(p) in first]
+        parts = [(self, head)] + blocks
+        if self.final_norm is not None:
+            parts.append((self.final_norm, final))
+        return parts
+
     # ---- forward ---------------------------------------------------------------
     def embed(self, input_ids: Tensor) -> Tensor:
         _, sequence = input_ids.shape

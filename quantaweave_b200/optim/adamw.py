@@ -4,6 +4,11 @@
 * One kernel computes the global gradient norm (fixed-order fp64 reduction, deterministic); the clip coefficient
   stays on the device and is folded into the single fused update kernel that walks every parameter.
 * The update matches ``torch.optim.AdamW`` (decoupled weight decay, bias-corrected moments).
+* ``overlap_with_forward(model)``: later ``step()`` calls run the update on a side stream, part by part in the order
+  the forward uses the parameters (``model.parameter_parts()``), and a forward pre-hook makes the compute stream
+  wait for a part just before its first use. The update is bound by HBM bandwidth and the next forward mostly by
+  the tensor cores, so most of it hides. The gradients and clip coefficient of an in-flight update stay referenced
+  until the next ``step()``; ``finish()`` joins the side stream (timers, checkpoints and ``state_dict`` need it).
 
 State is kept as the usual ``self.state[p]`` dict (``step``, ``exp_avg``, ``exp_avg_sq`` and ``master`` for bf16
 parameters), always in fp32; ``state_dict``/``load_state_dict`` preserve those dtypes.
@@ -32,6 +37,10 @@ class FusedAdamW(torch.optim.Optimizer):
         # 1/ep for expert gradients that the expert-parallel backward sums over every rank's tokens
         self.grad_scale: dict = {}
         self._norm_buf: Optional[Tensor] = None
+        self._side = None          # overlap: side stream, part of each parameter, pending per-part events
+        self._part_of: dict = {}
+        self._part_events: list = []
+        self._inflight = None
 
     # ---- state -----------------------------------------------------------------------------------
     def _init_state(self, p: Tensor) -> dict:
@@ -84,11 +93,11 @@ class FusedAdamW(torch.optim.Optimizer):
             rows.append((p.data_ptr(), g.data_ptr(), st["master"].data_ptr() if "master" in st else 0,
                          st["exp_avg"].data_ptr(), st["exp_avg_sq"].data_ptr(), p.numel(), tail, scale))
         key = (str(device), tuple(rows))
-        cached = getattr(self, "_table_cache", None)
-        if cached is not None and cached[0] == key:
-            return cached[1]
+        tables = self.__dict__.setdefault("_table_cache", {})  # one entry per parameter list (parts of a step)
+        if key in tables:
+            return tables[key]
         sizes = tuple(r[5] for r in rows)
-        chunk_cache = getattr(self, "_chunk_cache", {})
+        chunk_cache = self.__dict__.setdefault("_chunk_cache", {})
         if (str(device), sizes) not in chunk_cache:
             chunk = C.adam_chunk_size()
             numels = torch.tensor(sizes, dtype=torch.int64)
@@ -96,11 +105,12 @@ class FusedAdamW(torch.optim.Optimizer):
             owner = torch.repeat_interleave(torch.arange(len(sizes), dtype=torch.int32), counts)
             first = torch.repeat_interleave(torch.cumsum(counts, 0) - counts, counts)
             starts = (torch.arange(owner.numel(), dtype=torch.int64) - first) * chunk
-            chunk_cache = {(str(device), sizes): (owner.to(device), starts.to(device))}
-            self._chunk_cache = chunk_cache
+            chunk_cache[(str(device), sizes)] = (owner.to(device), starts.to(device))
         ct, cs = chunk_cache[(str(device), sizes)]
         table = torch.tensor(rows, dtype=torch.int64).pin_memory().to(device, non_blocking=True)
-        self._table_cache = (key, (table, ct, cs))
+        if len(tables) > 64:  # gradients were reallocated: drop the stale tables of earlier steps
+            tables.clear()
+        tables[key] = (table, ct, cs)
         return table, ct, cs
 
     def _live(self):
@@ -155,12 +165,32 @@ class FusedAdamW(torch.optim.Optimizer):
         n = norm.float().reshape(()) if norm is not None else torch.zeros((), device=coef.device)
         self._clip = torch.stack([n, coef.float().reshape(())])
 
+    # ---- overlap with the next forward -----------------------------------------------------------------
+    def overlap_with_forward(self, model) -> None:
+        """Run later updates on a side stream in the forward's order of use (see the module docstring)."""
+        parts = model.parameter_parts()
+        self._side = torch.cuda.Stream()
+        self._part_of = {id(p): i for i, (_, params) in enumerate(parts) for p in params}
+        self._part_events = [None] * len(parts)
+        for i, (module, _) in enumerate(parts):
+            module.register_forward_pre_hook(self._waiter(i))
+
+    def _waiter(self, i: int):
+        def hook(module, args):
+            event = self._part_events[i]
+            if event is not None:
+                torch.cuda.current_stream().wait_event(event)
+                self._part_events[i] = None
+        return hook
+
+    def finish(self) -> None:
+        """The current stream waits for every update in flight on the side stream."""
+        if self._side is not None:
+            torch.cuda.current_stream().wait_stream(self._side)
+            self._part_events = [None] * len(self._part_events)
+
     # ---- step ------------------------------------------------------------------------------------
-    @torch.no_grad()
-    def step(self, closure=None):
-        loss = closure() if closure is not None else None
-        C = ext()
-        live = self._live()
+    def _step_live(self, live: list) -> None:
         by_group: dict[int, list[Tensor]] = {}
         for group, p in live:
             by_group.setdefault(id(group), []).append(p)
@@ -176,6 +206,28 @@ class FusedAdamW(torch.optim.Optimizer):
                     self._step_tensors([p], group, self.state[p]["step"])
             else:
                 self._step_tensors(params, group, steps.pop() + 1)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = closure() if closure is not None else None
+        live = self._live()
+        if self._side is None or not live:
+            self._step_live(live)
+        else:
+            # the side stream starts after everything queued so far (gradients, clip coefficient); the gradients
+            # and the coefficient of this update stay referenced until the next step
+            self._side.wait_stream(torch.cuda.current_stream())
+            self._inflight = ([p.grad for _, p in live], self._clip)
+            parts: dict[int, list] = {}
+            for group, p in live:
+                parts.setdefault(self._part_of.get(id(p), 0), []).append((group, p))
+            with torch.cuda.stream(self._side):
+                for i in range(len(self._part_events)):
+                    if i in parts:
+                        self._step_live(parts[i])
+                    event = torch.cuda.Event()
+                    event.record(self._side)
+                    self._part_events[i] = event
         self._clip = None
         return loss
 
@@ -188,6 +240,7 @@ class FusedAdamW(torch.optim.Optimizer):
 
     # ---- checkpoints -----------------------------------------------------------------------------
     def state_dict(self) -> dict:
+        self.finish()
         index = {}
         groups = []
         for group in self.param_groups:
@@ -206,6 +259,7 @@ class FusedAdamW(torch.optim.Optimizer):
         return {"state": state, "param_groups": groups}
 
     def load_state_dict(self, state_dict: dict) -> None:
+        self.finish()
         params = [p for group in self.param_groups for p in group["params"]]
         for group, saved in zip(self.param_groups, state_dict["param_groups"]):
             for key, value in saved.items():

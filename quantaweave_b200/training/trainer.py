@@ -320,6 +320,8 @@ _HELP = {
     "microbatches": "micro-batches per pipeline step",
     "pipeline_schedule": "GPipe (all forwards, then all backwards) or 1F1B",
     "shard_optimizer": "ZeRO-style: each rank keeps the AdamW state of its share of the replicated parameters",
+    "optimizer_overlap": "run each AdamW update on a side stream under the next forward (fused CUDA AdamW, no "
+                         "pipeline or sharded optimizer)",
     "straggler_routing": "bias routing away from ranks whose experts run slower",
     "straggler_capacity": "scale each rank's expert capacity by its measured speed",
     "straggler_capacity_min": "lower bound of the per-rank capacity scale",
@@ -440,6 +442,7 @@ def build_parser() -> argparse.ArgumentParser:
     system.add_argument("--microbatches", type=int, default=1)
     system.add_argument("--pipeline-schedule", choices=("gpipe", "1f1b"), default="gpipe")
     system.add_argument("--shard-optimizer", action="store_true")
+    system.add_argument("--optimizer-overlap", action="store_true")
     system.add_argument("--straggler-routing", action="store_true")
     system.add_argument("--straggler-capacity", action="store_true")
     system.add_argument("--straggler-capacity-min", type=float, default=0.5)
@@ -778,6 +781,9 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
         optimizer = ShardedAdamW(model, ctx, lr=args.lr, betas=betas, weight_decay=args.weight_decay)
     else:
         optimizer = build_optimizer(args.optimizer, model.parameters(), args.lr, betas, args.weight_decay, device)
+        if getattr(args, "optimizer_overlap", False) and hasattr(optimizer, "overlap_with_forward") \
+                and not args.pipeline_parallel and hasattr(model, "parameter_parts"):
+            optimizer.overlap_with_forward(model)
     tracker = None
     if ep is not None and ep.world_size > 1 and (args.straggler_routing or args.straggler_capacity or args.device_metrics):
         from ..parallel.expert_parallel import DeviceLoadTracker
@@ -864,6 +870,8 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
                                      "router_aux_loss_coef": model.router_aux_loss_coef}}
 
     def save(path: Path, step: int) -> None:
+        if hasattr(optimizer, "finish"):
+            optimizer.finish()  # an update in flight on the side stream lands before the weights are read
         payload = tokenizer_payload(tokenizer) if tokenizer is not None else None
         if ctx is not None:
             from ..parallel.checkpoint import save_sharded_checkpoint

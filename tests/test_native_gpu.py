@@ -362,3 +362,52 @@ def test_quantized_moe_prefill_on_tensor_cores_matches_per_expert_path(bits):
         ref = moe(x.float())[0].float()
     _close(fast, ref, 3e-2)
     _status_ok()
+
+
+def test_optimizer_overlap_matches_serial_update():
+    """FusedAdamW.overlap_with_forward: the update of each step runs on a side stream under the next forward; after a
+    few steps every parameter is bit-identical to the serial optimizer's (same kernels, only the stream differs)."""
+    from quantaweave_b200 import QuantaWeaveMoEForCausalLM, preset
+    from quantaweave_b200.optim.adamw import FusedAdamW
+    from quantaweave_b200.training.native import prepare_model
+
+    cfg = preset("tiny-cpu", max_sequence_length=129)
+    ids = torch.randint(0, cfg.vocab_size, (4, 128), generator=torch.Generator().manual_seed(1)).cuda()
+    finals = []
+    for overlap in (False, True):
+        torch.manual_seed(7)
+        model = QuantaWeaveMoEForCausalLM(cfg).cuda()
+        prepare_model(model, "bf16")
+        opt = FusedAdamW(model.parameters(), lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)
+        if overlap:
+            opt.overlap_with_forward(model)
+        for _ in range(4):
+            out = model(ids, labels=ids, return_logits=False)
+            out["loss"].backward()
+            opt.clip_grad_norm_(1.0)
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+        opt.finish()
+        torch.cuda.synchronize()
+        finals.append({n: p.detach().clone() for n, p in model.named_parameters()})
+    for name, value in finals[0].items():
+        assert torch.equal(value, finals[1][name]), name
+    _status_ok()
+
+
+def test_trainer_optimizer_overlap_same_losses(tmp_path):
+    """run_training with --optimizer-overlap logs the same losses as without it (the update only moves streams)."""
+    import json
+
+    from quantaweave_b200.training.trainer import default_args, run_training
+
+    losses = []
+    for overlap in (False, True):
+        args = default_args(preset="tiny-cpu", synthetic_data="zipf", vocab_size=512, sequence_length=128,
+                            batch_size=8, steps=5, lr=1e-3, device="cuda", no_power_tracking=True,
+                            optimizer_overlap=overlap, output=tmp_path / f"o{overlap}",
+                            checkpoint_dir=tmp_path / f"c{overlap}", checkpoint_interval=0,
+                            metrics_file=tmp_path / f"m{overlap}.jsonl")
+        run_training(args)
+        losses.append([json.loads(line)["loss"] for line in (tmp_path / f"m{overlap}.jsonl").read_text().splitlines()])
+    assert losses[0] == losses[1]
