@@ -96,6 +96,8 @@ class FastDecoder:
         self.model = model
         self.config = cfg
         self.device = torch.device(device)
+        if self.device.type == "cuda" and self.device.index is None:  # a concrete GPU (collectives name it)
+            self.device = torch.device("cuda", torch.cuda.current_device())
         self.ep = ep if ep is not None and ep.world_size > 1 else None
         self.native = self.device.type == "cuda"
         if self.native:
@@ -193,7 +195,7 @@ class FastDecoder:
         self._ep_done = torch.zeros(1, dtype=torch.int32, device=dev)
         self._ep_timeout = transport.timeout_s
         torch.cuda.synchronize(dev)
-        dist.barrier(group=ep.group, device_ids=[dev.index])
+        dist.barrier(group=ep.group, device_ids=[dev.index if dev.index is not None else torch.cuda.current_device()])
 
     # ---- weight extraction -----------------------------------------------------------------------
     def _norm(self, norm):

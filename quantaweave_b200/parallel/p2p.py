@@ -19,6 +19,10 @@ from torch import Tensor
 _TRANSPORTS: dict = {}
 
 
+def _index(device: torch.device) -> int:
+    return device.index if device.index is not None else torch.cuda.current_device()
+
+
 class P2PTransport:
     def __init__(self, group, device: torch.device, capacity_bytes: int = 64 << 20) -> None:
         os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
@@ -46,7 +50,7 @@ class P2PTransport:
         self._peer_flags = [torch.tensor([p + parity * self.world * 4 for p in ptrs], dtype=torch.int64, device=device)
                             for parity in range(2)]
         self._done = torch.zeros(self.world, dtype=torch.int32, device=device)
-        dist.barrier(group=self.group, device_ids=[device.index] if device.type == "cuda" else None)
+        dist.barrier(group=self.group, device_ids=[_index(device)] if device.type == "cuda" else None)
         self._grow(capacity_bytes)
 
     def _group_name(self):
@@ -54,6 +58,9 @@ class P2PTransport:
 
     @classmethod
     def for_group(cls, group, device) -> "P2PTransport":
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:  # collectives and symmetric memory name the GPU
+            device = torch.device("cuda", torch.cuda.current_device())
         key = (id(group), str(device))
         if key not in _TRANSPORTS:
             _TRANSPORTS[key] = cls(group, device)
@@ -182,10 +189,13 @@ class FusedTransport(P2PTransport):
         self.send = _Channel(self)
         self.back = _Channel(self)
         self._stores: dict = {}
-        dist.barrier(group=self.group, device_ids=[device.index] if device.type == "cuda" else None)
+        dist.barrier(group=self.group, device_ids=[_index(device)] if device.type == "cuda" else None)
 
     @classmethod
     def for_group(cls, group, device) -> "FusedTransport":
+        device = torch.device(device)
+        if device.type == "cuda" and device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
         key = ("fused", id(group), str(device))
         if key not in _TRANSPORTS:
             _TRANSPORTS[key] = cls(group, device)

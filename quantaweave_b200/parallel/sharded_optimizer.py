@@ -110,7 +110,7 @@ class ShardedAdamW:
                       gpeers=torch.tensor([int(x) for x in hg.buffer_ptrs], dtype=torch.int64, device=device),
                       code=0 if dtype == torch.float32 else 1)
         torch.cuda.synchronize(device)
-        dist.barrier(group=self.group, device_ids=[device.index])
+        dist.barrier(group=self.group, device_ids=[device.index if device.index is not None else torch.cuda.current_device()])
         self._armed = False
         self._overlap = os.environ.get("QW_ZERO_OVERLAP", "1") != "0"
         if self._overlap:
