@@ -129,7 +129,19 @@ class FusedAdamW(torch.optim.Optimizer):
     @torch.no_grad()
     def clip_grad_norm_(self, max_norm: float, extra_sumsq: Optional[Tensor] = None) -> Tensor:
         """Global L2 norm of all gradients (plus ``extra_sumsq`` from other ranks' shards); the clip coefficient is
-        applied inside the next ``step()``. Returns the norm as a 0-d device tensor."""
+        applied inside the next ``step()``. Returns the norm as a 0-d device tensor.
+
+        With ``overlap_with_forward`` (and no ``extra_sumsq``) the norm pass is deferred into ``step()`` on the side
+        stream as well; the returned tensor then holds the norm once ``finish()`` has run."""
+        if self._side is not None and extra_sumsq is None:
+            live = self._live()
+            if not live:
+                return torch.zeros(())
+            device = live[0][1].device
+            if self._norm_buf is None or self._norm_buf.device != device:
+                self._norm_buf = torch.zeros(2, device=device, dtype=torch.float32)
+            self._deferred_clip = float(max_norm)
+            return self._norm_buf[0]
         C = ext()
         live = self._live()
         if not live:
@@ -222,6 +234,15 @@ class FusedAdamW(torch.optim.Optimizer):
             for group, p in live:
                 parts.setdefault(self._part_of.get(id(p), 0), []).append((group, p))
             with torch.cuda.stream(self._side):
+                clip_max = self.__dict__.pop("_deferred_clip", None)
+                if clip_max is not None:  # the norm pass deferred by clip_grad_norm_, ahead of the updates
+                    C = ext()
+                    params = [p for _, p in live]
+                    table, ct, cs = self._build_tables(params, params[0].device)
+                    partial = torch.empty(max(1, ct.numel()), device=params[0].device, dtype=torch.float64)
+                    C.adam_grad_norm(table, ct, cs, partial, None, clip_max, self._norm_buf)
+                    self._clip = self._norm_buf
+                    self._inflight = (self._inflight, partial, self._norm_buf)
                 for i in range(len(self._part_events)):
                     if i in parts:
                         self._step_live(parts[i])

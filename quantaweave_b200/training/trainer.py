@@ -959,6 +959,8 @@ def _run_training(args, original_outputs: tuple, temporary: list) -> dict:
         flush_now = (step % args.log_interval == 0 or step == args.steps or controller.should_update(step)
                      or (args.checkpoint_interval > 0 and step % args.checkpoint_interval == 0))
         if flush_now:
+            if hasattr(optimizer, "finish"):
+                optimizer.finish()  # a norm or update still on the optimizer's side stream lands before it is read
             for _, (loss_value, aux_value, dropped, overflow_count, domain_value, overflow_fraction) in \
                     scalars.flush(mean_over_ranks):
                 controller.observe(loss_value, overflow_fraction)
