@@ -419,7 +419,7 @@ void adam_sumsq(Tensor table, Tensor chunk_tensor, Tensor chunk_start, Tensor pa
 }
 
 void adam_step(Tensor table, Tensor chunk_tensor, Tensor chunk_start, double lr, double beta1, double beta2, double eps,
-               double weight_decay, int64_t step, OptT clip, bool eight_bit) {
+               double weight_decay, int64_t step, OptT clip, bool eight_bit, int64_t small_blocks) {
   CHECK_CUDA(table);
   qw::AdamHyper h;
   h.lr = static_cast<float>(lr);
@@ -432,7 +432,7 @@ void adam_step(Tensor table, Tensor chunk_tensor, Tensor chunk_start, double lr,
   c10::cuda::CUDAGuard g(table.device());
   qw::adam_step(reinterpret_cast<const qw::AdamTensor*>(table.data_ptr()), chunk_tensor.data_ptr<int>(),
                 chunk_start.data_ptr<int64_t>(), static_cast<int>(chunk_tensor.numel()), h, optptr<float>(clip),
-                eight_bit, stream());
+                eight_bit, stream(), static_cast<int>(small_blocks));
 }
 
 void cross_entropy_chunk(Tensor logits, Tensor labels, double grad_scale, Tensor loss_out, int64_t ignore_index) {
@@ -768,7 +768,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adam8_block_size", &adam8_block_size);
   m.def("adam_grad_norm", &adam_grad_norm);
   m.def("adam_sumsq", &adam_sumsq);
-  m.def("adam_step", &adam_step);
+  m.def("adam_step", &adam_step, py::arg("table"), py::arg("chunk_tensor"), py::arg("chunk_start"), py::arg("lr"),
+        py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("weight_decay"), py::arg("step"), py::arg("clip"),
+        py::arg("eight_bit"), py::arg("small_blocks") = 0);
   m.def("cross_entropy_chunk", &cross_entropy_chunk);
   m.def("scale_bf16", &scale_bf16);
   m.def("flash_attn_fwd", &flash_attn_fwd);

@@ -136,8 +136,10 @@ void adam_grad_norm(const AdamTensor* tensors, const int* chunk_tensor, const in
                     double* partial, const double* extra_sumsq, float max_norm, float* norm_out, cudaStream_t stream);
 void adam_sumsq(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
                 double* partial, cudaStream_t stream);
+// small_blocks > 0: 128-thread blocks, at most small_blocks of them striding over the chunks (an update that runs
+// beside other kernels)
 void adam_step(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
-               const AdamHyper& hyper, const float* clip, bool eight_bit, cudaStream_t stream);
+               const AdamHyper& hyper, const float* clip, bool eight_bit, cudaStream_t stream, int small_blocks = 0);
 int adam8_block_size();
 void cross_entropy_chunk(bf16* logits, int64_t rows, int64_t ld, int V, const int64_t* labels, float grad_scale,
                          float* loss_out, int ignore_index, cudaStream_t stream);

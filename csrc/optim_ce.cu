@@ -98,6 +98,69 @@ __device__ __forceinline__ void adam_update(float& p, float& m, float& v, float 
   p -= step_size * m / denom;
 }
 
+// Small-footprint variant for an update that runs beside other kernels (the optimizer overlapped with the next
+// forward): 128-thread blocks, a grid of a couple of blocks per SM striding over the chunks, two 4-element groups
+// in flight per thread. A block fits next to a persistent GEMM or attention CTA (registers and threads to spare,
+// no shared memory), so the update streams through HBM while those kernels run.
+__device__ __forceinline__ void adamw_chunk_small(const AdamTensor& t, int64_t begin, AdamHyper h, float coef) {
+  const int64_t end = min(t.numel, begin + kAdamChunk);
+  const float decay = 1.f - h.lr * h.weight_decay * t.decay_scale;
+  const float step_size = h.lr / h.bias_correction1;
+  float* master = t.master ? t.master : static_cast<float*>(t.param);
+  if (vec_ok(t)) {
+    for (int64_t i0 = begin + 4 * threadIdx.x; i0 < end; i0 += 8 * blockDim.x) {
+      float g[2][4];
+      float4 p[2], m[2], v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int64_t i = i0 + u * 4 * blockDim.x;
+        if (i >= end) break;
+        load4(t.grad, i, t.grad_dtype, g[u]);
+        p[u] = *reinterpret_cast<const float4*>(master + i);
+        m[u] = *reinterpret_cast<const float4*>(t.exp_avg + i);
+        v[u] = *reinterpret_cast<const float4*>(t.exp_avg_sq + i);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int64_t i = i0 + u * 4 * blockDim.x;
+        if (i >= end) break;
+        adam_update(p[u].x, m[u].x, v[u].x, g[u][0] * coef, h, decay, step_size);
+        adam_update(p[u].y, m[u].y, v[u].y, g[u][1] * coef, h, decay, step_size);
+        adam_update(p[u].z, m[u].z, v[u].z, g[u][2] * coef, h, decay, step_size);
+        adam_update(p[u].w, m[u].w, v[u].w, g[u][3] * coef, h, decay, step_size);
+        *reinterpret_cast<float4*>(master + i) = p[u];
+        *reinterpret_cast<float4*>(t.exp_avg + i) = m[u];
+        *reinterpret_cast<float4*>(t.exp_avg_sq + i) = v[u];
+        if (t.master) {
+          uint2 out;
+          out.x = pack_bf16(p[u].x, p[u].y);
+          out.y = pack_bf16(p[u].z, p[u].w);
+          *reinterpret_cast<uint2*>(static_cast<bf16*>(t.param) + i) = out;
+        }
+      }
+    }
+  } else {
+    for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x) {
+      float p = master[i], m = t.exp_avg[i], v = t.exp_avg_sq[i];
+      adam_update(p, m, v, load_val(t.grad, i, t.grad_dtype) * coef, h, decay, step_size);
+      master[i] = p;
+      t.exp_avg[i] = m;
+      t.exp_avg_sq[i] = v;
+      if (t.master) static_cast<bf16*>(t.param)[i] = __float2bfloat16(p);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128, 4) adamw_small_kernel(const AdamTensor* __restrict__ tensors,
+                                                             const int* __restrict__ chunk_tensor,
+                                                             const int64_t* __restrict__ chunk_start, int chunks,
+                                                             AdamHyper h, const float* __restrict__ clip) {
+  for (int chunk = blockIdx.x; chunk < chunks; chunk += gridDim.x) {
+    const AdamTensor& t = tensors[chunk_tensor[chunk]];
+    adamw_chunk_small(t, chunk_start[chunk], h, (clip ? clip[1] : 1.f) * t.grad_scale);
+  }
+}
+
 __global__ void adamw_kernel(const AdamTensor* __restrict__ tensors, const int* __restrict__ chunk_tensor,
                              const int64_t* __restrict__ chunk_start, AdamHyper h, const float* __restrict__ clip) {
   const int chunk = blockIdx.x;
@@ -388,9 +451,12 @@ void adam_sumsq(const AdamTensor* tensors, const int* chunk_tensor, const int64_
 }
 
 void adam_step(const AdamTensor* tensors, const int* chunk_tensor, const int64_t* chunk_start, int chunks,
-               const AdamHyper& hyper, const float* clip, bool eight_bit, cudaStream_t stream) {
+               const AdamHyper& hyper, const float* clip, bool eight_bit, cudaStream_t stream, int small_blocks) {
   if (chunks == 0) return;
-  if (eight_bit)
+  if (small_blocks > 0 && !eight_bit)
+    adamw_small_kernel<<<std::min(chunks, small_blocks), 128, 0, stream>>>(tensors, chunk_tensor, chunk_start, chunks,
+                                                                          hyper, clip);
+  else if (eight_bit)
     adamw8_kernel<<<chunks, 256, 0, stream>>>(tensors, chunk_tensor, chunk_start, hyper, clip);
   else
     adamw_kernel<<<chunks, 256, 0, stream>>>(tensors, chunk_tensor, chunk_start, hyper, clip);

@@ -182,6 +182,7 @@ class FusedAdamW(torch.optim.Optimizer):
         """Run later updates on a side stream in the forward's order of use (see the module docstring)."""
         parts = model.parameter_parts()
         self._side = torch.cuda.Stream()
+        self._small_blocks = 2 * torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
         self._part_of = {id(p): i for i, (_, params) in enumerate(parts) for p in params}
         self._part_events = [None] * len(parts)
         for i, (module, _) in enumerate(parts):
@@ -256,8 +257,10 @@ class FusedAdamW(torch.optim.Optimizer):
         C = ext()
         table, ct, cs = self._build_tables(params, params[0].device)
         beta1, beta2 = group["betas"]
+        # beside the next forward the update uses small strided blocks that fit next to its persistent kernels
+        small = self.__dict__.get("_small_blocks", 0) if torch.cuda.current_stream() == self._side else 0
         C.adam_step(table, ct, cs, float(group["lr"]), float(beta1), float(beta2), float(group["eps"]),
-                    float(group["weight_decay"]), int(step), self._clip, self.moment_bits == 8)
+                    float(group["weight_decay"]), int(step), self._clip, self.moment_bits == 8, small)
 
     # ---- checkpoints -----------------------------------------------------------------------------
     def state_dict(self) -> dict:
