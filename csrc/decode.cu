@@ -122,7 +122,7 @@ struct GemvArgs {
   const int* active;  // compact list of groups with entries (-1 padded); nullptr: blockIdx.y is the group
 };
 
-template <int FMT, bool SWIGLU>
+template <int FMT, bool SWIGLU, bool PRE>
 __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a) {
   using F = WF<FMT>;
   constexpr int NW = SWIGLU ? 2 * kGemvRows : kGemvRows;  // weight rows per warp
@@ -157,13 +157,14 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
       }
     }
   };
-  // Dense rows do not depend on the previous kernel: the first k-block of this warp's weights is loaded into
-  // registers before the programmatic-launch wait (for a 1024-wide bf16 row that is the whole row), the rest is
-  // pulled into L2.
-  const bool pre = !routed && n0 < a.N;
-  uint4 wpre[KU][NW];
-  float spre[KU][NW];
-  if (pre) {
+  // Dense rows (PRE: no routing lists) do not depend on the previous kernel: the first k-block of this warp's
+  // weights is loaded into registers before the programmatic-launch wait (for a 1024-wide bf16 row that is the
+  // whole row), the rest is pulled into L2. Routed launches keep those registers free.
+  const bool pre = PRE && !routed && n0 < a.N;
+  uint4 wpre[PRE ? KU : 1][NW];
+  float spre[PRE ? KU : 1][NW];
+  if constexpr (PRE) {
+   if (pre) {
     rows_of(blockIdx.y);
     load(lane * F::kVals, wpre, spre);
 #pragma unroll
@@ -171,6 +172,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
       if (!ok[r]) continue;
       for (int64_t b = static_cast<int64_t>(lane) * 128 + KU * 32 * 16; b < rb; b += 32 * 128) prefetch_l2(wrow[r] + b);
     }
+   }
   }
   griddep_wait();
   griddep_launch();
@@ -196,11 +198,15 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const GemvArgs a)
     for (int kb = lane * F::kVals; kb < a.K; kb += KU * 32 * F::kVals) {
       uint4 wv[KU][NW];
       float sc[KU][NW];
-      if (pre && c0 == 0 && kb == lane * F::kVals) {
+      if constexpr (PRE) {
+        if (pre && c0 == 0 && kb == lane * F::kVals) {
 #pragma unroll
-        for (int u = 0; u < KU; ++u)
+          for (int u = 0; u < KU; ++u)
 #pragma unroll
-          for (int r = 0; r < NW; ++r) { wv[u][r] = wpre[u][r]; sc[u][r] = spre[u][r]; }
+            for (int r = 0; r < NW; ++r) { wv[u][r] = wpre[u][r]; sc[u][r] = spre[u][r]; }
+        } else {
+          load(kb, wv, sc);
+        }
       } else {
         load(kb, wv, sc);
       }
@@ -810,7 +816,10 @@ __global__ void __launch_bounds__(256) decode_route_kernel(const bf16* __restric
 template <int FMT, bool SW>
 void launch_gemv(const GemvArgs& a, int groups, int grid_groups, cudaStream_t stream) {
   dim3 grid((a.N + kGemvWarps * kGemvRows - 1) / (kGemvWarps * kGemvRows), a.active ? grid_groups : groups);
-  launch_pdl(gemv_kernel<FMT, SW>, grid, dim3(kGemvWarps * 32), 0, stream, "grouped_gemv", a);
+  if (a.active == nullptr && a.cnt == nullptr)
+    launch_pdl(gemv_kernel<FMT, SW, true>, grid, dim3(kGemvWarps * 32), 0, stream, "grouped_gemv", a);
+  else
+    launch_pdl(gemv_kernel<FMT, SW, false>, grid, dim3(kGemvWarps * 32), 0, stream, "grouped_gemv", a);
 }
 
 }  // namespace
