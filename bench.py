@@ -53,9 +53,11 @@ def parse():
                    help="expert-parallel exchange: fused (dispatch kernel and expert-GEMM epilogue store rows "
                         "into peers over NVLink), p2p (peer-store exchange of padded buffers), nccl (all_to_all), "
                         "auto (fused on CUDA)")
-    p.add_argument("--optimizer-overlap", choices=("on", "off"), default="on",
+    p.add_argument("--optimizer-overlap", choices=("on", "off"), default="off",
                    help="run each step's AdamW update on a side stream under the next forward (the timed regions "
-                        "wait for the last update before they end)")
+                        "wait for the last update before they end). Off by default: measured on one B200 it did not "
+                        "help (311.7k vs 314.8k tokens/s), because the persistent GEMM and attention kernels leave "
+                        "the update too few SM resources to run beside them")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-launch-count", action="store_true",
                    help="skip the profiler-based launch count (for runs under an external profiler)")

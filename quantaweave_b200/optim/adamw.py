@@ -9,6 +9,8 @@
   wait for a part just before its first use. The update is bound by HBM bandwidth and the next forward mostly by
   the tensor cores, so most of it hides. The gradients and clip coefficient of an in-flight update stay referenced
   until the next ``step()``; ``finish()`` joins the side stream (timers, checkpoints and ``state_dict`` need it).
+  Measured on one B200 with benchmark configuration 2 it is neutral (the persistent GEMM and attention kernels of
+  the forward leave the update few SM resources), so it is opt-in.
 
 State is kept as the usual ``self.state[p]`` dict (``step``, ``exp_avg``, ``exp_avg_sq`` and ``master`` for bf16
 parameters), always in fp32; ``state_dict``/``load_state_dict`` preserve those dtypes.
@@ -182,7 +184,9 @@ class FusedAdamW(torch.optim.Optimizer):
         """Run later updates on a side stream in the forward's order of use (see the module docstring)."""
         parts = model.parameter_parts()
         self._side = torch.cuda.Stream()
-        self._small_blocks = 2 * torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+        # small strided blocks fit beside the forward's persistent kernels but stream too slowly: measured slower
+        # (291k vs 312k tokens/s on one B200) than full-size blocks on the side stream, so they stay off
+        self._small_blocks = 0
         self._part_of = {id(p): i for i, (_, params) in enumerate(parts) for p in params}
         self._part_events = [None] * len(parts)
         for i, (module, _) in enumerate(parts):
