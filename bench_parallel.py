@@ -115,7 +115,9 @@ def _tp_ep(args, rank, world, device):
     model.train()
     opt = _optimizer(model, device)
     gen = torch.Generator().manual_seed(args.seed)  # every rank gets the same sequences (one data-parallel group)
-    batches = [torch.randint(0, cfg.vocab_size, (seqs, seq + 1), generator=gen).to(device)
+    # seqs x seq token rows (each position predicts the next; the last has no target), so the rows split evenly
+    # over the sequence-parallel ranks
+    batches = [torch.randint(0, cfg.vocab_size, (seqs, seq), generator=gen).to(device)
                for _ in range(args.warmup + args.steps)]
 
     def step(batch):
