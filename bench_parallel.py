@@ -135,7 +135,7 @@ def _tp_ep(args, rank, world, device):
                    "global_batch": seqs, "seq_len": seq,
                    "parallelism": f"sp: attention tp{world} + experts ep{world} on the same ranks",
                    "activation_checkpointing": True, "ep_transport": ep.transport}
-    return step, batches, seqs * seq, description, model
+    return step, batches, seqs * seq, description, None
 
 
 def _pp_zero(args, rank, world, device):
@@ -187,7 +187,17 @@ def _pp_zero(args, rank, world, device):
                    "global_batch": micro * per_micro * pp.dp_size, "seq_len": seq,
                    "parallelism": f"pp{pp.num_stages} x dp{pp.dp_size}, gpipe, {micro} micro-batches",
                    "optimizer": "sharded AdamW over the data-parallel group" if pp.dp_size > 1 else "AdamW"}
-    return step, batches, micro * per_micro * seq * pp.dp_size, description, model
+    def replicas_identical() -> bool:
+        """Every data-parallel replica of this stage holds the same weights (experts included)."""
+        import torch.distributed as dist
+
+        total = torch.stack([p.detach().double().sum() for p in model.parameters()]).sum().reshape(1)
+        seen = [torch.zeros_like(total) for _ in range(pp.dp_size)]
+        dist.all_gather(seen, total, group=pp.dp_group)
+        return all(torch.equal(seen[0], x) for x in seen)
+
+    return step, batches, micro * per_micro * seq * pp.dp_size, description, replicas_identical if pp.dp_size > 1 \
+        else None
 
 
 def _optimizer(model, device):
@@ -210,7 +220,7 @@ def main() -> None:
     device = torch.device("cuda", local) if args.device == "cuda" else torch.device("cpu")
     try:
         build = _tp_ep if args.config == "tp-ep" else _pp_zero
-        step, batches, tokens_per_step, description, _ = build(args, rank, world, device)
+        step, batches, tokens_per_step, description, check = build(args, rank, world, device)
         for i in range(args.warmup):
             step(batches[i])
         if device.type == "cuda":
@@ -244,6 +254,8 @@ def main() -> None:
             record.update(dtype="fp32", note="CPU smoke run of the wiring on gloo ranks; not a measurement")
         if device.type == "cuda":
             record["peak_mem_gb"] = round(torch.cuda.max_memory_allocated() / 1e9, 1)
+        if callable(check):  # every rank takes part (a collective)
+            record["dp_replicas_identical"] = bool(check())
         if rank == 0:
             print(json.dumps(record), flush=True)
     finally:

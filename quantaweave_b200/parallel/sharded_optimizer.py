@@ -46,8 +46,13 @@ class ShardedAdamW:
         self.world = dist.get_world_size(self.group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(self.group) if dist.is_initialized() else 0
         named = list(model.named_parameters())
-        self.shared = [p for n, p in named if not is_expert_parameter(n)]
-        self.local = [p for n, p in named if is_expert_parameter(n)]
+        # expert weights are rank-local only in an expert-parallel model (each rank holds different experts); in a
+        # pipeline or plain data-parallel model every replica holds the same experts and they are sharded like the
+        # rest, so their gradients are averaged over the group and counted in the clip norm
+        ep = getattr(model, "expert_parallel", None)
+        experts_local = ep is not None and getattr(ep, "world_size", 1) > 1
+        self.shared = [p for n, p in named if not (experts_local and is_expert_parameter(n))]
+        self.local = [p for n, p in named if experts_local and is_expert_parameter(n)]
         self.defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay)
         self._groups: dict = {}
         for p in self.shared:

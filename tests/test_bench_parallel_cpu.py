@@ -35,3 +35,4 @@ def test_the_parallel_bench_runs_on_cpu_ranks(config, ranks):
     assert record["final_loss"] == pytest.approx(record["final_loss"]) and record["final_loss"] > 0
     if config == "pp-zero":
         assert record["config"]["parallelism"].startswith("pp2 x dp2") and "sharded" in record["config"]["optimizer"]
+        assert record["dp_replicas_identical"] is True  # experts are averaged over the replicas like the rest
