@@ -106,6 +106,35 @@ def count_launches(step_fn) -> int:
     return len(ours)
 
 
+E2E_D2H = ("every step's loss is copied into pinned host memory without blocking and read on the host once the "
+           "next step is queued (the last one before the timer stops)")
+
+
+def e2e_loop(step_fn, steps: int) -> float:
+    """Run ``step_fn(i)`` for ``steps`` steps (each copies its inputs from pinned host memory); every step's loss
+    goes device -> pinned host buffer with a non-blocking copy and is read on the host after the next step has been
+    queued, as a training loop with asynchronous loss logging does. Returns the last loss."""
+    import torch
+
+    slots = [torch.empty(1, dtype=torch.float32).pin_memory() for _ in range(2)]
+    pending = None
+    value = float("nan")
+    for i in range(steps):
+        loss = step_fn(i)
+        slot = slots[i % 2]
+        slot.copy_(loss.detach().float().reshape(1), non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record()
+        if pending is not None:  # the previous step's loss, read while this step runs
+            pending[1].synchronize()
+            value = float(pending[0][0])
+        pending = (slot, ready)
+    if pending is not None:
+        pending[1].synchronize()
+        value = float(pending[0][0])
+    return value
+
+
 def kernel_breakdown(step_fn, report: bool = True) -> None:
     """Per-kernel CUDA time of one step (shares only; numbers taken under a profiler are never reported)."""
     import torch
@@ -226,13 +255,12 @@ def run_native(args, rank, world, local):
     if not args.no_e2e:
         h2d = host_batches[0].numel() * host_batches[0].element_size()
         with DeviceTimer() as te:
-            for i in range(args.steps):
-                batch = host_batches[args.warmup + args.steps + i].to("cuda", non_blocking=True)
-                loss_value = float(train_step(batch).item())
+            loss_value = e2e_loop(lambda i: train_step(host_batches[args.warmup + args.steps + i].to(
+                "cuda", non_blocking=True)), args.steps)
             opt.finish()
         e2e = {"value": tokens_per_step / (te.ms / args.steps / 1000.0), "unit": "tokens/s",
                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": 4 * world, "ms_per_step": te.ms / args.steps,
-               "final_loss": loss_value}
+               "final_loss": loss_value, "d2h": E2E_D2H}
     def step_and_finish(batch):
         loss = train_step(batch)
         opt.finish()
@@ -420,13 +448,13 @@ def run_reference(args, rank, world, local):
         tokens = args.seqs_per_gpu * args.seq_len * world
         ms = t.ms / args.steps
         e2e = None
-        if not args.no_e2e:
+        if not args.no_e2e:  # the same loop as the native arm's
             with DeviceTimer() as te:
-                for i in range(args.steps):
-                    float(train_step(host[args.warmup + args.steps + i].to(device, non_blocking=True)).item())
+                e2e_loop(lambda i: train_step(host[args.warmup + args.steps + i].to(device, non_blocking=True)),
+                         args.steps)
             e2e = {"value": tokens / (te.ms / args.steps / 1000.0), "unit": "tokens/s",
                    "h2d_bytes_per_step": host[0].numel() * host[0].element_size() * world,
-                   "d2h_bytes_per_step": 4 * world}
+                   "d2h_bytes_per_step": 4 * world, "d2h": E2E_D2H}
         emit(rank, {"metric": METRIC, "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
                     "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                     "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "impl": "reference",
