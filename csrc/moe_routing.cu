@@ -308,9 +308,26 @@ __global__ void __launch_bounds__(1024) select_kernel(const int* __restrict__ co
   __shared__ int s_scan[1024];
   __shared__ int s_carry;
   const int* seg = sorted_routes + uoffsets[e];
-  if (threadIdx.x == 0) { s_prefix = 0; s_need = cap; }  // rank (1-based) of the threshold among the largest keys
+  // The keys of one expert share their leading bytes (route weights of similar size): the bytes above the first
+  // one in which two keys differ take no radix pass. These passes were the slowest, every key landing in one bin.
+  __shared__ unsigned long long s_diff;
+  if (threadIdx.x == 0) s_diff = 0;
   __syncthreads();
-  for (int shift = 56; shift >= 0; shift -= 8) {
+  const uint64_t key0 = route_key(top_w[seg[0]], seg[0]);
+  uint64_t diff = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) diff |= route_key(top_w[seg[i]], seg[i]) ^ key0;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) diff |= __shfl_xor_sync(0xffffffffu, diff, o);
+  if ((threadIdx.x & 31) == 0 && diff) atomicOr(&s_diff, static_cast<unsigned long long>(diff));
+  __syncthreads();
+  const uint64_t differ = s_diff;
+  const int first_shift = differ ? ((63 - __clzll(static_cast<long long>(differ))) / 8) * 8 : 0;
+  if (threadIdx.x == 0) {  // rank (1-based) of the threshold among the largest keys; the shared leading bytes
+    s_need = cap;
+    s_prefix = first_shift == 56 ? 0ull : (key0 & (~0ull << (first_shift + 8)));
+  }
+  __syncthreads();
+  for (int shift = first_shift; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint64_t prefix = s_prefix;
