@@ -234,10 +234,6 @@ def main() -> None:
                         loss = step(batches[args.warmup + i])
             check_device_status()
             clock_summary = clocks.summary()
-            if args.kernel_breakdown:  # every rank steps (collectives), rank 0 reports
-                from bench import kernel_breakdown
-
-                kernel_breakdown(lambda: step(batches[-1]), report=rank == 0)
         else:
             with _WallTimer() as timer:
                 for i in range(args.steps):
@@ -258,6 +254,10 @@ def main() -> None:
             record["dp_replicas_identical"] = bool(check())
         if rank == 0:
             print(json.dumps(record), flush=True)
+        if device.type == "cuda" and args.kernel_breakdown:  # every rank steps (collectives), rank 0 reports
+            from bench import kernel_breakdown
+
+            kernel_breakdown(lambda: step(batches[-1]), report=rank == 0)
     finally:
         if dist.is_initialized():
             dist.destroy_process_group()
