@@ -20,7 +20,7 @@ The overlap with backward is off here (there is no backward to hide behind); thi
 Timing: CUDA events around each phase on the launching stream, mean over ``--iters`` after ``--warmup``, the max
 over ranks. Every buffer is far larger than the 126 MB L2, so nothing is flushed between iterations. Rank 0 prints
 one JSON line with both implementations and, for the fused one, the NVLink bytes each rank moves per direction and
-the bound they give at 770 GB/s (a measured B200 peer copy), next to the HBM bound at 6538 GB/s (a measured copy).
+the bound they give at 770 GB/s (a measured B200 peer copy), next to the HBM bound at the measured copy bandwidth.
 """
 
 from __future__ import annotations
@@ -33,7 +33,15 @@ from types import SimpleNamespace
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 NVLINK_GBS = 770.0  # measured peer copy per direction per B200
-HBM_GBS = 6538.0  # measured copy bandwidth of one B200
+
+
+def _hbm_gbs() -> float:
+    """Copy bandwidth of one B200 from the measured-peaks file next to this script, else an earlier measurement."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 6650.0
 
 
 def parse():
@@ -162,8 +170,9 @@ def main() -> None:
         hbm_step = per * 28 + numel * 2
         f = results["fused"]
         f["nvlink_bytes_in_per_rank"], f["nvlink_bytes_out_per_rank"] = nv_in, nv_out
-        f["reduce_bound_ms"] = max(nv_in / NVLINK_GBS / 1e6, hbm_reduce / HBM_GBS / 1e6)
-        f["step_bound_ms"] = max(nv_out / NVLINK_GBS / 1e6, hbm_step / HBM_GBS / 1e6)
+        hbm = _hbm_gbs()
+        f["reduce_bound_ms"] = max(nv_in / NVLINK_GBS / 1e6, hbm_reduce / hbm / 1e6)
+        f["step_bound_ms"] = max(nv_out / NVLINK_GBS / 1e6, hbm_step / hbm / 1e6)
         f["fraction_of_bound"] = (f["reduce_bound_ms"] + f["step_bound_ms"]) / f["total_ms"]
         record = {"metric": "sharded AdamW exchange + update ms", "n_gpus": world, "numel": numel,
                   "tensors": args.tensors, "iters": args.iters, "warmup": args.warmup, "dtype": "bf16",
